@@ -1,0 +1,303 @@
+/*
+ * ll_b200.h -- C ABI of the B200 (sm_100a) low-latency MLP inference engine.
+ *
+ * The reference (mamedov-ma/low_latency_inference_gpu) has no library or FFI:
+ * its host code launches header-only kernels with <<<>>> and drives a
+ * TickBuffer mailbox by hand.  Every entry point below replaces one of those
+ * host-side constructs; the reference interface each one stands in for is
+ * cited beside it (paths are relative to the reference project root).
+ *
+ * Conventions: plain pointers and sizes only; every call returns an int status
+ * (LL_OK on success) instead of the reference's print-and-exit CUDA_CHECK
+ * (include/bench_utils.h:14-22); ll_last_error() gives the message of the
+ * calling thread's last failure.  Weights are host row-major [out x in]
+ * exactly as the reference's host vectors (src/bench_cublas_mlp.cu:69-80).
+ */
+#ifndef LL_B200_H
+#define LL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (replace CUDA_CHECK -> std::exit(1), include/bench_utils.h:14-22) ---- */
+enum {
+    LL_OK = 0,
+    LL_ERR_CUDA = 1,         /* a CUDA runtime / cuBLAS call failed */
+    LL_ERR_TIMEOUT = 2,      /* host-side wait ran out (request not answered in time) */
+    LL_ERR_BAD_DESC = 3,     /* network descriptor invalid or does not fit the device */
+    LL_ERR_DEVICE_FAULT = 4, /* the resident kernel reported an error (see ll_engine_info) */
+    LL_ERR_STOPPED = 5,      /* engine stopped */
+    LL_ERR_INVALID_ARG = 6,
+    LL_ERR_UNSUPPORTED = 7,
+    LL_ERR_BUSY = 8          /* a request is still outstanding */
+};
+
+/* ---- activations (include/ll/dense_warp.cuh:9-21 ActIdentity/ActRelu; GELU is new) ---- */
+enum { LL_ACT_IDENTITY = 0, LL_ACT_RELU = 1, LL_ACT_GELU = 2 };
+
+/* ---- weight storage types ---- */
+enum { LL_W_F32 = 0, LL_W_BF16 = 1, LL_W_I8 = 2 };
+
+/* ---- initialisers for ll_init_params ---- */
+enum { LL_INIT_XAVIER_UNIFORM = 0, LL_INIT_NORMAL_FANIN = 1 };
+
+/*
+ * Layer / network descriptors: the runtime form of include/net_config.h:6-26
+ * (netcfg::IN_DIM/H1_DIM/H2_DIM/OUT_DIM, compile-time constants there).
+ */
+typedef struct ll_layer_desc {
+    int32_t in_dim;
+    int32_t out_dim;
+    int32_t act;   /* LL_ACT_* applied after bias */
+    int32_t wtype; /* LL_W_*; all layers of one net share it */
+} ll_layer_desc;
+
+typedef struct ll_net_desc {
+    int32_t n_layers;
+    const ll_layer_desc *layers;
+    int32_t max_batch; /* rows per request the mailbox can carry (>= 1) */
+    int32_t reserved;
+} ll_net_desc;
+
+/*
+ * Mailbox header: field order and meaning of the reference's TickBuffer
+ * (src/bench_persistent_mbyv_mlp.cu:88-95, src/bench_persistent_mlp.cu:65-72):
+ * seq_in (0 = idle, host increments per request), seq_out (device echoes the
+ * finished seq), stop, then one 32-bit word the reference calls `pad`, used
+ * here as the request's row count (0 means 1).  The float x[] block follows at
+ * byte 16 and y[] right after x[] (in_dim * max_batch floats), so for a batch-1
+ * net the layout is byte-identical to the reference struct.
+ */
+typedef struct ll_tick_header {
+    volatile uint32_t seq_in;
+    volatile uint32_t seq_out;
+    volatile uint32_t stop;
+    uint32_t n_rows;
+} ll_tick_header;
+
+#define LL_STOP_SEQ 0xFFFFFFFFu /* src/bench_persistent_mbyv_mlp.cu:157 */
+
+typedef struct ll_engine_opts {
+    int32_t cluster_size;       /* CTAs per cluster: 1,2,4,8,16; 0 = automatic */
+    int32_t replicate_first;    /* first layer computed by every CTA: -1 auto, 0 no, 1 yes */
+    int32_t write_combined;     /* allocate the mailbox write-combined (reference default) */
+    int32_t poll_mode;          /* 0 = one acquire load in flight, 1 = pipelined relaxed loads */
+    uint64_t idle_timeout_ns;   /* resident kernel exits after this long idle; relaunched on demand */
+    uint64_t step_timeout_ns;   /* bound on every device wait inside one request */
+    int32_t max_stages;         /* cap on pipeline stages (clusters); 0 = automatic */
+    int32_t min_stages;         /* spread the layers over at least this many clusters; 0 = as few as fit */
+    int32_t reserved[6];
+} ll_engine_opts;
+
+typedef struct ll_engine_info {
+    int32_t n_stages;       /* clusters in the pipeline */
+    int32_t cluster_size;   /* CTAs per cluster */
+    int32_t threads;        /* threads per CTA */
+    int32_t smem_bytes;     /* dynamic shared memory per CTA */
+    int32_t image_bytes;    /* largest per-CTA resident weight image */
+    int32_t launches;       /* resident-kernel launches since create */
+    int32_t state;          /* 0 idle, 1 loading, 2 running, 3 exiting, 4 exited */
+    int32_t status;         /* last device status (LL_OK or LL_ERR_*) */
+    int32_t err_where;      /* device-side location code of the last error */
+    uint32_t served;        /* last seq the device published */
+    int32_t layer_modes[24];
+} ll_engine_info;
+
+/*
+ * Placement of a net on the GPU, as computed by the planner (no GPU needed).
+ * Each layer is split over the CTAs of one cluster ("stage"); the per-CTA
+ * shared-memory images hold the weight slices.  Layer modes: 0 replicated,
+ * 1 row-split + all-gather, 2 row-split kept local, 3 K-split gathered at
+ * rank 0, 4 row-split gathered at rank 0, 5 row-split handed to the next
+ * cluster through global memory.  The reference fixes this split at compile
+ * time per kernel (BLOCKS / WARPS template arguments, include/ll/mbyv.cuh:8-35).
+ */
+typedef struct ll_plan_layer {
+    int32_t mode, act, wtype, lpr_log2;
+    int32_t K, M, Mp, R;
+    int32_t in_buf, in_ld, out_buf, out_ld;
+    uint32_t w_off, b_off, s_off;
+    int32_t round_out;
+} ll_plan_layer;
+
+typedef struct ll_plan {
+    int32_t n_layers, n_stages, cluster_size, threads, bmax4, in_ld, act_bf16, reserved;
+    int32_t stage_first[9], stage_last[9], stage_in_ld[9];
+    uint32_t image_bytes[9];
+    uint32_t buf_off[6]; /* X, A, B, L, G, STAGE */
+    uint32_t smem_bytes;
+    uint32_t image_stride; /* bytes between consecutive CTA images (CTA = stage * cluster_size + rank) */
+    ll_plan_layer layers[24];
+} ll_plan;
+
+/*
+ * Plan a net without touching the GPU.  If images is non-NULL it receives the
+ * packed per-CTA images (n_stages * cluster_size * image_stride bytes, which
+ * must not exceed images_cap).  *images_bytes gets the required size.
+ */
+int ll_plan_net(const ll_net_desc *net, const void *const *W, const float *const *b, const float *const *scales,
+                const ll_engine_opts *opts, ll_plan *plan, uint8_t *images, size_t images_cap,
+                size_t *images_bytes);
+
+typedef struct ll_engine ll_engine;
+
+void ll_engine_opts_default(ll_engine_opts *opts);
+
+/*
+ * Create a resident engine: uploads the weights, plans the per-CTA shared-memory
+ * images and allocates the host-mapped mailbox.  Replaces the setup half of the
+ * reference's persistent benches (src/bench_persistent_mbyv_mlp.cu:386-491:
+ * cudaSetDeviceFlags, cudaMalloc/cudaMemcpy of W/b, cudaHostAlloc(Mapped) of the
+ * TickBuffer, kernel launch).  W[l] points to host data of the layer's wtype
+ * (float / uint16 bf16 bits / int8); b[l] fp32 [out_dim] (NULL = zeros);
+ * scales[l] fp32 [out_dim] for LL_W_I8 (ignored otherwise; scales may be NULL).
+ */
+int ll_engine_create(const ll_net_desc *net, const void *const *W, const float *const *b, const float *const *scales,
+                     int device, ll_engine **out);
+int ll_engine_create_ex(const ll_net_desc *net, const void *const *W, const float *const *b,
+                        const float *const *scales, int device, const ll_engine_opts *opts, ll_engine **out);
+
+/*
+ * Ping-pong floor: the same resident kernel and mailbox with no layers.  It
+ * waits for seq_in, reads in_dim floats of x, writes y[i] = x[i] (0 beyond
+ * in_dim) for i < out_dim and publishes seq_out.  in_dim = out_dim = 0 echoes
+ * only the sequence number.  The reference has no such kernel; its nearest is
+ * the empty-launch bench src/bench_main.cu:9-34.
+ */
+int ll_echo_engine_create(int device, int in_dim, int out_dim, const ll_engine_opts *opts, ll_engine **out);
+
+/* Host pointer of the mailbox (layout of ll_tick_header + x + y, see above). */
+void *ll_engine_mailbox(ll_engine *e);
+float *ll_engine_mailbox_x(ll_engine *e);
+float *ll_engine_mailbox_y(ll_engine *e);
+
+/* Launch the resident kernel (also done lazily by ll_submit). */
+int ll_engine_start(ll_engine *e);
+
+/*
+ * Host doorbell, the reference's per-request host code
+ * (src/bench_persistent_mbyv_mlp.cu:539-544): write x (skipped when x is
+ * NULL: the caller already wrote the mailbox), release-store seq_in; poll
+ * waits until seq_out == seq (or timeout_ns) and copies y out (y may be NULL).
+ */
+int ll_submit(ll_engine *e, const float *x, int n_rows, uint32_t *seq);
+int ll_poll(ll_engine *e, uint32_t seq, float *y, uint64_t timeout_ns);
+int ll_infer(ll_engine *e, const float *x, int n_rows, float *y, uint64_t timeout_ns);
+
+/* Stop (src/bench_persistent_mbyv_mlp.cu:553-559: stop = 1, bump seq_in, wait). */
+int ll_engine_stop(ll_engine *e);
+int ll_engine_destroy(ll_engine *e);
+int ll_engine_get_info(ll_engine *e, ll_engine_info *info);
+
+/*
+ * Closed-loop timing through the mailbox, in C++ so no interpreter sits in the
+ * loop: n_req sequential requests, request r taking xs[(r % n_x)] (n_rows rows
+ * each); lat_us[r] = host steady_clock time from writing x to reading y
+ * (src/bench_persistent_mbyv_mlp.cu:536-548 times the same span minus the x/y
+ * copies).  ys (may be NULL) receives every request's output, row-major.
+ */
+int ll_engine_bench_closed_loop(ll_engine *e, const float *xs, int n_x, int n_req, int n_rows, float *ys,
+                                double *lat_us);
+
+/*
+ * Device-resident queue: runs n_req sequential requests whose inputs d_x
+ * [n_req][n_rows][in_dim] already sit in device memory, writing d_y
+ * [n_req][n_rows][out_dim]; each request starts only after the previous one
+ * finished (batch-1 latency semantics, no PCIe).  *ms = CUDA-event time of the
+ * launch; d_stamps (device, may be NULL) gets a %globaltimer ns stamp per
+ * finished request.  The resident mailbox kernel is stopped first.
+ */
+int ll_engine_run_queue(ll_engine *e, const float *d_x, float *d_y, int n_req, int n_rows, float *ms,
+                        unsigned long long *d_stamps);
+
+const char *ll_last_error(void);
+
+/* ---- launch-per-layer kernels (sm_100a), one inference per launch sequence ---- */
+
+/* y = act(W x + b), W row-major [M x K]; replaces ll::dense_warp_rm_kernel (include/ll/dense_warp.cuh:33-90). */
+int ll_dense_warp_rm(const float *W, const float *b, const float *x, float *y, int M, int K, int act,
+                     void *stream);
+/* y = act(W_cm^T x + b_pad), W_cm K-major [K x Mpad]; replaces ll::launch_dense_mbyv_packed
+ * (include/ll/dense_mbyv_packed.cuh:53-63). */
+int ll_dense_mbyv_packed(const float *W_cm, const float *b_pad, const float *x, float *y, int M, int K, int act,
+                         void *stream);
+/* Host packing, include/ll/pack_weights.cuh:16-32. */
+void ll_pack_rm_to_kmajor_padded(const float *W_rm, size_t M, size_t K, float *W_cm, size_t Mpad);
+void ll_pack_bias_padded(const float *b, size_t M, float *b_pad, size_t Mpad);
+
+/*
+ * Launch-per-layer MLP object: one ll_dense_warp_rm launch per layer on
+ * device-resident weights, optionally captured in a CUDA graph; the comparison
+ * path of src/bench_custom_warp_mlp_graph.cu:96-152 and (with pinned copies
+ * inside the graph) src/bench_custom_warp_e2e.cu:165-194.
+ */
+typedef struct ll_layered_mlp ll_layered_mlp;
+enum { LL_RUN_DIRECT_KERNEL = 0, LL_RUN_GRAPH_KERNEL = 1, LL_RUN_GRAPH_E2E = 2, LL_RUN_DIRECT_E2E = 3,
+       LL_RUN_MAILBOX_TICK = 4 };
+int ll_layered_mlp_create(const ll_net_desc *net, const float *const *W, const float *const *b, int device,
+                          ll_layered_mlp **out);
+/* Times n_req requests in the given LL_RUN_* mode; lat_us[r] per request; y_last gets the last output. */
+int ll_layered_mlp_bench(ll_layered_mlp *m, int mode, const float *xs, int n_x, int n_req, float *y_last,
+                         double *lat_us);
+int ll_layered_mlp_destroy(ll_layered_mlp *m);
+
+/*
+ * cuBLAS comparison path: per layer cublasSgemm(OP_T, OP_N, M, 1, K) plus a
+ * bias(+ReLU) kernel, direct or captured in a CUDA graph
+ * (src/bench_cublas_mlp.cu:119-137, src/bench_cublas_mlp_graph.cu:119-187),
+ * e2e with pinned copies, or the mailbox-per-tick structure of
+ * src/bench_persistent_cublas_mlp.cu:226-271.  fp32 nets only.
+ */
+typedef struct ll_cublas_mlp ll_cublas_mlp;
+int ll_cublas_mlp_create(const ll_net_desc *net, const float *const *W, const float *const *b, int device,
+                         ll_cublas_mlp **out);
+int ll_cublas_mlp_bench(ll_cublas_mlp *m, int mode, const float *xs, int n_x, int n_req, float *y_last,
+                        double *lat_us);
+int ll_cublas_mlp_destroy(ll_cublas_mlp *m);
+
+/* ---- synthetic workload generators (the reference's host_init, src/bench_cublas_mlp.cu:37-43) ---- */
+
+/* std::mt19937(seed) + std::normal_distribution<float>(mean, stddev): bit-identical to host_init. */
+int ll_fill_normal(float *out, size_t n, float mean, float stddev, uint32_t seed);
+/* std::mt19937(seed) + std::uniform_real_distribution<float>(lo, hi). */
+int ll_fill_uniform(float *out, size_t n, float lo, float hi, uint32_t seed);
+/*
+ * Parameters of a whole net from ONE std::mt19937(seed) stream, drawn in the
+ * order W1, b1, W2, b2, ... (W row-major [out x in]); W Xavier-uniform
+ * U(+-sqrt(6/(in+out))) or N(0, 1/in); biases U[-0.01, 0.01].
+ */
+int ll_init_params(const ll_net_desc *net, int init, uint32_t seed, float *const *W, float *const *b);
+/* fp32 -> bf16 bit patterns, round to nearest even. */
+void ll_f32_to_bf16(const float *in, uint16_t *out, size_t n);
+/* Symmetric per-output-channel int8: s[m] = max|W[m,:]|/127, q = clamp(rint(W/s), -127, 127). */
+void ll_quantize_int8_rows(const float *W, int m, int k, int8_t *q, float *s);
+
+/* ---- statistics (include/bench_utils.h:140-171, linear-interpolated percentiles) ---- */
+typedef struct ll_stats {
+    double p50, p90, p99, min, max, mean, sd;
+} ll_stats;
+void ll_compute_stats(const double *xs, size_t n, ll_stats *out);
+
+/* ---- host-side mailbox protocol on any memory (used by the engine; testable without a GPU) ---- */
+/* Bytes of a mailbox for the given dims (header + x + y, rounded to 64). */
+size_t ll_mailbox_bytes(int in_dim, int out_dim, int max_batch);
+/* Write x (if non-NULL) and n_rows, then release-store seq_in = seq. */
+void ll_mailbox_post(void *mailbox, int in_dim, const float *x, int n_rows, uint32_t seq, int write_combined);
+/* Spin until seq_out == seq (acquire) or timeout; copies n_rows*out_dim floats of y. LL_OK / LL_ERR_TIMEOUT. */
+int ll_mailbox_wait(const void *mailbox, int in_dim, int out_dim, int max_batch, uint32_t seq, float *y,
+                    int n_rows, uint64_t timeout_ns);
+/* Next sequence number after seq: skips 0 (idle) and LL_STOP_SEQ. */
+uint32_t ll_next_seq(uint32_t seq);
+
+/* Library version string. */
+const char *ll_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LL_B200_H */

@@ -1,0 +1,1088 @@
+// Resident MLP engine: planner, weight-image packing, launch and the C ABI
+// around ll_resident_mlp_kernel (see resident_kernel.cuh).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstring>
+#include <thread>
+#include <vector>
+
+#include "common.h"
+#include "engine_types.h"
+#include "resident_kernel.cuh"
+
+#if defined(__x86_64__)
+#include <immintrin.h>
+#endif
+
+using namespace llk;
+
+namespace {
+
+constexpr int kSmemLimit = 227 * 1024 - 1024;  // dynamic smem budget per CTA (static Shared lives in the rest)
+
+inline void cpu_relax()
+{
+#if defined(__x86_64__)
+    _mm_pause();
+#endif
+}
+
+int elems_per_unit(int wtype)
+{
+    return wtype == LL_W_F32 ? 4 : (wtype == LL_W_BF16 ? 8 : 16);
+}
+
+int wbytes(int wtype)
+{
+    return wtype == LL_W_F32 ? 4 : (wtype == LL_W_BF16 ? 2 : 1);
+}
+
+int pow2_floor(int v)
+{
+    int p = 1;
+    while (p * 2 <= v)
+        p *= 2;
+    return p;
+}
+
+int log2i(int v)
+{
+    int l = 0;
+    while ((1 << (l + 1)) <= v)
+        ++l;
+    return l;
+}
+
+// lanes per row: each lane gets >= 2 weight units when the row is long enough.
+int choose_lpr_log2(int K, int wtype)
+{
+    const int U = K / elems_per_unit(wtype);
+    const int want = std::max(1, std::min(32, U / 2));
+    return log2i(pow2_floor(want));
+}
+
+struct LayerPlan {
+    int mode = 0;
+    int in = 0, out = 0, act = 0, wtype = 0;
+    int K = 0;   // padded dot length
+    int R = 0;   // rows per CTA (or OUTp for K-split)
+    int Mp = 0;  // padded full width
+    int in_buf = BUF_X, in_ld = 0, out_buf = BUF_X, out_ld = 0;
+    int stage = 0;
+};
+
+struct PlanResult {
+    int S = 1, C = 1;
+    std::vector<LayerPlan> L;
+    std::vector<int> stage_first, stage_last, stage_in_ld;
+    std::vector<size_t> stage_image;  // bytes per CTA image of each stage
+    size_t buf_floats[BUF_COUNT] = {0, 0, 0, 0, 0, 0};
+    size_t smem = 0;
+    std::string why;
+};
+
+size_t layer_image_bytes(const LayerPlan &l)
+{
+    size_t w = llh::round_up((size_t)l.R * (size_t)l.K * wbytes(l.wtype), 16);
+    size_t b = llh::round_up((size_t)l.R * 4, 16);
+    size_t s = l.wtype == LL_W_I8 ? b : 0;
+    return w + b + s;
+}
+
+// Assign modes / buffers to layers of a stage partition and size everything.
+bool build_plan(const ll_net_desc &net, int C, const std::vector<int> &bounds, bool replicate_first, PlanResult &pr)
+{
+    const int n = net.n_layers;
+    const int S = (int)bounds.size() - 1;
+    const int wt = net.layers[0].wtype;
+    const int E = elems_per_unit(wt);
+    const int Rq = std::max(4, E);
+    const int bmax4 = (int)llh::round_up((size_t)std::max(1, net.max_batch), 4);
+    pr = PlanResult();
+    pr.S = S;
+    pr.C = C;
+    pr.L.resize(n);
+    size_t x_ld_max = 0, ab_w = 0, l_w = 0, g_f = 0, st_w = 4;
+    for (int s = 0; s < S; ++s) {
+        const int f = bounds[s], e = bounds[s + 1] - 1;
+        pr.stage_first.push_back(f);
+        pr.stage_last.push_back(e);
+        int cur_buf = BUF_X;
+        int cur_ld = (s == 0) ? (int)llh::round_up((size_t)net.layers[0].in_dim, (size_t)E) : pr.L[f - 1].Mp;
+        pr.stage_in_ld.push_back(cur_ld);
+        x_ld_max = std::max(x_ld_max, (size_t)cur_ld);
+        int next_ab = BUF_A;
+        int local_R = 0;
+        size_t img = 0;
+        for (int l = f; l <= e; ++l) {
+            LayerPlan &lp = pr.L[l];
+            const ll_layer_desc &d = net.layers[l];
+            lp.in = d.in_dim;
+            lp.out = d.out_dim;
+            lp.act = d.act;
+            lp.wtype = wt;
+            lp.stage = s;
+            const bool last_stage = (s == S - 1);
+            int mode;
+            if (last_stage && l == e)
+                mode = (e > f) ? LM_KSPLIT_GATHER : LM_ROWSPLIT_GATHER;
+            else if (last_stage && l == e - 1)
+                mode = LM_ROWSPLIT_LOCAL;
+            else if (!last_stage && l == e)
+                mode = LM_ROWSPLIT_GLOBAL;
+            else if (s == 0 && l == f && replicate_first)
+                mode = LM_REPLICATED;
+            else
+                mode = LM_ROWSPLIT_ALLGATHER;
+            lp.mode = mode;
+            if (mode == LM_KSPLIT_GATHER) {
+                lp.K = local_R;
+                lp.R = (int)llh::round_up((size_t)d.out_dim, 4);
+                lp.Mp = lp.R;
+                lp.in_buf = BUF_L;
+                lp.in_ld = local_R;
+                lp.out_buf = BUF_G;
+                lp.out_ld = lp.R;
+                g_f = std::max(g_f, (size_t)C * bmax4 * lp.R);
+                st_w = std::max(st_w, (size_t)lp.R);
+            } else {
+                lp.K = cur_ld;
+                lp.in_buf = cur_buf;
+                lp.in_ld = cur_ld;
+                if (mode == LM_REPLICATED) {
+                    lp.R = (int)llh::round_up((size_t)d.out_dim, (size_t)Rq);
+                    lp.Mp = lp.R;
+                } else {
+                    lp.R = (int)llh::round_up((size_t)llh::ceil_div(d.out_dim, C), (size_t)Rq);
+                    lp.Mp = lp.R * C;
+                }
+                st_w = std::max(st_w, (size_t)lp.R);
+                if (mode == LM_REPLICATED || mode == LM_ROWSPLIT_ALLGATHER) {
+                    lp.out_buf = next_ab;
+                    lp.out_ld = lp.Mp;
+                    ab_w = std::max(ab_w, (size_t)lp.Mp);
+                    next_ab = next_ab == BUF_A ? BUF_B : BUF_A;
+                    cur_buf = lp.out_buf;
+                    cur_ld = lp.Mp;
+                } else if (mode == LM_ROWSPLIT_LOCAL) {
+                    lp.out_buf = BUF_L;
+                    lp.out_ld = lp.R;
+                    local_R = lp.R;
+                    l_w = std::max(l_w, (size_t)lp.R);
+                } else if (mode == LM_ROWSPLIT_GATHER) {
+                    lp.out_buf = BUF_G;
+                    lp.out_ld = lp.Mp;
+                    g_f = std::max(g_f, (size_t)bmax4 * lp.Mp);
+                } else {  // GLOBAL
+                    lp.out_buf = BUF_X;
+                    lp.out_ld = lp.Mp;
+                }
+            }
+            img += layer_image_bytes(lp);
+        }
+        pr.stage_image.push_back(img);
+    }
+    size_t max_img = 0;
+    for (size_t v : pr.stage_image)
+        max_img = std::max(max_img, v);
+    pr.buf_floats[BUF_X] = (size_t)bmax4 * x_ld_max;
+    pr.buf_floats[BUF_A] = (size_t)bmax4 * ab_w;
+    pr.buf_floats[BUF_B] = (size_t)bmax4 * ab_w;
+    pr.buf_floats[BUF_L] = (size_t)bmax4 * l_w;
+    pr.buf_floats[BUF_G] = g_f;
+    pr.buf_floats[BUF_STAGE] = (size_t)bmax4 * st_w;
+    size_t total = llh::round_up(max_img, 128);
+    for (int i = 0; i < BUF_COUNT; ++i)
+        total += llh::round_up(std::max<size_t>(pr.buf_floats[i], 4) * 4, 128);
+    pr.smem = total;
+    return total <= (size_t)kSmemLimit;
+}
+
+// Greedy partition of layers into stages so each CTA image fits.
+bool plan_net(const ll_net_desc &net, int C, int replicate_opt, int min_stages, int max_stages, PlanResult &out)
+{
+    const int n = net.n_layers;
+    for (int S = std::max(1, min_stages); S <= std::min(max_stages, n); ++S) {
+        // balanced contiguous split by weight bytes
+        std::vector<double> wsz(n);
+        double tot = 0;
+        for (int l = 0; l < n; ++l) {
+            wsz[l] = (double)net.layers[l].in_dim * net.layers[l].out_dim * wbytes(net.layers[l].wtype);
+            tot += wsz[l];
+        }
+        std::vector<int> bounds = {0};
+        double acc = 0;
+        int s = 1;
+        for (int l = 0; l < n && s < S; ++l) {
+            acc += wsz[l];
+            const int remaining_layers = n - (l + 1);
+            const int remaining_stages = S - s;
+            if ((acc >= tot * s / S && remaining_layers >= remaining_stages) || remaining_layers == remaining_stages) {
+                bounds.push_back(l + 1);
+                ++s;
+            }
+        }
+        bounds.push_back(n);
+        if ((int)bounds.size() != S + 1)
+            continue;
+        // the last stage needs >= 1 layer; a K-split tail needs 2 (else row-split gather)
+        const int n0 = bounds[1] - bounds[0];
+        bool rep;
+        if (replicate_opt == 1)
+            rep = n0 >= 3 || (S > 1 && n0 >= 2);
+        else if (replicate_opt == 0)
+            rep = false;
+        else {
+            const double first_bytes = (double)net.layers[0].in_dim * net.layers[0].out_dim * wbytes(net.layers[0].wtype);
+            rep = (n0 >= 3) && first_bytes <= 72.0 * 1024;
+        }
+        PlanResult pr;
+        if (build_plan(net, C, bounds, rep, pr)) {
+            out = pr;
+            return true;
+        }
+        if (rep && build_plan(net, C, bounds, false, pr)) {
+            out = pr;
+            return true;
+        }
+    }
+    return false;
+}
+
+// Pack the shared-memory image of CTA `rank` of stage `s` (dst == nullptr: offsets only).
+void pack_image(const ll_net_desc &net, const PlanResult &pr, int s, int rank, const void *const *W,
+                const float *const *b, const float *const *scales, uint8_t *dst, std::vector<uint32_t> &w_off,
+                std::vector<uint32_t> &b_off, std::vector<uint32_t> &s_off)
+{
+    (void)net;
+    size_t off = 0;
+    for (int l = pr.stage_first[s]; l <= pr.stage_last[s]; ++l) {
+        const LayerPlan &lp = pr.L[l];
+        const int wb = wbytes(lp.wtype);
+        const size_t wsz = llh::round_up((size_t)lp.R * lp.K * wb, 16);
+        const size_t bsz = llh::round_up((size_t)lp.R * 4, 16);
+        const bool has_s = lp.wtype == LL_W_I8;
+        w_off[l] = (uint32_t)off;
+        b_off[l] = (uint32_t)(off + wsz);
+        s_off[l] = has_s ? (uint32_t)(off + wsz + bsz) : 0xffffffffu;
+        if (dst) {
+            uint8_t *wdst = dst + off;
+            std::memset(wdst, 0, wsz);
+            float *bdst = reinterpret_cast<float *>(dst + off + wsz);
+            std::memset(bdst, 0, bsz);
+            float *sdst = has_s ? reinterpret_cast<float *>(dst + off + wsz + bsz) : nullptr;
+            if (sdst)
+                std::memset(sdst, 0, bsz);
+            const uint8_t *src = static_cast<const uint8_t *>(W[l]);
+            for (int r = 0; r < lp.R; ++r) {
+                int grow;  // global output row
+                int col0;  // first global input column of this slice
+                if (lp.mode == LM_KSPLIT_GATHER) {
+                    grow = r;
+                    col0 = rank * lp.K;
+                } else if (lp.mode == LM_REPLICATED) {
+                    grow = r;
+                    col0 = 0;
+                } else {
+                    grow = rank * lp.R + r;
+                    col0 = 0;
+                }
+                if (grow >= lp.out)
+                    continue;
+                for (int k = 0; k < lp.K; ++k) {
+                    const int gk = col0 + k;
+                    if (gk >= lp.in)
+                        break;
+                    std::memcpy(wdst + ((size_t)r * lp.K + k) * wb, src + ((size_t)grow * lp.in + gk) * wb, wb);
+                }
+                bdst[r] = b && b[l] ? b[l][grow] : 0.0f;
+                if (sdst)
+                    sdst[r] = scales && scales[l] ? scales[l][grow] : 1.0f;
+            }
+        }
+        off += wsz + bsz + (has_s ? bsz : 0);
+    }
+}
+
+}  // namespace
+
+struct ll_engine {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    Params base{};
+    bool echo = false;
+    int in_dim = 0, out_dim = 0, max_batch = 1;
+    int grid = 1;
+    PlanResult plan;
+    void *mb_host = nullptr;
+    ll_tick_header *mb_dev = nullptr;
+    size_t mb_bytes = 0;
+    int wc = 0;
+    EngineCtrl *ctrl_host = nullptr;
+    EngineCtrl *ctrl_dev = nullptr;
+    uint8_t *d_image = nullptr;
+    float *d_xfer = nullptr;
+    unsigned *d_words = nullptr;  // [kMaxStages] cnt, [2*kMaxStages] hdr, abort, q_done
+    uint32_t seq = 0;
+    uint32_t outstanding = 0;
+    uint32_t last_served = 0;
+    bool running = false;
+    int launches = 0;
+    int last_status = LL_OK;
+    ll_engine_opts opts{};
+    bool attrs_set = false;
+};
+
+extern "C" void ll_engine_opts_default(ll_engine_opts *o)
+{
+    std::memset(o, 0, sizeof(*o));
+    o->cluster_size = 0;
+    o->replicate_first = -1;
+    o->write_combined = 0;
+    o->poll_mode = 0;
+    o->idle_timeout_ns = 30ull * 1000 * 1000 * 1000;
+    o->step_timeout_ns = 200ull * 1000 * 1000;
+    o->max_stages = 0;
+}
+
+namespace {
+
+int validate_net(const ll_net_desc *net, const void *const *W)
+{
+    if (!net || net->n_layers < 1 || net->n_layers > kMaxLayers || !net->layers) {
+        llh::set_error("net descriptor: n_layers must be in [1, %d]", kMaxLayers);
+        return LL_ERR_BAD_DESC;
+    }
+    if (net->max_batch < 1 || net->max_batch > 64) {
+        llh::set_error("net descriptor: max_batch must be in [1, 64]");
+        return LL_ERR_BAD_DESC;
+    }
+    const int wt = net->layers[0].wtype;
+    for (int l = 0; l < net->n_layers; ++l) {
+        const ll_layer_desc &d = net->layers[l];
+        if (d.in_dim < 1 || d.out_dim < 1 || d.in_dim > 16384 || d.out_dim > 16384) {
+            llh::set_error("layer %d: dims out of range", l);
+            return LL_ERR_BAD_DESC;
+        }
+        if (l > 0 && net->layers[l - 1].out_dim != d.in_dim) {
+            llh::set_error("layer %d: in_dim %d != previous out_dim %d", l, d.in_dim, net->layers[l - 1].out_dim);
+            return LL_ERR_BAD_DESC;
+        }
+        if (d.act < LL_ACT_IDENTITY || d.act > LL_ACT_GELU) {
+            llh::set_error("layer %d: unknown activation %d", l, d.act);
+            return LL_ERR_BAD_DESC;
+        }
+        if (d.wtype != wt || wt < LL_W_F32 || wt > LL_W_I8) {
+            llh::set_error("layer %d: all layers must share one valid weight type", l);
+            return LL_ERR_BAD_DESC;
+        }
+        if (W && !W[l]) {
+            llh::set_error("layer %d: weight pointer is NULL", l);
+            return LL_ERR_INVALID_ARG;
+        }
+    }
+    return LL_OK;
+}
+
+int alloc_mailbox(ll_engine *e)
+{
+    e->mb_bytes = ll_mailbox_bytes(e->in_dim, e->out_dim, e->max_batch);
+    unsigned flags = cudaHostAllocMapped | cudaHostAllocPortable;
+    if (e->wc)
+        flags |= cudaHostAllocWriteCombined;
+    LL_CUDA_TRY(cudaHostAlloc(&e->mb_host, e->mb_bytes, flags));
+    std::memset(e->mb_host, 0, e->mb_bytes);
+    LL_CUDA_TRY(cudaHostGetDevicePointer((void **)&e->mb_dev, e->mb_host, 0));
+    LL_CUDA_TRY(cudaHostAlloc((void **)&e->ctrl_host, sizeof(EngineCtrl), cudaHostAllocMapped | cudaHostAllocPortable));
+    std::memset((void *)e->ctrl_host, 0, sizeof(EngineCtrl));
+    LL_CUDA_TRY(cudaHostGetDevicePointer((void **)&e->ctrl_dev, (void *)e->ctrl_host, 0));
+    return LL_OK;
+}
+
+// Shared-memory layout and per-stage tables (no CUDA).
+void layout_buffers(Params &p, const PlanResult &pr, int in_dim, int out_dim, int max_batch)
+{
+    p.C = pr.C;
+    p.n_stages = pr.S;
+    p.in_dim = in_dim;
+    p.out_dim = out_dim;
+    p.max_batch = max_batch;
+    p.bmax4 = (int)llh::round_up((size_t)max_batch, 4);
+    p.in_ld = pr.stage_in_ld.empty() ? (int)llh::round_up((size_t)std::max(in_dim, 1), 4) : pr.stage_in_ld[0];
+    for (int s = 0; s < kMaxStages; ++s) {
+        p.stage_first[s] = s < pr.S && !pr.stage_first.empty() ? pr.stage_first[s] : 0;
+        p.stage_last[s] = s < pr.S && !pr.stage_last.empty() ? pr.stage_last[s] : -1;
+        p.stage_in_ld[s] = s < (int)pr.stage_in_ld.size() ? pr.stage_in_ld[s] : p.in_ld;
+        p.image_bytes[s] = s < (int)pr.stage_image.size() ? (uint32_t)pr.stage_image[s] : 0u;
+    }
+    size_t max_img = 0;
+    for (size_t v : pr.stage_image)
+        max_img = std::max(max_img, v);
+    size_t off = llh::round_up(max_img, 128);
+    for (int i = 0; i < BUF_COUNT; ++i) {
+        p.buf_off[i] = (uint32_t)off;
+        off += llh::round_up(std::max<size_t>(pr.buf_floats[i], 4) * 4, 128);
+    }
+    p.smem_bytes = (uint32_t)off;
+}
+
+int finish_setup(ll_engine *e)
+{
+    const PlanResult &pr = e->plan;
+    Params &p = e->base;
+    e->grid = pr.S * pr.C;
+    p.mb = e->mb_dev;
+    p.mb_x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(e->mb_dev) + sizeof(ll_tick_header));
+    p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + sizeof(ll_tick_header) +
+                                       sizeof(float) * (size_t)e->in_dim * e->max_batch);
+    p.ctrl = e->ctrl_dev;
+    p.poll_mode = e->opts.poll_mode;
+    p.idle_ns = e->opts.idle_timeout_ns;
+    p.step_ns = e->opts.step_timeout_ns;
+    p.peer_margin_ns = 2ull * 1000 * 1000 * 1000;
+    // device words
+    LL_CUDA_TRY(cudaMalloc((void **)&e->d_words, sizeof(unsigned) * (4 * kMaxStages + 8)));
+    p.xfer_cnt = e->d_words;
+    p.xfer_hdr = e->d_words + kMaxStages;
+    p.abort_flag = e->d_words + 3 * kMaxStages;
+    p.q_done = e->d_words + 3 * kMaxStages + 1;
+    if (pr.S > 1) {
+        size_t stride = 0;
+        for (int l = 0; l < (int)pr.L.size(); ++l)
+            if (pr.L[l].mode == LM_ROWSPLIT_GLOBAL)
+                stride = std::max(stride, (size_t)p.bmax4 * pr.L[l].Mp);
+        stride = llh::round_up(stride, 64);
+        LL_CUDA_TRY(cudaMalloc((void **)&e->d_xfer, sizeof(float) * stride * pr.S));
+        LL_CUDA_TRY(cudaMemset(e->d_xfer, 0, sizeof(float) * stride * pr.S));
+        p.xfer = e->d_xfer;
+        p.xfer_stride = (uint32_t)stride;
+    }
+    LL_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    return LL_OK;
+}
+
+int set_kernel_attrs(ll_engine *e)
+{
+    if (e->attrs_set)
+        return LL_OK;
+    LL_CUDA_TRY(cudaFuncSetAttribute(ll_resident_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)e->base.smem_bytes));
+    if (e->base.C > 8)
+        LL_CUDA_TRY(cudaFuncSetAttribute(ll_resident_mlp_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    e->attrs_set = true;
+    return LL_OK;
+}
+
+int launch(ll_engine *e, const Params &p)
+{
+    int rc = set_kernel_attrs(e);
+    if (rc)
+        return rc;
+    LL_CUDA_TRY(cudaMemsetAsync(e->d_words, 0, sizeof(unsigned) * (4 * kMaxStages + 8), e->stream));
+    e->ctrl_host->state = ST_IDLE;
+    e->ctrl_host->status = LL_OK;
+    e->ctrl_host->err_where = 0;
+    e->ctrl_host->exit_reason = EXIT_NONE;
+    e->ctrl_host->served = p.last_seq;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)e->grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = p.smem_bytes;
+    cfg.stream = e->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int max_clusters = 0;
+    cudaError_t oe = cudaOccupancyMaxActiveClusters(&max_clusters, ll_resident_mlp_kernel, &cfg);
+    if (oe != cudaSuccess || max_clusters < p.n_stages) {
+        llh::set_error("resident kernel needs %d co-resident clusters of %d CTAs (%u B smem); device fits %d (%s)",
+                       p.n_stages, p.C, p.smem_bytes, max_clusters, cudaGetErrorString(oe));
+        cudaGetLastError();
+        return LL_ERR_BAD_DESC;
+    }
+    LL_CUDA_TRY(cudaLaunchKernelEx(&cfg, ll_resident_mlp_kernel, p));
+    ++e->launches;
+    return LL_OK;
+}
+
+// Collect a finished launch: returns LL_OK or LL_ERR_DEVICE_FAULT / LL_ERR_CUDA.
+int reap(ll_engine *e)
+{
+    cudaError_t ce = cudaStreamSynchronize(e->stream);
+    e->running = false;
+    if (ce != cudaSuccess) {
+        llh::set_error("resident kernel failed: %s", cudaGetErrorString(ce));
+        e->last_status = LL_ERR_CUDA;
+        return LL_ERR_CUDA;
+    }
+    e->last_served = e->ctrl_host->served;
+    if (e->ctrl_host->status != LL_OK) {
+        llh::set_error("resident kernel reported status %u at location 0x%x", e->ctrl_host->status,
+                       e->ctrl_host->err_where);
+        e->last_status = (int)e->ctrl_host->status;
+        return LL_ERR_DEVICE_FAULT;
+    }
+    return LL_OK;
+}
+
+int ensure_running(ll_engine *e)
+{
+    if (e->running) {
+        if (e->ctrl_host->state != ST_EXITED)
+            return LL_OK;
+        int rc = reap(e);
+        if (rc)
+            return rc;
+    }
+    LL_CUDA_TRY(cudaSetDevice(e->device));
+    Params p = e->base;
+    p.mode = MODE_MAILBOX;
+    p.last_seq = e->last_served;
+    // make sure the doorbell state is consistent: seq_out == last served
+    int rc = launch(e, p);
+    if (rc)
+        return rc;
+    e->running = true;
+    // wait until the weights are resident (bounded)
+    const auto t0 = std::chrono::steady_clock::now();
+    while (e->ctrl_host->state < ST_RUNNING) {
+        cpu_relax();
+        if (cudaStreamQuery(e->stream) != cudaErrorNotReady) {
+            int r2 = reap(e);
+            if (r2 == LL_OK) {
+                llh::set_error("resident kernel exited during start-up (exit reason %u)", e->ctrl_host->exit_reason);
+                return LL_ERR_DEVICE_FAULT;
+            }
+            return r2;
+        }
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10)) {
+            llh::set_error("resident kernel did not report ready within 10 s");
+            return LL_ERR_TIMEOUT;
+        }
+    }
+    return LL_OK;
+}
+
+int engine_common_create(ll_engine *e, const ll_engine_opts *opts)
+{
+    if (opts)
+        e->opts = *opts;
+    else
+        ll_engine_opts_default(&e->opts);
+    if (e->opts.idle_timeout_ns == 0)
+        e->opts.idle_timeout_ns = 30ull * 1000 * 1000 * 1000;
+    if (e->opts.step_timeout_ns == 0)
+        e->opts.step_timeout_ns = 200ull * 1000 * 1000;
+    e->wc = e->opts.write_combined;
+    LL_CUDA_TRY(cudaSetDevice(e->device));
+    return alloc_mailbox(e);
+}
+
+// Spin on seq_out with liveness checks; copies y.
+int engine_wait(ll_engine *e, uint32_t seq, float *y, int n_rows, uint64_t timeout_ns)
+{
+    const ll_tick_header *h = static_cast<const ll_tick_header *>(e->mb_host);
+    const auto t0 = std::chrono::steady_clock::now();
+    uint32_t spins = 0;
+    while (__atomic_load_n(const_cast<const uint32_t *>(&h->seq_out), __ATOMIC_ACQUIRE) != seq) {
+        cpu_relax();
+        if ((++spins & 4095u) == 0) {
+            if (e->ctrl_host->state == ST_EXITED &&
+                __atomic_load_n(const_cast<const uint32_t *>(&h->seq_out), __ATOMIC_ACQUIRE) != seq) {
+                // kernel left (idle exit raced this request, or a fault): relaunch picks the request up
+                int rc = ensure_running(e);
+                if (rc)
+                    return rc;
+            }
+            const auto dt = std::chrono::steady_clock::now() - t0;
+            if ((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(dt).count() > timeout_ns) {
+                llh::set_error("request seq %u not answered within %llu ns (device state %u, status %u)", seq,
+                               (unsigned long long)timeout_ns, e->ctrl_host->state, e->ctrl_host->status);
+                return LL_ERR_TIMEOUT;
+            }
+        }
+    }
+    if (y) {
+        const float *yd = reinterpret_cast<const float *>(static_cast<const char *>(e->mb_host) +
+                                                          sizeof(ll_tick_header) +
+                                                          sizeof(float) * (size_t)e->in_dim * e->max_batch);
+        std::memcpy(y, yd, sizeof(float) * (size_t)e->out_dim * n_rows);
+    }
+    e->last_served = seq;
+    return LL_OK;
+}
+
+int engine_stop_kernel(ll_engine *e)
+{
+    if (!e->running)
+        return LL_OK;
+    if (e->outstanding) {
+        engine_wait(e, e->outstanding, nullptr, 1, 1000ull * 1000 * 1000);
+        e->outstanding = 0;
+    }
+    ll_tick_header *h = static_cast<ll_tick_header *>(e->mb_host);
+    __atomic_store_n(const_cast<uint32_t *>(&h->stop), 1u, __ATOMIC_RELEASE);
+    const auto t0 = std::chrono::steady_clock::now();
+    while (cudaStreamQuery(e->stream) == cudaErrorNotReady) {
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10)) {
+            llh::set_error("resident kernel did not stop within 10 s");
+            return LL_ERR_TIMEOUT;
+        }
+    }
+    int rc = reap(e);
+    __atomic_store_n(const_cast<uint32_t *>(&h->stop), 0u, __ATOMIC_RELEASE);
+    e->last_served = h->seq_out;
+    return rc;
+}
+
+struct Packed {
+    PlanResult pr;
+    Params p{};
+    std::vector<uint8_t> images;
+};
+
+// Plan, pack and lay out a net; touches no CUDA state.
+int plan_and_pack(const ll_net_desc *net, const void *const *W, const float *const *b, const float *const *scales,
+                  const ll_engine_opts &o, bool want_images, Packed &pk)
+{
+    int rc = validate_net(net, want_images ? W : nullptr);
+    if (rc)
+        return rc;
+    if (want_images && !W) {
+        llh::set_error("W is NULL");
+        return LL_ERR_INVALID_ARG;
+    }
+    if (want_images && net->layers[0].wtype == LL_W_I8 && !scales) {
+        llh::set_error("int8 weights need per-channel scales");
+        return LL_ERR_INVALID_ARG;
+    }
+    int C = o.cluster_size == 0 ? 16 : o.cluster_size;
+    if (C != 1 && C != 2 && C != 4 && C != 8 && C != 16) {
+        llh::set_error("cluster_size must be 1, 2, 4, 8 or 16");
+        return LL_ERR_INVALID_ARG;
+    }
+    const int max_stages = o.max_stages > 0 ? std::min(o.max_stages, kMaxStages) : kMaxStages;
+    if (!plan_net(*net, C, o.replicate_first, o.min_stages, max_stages, pk.pr)) {
+        llh::set_error("network does not fit %d stages of %d CTAs in shared memory", max_stages, C);
+        return LL_ERR_BAD_DESC;
+    }
+    const PlanResult &pr = pk.pr;
+    Params &p = pk.p;
+    p.n_layers = net->n_layers;
+    p.act_bf16 = net->layers[0].wtype != LL_W_F32;
+    layout_buffers(p, pr, net->layers[0].in_dim, net->layers[net->n_layers - 1].out_dim, net->max_batch);
+    size_t stride = 16;
+    for (size_t v : pr.stage_image)
+        stride = std::max(stride, llh::round_up(v, 16));
+    p.image_stride = (uint32_t)stride;
+    std::vector<uint32_t> w_off(net->n_layers), b_off(net->n_layers), s_off(net->n_layers);
+    if (want_images)
+        pk.images.assign((size_t)pr.S * pr.C * stride, 0);
+    for (int s = 0; s < pr.S; ++s)
+        for (int r = 0; r < pr.C; ++r) {
+            if (want_images)
+                pack_image(*net, pr, s, r, W, b, scales, pk.images.data() + ((size_t)s * pr.C + r) * stride, w_off,
+                           b_off, s_off);
+            else if (r == 0)
+                pack_image(*net, pr, s, r, nullptr, nullptr, nullptr, nullptr, w_off, b_off, s_off);
+        }
+    for (int l = 0; l < net->n_layers; ++l) {
+        const LayerPlan &lp = pr.L[l];
+        LayerDev &d = p.L[l];
+        d.mode = lp.mode;
+        d.act = lp.act;
+        d.wtype = lp.wtype;
+        d.lpr_log2 = choose_lpr_log2(lp.K, lp.wtype);
+        d.K = lp.K;
+        d.M = lp.out;
+        d.Mp = lp.Mp;
+        d.R = lp.R;
+        d.in_buf = lp.in_buf;
+        d.in_ld = lp.in_ld;
+        d.out_buf = lp.out_buf;
+        d.out_ld = lp.out_ld;
+        d.w_off = w_off[l];
+        d.b_off = b_off[l];
+        d.s_off = s_off[l];
+        d.round_out = (p.act_bf16 && l + 1 < net->n_layers) ? 1 : 0;
+    }
+    return LL_OK;
+}
+
+void export_plan(const Params &p, ll_plan *out)
+{
+    std::memset(out, 0, sizeof(*out));
+    out->n_layers = p.n_layers;
+    out->n_stages = p.n_stages;
+    out->cluster_size = p.C;
+    out->threads = kThreads;
+    out->bmax4 = p.bmax4;
+    out->in_ld = p.in_ld;
+    out->act_bf16 = p.act_bf16;
+    for (int s = 0; s < kMaxStages; ++s) {
+        out->stage_first[s] = p.stage_first[s];
+        out->stage_last[s] = p.stage_last[s];
+        out->stage_in_ld[s] = p.stage_in_ld[s];
+        out->image_bytes[s] = p.image_bytes[s];
+    }
+    for (int i = 0; i < BUF_COUNT; ++i)
+        out->buf_off[i] = p.buf_off[i];
+    out->smem_bytes = p.smem_bytes;
+    out->image_stride = p.image_stride;
+    for (int l = 0; l < p.n_layers && l < 24; ++l) {
+        const LayerDev &d = p.L[l];
+        ll_plan_layer &o = out->layers[l];
+        o.mode = d.mode;
+        o.act = d.act;
+        o.wtype = d.wtype;
+        o.lpr_log2 = d.lpr_log2;
+        o.K = d.K;
+        o.M = d.M;
+        o.Mp = d.Mp;
+        o.R = d.R;
+        o.in_buf = d.in_buf;
+        o.in_ld = d.in_ld;
+        o.out_buf = d.out_buf;
+        o.out_ld = d.out_ld;
+        o.w_off = d.w_off;
+        o.b_off = d.b_off;
+        o.s_off = d.s_off;
+        o.round_out = d.round_out;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int ll_engine_create_ex(const ll_net_desc *net, const void *const *W, const float *const *b,
+                        const float *const *scales, int device, const ll_engine_opts *opts, ll_engine **out)
+{
+    if (!out) {
+        llh::set_error("out is NULL");
+        return LL_ERR_INVALID_ARG;
+    }
+    *out = nullptr;
+    ll_engine_opts o;
+    if (opts)
+        o = *opts;
+    else
+        ll_engine_opts_default(&o);
+    Packed pk;
+    int rc = plan_and_pack(net, W, b, scales, o, true, pk);
+    if (rc)
+        return rc;
+    ll_engine *e = new ll_engine();
+    e->device = device;
+    e->in_dim = net->layers[0].in_dim;
+    e->out_dim = net->layers[net->n_layers - 1].out_dim;
+    e->max_batch = net->max_batch;
+    rc = engine_common_create(e, &o);
+    if (rc) {
+        ll_engine_destroy(e);
+        return rc;
+    }
+    e->plan = pk.pr;
+    e->base = pk.p;
+    cudaError_t ce = cudaMalloc((void **)&e->d_image, pk.images.size());
+    if (ce == cudaSuccess)
+        ce = cudaMemcpy(e->d_image, pk.images.data(), pk.images.size(), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        llh::set_error("uploading weight images: %s", cudaGetErrorString(ce));
+        ll_engine_destroy(e);
+        return LL_ERR_CUDA;
+    }
+    e->base.image = e->d_image;
+    rc = finish_setup(e);
+    if (rc) {
+        ll_engine_destroy(e);
+        return rc;
+    }
+    *out = e;
+    return LL_OK;
+}
+
+int ll_plan_net(const ll_net_desc *net, const void *const *W, const float *const *b, const float *const *scales,
+                const ll_engine_opts *opts, ll_plan *plan, uint8_t *images, size_t images_cap, size_t *images_bytes)
+{
+    ll_engine_opts o;
+    if (opts)
+        o = *opts;
+    else
+        ll_engine_opts_default(&o);
+    Packed pk;
+    int rc = plan_and_pack(net, W, b, scales, o, images != nullptr, pk);
+    if (rc)
+        return rc;
+    const size_t need = (size_t)pk.pr.S * pk.pr.C * pk.p.image_stride;
+    if (images_bytes)
+        *images_bytes = need;
+    if (plan)
+        export_plan(pk.p, plan);
+    if (images) {
+        if (images_cap < need) {
+            llh::set_error("images buffer too small: %zu < %zu", images_cap, need);
+            return LL_ERR_INVALID_ARG;
+        }
+        std::memcpy(images, pk.images.data(), need);
+    }
+    return LL_OK;
+}
+
+int ll_engine_create(const ll_net_desc *net, const void *const *W, const float *const *b, const float *const *scales,
+                     int device, ll_engine **out)
+{
+    return ll_engine_create_ex(net, W, b, scales, device, nullptr, out);
+}
+
+int ll_echo_engine_create(int device, int in_dim, int out_dim, const ll_engine_opts *opts, ll_engine **out)
+{
+    if (!out || in_dim < 0 || out_dim < 0 || in_dim > 16384 || out_dim > 16384) {
+        llh::set_error("invalid echo engine arguments");
+        return LL_ERR_INVALID_ARG;
+    }
+    *out = nullptr;
+    ll_engine *e = new ll_engine();
+    e->device = device;
+    e->echo = true;
+    e->in_dim = in_dim;
+    e->out_dim = out_dim;
+    e->max_batch = 1;
+    int rc = engine_common_create(e, opts);
+    if (rc) {
+        ll_engine_destroy(e);
+        return rc;
+    }
+    PlanResult &pr = e->plan;
+    pr.S = 1;
+    pr.C = 1;
+    pr.stage_first = {0};
+    pr.stage_last = {-1};
+    pr.stage_in_ld = {(int)llh::round_up((size_t)std::max(in_dim, 4), 4)};
+    pr.stage_image = {0};
+    pr.buf_floats[BUF_X] = 4 * (size_t)pr.stage_in_ld[0];
+    e->base.n_layers = 0;
+    layout_buffers(e->base, pr, in_dim, out_dim, 1);
+    rc = finish_setup(e);
+    if (rc) {
+        ll_engine_destroy(e);
+        return rc;
+    }
+    *out = e;
+    return LL_OK;
+}
+
+void *ll_engine_mailbox(ll_engine *e)
+{
+    return e ? e->mb_host : nullptr;
+}
+
+float *ll_engine_mailbox_x(ll_engine *e)
+{
+    return e ? reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + sizeof(ll_tick_header)) : nullptr;
+}
+
+float *ll_engine_mailbox_y(ll_engine *e)
+{
+    return e ? reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + sizeof(ll_tick_header) +
+                                         sizeof(float) * (size_t)e->in_dim * e->max_batch)
+             : nullptr;
+}
+
+int ll_engine_start(ll_engine *e)
+{
+    if (!e) {
+        llh::set_error("engine is NULL");
+        return LL_ERR_INVALID_ARG;
+    }
+    return ensure_running(e);
+}
+
+int ll_submit(ll_engine *e, const float *x, int n_rows, uint32_t *seq)
+{
+    if (!e || n_rows < 1 || n_rows > e->max_batch) {
+        llh::set_error("ll_submit: bad engine or n_rows %d (max %d)", n_rows, e ? e->max_batch : 0);
+        return LL_ERR_INVALID_ARG;
+    }
+    if (e->outstanding) {
+        llh::set_error("ll_submit: request %u still outstanding (single-slot mailbox)", e->outstanding);
+        return LL_ERR_BUSY;
+    }
+    int rc = ensure_running(e);
+    if (rc)
+        return rc;
+    const uint32_t s = ll_next_seq(e->last_served > e->seq ? e->last_served : e->seq);
+    ll_mailbox_post(e->mb_host, e->in_dim, x, n_rows, s, e->wc);
+    e->seq = s;
+    e->outstanding = s;
+    if (seq)
+        *seq = s;
+    return LL_OK;
+}
+
+int ll_poll(ll_engine *e, uint32_t seq, float *y, uint64_t timeout_ns)
+{
+    if (!e) {
+        llh::set_error("engine is NULL");
+        return LL_ERR_INVALID_ARG;
+    }
+    const ll_tick_header *h = static_cast<const ll_tick_header *>(e->mb_host);
+    const int n_rows = h->n_rows == 0 ? 1 : (int)h->n_rows;
+    int rc = engine_wait(e, seq, y, n_rows, timeout_ns);
+    if (rc == LL_OK && e->outstanding == seq)
+        e->outstanding = 0;
+    return rc;
+}
+
+int ll_infer(ll_engine *e, const float *x, int n_rows, float *y, uint64_t timeout_ns)
+{
+    uint32_t s = 0;
+    int rc = ll_submit(e, x, n_rows, &s);
+    if (rc)
+        return rc;
+    return ll_poll(e, s, y, timeout_ns);
+}
+
+int ll_engine_stop(ll_engine *e)
+{
+    if (!e) {
+        llh::set_error("engine is NULL");
+        return LL_ERR_INVALID_ARG;
+    }
+    cudaSetDevice(e->device);
+    return engine_stop_kernel(e);
+}
+
+int ll_engine_destroy(ll_engine *e)
+{
+    if (!e)
+        return LL_OK;
+    cudaSetDevice(e->device);
+    int rc = LL_OK;
+    if (e->running)
+        rc = engine_stop_kernel(e);
+    if (e->stream)
+        cudaStreamDestroy(e->stream);
+    if (e->d_image)
+        cudaFree(e->d_image);
+    if (e->d_xfer)
+        cudaFree(e->d_xfer);
+    if (e->d_words)
+        cudaFree(e->d_words);
+    if (e->mb_host)
+        cudaFreeHost(e->mb_host);
+    if (e->ctrl_host)
+        cudaFreeHost((void *)e->ctrl_host);
+    delete e;
+    return rc;
+}
+
+int ll_engine_get_info(ll_engine *e, ll_engine_info *info)
+{
+    if (!e || !info) {
+        llh::set_error("NULL argument");
+        return LL_ERR_INVALID_ARG;
+    }
+    std::memset(info, 0, sizeof(*info));
+    info->n_stages = e->plan.S;
+    info->cluster_size = e->plan.C;
+    info->threads = kThreads;
+    info->smem_bytes = (int32_t)e->base.smem_bytes;
+    size_t mi = 0;
+    for (size_t v : e->plan.stage_image)
+        mi = std::max(mi, v);
+    info->image_bytes = (int32_t)mi;
+    info->launches = e->launches;
+    info->state = (int32_t)e->ctrl_host->state;
+    info->status = (int32_t)e->ctrl_host->status;
+    info->err_where = (int32_t)e->ctrl_host->err_where;
+    info->served = e->ctrl_host->served;
+    for (int l = 0; l < e->base.n_layers && l < 24; ++l)
+        info->layer_modes[l] = e->base.L[l].mode;
+    return LL_OK;
+}
+
+int ll_engine_bench_closed_loop(ll_engine *e, const float *xs, int n_x, int n_req, int n_rows, float *ys,
+                                double *lat_us)
+{
+    if (!e || !xs || n_x < 1 || n_req < 0 || n_rows < 1 || n_rows > e->max_batch) {
+        llh::set_error("ll_engine_bench_closed_loop: invalid arguments");
+        return LL_ERR_INVALID_ARG;
+    }
+    if (e->outstanding) {
+        llh::set_error("request outstanding");
+        return LL_ERR_BUSY;
+    }
+    int rc = ensure_running(e);
+    if (rc)
+        return rc;
+    const size_t xin = (size_t)e->in_dim * n_rows;
+    const size_t yout = (size_t)e->out_dim * n_rows;
+    std::vector<float> ybuf(yout);
+    for (int r = 0; r < n_req; ++r) {
+        const auto t0 = std::chrono::steady_clock::now();
+        const uint32_t s = ll_next_seq(e->last_served > e->seq ? e->last_served : e->seq);
+        ll_mailbox_post(e->mb_host, e->in_dim, xs + (size_t)(r % n_x) * xin, n_rows, s, e->wc);
+        e->seq = s;
+        e->outstanding = s;
+        rc = engine_wait(e, s, ys ? ys + (size_t)r * yout : ybuf.data(), n_rows, 2000ull * 1000 * 1000);
+        const auto t1 = std::chrono::steady_clock::now();
+        if (rc)
+            return rc;
+        e->outstanding = 0;
+        if (lat_us)
+            lat_us[r] = std::chrono::duration<double, std::micro>(t1 - t0).count();
+    }
+    return LL_OK;
+}
+
+int ll_engine_run_queue(ll_engine *e, const float *d_x, float *d_y, int n_req, int n_rows, float *ms,
+                        unsigned long long *d_stamps)
+{
+    if (!e || !d_x || !d_y || n_req < 1 || n_rows < 1 || n_rows > e->max_batch) {
+        llh::set_error("ll_engine_run_queue: invalid arguments");
+        return LL_ERR_INVALID_ARG;
+    }
+    LL_CUDA_TRY(cudaSetDevice(e->device));
+    int rc = engine_stop_kernel(e);
+    if (rc)
+        return rc;
+    Params p = e->base;
+    p.mode = MODE_QUEUE;
+    p.q_x = d_x;
+    p.q_y = d_y;
+    p.q_n = n_req;
+    p.q_rows = n_rows;
+    p.q_stamp = d_stamps;
+    cudaEvent_t a, b;
+    LL_CUDA_TRY(cudaEventCreate(&a));
+    LL_CUDA_TRY(cudaEventCreate(&b));
+    LL_CUDA_TRY(cudaEventRecord(a, e->stream));
+    rc = launch(e, p);
+    if (rc) {
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        return rc;
+    }
+    LL_CUDA_TRY(cudaEventRecord(b, e->stream));
+    e->running = true;
+    rc = reap(e);
+    float t = 0;
+    cudaEventElapsedTime(&t, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    if (ms)
+        *ms = t;
+    // the mailbox kernel is relaunched lazily; its doorbell baseline is unchanged
+    e->last_served = static_cast<ll_tick_header *>(e->mb_host)->seq_out;
+    return rc;
+}
+
+}  // extern "C"

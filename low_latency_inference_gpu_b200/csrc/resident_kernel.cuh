@@ -1,0 +1,709 @@
+// The resident (persistent) MLP kernel for sm_100a.
+//
+// One launch serves requests until told to stop.  The grid is n_stages
+// thread-block clusters of C CTAs (one CTA per SM).  Each CTA holds a slice of
+// its stage's layers in shared memory for the whole launch (the reference keeps
+// weights "resident" in registers / SMEM / global scratch per thread,
+// include/ll/weights_storage.cuh:7-240; here the slice is one bulk-copied SMEM
+// image).  Per request:
+//   stage 0  : every CTA polls the mailbox (host-mapped TickBuffer,
+//              src/bench_persistent_mbyv_mlp.cu:229-281) and reads x itself;
+//   layers   : row-split GEMV from SMEM, outputs pushed to peer CTAs with
+//              st.async + mbarrier complete_tx (DSMEM) instead of the
+//              reference's global-atomic layer barriers (:308-377);
+//   boundary : between clusters, rows go through L2 with a release counter;
+//   output   : last layer as K-split partials gathered at rank 0, which writes
+//              y and release-stores seq_out (:365-370).
+// Every wait is bounded by %globaltimer and reports an error status instead of
+// spinning forever (the reference spins unboundedly, :232-247).
+#pragma once
+#include <cuda_bf16.h>
+
+#include "engine_types.h"
+#include "ptx.cuh"
+
+namespace llk {
+
+constexpr uint32_t kCmdExit = 0u;  // 0 is never a live sequence number
+
+struct Shared {
+    uint64_t bar[5];  // 0 image load, 1 buffer A, 2 buffer B, 3 gather G, 4 queue go
+    uint32_t cmd;
+    uint32_t nrows;
+    uint32_t fail;
+    uint32_t abort;
+};
+
+__device__ __forceinline__ float act_apply(float v, int act)
+{
+    if (act == LL_ACT_RELU)
+        return v > 0.0f ? v : 0.0f;
+    if (act == LL_ACT_GELU)
+        return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+    return v;
+}
+
+__device__ __forceinline__ float round_bf16(float v)
+{
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// Load one 16-byte weight unit from shared memory as floats.
+template <int WT>
+__device__ __forceinline__ void load_unit(const uint8_t *p, float *w)
+{
+    if constexpr (WT == LL_W_F32) {
+        float4 v = *reinterpret_cast<const float4 *>(p);
+        w[0] = v.x;
+        w[1] = v.y;
+        w[2] = v.z;
+        w[3] = v.w;
+    } else if constexpr (WT == LL_W_BF16) {
+        uint4 u = *reinterpret_cast<const uint4 *>(p);
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w[2 * i] = __uint_as_float(q[i] << 16);
+            w[2 * i + 1] = __uint_as_float(q[i] & 0xffff0000u);
+        }
+    } else {
+        uint4 u = *reinterpret_cast<const uint4 *>(p);
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                w[4 * i + j] = static_cast<float>(static_cast<int8_t>((q[i] >> (8 * j)) & 0xffu));
+        }
+    }
+}
+
+template <int WT>
+struct UnitInfo {
+    static constexpr int elems = WT == LL_W_F32 ? 4 : (WT == LL_W_BF16 ? 8 : 16);
+    static constexpr int wbytes = WT == LL_W_F32 ? 4 : (WT == LL_W_BF16 ? 2 : 1);
+};
+
+// dot(W[r, 0:K], in[b, 0:K]) for r < R, b < B, computed by `lpr` lanes per row
+// with a butterfly reduction; epi(b, r, value) runs on the row's first lane.
+template <int WT, int BB, class Epi>
+__device__ __forceinline__ void rows_dot(const uint8_t *W, int R, int K, const float *in, int in_ld, int B,
+                                         int lpr_log2, Epi &&epi)
+{
+    constexpr int E = UnitInfo<WT>::elems;
+    const int U = K / E;
+    const int lpr = 1 << lpr_log2;
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int sub = lane & (lpr - 1);
+    const int rpw = 32 >> lpr_log2;  // rows per warp pass
+    const size_t row_bytes = (size_t)K * UnitInfo<WT>::wbytes;
+    for (int b0 = 0; b0 < B; b0 += BB) {
+        for (int rb = warp * rpw; rb < R; rb += (kThreads / 32) * rpw) {
+            const int r = rb + (lane >> lpr_log2);
+            const bool valid = r < R;
+            const int rr = valid ? r : R - 1;
+            const uint8_t *wrow = W + (size_t)rr * row_bytes;
+            float acc[BB];
+#pragma unroll
+            for (int bb = 0; bb < BB; ++bb)
+                acc[bb] = 0.0f;
+            for (int u = sub; u < U; u += lpr) {
+                float w[E];
+                load_unit<WT>(wrow + (size_t)u * 16, w);
+#pragma unroll
+                for (int bb = 0; bb < BB; ++bb) {
+                    const float *xr = in + (size_t)(b0 + bb) * in_ld + u * E;
+#pragma unroll
+                    for (int e = 0; e < E; e += 4) {
+                        const float4 x4 = *reinterpret_cast<const float4 *>(xr + e);
+                        acc[bb] = fmaf(w[e], x4.x, acc[bb]);
+                        acc[bb] = fmaf(w[e + 1], x4.y, acc[bb]);
+                        acc[bb] = fmaf(w[e + 2], x4.z, acc[bb]);
+                        acc[bb] = fmaf(w[e + 3], x4.w, acc[bb]);
+                    }
+                }
+            }
+            for (int off = lpr >> 1; off > 0; off >>= 1) {
+#pragma unroll
+                for (int bb = 0; bb < BB; ++bb)
+                    acc[bb] += __shfl_xor_sync(0xffffffffu, acc[bb], off);
+            }
+            if (valid && sub == 0) {
+#pragma unroll
+                for (int bb = 0; bb < BB; ++bb)
+                    if (b0 + bb < B)
+                        epi(b0 + bb, r, acc[bb]);
+            }
+        }
+    }
+}
+
+template <int BB, class Epi>
+__device__ __forceinline__ void rows_dot_any(int wtype, const uint8_t *W, int R, int K, const float *in, int in_ld,
+                                             int B, int lpr_log2, Epi &&epi)
+{
+    if (wtype == LL_W_BF16)
+        rows_dot<LL_W_BF16, BB>(W, R, K, in, in_ld, B, lpr_log2, epi);
+    else if (wtype == LL_W_I8)
+        rows_dot<LL_W_I8, BB>(W, R, K, in, in_ld, B, lpr_log2, epi);
+    else
+        rows_dot<LL_W_F32, BB>(W, R, K, in, in_ld, B, lpr_log2, epi);
+}
+
+template <class Epi>
+__device__ __forceinline__ void layer_dot(int wtype, const uint8_t *W, int R, int K, const float *in, int in_ld,
+                                          int B, int lpr_log2, Epi &&epi)
+{
+    if (B == 1)
+        rows_dot_any<1>(wtype, W, R, K, in, in_ld, 1, lpr_log2, epi);
+    else
+        rows_dot_any<4>(wtype, W, R, K, in, in_ld, B, lpr_log2, epi);
+}
+
+struct KernelCtx {
+    const Params *p;
+    Shared *sh;
+    uint8_t *smem;
+    uint32_t rank;
+    int stage;
+};
+
+// Record a device error (first writer wins is not needed: status is sticky per launch).
+__device__ __forceinline__ void report_error(const KernelCtx &k, uint32_t status, uint32_t where)
+{
+    st_relaxed_sys_u32(&k.p->ctrl->err_where, where);
+    st_relaxed_sys_u32(&k.p->ctrl->status, status);
+}
+
+// Tell every CTA of this cluster, and the other clusters, to leave the loop.
+__device__ __forceinline__ void broadcast_abort(const KernelCtx &k)
+{
+    const uint32_t a = smem_u32(&k.sh->abort);
+    for (int r = 0; r < k.p->C; ++r)
+        st_cluster_u32(mapa(a, (uint32_t)r), 1u);
+    atomicExch(k.p->abort_flag, 1u);
+}
+
+// All threads wait for an mbarrier phase; bounded; consistent verdict for the CTA.
+__device__ __forceinline__ bool cta_wait_bar(const KernelCtx &k, uint32_t bar, uint32_t parity, uint32_t where)
+{
+    const uint64_t deadline = globaltimer() + k.p->step_ns;
+    uint32_t r = 0;
+    for (uint32_t it = 0;; ++it) {
+        if (mbar_try_wait(bar, parity))
+            break;
+        if (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort)) {
+            r = 1;
+            break;
+        }
+        if ((it & 15u) == 15u && globaltimer() > deadline) {
+            r = 2;
+            break;
+        }
+    }
+    if (r)
+        atomicOr(&k.sh->fail, r);
+    __syncthreads();
+    const uint32_t f = *reinterpret_cast<volatile uint32_t *>(&k.sh->fail);
+    if (f != 0 && threadIdx.x == 0 && (f & 2u)) {
+        report_error(k, LL_ERR_DEVICE_FAULT, where);
+        broadcast_abort(k);
+    }
+    return f == 0;
+}
+
+__device__ __forceinline__ bool global_abort(const KernelCtx &k)
+{
+    return ld_relaxed_gpu_u32(k.p->abort_flag) != 0;
+}
+
+// Thread 0 of a stage-0 CTA: wait for a new request in the mailbox.
+// Returns the sequence number, or kCmdExit.  Leader (rank 0) alone honours
+// `stop` and the idle timeout; the others follow the leader's abort broadcast.
+__device__ uint32_t poll_mailbox(const KernelCtx &k, uint32_t last, bool leader, uint32_t *nrows)
+{
+    const Params &p = *k.p;
+    volatile uint32_t *seq_in = &p.mb->seq_in;
+    const uint64_t t0 = globaltimer();
+    const uint64_t bound = leader ? p.idle_ns : p.idle_ns + p.peer_margin_ns;
+    uint32_t s = 0;
+    bool found = false;
+    if (p.poll_mode == 1) {
+        // Four relaxed loads kept in flight, re-issued as each returns.
+        uint32_t v0 = ld_relaxed_sys(seq_in);
+        __nanosleep(100);
+        uint32_t v1 = ld_relaxed_sys(seq_in);
+        __nanosleep(100);
+        uint32_t v2 = ld_relaxed_sys(seq_in);
+        __nanosleep(100);
+        uint32_t v3 = ld_relaxed_sys(seq_in);
+        for (uint32_t it = 0;; ++it) {
+            if (v0 != last && v0 != 0) { s = v0; found = true; break; }
+            v0 = ld_relaxed_sys(seq_in);
+            if (v1 != last && v1 != 0) { s = v1; found = true; break; }
+            v1 = ld_relaxed_sys(seq_in);
+            if (v2 != last && v2 != 0) { s = v2; found = true; break; }
+            v2 = ld_relaxed_sys(seq_in);
+            if (v3 != last && v3 != 0) { s = v3; found = true; break; }
+            v3 = ld_relaxed_sys(seq_in);
+            if ((it & 7u) == 7u) {
+                if (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort) || global_abort(k))
+                    return kCmdExit;
+                if (leader && ld_relaxed_sys(&p.mb->stop)) {
+                    st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
+                    return kCmdExit;
+                }
+                if (globaltimer() - t0 > bound)
+                    break;
+            }
+        }
+        if (found)
+            fence_acq_rel_sys();
+    } else {
+        for (uint32_t it = 0;; ++it) {
+            const uint32_t v = ld_acquire_sys(seq_in);
+            if (v != last && v != 0) {
+                s = v;
+                found = true;
+                break;
+            }
+            if ((it & 31u) == 31u) {
+                if (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort) || global_abort(k))
+                    return kCmdExit;
+                if (leader && ld_relaxed_sys(&p.mb->stop)) {
+                    st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
+                    return kCmdExit;
+                }
+                if (globaltimer() - t0 > bound)
+                    break;
+            }
+        }
+    }
+    if (!found) {
+        if (leader) {
+            st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_IDLE);
+        } else {
+            report_error(k, LL_ERR_DEVICE_FAULT, EW_PEER_POLL);
+        }
+        return kCmdExit;
+    }
+    // A new sequence number together with `stop` is the reference's stop
+    // doorbell (stop = 1, then seq_in = ++seq; src/bench_persistent_mbyv_mlp.cu:554-557).
+    if (leader && ld_relaxed_sys(&p.mb->stop)) {
+        st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
+        return kCmdExit;
+    }
+    uint32_t n = ld_relaxed_sys(&p.mb->n_rows);
+    n = n == 0 ? 1u : n;
+    *nrows = n > (uint32_t)p.max_batch ? (uint32_t)p.max_batch : n;
+    return s;
+}
+
+__device__ __forceinline__ float *buf_ptr(const KernelCtx &k, int id)
+{
+    return reinterpret_cast<float *>(k.smem + k.p->buf_off[id]);
+}
+
+__device__ __forceinline__ uint32_t buf_addr(const KernelCtx &k, int id)
+{
+    return smem_u32(k.smem + k.p->buf_off[id]);
+}
+
+// Copy rows of a source vector into the X buffer (row stride in_ld), rounding to bf16 if asked.
+__device__ __forceinline__ void stage_input_mailbox(const KernelCtx &k, int nrows)
+{
+    const Params &p = *k.p;
+    float *X = buf_ptr(k, BUF_X);
+    const int in = p.in_dim;
+    if ((in & 3) == 0) {
+        const int q = in >> 2;
+        for (int t = threadIdx.x; t < nrows * q; t += kThreads) {
+            const int b = t / q, c = t - b * q;
+            float4 v = ld_relaxed_sys_v4(p.mb_x + (size_t)b * in + c * 4);
+            if (p.act_bf16) {
+                v.x = round_bf16(v.x);
+                v.y = round_bf16(v.y);
+                v.z = round_bf16(v.z);
+                v.w = round_bf16(v.w);
+            }
+            *reinterpret_cast<float4 *>(X + (size_t)b * p.in_ld + c * 4) = v;
+        }
+    } else {
+        for (int t = threadIdx.x; t < nrows * in; t += kThreads) {
+            const int b = t / in, c = t - b * in;
+            float v = ld_relaxed_sys_f32(p.mb_x + (size_t)b * in + c);
+            X[(size_t)b * p.in_ld + c] = p.act_bf16 ? round_bf16(v) : v;
+        }
+    }
+}
+
+__device__ __forceinline__ void stage_input_device(const KernelCtx &k, const float *src, int nrows)
+{
+    const Params &p = *k.p;
+    float *X = buf_ptr(k, BUF_X);
+    const int in = p.in_dim;
+    for (int t = threadIdx.x; t < nrows * in; t += kThreads) {
+        const int b = t / in, c = t - b * in;
+        float v = __ldg(src + (size_t)b * in + c);
+        X[(size_t)b * p.in_ld + c] = p.act_bf16 ? round_bf16(v) : v;
+    }
+}
+
+// Store helper for one finished output element of a row-split layer.
+struct EpiRows {
+    float *out;
+    int ld;
+    const float *bias;
+    const float *scale;
+    int act;
+    int round_out;
+    __device__ __forceinline__ void operator()(int b, int r, float acc) const
+    {
+        float v = scale ? acc * scale[r] : acc;
+        v = act_apply(v + bias[r], act);
+        out[(size_t)b * ld + r] = round_out ? round_bf16(v) : v;
+    }
+};
+
+struct EpiRaw {
+    float *out;
+    int ld;
+    __device__ __forceinline__ void operator()(int b, int r, float acc) const { out[(size_t)b * ld + r] = acc; }
+};
+
+// Push nrows x R floats from the staging buffer into `dst_buf` of cluster CTAs
+// [r_lo, r_hi) at column offset col0, completing tx on their `bar`.
+__device__ __forceinline__ void push_rows(const KernelCtx &k, const float *stage, int R, int nrows, uint32_t dst_base,
+                                          int dst_ld, int col0, uint32_t bar, int r_lo, int r_hi)
+{
+    const int n4 = R >> 2;
+    const int per = nrows * n4;
+    const int total = per * (r_hi - r_lo);
+    for (int t = threadIdx.x; t < total; t += kThreads) {
+        const int d = r_lo + t / per;
+        const int rem = t % per;
+        const int b = rem / n4, c4 = rem - b * n4;
+        const float4 v = *reinterpret_cast<const float4 *>(stage + (size_t)b * R + c4 * 4);
+        const uint32_t off = (uint32_t)(((size_t)b * dst_ld + col0 + c4 * 4) * 4);
+        st_async_v4(mapa(dst_base + off, (uint32_t)d), v, mapa(bar, (uint32_t)d));
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __grid_constant__ Params p)
+{
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) Shared sh;
+
+    KernelCtx k;
+    k.p = &p;
+    k.sh = &sh;
+    k.smem = smem;
+    k.rank = cluster_ctarank();
+    k.stage = (int)(blockIdx.x / (unsigned)p.C);
+    const int tid = threadIdx.x;
+    const bool leader = (k.stage == 0 && k.rank == 0);
+    const bool last_stage = (k.stage == p.n_stages - 1);
+    const bool final_writer = last_stage && k.rank == 0;
+    const uint32_t bar_load = smem_u32(&sh.bar[0]);
+    const uint32_t bar_ab[2] = {smem_u32(&sh.bar[1]), smem_u32(&sh.bar[2])};
+    const uint32_t bar_g = smem_u32(&sh.bar[3]);
+    const uint32_t bar_go = smem_u32(&sh.bar[4]);
+
+    if (tid == 0) {
+        for (int i = 0; i < 5; ++i)
+            mbar_init(smem_u32(&sh.bar[i]), 1);
+        sh.cmd = 0;
+        sh.nrows = 1;
+        sh.fail = 0;
+        sh.abort = 0;
+        fence_mbar_init_cluster();
+        if (leader)
+            st_relaxed_sys_u32(&p.ctrl->state, ST_LOADING);
+    }
+    // Zero all activation buffers once so padded columns are exact zeros.
+    {
+        const uint32_t img = p.image_bytes[k.stage];
+        uint4 *z = reinterpret_cast<uint4 *>(smem + p.buf_off[BUF_X]);
+        const uint32_t n16 = (p.smem_bytes - p.buf_off[BUF_X]) / 16;
+        for (uint32_t i = tid; i < n16; i += kThreads)
+            z[i] = make_uint4(0, 0, 0, 0);
+        (void)img;
+    }
+    __syncthreads();
+
+    bool ok = true;
+    const uint32_t img_bytes = p.image_bytes[k.stage];
+    if (img_bytes > 0) {
+        if (tid == 0) {
+            mbar_arrive_expect_tx(bar_load, img_bytes);
+            const uint8_t *src = p.image + (size_t)blockIdx.x * p.image_stride;
+            const uint32_t dst = smem_u32(smem);
+            for (uint32_t off = 0; off < img_bytes; off += 32768u) {
+                const uint32_t n = img_bytes - off < 32768u ? img_bytes - off : 32768u;
+                bulk_g2s(dst + off, src + off, n, bar_load);
+            }
+        }
+        ok = cta_wait_bar(k, bar_load, 0, EW_LOAD);
+    }
+    cluster_sync();  // barriers initialised and images resident in every CTA of the cluster
+    if (leader && tid == 0)
+        st_relaxed_sys_u32(&p.ctrl->state, ST_RUNNING);
+
+    uint32_t last = p.last_seq;
+    uint32_t n_done = 0;
+    uint32_t ph_ab[2] = {0, 0};
+    uint32_t ph_g = 0, ph_go = 0;
+    const int first_l = p.stage_first[k.stage];
+    const int last_l = p.stage_last[k.stage];
+
+    while (ok) {
+        // ---------------- 1. obtain the next request ----------------
+        uint32_t seq;
+        int nrows;
+        if (p.mode == MODE_QUEUE && (int)n_done >= p.q_n)
+            break;  // every stage knows the queue length
+        if (k.stage == 0) {
+            if (p.mode == MODE_QUEUE) {
+                if (n_done > 0) {
+                    if (p.n_stages == 1) {
+                        if (!cta_wait_bar(k, bar_go, ph_go & 1u, EW_QUEUE_GO))
+                            break;
+                        ++ph_go;
+                    } else {
+                        if (tid == 0) {
+                            const uint64_t deadline = globaltimer() + p.step_ns;
+                            uint32_t it = 0;
+                            while (ld_acquire_gpu(p.q_done) < n_done) {
+                                if ((++it & 31u) == 0 && (global_abort(k) || globaltimer() > deadline)) {
+                                    if (!global_abort(k)) {
+                                        report_error(k, LL_ERR_DEVICE_FAULT, EW_QUEUE_GO);
+                                        broadcast_abort(k);
+                                    }
+                                    sh.fail = 1;
+                                    break;
+                                }
+                            }
+                        }
+                        __syncthreads();
+                        if (sh.fail)
+                            break;
+                    }
+                }
+                seq = n_done + 1;
+                nrows = p.q_rows;
+                stage_input_device(k, p.q_x + (size_t)n_done * p.q_rows * p.in_dim, nrows);
+            } else {
+                if (tid == 0) {
+                    uint32_t nr = 1;
+                    const uint32_t c = poll_mailbox(k, last, leader, &nr);
+                    if (c == kCmdExit && leader)
+                        broadcast_abort(k);
+                    sh.cmd = c;
+                    sh.nrows = nr;
+                }
+                __syncthreads();
+                seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
+                nrows = (int)*reinterpret_cast<volatile uint32_t *>(&sh.nrows);
+                if (seq == kCmdExit)
+                    break;
+                stage_input_mailbox(k, nrows);
+            }
+        } else {
+            // Wait for the previous cluster's rows of this request (through L2).
+            if (tid == 0) {
+                const unsigned target = (unsigned)p.C * (n_done + 1u);
+                const unsigned *cnt = p.xfer_cnt + (k.stage - 1);
+                const uint64_t t0 = globaltimer();
+                uint32_t c = kCmdExit;
+                for (uint32_t it = 0;; ++it) {
+                    if (ld_acquire_gpu(cnt) >= target) {
+                        c = ld_relaxed_gpu_u32(p.xfer_hdr + 2 * (k.stage - 1));
+                        sh.nrows = ld_relaxed_gpu_u32(p.xfer_hdr + 2 * (k.stage - 1) + 1);
+                        break;
+                    }
+                    if ((it & 31u) == 31u) {
+                        if (sh.abort || global_abort(k))
+                            break;
+                        if (globaltimer() - t0 > p.idle_ns + 2 * p.peer_margin_ns) {
+                            report_error(k, LL_ERR_DEVICE_FAULT, EW_XFER);
+                            broadcast_abort(k);
+                            break;
+                        }
+                    }
+                }
+                sh.cmd = c;
+            }
+            __syncthreads();
+            seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
+            nrows = (int)*reinterpret_cast<volatile uint32_t *>(&sh.nrows);
+            if (seq == kCmdExit)
+                break;
+            const float *src = p.xfer + (size_t)(k.stage - 1) * p.xfer_stride;
+            float *X = buf_ptr(k, BUF_X);
+            const int ld = p.stage_in_ld[k.stage];
+            const int q = ld >> 2;
+            for (int t = tid; t < nrows * q; t += kThreads) {
+                const int b = t / q, c4 = t - b * q;
+                *reinterpret_cast<float4 *>(X + (size_t)b * ld + c4 * 4) = ld_cg_v4(src + (size_t)b * ld + c4 * 4);
+            }
+        }
+        __syncthreads();
+
+        // ---------------- 2. this stage's layers ----------------
+        for (int l = first_l; l <= last_l && ok; ++l) {
+            const LayerDev &L = p.L[l];
+            const uint8_t *W = smem + L.w_off;
+            const float *bias = reinterpret_cast<const float *>(smem + L.b_off);
+            const float *scale = L.s_off == 0xffffffffu ? nullptr : reinterpret_cast<const float *>(smem + L.s_off);
+            const float *in = buf_ptr(k, L.in_buf);
+            float *stg = buf_ptr(k, BUF_STAGE);
+            switch (L.mode) {
+            case LM_REPLICATED:
+            case LM_ROWSPLIT_LOCAL: {
+                EpiRows epi{buf_ptr(k, L.out_buf), L.out_ld, bias, scale, L.act, L.round_out};
+                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                __syncthreads();
+                break;
+            }
+            case LM_ROWSPLIT_ALLGATHER: {
+                EpiRows epi{stg, L.R, bias, scale, L.act, L.round_out};
+                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                __syncthreads();
+                const int bi = L.out_buf == BUF_A ? 0 : 1;
+                push_rows(k, stg, L.R, nrows, buf_addr(k, L.out_buf), L.out_ld, (int)k.rank * L.R, bar_ab[bi], 0,
+                          p.C);
+                if (tid == 0)
+                    mbar_arrive_expect_tx(bar_ab[bi], (uint32_t)(nrows * L.Mp * 4));
+                ok = cta_wait_bar(k, bar_ab[bi], ph_ab[bi] & 1u, EW_LAYER_BASE + (uint32_t)l);
+                ++ph_ab[bi];
+                break;
+            }
+            case LM_KSPLIT_GATHER: {
+                EpiRaw epi{stg, L.R};
+                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                __syncthreads();
+                // partials -> G[rank][b][OUTp] of rank 0
+                push_rows(k, stg, L.R, nrows, buf_addr(k, BUF_G) + k.rank * (uint32_t)(p.bmax4 * L.R * 4), L.R, 0,
+                          bar_g, 0, 1);
+                break;
+            }
+            case LM_ROWSPLIT_GATHER: {
+                EpiRows epi{stg, L.R, bias, scale, L.act, 0};
+                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                __syncthreads();
+                push_rows(k, stg, L.R, nrows, buf_addr(k, BUF_G), L.Mp, (int)k.rank * L.R, bar_g, 0, 1);
+                break;
+            }
+            case LM_ROWSPLIT_GLOBAL: {
+                EpiRows epi{stg, L.R, bias, scale, L.act, L.round_out};
+                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                __syncthreads();
+                float *dst = p.xfer + (size_t)k.stage * p.xfer_stride;
+                const int n4 = L.R >> 2;
+                for (int t = tid; t < nrows * n4; t += kThreads) {
+                    const int b = t / n4, c4 = t - b * n4;
+                    st_cg_v4(dst + (size_t)b * L.Mp + k.rank * L.R + c4 * 4,
+                             *reinterpret_cast<const float4 *>(stg + (size_t)b * L.R + c4 * 4));
+                }
+                if (tid == 0 && k.rank == 0) {
+                    st_relaxed_gpu_u32(p.xfer_hdr + 2 * k.stage, seq);
+                    st_relaxed_gpu_u32(p.xfer_hdr + 2 * k.stage + 1, (uint32_t)nrows);
+                }
+                __syncthreads();
+                if (tid == 0) {
+                    __threadfence();
+                    red_release_gpu_add(p.xfer_cnt + k.stage, 1u);
+                }
+                break;
+            }
+            default:
+                break;
+            }
+        }
+        if (!ok)
+            break;
+
+        // ---------------- 3. rank 0 of the last stage publishes ----------------
+        if (final_writer) {
+            const float *G;
+            bool ksplit = false;
+            int ld_g = 0;
+            const LayerDev *Lf = nullptr;
+            if (p.n_layers > 0) {
+                Lf = &p.L[p.n_layers - 1];
+                ksplit = Lf->mode == LM_KSPLIT_GATHER;
+                ld_g = Lf->mode == LM_KSPLIT_GATHER ? Lf->R : Lf->Mp;
+                const uint32_t bytes = ksplit ? (uint32_t)(p.C * nrows * Lf->R * 4) : (uint32_t)(nrows * Lf->Mp * 4);
+                if (tid == 0)
+                    mbar_arrive_expect_tx(bar_g, bytes);
+                ok = cta_wait_bar(k, bar_g, ph_g & 1u, EW_GATHER);
+                ++ph_g;
+                if (!ok)
+                    break;
+                G = buf_ptr(k, BUF_G);
+            } else {
+                G = buf_ptr(k, BUF_X);  // echo: y = x
+                ld_g = p.in_ld;
+            }
+            if (tid < 32) {
+                const int out = p.out_dim;
+                float *ydst = p.mode == MODE_QUEUE ? p.q_y + (size_t)n_done * p.q_rows * out : p.mb_y;
+                const float *fbias = Lf ? reinterpret_cast<const float *>(smem + Lf->b_off) : nullptr;
+                const float *fscale =
+                    (Lf && Lf->s_off != 0xffffffffu) ? reinterpret_cast<const float *>(smem + Lf->s_off) : nullptr;
+                const int fact = Lf ? Lf->act : LL_ACT_IDENTITY;
+                for (int idx = tid; idx < nrows * out; idx += 32) {
+                    const int b = idx / out, o = idx - b * out;
+                    float v;
+                    if (Lf == nullptr) {
+                        v = o < p.in_dim ? G[(size_t)b * ld_g + o] : 0.0f;
+                    } else if (ksplit) {
+                        float acc = 0.0f;
+                        for (int c = 0; c < p.C; ++c)
+                            acc += G[((size_t)c * p.bmax4 + b) * ld_g + o];
+                        if (fscale)
+                            acc *= fscale[o];
+                        v = act_apply(acc + fbias[o], fact);
+                    } else {
+                        v = G[(size_t)b * ld_g + o];
+                    }
+                    if (p.mode == MODE_QUEUE)
+                        ydst[idx] = v;
+                    else
+                        st_relaxed_sys_f32(ydst + idx, v);
+                }
+                __syncwarp();
+                if (tid == 0) {
+                    if (p.mode == MODE_QUEUE) {
+                        if (p.q_stamp)
+                            p.q_stamp[n_done] = globaltimer();
+                        if (p.n_stages == 1) {
+                            for (int r = 0; r < p.C; ++r)
+                                mbar_arrive_remote(mapa(bar_go, (uint32_t)r));
+                        } else {
+                            __threadfence();
+                            red_release_gpu_add(p.q_done, 1u);
+                        }
+                    } else {
+                        st_release_sys_u32(&p.mb->seq_out, seq);
+                        st_relaxed_sys_u32(&p.ctrl->served, seq);
+                    }
+                }
+            }
+        }
+        last = seq;
+        ++n_done;
+    }
+
+    // Leave together: no CTA may exit while a peer can still write its shared memory.
+    __syncthreads();
+    cluster_sync();
+    if (leader && tid == 0) {
+        if (p.mode == MODE_QUEUE)
+            st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_QUEUE_DONE);
+        st_release_sys_u32(&p.ctrl->state, ST_EXITED);
+    }
+}
+
+}  // namespace llk
