@@ -90,7 +90,10 @@ typedef struct ll_engine_opts {
     uint64_t step_timeout_ns;   /* bound on every device wait inside one request */
     int32_t max_stages;         /* cap on pipeline stages (clusters); 0 = automatic */
     int32_t min_stages;         /* spread the layers over at least this many clusters; 0 = as few as fit */
-    int32_t reserved[6];
+    int32_t diag_wait_never;    /* test hook: rank 0 waits on a barrier nothing completes, so the bounded
+                                   wait runs out after step_timeout_ns and the kernel reports
+                                   LL_ERR_DEVICE_FAULT at location 6 and leaves (no fault is caused) */
+    int32_t reserved[5];
 } ll_engine_opts;
 
 typedef struct ll_engine_info {

@@ -76,7 +76,8 @@ class EngineOpts(ctypes.Structure):
     _fields_ = [("cluster_size", ctypes.c_int32), ("replicate_first", ctypes.c_int32),
                 ("write_combined", ctypes.c_int32), ("poll_mode", ctypes.c_int32),
                 ("idle_timeout_ns", ctypes.c_uint64), ("step_timeout_ns", ctypes.c_uint64),
-                ("max_stages", ctypes.c_int32), ("min_stages", ctypes.c_int32), ("reserved", ctypes.c_int32 * 6)]
+                ("max_stages", ctypes.c_int32), ("min_stages", ctypes.c_int32), ("diag_wait_never", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 5)]
 
 
 class EngineInfo(ctypes.Structure):

@@ -442,6 +442,7 @@ int finish_setup(ll_engine *e)
     p.idle_ns = e->opts.idle_timeout_ns;
     p.step_ns = e->opts.step_timeout_ns;
     p.peer_margin_ns = 2ull * 1000 * 1000 * 1000;
+    p.diag_wait_never = e->opts.diag_wait_never;
     // device words
     LL_CUDA_TRY(cudaMalloc((void **)&e->d_words, sizeof(unsigned) * (4 * kMaxStages + 8)));
     p.xfer_cnt = e->d_words;

@@ -38,6 +38,7 @@ enum ErrWhere : uint32_t {
     EW_XFER = 3,         // inter-stage handoff
     EW_QUEUE_GO = 4,     // queue-mode sequencing
     EW_PEER_POLL = 5,    // a non-leader CTA outlived the leader's idle bound
+    EW_DIAG = 6,         // the diagnostic never-completing wait ran out (expected)
     EW_LAYER_BASE = 0x100 // + layer index: all-gather wait of that layer
 };
 
@@ -92,6 +93,7 @@ struct Params {
     unsigned *q_done;     // queue-mode completion counter (multi-stage)
     uint64_t idle_ns, step_ns, peer_margin_ns;
     uint32_t last_seq;
+    int32_t diag_wait_never;
     // queue mode
     const float *q_x;
     float *q_y;

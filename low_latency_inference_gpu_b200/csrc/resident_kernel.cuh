@@ -450,6 +450,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
     if (leader && tid == 0)
         st_relaxed_sys_u32(&p.ctrl->state, ST_RUNNING);
 
+    if (ok && p.diag_wait_never && leader) {
+        // bar[4] is never arrived on in mailbox mode: this bounded wait must run out
+        ok = cta_wait_bar(k, bar_go, 0, EW_DIAG);
+    }
+
     uint32_t last = p.last_seq;
     uint32_t n_done = 0;
     uint32_t ph_ab[2] = {0, 0};

@@ -202,18 +202,17 @@ def test_idle_exit_and_relaunch():
 
 
 def test_device_wait_that_runs_out_reports_status_and_context_survives():
-    """A 1 ns bound on in-request waits makes the first device wait run out: the kernel
-    records LL_ERR_DEVICE_FAULT with a location and leaves cleanly (no trap, no hang)."""
+    """A device wait on a barrier nothing completes (diag_wait_never) runs out after the
+    50 ms step bound: the kernel records LL_ERR_DEVICE_FAULT with its location and leaves
+    cleanly -- no trap, no hang -- and the CUDA context stays usable."""
     net, Ws, bs = ll.config_params(0)
     x = ll.config_inputs(0, 1)
-    with engine_for(net, Ws, bs, step_timeout_ns=1) as e:
+    with engine_for(net, Ws, bs, step_timeout_ns=int(50e6), diag_wait_never=1) as e:
         with pytest.raises(ll.LLError) as err:
-            e.infer(x[0])
-            e.infer(x[0])
-        assert err.value.code in (ll.LL_ERR_DEVICE_FAULT, ll.LL_ERR_TIMEOUT)
+            e.infer(x[0], timeout_s=5.0)
+        assert err.value.code == ll.LL_ERR_DEVICE_FAULT
         info = e.info()
-        assert info.status == ll.LL_ERR_DEVICE_FAULT and info.err_where != 0
-    # the CUDA context is still usable
+        assert info.status == ll.LL_ERR_DEVICE_FAULT and info.err_where == 6
     with engine_for(net, Ws, bs) as e:
         assert rel_err(e.infer(x[0]), oracle.mlp_f32(net.dims, net.acts, Ws, bs, x)) <= 1e-5
 
