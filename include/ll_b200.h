@@ -85,7 +85,7 @@ typedef struct ll_engine_opts {
     int32_t cluster_size;       /* CTAs per cluster: 1,2,4,8,16; 0 = automatic */
     int32_t replicate_first;    /* first layer computed by every CTA: -1 auto, 0 no, 1 yes */
     int32_t write_combined;     /* allocate the mailbox write-combined (reference default) */
-    int32_t poll_mode;          /* 0 = one acquire load in flight, 1 = pipelined relaxed loads */
+    int32_t mailbox_format;     /* 0 = the reference's TickBuffer layout (the only format so far) */
     uint64_t idle_timeout_ns;   /* resident kernel exits after this long idle; relaunched on demand */
     uint64_t step_timeout_ns;   /* bound on every device wait inside one request */
     int32_t max_stages;         /* cap on pipeline stages (clusters); 0 = automatic */
@@ -216,6 +216,16 @@ int ll_engine_bench_closed_loop(ll_engine *e, const float *xs, int n_x, int n_re
  */
 int ll_engine_run_queue(ll_engine *e, const float *d_x, float *d_y, int n_req, int n_rows, float *ms,
                         unsigned long long *d_stamps);
+
+/*
+ * Device timeline of the first n requests of every later launch: d_trace is a
+ * device buffer of n * 16 uint64 %globaltimer stamps per request (slot 0
+ * request seen, 1 x staged, 2 pushed to peers, 3.. after each layer of the
+ * first stage, 11 handoff received by the last stage, 12 gather complete,
+ * 13 y written, 14 published, 15 x received by rank 1).  NULL turns it off.
+ * The reference's only tracing is -lineinfo (CMakeLists.txt:9).
+ */
+int ll_engine_set_trace(ll_engine *e, unsigned long long *d_trace, int n);
 
 const char *ll_last_error(void);
 

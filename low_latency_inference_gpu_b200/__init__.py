@@ -51,7 +51,7 @@ EXPORTED_SYMBOLS = [
     "ll_layered_mlp_bench", "ll_layered_mlp_destroy", "ll_cublas_mlp_create", "ll_cublas_mlp_bench",
     "ll_cublas_mlp_destroy", "ll_fill_normal", "ll_fill_uniform", "ll_init_params", "ll_f32_to_bf16",
     "ll_quantize_int8_rows", "ll_compute_stats", "ll_mailbox_bytes", "ll_mailbox_post", "ll_mailbox_wait",
-    "ll_next_seq", "ll_version", "ll_plan_net",
+    "ll_next_seq", "ll_version", "ll_plan_net", "ll_engine_set_trace",
 ]
 
 
@@ -74,7 +74,7 @@ class NetDesc(ctypes.Structure):
 
 class EngineOpts(ctypes.Structure):
     _fields_ = [("cluster_size", ctypes.c_int32), ("replicate_first", ctypes.c_int32),
-                ("write_combined", ctypes.c_int32), ("poll_mode", ctypes.c_int32),
+                ("write_combined", ctypes.c_int32), ("mailbox_format", ctypes.c_int32),
                 ("idle_timeout_ns", ctypes.c_uint64), ("step_timeout_ns", ctypes.c_uint64),
                 ("max_stages", ctypes.c_int32), ("min_stages", ctypes.c_int32), ("diag_wait_never", ctypes.c_int32),
                 ("reserved", ctypes.c_int32 * 5)]
@@ -142,6 +142,7 @@ def _sig(lib):
         "ll_engine_get_info": (ctypes.c_int, [_vp, P(EngineInfo)]),
         "ll_engine_bench_closed_loop": (ctypes.c_int, [_vp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _fp, _dp]),
         "ll_engine_run_queue": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _fp, _vp]),
+        "ll_engine_set_trace": (ctypes.c_int, [_vp, _vp, ctypes.c_int]),
         "ll_last_error": (ctypes.c_char_p, []),
         "ll_dense_warp_rm": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
         "ll_dense_mbyv_packed": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
@@ -419,6 +420,10 @@ class Engine:
         _check(lib().ll_engine_run_queue(self.h, d_x_ptr, d_y_ptr, n_req, n_rows, ctypes.byref(ms),
                                          d_stamps_ptr or None))
         return ms.value
+
+    def set_trace(self, d_trace_ptr: int, n: int):
+        """Record a device timeline of the first n requests of later launches (16 uint64 per request)."""
+        _check(lib().ll_engine_set_trace(self.h, d_trace_ptr or None, n))
 
     def info(self) -> EngineInfo:
         inf = EngineInfo()

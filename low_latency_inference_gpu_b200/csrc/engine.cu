@@ -341,7 +341,7 @@ extern "C" void ll_engine_opts_default(ll_engine_opts *o)
     o->cluster_size = 0;
     o->replicate_first = -1;
     o->write_combined = 0;
-    o->poll_mode = 0;
+    o->mailbox_format = 0;
     o->idle_timeout_ns = 30ull * 1000 * 1000 * 1000;
     o->step_timeout_ns = 200ull * 1000 * 1000;
     o->max_stages = 0;
@@ -438,7 +438,7 @@ int finish_setup(ll_engine *e)
     p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + sizeof(ll_tick_header) +
                                        sizeof(float) * (size_t)e->in_dim * e->max_batch);
     p.ctrl = e->ctrl_dev;
-    p.poll_mode = e->opts.poll_mode;
+    p.mailbox_format = e->opts.mailbox_format;
     p.idle_ns = e->opts.idle_timeout_ns;
     p.step_ns = e->opts.step_timeout_ns;
     p.peer_margin_ns = 2ull * 1000 * 1000 * 1000;
@@ -983,6 +983,17 @@ int ll_engine_destroy(ll_engine *e)
         cudaFreeHost((void *)e->ctrl_host);
     delete e;
     return rc;
+}
+
+int ll_engine_set_trace(ll_engine *e, unsigned long long *d_trace, int n)
+{
+    if (!e || n < 0 || (n > 0 && !d_trace)) {
+        llh::set_error("ll_engine_set_trace: invalid arguments");
+        return LL_ERR_INVALID_ARG;
+    }
+    e->base.trace = n > 0 ? d_trace : nullptr;
+    e->base.trace_n = n;
+    return LL_OK;
 }
 
 int ll_engine_get_info(ll_engine *e, ll_engine_info *info)

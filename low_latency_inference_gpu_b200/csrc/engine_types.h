@@ -11,6 +11,7 @@ constexpr int kMaxLayers = 24;
 constexpr int kMaxStages = 9;
 constexpr int kThreads = 512;  // threads per CTA of the resident kernel
 constexpr int kMaxCluster = 16;
+constexpr int kTraceSlots = 16;  // per-request device timeline slots (globaltimer ns)
 
 // How one layer is spread over the CTAs of its stage's cluster.
 enum LayerMode : int32_t {
@@ -71,7 +72,7 @@ struct Params {
     float *mb_y;
     EngineCtrl *ctrl;    // device view of the control block
     int32_t mode;
-    int32_t poll_mode;
+    int32_t mailbox_format;
     int32_t in_dim, out_dim, max_batch, bmax4; // bmax4 = max_batch rounded up to 4
     int32_t in_ld;       // stage-0 X row stride
     int32_t n_layers, n_stages, C;
@@ -94,6 +95,8 @@ struct Params {
     uint64_t idle_ns, step_ns, peer_margin_ns;
     uint32_t last_seq;
     int32_t diag_wait_never;
+    unsigned long long *trace;  // optional [trace_n][kTraceSlots] timeline of the first requests
+    int32_t trace_n;
     // queue mode
     const float *q_x;
     float *q_y;

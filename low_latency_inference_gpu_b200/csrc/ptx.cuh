@@ -114,6 +114,17 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const volatile uint32_t *p)
     return v;
 }
 
+// 16-byte acquire load (the whole mailbox header in one PCIe read).
+__device__ __forceinline__ uint4 ld_acquire_sys_v4(const unsigned *p)
+{
+    uint4 v;
+    asm volatile("ld.acquire.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
 __device__ __forceinline__ uint32_t ld_relaxed_sys(const volatile uint32_t *p)
 {
     uint32_t v;

@@ -6,8 +6,10 @@
 // weights "resident" in registers / SMEM / global scratch per thread,
 // include/ll/weights_storage.cuh:7-240; here the slice is one bulk-copied SMEM
 // image).  Per request:
-//   stage 0  : every CTA polls the mailbox (host-mapped TickBuffer,
-//              src/bench_persistent_mbyv_mlp.cu:229-281) and reads x itself;
+//   stage 0  : rank 0 alone polls the mailbox header (host-mapped TickBuffer,
+//              src/bench_persistent_mbyv_mlp.cu:229-281) with one 16-byte acquire
+//              load, reads x once and pushes {seq, n_rows, x} into its peers'
+//              shared memory (st.async + mbarrier tx), so PCIe sees one poller;
 //   layers   : row-split GEMV from SMEM, outputs pushed to peer CTAs with
 //              st.async + mbarrier complete_tx (DSMEM) instead of the
 //              reference's global-atomic layer barriers (:308-377);
@@ -27,7 +29,8 @@ namespace llk {
 constexpr uint32_t kCmdExit = 0u;  // 0 is never a live sequence number
 
 struct Shared {
-    uint64_t bar[5];  // 0 image load, 1 buffer A, 2 buffer B, 3 gather G, 4 queue go
+    uint32_t hdr[4];  // request header pushed by the dispatcher: seq, n_rows (16-byte aligned: first member)
+    uint64_t bar[7];  // 0 image load, 1 buffer A, 2 buffer B, 3 gather G, 4 diagnostic, 5 header, 6 x rows
     uint32_t cmd;
     uint32_t nrows;
     uint32_t fail;
@@ -169,7 +172,7 @@ struct KernelCtx {
     int stage;
 };
 
-// Record a device error (first writer wins is not needed: status is sticky per launch).
+// Record a device error (status is sticky per launch).
 __device__ __forceinline__ void report_error(const KernelCtx &k, uint32_t status, uint32_t where)
 {
     st_relaxed_sys_u32(&k.p->ctrl->err_where, where);
@@ -185,27 +188,45 @@ __device__ __forceinline__ void broadcast_abort(const KernelCtx &k)
     atomicExch(k.p->abort_flag, 1u);
 }
 
-// All threads wait for an mbarrier phase; bounded; consistent verdict for the CTA.
-__device__ __forceinline__ bool cta_wait_bar(const KernelCtx &k, uint32_t bar, uint32_t parity, uint32_t where)
+__device__ __forceinline__ bool global_abort(const KernelCtx &k)
 {
-    const uint64_t deadline = globaltimer() + k.p->step_ns;
-    uint32_t r = 0;
+    return ld_relaxed_gpu_u32(k.p->abort_flag) != 0;
+}
+
+__device__ __forceinline__ void trace(const KernelCtx &k, uint32_t req, int slot)
+{
+    if (k.p->trace && req < (uint32_t)k.p->trace_n)
+        k.p->trace[(size_t)req * kTraceSlots + slot] = globaltimer();
+}
+
+// All threads wait for an mbarrier phase; thread 0 alone watches the clock.
+// Returns true when the phase completed; false on abort (quiet) or timeout
+// (reported with `where`).  The verdict is the same for every thread.
+__device__ __forceinline__ bool cta_wait_bar(const KernelCtx &k, uint32_t bar, uint32_t parity, uint32_t where,
+                                             uint64_t bound_ns)
+{
+    volatile uint32_t *abort = &k.sh->abort;
+    volatile uint32_t *fail = &k.sh->fail;
+    const bool timer = threadIdx.x == 0;
+    const uint64_t deadline = timer ? globaltimer() + bound_ns : 0;
     for (uint32_t it = 0;; ++it) {
         if (mbar_try_wait(bar, parity))
             break;
-        if (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort)) {
-            r = 1;
+        if (*abort) {
+            atomicOr(&k.sh->fail, 1u);
             break;
         }
-        if ((it & 15u) == 15u && globaltimer() > deadline) {
-            r = 2;
+        if (timer) {
+            if ((it & 15u) == 15u && globaltimer() > deadline) {
+                atomicOr(&k.sh->fail, 2u);
+                break;
+            }
+        } else if (*fail) {
             break;
         }
     }
-    if (r)
-        atomicOr(&k.sh->fail, r);
     __syncthreads();
-    const uint32_t f = *reinterpret_cast<volatile uint32_t *>(&k.sh->fail);
+    const uint32_t f = *fail;
     if (f != 0 && threadIdx.x == 0 && (f & 2u)) {
         report_error(k, LL_ERR_DEVICE_FAULT, where);
         broadcast_abort(k);
@@ -213,91 +234,35 @@ __device__ __forceinline__ bool cta_wait_bar(const KernelCtx &k, uint32_t bar, u
     return f == 0;
 }
 
-__device__ __forceinline__ bool global_abort(const KernelCtx &k)
-{
-    return ld_relaxed_gpu_u32(k.p->abort_flag) != 0;
-}
-
-// Thread 0 of a stage-0 CTA: wait for a new request in the mailbox.
-// Returns the sequence number, or kCmdExit.  Leader (rank 0) alone honours
-// `stop` and the idle timeout; the others follow the leader's abort broadcast.
-__device__ uint32_t poll_mailbox(const KernelCtx &k, uint32_t last, bool leader, uint32_t *nrows)
+// Thread 0 of the dispatcher (rank 0 of stage 0): wait for a new request.
+// One 16-byte acquire load returns seq_in, seq_out, stop and n_rows together.
+// Returns the sequence number, or kCmdExit (stop, idle bound, abort).
+__device__ uint32_t poll_mailbox(const KernelCtx &k, uint32_t last, uint32_t *nrows)
 {
     const Params &p = *k.p;
-    volatile uint32_t *seq_in = &p.mb->seq_in;
     const uint64_t t0 = globaltimer();
-    const uint64_t bound = leader ? p.idle_ns : p.idle_ns + p.peer_margin_ns;
-    uint32_t s = 0;
-    bool found = false;
-    if (p.poll_mode == 1) {
-        // Four relaxed loads kept in flight, re-issued as each returns.
-        uint32_t v0 = ld_relaxed_sys(seq_in);
-        __nanosleep(100);
-        uint32_t v1 = ld_relaxed_sys(seq_in);
-        __nanosleep(100);
-        uint32_t v2 = ld_relaxed_sys(seq_in);
-        __nanosleep(100);
-        uint32_t v3 = ld_relaxed_sys(seq_in);
-        for (uint32_t it = 0;; ++it) {
-            if (v0 != last && v0 != 0) { s = v0; found = true; break; }
-            v0 = ld_relaxed_sys(seq_in);
-            if (v1 != last && v1 != 0) { s = v1; found = true; break; }
-            v1 = ld_relaxed_sys(seq_in);
-            if (v2 != last && v2 != 0) { s = v2; found = true; break; }
-            v2 = ld_relaxed_sys(seq_in);
-            if (v3 != last && v3 != 0) { s = v3; found = true; break; }
-            v3 = ld_relaxed_sys(seq_in);
-            if ((it & 7u) == 7u) {
-                if (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort) || global_abort(k))
-                    return kCmdExit;
-                if (leader && ld_relaxed_sys(&p.mb->stop)) {
-                    st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
-                    return kCmdExit;
-                }
-                if (globaltimer() - t0 > bound)
-                    break;
-            }
+    for (uint32_t it = 0;; ++it) {
+        const uint4 h = ld_acquire_sys_v4(reinterpret_cast<const unsigned *>(p.mb));
+        if (h.z) {
+            // stop, with or without a doorbell bump (src/bench_persistent_mbyv_mlp.cu:554-557,
+            // src/bench_persistent_mlp.cu:409)
+            st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
+            return kCmdExit;
         }
-        if (found)
-            fence_acq_rel_sys();
-    } else {
-        for (uint32_t it = 0;; ++it) {
-            const uint32_t v = ld_acquire_sys(seq_in);
-            if (v != last && v != 0) {
-                s = v;
-                found = true;
-                break;
-            }
-            if ((it & 31u) == 31u) {
-                if (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort) || global_abort(k))
-                    return kCmdExit;
-                if (leader && ld_relaxed_sys(&p.mb->stop)) {
-                    st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
-                    return kCmdExit;
-                }
-                if (globaltimer() - t0 > bound)
-                    break;
+        if (h.x != last && h.x != 0) {
+            const uint32_t n = h.w == 0 ? 1u : h.w;
+            *nrows = n > (uint32_t)p.max_batch ? (uint32_t)p.max_batch : n;
+            return h.x;
+        }
+        if ((it & 63u) == 63u) {
+            if (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort) || global_abort(k))
+                return kCmdExit;
+            if (globaltimer() - t0 > p.idle_ns) {
+                st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_IDLE);
+                return kCmdExit;
             }
         }
     }
-    if (!found) {
-        if (leader) {
-            st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_IDLE);
-        } else {
-            report_error(k, LL_ERR_DEVICE_FAULT, EW_PEER_POLL);
-        }
-        return kCmdExit;
-    }
-    // A new sequence number together with `stop` is the reference's stop
-    // doorbell (stop = 1, then seq_in = ++seq; src/bench_persistent_mbyv_mlp.cu:554-557).
-    if (leader && ld_relaxed_sys(&p.mb->stop)) {
-        st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
-        return kCmdExit;
-    }
-    uint32_t n = ld_relaxed_sys(&p.mb->n_rows);
-    n = n == 0 ? 1u : n;
-    *nrows = n > (uint32_t)p.max_batch ? (uint32_t)p.max_batch : n;
-    return s;
 }
 
 __device__ __forceinline__ float *buf_ptr(const KernelCtx &k, int id)
@@ -310,7 +275,7 @@ __device__ __forceinline__ uint32_t buf_addr(const KernelCtx &k, int id)
     return smem_u32(k.smem + k.p->buf_off[id]);
 }
 
-// Copy rows of a source vector into the X buffer (row stride in_ld), rounding to bf16 if asked.
+// Copy the request rows from the mailbox into X (row stride in_ld), rounding to bf16 if asked.
 __device__ __forceinline__ void stage_input_mailbox(const KernelCtx &k, int nrows)
 {
     const Params &p = *k.p;
@@ -347,6 +312,33 @@ __device__ __forceinline__ void stage_input_device(const KernelCtx &k, const flo
         const int b = t / in, c = t - b * in;
         float v = __ldg(src + (size_t)b * in + c);
         X[(size_t)b * p.in_ld + c] = p.act_bf16 ? round_bf16(v) : v;
+    }
+}
+
+// Dispatcher: push {seq, n_rows} and the staged x rows into every peer CTA of the cluster.
+__device__ __forceinline__ void push_request(const KernelCtx &k, uint32_t seq, int nrows, uint32_t bar_hdr,
+                                             uint32_t bar_x)
+{
+    const Params &p = *k.p;
+    const int in4 = p.in_ld >> 2;
+    const int per = nrows * in4;
+    const int total = (p.C - 1) * (1 + per);
+    const float *X = buf_ptr(k, BUF_X);
+    const uint32_t x_addr = buf_addr(k, BUF_X);
+    const uint32_t h_addr = smem_u32(k.sh->hdr);
+    for (int t = threadIdx.x; t < total; t += kThreads) {
+        const uint32_t d = 1u + (uint32_t)(t / (1 + per));
+        const int j = t % (1 + per);
+        if (j == 0) {
+            st_async_v4(mapa(h_addr, d), make_float4(__uint_as_float(seq), __uint_as_float((uint32_t)nrows), 0.f, 0.f),
+                        mapa(bar_hdr, d));
+        } else {
+            const int idx = j - 1;
+            const int b = idx / in4, c4 = idx - b * in4;
+            const uint32_t off = (uint32_t)(((size_t)b * p.in_ld + c4 * 4) * 4);
+            st_async_v4(mapa(x_addr + off, d), *reinterpret_cast<const float4 *>(X + (size_t)b * p.in_ld + c4 * 4),
+                        mapa(bar_x, d));
+        }
     }
 }
 
@@ -393,7 +385,7 @@ __device__ __forceinline__ void push_rows(const KernelCtx &k, const float *stage
 __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __grid_constant__ Params p)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ __align__(8) Shared sh;
+    __shared__ __align__(16) Shared sh;
 
     KernelCtx k;
     k.p = &p;
@@ -402,16 +394,18 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
     k.rank = cluster_ctarank();
     k.stage = (int)(blockIdx.x / (unsigned)p.C);
     const int tid = threadIdx.x;
-    const bool leader = (k.stage == 0 && k.rank == 0);
+    const bool leader = (k.stage == 0 && k.rank == 0);  // dispatcher
     const bool last_stage = (k.stage == p.n_stages - 1);
     const bool final_writer = last_stage && k.rank == 0;
     const uint32_t bar_load = smem_u32(&sh.bar[0]);
     const uint32_t bar_ab[2] = {smem_u32(&sh.bar[1]), smem_u32(&sh.bar[2])};
     const uint32_t bar_g = smem_u32(&sh.bar[3]);
-    const uint32_t bar_go = smem_u32(&sh.bar[4]);
+    const uint32_t bar_diag = smem_u32(&sh.bar[4]);
+    const uint32_t bar_hdr = smem_u32(&sh.bar[5]);
+    const uint32_t bar_x = smem_u32(&sh.bar[6]);
 
     if (tid == 0) {
-        for (int i = 0; i < 5; ++i)
+        for (int i = 0; i < 7; ++i)
             mbar_init(smem_u32(&sh.bar[i]), 1);
         sh.cmd = 0;
         sh.nrows = 1;
@@ -423,12 +417,10 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
     }
     // Zero all activation buffers once so padded columns are exact zeros.
     {
-        const uint32_t img = p.image_bytes[k.stage];
         uint4 *z = reinterpret_cast<uint4 *>(smem + p.buf_off[BUF_X]);
         const uint32_t n16 = (p.smem_bytes - p.buf_off[BUF_X]) / 16;
         for (uint32_t i = tid; i < n16; i += kThreads)
             z[i] = make_uint4(0, 0, 0, 0);
-        (void)img;
     }
     __syncthreads();
 
@@ -444,21 +436,21 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 bulk_g2s(dst + off, src + off, n, bar_load);
             }
         }
-        ok = cta_wait_bar(k, bar_load, 0, EW_LOAD);
+        ok = cta_wait_bar(k, bar_load, 0, EW_LOAD, p.step_ns);
     }
     cluster_sync();  // barriers initialised and images resident in every CTA of the cluster
     if (leader && tid == 0)
         st_relaxed_sys_u32(&p.ctrl->state, ST_RUNNING);
 
     if (ok && p.diag_wait_never && leader) {
-        // bar[4] is never arrived on in mailbox mode: this bounded wait must run out
-        ok = cta_wait_bar(k, bar_go, 0, EW_DIAG);
+        // bar[4] is never arrived on: this bounded wait must run out
+        ok = cta_wait_bar(k, bar_diag, 0, EW_DIAG, p.step_ns);
     }
 
     uint32_t last = p.last_seq;
     uint32_t n_done = 0;
     uint32_t ph_ab[2] = {0, 0};
-    uint32_t ph_g = 0, ph_go = 0;
+    uint32_t ph_g = 0, ph_hdr = 0, ph_x = 0;
     const int first_l = p.stage_first[k.stage];
     const int last_l = p.stage_last[k.stage];
 
@@ -468,44 +460,41 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
         int nrows;
         if (p.mode == MODE_QUEUE && (int)n_done >= p.q_n)
             break;  // every stage knows the queue length
-        if (k.stage == 0) {
+        if (leader) {
             if (p.mode == MODE_QUEUE) {
-                if (n_done > 0) {
-                    if (p.n_stages == 1) {
-                        if (!cta_wait_bar(k, bar_go, ph_go & 1u, EW_QUEUE_GO))
-                            break;
-                        ++ph_go;
-                    } else {
-                        if (tid == 0) {
-                            const uint64_t deadline = globaltimer() + p.step_ns;
-                            uint32_t it = 0;
-                            while (ld_acquire_gpu(p.q_done) < n_done) {
-                                if ((++it & 31u) == 0 && (global_abort(k) || globaltimer() > deadline)) {
-                                    if (!global_abort(k)) {
-                                        report_error(k, LL_ERR_DEVICE_FAULT, EW_QUEUE_GO);
-                                        broadcast_abort(k);
-                                    }
-                                    sh.fail = 1;
-                                    break;
+                if (n_done > 0 && p.n_stages > 1) {
+                    if (tid == 0) {
+                        const uint64_t deadline = globaltimer() + p.step_ns;
+                        uint32_t it = 0;
+                        while (ld_acquire_gpu(p.q_done) < n_done) {
+                            if ((++it & 31u) == 0 && (global_abort(k) || globaltimer() > deadline)) {
+                                if (!global_abort(k)) {
+                                    report_error(k, LL_ERR_DEVICE_FAULT, EW_QUEUE_GO);
+                                    broadcast_abort(k);
                                 }
+                                sh.fail = 1;
+                                break;
                             }
                         }
-                        __syncthreads();
-                        if (sh.fail)
-                            break;
                     }
+                    __syncthreads();
+                    if (*reinterpret_cast<volatile uint32_t *>(&sh.fail))
+                        break;
                 }
                 seq = n_done + 1;
                 nrows = p.q_rows;
+                if (tid == 0)
+                    trace(k, n_done, 0);
                 stage_input_device(k, p.q_x + (size_t)n_done * p.q_rows * p.in_dim, nrows);
             } else {
                 if (tid == 0) {
                     uint32_t nr = 1;
-                    const uint32_t c = poll_mailbox(k, last, leader, &nr);
-                    if (c == kCmdExit && leader)
+                    const uint32_t c = poll_mailbox(k, last, &nr);
+                    if (c == kCmdExit)
                         broadcast_abort(k);
                     sh.cmd = c;
                     sh.nrows = nr;
+                    trace(k, n_done, 0);
                 }
                 __syncthreads();
                 seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
@@ -514,6 +503,31 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                     break;
                 stage_input_mailbox(k, nrows);
             }
+            __syncthreads();
+            if (tid == 0)
+                trace(k, n_done, 1);
+            if (p.C > 1)
+                push_request(k, seq, nrows, bar_hdr, bar_x);
+            if (tid == 0)
+                trace(k, n_done, 2);
+        } else if (k.stage == 0) {
+            // peer of the dispatcher: {seq, n_rows} then x arrive by DSMEM push
+            if (tid == 0)
+                mbar_arrive_expect_tx(bar_hdr, 16u);
+            if (!cta_wait_bar(k, bar_hdr, ph_hdr & 1u, EW_PEER_POLL, p.idle_ns + p.peer_margin_ns))
+                break;
+            ++ph_hdr;
+            seq = *reinterpret_cast<volatile uint32_t *>(&sh.hdr[0]);
+            nrows = (int)*reinterpret_cast<volatile uint32_t *>(&sh.hdr[1]);
+            if (nrows < 1 || nrows > p.max_batch)
+                nrows = 1;  // never index past the buffers, whatever arrived
+            if (tid == 0)
+                mbar_arrive_expect_tx(bar_x, (uint32_t)(nrows * p.in_ld * 4));
+            if (!cta_wait_bar(k, bar_x, ph_x & 1u, EW_PEER_POLL, p.step_ns))
+                break;
+            ++ph_x;
+            if (tid == 0 && k.rank == 1)
+                trace(k, n_done, 15);
         } else {
             // Wait for the previous cluster's rows of this request (through L2).
             if (tid == 0) {
@@ -538,12 +552,16 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                     }
                 }
                 sh.cmd = c;
+                if (final_writer)
+                    trace(k, n_done, 11);
             }
             __syncthreads();
             seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
             nrows = (int)*reinterpret_cast<volatile uint32_t *>(&sh.nrows);
             if (seq == kCmdExit)
                 break;
+            if (nrows < 1 || nrows > p.max_batch)
+                nrows = 1;
             const float *src = p.xfer + (size_t)(k.stage - 1) * p.xfer_stride;
             float *X = buf_ptr(k, BUF_X);
             const int ld = p.stage_in_ld[k.stage];
@@ -580,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                           p.C);
                 if (tid == 0)
                     mbar_arrive_expect_tx(bar_ab[bi], (uint32_t)(nrows * L.Mp * 4));
-                ok = cta_wait_bar(k, bar_ab[bi], ph_ab[bi] & 1u, EW_LAYER_BASE + (uint32_t)l);
+                ok = cta_wait_bar(k, bar_ab[bi], ph_ab[bi] & 1u, EW_LAYER_BASE + (uint32_t)l, p.step_ns);
                 ++ph_ab[bi];
                 break;
             }
@@ -625,6 +643,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
             default:
                 break;
             }
+            if (leader && tid == 0 && l - first_l < 8)
+                trace(k, n_done, 3 + (l - first_l));
         }
         if (!ok)
             break;
@@ -642,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 const uint32_t bytes = ksplit ? (uint32_t)(p.C * nrows * Lf->R * 4) : (uint32_t)(nrows * Lf->Mp * 4);
                 if (tid == 0)
                     mbar_arrive_expect_tx(bar_g, bytes);
-                ok = cta_wait_bar(k, bar_g, ph_g & 1u, EW_GATHER);
+                ok = cta_wait_bar(k, bar_g, ph_g & 1u, EW_GATHER, p.step_ns);
                 ++ph_g;
                 if (!ok)
                     break;
@@ -651,6 +671,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 G = buf_ptr(k, BUF_X);  // echo: y = x
                 ld_g = p.in_ld;
             }
+            if (tid == 0)
+                trace(k, n_done, 12);
             if (tid < 32) {
                 const int out = p.out_dim;
                 float *ydst = p.mode == MODE_QUEUE ? p.q_y + (size_t)n_done * p.q_rows * out : p.mb_y;
@@ -680,20 +702,20 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 }
                 __syncwarp();
                 if (tid == 0) {
+                    trace(k, n_done, 13);
                     if (p.mode == MODE_QUEUE) {
                         if (p.q_stamp)
                             p.q_stamp[n_done] = globaltimer();
-                        if (p.n_stages == 1) {
-                            for (int r = 0; r < p.C; ++r)
-                                mbar_arrive_remote(mapa(bar_go, (uint32_t)r));
-                        } else {
+                        if (p.n_stages > 1) {
                             __threadfence();
                             red_release_gpu_add(p.q_done, 1u);
                         }
                     } else {
+                        // release: y reaches the host before seq_out (src/bench_persistent_mbyv_mlp.cu:365-370)
                         st_release_sys_u32(&p.mb->seq_out, seq);
                         st_relaxed_sys_u32(&p.ctrl->served, seq);
                     }
+                    trace(k, n_done, 14);
                 }
             }
         }
