@@ -165,6 +165,9 @@ def main():
     ap.add_argument("--ref-requests", type=int, default=400000, help="reference arm: requests per step, all cores")
     ap.add_argument("--cpu-requests", type=int, default=100000, help="cpu_baseline sample (one core)")
     ap.add_argument("--no-compare", action="store_true", help="skip the cuBLAS / launch-per-layer comparison paths")
+    ap.add_argument("--only", default="all", choices=["all", "value"],
+                    help="value: run only the device-queue phase (bounded launches; usable under ncu, which "
+                         "serialises launches and so cannot drive the resident mailbox kernel)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -216,9 +219,11 @@ def main():
     xs_all = ll.config_inputs(0, R * world)
     xs = np.ascontiguousarray(xs_all[rank * R:(rank + 1) * R])
 
+    full = args.only == "all"
     # ---------------- ping-pong floor (same kernel, no layers) ----------------
-    floor = {}
-    for key, (i, o) in (("seq_only", (0, 0)), ("x_to_y", (64, 16))):
+    floor = {"seq_only": {"p50_us": float("nan"), "p99_us": float("nan")},
+             "x_to_y": {"p50_us": float("nan"), "p99_us": float("nan")}}
+    for key, (i, o) in ((("seq_only", (0, 0)), ("x_to_y", (64, 16))) if full else ()):
         with ll.EchoEngine(i, o, device=dev) as e:
             e.bench_closed_loop(xs if i else None, 2000)
             lat, _ = e.bench_closed_loop(xs if i else None, 20000)
@@ -258,21 +263,23 @@ def main():
     dev_stats = ll.compute_stats(np.array(dev_lat))
 
     # ---------------- e2e: mailbox with host buffers through the C ABI ----------------
-    engine.start()
-    for _ in range(W):
-        engine.bench_closed_loop(xs, R)
-    torch.cuda.current_stream().synchronize()
-    host_barrier()
     lat_all = []
     t0 = time.perf_counter()
-    for _ in range(K):
-        lat, _ = engine.bench_closed_loop(xs, R)
-        lat_all.append(lat)
+    if full:
+        engine.start()
+        for _ in range(W):
+            engine.bench_closed_loop(xs, R)
+        torch.cuda.current_stream().synchronize()
+        host_barrier()
+        t0 = time.perf_counter()
+        for _ in range(K):
+            lat, _ = engine.bench_closed_loop(xs, R)
+            lat_all.append(lat)
     t1 = time.perf_counter()
     host_barrier()
     clk = clocks.stop()
     e2e_s = host_max(t1 - t0)
-    lat_all = np.concatenate(lat_all)
+    lat_all = np.concatenate(lat_all) if lat_all else np.array([float("nan")])
     s_e2e = ll.compute_stats(lat_all)
     e2e_value = world * K * R / e2e_s
     engine.stop()
@@ -282,7 +289,7 @@ def main():
     # ---------------- comparison paths + CPU baseline (N=1, rank 0) ----------------
     compare = None
     cpu_baseline = None
-    if world == 1 and not args.no_compare:
+    if world == 1 and full and not args.no_compare:
         compare = {}
         for cls, name in ((ll.CublasMLP, "cublas"), (ll.LayeredMLP, "warp_gemv")):
             with cls(net, Ws, bs, device=dev) as m:
@@ -292,7 +299,7 @@ def main():
                     lat, _ = m.bench(mode, xs, 10000)
                     s = ll.compute_stats(lat)
                     compare[f"{name}_{mname}"] = {"p50_us": s["p50"], "p99_us": s["p99"]}
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and full:
         import oracle
 
         kind = "reference" if oracle.ref_available() else "port"
@@ -350,6 +357,9 @@ def main():
     }
     if compare:
         out["e2e"]["speedup_vs_cublas_graph_e2e_p50"] = compare["cublas_graph_e2e"]["p50_us"] / s_e2e["p50"]
+    if not full:  # device-queue phase only: no mailbox numbers were taken
+        out["e2e"] = None
+        out["latency_floor"] = None
     print(json.dumps(out), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -219,7 +219,8 @@ int ll_engine_run_queue(ll_engine *e, const float *d_x, float *d_y, int n_req, i
 
 /*
  * Device timeline of the first n requests of every later launch: d_trace is a
- * device buffer of n * 16 uint64 %globaltimer stamps per request (slot 0
+ * device buffer of n * 32 uint64 per request: 16 %globaltimer ns stamps, then
+ * the same 16 events as SM clock64 cycles (slot 0
  * request seen, 1 x staged, 2 pushed to peers, 3.. after each layer of the
  * first stage, 11 handoff received by the last stage, 12 gather complete,
  * 13 y written, 14 published, 15 x received by rank 1).  NULL turns it off.

@@ -422,7 +422,7 @@ class Engine:
         return ms.value
 
     def set_trace(self, d_trace_ptr: int, n: int):
-        """Record a device timeline of the first n requests of later launches (16 uint64 per request)."""
+        """Record a device timeline of the first n requests of later launches (32 uint64 per request)."""
         _check(lib().ll_engine_set_trace(self.h, d_trace_ptr or None, n))
 
     def info(self) -> EngineInfo:

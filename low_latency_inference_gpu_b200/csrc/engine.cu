@@ -20,7 +20,7 @@ using namespace llk;
 
 namespace {
 
-constexpr int kSmemLimit = 227 * 1024 - 1024;  // dynamic smem budget per CTA (static Shared lives in the rest)
+constexpr int kSmemLimit = 227 * 1024 - 4096;  // dynamic smem budget per CTA (static Shared + Params copy use the rest)
 
 inline void cpu_relax()
 {
@@ -522,7 +522,7 @@ int reap(ll_engine *e)
         e->last_status = LL_ERR_CUDA;
         return LL_ERR_CUDA;
     }
-    e->last_served = e->ctrl_host->served;
+    e->last_served = static_cast<ll_tick_header *>(e->mb_host)->seq_out;
     if (e->ctrl_host->status != LL_OK) {
         llh::set_error("resident kernel reported status %u at location 0x%x", e->ctrl_host->status,
                        e->ctrl_host->err_where);
@@ -1015,7 +1015,7 @@ int ll_engine_get_info(ll_engine *e, ll_engine_info *info)
     info->state = (int32_t)e->ctrl_host->state;
     info->status = (int32_t)e->ctrl_host->status;
     info->err_where = (int32_t)e->ctrl_host->err_where;
-    info->served = e->ctrl_host->served;
+    info->served = static_cast<ll_tick_header *>(e->mb_host)->seq_out;
     for (int l = 0; l < e->base.n_layers && l < 24; ++l)
         info->layer_modes[l] = e->base.L[l].mode;
     return LL_OK;

@@ -11,7 +11,7 @@ constexpr int kMaxLayers = 24;
 constexpr int kMaxStages = 9;
 constexpr int kThreads = 512;  // threads per CTA of the resident kernel
 constexpr int kMaxCluster = 16;
-constexpr int kTraceSlots = 16;  // per-request device timeline slots (globaltimer ns)
+constexpr int kTraceSlots = 32;  // per request: 16 %globaltimer ns stamps, then the same 16 events in SM clock64 cycles
 
 // How one layer is spread over the CTAs of its stage's cluster.
 enum LayerMode : int32_t {

@@ -195,8 +195,10 @@ __device__ __forceinline__ bool global_abort(const KernelCtx &k)
 
 __device__ __forceinline__ void trace(const KernelCtx &k, uint32_t req, int slot)
 {
-    if (k.p->trace && req < (uint32_t)k.p->trace_n)
+    if (k.p->trace && req < (uint32_t)k.p->trace_n) {
         k.p->trace[(size_t)req * kTraceSlots + slot] = globaltimer();
+        k.p->trace[(size_t)req * kTraceSlots + 16 + slot] = clock64();
+    }
 }
 
 // All threads wait for an mbarrier phase; thread 0 alone watches the clock.
@@ -382,10 +384,21 @@ __device__ __forceinline__ void push_rows(const KernelCtx &k, const float *stage
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __grid_constant__ Params p)
+__global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __grid_constant__ Params pg)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(16) Shared sh;
+    __shared__ __align__(16) Params sp;  // plan copied once: every later read is a shared-memory load
+
+    {
+        static_assert(sizeof(Params) % 4 == 0, "Params is copied word by word");
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(&pg);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(&sp);
+        for (int i = threadIdx.x; i < (int)(sizeof(Params) / 4); i += kThreads)
+            dst[i] = src[i];
+        __syncthreads();
+    }
+    const Params &p = sp;
 
     KernelCtx k;
     k.p = &p;
@@ -398,7 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
     const bool last_stage = (k.stage == p.n_stages - 1);
     const bool final_writer = last_stage && k.rank == 0;
     const uint32_t bar_load = smem_u32(&sh.bar[0]);
-    const uint32_t bar_ab[2] = {smem_u32(&sh.bar[1]), smem_u32(&sh.bar[2])};
+    const uint32_t bar_a = smem_u32(&sh.bar[1]);
+    const uint32_t bar_b = smem_u32(&sh.bar[2]);
     const uint32_t bar_g = smem_u32(&sh.bar[3]);
     const uint32_t bar_diag = smem_u32(&sh.bar[4]);
     const uint32_t bar_hdr = smem_u32(&sh.bar[5]);
@@ -449,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
 
     uint32_t last = p.last_seq;
     uint32_t n_done = 0;
-    uint32_t ph_ab[2] = {0, 0};
+    uint32_t ph_a = 0, ph_b = 0;
     uint32_t ph_g = 0, ph_hdr = 0, ph_x = 0;
     const int first_l = p.stage_first[k.stage];
     const int last_l = p.stage_last[k.stage];
@@ -593,13 +607,17 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 EpiRows epi{stg, L.R, bias, scale, L.act, L.round_out};
                 layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
                 __syncthreads();
-                const int bi = L.out_buf == BUF_A ? 0 : 1;
-                push_rows(k, stg, L.R, nrows, buf_addr(k, L.out_buf), L.out_ld, (int)k.rank * L.R, bar_ab[bi], 0,
-                          p.C);
+                const bool use_a = L.out_buf == BUF_A;
+                const uint32_t bar = use_a ? bar_a : bar_b;
+                const uint32_t ph = use_a ? ph_a : ph_b;
+                push_rows(k, stg, L.R, nrows, buf_addr(k, L.out_buf), L.out_ld, (int)k.rank * L.R, bar, 0, p.C);
                 if (tid == 0)
-                    mbar_arrive_expect_tx(bar_ab[bi], (uint32_t)(nrows * L.Mp * 4));
-                ok = cta_wait_bar(k, bar_ab[bi], ph_ab[bi] & 1u, EW_LAYER_BASE + (uint32_t)l, p.step_ns);
-                ++ph_ab[bi];
+                    mbar_arrive_expect_tx(bar, (uint32_t)(nrows * L.Mp * 4));
+                ok = cta_wait_bar(k, bar, ph & 1u, EW_LAYER_BASE + (uint32_t)l, p.step_ns);
+                if (use_a)
+                    ++ph_a;
+                else
+                    ++ph_b;
                 break;
             }
             case LM_KSPLIT_GATHER: {
@@ -713,7 +731,6 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                     } else {
                         // release: y reaches the host before seq_out (src/bench_persistent_mbyv_mlp.cu:365-370)
                         st_release_sys_u32(&p.mb->seq_out, seq);
-                        st_relaxed_sys_u32(&p.ctrl->served, seq);
                     }
                     trace(k, n_done, 14);
                 }

@@ -222,7 +222,7 @@ def test_dense_launch_per_layer_kernels():
     rng = np.random.default_rng(2)
     for M, K, act in ((256, 64, ll.ACT_RELU), (16, 256, ll.ACT_IDENTITY), (1, 64, ll.ACT_IDENTITY),
                       (597, 293, ll.ACT_GELU), (33, 5, ll.ACT_RELU)):
-        W = rng.standard_normal((M, K)).astype(np.float32) / np.sqrt(K)
+        W = (rng.standard_normal((M, K)) / np.sqrt(K)).astype(np.float32)
         b = rng.standard_normal(M).astype(np.float32) * 0.01
         x = rng.standard_normal(K).astype(np.float32)
         ref = oracle.gemv_bias_act(W, b, x, act)
