@@ -93,7 +93,9 @@ typedef struct ll_engine_opts {
     int32_t diag_wait_never;    /* test hook: rank 0 waits on a barrier nothing completes, so the bounded
                                    wait runs out after step_timeout_ns and the kernel reports
                                    LL_ERR_DEVICE_FAULT at location 6 and leaves (no fault is caused) */
-    int32_t reserved[5];
+    int32_t kernel_variant;     /* 0 = automatic, 1 = generic shared-memory kernel, 2 = register-resident
+                                   kernel compiled for the net's shape (3-layer fp32, batch 1) */
+    int32_t reserved[4];
 } ll_engine_opts;
 
 typedef struct ll_engine_info {
@@ -108,6 +110,8 @@ typedef struct ll_engine_info {
     int32_t err_where;      /* device-side location code of the last error */
     uint32_t served;        /* last seq the device published */
     int32_t layer_modes[24];
+    int32_t kernel_variant; /* 1 generic, 2 register-resident */
+    int32_t weight_regs;    /* register-resident: weights held per thread */
 } ll_engine_info;
 
 /*

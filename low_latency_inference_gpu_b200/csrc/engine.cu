@@ -10,6 +10,7 @@
 
 #include "common.h"
 #include "engine_types.h"
+#include "fast3_kernel.cuh"
 #include "resident_kernel.cuh"
 
 #if defined(__x86_64__)
@@ -306,6 +307,73 @@ void pack_image(const ll_net_desc &net, const PlanResult &pr, int s, int rank, c
     }
 }
 
+// Register-resident kernels compiled for specific 3-layer shapes.
+struct Fast3Entry {
+    int in, h1, h2, out, C;
+    const void *fn;
+    int K1, K2, K3, NB;
+    int S1, S2, R2;
+};
+
+template <int IN, int H1, int H2, int OUT, int C>
+Fast3Entry fast3_entry()
+{
+    using S = Fast3Shape<IN, H1, H2, OUT, C>;
+    return Fast3Entry{IN, H1, H2, OUT, C, reinterpret_cast<const void *>(&ll_fast3_kernel<IN, H1, H2, OUT, C>),
+                      S::K1, S::K2, S::K3, S::NB, S::S1, S::S2, S::R2};
+}
+
+const Fast3Entry *find_fast3(const ll_net_desc &net, int C)
+{
+    static const Fast3Entry table[] = {
+        fast3_entry<64, 256, 256, 16, 4>(),  // fp32 64->256->256->16 (the batch-1 latency workload)
+        fast3_entry<64, 256, 256, 16, 8>(),
+    };
+    if (net.n_layers != 3 || net.max_batch != 1 || net.layers[0].wtype != LL_W_F32)
+        return nullptr;
+    for (const Fast3Entry &e : table) {
+        if (e.in == net.layers[0].in_dim && e.h1 == net.layers[0].out_dim && e.h2 == net.layers[1].out_dim &&
+            e.out == net.layers[2].out_dim && (C == 0 || C == e.C))
+            return &e;
+    }
+    return nullptr;
+}
+
+// Per-CTA image of the register-resident kernel: [NW][kThreads] weights (thread-minor, so the
+// one-time load is coalesced), then biases b1[H1], this CTA's b2 rows, b3[OUT].
+std::vector<uint8_t> pack_fast3(const Fast3Entry &f, const void *const *W, const float *const *b, size_t &stride)
+{
+    const int T = kThreads, NW = f.K1 + f.K2 + f.K3;
+    stride = llh::round_up(((size_t)NW * T + f.NB) * 4, 256);
+    std::vector<uint8_t> img((size_t)f.C * stride, 0);
+    const float *W1 = static_cast<const float *>(W[0]);
+    const float *W2 = static_cast<const float *>(W[1]);
+    const float *W3 = static_cast<const float *>(W[2]);
+    for (int c = 0; c < f.C; ++c) {
+        float *o = reinterpret_cast<float *>(img.data() + (size_t)c * stride);
+        for (int t = 0; t < T; ++t) {
+            const int r1 = t / f.S1, s1 = t % f.S1;
+            for (int j = 0; j < f.K1; ++j)
+                o[(size_t)j * T + t] = W1[(size_t)r1 * f.in + s1 * f.K1 + j];
+            const int g2 = c * f.R2 + t / f.S2, s2 = t % f.S2;
+            for (int j = 0; j < f.K2; ++j)
+                o[(size_t)(f.K1 + j) * T + t] = W2[(size_t)g2 * f.h1 + s2 * f.K2 + j];
+            const int w = t / 32, lane = t % 32;
+            for (int j = 0; j < f.K3; ++j)
+                o[(size_t)(f.K1 + f.K2 + j) * T + t] =
+                    w < f.out ? W3[(size_t)w * f.h2 + c * f.R2 + lane * f.K3 + j] : 0.0f;
+        }
+        float *bo = o + (size_t)NW * T;
+        for (int i = 0; i < f.h1; ++i)
+            bo[i] = b && b[0] ? b[0][i] : 0.0f;
+        for (int i = 0; i < f.R2; ++i)
+            bo[f.h1 + i] = b && b[1] ? b[1][c * f.R2 + i] : 0.0f;
+        for (int i = 0; i < f.out; ++i)
+            bo[f.h1 + f.R2 + i] = b && b[2] ? b[2][i] : 0.0f;
+    }
+    return img;
+}
+
 }  // namespace
 
 struct ll_engine {
@@ -333,6 +401,9 @@ struct ll_engine {
     int last_status = LL_OK;
     ll_engine_opts opts{};
     bool attrs_set = false;
+    const void *kfn = nullptr;  // kernel launched (generic or register-resident)
+    int variant = 1;
+    int weight_regs = 0;
 };
 
 extern "C" void ll_engine_opts_default(ll_engine_opts *o)
@@ -468,10 +539,12 @@ int set_kernel_attrs(ll_engine *e)
 {
     if (e->attrs_set)
         return LL_OK;
-    LL_CUDA_TRY(cudaFuncSetAttribute(ll_resident_mlp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)e->base.smem_bytes));
+    if (!e->kfn)
+        e->kfn = reinterpret_cast<const void *>(&ll_resident_mlp_kernel);
+    if (e->base.smem_bytes > 0)
+        LL_CUDA_TRY(cudaFuncSetAttribute(e->kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->base.smem_bytes));
     if (e->base.C > 8)
-        LL_CUDA_TRY(cudaFuncSetAttribute(ll_resident_mlp_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        LL_CUDA_TRY(cudaFuncSetAttribute(e->kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     e->attrs_set = true;
     return LL_OK;
 }
@@ -500,14 +573,15 @@ int launch(ll_engine *e, const Params &p)
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int max_clusters = 0;
-    cudaError_t oe = cudaOccupancyMaxActiveClusters(&max_clusters, ll_resident_mlp_kernel, &cfg);
+    cudaError_t oe = cudaOccupancyMaxActiveClusters(&max_clusters, e->kfn, &cfg);
     if (oe != cudaSuccess || max_clusters < p.n_stages) {
         llh::set_error("resident kernel needs %d co-resident clusters of %d CTAs (%u B smem); device fits %d (%s)",
                        p.n_stages, p.C, p.smem_bytes, max_clusters, cudaGetErrorString(oe));
         cudaGetLastError();
         return LL_ERR_BAD_DESC;
     }
-    LL_CUDA_TRY(cudaLaunchKernelEx(&cfg, ll_resident_mlp_kernel, p));
+    void *args[] = {const_cast<Params *>(&p)};
+    LL_CUDA_TRY(cudaLaunchKernelExC(&cfg, e->kfn, args));
     ++e->launches;
     return LL_OK;
 }
@@ -759,6 +833,60 @@ void export_plan(const Params &p, ll_plan *out)
     }
 }
 
+int create_fast3(const ll_net_desc *net, const void *const *W, const float *const *b, int device,
+                 const ll_engine_opts &o, const Fast3Entry &f, ll_engine **out)
+{
+    size_t stride = 0;
+    std::vector<uint8_t> img = pack_fast3(f, W, b, stride);
+    ll_engine *e = new ll_engine();
+    e->device = device;
+    e->in_dim = f.in;
+    e->out_dim = f.out;
+    e->max_batch = 1;
+    e->kfn = f.fn;
+    e->variant = 2;
+    e->weight_regs = f.K1 + f.K2 + f.K3;
+    int rc = engine_common_create(e, &o);
+    if (rc) {
+        ll_engine_destroy(e);
+        return rc;
+    }
+    PlanResult &pr = e->plan;
+    pr.S = 1;
+    pr.C = f.C;
+    pr.stage_first = {0};
+    pr.stage_last = {2};
+    pr.stage_in_ld = {f.in};
+    pr.stage_image = {img.size() / f.C};
+    Params &p = e->base;
+    p.n_layers = 3;
+    p.act_bf16 = 0;
+    for (int l = 0; l < 3; ++l) {
+        p.L[l] = LayerDev{};
+        p.L[l].act = net->layers[l].act;
+        p.L[l].M = net->layers[l].out_dim;
+    }
+    layout_buffers(p, pr, f.in, f.out, 1);
+    p.smem_bytes = 0;  // all shared memory of this kernel is static
+    p.image_stride = (uint32_t)stride;
+    cudaError_t ce = cudaMalloc((void **)&e->d_image, img.size());
+    if (ce == cudaSuccess)
+        ce = cudaMemcpy(e->d_image, img.data(), img.size(), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        llh::set_error("uploading register images: %s", cudaGetErrorString(ce));
+        ll_engine_destroy(e);
+        return LL_ERR_CUDA;
+    }
+    p.image = e->d_image;
+    rc = finish_setup(e);
+    if (rc) {
+        ll_engine_destroy(e);
+        return rc;
+    }
+    *out = e;
+    return LL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -776,8 +904,22 @@ int ll_engine_create_ex(const ll_net_desc *net, const void *const *W, const floa
         o = *opts;
     else
         ll_engine_opts_default(&o);
+    int rc = validate_net(net, W);
+    if (rc)
+        return rc;
+    if (!W) {
+        llh::set_error("W is NULL");
+        return LL_ERR_INVALID_ARG;
+    }
+    const Fast3Entry *f3 = o.kernel_variant == 1 ? nullptr : find_fast3(*net, o.cluster_size);
+    if (o.kernel_variant == 2 && !f3) {
+        llh::set_error("no register-resident kernel is compiled for this net shape / cluster size");
+        return LL_ERR_UNSUPPORTED;
+    }
+    if (f3)
+        return create_fast3(net, W, b, device, o, *f3, out);
     Packed pk;
-    int rc = plan_and_pack(net, W, b, scales, o, true, pk);
+    rc = plan_and_pack(net, W, b, scales, o, true, pk);
     if (rc)
         return rc;
     ll_engine *e = new ll_engine();
@@ -1018,6 +1160,8 @@ int ll_engine_get_info(ll_engine *e, ll_engine_info *info)
     info->served = static_cast<ll_tick_header *>(e->mb_host)->seq_out;
     for (int l = 0; l < e->base.n_layers && l < 24; ++l)
         info->layer_modes[l] = e->base.L[l].mode;
+    info->kernel_variant = e->variant;
+    info->weight_regs = e->weight_regs;
     return LL_OK;
 }
 

@@ -1,0 +1,292 @@
+// Register-resident resident kernel for 3-layer fp32 nets (IN -> H1 -> H2 -> OUT),
+// batch 1, compiled per shape.
+//
+// Every weight lives in a register for the whole launch (the register file is
+// 256 KB per SM; a cluster of C CTAs holds the net), so per request only x and
+// the activations move, through shared memory and DSMEM:
+//   rank 0  : polls the mailbox header (one 16-byte acquire load), reads x once,
+//             pushes {seq, x} into every peer's shared memory (st.async, one mbarrier);
+//   layer 1 : replicated in every CTA, S1 = T/H1 threads per row, K1 = IN/S1 weights
+//             per thread, butterfly over the S1 lanes;
+//   layer 2 : rows split over the cluster (R2 = H2/C per CTA), S2 = T/R2 threads per
+//             row, K2 = H1/S2 weights per thread;
+//   layer 3 : K-split over the local R2 rows: warp w owns output w, each lane K3 = R2/32
+//             weights; one partial per output is pushed to rank 0, which adds the C
+//             partials in rank order, writes y and release-stores seq_out.
+// The reference's closest kernel keeps only layer 1 resident (registers / SMEM /
+// global scratch per thread, src/bench_persistent_mbyv_mlp.cu:159-221) and re-reads
+// the rest every tick; its layer barriers are global atomics (:308-377).
+#pragma once
+#include "engine_types.h"
+#include "ptx.cuh"
+#include "resident_kernel.cuh"
+
+namespace llk {
+
+template <int IN, int H1, int H2, int OUT, int C>
+struct Fast3Shape {
+    static constexpr int T = kThreads;
+    static constexpr int S1 = T / H1;
+    static constexpr int K1 = IN / S1;
+    static constexpr int R2 = H2 / C;
+    static constexpr int S2 = T / R2;
+    static constexpr int K2 = H1 / S2;
+    static constexpr int K3 = R2 / 32;
+    static constexpr int NW = K1 + K2 + K3;  // weights per thread
+    static_assert(T % H1 == 0 && IN % S1 == 0 && K1 % 4 == 0, "layer-1 split");
+    static_assert(H2 % C == 0 && T % R2 == 0 && H1 % S2 == 0 && K2 % 4 == 0, "layer-2 split");
+    static_assert(R2 % 32 == 0 && K3 >= 1, "layer-3 split");
+    static_assert(OUT >= 1 && OUT <= T / 32 && OUT % 4 == 0, "one warp per output, float4 stores");
+    static_assert(S1 <= 32 && S2 <= 32 && (S1 & (S1 - 1)) == 0 && (S2 & (S2 - 1)) == 0, "butterfly groups");
+    static_assert(IN % 4 == 0, "x is moved in 16-byte pieces");
+    static constexpr int NB = H1 + R2 + OUT;  // biases per CTA image
+};
+
+__device__ __forceinline__ float relu_or(float v, int act)
+{
+    return act == LL_ACT_RELU ? fmaxf(v, 0.0f) : (act == LL_ACT_GELU ? act_apply(v, LL_ACT_GELU) : v);
+}
+
+template <int IN, int H1, int H2, int OUT, int C>
+__global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_constant__ Params pg)
+{
+    using S = Fast3Shape<IN, H1, H2, OUT, C>;
+    __shared__ __align__(16) float xs[IN];
+    __shared__ __align__(16) float h1[H1];
+    __shared__ __align__(16) float h2[S::R2];
+    __shared__ __align__(16) float gath[C * OUT];
+    __shared__ __align__(16) float bias[S::NB];
+    __shared__ __align__(16) Shared sh;
+    __shared__ __align__(16) Params sp;
+    {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(&pg);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(&sp);
+        for (int i = threadIdx.x; i < (int)(sizeof(Params) / 4); i += kThreads)
+            dst[i] = src[i];
+    }
+    __syncthreads();
+    const Params &p = sp;
+    KernelCtx k;
+    k.p = &p;
+    k.sh = &sh;
+    k.smem = nullptr;
+    k.rank = cluster_ctarank();
+    k.stage = 0;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool leader = k.rank == 0;
+    const uint32_t bar_req = smem_u32(&sh.bar[5]);
+    const uint32_t bar_g = smem_u32(&sh.bar[3]);
+    const uint32_t bar_diag = smem_u32(&sh.bar[4]);
+    const int act1 = p.L[0].act, act2 = p.L[1].act, act3 = p.L[2].act;
+
+    if (tid == 0) {
+        for (int i = 0; i < 7; ++i)
+            mbar_init(smem_u32(&sh.bar[i]), 1);
+        sh.cmd = 0;
+        sh.fail = 0;
+        sh.abort = 0;
+        fence_mbar_init_cluster();
+        if (leader)
+            st_relaxed_sys_u32(&p.ctrl->state, ST_LOADING);
+    }
+    // ---- weights into registers (coalesced: image is [NW][T] floats per CTA), biases into SMEM ----
+    const float *img = reinterpret_cast<const float *>(p.image + (size_t)blockIdx.x * p.image_stride);
+    float w1[S::K1], w2[S::K2], w3[S::K3];
+#pragma unroll
+    for (int j = 0; j < S::K1; ++j)
+        w1[j] = __ldg(img + (size_t)j * kThreads + tid);
+#pragma unroll
+    for (int j = 0; j < S::K2; ++j)
+        w2[j] = __ldg(img + (size_t)(S::K1 + j) * kThreads + tid);
+#pragma unroll
+    for (int j = 0; j < S::K3; ++j)
+        w3[j] = __ldg(img + (size_t)(S::K1 + S::K2 + j) * kThreads + tid);
+    for (int i = tid; i < S::NB; i += kThreads)
+        bias[i] = __ldg(img + (size_t)S::NW * kThreads + i);
+    for (int i = tid; i < C * OUT; i += kThreads)
+        gath[i] = 0.0f;
+    __syncthreads();
+    cluster_sync();
+    if (leader && tid == 0)
+        st_relaxed_sys_u32(&p.ctrl->state, ST_RUNNING);
+
+    bool ok = true;
+    if (p.diag_wait_never && leader)
+        ok = cta_wait_bar(k, bar_diag, 0, EW_DIAG, p.step_ns);
+
+    const int r1 = tid / S::S1, s1 = tid % S::S1;
+    const int r2 = tid / S::S2, s2 = tid % S::S2;
+    const uint32_t x_addr = smem_u32(xs), h_addr = smem_u32(sh.hdr), g_addr = smem_u32(gath);
+    uint32_t last = p.last_seq, n_done = 0, ph_req = 0, ph_g = 0;
+
+    while (ok) {
+        uint32_t seq;
+        if (p.mode == MODE_QUEUE && (int)n_done >= p.q_n)
+            break;
+        // ---------------- request ----------------
+        if (leader) {
+            if (p.mode == MODE_QUEUE) {
+                seq = n_done + 1;
+                if (tid == 0)
+                    trace(k, n_done, 0);
+                const float *src = p.q_x + (size_t)n_done * IN;
+                if (tid < IN / 4)
+                    reinterpret_cast<float4 *>(xs)[tid] = __ldg(reinterpret_cast<const float4 *>(src) + tid);
+            } else {
+                if (tid == 0) {
+                    uint32_t nr = 1;
+                    const uint32_t c = poll_mailbox(k, last, &nr);
+                    if (c == kCmdExit)
+                        broadcast_abort(k);
+                    sh.cmd = c;
+                    trace(k, n_done, 0);
+                }
+                __syncthreads();
+                seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
+                if (seq == kCmdExit)
+                    break;
+                if (tid < IN / 4)
+                    reinterpret_cast<float4 *>(xs)[tid] = ld_relaxed_sys_v4(p.mb_x + tid * 4);
+            }
+            __syncthreads();
+            if (tid == 0)
+                trace(k, n_done, 1);
+            // push {seq} + x to every peer: (C-1) * (1 + IN/4) st.async of 16 bytes, one mbarrier each
+            constexpr int per = 1 + IN / 4;
+            if (tid < (C - 1) * per) {
+                const uint32_t d = 1u + (uint32_t)(tid / per);
+                const int j = tid % per;
+                if (j == 0)
+                    st_async_v4(mapa(h_addr, d), make_float4(__uint_as_float(seq), 0.f, 0.f, 0.f), mapa(bar_req, d));
+                else
+                    st_async_v4(mapa(x_addr + (uint32_t)(j - 1) * 16u, d), reinterpret_cast<const float4 *>(xs)[j - 1],
+                                mapa(bar_req, d));
+            }
+            if (tid == 0)
+                trace(k, n_done, 2);
+        } else {
+            if (tid == 0)
+                mbar_arrive_expect_tx(bar_req, 16u + 4u * IN);
+            if (!cta_wait_bar(k, bar_req, ph_req & 1u, EW_PEER_POLL, p.idle_ns + p.peer_margin_ns))
+                break;
+            ++ph_req;
+            seq = *reinterpret_cast<volatile uint32_t *>(&sh.hdr[0]);
+            if (tid == 0 && k.rank == 1)
+                trace(k, n_done, 15);
+        }
+
+        // ---------------- layer 1 (replicated) ----------------
+        {
+            const float4 *x4 = reinterpret_cast<const float4 *>(xs + s1 * S::K1);
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < S::K1 / 4; ++j) {
+                const float4 v = x4[j];
+                a0 = fmaf(w1[4 * j], v.x, a0);
+                a1 = fmaf(w1[4 * j + 1], v.y, a1);
+                a0 = fmaf(w1[4 * j + 2], v.z, a0);
+                a1 = fmaf(w1[4 * j + 3], v.w, a1);
+            }
+            float acc = a0 + a1;
+#pragma unroll
+            for (int o = S::S1 / 2; o > 0; o >>= 1)
+                acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (s1 == 0)
+                h1[r1] = relu_or(acc + bias[r1], act1);
+        }
+        __syncthreads();
+        if (leader && tid == 0)
+            trace(k, n_done, 3);
+        // ---------------- layer 2 (rows split over the cluster) ----------------
+        {
+            const float4 *v4 = reinterpret_cast<const float4 *>(h1 + s2 * S::K2);
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < S::K2 / 4; ++j) {
+                const float4 v = v4[j];
+                a0 = fmaf(w2[4 * j], v.x, a0);
+                a1 = fmaf(w2[4 * j + 1], v.y, a1);
+                a0 = fmaf(w2[4 * j + 2], v.z, a0);
+                a1 = fmaf(w2[4 * j + 3], v.w, a1);
+            }
+            float acc = a0 + a1;
+#pragma unroll
+            for (int o = S::S2 / 2; o > 0; o >>= 1)
+                acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (s2 == 0)
+                h2[r2] = relu_or(acc + bias[H1 + r2], act2);
+        }
+        __syncthreads();
+        if (leader && tid == 0)
+            trace(k, n_done, 4);
+        // ---------------- layer 3 (K-split partials -> rank 0) ----------------
+        if (warp < OUT) {
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < S::K3; ++j)
+                acc = fmaf(w3[j], h2[lane * S::K3 + j], acc);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+                acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (lane == 0)
+                st_async_u32(mapa(g_addr + (uint32_t)(k.rank * OUT + warp) * 4u, 0u), __float_as_uint(acc),
+                             mapa(bar_g, 0u));
+        }
+        if (leader && tid == 0)
+            trace(k, n_done, 5);
+
+        // ---------------- rank 0: sum partials, write y, publish ----------------
+        if (leader) {
+            if (tid == 0)
+                mbar_arrive_expect_tx(bar_g, (uint32_t)(C * OUT * 4));
+            ok = cta_wait_bar(k, bar_g, ph_g & 1u, EW_GATHER, p.step_ns);
+            ++ph_g;
+            if (!ok)
+                break;
+            if (tid == 0)
+                trace(k, n_done, 12);
+            if (warp == 0) {
+                float v = 0.f;
+                if (lane < OUT) {
+#pragma unroll
+                    for (int c = 0; c < C; ++c)
+                        v += gath[c * OUT + lane];
+                    v = relu_or(v + bias[H1 + S::R2 + lane], act3);
+                }
+                // lanes 0..OUT/4-1 gather four neighbours and store 16 bytes
+                const float v1 = __shfl_down_sync(0xffffffffu, v, 1);
+                const float v2 = __shfl_down_sync(0xffffffffu, v, 2);
+                const float v3 = __shfl_down_sync(0xffffffffu, v, 3);
+                const float4 q = make_float4(v, v1, v2, v3);
+                if ((lane & 3) == 0 && lane < OUT) {
+                    if (p.mode == MODE_QUEUE)
+                        reinterpret_cast<float4 *>(p.q_y + (size_t)n_done * OUT)[lane >> 2] = q;
+                    else
+                        st_relaxed_sys_v4(p.mb_y + lane, q);
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    trace(k, n_done, 13);
+                    if (p.mode == MODE_QUEUE) {
+                        if (p.q_stamp)
+                            p.q_stamp[n_done] = globaltimer();
+                    } else {
+                        st_release_sys_u32(&p.mb->seq_out, seq);
+                    }
+                    trace(k, n_done, 14);
+                }
+            }
+        }
+        last = seq;
+        ++n_done;
+    }
+    __syncthreads();
+    cluster_sync();
+    if (leader && tid == 0) {
+        if (p.mode == MODE_QUEUE)
+            st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_QUEUE_DONE);
+        st_release_sys_u32(&p.ctrl->state, ST_EXITED);
+    }
+}
+
+}  // namespace llk

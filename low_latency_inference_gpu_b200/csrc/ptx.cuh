@@ -92,6 +92,13 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float4 v, uin
                  : "memory");
 }
 
+__device__ __forceinline__ void st_async_u32(uint32_t cluster_addr, uint32_t v, uint32_t cluster_bar)
+{
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(cluster_addr),
+                 "r"(v), "r"(cluster_bar)
+                 : "memory");
+}
+
 __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v)
 {
     asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");

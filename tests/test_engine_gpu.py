@@ -65,7 +65,7 @@ def test_config0_parity_oracle_and_golden(golden):
     with engine_for(net, Ws, bs) as e:
         ys = np.stack([e.infer(xs[i])[0] for i in range(64)])
         info = e.info()
-    assert info.n_stages == 1 and info.cluster_size == 16
+    assert info.kernel_variant == 2 and info.cluster_size == 4  # register-resident kernel by default
     ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
     assert rel_err(ys, ref) <= 1e-5
     gy = unbits(g["y"]).reshape(g["n"], -1)
@@ -94,13 +94,41 @@ def test_config1_multi_cluster_parity(golden):
     assert rel_err(ys[: g["n"]], unbits(g["y"]).reshape(g["n"], -1)) <= 1e-5
 
 
-@pytest.mark.parametrize("C,rep", [(2, 0), (4, 1), (8, 0), (8, 1), (16, 0)])
-def test_config0_cluster_sizes(C, rep):
+@pytest.mark.parametrize("C,rep", [(2, 0), (4, 1), (8, 0), (8, 1), (16, 0), (16, 1)])
+def test_config0_generic_kernel_cluster_sizes(C, rep):
     net, Ws, bs = ll.config_params(0)
     xs = ll.config_inputs(0, 8)
-    with engine_for(net, Ws, bs, cluster_size=C, replicate_first=rep) as e:
+    with engine_for(net, Ws, bs, cluster_size=C, replicate_first=rep, kernel_variant=1) as e:
         ys = np.stack([e.infer(xs[i])[0] for i in range(8)])
+        assert e.info().kernel_variant == 1
     assert rel_err(ys, oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)) <= 1e-5
+
+
+@pytest.mark.parametrize("C", [4, 8])
+def test_config0_register_resident_kernel(C):
+    torch = pytest.importorskip("torch")
+    net, Ws, bs = ll.config_params(0)
+    n = 300
+    xs = ll.config_inputs(0, n)
+    ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
+    with engine_for(net, Ws, bs, cluster_size=C, kernel_variant=2) as e:
+        info = e.info()
+        assert info.kernel_variant == 2 and info.cluster_size == C and info.weight_regs > 0
+        lat, ys = e.bench_closed_loop(xs, n, keep_outputs=True)
+        dx = torch.from_numpy(xs).cuda()
+        dy = torch.zeros((n, 16), device="cuda")
+        torch.cuda.synchronize()
+        e.run_queue(dx.data_ptr(), dy.data_ptr(), n, 1)
+    assert rel_err(ys[:, 0, :], ref) <= 1e-5
+    assert rel_err(dy.cpu().numpy(), ref) <= 1e-5
+
+
+def test_register_resident_kernel_refuses_other_shapes():
+    net = ll.mlp([32, 64, 16], ll.ACT_RELU)
+    Ws, bs = ll.init_params(net, ll.INIT_XAVIER_UNIFORM, 1)
+    with pytest.raises(ll.LLError) as e:
+        engine_for(net, Ws, bs, kernel_variant=2)
+    assert e.value.code == ll.LL_ERR_UNSUPPORTED
 
 
 @pytest.mark.parametrize("wtype,act,rows", [(ll.W_F32, ll.ACT_RELU, 3), (ll.W_BF16, ll.ACT_GELU, 5),
@@ -166,7 +194,8 @@ def test_closed_loop_bench_outputs():
     assert rel_err(ys[:, 0, :], ref[np.arange(500) % 32]) <= 1e-5
 
 
-def test_device_resident_queue():
+@pytest.mark.parametrize("variant", [1, 2])
+def test_device_resident_queue(variant):
     torch = pytest.importorskip("torch")
     net, Ws, bs = ll.config_params(0)
     n = 256
@@ -176,7 +205,7 @@ def test_device_resident_queue():
     dy = torch.zeros((n, 16), dtype=torch.float32, device="cuda:0")
     st = torch.zeros(n, dtype=torch.int64, device="cuda:0")
     torch.cuda.synchronize()
-    with engine_for(net, Ws, bs) as e:
+    with engine_for(net, Ws, bs, kernel_variant=variant) as e:
         ms = e.run_queue(dx.data_ptr(), dy.data_ptr(), n, 1, st.data_ptr())
         # the mailbox path still works after a queue run
         y = e.infer(xs[3])
@@ -187,11 +216,12 @@ def test_device_resident_queue():
     assert (np.diff(stamps) > 0).all()
 
 
-def test_idle_exit_and_relaunch():
+@pytest.mark.parametrize("variant", [1, 2])
+def test_idle_exit_and_relaunch(variant):
     net, Ws, bs = ll.config_params(0)
     xs = ll.config_inputs(0, 4)
     ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
-    with engine_for(net, Ws, bs, idle_timeout_ns=int(50e6)) as e:
+    with engine_for(net, Ws, bs, idle_timeout_ns=int(50e6), kernel_variant=variant) as e:
         y0 = e.infer(xs[0])
         time.sleep(0.3)  # longer than the idle bound: the resident kernel leaves on its own
         assert e.info().state == 4
@@ -201,13 +231,14 @@ def test_idle_exit_and_relaunch():
     assert rel_err(np.stack([y0[0], y1[0]]), ref[:2]) <= 1e-5
 
 
-def test_device_wait_that_runs_out_reports_status_and_context_survives():
+@pytest.mark.parametrize("variant", [1, 2])
+def test_device_wait_that_runs_out_reports_status_and_context_survives(variant):
     """A device wait on a barrier nothing completes (diag_wait_never) runs out after the
     50 ms step bound: the kernel records LL_ERR_DEVICE_FAULT with its location and leaves
     cleanly -- no trap, no hang -- and the CUDA context stays usable."""
     net, Ws, bs = ll.config_params(0)
     x = ll.config_inputs(0, 1)
-    with engine_for(net, Ws, bs, step_timeout_ns=int(50e6), diag_wait_never=1) as e:
+    with engine_for(net, Ws, bs, step_timeout_ns=int(50e6), diag_wait_never=1, kernel_variant=variant) as e:
         with pytest.raises(ll.LLError) as err:
             e.infer(x[0], timeout_s=5.0)
         assert err.value.code == ll.LL_ERR_DEVICE_FAULT
