@@ -351,17 +351,19 @@ std::vector<uint8_t> pack_fast3(const Fast3Entry &f, const void *const *W, const
     const float *W3 = static_cast<const float *>(W[2]);
     for (int c = 0; c < f.C; ++c) {
         float *o = reinterpret_cast<float *>(img.data() + (size_t)c * stride);
+        // weight j of a thread pairs with input element 4*(s + S*(j/4)) + j%4 (16-byte pieces
+        // interleaved across the S lanes of a row group); layer 3: local row lane + 32*j
         for (int t = 0; t < T; ++t) {
             const int r1 = t / f.S1, s1 = t % f.S1;
             for (int j = 0; j < f.K1; ++j)
-                o[(size_t)j * T + t] = W1[(size_t)r1 * f.in + s1 * f.K1 + j];
+                o[(size_t)j * T + t] = W1[(size_t)r1 * f.in + 4 * (s1 + f.S1 * (j / 4)) + j % 4];
             const int g2 = c * f.R2 + t / f.S2, s2 = t % f.S2;
             for (int j = 0; j < f.K2; ++j)
-                o[(size_t)(f.K1 + j) * T + t] = W2[(size_t)g2 * f.h1 + s2 * f.K2 + j];
+                o[(size_t)(f.K1 + j) * T + t] = W2[(size_t)g2 * f.h1 + 4 * (s2 + f.S2 * (j / 4)) + j % 4];
             const int w = t / 32, lane = t % 32;
             for (int j = 0; j < f.K3; ++j)
                 o[(size_t)(f.K1 + f.K2 + j) * T + t] =
-                    w < f.out ? W3[(size_t)w * f.h2 + c * f.R2 + lane * f.K3 + j] : 0.0f;
+                    w < f.out ? W3[(size_t)w * f.h2 + c * f.R2 + lane + 32 * j] : 0.0f;
         }
         float *bo = o + (size_t)NW * T;
         for (int i = 0; i < f.h1; ++i)

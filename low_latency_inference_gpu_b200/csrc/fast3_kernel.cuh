@@ -10,8 +10,10 @@
 //             per thread, butterfly over the S1 lanes;
 //   layer 2 : rows split over the cluster (R2 = H2/C per CTA), S2 = T/R2 threads per
 //             row, K2 = H1/S2 weights per thread;
-//   layer 3 : K-split over the local R2 rows: warp w owns output w, each lane K3 = R2/32
-//             weights; one partial per output is pushed to rank 0, which adds the C
+//   (lane s of a row group takes the 16-byte input pieces s, s+S, s+2S, ... so the
+//   eight lanes of a quarter-warp read 128 consecutive bytes: no bank conflicts)
+//   layer 3 : K-split over the local R2 rows: warp w owns output w, lane l takes local
+//             rows l, l+32, ...; one partial per output is pushed to rank 0, which adds the C
 //             partials in rank order, writes y and release-stores seq_out.
 // The reference's closest kernel keeps only layer 1 resident (registers / SMEM /
 // global scratch per thread, src/bench_persistent_mbyv_mlp.cu:159-221) and re-reads
@@ -91,16 +93,17 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
     }
     // ---- weights into registers (coalesced: image is [NW][T] floats per CTA), biases into SMEM ----
     const float *img = reinterpret_cast<const float *>(p.image + (size_t)blockIdx.x * p.image_stride);
+    // volatile loads: the compiler may not re-issue them later, so the weights stay in registers
     float w1[S::K1], w2[S::K2], w3[S::K3];
 #pragma unroll
     for (int j = 0; j < S::K1; ++j)
-        w1[j] = __ldg(img + (size_t)j * kThreads + tid);
+        w1[j] = ld_once_f32(img + (size_t)j * kThreads + tid);
 #pragma unroll
     for (int j = 0; j < S::K2; ++j)
-        w2[j] = __ldg(img + (size_t)(S::K1 + j) * kThreads + tid);
+        w2[j] = ld_once_f32(img + (size_t)(S::K1 + j) * kThreads + tid);
 #pragma unroll
     for (int j = 0; j < S::K3; ++j)
-        w3[j] = __ldg(img + (size_t)(S::K1 + S::K2 + j) * kThreads + tid);
+        w3[j] = ld_once_f32(img + (size_t)(S::K1 + S::K2 + j) * kThreads + tid);
     for (int i = tid; i < S::NB; i += kThreads)
         bias[i] = __ldg(img + (size_t)S::NW * kThreads + i);
     for (int i = tid; i < C * OUT; i += kThreads)
@@ -177,11 +180,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
 
         // ---------------- layer 1 (replicated) ----------------
         {
-            const float4 *x4 = reinterpret_cast<const float4 *>(xs + s1 * S::K1);
+            const float4 *x4 = reinterpret_cast<const float4 *>(xs) + s1;
             float a0 = 0.f, a1 = 0.f;
 #pragma unroll
             for (int j = 0; j < S::K1 / 4; ++j) {
-                const float4 v = x4[j];
+                const float4 v = x4[j * S::S1];
                 a0 = fmaf(w1[4 * j], v.x, a0);
                 a1 = fmaf(w1[4 * j + 1], v.y, a1);
                 a0 = fmaf(w1[4 * j + 2], v.z, a0);
@@ -199,11 +202,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             trace(k, n_done, 3);
         // ---------------- layer 2 (rows split over the cluster) ----------------
         {
-            const float4 *v4 = reinterpret_cast<const float4 *>(h1 + s2 * S::K2);
+            const float4 *v4 = reinterpret_cast<const float4 *>(h1) + s2;
             float a0 = 0.f, a1 = 0.f;
 #pragma unroll
             for (int j = 0; j < S::K2 / 4; ++j) {
-                const float4 v = v4[j];
+                const float4 v = v4[j * S::S2];
                 a0 = fmaf(w2[4 * j], v.x, a0);
                 a1 = fmaf(w2[4 * j + 1], v.y, a1);
                 a0 = fmaf(w2[4 * j + 2], v.z, a0);
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             float acc = 0.f;
 #pragma unroll
             for (int j = 0; j < S::K3; ++j)
-                acc = fmaf(w3[j], h2[lane * S::K3 + j], acc);
+                acc = fmaf(w3[j], h2[lane + 32 * j], acc);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1)
                 acc += __shfl_xor_sync(0xffffffffu, acc, o);

@@ -213,6 +213,14 @@ __device__ __forceinline__ uint32_t ld_relaxed_gpu_u32(const unsigned *p)
     return v;
 }
 
+// A load the compiler must keep: used to pin values in registers (no rematerialisation).
+__device__ __forceinline__ float ld_once_f32(const float *p)
+{
+    float v;
+    asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ float4 ld_cg_v4(const float *p)
 {
     float4 v;
