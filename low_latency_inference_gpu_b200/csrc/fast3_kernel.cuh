@@ -87,6 +87,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
         sh.cmd = 0;
         sh.fail = 0;
         sh.abort = 0;
+        sh.hstop = 0;
         fence_mbar_init_cluster();
         if (leader)
             st_relaxed_sys_u32(&p.ctrl->state, ST_LOADING);
@@ -137,8 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     reinterpret_cast<float4 *>(xs)[tid] = __ldg(reinterpret_cast<const float4 *>(src) + tid);
             } else {
                 if (tid == 0) {
-                    uint32_t nr = 1;
-                    const uint32_t c = poll_mailbox(k, last, &nr);
+                    const uint32_t c = poll_mailbox(k, last);
                     if (c == kCmdExit)
                         broadcast_abort(k);
                     sh.cmd = c;
@@ -148,10 +148,20 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                 seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
                 if (seq == kCmdExit)
                     break;
+                // header (stop flag) and x in one round trip
                 if (tid < IN / 4)
                     reinterpret_cast<float4 *>(xs)[tid] = ld_relaxed_sys_v4(p.mb_x + tid * 4);
+                else if (tid == kThreads - 32)
+                    read_header(k);
             }
             __syncthreads();
+            if (*reinterpret_cast<volatile uint32_t *>(&sh.hstop)) {
+                if (tid == 0) {
+                    st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
+                    broadcast_abort(k);
+                }
+                break;
+            }
             if (tid == 0)
                 trace(k, n_done, 1);
             // push {seq} + x to every peer: (C-1) * (1 + IN/4) st.async of 16 bytes, one mbarrier each

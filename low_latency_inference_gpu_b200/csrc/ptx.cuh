@@ -144,6 +144,16 @@ __device__ __forceinline__ void fence_acq_rel_sys()
     asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4_u32(const unsigned *p)
+{
+    uint4 v;
+    asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
 __device__ __forceinline__ float4 ld_relaxed_sys_v4(const float *p)
 {
     float4 v;

@@ -35,6 +35,7 @@ struct Shared {
     uint32_t nrows;
     uint32_t fail;
     uint32_t abort;
+    uint32_t hstop;  // stop flag seen in the header that came with the current doorbell
 };
 
 __device__ __forceinline__ float act_apply(float v, int act)
@@ -237,34 +238,43 @@ __device__ __forceinline__ bool cta_wait_bar(const KernelCtx &k, uint32_t bar, u
 }
 
 // Thread 0 of the dispatcher (rank 0 of stage 0): wait for a new request.
-// One 16-byte acquire load returns seq_in, seq_out, stop and n_rows together.
+// The poll reads seq_in alone: a wider load would cover seq_out, which this
+// thread has just release-stored, and would wait behind that PCIe write.
+// `stop` is checked on the idle cadence here; a stop that arrives with a
+// doorbell (src/bench_persistent_mbyv_mlp.cu:554-557) is caught by
+// header_says_stop() in the same round trip that fetches x.
 // Returns the sequence number, or kCmdExit (stop, idle bound, abort).
-__device__ uint32_t poll_mailbox(const KernelCtx &k, uint32_t last, uint32_t *nrows)
+__device__ uint32_t poll_mailbox(const KernelCtx &k, uint32_t last)
 {
     const Params &p = *k.p;
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 0;; ++it) {
-        const uint4 h = ld_acquire_sys_v4(reinterpret_cast<const unsigned *>(p.mb));
-        if (h.z) {
-            // stop, with or without a doorbell bump (src/bench_persistent_mbyv_mlp.cu:554-557,
-            // src/bench_persistent_mlp.cu:409)
-            st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
-            return kCmdExit;
-        }
-        if (h.x != last && h.x != 0) {
-            const uint32_t n = h.w == 0 ? 1u : h.w;
-            *nrows = n > (uint32_t)p.max_batch ? (uint32_t)p.max_batch : n;
-            return h.x;
-        }
+        const uint32_t s = ld_acquire_sys(&p.mb->seq_in);
+        if (s != last && s != 0)
+            return s;
         if ((it & 63u) == 63u) {
             if (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort) || global_abort(k))
                 return kCmdExit;
+            if (ld_relaxed_sys(&p.mb->stop)) {  // stop without a doorbell (src/bench_persistent_mlp.cu:409)
+                st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
+                return kCmdExit;
+            }
             if (globaltimer() - t0 > p.idle_ns) {
                 st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_IDLE);
                 return kCmdExit;
             }
         }
     }
+}
+
+// One thread reads the 16-byte header after the doorbell: stop flag and row count.
+__device__ __forceinline__ void read_header(const KernelCtx &k)
+{
+    const Params &p = *k.p;
+    const uint4 h = ld_relaxed_sys_v4_u32(reinterpret_cast<const unsigned *>(p.mb));
+    const uint32_t n = h.w == 0 ? 1u : h.w;
+    k.sh->nrows = n > (uint32_t)p.max_batch ? (uint32_t)p.max_batch : n;
+    k.sh->hstop = h.z;
 }
 
 __device__ __forceinline__ float *buf_ptr(const KernelCtx &k, int id)
@@ -425,6 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
         sh.nrows = 1;
         sh.fail = 0;
         sh.abort = 0;
+        sh.hstop = 0;
         fence_mbar_init_cluster();
         if (leader)
             st_relaxed_sys_u32(&p.ctrl->state, ST_LOADING);
@@ -502,20 +513,36 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 stage_input_device(k, p.q_x + (size_t)n_done * p.q_rows * p.in_dim, nrows);
             } else {
                 if (tid == 0) {
-                    uint32_t nr = 1;
-                    const uint32_t c = poll_mailbox(k, last, &nr);
+                    const uint32_t c = poll_mailbox(k, last);
                     if (c == kCmdExit)
                         broadcast_abort(k);
                     sh.cmd = c;
-                    sh.nrows = nr;
                     trace(k, n_done, 0);
                 }
                 __syncthreads();
                 seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
-                nrows = (int)*reinterpret_cast<volatile uint32_t *>(&sh.nrows);
                 if (seq == kCmdExit)
                     break;
-                stage_input_mailbox(k, nrows);
+                if (p.max_batch == 1) {
+                    // header and x in one round trip
+                    if (tid == kThreads - 32)
+                        read_header(k);
+                    stage_input_mailbox(k, 1);
+                    __syncthreads();
+                } else {
+                    if (tid == 0)
+                        read_header(k);
+                    __syncthreads();
+                    stage_input_mailbox(k, (int)*reinterpret_cast<volatile uint32_t *>(&sh.nrows));
+                }
+                nrows = (int)*reinterpret_cast<volatile uint32_t *>(&sh.nrows);
+                if (*reinterpret_cast<volatile uint32_t *>(&sh.hstop)) {
+                    if (tid == 0) {
+                        st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
+                        broadcast_abort(k);
+                    }
+                    break;
+                }
             }
             __syncthreads();
             if (tid == 0)
