@@ -240,9 +240,9 @@ __device__ __forceinline__ bool cta_wait_bar(const KernelCtx &k, uint32_t bar, u
 // Thread 0 of the dispatcher (rank 0 of stage 0): wait for a new request.
 // The poll reads seq_in alone: a wider load would cover seq_out, which this
 // thread has just release-stored, and would wait behind that PCIe write.
-// `stop` is checked on the idle cadence here; a stop that arrives with a
-// doorbell (src/bench_persistent_mbyv_mlp.cu:554-557) is caught by
-// header_says_stop() in the same round trip that fetches x.
+// `stop` is checked on the idle cadence here; for batched nets a stop that
+// arrives with a doorbell (src/bench_persistent_mbyv_mlp.cu:554-557) is also
+// caught by read_header() before the request's rows are read.
 // Returns the sequence number, or kCmdExit (stop, idle bound, abort).
 __device__ uint32_t poll_mailbox(const KernelCtx &k, uint32_t last)
 {
@@ -524,9 +524,12 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 if (seq == kCmdExit)
                     break;
                 if (p.max_batch == 1) {
-                    // header and x in one round trip
-                    if (tid == kThreads - 32)
-                        read_header(k);
+                    // batch 1: no header fetch (n_rows is 1; stop is seen on the idle cadence, so a
+                    // stop that comes with a doorbell bump costs one extra, harmless reply)
+                    if (tid == 0) {
+                        sh.nrows = 1;
+                        sh.hstop = 0;
+                    }
                     stage_input_mailbox(k, 1);
                     __syncthreads();
                 } else {
