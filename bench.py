@@ -39,6 +39,11 @@ WORKLOAD = "config-0 MLP 64->256->256->16 fp32 (ReLU, identity out), batch 1, se
 WEIGHT_BYTES = (64 * 256 + 256 * 256 + 256 * 16) * 4 + (256 + 256 + 16) * 4  # resident weights + biases
 IO_BYTES = 64 * 4 + 16 * 4
 FALLBACK_HBM_GBS = 6650.0
+# DRAM traffic of one device-queue launch, from the committed ncu capture
+# (profiles/ll_fast3_kernel_config0_queue_full.md: 1.080 MB for 2000 requests):
+# the weights once, then ~367 B per request (input row, output, stamp); scaled to R requests.
+TRAFFIC_FIXED_BYTES = 345_000
+TRAFFIC_PER_REQUEST_BYTES = 367
 
 
 def env_int(name, default):
@@ -351,7 +356,8 @@ def main():
                           "e2e_p50_over_io_floor": s_e2e["p50"] / floor["x_to_y"]["p50_us"]},
         "comparison_paths": compare,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": None,
+                     "peak_kind": peak_kind,
+                     "traffic": TRAFFIC_FIXED_BYTES + R * TRAFFIC_PER_REQUEST_BYTES if info.kernel_variant == 2 else None,
                      "note": "algorithmic bytes = resident weights+biases (345 KB) + x/y per request; the batch-1 "
                              "path is latency-bound, latency_floor is its relevant bound"},
         "cpu_baseline": cpu_baseline,
