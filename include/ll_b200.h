@@ -243,6 +243,28 @@ int ll_dense_warp_rm(const float *W, const float *b, const float *x, float *y, i
  * (include/ll/dense_mbyv_packed.cuh:53-63). */
 int ll_dense_mbyv_packed(const float *W_cm, const float *b_pad, const float *x, float *y, int M, int K, int act,
                          void *stream);
+/*
+ * MLP forward that allocates nothing (no counterpart in the reference).
+ * For callers that cannot call cudaMalloc on their request path -- it may
+ * implicitly synchronise the device and take milliseconds -- or whose device
+ * memory is owned by another allocator.  Same kernels as ll_layered_mlp's direct
+ * path: one ll_dense_warp_rm launch per layer on `stream`, on the current device.
+ * d_W / d_b are host arrays of device pointers (fp32, row-major [out x in];
+ * d_b may be NULL), d_x / d_y device vectors; batch 1.
+ * The hidden activations live in a library-owned static device array of
+ * 2 x LL_NOALLOC_MAX_WIDTH floats (64 KB per GPU, held until the process
+ * exits); a hidden width above LL_NOALLOC_MAX_WIDTH is rejected with
+ * LL_ERR_INVALID_ARG.  The first call on a device looks the array up with
+ * cudaGetSymbolAddress; make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller.  Nothing in
+ * the array needs to start at zero: every layer writes all the values the next
+ * one reads.
+ */
+#define LL_NOALLOC_MAX_WIDTH 8192
+int ll_mlp_forward_noalloc(const ll_net_desc *net, const float *const *d_W, const float *const *d_b,
+                           const float *d_x, float *d_y, void *stream);
+
 /* Host packing, include/ll/pack_weights.cuh:16-32. */
 void ll_pack_rm_to_kmajor_padded(const float *W_rm, size_t M, size_t K, float *W_cm, size_t Mpad);
 void ll_pack_bias_padded(const float *b, size_t M, float *b_pad, size_t Mpad);

@@ -51,7 +51,7 @@ EXPORTED_SYMBOLS = [
     "ll_layered_mlp_bench", "ll_layered_mlp_destroy", "ll_cublas_mlp_create", "ll_cublas_mlp_bench",
     "ll_cublas_mlp_destroy", "ll_fill_normal", "ll_fill_uniform", "ll_init_params", "ll_f32_to_bf16",
     "ll_quantize_int8_rows", "ll_compute_stats", "ll_mailbox_bytes", "ll_mailbox_post", "ll_mailbox_wait",
-    "ll_next_seq", "ll_version", "ll_plan_net", "ll_engine_set_trace",
+    "ll_next_seq", "ll_version", "ll_plan_net", "ll_engine_set_trace", "ll_mlp_forward_noalloc",
 ]
 
 
@@ -144,6 +144,7 @@ def _sig(lib):
         "ll_engine_bench_closed_loop": (ctypes.c_int, [_vp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _fp, _dp]),
         "ll_engine_run_queue": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _fp, _vp]),
         "ll_engine_set_trace": (ctypes.c_int, [_vp, _vp, ctypes.c_int]),
+        "ll_mlp_forward_noalloc": (ctypes.c_int, [P(NetDesc), P(_vp), P(_vp), _vp, _vp, _vp]),
         "ll_last_error": (ctypes.c_char_p, []),
         "ll_dense_warp_rm": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
         "ll_dense_mbyv_packed": (ctypes.c_int, [_vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
@@ -556,3 +557,15 @@ def plan_net(net: Net, W=None, b=None, scales=None, opts: Optional[EngineOpts] =
                              img.ctypes.data, img.size, ctypes.byref(need)))
     del keep
     return plan, img
+
+
+NOALLOC_MAX_WIDTH = 8192
+
+
+def mlp_forward_noalloc(net: Net, d_W_ptrs, d_b_ptrs, d_x_ptr: int, d_y_ptr: int, stream: int = 0):
+    """Forward pass that allocates nothing (see ll_mlp_forward_noalloc in include/ll_b200.h):
+    device pointers in, device pointer out, hidden activations in a static library-owned array."""
+    d = net.desc()
+    Wp = (_vp * net.n_layers)(*d_W_ptrs)
+    bp = (_vp * net.n_layers)(*d_b_ptrs) if d_b_ptrs is not None else None
+    _check(lib().ll_mlp_forward_noalloc(ctypes.byref(d), Wp, bp, d_x_ptr, d_y_ptr, stream or None))
