@@ -85,7 +85,8 @@ typedef struct ll_engine_opts {
     int32_t cluster_size;       /* CTAs per cluster: 1,2,4,8,16; 0 = automatic */
     int32_t replicate_first;    /* first layer computed by every CTA: -1 auto, 0 no, 1 yes */
     int32_t write_combined;     /* allocate the mailbox write-combined (reference default) */
-    int32_t mailbox_format;     /* 0 = the reference's TickBuffer layout (the only format so far) */
+    int32_t mailbox_format;     /* 0 = the reference's TickBuffer layout; 1 = tagged chunks (batch 1,
+                                   see ll_tagged_post): no x read after the doorbell, no release fence */
     uint64_t idle_timeout_ns;   /* resident kernel exits after this long idle; relaunched on demand */
     uint64_t step_timeout_ns;   /* bound on every device wait inside one request */
     int32_t max_stages;         /* cap on pipeline stages (clusters); 0 = automatic */
@@ -330,6 +331,22 @@ void ll_mailbox_post(void *mailbox, int in_dim, const float *x, int n_rows, uint
 /* Spin until seq_out == seq (acquire) or timeout; copies n_rows*out_dim floats of y. LL_OK / LL_ERR_TIMEOUT. */
 int ll_mailbox_wait(const void *mailbox, int in_dim, int out_dim, int max_batch, uint32_t seq, float *y,
                     int n_rows, uint64_t timeout_ns);
+/*
+ * Tagged mailbox (mailbox_format 1, batch-1 nets; no counterpart in the reference,
+ * whose TickBuffer needs a second PCIe round trip to read x after seq_in and a
+ * release fence before seq_out).  Layout: the 16-byte header, then
+ * ceil(in_dim/3) x chunks, then ceil(out_dim/3) y chunks; a chunk is 16 bytes
+ * {v0, v1, v2, tag} written with one aligned 16-byte store (atomic on x86 CPUs
+ * with AVX and for one 16-byte GPU access), tag = the request's sequence number.
+ * The device polls the x chunks themselves and takes the request when every tag
+ * carries the same new sequence number; it writes the y chunks with relaxed
+ * stores and the host waits until every y tag equals its sequence number.
+ * Limits: in_dim <= 384, out_dim <= 96.
+ */
+size_t ll_tagged_mailbox_bytes(int in_dim, int out_dim);
+void ll_tagged_post(void *mailbox, int in_dim, const float *x, uint32_t seq);
+int ll_tagged_wait(const void *mailbox, int in_dim, int out_dim, uint32_t seq, float *y, uint64_t timeout_ns);
+
 /* Next sequence number after seq: skips 0 (idle) and LL_STOP_SEQ. */
 uint32_t ll_next_seq(uint32_t seq);
 

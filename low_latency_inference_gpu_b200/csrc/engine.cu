@@ -461,7 +461,17 @@ int validate_net(const ll_net_desc *net, const void *const *W)
 
 int alloc_mailbox(ll_engine *e)
 {
-    e->mb_bytes = ll_mailbox_bytes(e->in_dim, e->out_dim, e->max_batch);
+    if (e->opts.mailbox_format == 1) {
+        if (e->max_batch != 1 || e->in_dim > 384 || e->out_dim > 96 || e->in_dim < 1 || e->out_dim < 1) {
+            llh::set_error("tagged mailbox (format 1) needs batch 1, 1 <= in_dim <= 384, 1 <= out_dim <= 96");
+            return LL_ERR_UNSUPPORTED;
+        }
+    } else if (e->opts.mailbox_format != 0) {
+        llh::set_error("unknown mailbox format %d", e->opts.mailbox_format);
+        return LL_ERR_INVALID_ARG;
+    }
+    e->mb_bytes = e->opts.mailbox_format == 1 ? ll_tagged_mailbox_bytes(e->in_dim, e->out_dim)
+                                              : ll_mailbox_bytes(e->in_dim, e->out_dim, e->max_batch);
     unsigned flags = cudaHostAllocMapped | cudaHostAllocPortable;
     if (e->wc)
         flags |= cudaHostAllocWriteCombined;
@@ -508,7 +518,11 @@ int finish_setup(ll_engine *e)
     e->grid = pr.S * pr.C;
     p.mb = e->mb_dev;
     p.mb_x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(e->mb_dev) + sizeof(ll_tick_header));
-    p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + sizeof(ll_tick_header) +
+    if (e->opts.mailbox_format == 1)
+        p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + sizeof(ll_tick_header) +
+                                           16 * (size_t)((e->in_dim + 2) / 3));
+    else
+        p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + sizeof(ll_tick_header) +
                                        sizeof(float) * (size_t)e->in_dim * e->max_batch);
     p.ctrl = e->ctrl_dev;
     p.mailbox_format = e->opts.mailbox_format;
@@ -662,16 +676,41 @@ int engine_common_create(ll_engine *e, const ll_engine_opts *opts)
 }
 
 // Spin on seq_out with liveness checks; copies y.
+// Format 1: true once every y chunk carries `seq` (then y is copied out).
+bool tagged_done(ll_engine *e, uint32_t seq, float *y)
+{
+    const int xc = (e->in_dim + 2) / 3, yc = (e->out_dim + 2) / 3;
+    const char *base = static_cast<const char *>(e->mb_host) + sizeof(ll_tick_header) + 16 * (size_t)xc;
+    alignas(16) uint32_t w[4];
+    asm volatile("" ::: "memory");
+    for (int c = 0; c < yc; ++c) {
+        _mm_store_si128(reinterpret_cast<__m128i *>(w), _mm_load_si128(reinterpret_cast<const __m128i *>(base + 16 * c)));
+        if (w[3] != seq)
+            return false;
+        if (y) {
+            float v[3];
+            std::memcpy(v, w, 12);
+            for (int k = 0; k < 3 && 3 * c + k < e->out_dim; ++k)
+                y[3 * c + k] = v[k];
+        }
+    }
+    return true;
+}
+
 int engine_wait(ll_engine *e, uint32_t seq, float *y, int n_rows, uint64_t timeout_ns)
 {
     const ll_tick_header *h = static_cast<const ll_tick_header *>(e->mb_host);
+    const bool tagged = e->opts.mailbox_format == 1;
     const auto t0 = std::chrono::steady_clock::now();
     uint32_t spins = 0;
-    while (__atomic_load_n(const_cast<const uint32_t *>(&h->seq_out), __ATOMIC_ACQUIRE) != seq) {
+    auto done = [&]() {
+        return tagged ? tagged_done(e, seq, y)
+                      : __atomic_load_n(const_cast<const uint32_t *>(&h->seq_out), __ATOMIC_ACQUIRE) == seq;
+    };
+    while (!done()) {
         cpu_relax();
         if ((++spins & 4095u) == 0) {
-            if (e->ctrl_host->state == ST_EXITED &&
-                __atomic_load_n(const_cast<const uint32_t *>(&h->seq_out), __ATOMIC_ACQUIRE) != seq) {
+            if (e->ctrl_host->state == ST_EXITED && !done()) {
                 // kernel left (idle exit raced this request, or a fault): relaunch picks the request up
                 int rc = ensure_running(e);
                 if (rc)
@@ -685,7 +724,7 @@ int engine_wait(ll_engine *e, uint32_t seq, float *y, int n_rows, uint64_t timeo
             }
         }
     }
-    if (y) {
+    if (y && !tagged) {
         const float *yd = reinterpret_cast<const float *>(static_cast<const char *>(e->mb_host) +
                                                           sizeof(ll_tick_header) +
                                                           sizeof(float) * (size_t)e->in_dim * e->max_batch);
@@ -693,6 +732,15 @@ int engine_wait(ll_engine *e, uint32_t seq, float *y, int n_rows, uint64_t timeo
     }
     e->last_served = seq;
     return LL_OK;
+}
+
+// Post one request in the engine's mailbox format.
+void engine_post(ll_engine *e, const float *x, int n_rows, uint32_t seq)
+{
+    if (e->opts.mailbox_format == 1)
+        ll_tagged_post(e->mb_host, e->in_dim, x, seq);
+    else
+        ll_mailbox_post(e->mb_host, e->in_dim, x, n_rows, seq, e->wc);
 }
 
 int engine_stop_kernel(ll_engine *e)
@@ -1036,9 +1084,13 @@ float *ll_engine_mailbox_x(ll_engine *e)
 
 float *ll_engine_mailbox_y(ll_engine *e)
 {
-    return e ? reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + sizeof(ll_tick_header) +
-                                         sizeof(float) * (size_t)e->in_dim * e->max_batch)
-             : nullptr;
+    if (!e)
+        return nullptr;
+    if (e->opts.mailbox_format == 1)  // first y chunk
+        return reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + sizeof(ll_tick_header) +
+                                         16 * (size_t)((e->in_dim + 2) / 3));
+    return reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + sizeof(ll_tick_header) +
+                                     sizeof(float) * (size_t)e->in_dim * e->max_batch);
 }
 
 int ll_engine_start(ll_engine *e)
@@ -1064,7 +1116,11 @@ int ll_submit(ll_engine *e, const float *x, int n_rows, uint32_t *seq)
     if (rc)
         return rc;
     const uint32_t s = ll_next_seq(e->last_served > e->seq ? e->last_served : e->seq);
-    ll_mailbox_post(e->mb_host, e->in_dim, x, n_rows, s, e->wc);
+    if (e->opts.mailbox_format == 1 && !x) {
+        llh::set_error("ll_submit: the tagged mailbox needs x (the chunks carry the sequence number)");
+        return LL_ERR_INVALID_ARG;
+    }
+    engine_post(e, x, n_rows, s);
     e->seq = s;
     e->outstanding = s;
     if (seq)
@@ -1187,7 +1243,7 @@ int ll_engine_bench_closed_loop(ll_engine *e, const float *xs, int n_x, int n_re
     for (int r = 0; r < n_req; ++r) {
         const auto t0 = std::chrono::steady_clock::now();
         const uint32_t s = ll_next_seq(e->last_served > e->seq ? e->last_served : e->seq);
-        ll_mailbox_post(e->mb_host, e->in_dim, xs + (size_t)(r % n_x) * xin, n_rows, s, e->wc);
+        engine_post(e, xs + (size_t)(r % n_x) * xin, n_rows, s);
         e->seq = s;
         e->outstanding = s;
         rc = engine_wait(e, s, ys ? ys + (size_t)r * yout : ybuf.data(), n_rows, 2000ull * 1000 * 1000);

@@ -137,7 +137,17 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                 if (tid < IN / 4)
                     reinterpret_cast<float4 *>(xs)[tid] = __ldg(reinterpret_cast<const float4 *>(src) + tid);
             } else {
-                if (tid == 0) {
+                if (p.mailbox_format == 1) {
+                    if (warp == 0) {
+                        const uint32_t c = poll_tagged(k, last, xs);  // x arrives with the doorbell
+                        if (tid == 0) {
+                            if (c == kCmdExit)
+                                broadcast_abort(k);
+                            sh.cmd = c;
+                            trace(k, n_done, 0);
+                        }
+                    }
+                } else if (tid == 0) {
                     const uint32_t c = poll_mailbox(k, last);
                     if (c == kCmdExit)
                         broadcast_abort(k);
@@ -150,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     break;
                 // batch 1: no header fetch (n_rows is 1; stop is seen on the idle cadence, so a
                 // stop that comes with a doorbell bump costs one extra, harmless reply)
-                if (tid < IN / 4)
+                if (p.mailbox_format == 0 && tid < IN / 4)
                     reinterpret_cast<float4 *>(xs)[tid] = ld_relaxed_sys_v4(p.mb_x + tid * 4);
             }
             __syncthreads();
@@ -263,7 +273,18 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                 const float v2 = __shfl_down_sync(0xffffffffu, v, 2);
                 const float v3 = __shfl_down_sync(0xffffffffu, v, 3);
                 const float4 q = make_float4(v, v1, v2, v3);
-                if ((lane & 3) == 0 && lane < OUT) {
+                const bool tagged = p.mode == MODE_MAILBOX && p.mailbox_format == 1;
+                // tagged output: lane c packs {y[3c], y[3c+1], y[3c+2], seq}
+                constexpr int NYC = (OUT + 2) / 3;
+                const float t0 = __shfl_sync(0xffffffffu, v, (3 * lane) & 31);
+                const float t1 = __shfl_sync(0xffffffffu, v, (3 * lane + 1) & 31);
+                const float t2 = __shfl_sync(0xffffffffu, v, (3 * lane + 2) & 31);
+                if (tagged) {
+                    if (lane < NYC)
+                        st_relaxed_sys_v4(p.mb_y + 4 * lane,
+                                          make_float4(t0, 3 * lane + 1 < OUT ? t1 : 0.f, 3 * lane + 2 < OUT ? t2 : 0.f,
+                                                      __uint_as_float(seq)));
+                } else if ((lane & 3) == 0 && lane < OUT) {
                     if (p.mode == MODE_QUEUE)
                         reinterpret_cast<float4 *>(p.q_y + (size_t)n_done * OUT)[lane >> 2] = q;
                     else
@@ -275,6 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     if (p.mode == MODE_QUEUE) {
                         if (p.q_stamp)
                             p.q_stamp[n_done] = globaltimer();
+                    } else if (tagged) {
+                        st_relaxed_sys_u32(&p.mb->seq_out, seq);  // bookkeeping only: the host waits on the tags
                     } else {
                         st_release_sys_u32(&p.mb->seq_out, seq);
                     }

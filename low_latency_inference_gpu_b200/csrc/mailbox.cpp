@@ -76,6 +76,75 @@ size_t ll_mailbox_bytes(int in_dim, int out_dim, int max_batch)
     return llh::round_up(sizeof(ll_tick_header) + 4 * b * (size_t)in_dim + 4 * b * (size_t)out_dim, 64);
 }
 
+size_t ll_tagged_mailbox_bytes(int in_dim, int out_dim)
+{
+    const size_t xc = (size_t)(in_dim + 2) / 3, yc = (size_t)(out_dim + 2) / 3;
+    return llh::round_up(sizeof(ll_tick_header) + 16 * (xc + yc), 64);
+}
+
+void ll_tagged_post(void *mailbox, int in_dim, const float *x, uint32_t seq)
+{
+    const int xc = (in_dim + 2) / 3;
+    char *base = static_cast<char *>(mailbox) + sizeof(ll_tick_header);
+    for (int c = 0; c < xc; ++c) {
+        float v[3];
+        for (int e = 0; e < 3; ++e)
+            v[e] = 3 * c + e < in_dim ? x[3 * c + e] : 0.0f;
+        uint32_t w[4];
+        std::memcpy(w, v, 12);
+        w[3] = seq;
+#if defined(__x86_64__)
+        // one aligned 16-byte store: the device never sees half a chunk
+        _mm_store_si128(reinterpret_cast<__m128i *>(base + 16 * c),
+                        _mm_set_epi32((int)w[3], (int)w[2], (int)w[1], (int)w[0]));
+#else
+        __atomic_store(reinterpret_cast<__int128 *>(base + 16 * c), reinterpret_cast<__int128 *>(w), __ATOMIC_RELAXED);
+#endif
+    }
+    auto *h = static_cast<ll_tick_header *>(mailbox);
+    h->n_rows = 1;
+    // seq_in keeps its meaning for hosts and tools that watch it; the device polls the chunks
+    __atomic_store_n(const_cast<uint32_t *>(&h->seq_in), seq, __ATOMIC_RELEASE);
+}
+
+int ll_tagged_wait(const void *mailbox, int in_dim, int out_dim, uint32_t seq, float *y, uint64_t timeout_ns)
+{
+    const int xc = (in_dim + 2) / 3, yc = (out_dim + 2) / 3;
+    const char *base = static_cast<const char *>(mailbox) + sizeof(ll_tick_header) + 16 * (size_t)xc;
+    const auto t0 = std::chrono::steady_clock::now();
+    uint32_t spins = 0;
+    alignas(16) uint32_t w[4];
+    for (;;) {
+        asm volatile("" ::: "memory");  // re-read the chunks every iteration
+        int c = 0;
+        for (; c < yc; ++c) {
+#if defined(__x86_64__)
+            _mm_store_si128(reinterpret_cast<__m128i *>(w), _mm_load_si128(reinterpret_cast<const __m128i *>(base + 16 * c)));
+#else
+            __atomic_load(reinterpret_cast<const __int128 *>(base + 16 * c), reinterpret_cast<__int128 *>(w), __ATOMIC_ACQUIRE);
+#endif
+            if (w[3] != seq)
+                break;
+            if (y) {
+                float v[3];
+                std::memcpy(v, w, 12);
+                for (int e = 0; e < 3 && 3 * c + e < out_dim; ++e)
+                    y[3 * c + e] = v[e];
+            }
+        }
+        if (c == yc)
+            return LL_OK;
+        cpu_relax();
+        if ((++spins & 1023u) == 0) {
+            const auto dt = std::chrono::steady_clock::now() - t0;
+            if ((uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(dt).count() > timeout_ns) {
+                llh::set_error("tagged mailbox wait for seq %u timed out", seq);
+                return LL_ERR_TIMEOUT;
+            }
+        }
+    }
+}
+
 uint32_t ll_next_seq(uint32_t seq)
 {
     uint32_t n = seq + 1u;

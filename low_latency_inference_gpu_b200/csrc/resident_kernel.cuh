@@ -267,6 +267,64 @@ __device__ uint32_t poll_mailbox(const KernelCtx &k, uint32_t last)
     }
 }
 
+// Tagged mailbox (format 1), warp 0 of the dispatcher: every lane loads up to
+// kTagChunksPerLane 16-byte x chunks {v0, v1, v2, tag} per poll; the request is
+// taken when every chunk carries the same new tag, and its floats go straight
+// into X -- detection and the x read are one PCIe round trip.
+constexpr int kTagChunksPerLane = 4;
+
+__device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X)
+{
+    const Params &p = *k.p;
+    const int lane = threadIdx.x & 31;
+    const int nxc = (p.in_dim + 2) / 3;
+    const uint4 *chunks = reinterpret_cast<const uint4 *>(p.mb_x);
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+        uint4 c[kTagChunksPerLane];
+#pragma unroll
+        for (int j = 0; j < kTagChunksPerLane; ++j)
+            if (lane + 32 * j < nxc)
+                c[j] = ld_relaxed_sys_v4_u32(reinterpret_cast<const unsigned *>(chunks + lane + 32 * j));
+        const uint32_t tag = __shfl_sync(0xffffffffu, c[0].w, 0);
+        bool same = true;
+#pragma unroll
+        for (int j = 0; j < kTagChunksPerLane; ++j)
+            if (lane + 32 * j < nxc && c[j].w != tag)
+                same = false;
+        if (__all_sync(0xffffffffu, same) && tag != last && tag != 0) {
+#pragma unroll
+            for (int j = 0; j < kTagChunksPerLane; ++j) {
+                const int ch = lane + 32 * j;
+                if (ch < nxc) {
+                    const float v[3] = {__uint_as_float(c[j].x), __uint_as_float(c[j].y), __uint_as_float(c[j].z)};
+#pragma unroll
+                    for (int e = 0; e < 3; ++e)
+                        if (3 * ch + e < p.in_dim)
+                            X[3 * ch + e] = p.act_bf16 ? round_bf16(v[e]) : v[e];
+                }
+            }
+            return tag;
+        }
+        if ((it & 63u) == 63u) {
+            uint32_t verdict = 0;
+            if (lane == 0) {
+                if (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort) || global_abort(k)) {
+                    verdict = 1;
+                } else if (ld_relaxed_sys(&p.mb->stop)) {
+                    st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_STOP);
+                    verdict = 1;
+                } else if (globaltimer() - t0 > p.idle_ns) {
+                    st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_IDLE);
+                    verdict = 1;
+                }
+            }
+            if (__shfl_sync(0xffffffffu, verdict, 0))
+                return kCmdExit;
+        }
+    }
+}
+
 // One thread reads the 16-byte header after the doorbell: stop flag and row count.
 __device__ __forceinline__ void read_header(const KernelCtx &k)
 {
@@ -512,7 +570,19 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                     trace(k, n_done, 0);
                 stage_input_device(k, p.q_x + (size_t)n_done * p.q_rows * p.in_dim, nrows);
             } else {
-                if (tid == 0) {
+                if (p.mailbox_format == 1) {
+                    if (tid < 32) {
+                        const uint32_t c = poll_tagged(k, last, buf_ptr(k, BUF_X));
+                        if (tid == 0) {
+                            if (c == kCmdExit)
+                                broadcast_abort(k);
+                            sh.cmd = c;
+                            sh.nrows = 1;
+                            sh.hstop = 0;
+                            trace(k, n_done, 0);
+                        }
+                    }
+                } else if (tid == 0) {
                     const uint32_t c = poll_mailbox(k, last);
                     if (c == kCmdExit)
                         broadcast_abort(k);
@@ -523,7 +593,9 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
                 if (seq == kCmdExit)
                     break;
-                if (p.max_batch == 1) {
+                if (p.mailbox_format == 1) {
+                    // x already in X
+                } else if (p.max_batch == 1) {
                     // batch 1: no header fetch (n_rows is 1; stop is seen on the idle cadence, so a
                     // stop that comes with a doorbell bump costs one extra, harmless reply)
                     if (tid == 0) {
@@ -721,7 +793,41 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
             }
             if (tid == 0)
                 trace(k, n_done, 12);
-            if (tid < 32) {
+            if (tid < 32 && p.mode == MODE_MAILBOX && p.mailbox_format == 1) {
+                // tagged output: chunk c = {y[3c], y[3c+1], y[3c+2], seq}, relaxed stores, no fence
+                const int out = p.out_dim, nyc = (out + 2) / 3;
+                const float *fbias = Lf ? reinterpret_cast<const float *>(smem + Lf->b_off) : nullptr;
+                const float *fscale =
+                    (Lf && Lf->s_off != 0xffffffffu) ? reinterpret_cast<const float *>(smem + Lf->s_off) : nullptr;
+                const int fact = Lf ? Lf->act : LL_ACT_IDENTITY;
+                for (int ch = tid; ch < nyc; ch += 32) {
+                    float v[3] = {0.f, 0.f, 0.f};
+                    for (int e = 0; e < 3; ++e) {
+                        const int o = 3 * ch + e;
+                        if (o >= out)
+                            break;
+                        if (Lf == nullptr) {
+                            v[e] = o < p.in_dim ? G[o] : 0.0f;
+                        } else if (ksplit) {
+                            float acc = 0.0f;
+                            for (int c = 0; c < p.C; ++c)
+                                acc += G[(size_t)c * p.bmax4 * ld_g + o];
+                            if (fscale)
+                                acc *= fscale[o];
+                            v[e] = act_apply(acc + fbias[o], fact);
+                        } else {
+                            v[e] = G[o];
+                        }
+                    }
+                    st_relaxed_sys_v4(p.mb_y + 4 * ch, make_float4(v[0], v[1], v[2], __uint_as_float(seq)));
+                }
+                __syncwarp();
+                if (tid == 0) {
+                    trace(k, n_done, 13);
+                    st_relaxed_sys_u32(&p.mb->seq_out, seq);  // bookkeeping only: the host waits on the tags
+                    trace(k, n_done, 14);
+                }
+            } else if (tid < 32) {
                 const int out = p.out_dim;
                 float *ydst = p.mode == MODE_QUEUE ? p.q_y + (size_t)n_done * p.q_rows * out : p.mb_y;
                 const float *fbias = Lf ? reinterpret_cast<const float *>(smem + Lf->b_off) : nullptr;

@@ -183,3 +183,63 @@ def test_invalid_arguments_are_rejected_without_gpu():
     assert lib.ll_engine_create_ex(None, None, None, None, 0, None, ctypes.byref(h)) == ll.LL_ERR_BAD_DESC
     assert lib.ll_dense_warp_rm(None, None, None, None, 4, 4, 0, None) == ll.LL_ERR_INVALID_ARG
     assert lib.ll_submit(None, None, 1, None) == ll.LL_ERR_INVALID_ARG
+
+
+class FakeTaggedDevice(threading.Thread):
+    """CPU stand-in for the device on the tagged mailbox: takes a request when every x chunk
+    carries the same new tag, answers y = 2*x[:out] + seq in tagged chunks (floats, then tag)."""
+
+    def __init__(self, buf, in_dim, out_dim):
+        super().__init__(daemon=True)
+        self.buf, self.in_dim, self.out_dim = buf, in_dim, out_dim
+        self.stop_flag = False
+
+    def run(self):
+        xc, yc = (self.in_dim + 2) // 3, (self.out_dim + 2) // 3
+        xw = np.frombuffer(self.buf, np.uint32, 4 * xc, 16).reshape(xc, 4)
+        yw = np.frombuffer(self.buf, np.uint32, 4 * yc, 16 + 16 * xc).reshape(yc, 4)
+        last = 0
+        while not self.stop_flag:
+            snap = xw.copy()
+            tags = snap[:, 3]
+            if (tags == tags[0]).all() and tags[0] != last and tags[0] != 0:
+                s = int(tags[0])
+                x = snap[:, :3].copy().view(np.float32).ravel()[: self.in_dim]
+                y = np.zeros(3 * yc, np.float32)
+                y[: self.out_dim] = 2 * x[: self.out_dim] + s
+                yv = y.view(np.uint32).reshape(yc, 3)
+                for c in range(yc):
+                    yw[c, :3] = yv[c]
+                    yw[c, 3] = s
+                last = s
+            else:
+                time.sleep(0)
+
+
+@pytest.mark.parametrize("in_dim,out_dim", [(64, 16), (7, 5), (1, 1), (384, 96)])
+def test_tagged_mailbox_round_trips_with_fake_device(in_dim, out_dim):
+    lib = ll.lib()
+    n = lib.ll_tagged_mailbox_bytes(in_dim, out_dim)
+    assert n % 64 == 0 and n >= 16 + 16 * ((in_dim + 2) // 3 + (out_dim + 2) // 3)
+    buf = (ctypes.c_uint8 * n)()
+    dev = FakeTaggedDevice(buf, in_dim, out_dim)
+    dev.start()
+    seq = 0
+    try:
+        for r in range(20):
+            x = (np.arange(in_dim, dtype=np.float32) * 0.5 + r).astype(np.float32)
+            seq = lib.ll_next_seq(seq)
+            lib.ll_tagged_post(ctypes.addressof(buf), in_dim, x.ctypes.data_as(ll._fp), seq)
+            y = np.empty(out_dim, np.float32)
+            rc = lib.ll_tagged_wait(ctypes.addressof(buf), in_dim, out_dim, seq, y.ctypes.data_as(ll._fp), int(2e9))
+            assert rc == ll.LL_OK
+            assert np.array_equal(y, 2 * x[:out_dim] + seq)
+        # a reply that never comes times out
+        seq2 = lib.ll_next_seq(seq)
+        dev.stop_flag = True
+        dev.join(2)
+        rc = lib.ll_tagged_wait(ctypes.addressof(buf), in_dim, out_dim, seq2, None, int(20e6))
+        assert rc == ll.LL_ERR_TIMEOUT
+    finally:
+        dev.stop_flag = True
+        dev.join(2)

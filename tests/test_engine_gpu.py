@@ -283,3 +283,42 @@ def test_comparison_paths_parity(cls, mode):
         lat, y = m.bench(mode, xs, 5)
     assert (lat > 0).all()
     assert rel_err(y, ref[4]) <= 1e-5  # the last request used xs[4]
+
+
+@pytest.mark.parametrize("variant", [1, 2])
+def test_tagged_mailbox_config0(variant):
+    net, Ws, bs = ll.config_params(0)
+    n = 300
+    xs = ll.config_inputs(0, n)
+    ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
+    with engine_for(net, Ws, bs, mailbox_format=1, kernel_variant=variant) as e:
+        lat, ys = e.bench_closed_loop(xs, n, keep_outputs=True)
+        y1 = e.infer(xs[5])
+    assert rel_err(ys[:, 0, :], ref) <= 1e-5
+    assert rel_err(y1[0], ref[5]) <= 1e-5
+
+
+@pytest.mark.parametrize("dims", [[33, 100, 7], [5, 3], [130, 40, 40, 2]])
+def test_tagged_mailbox_odd_widths_generic(dims):
+    net = ll.mlp(dims, ll.ACT_RELU, ll.ACT_IDENTITY, ll.W_F32, 1)
+    Ws, bs = ll.init_params(net, ll.INIT_XAVIER_UNIFORM, 9)
+    xs = ll.fill_uniform(6 * dims[0], -1, 1, 4).reshape(6, -1)
+    with engine_for(net, Ws, bs, cluster_size=4, mailbox_format=1) as e:
+        ys = np.stack([e.infer(xs[i])[0] for i in range(6)])
+    assert rel_err(ys, oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)) <= 1e-5
+
+
+def test_tagged_echo_floor_copies_x():
+    o = opts(mailbox_format=1)
+    with ll.EchoEngine(64, 16, opts=o) as e:
+        xs = ll.config_inputs(0, 10)
+        for i in range(10):
+            assert np.array_equal(e.infer(xs[i])[0], xs[i, :16])
+
+
+def test_tagged_mailbox_rejects_batches():
+    net = ll.mlp([8, 16, 4], ll.ACT_RELU, ll.ACT_IDENTITY, ll.W_F32, 4)
+    Ws, bs = ll.init_params(net, ll.INIT_XAVIER_UNIFORM, 1)
+    with pytest.raises(ll.LLError) as err:
+        engine_for(net, Ws, bs, mailbox_format=1)
+    assert err.value.code == ll.LL_ERR_UNSUPPORTED
