@@ -341,9 +341,13 @@ int ll_mailbox_wait(const void *mailbox, int in_dim, int out_dim, int max_batch,
  * The device polls the x chunks themselves and takes the request when every tag
  * carries the same new sequence number; it writes the y chunks with relaxed
  * stores and the host waits until every y tag equals its sequence number.
+ * The y chunks start on a fresh 64-byte line (ll_tagged_y_offset): no cache
+ * line holds both host-written x and device-written y.
  * Limits: in_dim <= 384, out_dim <= 96.
  */
 size_t ll_tagged_mailbox_bytes(int in_dim, int out_dim);
+/* Byte offset of the first y chunk: the x chunks' end rounded up to 64. */
+size_t ll_tagged_y_offset(int in_dim);
 void ll_tagged_post(void *mailbox, int in_dim, const float *x, uint32_t seq);
 int ll_tagged_wait(const void *mailbox, int in_dim, int out_dim, uint32_t seq, float *y, uint64_t timeout_ns);
 

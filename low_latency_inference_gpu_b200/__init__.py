@@ -52,7 +52,7 @@ EXPORTED_SYMBOLS = [
     "ll_cublas_mlp_destroy", "ll_fill_normal", "ll_fill_uniform", "ll_init_params", "ll_f32_to_bf16",
     "ll_quantize_int8_rows", "ll_compute_stats", "ll_mailbox_bytes", "ll_mailbox_post", "ll_mailbox_wait",
     "ll_next_seq", "ll_version", "ll_plan_net", "ll_engine_set_trace", "ll_mlp_forward_noalloc",
-    "ll_tagged_mailbox_bytes", "ll_tagged_post", "ll_tagged_wait",
+    "ll_tagged_mailbox_bytes", "ll_tagged_y_offset", "ll_tagged_post", "ll_tagged_wait",
 ]
 
 
@@ -169,6 +169,7 @@ def _sig(lib):
                                            ctypes.c_int, ctypes.c_uint64]),
         "ll_next_seq": (ctypes.c_uint32, [ctypes.c_uint32]),
         "ll_tagged_mailbox_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+        "ll_tagged_y_offset": (ctypes.c_size_t, [ctypes.c_int]),
         "ll_tagged_post": (None, [_vp, ctypes.c_int, _fp, ctypes.c_uint32]),
         "ll_tagged_wait": (ctypes.c_int, [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_uint32, _fp, ctypes.c_uint64]),
         "ll_version": (ctypes.c_char_p, []),

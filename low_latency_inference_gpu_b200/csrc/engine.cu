@@ -519,8 +519,7 @@ int finish_setup(ll_engine *e)
     p.mb = e->mb_dev;
     p.mb_x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(e->mb_dev) + sizeof(ll_tick_header));
     if (e->opts.mailbox_format == 1)
-        p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + sizeof(ll_tick_header) +
-                                           16 * (size_t)((e->in_dim + 2) / 3));
+        p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + ll_tagged_y_offset(e->in_dim));
     else
         p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + sizeof(ll_tick_header) +
                                        sizeof(float) * (size_t)e->in_dim * e->max_batch);
@@ -679,12 +678,11 @@ int engine_common_create(ll_engine *e, const ll_engine_opts *opts)
 // Format 1: true once every y chunk carries `seq` (then y is copied out).
 bool tagged_done(ll_engine *e, uint32_t seq, float *y)
 {
-    const int xc = (e->in_dim + 2) / 3, yc = (e->out_dim + 2) / 3;
-    const char *base = static_cast<const char *>(e->mb_host) + sizeof(ll_tick_header) + 16 * (size_t)xc;
-    alignas(16) uint32_t w[4];
-    asm volatile("" ::: "memory");
+    const int yc = (e->out_dim + 2) / 3;
+    const char *base = static_cast<const char *>(e->mb_host) + ll_tagged_y_offset(e->in_dim);
+    uint32_t w[4];
     for (int c = 0; c < yc; ++c) {
-        _mm_store_si128(reinterpret_cast<__m128i *>(w), _mm_load_si128(reinterpret_cast<const __m128i *>(base + 16 * c)));
+        llh::load16(base + 16 * c, w);  // the whole chunk in one load: tag and values together
         if (w[3] != seq)
             return false;
         if (y) {
@@ -1087,8 +1085,7 @@ float *ll_engine_mailbox_y(ll_engine *e)
     if (!e)
         return nullptr;
     if (e->opts.mailbox_format == 1)  // first y chunk
-        return reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + sizeof(ll_tick_header) +
-                                         16 * (size_t)((e->in_dim + 2) / 3));
+        return reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + ll_tagged_y_offset(e->in_dim));
     return reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + sizeof(ll_tick_header) +
                                      sizeof(float) * (size_t)e->in_dim * e->max_batch);
 }

@@ -76,10 +76,14 @@ size_t ll_mailbox_bytes(int in_dim, int out_dim, int max_batch)
     return llh::round_up(sizeof(ll_tick_header) + 4 * b * (size_t)in_dim + 4 * b * (size_t)out_dim, 64);
 }
 
+size_t ll_tagged_y_offset(int in_dim)
+{
+    return llh::round_up(sizeof(ll_tick_header) + 16 * (size_t)((in_dim + 2) / 3), 64);
+}
+
 size_t ll_tagged_mailbox_bytes(int in_dim, int out_dim)
 {
-    const size_t xc = (size_t)(in_dim + 2) / 3, yc = (size_t)(out_dim + 2) / 3;
-    return llh::round_up(sizeof(ll_tick_header) + 16 * (xc + yc), 64);
+    return llh::round_up(ll_tagged_y_offset(in_dim) + 16 * (size_t)((out_dim + 2) / 3), 64);
 }
 
 void ll_tagged_post(void *mailbox, int in_dim, const float *x, uint32_t seq)
@@ -93,13 +97,7 @@ void ll_tagged_post(void *mailbox, int in_dim, const float *x, uint32_t seq)
         uint32_t w[4];
         std::memcpy(w, v, 12);
         w[3] = seq;
-#if defined(__x86_64__)
-        // one aligned 16-byte store: the device never sees half a chunk
-        _mm_store_si128(reinterpret_cast<__m128i *>(base + 16 * c),
-                        _mm_set_epi32((int)w[3], (int)w[2], (int)w[1], (int)w[0]));
-#else
-        __atomic_store(reinterpret_cast<__int128 *>(base + 16 * c), reinterpret_cast<__int128 *>(w), __ATOMIC_RELAXED);
-#endif
+        llh::store16(base + 16 * c, w);  // one aligned 16-byte store: the device never sees half a chunk
     }
     auto *h = static_cast<ll_tick_header *>(mailbox);
     h->n_rows = 1;
@@ -109,20 +107,15 @@ void ll_tagged_post(void *mailbox, int in_dim, const float *x, uint32_t seq)
 
 int ll_tagged_wait(const void *mailbox, int in_dim, int out_dim, uint32_t seq, float *y, uint64_t timeout_ns)
 {
-    const int xc = (in_dim + 2) / 3, yc = (out_dim + 2) / 3;
-    const char *base = static_cast<const char *>(mailbox) + sizeof(ll_tick_header) + 16 * (size_t)xc;
+    const int yc = (out_dim + 2) / 3;
+    const char *base = static_cast<const char *>(mailbox) + ll_tagged_y_offset(in_dim);
     const auto t0 = std::chrono::steady_clock::now();
     uint32_t spins = 0;
-    alignas(16) uint32_t w[4];
+    uint32_t w[4];
     for (;;) {
-        asm volatile("" ::: "memory");  // re-read the chunks every iteration
         int c = 0;
         for (; c < yc; ++c) {
-#if defined(__x86_64__)
-            _mm_store_si128(reinterpret_cast<__m128i *>(w), _mm_load_si128(reinterpret_cast<const __m128i *>(base + 16 * c)));
-#else
-            __atomic_load(reinterpret_cast<const __int128 *>(base + 16 * c), reinterpret_cast<__int128 *>(w), __ATOMIC_ACQUIRE);
-#endif
+            llh::load16(base + 16 * c, w);  // the whole chunk in one load: tag and values together
             if (w[3] != seq)
                 break;
             if (y) {

@@ -197,7 +197,7 @@ class FakeTaggedDevice(threading.Thread):
     def run(self):
         xc, yc = (self.in_dim + 2) // 3, (self.out_dim + 2) // 3
         xw = np.frombuffer(self.buf, np.uint32, 4 * xc, 16).reshape(xc, 4)
-        yw = np.frombuffer(self.buf, np.uint32, 4 * yc, 16 + 16 * xc).reshape(yc, 4)
+        yw = np.frombuffer(self.buf, np.uint32, 4 * yc, ll.lib().ll_tagged_y_offset(self.in_dim)).reshape(yc, 4)
         last = 0
         while not self.stop_flag:
             snap = xw.copy()
@@ -220,7 +220,9 @@ class FakeTaggedDevice(threading.Thread):
 def test_tagged_mailbox_round_trips_with_fake_device(in_dim, out_dim):
     lib = ll.lib()
     n = lib.ll_tagged_mailbox_bytes(in_dim, out_dim)
-    assert n % 64 == 0 and n >= 16 + 16 * ((in_dim + 2) // 3 + (out_dim + 2) // 3)
+    yoff = lib.ll_tagged_y_offset(in_dim)
+    assert yoff % 64 == 0 and yoff >= 16 + 16 * ((in_dim + 2) // 3)  # y never shares a line with x
+    assert n % 64 == 0 and n >= yoff + 16 * ((out_dim + 2) // 3)
     buf = (ctypes.c_uint8 * n)()
     dev = FakeTaggedDevice(buf, in_dim, out_dim)
     dev.start()
