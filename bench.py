@@ -11,12 +11,15 @@ Reported:
   value   inferences/s with inputs already in HBM: the resident kernel's
           device-queue mode (each request starts after the previous finished,
           so this is 1 / device latency), timed with CUDA events per launch.
-  e2e     inferences/s through the C ABI with host buffers: each request writes
-          x into the host-mapped mailbox, rings seq_in and spins on seq_out, then
-          copies y out (host steady clock; p50/p99 latency included).
-  latency the empty-mailbox ping-pong floor (same kernel, no layers) and the
-          engine's p50 over that floor; the cuBLAS+graph and launch-per-layer
-          graph paths timed end to end in the same run (N=1).
+  e2e     inferences/s through the C ABI (ll_infer's closed loop) with host
+          buffers: each request writes x into the host-mapped mailbox and spins
+          until y is there, then copies y out (host steady clock; p50/p99
+          latency included).  The headline uses the tagged mailbox (x and y in
+          16-byte chunks stamped with the sequence number); `e2e_tickbuffer` is
+          the same loop on the reference's TickBuffer layout.
+  latency the empty-mailbox ping-pong floors (same kernel, no layers) for both
+          formats and the engine's p50 over them; the cuBLAS+graph and
+          launch-per-layer graph paths timed end to end in the same run (N=1).
   cpu_baseline  the reference's own CPU forward (oracle/_ref) on one host core.
   --impl reference  runs the reference's CPU forward on all host cores instead.
 """
@@ -226,16 +229,23 @@ def main():
 
     full = args.only == "all"
     # ---------------- ping-pong floor (same kernel, no layers) ----------------
-    floor = {"seq_only": {"p50_us": float("nan"), "p99_us": float("nan")},
-             "x_to_y": {"p50_us": float("nan"), "p99_us": float("nan")}}
-    for key, (i, o) in ((("seq_only", (0, 0)), ("x_to_y", (64, 16))) if full else ()):
-        with ll.EchoEngine(i, o, device=dev) as e:
-            e.bench_closed_loop(xs if i else None, 2000)
-            lat, _ = e.bench_closed_loop(xs if i else None, 20000)
+    def opts(fmt):
+        o = ll.default_opts()
+        o.mailbox_format = fmt
+        return o
+
+    nan = {"p50_us": float("nan"), "p99_us": float("nan")}
+    floor = {"seq_only": nan, "x_to_y": nan, "tagged_one_chunk": nan, "tagged_x_to_y": nan}
+    floor_cases = (("seq_only", 0, 0, 0), ("x_to_y", 64, 16, 0), ("tagged_one_chunk", 3, 3, 1),
+                   ("tagged_x_to_y", 64, 16, 1))
+    for key, i, o, fmt in (floor_cases if full else ()):
+        with ll.EchoEngine(i, o, device=dev, opts=opts(fmt)) as e:
+            e.bench_closed_loop(xs[:, :i] if i else None, 2000)
+            lat, _ = e.bench_closed_loop(xs[:, :i] if i else None, 20000)
         s = ll.compute_stats(lat)
         floor[key] = {"p50_us": s["p50"], "p99_us": s["p99"]}
 
-    engine = ll.Engine(net, Ws, bs, device=dev)
+    engine = ll.Engine(net, Ws, bs, device=dev, opts=opts(1))
     info = engine.info()
 
     # ---------------- value: device-resident sequential queue ----------------
@@ -268,30 +278,39 @@ def main():
     dev_stats = ll.compute_stats(np.array(dev_lat))
 
     # ---------------- e2e: mailbox with host buffers through the C ABI ----------------
-    lat_all = []
-    t0 = time.perf_counter()
-    e2e_launches = 0
-    if full:
-        engine.start()
-        launches_before = engine.info().launches
+    def closed_loop(eng):
+        """K timed steps of R sequential requests; returns (seconds, latencies, relaunches)."""
+        lat_all = []
+        eng.start()
+        before = eng.info().launches
         for _ in range(W):
-            engine.bench_closed_loop(xs, R)
+            eng.bench_closed_loop(xs, R)
         torch.cuda.current_stream().synchronize()
         host_barrier()
         t0 = time.perf_counter()
         for _ in range(K):
-            lat, _ = engine.bench_closed_loop(xs, R)
+            lat, _ = eng.bench_closed_loop(xs, R)
             lat_all.append(lat)
-    t1 = time.perf_counter()
+        t1 = time.perf_counter()
+        relaunches = eng.info().launches - before  # relaunches inside the timed region (normally 0)
+        host_barrier()
+        eng.stop()
+        return t1 - t0, np.concatenate(lat_all), relaunches
+
+    e2e_launches = 0
+    e2e_local_s, lat_all, tb_s, lat_tb = float("nan"), np.array([float("nan")]), float("nan"), None
     if full:
-        e2e_launches = engine.info().launches - launches_before  # relaunches inside the timed region (normally 0)
-    host_barrier()
+        e2e_local_s, lat_all, n = closed_loop(engine)
+        e2e_launches += n
+        with ll.Engine(net, Ws, bs, device=dev, opts=opts(0)) as tb_engine:
+            tb_s, lat_tb, n = closed_loop(tb_engine)
+        e2e_launches += n
     clk = clocks.stop()
-    e2e_s = host_max(t1 - t0)
-    lat_all = np.concatenate(lat_all) if lat_all else np.array([float("nan")])
+    e2e_s = host_max(e2e_local_s)
     s_e2e = ll.compute_stats(lat_all)
     e2e_value = world * K * R / e2e_s
-    engine.stop()
+    s_tb = ll.compute_stats(lat_tb) if lat_tb is not None else None
+    tb_value = world * K * R / host_max(tb_s)
 
     # ---------------- comparison paths + CPU baseline (N=1, rank 0) ----------------
     compare = None
@@ -321,7 +340,7 @@ def main():
     peak, peak_kind = measured_peak_hbm()
     avg_launch_s = (sum(launch_ms) / len(launch_ms)) / 1000.0
     achieved = R * (WEIGHT_BYTES + IO_BYTES) / avg_launch_s / 1e9
-    per_rank = host_gather({"rank": rank, "value": K * R / (sum(launch_ms) / 1000.0), "e2e": K * R / (t1 - t0),
+    per_rank = host_gather({"rank": rank, "value": K * R / (sum(launch_ms) / 1000.0), "e2e": K * R / e2e_local_s,
                             "e2e_p50_us": s_e2e["p50"], "e2e_p99_us": s_e2e["p99"], "core": core})
     if rank != 0:
         if world > 1:
@@ -350,10 +369,18 @@ def main():
                          "shared memory) for the whole launch by design"},
         "e2e": {"value": e2e_value, "unit": "inferences/s", "h2d_bytes_per_step": R * 64 * 4,
                 "d2h_bytes_per_step": R * 16 * 4, "p50_us": s_e2e["p50"], "p99_us": s_e2e["p99"],
-                "p90_us": s_e2e["p90"], "timing": "host steady_clock per request, x write to y read"},
+                "p90_us": s_e2e["p90"], "mailbox": "tagged (mailbox_format 1)",
+                "timing": "host steady_clock per request, x write to y read"},
+        "e2e_tickbuffer": None if s_tb is None else {
+            "value": tb_value, "unit": "inferences/s", "p50_us": s_tb["p50"], "p99_us": s_tb["p99"],
+            "p90_us": s_tb["p90"], "mailbox": "the reference's TickBuffer layout (mailbox_format 0)"},
         "device_latency_us": {"p50": dev_stats["p50"], "p99": dev_stats["p99"], "mean": dev_stats["mean"]},
-        "latency_floor": {**floor, "e2e_p50_over_seq_floor": s_e2e["p50"] / floor_p50,
-                          "e2e_p50_over_io_floor": s_e2e["p50"] / floor["x_to_y"]["p50_us"]},
+        "latency_floor": {**floor,
+                          "e2e_p50_over_seq_floor": s_e2e["p50"] / floor_p50,
+                          "e2e_p50_over_tagged_io_floor": s_e2e["p50"] / floor["tagged_x_to_y"]["p50_us"],
+                          "e2e_p50_over_tagged_one_chunk_floor": s_e2e["p50"] / floor["tagged_one_chunk"]["p50_us"],
+                          "tickbuffer_p50_over_io_floor": (s_tb["p50"] if s_tb else float("nan"))
+                          / floor["x_to_y"]["p50_us"]},
         "comparison_paths": compare,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_kind": peak_kind,
@@ -369,6 +396,7 @@ def main():
         out["e2e"]["speedup_vs_cublas_graph_e2e_p50"] = compare["cublas_graph_e2e"]["p50_us"] / s_e2e["p50"]
     if not full:  # device-queue phase only: no mailbox numbers were taken
         out["e2e"] = None
+        out["e2e_tickbuffer"] = None
         out["latency_floor"] = None
     print(json.dumps(out), flush=True)
     if world > 1:
