@@ -266,6 +266,63 @@ int ll_dense_mbyv_packed(const float *W_cm, const float *b_pad, const float *x, 
 int ll_mlp_forward_noalloc(const ll_net_desc *net, const float *const *d_W, const float *const *d_b,
                            const float *d_x, float *d_y, void *stream);
 
+/*
+ * Batched dense path on the tensor cores (tcgen05 + TMEM), for the batched
+ * configurations: an MLP forward over up to max_batch rows as one tensor-core
+ * layer kernel per layer (128-row x bn tiles; the K splits of a tile run as one
+ * thread-block cluster and add their partials in rank order through distributed
+ * shared memory, so results are deterministic), chained with programmatic
+ * dependent launch.  No counterpart
+ * kernel in the reference, whose batched GEMMs are cuBLAS SGEMM calls
+ * (src/bench_cublas_mlp.cu, src/bench_cublas_mlp_graph.cu:119-187); the layer
+ * contract y = act(W x + b) and the row-major weight layout are the reference's.
+ * Weights: bf16 (uint16 bit patterns) or int8 with per-output-channel fp32
+ * scales (y = act(s * (q . x) + b)); every layer shares one type; in_dim and
+ * out_dim multiples of 64.  x is fp32 and rounded to bf16; hidden activations
+ * are bf16; y is fp32.
+ */
+#define LL_MAX_LAYERS 24
+typedef struct ll_batched_mlp ll_batched_mlp;
+typedef struct {
+    int32_t bn;          /* output channels per CTA tile: 0 = auto, 64, 128 or 256 */
+    int32_t splits;      /* K splits per tile (= cluster size): 0 = auto, else a power of two <= 16 dividing in_dim/64 */
+    int32_t pdl;         /* 1 = chain layers with programmatic dependent launch (default) */
+    int32_t reserved0;
+    uint64_t wait_ns;    /* bound on every device-side wait; 0 = 1 s */
+    int32_t reserved[4];
+} ll_batched_opts;
+typedef struct {
+    int32_t n_layers;
+    int32_t rows_pad;    /* max_batch rounded up to 128 */
+    int32_t bn[LL_MAX_LAYERS];
+    int32_t splits[LL_MAX_LAYERS];
+    int32_t ctas[LL_MAX_LAYERS];       /* at max_batch rows */
+    int32_t smem_bytes[LL_MAX_LAYERS];
+} ll_batched_info;
+void ll_batched_opts_default(ll_batched_opts *opts);
+/* Host-only tiling estimate (no GPU needed): the most CTAs up to one per SM.  ll_batched_mlp_create
+ * refines it with the device's cluster occupancy so that every layer runs in one wave;
+ * ll_batched_mlp_info reports the tiling actually used. */
+int ll_batched_plan(const ll_net_desc *net, const ll_batched_opts *opts, ll_batched_info *info);
+int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const float *const *b,
+                          const float *const *scales, int device, const ll_batched_opts *opts,
+                          ll_batched_mlp **out);
+/* Enqueue one forward on `stream` (device pointers; x [n_rows x in], y [n_rows x out], fp32).
+ * Returns launch errors only; ll_batched_mlp_check reports device-side ones. */
+int ll_batched_mlp_forward(ll_batched_mlp *m, const float *d_x, float *d_y, int n_rows, void *stream);
+/* Synchronise `stream` and read the device status word: LL_OK, or LL_ERR_DEVICE_FAULT when a
+ * bounded wait ran out (the workspace is then cleared so the next forward starts clean). */
+int ll_batched_mlp_check(ll_batched_mlp *m, void *stream);
+/* Host buffers: copy x in, forward, check, copy y out (on the object's own stream). */
+int ll_batched_mlp_infer(ll_batched_mlp *m, const float *x, float *y, int n_rows);
+int ll_batched_mlp_info(ll_batched_mlp *m, ll_batched_info *info);
+/* Optional phase trace (device buffer of n >= n_layers * max_ctas * 8 entries, or NULL to stop):
+ * every CTA of layer l writes 8 globaltimer stamps at d_trace[(l * max_ctas + cta) * 8 + k],
+ * max_ctas = the largest ctas[] of ll_batched_mlp_info; k = entry, previous layer done, first
+ * stage landed, last MMA issued, accumulator complete, cluster barrier 1, cluster barrier 2, end. */
+int ll_batched_mlp_set_trace(ll_batched_mlp *m, unsigned long long *d_trace, size_t n);
+int ll_batched_mlp_destroy(ll_batched_mlp *m);
+
 /* Host packing, include/ll/pack_weights.cuh:16-32. */
 void ll_pack_rm_to_kmajor_padded(const float *W_rm, size_t M, size_t K, float *W_cm, size_t Mpad);
 void ll_pack_bias_padded(const float *b, size_t M, float *b_pad, size_t Mpad);

@@ -53,7 +53,11 @@ EXPORTED_SYMBOLS = [
     "ll_quantize_int8_rows", "ll_compute_stats", "ll_mailbox_bytes", "ll_mailbox_post", "ll_mailbox_wait",
     "ll_next_seq", "ll_version", "ll_plan_net", "ll_engine_set_trace", "ll_mlp_forward_noalloc",
     "ll_tagged_mailbox_bytes", "ll_tagged_y_offset", "ll_tagged_post", "ll_tagged_wait",
+    "ll_batched_opts_default", "ll_batched_plan", "ll_batched_mlp_create", "ll_batched_mlp_forward",
+    "ll_batched_mlp_check", "ll_batched_mlp_infer", "ll_batched_mlp_info", "ll_batched_mlp_destroy",
+    "ll_batched_mlp_set_trace",
 ]
+MAX_LAYERS = 24
 
 
 class LLError(RuntimeError):
@@ -112,6 +116,16 @@ class Plan(ctypes.Structure):
                 ("stage_in_ld", ctypes.c_int32 * 9), ("image_bytes", ctypes.c_uint32 * 9),
                 ("buf_off", ctypes.c_uint32 * 6), ("smem_bytes", ctypes.c_uint32), ("image_stride", ctypes.c_uint32),
                 ("layers", PlanLayer * 24)]
+
+
+class BatchedOpts(ctypes.Structure):
+    _fields_ = [("bn", ctypes.c_int32), ("splits", ctypes.c_int32), ("pdl", ctypes.c_int32),
+                ("reserved0", ctypes.c_int32), ("wait_ns", ctypes.c_uint64), ("reserved", ctypes.c_int32 * 4)]
+
+
+class BatchedInfo(ctypes.Structure):
+    _fields_ = [("n_layers", ctypes.c_int32), ("rows_pad", ctypes.c_int32), ("bn", ctypes.c_int32 * 24),
+                ("splits", ctypes.c_int32 * 24), ("ctas", ctypes.c_int32 * 24), ("smem_bytes", ctypes.c_int32 * 24)]
 
 
 LAYER_MODE_NAMES = {0: "replicated", 1: "rowsplit_allgather", 2: "rowsplit_local", 3: "ksplit_gather",
@@ -175,6 +189,16 @@ def _sig(lib):
         "ll_version": (ctypes.c_char_p, []),
         "ll_plan_net": (ctypes.c_int, [P(NetDesc), P(_vp), P(_fp), P(_fp), P(EngineOpts), P(Plan), _vp,
                                        ctypes.c_size_t, P(ctypes.c_size_t)]),
+        "ll_batched_opts_default": (None, [P(BatchedOpts)]),
+        "ll_batched_plan": (ctypes.c_int, [P(NetDesc), P(BatchedOpts), P(BatchedInfo)]),
+        "ll_batched_mlp_create": (ctypes.c_int, [P(NetDesc), P(_vp), P(_fp), P(_fp), ctypes.c_int, P(BatchedOpts),
+                                                 P(_vp)]),
+        "ll_batched_mlp_forward": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, _vp]),
+        "ll_batched_mlp_check": (ctypes.c_int, [_vp, _vp]),
+        "ll_batched_mlp_infer": (ctypes.c_int, [_vp, _fp, _fp, ctypes.c_int]),
+        "ll_batched_mlp_info": (ctypes.c_int, [_vp, P(BatchedInfo)]),
+        "ll_batched_mlp_destroy": (ctypes.c_int, [_vp]),
+        "ll_batched_mlp_set_trace": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t]),
     }
     for name, (res, args) in s.items():
         f = getattr(lib, name)
@@ -574,3 +598,83 @@ def mlp_forward_noalloc(net: Net, d_W_ptrs, d_b_ptrs, d_x_ptr: int, d_y_ptr: int
     Wp = (_vp * net.n_layers)(*d_W_ptrs)
     bp = (_vp * net.n_layers)(*d_b_ptrs) if d_b_ptrs is not None else None
     _check(lib().ll_mlp_forward_noalloc(ctypes.byref(d), Wp, bp, d_x_ptr, d_y_ptr, stream or None))
+
+
+# ---- batched dense path (tensor cores) ----
+def batched_opts(bn: int = 0, splits: int = 0, pdl: int = 1, wait_ns: int = 0) -> BatchedOpts:
+    o = BatchedOpts()
+    lib().ll_batched_opts_default(ctypes.byref(o))
+    o.bn, o.splits, o.pdl, o.wait_ns = bn, splits, pdl, wait_ns
+    return o
+
+
+def _batched_info_dict(info: BatchedInfo) -> dict:
+    n = info.n_layers
+    return {"rows_pad": info.rows_pad, "bn": list(info.bn[:n]), "splits": list(info.splits[:n]),
+            "ctas": list(info.ctas[:n]), "smem_bytes": list(info.smem_bytes[:n])}
+
+
+def batched_plan(net: Net, opts: Optional[BatchedOpts] = None) -> dict:
+    """Tiling the batched path would use for `net` at max_batch rows (host only)."""
+    d = net.desc()
+    info = BatchedInfo()
+    _check(lib().ll_batched_plan(ctypes.byref(d), ctypes.byref(opts) if opts is not None else None,
+                                 ctypes.byref(info)))
+    return _batched_info_dict(info)
+
+
+class BatchedMLP:
+    """tcgen05 tensor-core MLP over many rows (bf16 or int8 + per-channel scales weights)."""
+
+    def __init__(self, net: Net, W, b, scales=None, device: int = 0, opts: Optional[BatchedOpts] = None):
+        self.net = net
+        self.in_dim, self.out_dim = net.dims[0], net.dims[-1]
+        self.h = ctypes.c_void_p()
+        self._keep = [np.ascontiguousarray(w) for w in W]
+        self._keepb = [np.ascontiguousarray(x, np.float32) for x in b] if b is not None else None
+        self._keeps = [np.ascontiguousarray(x, np.float32) for x in scales] if scales is not None else None
+        Wp = (_vp * net.n_layers)(*[w.ctypes.data for w in self._keep])
+        bp = (_fp * net.n_layers)(*[_f(x) for x in self._keepb]) if self._keepb is not None else None
+        sp = (_fp * net.n_layers)(*[_f(x) for x in self._keeps]) if self._keeps is not None else None
+        d = net.desc()
+        _check(lib().ll_batched_mlp_create(ctypes.byref(d), Wp, bp, sp, device,
+                                           ctypes.byref(opts) if opts is not None else None, ctypes.byref(self.h)))
+        self._keep = self._keepb = self._keeps = None  # copied to the device
+
+    def forward(self, d_x_ptr: int, d_y_ptr: int, n_rows: int, stream: int = 0):
+        _check(lib().ll_batched_mlp_forward(self.h, d_x_ptr, d_y_ptr, n_rows, stream or None))
+
+    def check(self, stream: int = 0):
+        _check(lib().ll_batched_mlp_check(self.h, stream or None))
+
+    def infer(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, self.in_dim)
+        y = np.empty((x.shape[0], self.out_dim), np.float32)
+        _check(lib().ll_batched_mlp_infer(self.h, _f(x), _f(y), x.shape[0]))
+        return y
+
+    def info(self) -> dict:
+        info = BatchedInfo()
+        _check(lib().ll_batched_mlp_info(self.h, ctypes.byref(info)))
+        return _batched_info_dict(info)
+
+    def set_trace(self, d_trace_ptr: int, n: int):
+        """Per-CTA phase stamps (see ll_batched_mlp_set_trace); d_trace_ptr = 0 turns tracing off."""
+        _check(lib().ll_batched_mlp_set_trace(self.h, d_trace_ptr or None, n))
+
+    def close(self):
+        if self.h:
+            lib().ll_batched_mlp_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

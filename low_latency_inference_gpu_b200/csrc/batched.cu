@@ -1,0 +1,604 @@
+// Batched dense path: an MLP forward over many rows as one tcgen05 layer kernel
+// per layer (tc_layer.cuh), chained with programmatic dependent launch so each
+// layer's set-up overlaps the previous layer's tail.  Weights stay resident in
+// HBM in their own type (int8 + per-channel scales, or bf16); activations move
+// between layers as bf16 row-major buffers padded to 128 rows.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.h"
+#include "tc_layer.cuh"
+
+using namespace llk;
+
+namespace {
+
+constexpr int kMaxSplitCTAs = 148;  // one CTA per SM
+
+struct LayerRun {
+    int bn = 256, splits = 1, ctas = 0, smem = 0;
+    int K = 0, N = 0, act = 0, out_f32 = 0;
+    const void *kfn = nullptr;
+    TcLayerParams p{};
+};
+
+template <int BN, bool I8>
+constexpr int stages_for()
+{
+    return (I8 && BN == 256) ? 3 : 4;
+}
+
+template <int BN, bool I8>
+const void *kernel_for(int &smem)
+{
+    constexpr int ST = stages_for<BN, I8>();
+    smem = TcSmem<BN, I8, ST>::ALLOC;
+    return reinterpret_cast<const void *>(&ll_tc_layer_kernel<BN, I8, ST>);
+}
+
+const void *pick_kernel(int bn, bool i8, int &smem)
+{
+    if (i8)
+        return bn == 256 ? kernel_for<256, true>(smem) : bn == 128 ? kernel_for<128, true>(smem)
+                                                                  : kernel_for<64, true>(smem);
+    return bn == 256 ? kernel_for<256, false>(smem) : bn == 128 ? kernel_for<128, false>(smem)
+                                                               : kernel_for<64, false>(smem);
+}
+
+// Largest power of two <= cap (and <= 16, the largest cluster) that divides n.
+// The 256-wide tile has no shared memory left for the split-K exchange.
+bool can_split(int bn, bool i8)
+{
+    if (bn == 256)
+        return i8 ? TcSmem<256, true, stages_for<256, true>()>::CAN_SPLIT
+                  : TcSmem<256, false, stages_for<256, false>()>::CAN_SPLIT;
+    if (bn == 128)
+        return i8 ? TcSmem<128, true, 4>::CAN_SPLIT : TcSmem<128, false, 4>::CAN_SPLIT;
+    return i8 ? TcSmem<64, true, 4>::CAN_SPLIT : TcSmem<64, false, 4>::CAN_SPLIT;
+}
+
+int split_at_most(int n, int cap)
+{
+    for (int d = 16; d >= 1; d >>= 1)
+        if (d <= cap && n % d == 0)
+            return d;
+    return 1;
+}
+
+// Tile width and split count of one layer: the most CTAs up to one per SM, each
+// with at least two 64-deep K steps; ties go to the wider tile (fewer X re-reads).
+// The splits of a tile run as one cluster, so a split count is a power of two <= 16.
+void plan_layer(int K, int N, int rows_pad, bool i8, const ll_batched_opts *o, int &bn, int &splits)
+{
+    const int mt = rows_pad / kTcRows;
+    int best_bn = 0, best_s = 1, best_ctas = -1;
+    for (int cand : {256, 128, 64}) {
+        if (N % cand != 0 || (o && o->bn && o->bn != cand))
+            continue;
+        const int tiles = (N / cand) * mt;
+        int s;
+        if (o && o->splits > 0)
+            s = o->splits;
+        else
+            s = can_split(cand, i8)
+                    ? split_at_most(K / kTcK, std::min(std::max(1, kMaxSplitCTAs / tiles), std::max(1, K / 128)))
+                    : 1;
+        const int ctas = tiles * s;
+        if (ctas > best_ctas) {
+            best_ctas = ctas;
+            best_bn = cand;
+            best_s = s;
+        }
+    }
+    bn = best_bn;
+    splits = best_s;
+}
+
+int validate(const ll_net_desc *net, const ll_batched_opts *o)
+{
+    if (!net || net->n_layers < 1 || net->n_layers > LL_MAX_LAYERS || !net->layers) {
+        llh::set_error("batched net: n_layers must be in [1, %d]", LL_MAX_LAYERS);
+        return LL_ERR_BAD_DESC;
+    }
+    if (net->max_batch < 1 || net->max_batch > 65536) {
+        llh::set_error("batched net: max_batch must be in [1, 65536]");
+        return LL_ERR_BAD_DESC;
+    }
+    const int wt = net->layers[0].wtype;
+    if (wt != LL_W_BF16 && wt != LL_W_I8) {
+        llh::set_error("batched net: weights must be bf16 or int8 (the tensor-core path)");
+        return LL_ERR_BAD_DESC;
+    }
+    for (int l = 0; l < net->n_layers; ++l) {
+        const ll_layer_desc &d = net->layers[l];
+        if (d.wtype != wt) {
+            llh::set_error("layer %d: all layers must share one weight type", l);
+            return LL_ERR_BAD_DESC;
+        }
+        if (d.in_dim < kTcK || d.in_dim % kTcK != 0 || d.in_dim > 65536) {
+            llh::set_error("layer %d: in_dim %d must be a positive multiple of 64", l, d.in_dim);
+            return LL_ERR_BAD_DESC;
+        }
+        if (d.out_dim < 64 || d.out_dim % 64 != 0 || d.out_dim > 65536) {
+            llh::set_error("layer %d: out_dim %d must be a positive multiple of 64", l, d.out_dim);
+            return LL_ERR_BAD_DESC;
+        }
+        if (l > 0 && net->layers[l - 1].out_dim != d.in_dim) {
+            llh::set_error("layer %d: in_dim %d != previous out_dim %d", l, d.in_dim, net->layers[l - 1].out_dim);
+            return LL_ERR_BAD_DESC;
+        }
+        if (d.act < LL_ACT_IDENTITY || d.act > LL_ACT_GELU) {
+            llh::set_error("layer %d: unknown activation %d", l, d.act);
+            return LL_ERR_BAD_DESC;
+        }
+    }
+    if (o && ((o->bn != 0 && o->bn != 64 && o->bn != 128 && o->bn != 256) || o->splits < 0 || o->splits > 16 ||
+              (o->splits & (o->splits - 1)) != 0)) {
+        llh::set_error("batched opts: bn must be 0/64/128/256 and splits 0 (auto) or a power of two <= 16");
+        return LL_ERR_INVALID_ARG;
+    }
+    if (o && o->splits > 0) {
+        for (int l = 0; l < net->n_layers; ++l)
+            if ((net->layers[l].in_dim / kTcK) % o->splits != 0) {
+                llh::set_error("layer %d: splits %d must divide in_dim/64", l, o->splits);
+                return LL_ERR_INVALID_ARG;
+            }
+    }
+    if (o && o->bn && o->splits > 1 && !can_split(o->bn, wt == LL_W_I8)) {
+        llh::set_error("batched opts: a %d-wide tile cannot be split (no shared memory for the exchange)", o->bn);
+        return LL_ERR_INVALID_ARG;
+    }
+    if (o && o->bn) {
+        for (int l = 0; l < net->n_layers; ++l)
+            if (net->layers[l].out_dim % o->bn != 0) {
+                llh::set_error("layer %d: out_dim %d is not a multiple of bn %d", l, net->layers[l].out_dim, o->bn);
+                return LL_ERR_INVALID_ARG;
+            }
+    }
+    return LL_OK;
+}
+
+void fill_info(const ll_net_desc *net, const ll_batched_opts *o, ll_batched_info *info)
+{
+    std::memset(info, 0, sizeof(*info));
+    const int rows_pad = (int)llh::round_up((size_t)net->max_batch, kTcRows);
+    info->n_layers = net->n_layers;
+    info->rows_pad = rows_pad;
+    const bool i8 = net->layers[0].wtype == LL_W_I8;
+    for (int l = 0; l < net->n_layers; ++l) {
+        int bn, s, smem;
+        plan_layer(net->layers[l].in_dim, net->layers[l].out_dim, rows_pad, i8, o, bn, s);
+        pick_kernel(bn, i8, smem);
+        info->bn[l] = bn;
+        info->splits[l] = s;
+        info->ctas[l] = (net->layers[l].out_dim / bn) * (rows_pad / kTcRows) * s;
+        info->smem_bytes[l] = smem;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D row-major tensor map: inner dim `cols` elements, `rows` rows, box {64, box_rows}.
+bool make_map(CUtensorMap *m, CUtensorMapDataType t, int esize, const void *base, int cols, int rows, int box_rows,
+              bool swizzle)
+{
+    auto fn = encode_fn();
+    if (!fn)
+        return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * (cuuint64_t)esize};
+    cuuint32_t box[2] = {(cuuint32_t)kTcK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, t, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// fp32 rows -> bf16 (round to nearest even) into the padded layer-0 buffer.
+__global__ void to_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ out, size_t n)
+{
+    griddep_wait();
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __float2bfloat16_rn(x[i]);
+    griddep_launch_dependents();
+}
+
+int max_active_clusters(const void *kfn, int smem, int S)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, (unsigned)S);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cudaLaunchAttribute ca[1];
+    ca[0].id = cudaLaunchAttributeClusterDimension;
+    ca[0].val.clusterDim.x = 1;
+    ca[0].val.clusterDim.y = 1;
+    ca[0].val.clusterDim.z = (unsigned)S;
+    cfg.attrs = ca;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+// On the device: the (bn, splits) with the most CTAs such that every cluster of
+// the layer is resident at once (one wave; the occupancy query knows how many
+// clusters of S CTAs the GPCs can hold), each split at least two 64-deep K steps.
+// Ties go to the wider tile.  Forced options are taken as given.
+bool choose_tiling(int K, int N, int rows_pad, bool i8, const ll_batched_opts *o, LayerRun &r)
+{
+    const int mt = rows_pad / kTcRows;
+    int best = -1;
+    for (int bn : {256, 128, 64}) {
+        if (N % bn != 0 || (o && o->bn && o->bn != bn))
+            continue;
+        int smem = 0;
+        const void *kfn = pick_kernel(bn, i8, smem);
+        if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+            cudaFuncSetAttribute(kfn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+            return false;
+        const int tiles = (N / bn) * mt;
+        for (int S = 16; S >= 1; S >>= 1) {
+            if (o && o->splits && o->splits != S)
+                continue;
+            if ((K / kTcK) % S != 0 || (!(o && o->splits) && S > 1 && K / S < 128) || (S > 1 && !can_split(bn, i8)))
+                continue;
+            const int fit = max_active_clusters(kfn, smem, S);
+            if (fit < 1)
+                continue;
+            if (!(o && (o->splits || o->bn)) && tiles > fit)
+                continue;  // would need a second wave
+            const int ctas = tiles * S;
+            if (ctas > best) {
+                best = ctas;
+                r.bn = bn;
+                r.splits = S;
+                r.ctas = ctas;
+                r.smem = smem;
+                r.kfn = kfn;
+            }
+        }
+    }
+    if (best < 0 && !(o && (o->splits || o->bn))) {  // nothing fits one wave: smallest legal grid
+        int smem = 0;
+        const int bn = N % 256 == 0 ? 256 : N % 128 == 0 ? 128 : 64;
+        r.kfn = pick_kernel(bn, i8, smem);
+        r.bn = bn;
+        r.splits = 1;
+        r.ctas = (N / bn) * mt;
+        r.smem = smem;
+        best = r.ctas;
+    }
+    return best > 0;
+}
+
+}  // namespace
+
+struct ll_batched_mlp {
+    int device = 0;
+    int n_layers = 0, in_dim = 0, out_dim = 0, max_rows = 0, rows_pad = 0, wtype = 0;
+    std::vector<void *> d_w;
+    std::vector<float *> d_b, d_s;
+    __nv_bfloat16 *act[2] = {nullptr, nullptr};
+    float *out_pad = nullptr;  // fp32 [rows_pad x out] for the last layer
+    unsigned *status = nullptr;
+    std::vector<LayerRun> runs;
+    int max_ctas = 0;
+    cudaStream_t own = nullptr;  // non-blocking stream for ll_batched_mlp_infer
+    int pdl = 1;
+    unsigned long long wait_ns = 1000ull * 1000 * 1000;
+};
+
+namespace {
+
+void destroy_all(ll_batched_mlp *m)
+{
+    if (!m)
+        return;
+    cudaSetDevice(m->device);
+    for (void *p : m->d_w)
+        cudaFree(p);
+    for (float *p : m->d_b)
+        cudaFree(p);
+    for (float *p : m->d_s)
+        cudaFree(p);
+    cudaFree(m->act[0]);
+    cudaFree(m->act[1]);
+    cudaFree(m->out_pad);
+    cudaFree(m->status);
+    if (m->own)
+        cudaStreamDestroy(m->own);
+    delete m;
+}
+
+}  // namespace
+
+extern "C" {
+
+void ll_batched_opts_default(ll_batched_opts *o)
+{
+    if (!o)
+        return;
+    std::memset(o, 0, sizeof(*o));
+    o->pdl = 1;
+}
+
+int ll_batched_plan(const ll_net_desc *net, const ll_batched_opts *opts, ll_batched_info *info)
+{
+    if (!info)
+        return LL_ERR_INVALID_ARG;
+    int rc = validate(net, opts);
+    if (rc)
+        return rc;
+    fill_info(net, opts, info);
+    return LL_OK;
+}
+
+int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const float *const *b,
+                          const float *const *scales, int device, const ll_batched_opts *opts, ll_batched_mlp **out)
+{
+    if (!out || !W)
+        return LL_ERR_INVALID_ARG;
+    *out = nullptr;
+    int rc = validate(net, opts);
+    if (rc)
+        return rc;
+    const bool i8 = net->layers[0].wtype == LL_W_I8;
+    for (int l = 0; l < net->n_layers; ++l) {
+        if (!W[l] || (i8 && (!scales || !scales[l]))) {
+            llh::set_error("layer %d: weights%s missing", l, i8 ? " or scales" : "");
+            return LL_ERR_INVALID_ARG;
+        }
+    }
+    if (!encode_fn()) {
+        llh::set_error("cuTensorMapEncodeTiled is not available from the driver");
+        return LL_ERR_CUDA;
+    }
+    ll_batched_info info;
+    fill_info(net, opts, &info);
+
+    auto *m = new ll_batched_mlp();
+    m->device = device;
+    m->n_layers = net->n_layers;
+    m->in_dim = net->layers[0].in_dim;
+    m->out_dim = net->layers[net->n_layers - 1].out_dim;
+    m->max_rows = net->max_batch;
+    m->rows_pad = info.rows_pad;
+    m->wtype = net->layers[0].wtype;
+    m->pdl = opts ? opts->pdl : 1;
+    if (opts && opts->wait_ns)
+        m->wait_ns = opts->wait_ns;
+    auto fail = [&](int code) {
+        destroy_all(m);
+        return code;
+    };
+#define LLB_TRY(call)                                                                                        \
+    do {                                                                                                     \
+        cudaError_t _e = (call);                                                                             \
+        if (_e != cudaSuccess) {                                                                             \
+            llh::set_error("%s failed: %s", #call, cudaGetErrorString(_e));                                   \
+            return fail(LL_ERR_CUDA);                                                                        \
+        }                                                                                                    \
+    } while (0)
+    LLB_TRY(cudaSetDevice(device));
+    LLB_TRY(cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking));
+    int max_w = m->in_dim;
+    for (int l = 0; l < net->n_layers; ++l) {
+        const ll_layer_desc &d = net->layers[l];
+        max_w = std::max(max_w, d.out_dim);
+        const size_t welems = (size_t)d.in_dim * (size_t)d.out_dim;
+        void *dw = nullptr;
+        LLB_TRY(cudaMalloc(&dw, welems * (i8 ? 1 : 2)));
+        m->d_w.push_back(dw);
+        LLB_TRY(cudaMemcpy(dw, W[l], welems * (i8 ? 1 : 2), cudaMemcpyHostToDevice));
+        float *db = nullptr;
+        LLB_TRY(cudaMalloc(&db, sizeof(float) * d.out_dim));
+        m->d_b.push_back(db);
+        if (b && b[l])
+            LLB_TRY(cudaMemcpy(db, b[l], sizeof(float) * d.out_dim, cudaMemcpyHostToDevice));
+        else
+            LLB_TRY(cudaMemset(db, 0, sizeof(float) * d.out_dim));
+        float *ds = nullptr;
+        if (i8) {
+            LLB_TRY(cudaMalloc(&ds, sizeof(float) * d.out_dim));
+            LLB_TRY(cudaMemcpy(ds, scales[l], sizeof(float) * d.out_dim, cudaMemcpyHostToDevice));
+        }
+        m->d_s.push_back(ds);
+    }
+    const size_t act_elems = (size_t)m->rows_pad * (size_t)max_w;
+    for (int i = 0; i < 2; ++i) {
+        LLB_TRY(cudaMalloc(&m->act[i], act_elems * 2));
+        LLB_TRY(cudaMemset(m->act[i], 0, act_elems * 2));  // padded rows stay zero
+    }
+    LLB_TRY(cudaMalloc(&m->out_pad, sizeof(float) * (size_t)m->rows_pad * m->out_dim));
+    LLB_TRY(cudaMalloc(&m->status, sizeof(unsigned)));
+    LLB_TRY(cudaMemset(m->status, 0, sizeof(unsigned)));
+
+    for (int l = 0; l < net->n_layers; ++l) {
+        const ll_layer_desc &d = net->layers[l];
+        LayerRun r;
+        r.bn = info.bn[l];
+        r.splits = info.splits[l];
+        r.ctas = info.ctas[l];
+        r.K = d.in_dim;
+        r.N = d.out_dim;
+        r.act = d.act;
+        r.out_f32 = (l + 1 == net->n_layers);
+        if (!choose_tiling(d.in_dim, d.out_dim, m->rows_pad, i8, opts, r)) {
+            llh::set_error("layer %d: no tile / cluster shape can be scheduled on this device", l);
+            return fail(LL_ERR_BAD_DESC);
+        }
+        TcLayerParams &p = r.p;
+        if (!make_map(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->act[l & 1], d.in_dim, m->rows_pad, kTcRows,
+                      true) ||
+            !make_map(&p.tm_w, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, i8 ? 1 : 2,
+                      m->d_w[l], d.in_dim, d.out_dim, r.bn, !i8)) {
+            llh::set_error("layer %d: tensor map encoding failed", l);
+            return fail(LL_ERR_CUDA);
+        }
+        p.bias = m->d_b[l];
+        p.scale = m->d_s[l];
+        p.out = r.out_f32 ? static_cast<void *>(m->out_pad) : static_cast<void *>(m->act[(l + 1) & 1]);
+        p.status = m->status;
+        p.K = d.in_dim;
+        p.N = d.out_dim;
+        p.k_chunk = d.in_dim / r.splits;
+        p.splits = r.splits;
+        p.act = d.act;
+        p.out_f32 = r.out_f32;
+        p.wait_ns = m->wait_ns;
+        p.trace = nullptr;
+        m->max_ctas = std::max(m->max_ctas, r.ctas);
+        m->runs.push_back(r);
+    }
+#undef LLB_TRY
+    *out = m;
+    return LL_OK;
+}
+
+int ll_batched_mlp_forward(ll_batched_mlp *m, const float *d_x, float *d_y, int n_rows, void *stream)
+{
+    if (!m || !d_x || !d_y || n_rows < 1 || n_rows > m->max_rows) {
+        llh::set_error("batched forward: bad arguments (n_rows must be in [1, max_batch])");
+        return LL_ERR_INVALID_ARG;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    LL_CUDA_TRY(cudaSetDevice(m->device));
+    const size_t n = (size_t)n_rows * m->in_dim;
+    to_bf16_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 1184), 256, 0, st>>>(d_x, m->act[0], n);
+    LL_CUDA_TRY(cudaGetLastError());
+    const int mt = (n_rows + kTcRows - 1) / kTcRows;
+    for (LayerRun &r : m->runs) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(r.N / r.bn), (unsigned)mt, (unsigned)r.splits);
+        cfg.blockDim = dim3(kTcThreads, 1, 1);
+        cfg.dynamicSmemBytes = (size_t)r.smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = m->pdl ? 1 : 0;
+        attr[1].id = cudaLaunchAttributeClusterDimension;  // the K splits of a tile form one cluster
+        attr[1].val.clusterDim.x = 1;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = (unsigned)r.splits;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        void *args[] = {&r.p};
+        LL_CUDA_TRY(cudaLaunchKernelExC(&cfg, r.kfn, args));
+    }
+    // the last layer wrote [rows_pad x out] fp32; hand the caller its n_rows
+    LL_CUDA_TRY(cudaMemcpyAsync(d_y, m->out_pad, sizeof(float) * (size_t)n_rows * m->out_dim,
+                                cudaMemcpyDeviceToDevice, st));
+    return LL_OK;
+}
+
+int ll_batched_mlp_check(ll_batched_mlp *m, void *stream)
+{
+    if (!m)
+        return LL_ERR_INVALID_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    LL_CUDA_TRY(cudaSetDevice(m->device));
+    // stream-ordered only: a resident engine on the same GPU never finishes, so no device-wide sync
+    unsigned s = 0;
+    LL_CUDA_TRY(cudaMemcpyAsync(&s, m->status, sizeof(s), cudaMemcpyDeviceToHost, st));
+    LL_CUDA_TRY(cudaStreamSynchronize(st));
+    if (s) {
+        cudaMemsetAsync(m->status, 0, sizeof(unsigned), st);
+        cudaStreamSynchronize(st);
+        llh::set_error("batched forward: a device wait ran out (status 0x%x, role %u)", s, (s >> 8) & 0xffu);
+        return LL_ERR_DEVICE_FAULT;
+    }
+    return LL_OK;
+}
+
+int ll_batched_mlp_infer(ll_batched_mlp *m, const float *x, float *y, int n_rows)
+{
+    if (!m || !x || !y || n_rows < 1 || n_rows > m->max_rows) {
+        llh::set_error("batched infer: bad arguments");
+        return LL_ERR_INVALID_ARG;
+    }
+    LL_CUDA_TRY(cudaSetDevice(m->device));
+    float *dx = nullptr, *dy = nullptr;
+    LL_CUDA_TRY(cudaMalloc(&dx, sizeof(float) * (size_t)n_rows * m->in_dim));
+    if (cudaMalloc(&dy, sizeof(float) * (size_t)n_rows * m->out_dim) != cudaSuccess) {
+        cudaFree(dx);
+        llh::set_error("batched infer: cudaMalloc failed");
+        return LL_ERR_CUDA;
+    }
+    int rc = LL_OK;
+    if (cudaMemcpyAsync(dx, x, sizeof(float) * (size_t)n_rows * m->in_dim, cudaMemcpyHostToDevice, m->own) !=
+        cudaSuccess)
+        rc = LL_ERR_CUDA;
+    if (rc == LL_OK)
+        rc = ll_batched_mlp_forward(m, dx, dy, n_rows, m->own);
+    if (rc == LL_OK)
+        rc = ll_batched_mlp_check(m, m->own);
+    if (rc == LL_OK && (cudaMemcpyAsync(y, dy, sizeof(float) * (size_t)n_rows * m->out_dim, cudaMemcpyDeviceToHost,
+                                        m->own) != cudaSuccess ||
+                        cudaStreamSynchronize(m->own) != cudaSuccess))
+        rc = LL_ERR_CUDA;
+    cudaFree(dx);
+    cudaFree(dy);
+    return rc;
+}
+
+int ll_batched_mlp_set_trace(ll_batched_mlp *m, unsigned long long *d_trace, size_t n)
+{
+    if (!m)
+        return LL_ERR_INVALID_ARG;
+    const size_t per_layer = (size_t)m->max_ctas * 8;
+    if (d_trace && n < per_layer * m->runs.size()) {
+        llh::set_error("trace buffer needs %zu entries", per_layer * m->runs.size());
+        return LL_ERR_INVALID_ARG;
+    }
+    for (size_t l = 0; l < m->runs.size(); ++l)
+        m->runs[l].p.trace = d_trace ? d_trace + l * per_layer : nullptr;
+    return LL_OK;
+}
+
+int ll_batched_mlp_info(ll_batched_mlp *m, ll_batched_info *info)
+{
+    if (!m || !info)
+        return LL_ERR_INVALID_ARG;
+    std::memset(info, 0, sizeof(*info));
+    info->n_layers = m->n_layers;
+    info->rows_pad = m->rows_pad;
+    for (int l = 0; l < m->n_layers; ++l) {
+        info->bn[l] = m->runs[l].bn;
+        info->splits[l] = m->runs[l].splits;
+        info->ctas[l] = m->runs[l].ctas;
+        info->smem_bytes[l] = m->runs[l].smem;
+    }
+    return LL_OK;
+}
+
+int ll_batched_mlp_destroy(ll_batched_mlp *m)
+{
+    if (!m)
+        return LL_ERR_INVALID_ARG;
+    destroy_all(m);
+    return LL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,628 @@
+// Batched dense layer on the 5th-generation tensor cores (tcgen05 + TMEM), one
+// launch per layer:
+//
+//   Y[rows x N] = act( (X[rows x K] . Wd[N x K]^T) * scale[N] + bias[N] )
+//
+// X is bf16 (row-major), W is bf16 or int8 (row-major, per-output-channel fp32
+// scale applied after accumulation; int8 -> bf16 is exact), accumulation fp32 in
+// TMEM, Y bf16 (hidden layers) or fp32 (last layer).
+//
+// CTA tile: 128 rows x BN output channels, K walked in 64-element steps through a
+// STAGES-deep shared-memory ring; the grid's z dimension splits K, and the S
+// splits of a tile form one thread-block cluster that adds its partials through
+// distributed shared memory: each CTA stages its partial tile and bulk-copies each
+// owner its rows (each CTA finishes 128/S rows of the tile).
+// Roles (one CTA per SM):
+//   warp 0        TMA producer: X tile [128 x 64] bf16 and W tile [BN x 64]
+//                 (bf16 straight into the 128-byte-swizzled operand layout; int8
+//                 into a staging buffer);
+//   warp 1        TMEM allocation + the single thread that issues tcgen05.mma
+//                 (M=128, N=BN, K=16, bf16 x bf16 -> fp32) and tcgen05.commit;
+//   warps 4..11   int8 only: convert the staged int8 tile into the swizzled bf16
+//                 operand (exact), fence the async proxy, arrive;
+//   warps 4..7    epilogue: tcgen05.ld of their 32 TMEM lanes (= tile rows), then
+//                 the rows go out (no split) or to their owner CTA (split-K);
+//   all threads   split-K: sum of the cluster's S partial slots for this CTA's rows.
+// Every wait is bounded (globaltimer); a wait that runs out records the error
+// and the CTA drains and frees its TMEM before returning.
+//
+// Reference: the batched configurations have no counterpart kernel in the
+// reference (its batched GEMMs are cuBLAS SGEMM calls, src/bench_cublas_mlp.cu);
+// the arithmetic follows its layer contract y = act(W x + b).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "ptx.cuh"
+
+namespace llk {
+
+constexpr int kTcRows = 128;      // tile rows (MMA M)
+constexpr int kTcK = 64;          // K per pipeline stage (128 bytes of bf16: one swizzle row)
+constexpr int kTcThreads = 384;   // 12 warps
+constexpr int kTcEpiWarp0 = 4;    // epilogue warps 4..7
+constexpr int kTcConvWarp0 = 4;   // converter warps 4..11
+constexpr int kTcConvThreads = 256;
+
+struct TcLayerParams {
+    CUtensorMap tm_x;   // bf16 [rows_pad][K], box {64, 128}, 128-byte swizzle
+    CUtensorMap tm_w;   // bf16 [N][K] box {64, BN} swizzled, or int8 [N][K] box {64, BN} unswizzled
+    const float *bias;  // [N]
+    const float *scale; // [N] or nullptr
+    void *out;          // bf16 or fp32 [rows_pad][N]
+    unsigned *status;   // device error word: bit 0 wait ran out; the failing role in bits 8..15
+    int K, N;
+    int k_chunk;        // K per split (multiple of 64)
+    int splits;         // = cluster size along z: 1, 2, 4, 8 or 16
+    int act;            // LL_ACT_*
+    int out_f32;
+    unsigned long long wait_ns;
+    unsigned long long *trace;  // optional: 8 globaltimer stamps per CTA (see kTcTrace*), or null
+};
+
+// Trace stamps per CTA (CTA id = x + gridDim.x * (y + gridDim.y * z)).
+enum {
+    kTcTraceEntry = 0,     // kernel entry
+    kTcTraceDepDone = 1,   // previous layer complete (griddepcontrol.wait returned)
+    kTcTraceFirstData = 2, // MMA thread: first stage landed (and converted)
+    kTcTraceMmaIssued = 3, // MMA thread: last MMA issued
+    kTcTraceAccum = 4,     // epilogue: accumulator complete
+    kTcTraceClusterA = 5,  // after the first cluster barrier
+    kTcTraceClusterB = 6,  // after the partial rows were exchanged
+    kTcTraceEnd = 7        // rows written
+};
+
+// ---- PTX wrappers used only by this kernel ----
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm, int x, int y, uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *tm)
+{
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
+}
+
+// Add expected transaction bytes to the current phase without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Bulk copy of this CTA's shared memory into a peer's (cluster address), completing
+// the byte count on the peer's mbarrier (cluster address).
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                               uint32_t bar_cluster)
+{
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst_cluster),
+                 "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group()
+{
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until every committed bulk copy of this thread has finished reading its source.
+__device__ __forceinline__ void bulk_wait_group_read0()
+{
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_local(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before()
+{
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after()
+{
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_wait()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand in the 128-byte swizzle layout
+// (rows of 128 bytes, 8-row atoms of 1024 bytes; leading offset unused = 1,
+// stride offset = 1024 bytes between 8-row groups; version 1; layout 2 = 128B swizzle).
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr)
+{
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: A = B = bf16, D = fp32, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t tc_idesc_bf16(int n)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTcRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns: thread i of the warp gets lane (base lane + i).
+__device__ __forceinline__ void tc_ld_32cols(uint32_t taddr, float (&v)[32])
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float tc_act(float v, int act)
+{
+    if (act == 1)  // LL_ACT_RELU
+        return fmaxf(v, 0.0f);
+    if (act == 2)  // LL_ACT_GELU: 0.5 x (1 + erf(x / sqrt 2))
+        return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    return v;
+}
+
+// Bounded mbarrier wait; false when the bound ran out (or another role already failed).
+__device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity, unsigned long long bound_ns,
+                                        volatile uint32_t *fail, unsigned *status, uint32_t role)
+{
+    if (mbar_try_wait(bar, parity))
+        return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity))
+            return true;
+        if ((it & 63u) == 0) {
+            if (*fail)
+                return false;
+            if (globaltimer() - t0 > bound_ns) {
+                *fail = 1u;
+                atomicOr(status, 1u | (role << 8));
+                return false;
+            }
+        }
+    }
+}
+
+// Warp-collective bounded wait: every lane observes the phase itself (so the
+// data the phase guards is visible to each of them) and the verdict is uniform
+// across the warp, so the warp never splits at a later __syncwarp or bar.sync.
+__device__ __forceinline__ bool tc_wait_warp(uint32_t bar, uint32_t parity, unsigned long long bound_ns,
+                                             volatile uint32_t *fail, unsigned *status, uint32_t role)
+{
+    const int lane = threadIdx.x & 31;
+    const uint64_t t0 = lane == 0 ? globaltimer() : 0;
+    bool done = mbar_try_wait(bar, parity);
+    for (uint32_t it = 1;; ++it) {
+        if (__all_sync(0xffffffffu, done))
+            return true;
+        if ((it & 63u) == 0) {
+            uint32_t give_up = 0;
+            if (lane == 0) {
+                if (*fail) {
+                    give_up = 1;
+                } else if (globaltimer() - t0 > bound_ns) {
+                    *fail = 1u;
+                    atomicOr(status, 1u | (role << 8));
+                    give_up = 1;
+                }
+            }
+            if (__shfl_sync(0xffffffffu, give_up, 0))
+                return false;
+        }
+        if (!done)
+            done = mbar_try_wait(bar, parity);
+    }
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel)
+{
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b)
+{
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// 4 int8 (k order) -> 2 bf16x2 words, exact for every int8 value: the bf16 with bits
+// 0x43mm is 128 + mm for a magnitude mm in [0, 128] (7 stored mantissa bits; 0x4380 is
+// 256), so 0x43|mm minus 128 is the exact magnitude; the sign bit of each source byte
+// is then copied to bit 15 of its half (prmt's sign-replicating selector nibbles 8..b).
+__device__ __forceinline__ void i8x4_to_bf16x4(uint32_t w, uint32_t &lo, uint32_t &hi)
+{
+    const uint32_t mag = __vabs4(w);  // per-byte |v|, -128 -> 0x80 = 128
+    const uint32_t c128 = 0x43004300u;
+    lo = bf16x2_sub(prmt(mag, 0x43434343u, 0x4140u), c128);
+    hi = bf16x2_sub(prmt(mag, 0x43434343u, 0x4342u), c128);
+    lo |= prmt(w, 0u, 0x9484u) & 0x80008000u;
+    hi |= prmt(w, 0u, 0xB4A4u) & 0x80008000u;
+}
+
+// 16 int8 -> 16 bf16 (exact), packed as 8 bf16x2 words in k order.
+__device__ __forceinline__ void i8x16_to_bf16(uint4 q, uint32_t (&o)[8])
+{
+    i8x4_to_bf16x4(q.x, o[0], o[1]);
+    i8x4_to_bf16x4(q.y, o[2], o[3]);
+    i8x4_to_bf16x4(q.z, o[4], o[5]);
+    i8x4_to_bf16x4(q.w, o[6], o[7]);
+}
+
+template <int BN, bool WINT8, int STAGES>
+struct TcSmem {
+    static constexpr int XB = kTcRows * kTcK * 2;   // X tile bytes (16 KB)
+    static constexpr int WB = BN * kTcK * 2;        // W bf16 tile bytes
+    static constexpr int QB = WINT8 ? BN * kTcK : 0; // W int8 staging bytes
+    static constexpr int OFF_X = 0;
+    static constexpr int OFF_W = STAGES * XB;
+    static constexpr int OFF_Q = OFF_W + STAGES * WB;
+    static constexpr int PIPE_END = OFF_Q + STAGES * QB;
+    // split-K exchange, reusing the pipeline buffers once the MMAs are done: the CTA's
+    // partial tile (rows of RS bytes, padded against bank conflicts), then S slots of
+    // R rows each that receive the owners' rows (slot `src` = partial rows of CTA src)
+    static constexpr int RS = BN * 4 + 16;
+    static constexpr int OFF_STAGE = 0;
+    static constexpr int OFF_SLOT = kTcRows * RS;
+    static constexpr int XCHG_END = 2 * kTcRows * RS;
+    static constexpr bool CAN_SPLIT = XCHG_END + 8 * 1024 <= 227 * 1024;
+    static constexpr int REGION = (PIPE_END > XCHG_END || !CAN_SPLIT) ? PIPE_END : XCHG_END;
+    static constexpr int OFF_BAR = (REGION + 1023) / 1024 * 1024;  // full[S], qfull[S], conv[S], empty[S], accf, xchg
+    static constexpr int N_BAR = 4 * STAGES + 2;
+    static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;          // tmem base, fail flag
+    static constexpr int OFF_BIAS = OFF_MISC + 16;                // bias[BN], scale[BN]
+    static constexpr int BYTES = OFF_BIAS + 8 * BN;
+    static constexpr int ALLOC = BYTES + 1024;                    // slack to align the base to 1024
+    static_assert(XB % 1024 == 0 && WB % 1024 == 0 && QB % 1024 == 0, "1024-byte aligned tiles");
+    static_assert(BN == 64 || BN == 128 || BN == 256, "N tile");
+    static_assert(ALLOC <= 227 * 1024, "shared memory");
+};
+
+template <int BN, bool WINT8, int STAGES>
+__global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid_constant__ TcLayerParams p)
+{
+    using L = TcSmem<BN, WINT8, STAGES>;
+    extern __shared__ uint8_t tc_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint32_t *misc = reinterpret_cast<uint32_t *>(smem + L::OFF_MISC);
+    volatile uint32_t *fail = misc + 1;
+    float *s_bias = reinterpret_cast<float *>(smem + L::OFF_BIAS);
+    float *s_scale = s_bias + BN;
+    auto bar = [&](int i) { return sbase + (uint32_t)L::OFF_BAR + 8u * (uint32_t)i; };
+    // barrier indices
+    auto b_full = [&](int s) { return bar(s); };
+    auto b_qfull = [&](int s) { return bar(STAGES + s); };
+    auto b_conv = [&](int s) { return bar(2 * STAGES + s); };
+    auto b_empty = [&](int s) { return bar(3 * STAGES + s); };
+    const uint32_t b_accf = bar(4 * STAGES);
+    const uint32_t b_xchg = bar(4 * STAGES + 1);
+
+    const uint32_t cta_lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    auto stamp = [&](int k) {
+        if (p.trace)
+            p.trace[cta_lin * 8u + (uint32_t)k] = globaltimer();
+    };
+    if (tid == 0)
+        stamp(kTcTraceEntry);
+    const int n0 = blockIdx.x * BN;
+    const int m0 = blockIdx.y * kTcRows;
+    const int k0 = blockIdx.z * p.k_chunk;
+    const int nk = p.k_chunk / kTcK;
+    const int S = p.splits;
+    const int R = kTcRows / S;
+
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(b_full(s), 1);
+            mbar_init(b_qfull(s), 1);
+            mbar_init(b_conv(s), kTcConvThreads / 32);
+            mbar_init(b_empty(s), 1);
+        }
+        mbar_init(b_accf, 1);
+        mbar_init(b_xchg, 1);
+        misc[1] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        prefetch_tmap(&p.tm_x);
+        prefetch_tmap(&p.tm_w);
+    }
+    if (warp == 1) {  // whole warp: allocate BN TMEM columns (power of two >= 32)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         sbase + (uint32_t)L::OFF_MISC),
+                     "r"((uint32_t)BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = misc[0];
+    griddep_launch_dependents();  // the next layer may start its own set-up on free SMs
+
+    // Weights, biases and scales do not depend on the previous layer: fetch them
+    // before waiting for it, so their latency hides behind the previous layer's tail.
+    const int npre = nk < STAGES ? nk : STAGES;
+    if (warp == 0 && lane == 0) {
+        for (int kb = 0; kb < npre; ++kb) {
+            const int kx = k0 + kb * kTcK;
+            if (WINT8) {
+                mbar_arrive_expect_tx(b_qfull(kb), L::QB);
+                tma_load_2d(sbase + L::OFF_Q + kb * L::QB, &p.tm_w, kx, n0, b_qfull(kb));
+            } else {
+                mbar_expect_tx(b_full(kb), L::WB);
+                tma_load_2d(sbase + L::OFF_W + kb * L::WB, &p.tm_w, kx, n0, b_full(kb));
+            }
+        }
+    } else if (warp == 2 || warp == 3) {
+        for (int i = tid - 64; i < BN; i += 64) {
+            s_bias[i] = __ldg(p.bias + n0 + i);
+            s_scale[i] = p.scale ? __ldg(p.scale + n0 + i) : 1.0f;
+        }
+    }
+    griddep_wait();  // X belongs to the previous layer (and Y to the one before it) until here
+    if (tid == 0)
+        stamp(kTcTraceDepDone);
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % STAGES;
+                if (kb >= STAGES && !tc_wait(b_empty(s), ((kb / STAGES) - 1) & 1, p.wait_ns, fail, p.status, 1))
+                    break;
+                const int kx = k0 + kb * kTcK;
+                if (kb >= npre) {  // weight tiles past the prefetched ones
+                    if (WINT8) {
+                        mbar_arrive_expect_tx(b_qfull(s), L::QB);
+                        tma_load_2d(sbase + L::OFF_Q + s * L::QB, &p.tm_w, kx, n0, b_qfull(s));
+                    } else {
+                        mbar_expect_tx(b_full(s), L::WB);
+                        tma_load_2d(sbase + L::OFF_W + s * L::WB, &p.tm_w, kx, n0, b_full(s));
+                    }
+                }
+                mbar_arrive_expect_tx(b_full(s), L::XB);
+                tma_load_2d(sbase + L::OFF_X + s * L::XB, &p.tm_x, kx, m0, b_full(s));
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc_idesc_bf16(BN);
+            bool ok = true;
+            for (int kb = 0; kb < nk && ok; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t ph = (kb / STAGES) & 1;
+                ok = tc_wait(b_full(s), ph, p.wait_ns, fail, p.status, 2);
+                if (ok && WINT8)
+                    ok = tc_wait(b_conv(s), ph, p.wait_ns, fail, p.status, 2);
+                if (!ok)
+                    break;
+                if (kb == 0)
+                    stamp(kTcTraceFirstData);
+                tc_fence_after();
+                const uint32_t xa = sbase + L::OFF_X + s * L::XB, wa = sbase + L::OFF_W + s * L::WB;
+#pragma unroll
+                for (int kk = 0; kk < kTcK / 16; ++kk)
+                    tc_mma_bf16(tmem, sw128_kmajor_desc(xa + kk * 32), sw128_kmajor_desc(wa + kk * 32), idesc,
+                                (kb | kk) != 0);
+                tc_commit(b_empty(s));  // frees stage s when these MMAs complete
+            }
+            stamp(kTcTraceMmaIssued);
+            tc_commit(b_accf);  // accumulator complete (also arrives when nothing was issued)
+        }
+    } else if (WINT8 && warp >= kTcConvWarp0) {
+        // ---------------- int8 -> bf16 operand conversion ----------------
+        const int ct = tid - kTcConvWarp0 * 32;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % STAGES;
+            if (!tc_wait_warp(b_qfull(s), (kb / STAGES) & 1, p.wait_ns, fail, p.status, 3))
+                break;
+            const uint8_t *q = smem + L::OFF_Q + s * L::QB;
+            uint8_t *w = smem + L::OFF_W + s * L::WB;
+            for (int c = ct; c < BN * 4; c += kTcConvThreads) {
+                const int r = c >> 2, j = c & 3;  // row, 16-byte piece of the 64-byte int8 row
+                const uint4 v = *reinterpret_cast<const uint4 *>(q + r * 64 + j * 16);
+                uint32_t o[8];
+                i8x16_to_bf16(v, o);
+                uint8_t *row = w + r * 128;
+                *reinterpret_cast<uint4 *>(row + (((2 * j) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<uint4 *>(row + (((2 * j + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+            fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core (async proxy)
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive_local(b_conv(s));
+        }
+    }
+
+    // ---------------- epilogue ----------------
+    // Warps 4..7 read the accumulator (warp w owns TMEM lanes 32*(w%4)..+31 = tile rows).
+    // Without a K split they finish their rows straight from TMEM.  With a split, the S
+    // CTAs of the cluster each own R = 128/S rows of the tile: every CTA stages its
+    // partial tile in shared memory and sends each owner its R rows with one bulk copy
+    // into the owner's slot for it (completing on the owner's exchange barrier); the
+    // owner adds the S slots in rank order (deterministic) and finishes its rows.
+    // The exchange runs on every path, failed or not, so no copy ever targets a CTA
+    // that has left; only the final writes depend on success.
+    const bool epi = warp >= kTcEpiWarp0 && warp < kTcEpiWarp0 + 4;
+    const int q = warp & 3;
+    const int trow = 32 * q + lane;  // tile row of this epilogue thread
+    if (epi) {
+        tc_wait_warp(b_accf, 0, p.wait_ns, fail, p.status, 4);
+        tc_fence_after();
+        if (tid == kTcEpiWarp0 * 32)
+            stamp(kTcTraceAccum);
+    }
+    const uint32_t rank = S > 1 ? cluster_ctarank() : 0u;
+    if (S > 1) {
+        if (tid == 0)  // bytes the S-1 peers will send into this CTA's slots
+            mbar_arrive_expect_tx(b_xchg, (uint32_t)((S - 1) * R * L::RS));
+        __syncwarp();
+        cluster_sync();  // A: every CTA's MMAs are done: its pipeline buffers may be overwritten
+    } else {
+        __syncthreads();
+    }
+    if (tid == 0)
+        stamp(kTcTraceClusterA);
+    const bool go = *fail == 0u;  // the roles have all finished: stable from here on
+    if (epi && (go || S > 1)) {
+        // own rows go straight into this CTA's own slot; the others to the staging tile
+        const int owner = trow / R;
+        uint8_t *dst_row = (S > 1 && owner != (int)rank) ? smem + L::OFF_STAGE + (size_t)trow * L::RS
+                                                         : smem + L::OFF_SLOT + (size_t)(rank * R + (trow - owner * R)) * L::RS;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+            float v[32];
+            tc_ld_32cols(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+            if (S == 1) {
+                const int n = n0 + c0;
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    v[i] = tc_act(fmaf(v[i], s_scale[c0 + i], s_bias[c0 + i]), p.act);
+                const size_t off = (size_t)(m0 + trow) * p.N + n;
+                if (p.out_f32) {
+                    float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + off);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                } else {
+                    uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.out) + off);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        uint32_t u[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * i + 2 * e], v[8 * i + 2 * e + 1]);
+                            u[e] = *reinterpret_cast<const uint32_t *>(&h);
+                        }
+                        dst[i] = make_uint4(u[0], u[1], u[2], u[3]);
+                    }
+                }
+            } else {
+                float4 *d4 = reinterpret_cast<float4 *>(dst_row + (size_t)c0 * 4);
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            }
+        }
+        if (S > 1)
+            fence_proxy_async_smem();  // staged rows -> visible to the bulk-copy engine
+    }
+    if (S > 1) {
+        __syncthreads();  // the staging tile is complete
+        if (tid == 0) {
+            for (int o = 0; o < S; ++o) {
+                if (o == (int)rank)
+                    continue;
+                const uint32_t src = sbase + (uint32_t)(L::OFF_STAGE + o * R * L::RS);
+                const uint32_t dst = mapa(sbase + (uint32_t)(L::OFF_SLOT + (int)rank * R * L::RS), (uint32_t)o);
+                bulk_s2cluster(dst, src, (uint32_t)(R * L::RS), mapa(b_xchg, (uint32_t)o));
+            }
+            bulk_commit_group();
+        }
+        if (warp == 0) {  // every peer's rows have arrived in this CTA's slots
+            tc_wait_warp(b_xchg, 0, p.wait_ns, fail, p.status, 5);
+        }
+        if (tid == 0)
+            bulk_wait_group_read0();  // this CTA's outgoing copies have read the staging tile
+        __syncthreads();
+        if (tid == 0)
+            stamp(kTcTraceClusterB);
+        if (go && *fail == 0u) {
+            constexpr int C4 = BN / 4;
+            for (int idx = tid; idx < R * C4; idx += kTcThreads) {
+                const int r = idx / C4, c = (idx % C4) * 4;
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int src = 0; src < S; ++src) {
+                    const float4 v =
+                        *reinterpret_cast<const float4 *>(smem + L::OFF_SLOT + (size_t)(src * R + r) * L::RS + (size_t)c * 4);
+                    a.x += v.x;
+                    a.y += v.y;
+                    a.z += v.z;
+                    a.w += v.w;
+                }
+                float o4[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    o4[e] = tc_act(fmaf(o4[e], s_scale[c + e], s_bias[c + e]), p.act);
+                const size_t off = (size_t)(m0 + (int)rank * R + r) * p.N + n0 + c;
+                if (p.out_f32) {
+                    *reinterpret_cast<float4 *>(static_cast<float *>(p.out) + off) =
+                        make_float4(o4[0], o4[1], o4[2], o4[3]);
+                } else {
+                    const __nv_bfloat162 h0 = __floats2bfloat162_rn(o4[0], o4[1]);
+                    const __nv_bfloat162 h1 = __floats2bfloat162_rn(o4[2], o4[3]);
+                    *reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(p.out) + off) =
+                        make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+                }
+            }
+        }
+    }
+
+    // ---------------- drain and free ----------------
+    // A role that gave up leaves copies or MMAs in flight: wait (bounded) until the
+    // accumulator barrier shows every issued MMA finished before TMEM is freed.
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0)
+        stamp(kTcTraceEnd);
+    if (warp == 1) {
+        if (*fail && lane == 0) {
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(b_accf, 0) && globaltimer() - t0 < p.wait_ns) {
+            }
+        }
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN)
+                     : "memory");
+    }
+}
+
+}  // namespace llk

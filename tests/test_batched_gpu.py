@@ -1,0 +1,105 @@
+"""Batched dense path on the tensor cores (tcgen05), against the oracle (need a B200).
+
+Tolerances (norm-wise relative error max|y - ref| / max|ref|, per weight type as
+stated for the workloads): bf16 1e-2, int8 2e-2.  The oracle rounds the input and
+every hidden activation to bf16 like the device path; only the summation order
+differs (tensor-core tiles and split-K partials against a sequential sum).  The
+device path itself is deterministic: split-K partials are added in a fixed order.
+"""
+import numpy as np
+import pytest
+import torch
+
+import low_latency_inference_gpu_b200 as ll
+import oracle
+from conftest import rel_err
+
+pytestmark = [pytest.mark.gpu, pytest.mark.timeout(600)]
+
+TOL = {ll.W_BF16: 1e-2, ll.W_I8: 2e-2}
+
+
+def params(net, seed=0):
+    Ws, bs = ll.init_params(net, ll.INIT_NORMAL_FANIN, seed)
+    return Ws, bs
+
+
+def oracle_out(net, Ws, bs, xs):
+    if net.wtype == ll.W_BF16:
+        return oracle.mlp_bf16(net.dims, net.acts, [ll.f32_to_bf16(w) for w in Ws], bs, xs)
+    qs = [oracle.quantize_int8_rows(w) for w in Ws]
+    return oracle.mlp_int8(net.dims, net.acts, [q for q, _ in qs], [s for _, s in qs], bs, xs)
+
+
+def make(net, Ws, bs, **kw):
+    Wd, bd, sd = ll.device_weights(net, Ws, bs)
+    return ll.BatchedMLP(net, Wd, bd, sd, device=0, opts=ll.batched_opts(**kw) if kw else None)
+
+
+def run_device(m, xs):
+    dx = torch.from_numpy(np.ascontiguousarray(xs, np.float32)).cuda()
+    dy = torch.empty((xs.shape[0], m.out_dim), dtype=torch.float32, device="cuda")
+    s = torch.cuda.current_stream()
+    m.forward(dx.data_ptr(), dy.data_ptr(), xs.shape[0], s.cuda_stream)
+    m.check(s.cuda_stream)
+    return dy.cpu().numpy()
+
+
+@pytest.mark.parametrize("wtype", [ll.W_BF16, ll.W_I8])
+@pytest.mark.parametrize("bn,splits", [(64, 1), (128, 1), (256, 1), (64, 2), (64, 4), (128, 2), (128, 4)])
+def test_small_net_every_tile_shape(wtype, bn, splits):
+    # 256 -> 256 -> 256, ReLU then identity: every kernel variant, with and without split-K
+    net = ll.mlp([256, 256, 256], ll.ACT_RELU, ll.ACT_IDENTITY, wtype, 200)
+    Ws, bs = params(net, 11)
+    xs = ll.fill_uniform(200 * 256, -1.0, 1.0, 12).reshape(200, 256)
+    with make(net, Ws, bs, bn=bn, splits=splits) as m:
+        info = m.info()
+        assert info["bn"] == [bn, bn] and info["splits"] == [splits, splits]
+        y = run_device(m, xs)
+    ref = oracle_out(net, Ws, bs, xs)
+    assert rel_err(y, ref) <= TOL[wtype], (bn, splits)
+
+
+@pytest.mark.parametrize("rows", [1, 7, 128, 129, 256])
+def test_config3_int8_rows(rows):
+    # 1024 -> 2048 x 6 -> 256 int8 weights, per-channel scales, bf16 activations; ragged row counts
+    net = ll.config_net(3)
+    Ws, bs = ll.config_params(3)[1:]
+    xs = ll.config_inputs(3, rows)
+    with make(net, Ws, bs) as m:
+        y = run_device(m, xs)
+    check = np.r_[0:min(rows, 12), max(0, rows - 12):rows]
+    ref = oracle_out(net, Ws, bs, xs[check])
+    assert rel_err(y[check], ref) <= TOL[ll.W_I8]
+
+
+def test_config3_repeated_forwards_are_identical():
+    # the K splits of a tile add their partials in cluster-rank order through shared
+    # memory: no atomics, no workspace, so every forward gives the same bits
+    net = ll.config_net(3)
+    Ws, bs = ll.config_params(3)[1:]
+    xs = ll.config_inputs(3, 256)
+    with make(net, Ws, bs) as m:
+        ys = [run_device(m, xs) for _ in range(3)]
+        y_host = m.infer(xs)
+    assert all(np.array_equal(ys[0], y) for y in ys[1:])
+    assert np.array_equal(ys[0], y_host)
+
+
+@pytest.mark.parametrize("rows", [1, 2, 4, 8, 16, 32])
+def test_config2_bf16_gelu_batch_sweep(rows):
+    net = ll.config_net(2)
+    Ws, bs = ll.config_params(2)[1:]
+    xs = ll.config_inputs(2, rows)
+    with make(net, Ws, bs) as m:
+        y = run_device(m, xs)
+    ref = oracle_out(net, Ws, bs, xs)
+    assert rel_err(y, ref) <= TOL[ll.W_BF16]
+
+
+def test_without_programmatic_launch_matches():
+    net = ll.config_net(2)
+    Ws, bs = ll.config_params(2)[1:]
+    xs = ll.config_inputs(2, 32)
+    with make(net, Ws, bs) as a, make(net, Ws, bs, pdl=0) as b:
+        assert np.array_equal(run_device(a, xs), run_device(b, xs))

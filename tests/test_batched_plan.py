@@ -1,0 +1,42 @@
+"""Host-side checks of the batched tensor-core path (no GPU): tiling choices and
+descriptor validation."""
+import pytest
+
+import low_latency_inference_gpu_b200 as ll
+
+
+def test_config3_fills_the_gpu():
+    p = ll.batched_plan(ll.config_net(3))
+    assert p["rows_pad"] == 256
+    assert all(c <= 148 for c in p["ctas"])
+    assert min(p["ctas"]) >= 128  # every layer uses at least 128 of the 148 SMs
+    assert all(s <= 227 * 1024 for s in p["smem_bytes"])
+    # the square layers: 128-wide tiles split 4 ways (a split 256-wide tile has no room to exchange)
+    assert p["bn"][1:7] == [128] * 6 and p["splits"][1:7] == [4] * 6
+
+
+def test_config2_batch_sweep_plans():
+    for rows in (1, 2, 4, 8, 16, 32):
+        p = ll.batched_plan(ll.config_net(2, rows))
+        assert p["rows_pad"] == 128
+        assert all(1 <= c <= 148 for c in p["ctas"])
+
+
+def test_forced_tiles_are_honoured_and_checked():
+    net = ll.mlp([256, 256, 256], ll.ACT_RELU, ll.ACT_IDENTITY, ll.W_I8, 64)
+    p = ll.batched_plan(net, ll.batched_opts(bn=128, splits=2))
+    assert p["bn"] == [128, 128] and p["splits"] == [2, 2]
+    with pytest.raises(ll.LLError):
+        ll.batched_plan(net, ll.batched_opts(splits=3))  # 3 does not divide 256/64
+    with pytest.raises(ll.LLError):
+        ll.batched_plan(net, ll.batched_opts(bn=96))
+    with pytest.raises(ll.LLError):
+        ll.batched_plan(net, ll.batched_opts(bn=256, splits=2))  # no shared memory for the exchange
+
+
+@pytest.mark.parametrize("dims,wtype", [([100, 256], ll.W_BF16), ([256, 100], ll.W_I8), ([256, 256], ll.W_F32)])
+def test_unsupported_nets_are_rejected(dims, wtype):
+    net = ll.mlp(dims, ll.ACT_RELU, ll.ACT_IDENTITY, wtype, 8)
+    with pytest.raises(ll.LLError) as e:
+        ll.batched_plan(net)
+    assert e.value.code == ll.LL_ERR_BAD_DESC
