@@ -21,6 +21,11 @@ Reported:
           formats and the engine's p50 over them; the cuBLAS+graph and
           launch-per-layer graph paths timed end to end in the same run (N=1).
   cpu_baseline  the reference's own CPU forward (oracle/_ref) on one host core.
+  batched the batched dense path on the tensor cores (tcgen05), N=1: the int8
+          1024->2048x6->256 MLP at 256 rows against the measured bf16 peak, and
+          the bf16 GELU 256->1024x4->64 MLP over rows 1..32 against HBM bandwidth
+          (L2 flushed between forwards; kernel-only and end-to-end with pinned
+          host copies).
   --impl reference  runs the reference's CPU forward on all host cores instead.
 """
 import argparse
@@ -54,6 +59,83 @@ def env_int(name, default):
         return int(os.environ.get(name, default))
     except ValueError:
         return default
+
+
+def measured_peak(key, fallback):
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)[key]), "measured"
+    except Exception:
+        return fallback, "fallback"
+
+
+def run_batched(ll, torch, dev, iters=30):
+    """Batched tensor-core path: per-forward device time (CUDA events on the launching
+    stream, 256 MiB L2 flush before each) and end to end (pinned host x -> device ->
+    forward -> pinned host y, all inside the events)."""
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=f"cuda:{dev}")
+    out = {}
+
+    def timed(m, rows, cfg):
+        xs = ll.config_inputs(cfg, rows)
+        hx = torch.from_numpy(xs).pin_memory()
+        hy = torch.empty((rows, m.out_dim), dtype=torch.float32).pin_memory()
+        dx = hx.to(f"cuda:{dev}")
+        dy = torch.empty((rows, m.out_dim), dtype=torch.float32, device=f"cuda:{dev}")
+        for _ in range(5):
+            m.forward(dx.data_ptr(), dy.data_ptr(), rows, stream.cuda_stream)
+        m.check(stream.cuda_stream)
+        dev_ms, e2e_ms = [], []
+        for it in range(2 * iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if it % 2:
+                dx.copy_(hx, non_blocking=True)
+            m.forward(dx.data_ptr(), dy.data_ptr(), rows, stream.cuda_stream)
+            if it % 2:
+                hy.copy_(dy, non_blocking=True)
+            e1.record(stream)
+            e1.synchronize()
+            (e2e_ms if it % 2 else dev_ms).append(e0.elapsed_time(e1))
+        m.check(stream.cuda_stream)
+        return statistics.median(dev_ms), statistics.median(e2e_ms)
+
+    # int8 weights + per-channel scales, bf16 activations, batch 256
+    net, Ws, bs = ll.config_params(3)
+    Wd, bd, sd = ll.device_weights(net, Ws, bs)
+    tf_peak, tf_kind = measured_peak("bf16_tflops", 1590.0)
+    with ll.BatchedMLP(net, Wd, bd, sd, device=dev) as m:
+        ms, e2e = timed(m, 256, 3)
+        flops = 2.0 * 256 * net.n_params
+        achieved = flops / (ms * 1e-3) / 1e12
+        out["int8_mlp_1024x2048x6x256_rows256"] = {
+            "ms_per_forward": ms, "e2e_ms_per_forward": e2e, "forwards_per_s": 1e3 / ms,
+            "rows_per_s": 256e3 / ms, "tiling": m.info(),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak, "peak_kind": tf_kind,
+                         "unit": "TFLOP/s", "frac": achieved / tf_peak,
+                         "algorithmic": f"{flops / 1e9:.2f} GFLOP per forward (2 x 256 rows x {net.n_params} weights)"}}
+    # bf16 weights, GELU, batch sweep 1..32
+    net, Ws, bs = ll.config_params(2)
+    Wd, bd, sd = ll.device_weights(net, Ws, bs)
+    wbytes = sum(w.nbytes for w in Wd) + sum(b.nbytes for b in bd)
+    hbm, hbm_kind = measured_peak("hbm_gbs", FALLBACK_HBM_GBS)
+    sweep = []
+    with ll.BatchedMLP(net, Wd, bd, sd, device=dev) as m:
+        for rows in (1, 2, 4, 8, 16, 32):
+            ms, e2e = timed(m, rows, 2)
+            nbytes = wbytes + rows * (net.dims[0] + net.dims[-1]) * 4
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            sweep.append({"rows": rows, "us_per_forward": ms * 1e3, "e2e_us_per_forward": e2e * 1e3,
+                          "rows_per_s": rows * 1e3 / ms,
+                          "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "peak_kind": hbm_kind,
+                                       "unit": "GB/s", "frac": gbs / hbm}})
+        tiling = m.info()
+    out["bf16_gelu_mlp_256x1024x4x64_sweep"] = {"points": sweep, "tiling": tiling,
+                                                "algorithmic": "bf16 weights + biases + rows x (in + out) fp32"}
+    return out
 
 
 def measured_peak_hbm():
@@ -173,9 +255,11 @@ def main():
     ap.add_argument("--ref-requests", type=int, default=400000, help="reference arm: requests per step, all cores")
     ap.add_argument("--cpu-requests", type=int, default=100000, help="cpu_baseline sample (one core)")
     ap.add_argument("--no-compare", action="store_true", help="skip the cuBLAS / launch-per-layer comparison paths")
-    ap.add_argument("--only", default="all", choices=["all", "value"],
+    ap.add_argument("--no-batched", action="store_true", help="skip the batched tensor-core section")
+    ap.add_argument("--only", default="all", choices=["all", "value", "batched"],
                     help="value: run only the device-queue phase (bounded launches; usable under ncu, which "
-                         "serialises launches and so cannot drive the resident mailbox kernel)")
+                         "serialises launches and so cannot drive the resident mailbox kernel); batched: only "
+                         "the batched tensor-core section, printed as its own JSON line")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -194,6 +278,9 @@ def main():
 
     torch.cuda.set_device(local_rank)
     dev = local_rank
+    if args.only == "batched":
+        print(json.dumps({"batched": run_batched(ll, torch, dev, iters=10)}), flush=True)
+        return
     host_group = None
     if world > 1:
         from datetime import timedelta
@@ -325,6 +412,9 @@ def main():
                     lat, _ = m.bench(mode, xs, 10000)
                     s = ll.compute_stats(lat)
                     compare[f"{name}_{mname}"] = {"p50_us": s["p50"], "p99_us": s["p99"]}
+    batched = None
+    if world == 1 and full and not args.no_batched:
+        batched = run_batched(ll, torch, dev)
     if rank == 0 and world == 1 and full:
         import oracle
 
@@ -388,6 +478,7 @@ def main():
                      "note": "algorithmic bytes = resident weights+biases (345 KB) + x/y per request; the batch-1 "
                              "path is latency-bound, latency_floor is its relevant bound"},
         "cpu_baseline": cpu_baseline,
+        "batched": batched,
         "clocks": clk,
         "gpu_launches": K + e2e_launches,
         "per_rank": per_rank,

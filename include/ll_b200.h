@@ -96,7 +96,10 @@ typedef struct ll_engine_opts {
                                    LL_ERR_DEVICE_FAULT at location 6 and leaves (no fault is caused) */
     int32_t kernel_variant;     /* 0 = automatic, 1 = generic shared-memory kernel, 2 = register-resident
                                    kernel compiled for the net's shape (3-layer fp32, batch 1) */
-    int32_t reserved[4];
+    int32_t ring_slots;         /* tagged mailbox only: request slots (1..64; 0 = 1).  Up to ring_slots
+                                   requests may be outstanding (ll_submit before the earlier ll_poll);
+                                   the device serves them in order, slot after slot */
+    int32_t reserved[3];
 } ll_engine_opts;
 
 typedef struct ll_engine_info {
@@ -316,10 +319,11 @@ int ll_batched_mlp_check(ll_batched_mlp *m, void *stream);
 /* Host buffers: copy x in, forward, check, copy y out (on the object's own stream). */
 int ll_batched_mlp_infer(ll_batched_mlp *m, const float *x, float *y, int n_rows);
 int ll_batched_mlp_info(ll_batched_mlp *m, ll_batched_info *info);
-/* Optional phase trace (device buffer of n >= n_layers * max_ctas * 8 entries, or NULL to stop):
- * every CTA of layer l writes 8 globaltimer stamps at d_trace[(l * max_ctas + cta) * 8 + k],
- * max_ctas = the largest ctas[] of ll_batched_mlp_info; k = entry, previous layer done, first
- * stage landed, last MMA issued, accumulator complete, cluster barrier 1, cluster barrier 2, end. */
+/* Optional phase trace (device buffer of n >= n_layers * max_ctas * 16 entries, or NULL to stop):
+ * every CTA of layer l writes globaltimer stamps at d_trace[(l * max_ctas + cta) * 16 + k],
+ * max_ctas = the largest ctas[] of ll_batched_mlp_info; k = 0 entry, 1 previous layer done,
+ * 2 first stage landed, 3 last MMA issued, 4 accumulator complete, 5 cluster barrier,
+ * 6 partial rows exchanged, 7 end, 8 partial tile staged (split-K only). */
 int ll_batched_mlp_set_trace(ll_batched_mlp *m, unsigned long long *d_trace, size_t n);
 int ll_batched_mlp_destroy(ll_batched_mlp *m);
 
@@ -410,6 +414,22 @@ int ll_tagged_wait(const void *mailbox, int in_dim, int out_dim, uint32_t seq, f
 
 /* Next sequence number after seq: skips 0 (idle) and LL_STOP_SEQ. */
 uint32_t ll_next_seq(uint32_t seq);
+
+/*
+ * Open-loop serving of a Poisson request stream (no counterpart in the reference,
+ * whose benches are closed loops).  The stream has n_total requests with
+ * exponential gaps of mean 1/rate_per_s (std::mt19937_64(seed)); after each gap
+ * a GPU is drawn uniformly from [0, world) from the same generator, so every
+ * rank sees the same stream and serves the requests drawn for `rank`, in
+ * arrival order, input row (request index % n_x) of xs.  A request is posted
+ * when its arrival time has come and a mailbox slot is free (up to ring_slots
+ * outstanding on the tagged mailbox, one on the TickBuffer); lat_us[j] (capacity
+ * n_total) receives the time from the scheduled arrival of this rank's j-th
+ * request to the host seeing its reply, in microseconds.  *n_served = requests
+ * of this rank, *elapsed_s = start to the last reply.  Batch-1 engines.
+ */
+int ll_engine_serve_poisson(ll_engine *e, const float *xs, int n_x, int n_total, double rate_per_s, uint64_t seed,
+                            int rank, int world, double *lat_us, int *n_served, double *elapsed_s);
 
 /* Library version string. */
 const char *ll_version(void);

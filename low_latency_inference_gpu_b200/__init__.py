@@ -55,7 +55,7 @@ EXPORTED_SYMBOLS = [
     "ll_tagged_mailbox_bytes", "ll_tagged_y_offset", "ll_tagged_post", "ll_tagged_wait",
     "ll_batched_opts_default", "ll_batched_plan", "ll_batched_mlp_create", "ll_batched_mlp_forward",
     "ll_batched_mlp_check", "ll_batched_mlp_infer", "ll_batched_mlp_info", "ll_batched_mlp_destroy",
-    "ll_batched_mlp_set_trace",
+    "ll_batched_mlp_set_trace", "ll_engine_serve_poisson",
 ]
 MAX_LAYERS = 24
 
@@ -82,7 +82,7 @@ class EngineOpts(ctypes.Structure):
                 ("write_combined", ctypes.c_int32), ("mailbox_format", ctypes.c_int32),
                 ("idle_timeout_ns", ctypes.c_uint64), ("step_timeout_ns", ctypes.c_uint64),
                 ("max_stages", ctypes.c_int32), ("min_stages", ctypes.c_int32), ("diag_wait_never", ctypes.c_int32),
-                ("kernel_variant", ctypes.c_int32), ("reserved", ctypes.c_int32 * 4)]
+                ("kernel_variant", ctypes.c_int32), ("ring_slots", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
 
 
 class EngineInfo(ctypes.Structure):
@@ -199,6 +199,9 @@ def _sig(lib):
         "ll_batched_mlp_info": (ctypes.c_int, [_vp, P(BatchedInfo)]),
         "ll_batched_mlp_destroy": (ctypes.c_int, [_vp]),
         "ll_batched_mlp_set_trace": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t]),
+        "ll_engine_serve_poisson": (ctypes.c_int, [_vp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_double,
+                                                   ctypes.c_uint64, ctypes.c_int, ctypes.c_int, _dp,
+                                                   ctypes.POINTER(ctypes.c_int), _dp]),
     }
     for name, (res, args) in s.items():
         f = getattr(lib, name)
@@ -445,6 +448,18 @@ class Engine:
         _check(lib().ll_engine_bench_closed_loop(self.h, _f(xs), xs.shape[0], n_req, n_rows,
                                                  _f(ys) if ys is not None else None, _d(lat)))
         return lat, ys
+
+    def serve_poisson(self, xs: np.ndarray, n_total: int, rate_per_s: float, seed: int = 5, rank: int = 0,
+                      world: int = 1):
+        """Open-loop Poisson stream (see ll_engine_serve_poisson): (latencies in us of this rank's
+        requests, from their scheduled arrival; seconds from the start to the last reply)."""
+        xs = np.ascontiguousarray(xs, np.float32).reshape(-1, self.in_dim)
+        lat = np.empty(max(1, n_total), np.float64)
+        n = ctypes.c_int()
+        el = ctypes.c_double()
+        _check(lib().ll_engine_serve_poisson(self.h, _f(xs), xs.shape[0], n_total, rate_per_s, seed, rank, world,
+                                             _d(lat), ctypes.byref(n), ctypes.byref(el)))
+        return lat[:n.value].copy(), el.value
 
     def run_queue(self, d_x_ptr: int, d_y_ptr: int, n_req: int, n_rows: int = 1, d_stamps_ptr: int = 0) -> float:
         ms = ctypes.c_float()

@@ -31,7 +31,8 @@ struct LayerRun {
 template <int BN, bool I8>
 constexpr int stages_for()
 {
-    return (I8 && BN == 256) ? 3 : 4;
+    // as many stages as fit beside the exchange region: more bytes in flight per SM
+    return I8 ? (BN == 256 ? 3 : BN == 128 ? 5 : 6) : (BN == 256 ? 4 : BN == 128 ? 6 : 8);
 }
 
 template <int BN, bool I8>
@@ -59,8 +60,10 @@ bool can_split(int bn, bool i8)
         return i8 ? TcSmem<256, true, stages_for<256, true>()>::CAN_SPLIT
                   : TcSmem<256, false, stages_for<256, false>()>::CAN_SPLIT;
     if (bn == 128)
-        return i8 ? TcSmem<128, true, 4>::CAN_SPLIT : TcSmem<128, false, 4>::CAN_SPLIT;
-    return i8 ? TcSmem<64, true, 4>::CAN_SPLIT : TcSmem<64, false, 4>::CAN_SPLIT;
+        return i8 ? TcSmem<128, true, stages_for<128, true>()>::CAN_SPLIT
+                  : TcSmem<128, false, stages_for<128, false>()>::CAN_SPLIT;
+    return i8 ? TcSmem<64, true, stages_for<64, true>()>::CAN_SPLIT
+              : TcSmem<64, false, stages_for<64, false>()>::CAN_SPLIT;
 }
 
 int split_at_most(int n, int cap)
@@ -567,7 +570,7 @@ int ll_batched_mlp_set_trace(ll_batched_mlp *m, unsigned long long *d_trace, siz
 {
     if (!m)
         return LL_ERR_INVALID_ARG;
-    const size_t per_layer = (size_t)m->max_ctas * 8;
+    const size_t per_layer = (size_t)m->max_ctas * kTcTraceSlots;
     if (d_trace && n < per_layer * m->runs.size()) {
         llh::set_error("trace buffer needs %zu entries", per_layer * m->runs.size());
         return LL_ERR_INVALID_ARG;

@@ -5,7 +5,10 @@
 #include <algorithm>
 #include <chrono>
 #include <cstring>
+#include <deque>
+#include <random>
 #include <thread>
+#include <utility>
 #include <vector>
 
 #include "common.h"
@@ -396,7 +399,12 @@ struct ll_engine {
     float *d_xfer = nullptr;
     unsigned *d_words = nullptr;  // [kMaxStages] cnt, [2*kMaxStages] hdr, abort, q_done
     uint32_t seq = 0;
-    uint32_t outstanding = 0;
+    // requests posted and not yet collected, oldest first: (seq, ring index); the
+    // tagged ring holds up to `ring` of them, the TickBuffer one
+    std::deque<std::pair<uint32_t, uint64_t>> inflight;
+    int ring = 1;           // tagged ring slots
+    size_t ring_stride = 0; // bytes between slots
+    uint64_t ring_next = 0; // ring index of the next request to post
     uint32_t last_served = 0;
     bool running = false;
     int launches = 0;
@@ -470,8 +478,17 @@ int alloc_mailbox(ll_engine *e)
         llh::set_error("unknown mailbox format %d", e->opts.mailbox_format);
         return LL_ERR_INVALID_ARG;
     }
-    e->mb_bytes = e->opts.mailbox_format == 1 ? ll_tagged_mailbox_bytes(e->in_dim, e->out_dim)
-                                              : ll_mailbox_bytes(e->in_dim, e->out_dim, e->max_batch);
+    e->ring = e->opts.ring_slots < 1 ? 1 : e->opts.ring_slots;
+    if (e->ring > 1 && (e->opts.mailbox_format != 1 || e->ring > 64)) {
+        llh::set_error("a request ring (ring_slots %d) needs the tagged mailbox and at most 64 slots", e->ring);
+        return LL_ERR_UNSUPPORTED;
+    }
+    if (e->opts.mailbox_format == 1) {
+        e->ring_stride = llh::round_up(ll_tagged_y_offset(e->in_dim) + 16 * (size_t)((e->out_dim + 2) / 3), 64);
+        e->mb_bytes = e->ring_stride * (size_t)e->ring;  // one slot: exactly ll_tagged_mailbox_bytes
+    } else {
+        e->mb_bytes = ll_mailbox_bytes(e->in_dim, e->out_dim, e->max_batch);
+    }
     unsigned flags = cudaHostAllocMapped | cudaHostAllocPortable;
     if (e->wc)
         flags |= cudaHostAllocWriteCombined;
@@ -525,6 +542,9 @@ int finish_setup(ll_engine *e)
                                        sizeof(float) * (size_t)e->in_dim * e->max_batch);
     p.ctrl = e->ctrl_dev;
     p.mailbox_format = e->opts.mailbox_format;
+    p.ring_slots = e->ring;
+    p.ring_stride_f = (uint32_t)(e->ring_stride / 4);
+    p.ring_base = 0;
     p.idle_ns = e->opts.idle_timeout_ns;
     p.step_ns = e->opts.step_timeout_ns;
     p.peer_margin_ns = 2ull * 1000 * 1000 * 1000;
@@ -634,6 +654,16 @@ int ensure_running(ll_engine *e)
     Params p = e->base;
     p.mode = MODE_MAILBOX;
     p.last_seq = e->last_served;
+    // ring position of the first request the device has not taken: just after the
+    // last one it answered, else the oldest one still in flight
+    p.ring_base = (uint32_t)(e->ring_next % (uint64_t)e->ring);
+    if (!e->inflight.empty()) {
+        uint64_t idx = e->inflight.front().second;
+        for (const auto &f : e->inflight)
+            if (f.first == e->last_served)
+                idx = f.second + 1;
+        p.ring_base = (uint32_t)(idx % (uint64_t)e->ring);
+    }
     // make sure the doorbell state is consistent: seq_out == last served
     int rc = launch(e, p);
     if (rc)
@@ -676,10 +706,19 @@ int engine_common_create(ll_engine *e, const ll_engine_opts *opts)
 
 // Spin on seq_out with liveness checks; copies y.
 // Format 1: true once every y chunk carries `seq` (then y is copied out).
+size_t ring_slot_of(const ll_engine *e, uint32_t seq)
+{
+    for (const auto &f : e->inflight)
+        if (f.first == seq)
+            return (size_t)(f.second % (uint64_t)e->ring);
+    return 0;
+}
+
 bool tagged_done(ll_engine *e, uint32_t seq, float *y)
 {
     const int yc = (e->out_dim + 2) / 3;
-    const char *base = static_cast<const char *>(e->mb_host) + ll_tagged_y_offset(e->in_dim);
+    const char *base = static_cast<const char *>(e->mb_host) + ring_slot_of(e, seq) * e->ring_stride +
+                       ll_tagged_y_offset(e->in_dim);
     uint32_t w[4];
     for (int c = 0; c < yc; ++c) {
         llh::load16(base + 16 * c, w);  // the whole chunk in one load: tag and values together
@@ -728,26 +767,51 @@ int engine_wait(ll_engine *e, uint32_t seq, float *y, int n_rows, uint64_t timeo
                                                           sizeof(float) * (size_t)e->in_dim * e->max_batch);
         std::memcpy(y, yd, sizeof(float) * (size_t)e->out_dim * n_rows);
     }
-    e->last_served = seq;
+    // a ring's device position comes from seq_out alone (reap): replies may be collected
+    // out of order, so a collected seq says nothing about what the device took last
+    if (e->ring == 1)
+        e->last_served = seq;
+    for (auto it = e->inflight.begin(); it != e->inflight.end(); ++it)
+        if (it->first == seq) {
+            e->inflight.erase(it);
+            break;
+        }
     return LL_OK;
 }
 
-// Post one request in the engine's mailbox format.
+// Post one request in the engine's mailbox format (tagged: into the next ring slot).
 void engine_post(ll_engine *e, const float *x, int n_rows, uint32_t seq)
 {
-    if (e->opts.mailbox_format == 1)
-        ll_tagged_post(e->mb_host, e->in_dim, x, seq);
-    else
+    if (e->opts.mailbox_format == 1) {
+        const size_t slot = (size_t)(e->ring_next % (uint64_t)e->ring);
+        char *base = static_cast<char *>(e->mb_host) + slot * e->ring_stride + sizeof(ll_tick_header);
+        const int xc = (e->in_dim + 2) / 3;
+        for (int c = 0; c < xc; ++c) {
+            uint32_t w[4] = {0u, 0u, 0u, seq};
+            for (int k = 0; k < 3 && 3 * c + k < e->in_dim; ++k)
+                std::memcpy(&w[k], &x[3 * c + k], 4);
+            llh::store16(base + 16 * c, w);  // one aligned 16-byte store per chunk
+        }
+        auto *h = static_cast<ll_tick_header *>(e->mb_host);
+        h->n_rows = 1;
+        __atomic_store_n(const_cast<uint32_t *>(&h->seq_in), seq, __ATOMIC_RELEASE);  // bookkeeping only
+    } else {
         ll_mailbox_post(e->mb_host, e->in_dim, x, n_rows, seq, e->wc);
+    }
+    e->inflight.emplace_back(seq, e->ring_next++);
+    e->seq = seq;
 }
 
 int engine_stop_kernel(ll_engine *e)
 {
     if (!e->running)
         return LL_OK;
-    if (e->outstanding) {
-        engine_wait(e, e->outstanding, nullptr, 1, 1000ull * 1000 * 1000);
-        e->outstanding = 0;
+    while (!e->inflight.empty()) {
+        const uint32_t s = e->inflight.front().first;
+        if (engine_wait(e, s, nullptr, 1, 1000ull * 1000 * 1000) != LL_OK) {
+            e->inflight.clear();
+            break;
+        }
     }
     ll_tick_header *h = static_cast<ll_tick_header *>(e->mb_host);
     __atomic_store_n(const_cast<uint32_t *>(&h->stop), 1u, __ATOMIC_RELEASE);
@@ -1105,8 +1169,9 @@ int ll_submit(ll_engine *e, const float *x, int n_rows, uint32_t *seq)
         llh::set_error("ll_submit: bad engine or n_rows %d (max %d)", n_rows, e ? e->max_batch : 0);
         return LL_ERR_INVALID_ARG;
     }
-    if (e->outstanding) {
-        llh::set_error("ll_submit: request %u still outstanding (single-slot mailbox)", e->outstanding);
+    const size_t cap = e->opts.mailbox_format == 1 ? (size_t)e->ring : 1u;
+    if (e->inflight.size() >= cap) {
+        llh::set_error("ll_submit: %zu request(s) outstanding (the mailbox holds %zu)", e->inflight.size(), cap);
         return LL_ERR_BUSY;
     }
     int rc = ensure_running(e);
@@ -1118,8 +1183,6 @@ int ll_submit(ll_engine *e, const float *x, int n_rows, uint32_t *seq)
         return LL_ERR_INVALID_ARG;
     }
     engine_post(e, x, n_rows, s);
-    e->seq = s;
-    e->outstanding = s;
     if (seq)
         *seq = s;
     return LL_OK;
@@ -1133,10 +1196,7 @@ int ll_poll(ll_engine *e, uint32_t seq, float *y, uint64_t timeout_ns)
     }
     const ll_tick_header *h = static_cast<const ll_tick_header *>(e->mb_host);
     const int n_rows = h->n_rows == 0 ? 1 : (int)h->n_rows;
-    int rc = engine_wait(e, seq, y, n_rows, timeout_ns);
-    if (rc == LL_OK && e->outstanding == seq)
-        e->outstanding = 0;
-    return rc;
+    return engine_wait(e, seq, y, n_rows, timeout_ns);
 }
 
 int ll_infer(ll_engine *e, const float *x, int n_rows, float *y, uint64_t timeout_ns)
@@ -1227,7 +1287,7 @@ int ll_engine_bench_closed_loop(ll_engine *e, const float *xs, int n_x, int n_re
         llh::set_error("ll_engine_bench_closed_loop: invalid arguments");
         return LL_ERR_INVALID_ARG;
     }
-    if (e->outstanding) {
+    if (!e->inflight.empty()) {
         llh::set_error("request outstanding");
         return LL_ERR_BUSY;
     }
@@ -1241,16 +1301,95 @@ int ll_engine_bench_closed_loop(ll_engine *e, const float *xs, int n_x, int n_re
         const auto t0 = std::chrono::steady_clock::now();
         const uint32_t s = ll_next_seq(e->last_served > e->seq ? e->last_served : e->seq);
         engine_post(e, xs + (size_t)(r % n_x) * xin, n_rows, s);
-        e->seq = s;
-        e->outstanding = s;
         rc = engine_wait(e, s, ys ? ys + (size_t)r * yout : ybuf.data(), n_rows, 2000ull * 1000 * 1000);
         const auto t1 = std::chrono::steady_clock::now();
         if (rc)
             return rc;
-        e->outstanding = 0;
         if (lat_us)
             lat_us[r] = std::chrono::duration<double, std::micro>(t1 - t0).count();
     }
+    return LL_OK;
+}
+
+int ll_engine_serve_poisson(ll_engine *e, const float *xs, int n_x, int n_total, double rate_per_s, uint64_t seed,
+                            int rank, int world, double *lat_us, int *n_served, double *elapsed_s)
+{
+    if (!e || !xs || n_x < 1 || n_total < 0 || !(rate_per_s > 0) || world < 1 || rank < 0 || rank >= world ||
+        !lat_us || e->max_batch != 1) {
+        llh::set_error("ll_engine_serve_poisson: invalid arguments");
+        return LL_ERR_INVALID_ARG;
+    }
+    if (!e->inflight.empty()) {
+        llh::set_error("request outstanding");
+        return LL_ERR_BUSY;
+    }
+    // the whole stream, identical on every rank: exponential gaps, then a uniform GPU per request
+    std::mt19937_64 rng(seed);
+    std::exponential_distribution<double> gap(rate_per_s);
+    std::uniform_int_distribution<int> gpu(0, world - 1);
+    std::vector<double> arrive;  // seconds from the start, this rank's requests
+    std::vector<int> which;      // global request index (selects the input row)
+    double t = 0.0;
+    for (int i = 0; i < n_total; ++i) {
+        t += gap(rng);
+        if (gpu(rng) == rank) {
+            arrive.push_back(t);
+            which.push_back(i);
+        }
+    }
+    int rc = ensure_running(e);
+    if (rc)
+        return rc;
+    const size_t cap = e->opts.mailbox_format == 1 ? (size_t)e->ring : 1u;
+    const size_t n = arrive.size();
+    const size_t xin = (size_t)e->in_dim;
+    using clk = std::chrono::steady_clock;
+    const auto t0 = clk::now() + std::chrono::microseconds(200);
+    auto at = [&](size_t j) { return t0 + std::chrono::nanoseconds((int64_t)(arrive[j] * 1e9)); };
+    size_t posted = 0, done = 0;
+    auto last_progress = clk::now();
+    while (done < n) {
+        const auto now = clk::now();
+        while (posted < n && e->inflight.size() < cap && now >= at(posted)) {
+            const uint32_t s = ll_next_seq(e->last_served > e->seq ? e->last_served : e->seq);
+            engine_post(e, xs + (size_t)(which[posted] % n_x) * xin, 1, s);
+            ++posted;
+        }
+        if (!e->inflight.empty()) {
+            const uint32_t s = e->inflight.front().first;
+            const bool ok = e->opts.mailbox_format == 1
+                                ? tagged_done(e, s, nullptr)
+                                : __atomic_load_n(const_cast<const uint32_t *>(&static_cast<ll_tick_header *>(
+                                                      e->mb_host)->seq_out),
+                                                  __ATOMIC_ACQUIRE) == s;
+            if (ok) {
+                rc = engine_wait(e, s, nullptr, 1, 0);  // bookkeeping: the reply is there
+                if (rc)
+                    return rc;
+                const auto tdone = clk::now();
+                lat_us[done] = std::chrono::duration<double, std::micro>(tdone - at(done)).count();
+                ++done;
+                last_progress = tdone;
+                continue;
+            }
+            if (now - last_progress > std::chrono::seconds(2)) {
+                if (e->ctrl_host->state == ST_EXITED) {
+                    rc = ensure_running(e);
+                    if (rc)
+                        return rc;
+                    last_progress = clk::now();
+                    continue;
+                }
+                llh::set_error("serve: request seq %u not answered within 2 s", s);
+                return LL_ERR_TIMEOUT;
+            }
+        }
+        cpu_relax();
+    }
+    if (n_served)
+        *n_served = (int)n;
+    if (elapsed_s)
+        *elapsed_s = std::chrono::duration<double>(clk::now() - t0).count();
     return LL_OK;
 }
 

@@ -94,6 +94,11 @@ struct Params {
     unsigned *q_done;     // queue-mode completion counter (multi-stage)
     uint64_t idle_ns, step_ns, peer_margin_ns;
     uint32_t last_seq;
+    // tagged request ring: request n of this launch uses slot (ring_base + n) % ring_slots,
+    // ring_stride_f floats apart (1 slot = the single tagged mailbox)
+    int32_t ring_slots;
+    uint32_t ring_stride_f;
+    uint32_t ring_base;
     int32_t diag_wait_never;
     unsigned long long *trace;  // optional [trace_n][kTraceSlots] timeline of the first requests
     int32_t trace_n;

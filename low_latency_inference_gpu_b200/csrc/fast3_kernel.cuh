@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             } else {
                 if (p.mailbox_format == 1) {
                     if (warp == 0) {
-                        const uint32_t c = poll_tagged(k, last, xs);  // x arrives with the doorbell
+                        const uint32_t c = poll_tagged(k, last, xs, ring_slot(p, n_done));  // x arrives with the doorbell
                         if (tid == 0) {
                             if (c == kCmdExit)
                                 broadcast_abort(k);
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                 const float t2 = __shfl_sync(0xffffffffu, v, (3 * lane + 2) & 31);
                 if (tagged) {
                     if (lane < NYC)
-                        st_relaxed_sys_v4(p.mb_y + 4 * lane,
+                        st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done) * p.ring_stride_f + 4 * lane,
                                           make_float4(t0, 3 * lane + 1 < OUT ? t1 : 0.f, 3 * lane + 2 < OUT ? t2 : 0.f,
                                                       __uint_as_float(seq)));
                 } else if ((lane & 3) == 0 && lane < OUT) {

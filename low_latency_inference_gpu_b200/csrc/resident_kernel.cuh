@@ -270,15 +270,30 @@ __device__ uint32_t poll_mailbox(const KernelCtx &k, uint32_t last)
 // Tagged mailbox (format 1), warp 0 of the dispatcher: every lane loads up to
 // kTagChunksPerLane 16-byte x chunks {v0, v1, v2, tag} per poll; the request is
 // taken when every chunk carries the same new tag, and its floats go straight
-// into X -- detection and the x read are one PCIe round trip.
+// into X -- detection and the x read are one PCIe round trip.  With a ring of
+// slots the new tag must be exactly the next sequence number (a slot's previous
+// lap holds an older one); a single slot accepts any tag other than the last.
 constexpr int kTagChunksPerLane = 4;
 
-__device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X)
+__device__ __forceinline__ uint32_t next_seq_dev(uint32_t s)
+{
+    const uint32_t n = s + 1u;
+    return (n == 0u || n == LL_STOP_SEQ) ? 1u : n;
+}
+
+// Slot of request n of this launch in the tagged ring (x and y bases).
+__device__ __forceinline__ uint32_t ring_slot(const Params &p, uint32_t n)
+{
+    return p.ring_slots > 1 ? (p.ring_base + n) % (uint32_t)p.ring_slots : 0u;
+}
+
+__device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uint32_t slot)
 {
     const Params &p = *k.p;
     const int lane = threadIdx.x & 31;
     const int nxc = (p.in_dim + 2) / 3;
-    const uint4 *chunks = reinterpret_cast<const uint4 *>(p.mb_x);
+    const uint4 *chunks = reinterpret_cast<const uint4 *>(p.mb_x + (size_t)slot * p.ring_stride_f);
+    const uint32_t want = next_seq_dev(last);
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 0;; ++it) {
         uint4 c[kTagChunksPerLane];
@@ -292,7 +307,7 @@ __device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X)
         for (int j = 0; j < kTagChunksPerLane; ++j)
             if (lane + 32 * j < nxc && c[j].w != tag)
                 same = false;
-        if (__all_sync(0xffffffffu, same) && tag != last && tag != 0) {
+        if (__all_sync(0xffffffffu, same) && (p.ring_slots > 1 ? tag == want : (tag != last && tag != 0))) {
 #pragma unroll
             for (int j = 0; j < kTagChunksPerLane; ++j) {
                 const int ch = lane + 32 * j;
@@ -572,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
             } else {
                 if (p.mailbox_format == 1) {
                     if (tid < 32) {
-                        const uint32_t c = poll_tagged(k, last, buf_ptr(k, BUF_X));
+                        const uint32_t c = poll_tagged(k, last, buf_ptr(k, BUF_X), ring_slot(p, n_done));
                         if (tid == 0) {
                             if (c == kCmdExit)
                                 broadcast_abort(k);
@@ -819,7 +834,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                             v[e] = G[o];
                         }
                     }
-                    st_relaxed_sys_v4(p.mb_y + 4 * ch, make_float4(v[0], v[1], v[2], __uint_as_float(seq)));
+                    st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done) * p.ring_stride_f + 4 * ch,
+                                      make_float4(v[0], v[1], v[2], __uint_as_float(seq)));
                 }
                 __syncwarp();
                 if (tid == 0) {

@@ -57,7 +57,7 @@ struct TcLayerParams {
     int act;            // LL_ACT_*
     int out_f32;
     unsigned long long wait_ns;
-    unsigned long long *trace;  // optional: 8 globaltimer stamps per CTA (see kTcTrace*), or null
+    unsigned long long *trace;  // optional: kTcTraceSlots globaltimer stamps per CTA (see kTcTrace*), or null
 };
 
 // Trace stamps per CTA (CTA id = x + gridDim.x * (y + gridDim.y * z)).
@@ -69,7 +69,9 @@ enum {
     kTcTraceAccum = 4,     // epilogue: accumulator complete
     kTcTraceClusterA = 5,  // after the first cluster barrier
     kTcTraceClusterB = 6,  // after the partial rows were exchanged
-    kTcTraceEnd = 7        // rows written
+    kTcTraceEnd = 7,       // rows written
+    kTcTraceStaged = 8,    // split-K: partial tile staged in shared memory
+    kTcTraceSlots = 16
 };
 
 // ---- PTX wrappers used only by this kernel ----
@@ -192,6 +194,23 @@ __device__ __forceinline__ void tc_ld_32cols(uint32_t taddr, float (&v)[32])
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i)
+        v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 64 consecutive fp32 columns: two 32-column loads and one wait in a single
+// asm block, so no use of the registers can be scheduled before the wait.
+__device__ __forceinline__ void tc_ld_64cols(uint32_t taddr, float (&v)[64])
+{
+    uint32_t r[64];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%64];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%65];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr), "r"(taddr + 32u)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
         v[i] = __uint_as_float(r[i]);
 }
 
@@ -347,7 +366,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
     const uint32_t cta_lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
     auto stamp = [&](int k) {
         if (p.trace)
-            p.trace[cta_lin * 8u + (uint32_t)k] = globaltimer();
+            p.trace[cta_lin * (uint32_t)kTcTraceSlots + (uint32_t)k] = globaltimer();
     };
     if (tid == 0)
         stamp(kTcTraceEntry);
@@ -517,24 +536,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
         uint8_t *dst_row = (S > 1 && owner != (int)rank) ? smem + L::OFF_STAGE + (size_t)trow * L::RS
                                                          : smem + L::OFF_SLOT + (size_t)(rank * R + (trow - owner * R)) * L::RS;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-            float v[32];
-            tc_ld_32cols(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+            float v[64];
+            tc_ld_64cols(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
             if (S == 1) {
                 const int n = n0 + c0;
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
+                for (int i = 0; i < 64; ++i)
                     v[i] = tc_act(fmaf(v[i], s_scale[c0 + i], s_bias[c0 + i]), p.act);
                 const size_t off = (size_t)(m0 + trow) * p.N + n;
                 if (p.out_f32) {
                     float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + off);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
+                    for (int i = 0; i < 16; ++i)
                         dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                 } else {
                     uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.out) + off);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
+                    for (int i = 0; i < 8; ++i) {
                         uint32_t u[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
@@ -547,7 +566,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
             } else {
                 float4 *d4 = reinterpret_cast<float4 *>(dst_row + (size_t)c0 * 4);
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
+                for (int i = 0; i < 16; ++i)
                     d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             }
         }
@@ -557,6 +576,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
     if (S > 1) {
         __syncthreads();  // the staging tile is complete
         if (tid == 0) {
+            stamp(kTcTraceStaged);
             for (int o = 0; o < S; ++o) {
                 if (o == (int)rank)
                     continue;

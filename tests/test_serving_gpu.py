@@ -1,0 +1,80 @@
+"""Request ring on the tagged mailbox and the open-loop Poisson driver (need a B200).
+
+Outputs are checked against the oracle (fp32: 1e-5 norm-wise relative error)."""
+import time
+
+import numpy as np
+import pytest
+
+import low_latency_inference_gpu_b200 as ll
+import oracle
+from conftest import rel_err
+
+pytestmark = [pytest.mark.gpu, pytest.mark.timeout(300)]
+
+
+def opts(**kw):
+    o = ll.default_opts()
+    o.mailbox_format = 1
+    for k, v in kw.items():
+        setattr(o, k, v)
+    return o
+
+
+@pytest.fixture(scope="module")
+def cfg0():
+    net, Ws, bs = ll.config_params(0)
+    xs = ll.config_inputs(0, 64)
+    ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
+    return net, Ws, bs, xs, ref
+
+
+@pytest.mark.parametrize("variant", [1, 2])
+def test_ring_holds_several_requests_in_flight(cfg0, variant):
+    net, Ws, bs, xs, ref = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=4, kernel_variant=variant)) as e:
+        assert e.info().kernel_variant == variant
+        for base in range(0, 24, 4):
+            seqs = [e.submit(xs[base + i]) for i in range(4)]
+            with pytest.raises(ll.LLError) as busy:
+                e.submit(xs[0])
+            assert busy.value.code == ll.LL_ERR_BUSY
+            order = [0, 1, 2, 3] if base % 8 == 0 else [2, 0, 3, 1]  # replies may be collected in any order
+            for i in order:
+                y = e.poll(seqs[i])
+                assert rel_err(y[0], ref[base + i]) <= 1e-5
+        # single requests keep working after the ring has wrapped several times
+        for i in range(24, 40):
+            assert rel_err(e.infer(xs[i])[0], ref[i]) <= 1e-5
+        assert e.info().status == ll.LL_OK
+
+
+def test_ring_survives_idle_relaunch(cfg0):
+    net, Ws, bs, xs, ref = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=3, idle_timeout_ns=30_000_000)) as e:
+        n = 0
+        for rnd in range(3):
+            seqs = [e.submit(xs[n + i]) for i in range(2)]
+            for i, s in enumerate(seqs):
+                assert rel_err(e.poll(s)[0], ref[n + i]) <= 1e-5
+            n += 2
+            time.sleep(0.15)  # the kernel leaves after 30 ms idle; the next submit relaunches it
+        assert e.info().launches >= 3
+        for i in range(n, n + 5):
+            assert rel_err(e.infer(xs[i])[0], ref[i]) <= 1e-5
+
+
+def test_poisson_stream_is_split_across_ranks_and_fully_served(cfg0):
+    net, Ws, bs, xs, _ = cfg0
+    total = 3000
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=8)) as e:
+        lat0, el0 = e.serve_poisson(xs, total, 100_000.0, seed=5, rank=0, world=2)
+        lat1, el1 = e.serve_poisson(xs, total, 100_000.0, seed=5, rank=1, world=2)
+        lat, el = e.serve_poisson(xs, total, 100_000.0, seed=5)
+        assert e.info().status == ll.LL_OK
+    assert len(lat0) + len(lat1) == total and abs(len(lat0) - len(lat1)) < 300
+    assert len(lat) == total
+    for a in (lat0, lat1, lat):
+        assert np.all(np.isfinite(a)) and a.min() > 0.5 and np.median(a) < 1000
+    # 100k requests/s over 3000 requests is a 30 ms stream
+    assert 0.025 < el < 0.5
