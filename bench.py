@@ -26,6 +26,9 @@ Reported:
           the bf16 GELU 256->1024x4->64 MLP over rows 1..32 against HBM bandwidth
           (L2 flushed between forwards; kernel-only and end-to-end with pinned
           host copies).
+  serving open-loop Poisson arrivals at 50k / 200k / 1M requests/s aggregate over the
+          N GPUs (config-0 MLP on every GPU, 8-slot tagged request ring): p50/p99
+          latency from the scheduled arrival and sustained throughput.
   --impl reference  runs the reference's CPU forward on all host cores instead.
 """
 import argparse
@@ -59,6 +62,78 @@ def env_int(name, default):
         return int(os.environ.get(name, default))
     except ValueError:
         return default
+
+
+class HostGroup:
+    """Host-side collectives over a gloo group (a device-wide synchronize would wait for
+    the resident kernel, so ranks meet on the host).  world == 1: no-ops."""
+
+    def __init__(self, world, group=None):
+        self.world, self.group = world, group
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(group=self.group)
+
+    def max(self, v):
+        if self.world == 1:
+            return v
+        import torch
+        import torch.distributed as dist
+
+        t = torch.tensor([float(v)], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        return float(t.item())
+
+    def gather(self, v):
+        if self.world == 1:
+            return [v]
+        import torch.distributed as dist
+
+        out = [None] * self.world
+        dist.all_gather_object(out, v, group=self.group)
+        return out
+
+
+SERVING_RATES = (50_000.0, 200_000.0, 1_000_000.0)
+SERVING_SECONDS = 0.2
+
+
+def merge_serving(per_rank, rate, n_total):
+    """One line for one arrival rate from every rank's (latencies in us, elapsed s): latency
+    percentiles over the merged requests of all ranks (from the scheduled arrival),
+    sustained throughput = all requests served / the slowest rank's elapsed time."""
+    lat = np.concatenate([np.asarray(l, np.float64) for l, _ in per_rank]) if per_rank else np.array([])
+    served = int(lat.size)
+    elapsed = max(e for _, e in per_rank) if per_rank else float("nan")
+    q = np.percentile(lat, [50, 90, 99, 99.9]) if served else [float("nan")] * 4
+    return {"offered_per_s": rate, "requests": n_total, "served": served,
+            "sustained_per_s": served / elapsed if elapsed > 0 else float("nan"),
+            "p50_us": float(q[0]), "p90_us": float(q[1]), "p99_us": float(q[2]), "p999_us": float(q[3]),
+            "per_rank_served": [int(len(l)) for l, _ in per_rank]}
+
+
+def run_serving(ll, net, Ws, bs, xs, rank, world, hg, dev):
+    """Open-loop Poisson streams (seed 5) over all ranks: each rank serves the requests drawn
+    for it through its own engine (tagged mailbox, 8-slot ring); latency from the scheduled
+    arrival; merged on rank 0."""
+    o = ll.default_opts()
+    o.mailbox_format = 1
+    o.ring_slots = 8
+    out = []
+    with ll.Engine(net, Ws, bs, device=dev, opts=o) as e:
+        e.serve_poisson(xs, 2000, 50_000.0, seed=99, rank=rank, world=world)  # warm-up stream
+        for rate in SERVING_RATES:
+            n_total = int(rate * SERVING_SECONDS)
+            hg.barrier()
+            lat, el = e.serve_poisson(xs, n_total, rate, seed=5, rank=rank, world=world)
+            per_rank = hg.gather((lat.tolist(), el))
+            out.append(merge_serving(per_rank, rate, n_total))
+    return {"workload": "config-0 MLP replicated per GPU, Poisson arrivals (std::mt19937_64 seed 5), "
+                        "each request to a GPU drawn uniformly; U[-1,1] inputs",
+            "mailbox": "tagged, 8-slot request ring", "seconds_of_arrivals": SERVING_SECONDS, "rates": out}
 
 
 def measured_peak(key, fallback):
@@ -256,6 +331,7 @@ def main():
     ap.add_argument("--cpu-requests", type=int, default=100000, help="cpu_baseline sample (one core)")
     ap.add_argument("--no-compare", action="store_true", help="skip the cuBLAS / launch-per-layer comparison paths")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched tensor-core section")
+    ap.add_argument("--no-serving", action="store_true", help="skip the open-loop Poisson serving section")
     ap.add_argument("--only", default="all", choices=["all", "value", "batched"],
                     help="value: run only the device-queue phase (bounded launches; usable under ncu, which "
                          "serialises launches and so cannot drive the resident mailbox kernel); batched: only "
@@ -287,24 +363,8 @@ def main():
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", dev))
         host_group = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
-
-    def host_barrier():
-        if world > 1:
-            dist.barrier(group=host_group)
-
-    def host_max(v):
-        if world == 1:
-            return v
-        t = torch.tensor([float(v)], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=host_group)
-        return float(t.item())
-
-    def host_gather(v):
-        if world == 1:
-            return [v]
-        out = [None] * world
-        dist.all_gather_object(out, v, group=host_group)
-        return out
+    hg = HostGroup(world, host_group)
+    host_barrier, host_max, host_gather = hg.barrier, hg.max, hg.gather
 
     core = pin_host_thread(local_rank)
     R, K, W = args.requests, args.steps, args.warmup
@@ -412,6 +472,9 @@ def main():
                     lat, _ = m.bench(mode, xs, 10000)
                     s = ll.compute_stats(lat)
                     compare[f"{name}_{mname}"] = {"p50_us": s["p50"], "p99_us": s["p99"]}
+    serving = None
+    if full and not args.no_serving:
+        serving = run_serving(ll, net, Ws, bs, xs_all, rank, world, hg, dev)
     batched = None
     if world == 1 and full and not args.no_batched:
         batched = run_batched(ll, torch, dev)
@@ -479,6 +542,7 @@ def main():
                              "path is latency-bound, latency_floor is its relevant bound"},
         "cpu_baseline": cpu_baseline,
         "batched": batched,
+        "serving": serving,
         "clocks": clk,
         "gpu_launches": K + e2e_launches,
         "per_rank": per_rank,

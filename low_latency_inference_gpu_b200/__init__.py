@@ -677,6 +677,38 @@ class BatchedMLP:
         """Per-CTA phase stamps (see ll_batched_mlp_set_trace); d_trace_ptr = 0 turns tracing off."""
         _check(lib().ll_batched_mlp_set_trace(self.h, d_trace_ptr or None, n))
 
+    TRACE_PHASES = ("entry", "prev_layer_done", "first_stage", "mma_issued", "accumulated", "cluster_barrier",
+                    "exchanged", "end", "staged")
+
+    def phase_trace(self, x: np.ndarray, warm: int = 3) -> list:
+        """One traced forward of x (after `warm` untraced ones): per layer, the median over
+        its CTAs of each phase stamp in microseconds from the first CTA's entry into
+        layer 0, plus the last CTA's end (needs torch for the device buffers)."""
+        import torch
+
+        info = self.info()
+        n_layers, mx = len(info["ctas"]), max(info["ctas"])
+        tr = torch.zeros(n_layers * mx * 16, dtype=torch.int64, device="cuda")
+        dx = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+        dy = torch.empty((x.shape[0], self.out_dim), dtype=torch.float32, device="cuda")
+        st = torch.cuda.current_stream().cuda_stream
+        for _ in range(warm):
+            self.forward(dx.data_ptr(), dy.data_ptr(), x.shape[0], st)
+        self.set_trace(tr.data_ptr(), tr.numel())
+        self.forward(dx.data_ptr(), dy.data_ptr(), x.shape[0], st)
+        self.set_trace(0, 0)
+        self.check(st)
+        t = tr.cpu().numpy().reshape(n_layers, mx, 16).astype(np.float64)
+        t0 = min(t[l, :info["ctas"][l], 0].min() for l in range(n_layers))
+        out = []
+        for l in range(n_layers):
+            c = (t[l, :info["ctas"][l]] - t0) / 1000.0
+            row = {name: float(np.median(c[:, k])) for k, name in enumerate(self.TRACE_PHASES)
+                   if k != 8 or info["splits"][l] > 1}
+            row["end_max"] = float(c[:, 7].max())
+            out.append(row)
+        return out
+
     def close(self):
         if self.h:
             lib().ll_batched_mlp_destroy(self.h)

@@ -111,7 +111,7 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float4 v)
                  : "memory");
 }
 
-// ---- 1-D bulk copy global -> this CTA's shared memory (TMA engine, no multicast) ----
+// ---- 1-D bulk copy global -> this CTA's shared memory (TMA engine, this CTA only) ----
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
