@@ -269,10 +269,9 @@ __device__ uint32_t poll_mailbox(const KernelCtx &k, uint32_t last)
 
 // Tagged mailbox (format 1), warp 0 of the dispatcher: every lane loads up to
 // kTagChunksPerLane 16-byte x chunks {v0, v1, v2, tag} per poll; the request is
-// taken when every chunk carries the same new tag, and its floats go straight
-// into X -- detection and the x read are one PCIe round trip.  With a ring of
-// slots the new tag must be exactly the next sequence number (a slot's previous
-// lap holds an older one); a single slot accepts any tag other than the last.
+// taken when every chunk carries exactly the next sequence number, and its floats
+// go straight into X -- detection and the x read are one PCIe round trip.  (A
+// slot's previous lap, or an older snapshot, holds an older number.)
 constexpr int kTagChunksPerLane = 4;
 
 __device__ __forceinline__ uint32_t next_seq_dev(uint32_t s)
@@ -307,7 +306,7 @@ __device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uin
         for (int j = 0; j < kTagChunksPerLane; ++j)
             if (lane + 32 * j < nxc && c[j].w != tag)
                 same = false;
-        if (__all_sync(0xffffffffu, same) && (p.ring_slots > 1 ? tag == want : (tag != last && tag != 0))) {
+        if (__all_sync(0xffffffffu, same) && tag == want) {
 #pragma unroll
             for (int j = 0; j < kTagChunksPerLane; ++j) {
                 const int ch = lane + 32 * j;
