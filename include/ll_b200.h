@@ -431,6 +431,25 @@ uint32_t ll_next_seq(uint32_t seq);
 int ll_engine_serve_poisson(ll_engine *e, const float *xs, int n_x, int n_total, double rate_per_s, uint64_t seed,
                             int rank, int world, double *lat_us, int *n_served, double *elapsed_s);
 
+/*
+ * Weight files (no counterpart in the reference, which generates its weights in
+ * process with host_init, src/bench_cublas_mlp.cu:37-43): the net descriptor and
+ * its row-major weights (in the net's type), fp32 biases and int8 scales in one
+ * little-endian file ("LLWB" v1: 32-byte header, 16-byte layer records, 64-byte
+ * aligned sections, FNV-1a 64 checksum of the payload).  b may be NULL (no
+ * biases stored); scales are required for int8 nets.  ll_weights_load validates
+ * magic, version, dims, sizes and checksum (LL_ERR_BAD_DESC / LL_ERR_UNSUPPORTED);
+ * ll_weights_arrays fills n_layers pointers for ll_engine_create and friends,
+ * valid until ll_weights_free.
+ */
+typedef struct ll_weights ll_weights;
+int ll_weights_save(const char *path, const ll_net_desc *net, const void *const *W, const float *const *b,
+                    const float *const *scales);
+int ll_weights_load(const char *path, ll_weights **out);
+const ll_net_desc *ll_weights_net(const ll_weights *w);
+int ll_weights_arrays(const ll_weights *w, const void **W, const float **b, const float **scales);
+void ll_weights_free(ll_weights *w);
+
 /* Library version string. */
 const char *ll_version(void);
 

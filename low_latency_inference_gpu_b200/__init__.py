@@ -56,6 +56,7 @@ EXPORTED_SYMBOLS = [
     "ll_batched_opts_default", "ll_batched_plan", "ll_batched_mlp_create", "ll_batched_mlp_forward",
     "ll_batched_mlp_check", "ll_batched_mlp_infer", "ll_batched_mlp_info", "ll_batched_mlp_destroy",
     "ll_batched_mlp_set_trace", "ll_engine_serve_poisson",
+    "ll_weights_save", "ll_weights_load", "ll_weights_net", "ll_weights_arrays", "ll_weights_free",
 ]
 MAX_LAYERS = 24
 
@@ -199,6 +200,11 @@ def _sig(lib):
         "ll_batched_mlp_info": (ctypes.c_int, [_vp, P(BatchedInfo)]),
         "ll_batched_mlp_destroy": (ctypes.c_int, [_vp]),
         "ll_batched_mlp_set_trace": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t]),
+        "ll_weights_save": (ctypes.c_int, [ctypes.c_char_p, P(NetDesc), P(_vp), P(_fp), P(_fp)]),
+        "ll_weights_load": (ctypes.c_int, [ctypes.c_char_p, P(_vp)]),
+        "ll_weights_net": (P(NetDesc), [_vp]),
+        "ll_weights_arrays": (ctypes.c_int, [_vp, P(_vp), P(_fp), P(_fp)]),
+        "ll_weights_free": (None, [_vp]),
         "ll_engine_serve_poisson": (ctypes.c_int, [_vp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_double,
                                                    ctypes.c_uint64, ctypes.c_int, ctypes.c_int, _dp,
                                                    ctypes.POINTER(ctypes.c_int), _dp]),
@@ -725,3 +731,44 @@ class BatchedMLP:
             self.close()
         except Exception:
             pass
+
+
+# ---- weight files ----
+_W_DTYPE = {W_F32: np.float32, W_BF16: np.uint16, W_I8: np.int8}
+
+
+def save_weights(path: str, net: Net, W, b=None, scales=None):
+    """Write net + weights (in the net's type: fp32, bf16 bits as uint16, int8) + biases
+    + int8 scales to one file (see ll_weights_save)."""
+    d = net.desc()
+    keep = [np.ascontiguousarray(w, _W_DTYPE[net.wtype]) for w in W]
+    keepb = [np.ascontiguousarray(x, np.float32) for x in b] if b is not None else None
+    keeps = [np.ascontiguousarray(x, np.float32) for x in scales] if scales is not None else None
+    Wp = (_vp * net.n_layers)(*[w.ctypes.data for w in keep])
+    bp = (_fp * net.n_layers)(*[_f(x) for x in keepb]) if keepb is not None else None
+    sp = (_fp * net.n_layers)(*[_f(x) for x in keeps]) if keeps is not None else None
+    _check(lib().ll_weights_save(os.fsencode(path), ctypes.byref(d), Wp, bp, sp))
+
+
+def load_weights(path: str):
+    """(net, W, b, scales) from a weight file; b / scales are None when the file has none."""
+    h = ctypes.c_void_p()
+    _check(lib().ll_weights_load(os.fsencode(path), ctypes.byref(h)))
+    try:
+        nd = lib().ll_weights_net(h).contents
+        n = nd.n_layers
+        layers = [nd.layers[i] for i in range(n)]
+        wt = layers[0].wtype
+        net = Net([layers[0].in_dim] + [x.out_dim for x in layers], [x.act for x in layers], wt, nd.max_batch)
+        Wp, bp, sp = (_vp * n)(), (_fp * n)(), (_fp * n)()
+        _check(lib().ll_weights_arrays(h, Wp, bp, sp))
+        W, b, s = [], [], []
+        for l, x in enumerate(layers):
+            nel = x.out_dim * x.in_dim
+            buf = (ctypes.c_uint8 * (nel * np.dtype(_W_DTYPE[wt]).itemsize)).from_address(Wp[l])
+            W.append(np.frombuffer(buf, _W_DTYPE[wt]).reshape(x.out_dim, x.in_dim).copy())
+            b.append(np.ctypeslib.as_array(bp[l], (x.out_dim,)).copy() if bp[l] else None)
+            s.append(np.ctypeslib.as_array(sp[l], (x.out_dim,)).copy() if sp[l] else None)
+        return net, W, (b if all(v is not None for v in b) else None), (s if wt == W_I8 else None)
+    finally:
+        lib().ll_weights_free(h)
