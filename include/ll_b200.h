@@ -323,7 +323,8 @@ int ll_batched_mlp_info(ll_batched_mlp *m, ll_batched_info *info);
  * every CTA of layer l writes globaltimer stamps at d_trace[(l * max_ctas + cta) * 16 + k],
  * max_ctas = the largest ctas[] of ll_batched_mlp_info; k = 0 entry, 1 previous layer done,
  * 2 first stage landed, 3 last MMA issued, 4 accumulator complete, 5 cluster barrier,
- * 6 partial rows exchanged, 7 end, 8 partial tile staged (split-K only). */
+ * 6 partial rows exchanged, 7 end, 8 partial tile staged (split-K only), 9..12 K steps 0..3 ready
+ * for the MMA, 13 first stage re-issued, 14 that stage ready, 15 K step 0 converted (int8). */
 int ll_batched_mlp_set_trace(ll_batched_mlp *m, unsigned long long *d_trace, size_t n);
 int ll_batched_mlp_destroy(ll_batched_mlp *m);
 

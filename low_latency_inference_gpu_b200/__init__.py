@@ -684,7 +684,8 @@ class BatchedMLP:
         _check(lib().ll_batched_mlp_set_trace(self.h, d_trace_ptr or None, n))
 
     TRACE_PHASES = ("entry", "prev_layer_done", "first_stage", "mma_issued", "accumulated", "cluster_barrier",
-                    "exchanged", "end", "staged")
+                    "exchanged", "end", "staged", "k0_ready", "k1_ready", "k2_ready", "k3_ready", "reissue",
+                    "reissue_ready", "k0_converted")
 
     def phase_trace(self, x: np.ndarray, warm: int = 3) -> list:
         """One traced forward of x (after `warm` untraced ones): per layer, the median over
@@ -710,7 +711,7 @@ class BatchedMLP:
         for l in range(n_layers):
             c = (t[l, :info["ctas"][l]] - t0) / 1000.0
             row = {name: float(np.median(c[:, k])) for k, name in enumerate(self.TRACE_PHASES)
-                   if k != 8 or info["splits"][l] > 1}
+                   if (k != 8 or info["splits"][l] > 1) and np.all(c[:, k] > -1e6)}
             row["end_max"] = float(c[:, 7].max())
             out.append(row)
         return out

@@ -71,6 +71,10 @@ enum {
     kTcTraceClusterB = 6,  // after the partial rows were exchanged
     kTcTraceEnd = 7,       // rows written
     kTcTraceStaged = 8,    // split-K: partial tile staged in shared memory
+    kTcTraceStageReady = 9,   // 9..12: MMA thread, K steps 0..3 ready (landed and converted)
+    kTcTraceReissue = 13,     // producer: first stage re-issued (after the MMAs freed it)
+    kTcTraceReissueReady = 14,// MMA thread: that re-issued stage ready
+    kTcTraceConvDone = 15,    // converter warp: K step 0 converted
     kTcTraceSlots = 16
 };
 
@@ -435,6 +439,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
                 const int s = kb % STAGES;
                 if (kb >= STAGES && !tc_wait(b_empty(s), ((kb / STAGES) - 1) & 1, p.wait_ns, fail, p.status, 1))
                     break;
+                if (kb == STAGES)
+                    stamp(kTcTraceReissue);
                 const int kx = k0 + kb * kTcK;
                 if (kb >= npre) {  // weight tiles past the prefetched ones
                     if (WINT8) {
@@ -464,6 +470,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
                     break;
                 if (kb == 0)
                     stamp(kTcTraceFirstData);
+                if (kb < 4)
+                    stamp(kTcTraceStageReady + kb);
+                if (kb == STAGES)
+                    stamp(kTcTraceReissueReady);
                 tc_fence_after();
                 const uint32_t xa = sbase + L::OFF_X + s * L::XB, wa = sbase + L::OFF_W + s * L::WB;
 #pragma unroll
@@ -497,6 +507,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
             __syncwarp();
             if (lane == 0)
                 mbar_arrive_local(b_conv(s));
+            if (kb == 0 && tid == kTcConvWarp0 * 32)
+                stamp(kTcTraceConvDone);
         }
     }
 
