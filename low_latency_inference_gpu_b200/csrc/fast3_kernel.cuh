@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
     __shared__ __align__(16) float h1[H1];
     __shared__ __align__(16) float h2[S::R2];
     __shared__ __align__(16) float gath[C * OUT];
+    __shared__ __align__(16) float yo[3 * ((OUT + 2) / 3) + 4];  // the output row, zero-padded
     __shared__ __align__(16) float bias[S::NB];
     __shared__ __align__(16) Shared sh;
     __shared__ __align__(16) Params sp;
@@ -109,6 +110,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
         bias[i] = __ldg(img + (size_t)S::NW * kThreads + i);
     for (int i = tid; i < C * OUT; i += kThreads)
         gath[i] = 0.0f;
+    for (int i = tid; i < 3 * ((OUT + 2) / 3) + 4; i += kThreads)
+        yo[i] = 0.0f;
     __syncthreads();
     cluster_sync();
     if (leader && tid == 0)
@@ -261,34 +264,31 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             if (tid == 0)
                 trace(k, n_done, 12);
             if (warp == 0) {
-                float v = 0.f;
+                // the output row goes through shared memory: lanes < OUT finish one output
+                // each, then the storing lanes pick up their 16-byte groups (full-warp
+                // shuffles here cost ~1650 cycles in this loop, the shared-memory round ~60)
                 if (lane < OUT) {
+                    float v = 0.f;
 #pragma unroll
                     for (int c = 0; c < C; ++c)
                         v += gath[c * OUT + lane];
-                    v = relu_or(v + bias[H1 + S::R2 + lane], act3);
+                    yo[lane] = relu_or(v + bias[H1 + S::R2 + lane], act3);
                 }
-                // lanes 0..OUT/4-1 gather four neighbours and store 16 bytes
-                const float v1 = __shfl_down_sync(0xffffffffu, v, 1);
-                const float v2 = __shfl_down_sync(0xffffffffu, v, 2);
-                const float v3 = __shfl_down_sync(0xffffffffu, v, 3);
-                const float4 q = make_float4(v, v1, v2, v3);
+                __syncwarp();
                 const bool tagged = p.mode == MODE_MAILBOX && p.mailbox_format == 1;
                 // tagged output: lane c packs {y[3c], y[3c+1], y[3c+2], seq}
                 constexpr int NYC = (OUT + 2) / 3;
-                const float t0 = __shfl_sync(0xffffffffu, v, (3 * lane) & 31);
-                const float t1 = __shfl_sync(0xffffffffu, v, (3 * lane + 1) & 31);
-                const float t2 = __shfl_sync(0xffffffffu, v, (3 * lane + 2) & 31);
                 if (tagged) {
                     if (lane < NYC)
                         st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done) * p.ring_stride_f + 4 * lane,
-                                          make_float4(t0, 3 * lane + 1 < OUT ? t1 : 0.f, 3 * lane + 2 < OUT ? t2 : 0.f,
+                                          make_float4(yo[3 * lane], yo[3 * lane + 1], yo[3 * lane + 2],
                                                       __uint_as_float(seq)));
-                } else if ((lane & 3) == 0 && lane < OUT) {
+                } else if (lane < OUT / 4) {
+                    const float4 q = reinterpret_cast<const float4 *>(yo)[lane];
                     if (p.mode == MODE_QUEUE)
-                        reinterpret_cast<float4 *>(p.q_y + (size_t)n_done * OUT)[lane >> 2] = q;
+                        reinterpret_cast<float4 *>(p.q_y + (size_t)n_done * OUT)[lane] = q;
                     else
-                        st_relaxed_sys_v4(p.mb_y + lane, q);
+                        st_relaxed_sys_v4(p.mb_y + 4 * lane, q);
                 }
                 __syncwarp();
                 if (lane == 0) {

@@ -65,7 +65,7 @@ def test_config0_parity_oracle_and_golden(golden):
     with engine_for(net, Ws, bs) as e:
         ys = np.stack([e.infer(xs[i])[0] for i in range(64)])
         info = e.info()
-    assert info.kernel_variant == 2 and info.cluster_size == 4  # register-resident kernel by default
+    assert info.kernel_variant == 2 and info.cluster_size == 8  # register-resident kernel by default
     ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
     assert rel_err(ys, ref) <= 1e-5
     gy = unbits(g["y"]).reshape(g["n"], -1)
