@@ -50,11 +50,11 @@ WORKLOAD = "config-0 MLP 64->256->256->16 fp32 (ReLU, identity out), batch 1, se
 WEIGHT_BYTES = (64 * 256 + 256 * 256 + 256 * 16) * 4 + (256 + 256 + 16) * 4  # resident weights + biases
 IO_BYTES = 64 * 4 + 16 * 4
 FALLBACK_HBM_GBS = 6650.0
-# DRAM traffic of one device-queue launch, from the committed ncu capture
-# (profiles/ll_fast3_kernel_config0_queue_full.md: 1.080 MB for 2000 requests):
-# the weights once, then ~367 B per request (input row, output, stamp); scaled to R requests.
-TRAFFIC_FIXED_BYTES = 345_000
-TRAFFIC_PER_REQUEST_BYTES = 367
+# DRAM traffic of one device-queue launch of the 8-CTA register-resident kernel, from
+# the committed ncu capture (1.352 MB for 2000 requests): the eight per-CTA register
+# images once (812 KB), then ~270 B per request (input row, stamp); scaled to R requests.
+TRAFFIC_FIXED_BYTES = 812_500
+TRAFFIC_PER_REQUEST_BYTES = 270
 
 
 def env_int(name, default):
