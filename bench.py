@@ -192,6 +192,19 @@ def run_batched(ll, torch, dev, iters=30):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak, "peak_kind": tf_kind,
                          "unit": "TFLOP/s", "frac": achieved / tf_peak,
                          "algorithmic": f"{flops / 1e9:.2f} GFLOP per forward (2 x 256 rows x {net.n_params} weights)"}}
+    # the same net with 8 batches of 256 rows in one forward (2048 rows): the per-layer costs
+    # (dependency, first loads, tails) are shared, so this is the path's throughput
+    stacked = ll.Net(net.dims, net.acts, net.wtype, 2048)
+    with ll.BatchedMLP(stacked, Wd, bd, sd, device=dev) as m:
+        ms, e2e = timed(m, 2048, 3)
+        flops = 2.0 * 2048 * net.n_params
+        achieved = flops / (ms * 1e-3) / 1e12
+        out["int8_mlp_1024x2048x6x256_8x256rows_stacked"] = {
+            "ms_per_forward": ms, "us_per_256_rows": ms * 1e3 / 8, "e2e_ms_per_forward": e2e,
+            "rows_per_s": 2048e3 / ms, "tiling": m.info(),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak, "peak_kind": tf_kind,
+                         "unit": "TFLOP/s", "frac": achieved / tf_peak,
+                         "algorithmic": f"{flops / 1e9:.2f} GFLOP per forward (2 x 2048 rows x {net.n_params} weights)"}}
     # bf16 weights, GELU, batch sweep 1..32
     net, Ws, bs = ll.config_params(2)
     Wd, bd, sd = ll.device_weights(net, Ws, bs)

@@ -104,13 +104,6 @@ __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v
     asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float4 v)
-{
-    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "f"(v.x), "f"(v.y),
-                 "f"(v.z), "f"(v.w)
-                 : "memory");
-}
-
 // ---- 1-D bulk copy global -> this CTA's shared memory (TMA engine, this CTA only) ----
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar)
 {
