@@ -290,17 +290,22 @@ typedef struct {
     int32_t bn;          /* output channels per CTA tile: 0 = auto, 64, 128 or 256 */
     int32_t splits;      /* K splits per tile (= cluster size): 0 = auto, else a power of two <= 16 dividing in_dim/64 */
     int32_t pdl;         /* 1 = chain layers with programmatic dependent launch (default) */
-    int32_t reserved0;
+    int32_t kernel;      /* 0 = auto; 1 = split-K tiles (128 rows x bn, K split over a cluster);
+                            2 = weights-in-TMEM tiles (128 channels x 256 rows, whole K; the weights
+                            go global -> registers -> tensor memory as the MMA's A operand, only the
+                            rows pass through shared memory).  Auto takes 2 for a layer with >= 96
+                            such tiles (stacked batches), else 1. */
     uint64_t wait_ns;    /* bound on every device-side wait; 0 = 1 s */
     int32_t reserved[4];
 } ll_batched_opts;
 typedef struct {
     int32_t n_layers;
-    int32_t rows_pad;    /* max_batch rounded up to 128 */
+    int32_t rows_pad;    /* max_batch rounded up to 256 */
     int32_t bn[LL_MAX_LAYERS];
     int32_t splits[LL_MAX_LAYERS];
     int32_t ctas[LL_MAX_LAYERS];       /* at max_batch rows */
     int32_t smem_bytes[LL_MAX_LAYERS];
+    int32_t kind[LL_MAX_LAYERS];       /* 1 split-K tiles, 2 weights-in-TMEM tiles */
 } ll_batched_info;
 void ll_batched_opts_default(ll_batched_opts *opts);
 /* Host-only tiling estimate (no GPU needed): the most CTAs up to one per SM.  ll_batched_mlp_create

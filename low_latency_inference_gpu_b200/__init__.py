@@ -121,12 +121,13 @@ class Plan(ctypes.Structure):
 
 class BatchedOpts(ctypes.Structure):
     _fields_ = [("bn", ctypes.c_int32), ("splits", ctypes.c_int32), ("pdl", ctypes.c_int32),
-                ("reserved0", ctypes.c_int32), ("wait_ns", ctypes.c_uint64), ("reserved", ctypes.c_int32 * 4)]
+                ("kernel", ctypes.c_int32), ("wait_ns", ctypes.c_uint64), ("reserved", ctypes.c_int32 * 4)]
 
 
 class BatchedInfo(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int32), ("rows_pad", ctypes.c_int32), ("bn", ctypes.c_int32 * 24),
-                ("splits", ctypes.c_int32 * 24), ("ctas", ctypes.c_int32 * 24), ("smem_bytes", ctypes.c_int32 * 24)]
+                ("splits", ctypes.c_int32 * 24), ("ctas", ctypes.c_int32 * 24), ("smem_bytes", ctypes.c_int32 * 24),
+                ("kind", ctypes.c_int32 * 24)]
 
 
 LAYER_MODE_NAMES = {0: "replicated", 1: "rowsplit_allgather", 2: "rowsplit_local", 3: "ksplit_gather",
@@ -622,17 +623,20 @@ def mlp_forward_noalloc(net: Net, d_W_ptrs, d_b_ptrs, d_x_ptr: int, d_y_ptr: int
 
 
 # ---- batched dense path (tensor cores) ----
-def batched_opts(bn: int = 0, splits: int = 0, pdl: int = 1, wait_ns: int = 0) -> BatchedOpts:
+KERNEL_SPLITK, KERNEL_WEIGHTS_IN_TMEM = 1, 2
+
+
+def batched_opts(bn: int = 0, splits: int = 0, pdl: int = 1, wait_ns: int = 0, kernel: int = 0) -> BatchedOpts:
     o = BatchedOpts()
     lib().ll_batched_opts_default(ctypes.byref(o))
-    o.bn, o.splits, o.pdl, o.wait_ns = bn, splits, pdl, wait_ns
+    o.bn, o.splits, o.pdl, o.wait_ns, o.kernel = bn, splits, pdl, wait_ns, kernel
     return o
 
 
 def _batched_info_dict(info: BatchedInfo) -> dict:
     n = info.n_layers
     return {"rows_pad": info.rows_pad, "bn": list(info.bn[:n]), "splits": list(info.splits[:n]),
-            "ctas": list(info.ctas[:n]), "smem_bytes": list(info.smem_bytes[:n])}
+            "ctas": list(info.ctas[:n]), "smem_bytes": list(info.smem_bytes[:n]), "kind": list(info.kind[:n])}
 
 
 def batched_plan(net: Net, opts: Optional[BatchedOpts] = None) -> dict:

@@ -14,6 +14,7 @@
 
 #include "common.h"
 #include "tc_layer.cuh"
+#include "tc_swap.cuh"
 
 using namespace llk;
 
@@ -21,12 +22,28 @@ namespace {
 
 constexpr int kMaxSplitCTAs = 148;  // one CTA per SM
 
+enum { kKindSplitK = 1, kKindWeightsInTmem = 2 };
+
 struct LayerRun {
+    int kind = kKindSplitK;
     int bn = 256, splits = 1, ctas = 0, smem = 0;
     int K = 0, N = 0, act = 0, out_f32 = 0;
     const void *kfn = nullptr;
+    const void *w = nullptr;  // device weights (weights-in-TMEM kernel)
     TcLayerParams p{};
 };
+
+// Weights-in-TMEM tiles (128 channels x 256 rows, K whole) for a layer when there are
+// enough of them to fill most of the GPU; otherwise the split-K tiles.  The rule uses
+// shapes only, so the host-side plan and the device agree.
+int layer_kind(int N, int rows_pad, const ll_batched_opts *o)
+{
+    if (o && o->kernel)
+        return (o->kernel == kKindWeightsInTmem && N % kSwChan == 0 && rows_pad % kSwRows == 0) ? kKindWeightsInTmem
+                                                                                                : kKindSplitK;
+    const int tiles = (N % kSwChan == 0 && rows_pad % kSwRows == 0) ? (N / kSwChan) * (rows_pad / kSwRows) : 0;
+    return tiles >= 96 ? kKindWeightsInTmem : kKindSplitK;
+}
 
 template <int BN, bool I8>
 constexpr int stages_for()
@@ -77,9 +94,9 @@ int split_at_most(int n, int cap)
 // Tile width and split count of one layer: the most CTAs up to one per SM, each
 // with at least two 64-deep K steps; ties go to the wider tile (fewer X re-reads).
 // The splits of a tile run as one cluster, so a split count is a power of two <= 16.
-void plan_layer(int K, int N, int rows_pad, bool i8, const ll_batched_opts *o, int &bn, int &splits)
+void plan_layer(int K, int N, int rows, bool i8, const ll_batched_opts *o, int &bn, int &splits)
 {
-    const int mt = rows_pad / kTcRows;
+    const int mt = (rows + kTcRows - 1) / kTcRows;
     int best_bn = 0, best_s = 1, best_ctas = -1;
     for (int cand : {256, 128, 64}) {
         if (N % cand != 0 || (o && o->bn && o->bn != cand))
@@ -142,7 +159,7 @@ int validate(const ll_net_desc *net, const ll_batched_opts *o)
         }
     }
     if (o && ((o->bn != 0 && o->bn != 64 && o->bn != 128 && o->bn != 256) || o->splits < 0 || o->splits > 16 ||
-              (o->splits & (o->splits - 1)) != 0)) {
+              (o->splits & (o->splits - 1)) != 0 || o->kernel < 0 || o->kernel > 2)) {
         llh::set_error("batched opts: bn must be 0/64/128/256 and splits 0 (auto) or a power of two <= 16");
         return LL_ERR_INVALID_ARG;
     }
@@ -170,17 +187,25 @@ int validate(const ll_net_desc *net, const ll_batched_opts *o)
 void fill_info(const ll_net_desc *net, const ll_batched_opts *o, ll_batched_info *info)
 {
     std::memset(info, 0, sizeof(*info));
-    const int rows_pad = (int)llh::round_up((size_t)net->max_batch, kTcRows);
+    const int rows_pad = (int)llh::round_up((size_t)net->max_batch, kSwRows);
     info->n_layers = net->n_layers;
     info->rows_pad = rows_pad;
     const bool i8 = net->layers[0].wtype == LL_W_I8;
     for (int l = 0; l < net->n_layers; ++l) {
         int bn, s, smem;
-        plan_layer(net->layers[l].in_dim, net->layers[l].out_dim, rows_pad, i8, o, bn, s);
+        info->kind[l] = layer_kind(net->layers[l].out_dim, rows_pad, o);
+        if (info->kind[l] == kKindWeightsInTmem) {
+            info->bn[l] = kSwChan;
+            info->splits[l] = 1;
+            info->ctas[l] = (net->layers[l].out_dim / kSwChan) * (rows_pad / kSwRows);
+            info->smem_bytes[l] = TcSwapSmem::ALLOC;
+            continue;
+        }
+        plan_layer(net->layers[l].in_dim, net->layers[l].out_dim, net->max_batch, i8, o, bn, s);
         pick_kernel(bn, i8, smem);
         info->bn[l] = bn;
         info->splits[l] = s;
-        info->ctas[l] = (net->layers[l].out_dim / bn) * (rows_pad / kTcRows) * s;
+        info->ctas[l] = (net->layers[l].out_dim / bn) * ((net->max_batch + kTcRows - 1) / kTcRows) * s;
         info->smem_bytes[l] = smem;
     }
 }
@@ -249,9 +274,9 @@ int max_active_clusters(const void *kfn, int smem, int S)
 // the layer is resident at once (one wave; the occupancy query knows how many
 // clusters of S CTAs the GPCs can hold), each split at least two 64-deep K steps.
 // Ties go to the wider tile.  Forced options are taken as given.
-bool choose_tiling(int K, int N, int rows_pad, bool i8, const ll_batched_opts *o, LayerRun &r)
+bool choose_tiling(int K, int N, int rows, bool i8, const ll_batched_opts *o, LayerRun &r)
 {
-    const int mt = rows_pad / kTcRows;
+    const int mt = (rows + kTcRows - 1) / kTcRows;
     int best = -1;
     for (int bn : {256, 128, 64}) {
         if (N % bn != 0 || (o && o->bn && o->bn != bn))
@@ -448,12 +473,23 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
         r.N = d.out_dim;
         r.act = d.act;
         r.out_f32 = (l + 1 == net->n_layers);
-        if (!choose_tiling(d.in_dim, d.out_dim, m->rows_pad, i8, opts, r)) {
+        r.kind = info.kind[l];
+        r.w = m->d_w[l];
+        if (r.kind == kKindWeightsInTmem) {
+            r.bn = kSwChan;
+            r.splits = 1;
+            r.ctas = info.ctas[l];
+            r.smem = TcSwapSmem::ALLOC;
+            r.kfn = i8 ? reinterpret_cast<const void *>(&ll_tc_swap_kernel<true>)
+                       : reinterpret_cast<const void *>(&ll_tc_swap_kernel<false>);
+            LLB_TRY(cudaFuncSetAttribute(r.kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, r.smem));
+        } else if (!choose_tiling(d.in_dim, d.out_dim, m->max_rows, i8, opts, r)) {
             llh::set_error("layer %d: no tile / cluster shape can be scheduled on this device", l);
             return fail(LL_ERR_BAD_DESC);
         }
         TcLayerParams &p = r.p;
-        if (!make_map(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->act[l & 1], d.in_dim, m->rows_pad, kTcRows,
+        const int x_box = r.kind == kKindWeightsInTmem ? kSwRows : kTcRows;
+        if (!make_map(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->act[l & 1], d.in_dim, m->rows_pad, x_box,
                       true) ||
             !make_map(&p.tm_w, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, i8 ? 1 : 2,
                       m->d_w[l], d.in_dim, d.out_dim, r.bn, !i8)) {
@@ -492,10 +528,13 @@ int ll_batched_mlp_forward(ll_batched_mlp *m, const float *d_x, float *d_y, int 
     to_bf16_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 1184), 256, 0, st>>>(d_x, m->act[0], n);
     LL_CUDA_TRY(cudaGetLastError());
     const int mt = (n_rows + kTcRows - 1) / kTcRows;
+    const int mt_sw = (n_rows + kSwRows - 1) / kSwRows;
     for (LayerRun &r : m->runs) {
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(r.N / r.bn), (unsigned)mt, (unsigned)r.splits);
-        cfg.blockDim = dim3(kTcThreads, 1, 1);
+        const bool sw = r.kind == kKindWeightsInTmem;
+        cfg.gridDim = sw ? dim3((unsigned)(r.N / kSwChan), (unsigned)mt_sw, 1u)
+                         : dim3((unsigned)(r.N / r.bn), (unsigned)mt, (unsigned)r.splits);
+        cfg.blockDim = dim3(sw ? kSwThreads : kTcThreads, 1, 1);
         cfg.dynamicSmemBytes = (size_t)r.smem;
         cfg.stream = st;
         cudaLaunchAttribute attr[2];
@@ -507,8 +546,10 @@ int ll_batched_mlp_forward(ll_batched_mlp *m, const float *d_x, float *d_y, int 
         attr[1].val.clusterDim.z = (unsigned)r.splits;
         cfg.attrs = attr;
         cfg.numAttrs = 2;
+        const uint8_t *wp = static_cast<const uint8_t *>(r.w);
+        void *args_sw[] = {&r.p, &wp};
         void *args[] = {&r.p};
-        LL_CUDA_TRY(cudaLaunchKernelExC(&cfg, r.kfn, args));
+        LL_CUDA_TRY(cudaLaunchKernelExC(&cfg, r.kfn, sw ? args_sw : args));
     }
     // the last layer wrote [rows_pad x out] fp32; hand the caller its n_rows
     LL_CUDA_TRY(cudaMemcpyAsync(d_y, m->out_pad, sizeof(float) * (size_t)n_rows * m->out_dim,
@@ -588,6 +629,7 @@ int ll_batched_mlp_info(ll_batched_mlp *m, ll_batched_info *info)
     info->n_layers = m->n_layers;
     info->rows_pad = m->rows_pad;
     for (int l = 0; l < m->n_layers; ++l) {
+        info->kind[l] = m->runs[l].kind;
         info->bn[l] = m->runs[l].bn;
         info->splits[l] = m->runs[l].splits;
         info->ctas[l] = m->runs[l].ctas;

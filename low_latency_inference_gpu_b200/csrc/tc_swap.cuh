@@ -1,0 +1,301 @@
+// Batched dense layer for many rows (stacked batches): weights as the MMA's A
+// operand in tensor memory, rows as N.
+//
+//   D[128 channels x 256 rows] = W[n0:n0+128, :] . X[m0:m0+256, :]^T     (fp32, TMEM)
+//   Y[row][channel] = act(D * scale[channel] + bias[channel])
+//
+// Per 64-deep K step the SM moves only X through shared memory (TMA, 128-byte
+// swizzle, read once by the MMA as the B operand): the weight tile goes global ->
+// registers -> (int8: exact bf16 conversion) -> tensor memory with tcgen05.st,
+// where tcgen05.mma reads it as A.  That halves the shared-memory traffic of the
+// split-K layer kernel (tc_layer.cuh), whose int8 operand conversion made shared
+// memory the bound.  K is not split: one CTA owns a 128 x 256 output tile.
+// Roles (256 threads): warp 0 TMA for X; warp 1 TMEM allocation + the MMA thread;
+// warps 4..7 load/convert/store the weight stages to their TMEM lane quarter and
+// run the epilogue for the same lanes (= channels).  Every wait is bounded.
+#pragma once
+#include "tc_layer.cuh"
+
+namespace llk {
+
+constexpr int kSwRows = 256;      // rows per tile (MMA N)
+constexpr int kSwChan = 128;      // channels per tile (MMA M)
+constexpr int kSwThreads = 256;
+constexpr int kSwXStages = 5;     // X ring in shared memory (32 KB each)
+constexpr int kSwAStages = 4;     // weight stages in TMEM (32 columns each)
+constexpr int kSwPrefetch = 4;    // weight stages held in registers ahead of use
+constexpr uint32_t kSwTmemCols = 512;  // D: columns [0, 256); A stages: [256, 384)
+
+struct TcSwapSmem {
+    static constexpr int XB = kSwRows * kTcK * 2;  // 32 KB
+    static constexpr int OFF_X = 0;
+    static constexpr int OFF_BAR = kSwXStages * XB;  // xfull[S], xempty[S], afull[A], aempty[A], accf
+    static constexpr int N_BAR = 2 * kSwXStages + 2 * kSwAStages + 1;
+    static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;  // tmem base, fail flag
+    static constexpr int OFF_BIAS = OFF_MISC + 16;        // bias[128], scale[128]
+    static constexpr int BYTES = OFF_BIAS + 8 * kSwChan;
+    static constexpr int ALLOC = BYTES + 1024;
+    static_assert(XB % 1024 == 0, "1024-byte aligned tiles");
+    static_assert(ALLOC <= 227 * 1024, "shared memory");
+};
+
+// Store 32 consecutive 32-bit TMEM columns of this warp's 32 lanes (one row each).
+__device__ __forceinline__ void tc_st_32cols(uint32_t taddr, const uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// One weight row's 64-deep K slice as packed bf16 pairs (low half = even k).
+template <bool WINT8>
+struct WSlice {
+    static constexpr int NV = WINT8 ? 4 : 8;  // 16-byte loads per slice
+    uint4 v[NV];
+    __device__ __forceinline__ void load(const uint8_t *row, int k0)
+    {
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+            v[i] = ld_nc_v4(row + (size_t)k0 * (WINT8 ? 1 : 2) + 16 * i);
+    }
+    __device__ __forceinline__ void pack(uint32_t (&o)[32]) const
+    {
+        if constexpr (WINT8) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                uint32_t t[8];
+                i8x16_to_bf16(v[i], t);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    o[8 * i + j] = t[j];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                o[4 * i] = v[i].x;
+                o[4 * i + 1] = v[i].y;
+                o[4 * i + 2] = v[i].z;
+                o[4 * i + 3] = v[i].w;
+            }
+        }
+    }
+};
+
+template <bool WINT8>
+__global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_constant__ TcLayerParams p,
+                                                                    const uint8_t *__restrict__ wbase)
+{
+    using L = TcSwapSmem;
+    extern __shared__ uint8_t sw_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sw_smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint32_t *misc = reinterpret_cast<uint32_t *>(smem + L::OFF_MISC);
+    volatile uint32_t *fail = misc + 1;
+    float *s_bias = reinterpret_cast<float *>(smem + L::OFF_BIAS);
+    float *s_scale = s_bias + kSwChan;
+    auto bar = [&](int i) { return sbase + (uint32_t)L::OFF_BAR + 8u * (uint32_t)i; };
+    auto b_xfull = [&](int s) { return bar(s); };
+    auto b_xempty = [&](int s) { return bar(kSwXStages + s); };
+    auto b_afull = [&](int s) { return bar(2 * kSwXStages + s); };
+    auto b_aempty = [&](int s) { return bar(2 * kSwXStages + kSwAStages + s); };
+    const uint32_t b_accf = bar(2 * kSwXStages + 2 * kSwAStages);
+
+    const uint32_t cta_lin = blockIdx.x + gridDim.x * blockIdx.y;
+    auto stamp = [&](int k) {
+        if (p.trace)
+            p.trace[cta_lin * (uint32_t)kTcTraceSlots + (uint32_t)k] = globaltimer();
+    };
+    if (tid == 0)
+        stamp(kTcTraceEntry);
+    const int n0 = blockIdx.x * kSwChan;   // first channel
+    const int m0 = blockIdx.y * kSwRows;   // first row
+    const int nk = p.K / kTcK;
+
+    if (tid == 0) {
+        for (int s = 0; s < kSwXStages; ++s) {
+            mbar_init(b_xfull(s), 1);
+            mbar_init(b_xempty(s), 1);
+        }
+        for (int s = 0; s < kSwAStages; ++s) {
+            mbar_init(b_afull(s), 4);  // one arrive per converter warp
+            mbar_init(b_aempty(s), 1);
+        }
+        mbar_init(b_accf, 1);
+        misc[1] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        prefetch_tmap(&p.tm_x);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         sbase + (uint32_t)L::OFF_MISC),
+                     "r"(kSwTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = misc[0];
+    griddep_launch_dependents();
+
+    const bool conv = warp >= 4;
+    const int q = warp & 3;
+    const int chan = 32 * q + lane;  // this thread's TMEM lane = output channel within the tile
+    const uint8_t *wrow = wbase + (size_t)(n0 + chan) * p.K * (WINT8 ? 1 : 2);
+    WSlice<WINT8> pre[kSwPrefetch];
+    if (conv) {
+        // weights, biases and scales do not depend on the previous layer
+#pragma unroll
+        for (int i = 0; i < kSwPrefetch; ++i)
+            if (i < nk)
+                pre[i].load(wrow, i * kTcK);
+        if (q == 0) {
+            for (int i = lane; i < kSwChan; i += 32) {
+                s_bias[i] = __ldg(p.bias + n0 + i);
+                s_scale[i] = p.scale ? __ldg(p.scale + n0 + i) : 1.0f;
+            }
+        }
+    }
+    griddep_wait();  // X belongs to the previous layer (and Y to the one before it) until here
+    if (tid == 0)
+        stamp(kTcTraceDepDone);
+
+    if (warp == 0) {
+        // ---------------- TMA producer: X tiles ----------------
+        if (lane == 0) {
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % kSwXStages;
+                if (kb >= kSwXStages &&
+                    !tc_wait(b_xempty(s), ((kb / kSwXStages) - 1) & 1, p.wait_ns, fail, p.status, 1))
+                    break;
+                mbar_arrive_expect_tx(b_xfull(s), L::XB);
+                tma_load_2d(sbase + L::OFF_X + s * L::XB, &p.tm_x, kb * kTcK, m0, b_xfull(s));
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc_idesc_bf16(kSwRows);  // M = 128 channels, N = 256 rows
+            bool ok = true;
+            for (int kb = 0; kb < nk && ok; ++kb) {
+                const int s = kb % kSwXStages, sa = kb % kSwAStages;
+                ok = tc_wait(b_xfull(s), (kb / kSwXStages) & 1, p.wait_ns, fail, p.status, 2) &&
+                     tc_wait(b_afull(sa), (kb / kSwAStages) & 1, p.wait_ns, fail, p.status, 2);
+                if (!ok)
+                    break;
+                if (kb == 0)
+                    stamp(kTcTraceFirstData);
+                if (kb < 4)
+                    stamp(kTcTraceStageReady + kb);
+                tc_fence_after();
+                const uint32_t xa = sbase + L::OFF_X + s * L::XB;
+                const uint32_t aa = tmem + 256u + (uint32_t)sa * 32u;
+#pragma unroll
+                for (int kk = 0; kk < kTcK / 16; ++kk)
+                    tc_mma_bf16_ts(tmem, aa + (uint32_t)kk * 8u, sw128_kmajor_desc(xa + kk * 32), idesc,
+                                   (kb | kk) != 0);
+                tc_commit(b_xempty(s));   // X stage free when these MMAs complete
+                tc_commit(b_aempty(sa));  // and the weight stage in TMEM
+            }
+            stamp(kTcTraceMmaIssued);
+            tc_commit(b_accf);
+        }
+    } else if (conv) {
+        // ---------------- weights: registers -> bf16 -> TMEM (lanes of quarter q) ----------------
+        for (int kb = 0; kb < nk; ++kb) {
+            const int sa = kb % kSwAStages;
+            if (kb >= kSwAStages &&
+                !tc_wait_warp(b_aempty(sa), ((kb / kSwAStages) - 1) & 1, p.wait_ns, fail, p.status, 3))
+                break;
+            uint32_t o[32];
+            pre[0].pack(o);
+#pragma unroll
+            for (int i = 0; i + 1 < kSwPrefetch; ++i)
+                pre[i] = pre[i + 1];
+            if (kb + kSwPrefetch < nk)
+                pre[kSwPrefetch - 1].load(wrow, (kb + kSwPrefetch) * kTcK);
+            tc_st_32cols(tmem + ((uint32_t)(32 * q) << 16) + 256u + (uint32_t)sa * 32u, o);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive_local(b_afull(sa));
+            if (kb == 0 && lane == 0 && q == 0)
+                stamp(kTcTraceConvDone);
+        }
+    }
+
+    // ---------------- epilogue: warps 4..7, lane = channel, columns = rows ----------------
+    if (conv) {
+        tc_wait_warp(b_accf, 0, p.wait_ns, fail, p.status, 4);
+        tc_fence_after();
+        if (tid == 128)
+            stamp(kTcTraceAccum);
+    }
+    __syncthreads();  // every role is done; bias and scale are in shared memory
+    const bool go = *fail == 0u;
+    if (conv && go) {
+        const float sc = s_scale[chan], bi = s_bias[chan];
+        const int n = n0 + chan;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kSwRows; c0 += 64) {
+            float v[64];
+            tc_ld_64cols(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                const float y = tc_act(fmaf(v[i], sc, bi), p.act);
+                const size_t off = (size_t)(m0 + c0 + i) * p.N + n;  // 32 consecutive channels per warp store
+                if (p.out_f32)
+                    static_cast<float *>(p.out)[off] = y;
+                else
+                    static_cast<__nv_bfloat16 *>(p.out)[off] = __float2bfloat16_rn(y);
+            }
+        }
+    }
+
+    // ---------------- drain and free ----------------
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0)
+        stamp(kTcTraceEnd);
+    if (warp == 1) {
+        if (*fail && lane == 0) {
+            const uint64_t t0 = globaltimer();
+            while (!mbar_try_wait(b_accf, 0) && globaltimer() - t0 < p.wait_ns) {
+            }
+        }
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kSwTmemCols)
+                     : "memory");
+    }
+}
+
+}  // namespace llk

@@ -103,3 +103,30 @@ def test_without_programmatic_launch_matches():
     xs = ll.config_inputs(2, 32)
     with make(net, Ws, bs) as a, make(net, Ws, bs, pdl=0) as b:
         assert np.array_equal(run_device(a, xs), run_device(b, xs))
+
+
+@pytest.mark.parametrize("wtype", [ll.W_BF16, ll.W_I8])
+def test_weights_in_tmem_tiles_small_net(wtype):
+    # 256 -> 384 -> 256, 512 rows, forced onto the weights-in-TMEM kernel (A operand in TMEM)
+    net = ll.mlp([256, 384, 256], ll.ACT_RELU, ll.ACT_IDENTITY, wtype, 512)
+    Ws, bs = params(net, 21)
+    xs = ll.fill_uniform(512 * 256, -1.0, 1.0, 22).reshape(512, 256)
+    with make(net, Ws, bs, kernel=2) as m:
+        assert m.info()["kind"] == [2, 2]
+        y = run_device(m, xs)
+        y300 = run_device(m, xs[:300])  # a ragged row count: the second row block is partial
+    ref = oracle_out(net, Ws, bs, xs)
+    assert rel_err(y, ref) <= TOL[wtype]
+    assert np.array_equal(y300, y[:300])
+
+
+def test_config3_stacked_batches_auto():
+    net = ll.config_net(3, 2048)
+    Ws, bs = ll.config_params(3)[1:]
+    xs = ll.config_inputs(3, 2048)
+    with make(net, Ws, bs) as m:
+        assert m.info()["kind"][:7] == [2] * 7
+        y = run_device(m, xs)
+    check = np.r_[0:8, 1020:1030, 2040:2048]
+    ref = oracle_out(net, Ws, bs, xs[check])
+    assert rel_err(y[check], ref) <= TOL[ll.W_I8]

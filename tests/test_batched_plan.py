@@ -18,7 +18,7 @@ def test_config3_fills_the_gpu():
 def test_config2_batch_sweep_plans():
     for rows in (1, 2, 4, 8, 16, 32):
         p = ll.batched_plan(ll.config_net(2, rows))
-        assert p["rows_pad"] == 128
+        assert p["rows_pad"] == 256 and p["kind"] == [1] * 6  # split-K tiles for small batches
         assert all(1 <= c <= 148 for c in p["ctas"])
 
 
@@ -40,3 +40,13 @@ def test_unsupported_nets_are_rejected(dims, wtype):
     with pytest.raises(ll.LLError) as e:
         ll.batched_plan(net)
     assert e.value.code == ll.LL_ERR_BAD_DESC
+
+
+def test_stacked_batches_use_weights_in_tmem_tiles():
+    p = ll.batched_plan(ll.config_net(3, 2048))
+    # 16 channel tiles x 8 row blocks of 256 for every 2048-wide layer; the 256-wide last
+    # layer has only 16 such tiles and keeps the split-K kernel
+    assert p["kind"] == [2] * 7 + [1]
+    assert p["ctas"][:7] == [128] * 7 and p["splits"][:7] == [1] * 7
+    forced = ll.batched_plan(ll.config_net(3, 256), ll.batched_opts(kernel=2))
+    assert forced["kind"] == [2] * 8
