@@ -21,9 +21,14 @@ namespace llk {
 constexpr int kSwRows = 256;      // rows per tile (MMA N)
 constexpr int kSwChan = 128;      // channels per tile (MMA M)
 constexpr int kSwThreads = 256;
-constexpr int kSwXStages = 5;     // X ring in shared memory (32 KB each)
+constexpr int kSwXStages = 6;     // X ring in shared memory (32 KB each); even: each producer owns fixed stages
 constexpr int kSwAStages = 4;     // weight stages in TMEM (32 columns each)
-constexpr int kSwPrefetch = 4;    // weight stages held in registers ahead of use
+// weight stages held in registers ahead of use: int8 slices are 4 x 16 B, bf16 8 x 16 B
+template <bool WINT8>
+constexpr int sw_prefetch()
+{
+    return WINT8 ? 8 : 4;
+}
 constexpr uint32_t kSwTmemCols = 512;  // D: columns [0, 256); A stages: [256, 384)
 
 struct TcSwapSmem {
@@ -169,6 +174,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     const int q = warp & 3;
     const int chan = 32 * q + lane;  // this thread's TMEM lane = output channel within the tile
     const uint8_t *wrow = wbase + (size_t)(n0 + chan) * p.K * (WINT8 ? 1 : 2);
+    constexpr int kSwPrefetch = sw_prefetch<WINT8>();
     WSlice<WINT8> pre[kSwPrefetch];
     if (conv) {
         // weights, biases and scales do not depend on the previous layer
@@ -187,10 +193,12 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     if (tid == 0)
         stamp(kTcTraceDepDone);
 
-    if (warp == 0) {
-        // ---------------- TMA producer: X tiles ----------------
+    if (warp == 0 || warp == 2) {
+        // ---------------- TMA producers: X tiles, even K steps from warp 0, odd from warp 2 ----------------
+        // (a thread issuing back-to-back tensor loads holds each for hundreds of cycles;
+        // two issuers raise the SM's TMA throughput ~1.6x)
         if (lane == 0) {
-            for (int kb = 0; kb < nk; ++kb) {
+            for (int kb = warp >> 1; kb < nk; kb += 2) {
                 const int s = kb % kSwXStages;
                 if (kb >= kSwXStages &&
                     !tc_wait(b_xempty(s), ((kb / kSwXStages) - 1) & 1, p.wait_ns, fail, p.status, 1))
