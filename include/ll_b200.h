@@ -293,8 +293,14 @@ typedef struct {
     int32_t kernel;      /* 0 = auto; 1 = split-K tiles (128 rows x bn, K split over a cluster);
                             2 = weights-in-TMEM tiles (128 channels x 256 rows, whole K; the weights
                             go global -> registers -> tensor memory as the MMA's A operand, only the
-                            rows pass through shared memory).  Auto takes 2 for a layer with >= 96
-                            such tiles (stacked batches), else 1. */
+                            rows pass through shared memory);
+                            3 = small-batch matrix-by-vector (max_batch <= 32): the whole forward
+                            is ONE cooperative launch, one CTA per SM; each CTA holds its row slice
+                            of every layer's weights in shared memory and the layers hand off
+                            through L2 behind a grid-wide layer barrier (bounded waits).
+                            Auto takes 3 when max_batch <= 32 and the slices fit (and bn / splits
+                            are not forced), else per layer 2 for >= 96 weights-in-TMEM tiles
+                            (stacked batches) and 1 otherwise. */
     uint64_t wait_ns;    /* bound on every device-side wait; 0 = 1 s */
     int32_t reserved[4];
 } ll_batched_opts;
@@ -305,7 +311,8 @@ typedef struct {
     int32_t splits[LL_MAX_LAYERS];
     int32_t ctas[LL_MAX_LAYERS];       /* at max_batch rows */
     int32_t smem_bytes[LL_MAX_LAYERS];
-    int32_t kind[LL_MAX_LAYERS];       /* 1 split-K tiles, 2 weights-in-TMEM tiles */
+    int32_t kind[LL_MAX_LAYERS];       /* 1 split-K tiles, 2 weights-in-TMEM tiles, 3 small-batch
+                                          (then bn = output channels per CTA, ctas = SMs) */
 } ll_batched_info;
 void ll_batched_opts_default(ll_batched_opts *opts);
 /* Host-only tiling estimate (no GPU needed): the most CTAs up to one per SM.  ll_batched_mlp_create
@@ -315,8 +322,9 @@ int ll_batched_plan(const ll_net_desc *net, const ll_batched_opts *opts, ll_batc
 int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const float *const *b,
                           const float *const *scales, int device, const ll_batched_opts *opts,
                           ll_batched_mlp **out);
-/* Enqueue one forward on `stream` (device pointers; x [n_rows x in], y [n_rows x out], fp32).
- * Returns launch errors only; ll_batched_mlp_check reports device-side ones. */
+/* Enqueue one forward on `stream` (device pointers; x [n_rows x in], y [n_rows x out], fp32;
+ * x 16-byte aligned).  Returns launch errors only; ll_batched_mlp_check reports device-side
+ * ones.  Forwards of one object run one after another on one stream. */
 int ll_batched_mlp_forward(ll_batched_mlp *m, const float *d_x, float *d_y, int n_rows, void *stream);
 /* Synchronise `stream` and read the device status word: LL_OK, or LL_ERR_DEVICE_FAULT when a
  * bounded wait ran out (the workspace is then cleared so the next forward starts clean). */

@@ -623,7 +623,7 @@ def mlp_forward_noalloc(net: Net, d_W_ptrs, d_b_ptrs, d_x_ptr: int, d_y_ptr: int
 
 
 # ---- batched dense path (tensor cores) ----
-KERNEL_SPLITK, KERNEL_WEIGHTS_IN_TMEM = 1, 2
+KERNEL_SPLITK, KERNEL_WEIGHTS_IN_TMEM, KERNEL_GEMV = 1, 2, 3
 
 
 def batched_opts(bn: int = 0, splits: int = 0, pdl: int = 1, wait_ns: int = 0, kernel: int = 0) -> BatchedOpts:

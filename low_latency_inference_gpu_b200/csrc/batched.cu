@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "common.h"
+#include "gemv_net.cuh"
 #include "tc_layer.cuh"
 #include "tc_swap.cuh"
 
@@ -22,7 +23,10 @@ namespace {
 
 constexpr int kMaxSplitCTAs = 148;  // one CTA per SM
 
-enum { kKindSplitK = 1, kKindWeightsInTmem = 2 };
+enum { kKindSplitK = 1, kKindWeightsInTmem = 2, kKindGemv = 3 };
+
+constexpr int kGvPlanCtas = 148;                   // SMs assumed by the host-only plan (B200)
+constexpr size_t kGvSmemLimit = 232448 - 1024;     // dynamic shared memory per CTA, static part aside
 
 struct LayerRun {
     int kind = kKindSplitK;
@@ -43,6 +47,72 @@ int layer_kind(int N, int rows_pad, const ll_batched_opts *o)
                                                                                                 : kKindSplitK;
     const int tiles = (N % kSwChan == 0 && rows_pad % kSwRows == 0) ? (N / kSwChan) * (rows_pad / kSwRows) : 0;
     return tiles >= 96 ? kKindWeightsInTmem : kKindSplitK;
+}
+
+// Shared-memory layout of the small-batch kernel for G CTAs: the per-CTA image
+// (biases and scales of every layer's slice, then each layer's weight slice of
+// ceil(N/G) rows), the per-warp partial sums, two mbarriers, then the staged input
+// rows (fp32, largest in_dim + 4 floats apart).
+struct GemvLayout {
+    int rmax[LL_MAX_LAYERS] = {};
+    uint32_t woff[LL_MAX_LAYERS] = {}, boff[LL_MAX_LAYERS] = {};
+    uint32_t img_bytes = 0, img_a_bytes = 0;
+    uint32_t off_part = 0, off_bar = 0, off_x = 0;
+    int xstride = 0;
+    size_t smem(int bp) const { return off_x + (size_t)bp * (size_t)xstride * sizeof(float); }
+};
+
+int gemv_bp(int rows)
+{
+    return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : rows <= 8 ? 8 : rows <= 16 ? 16 : 32;
+}
+
+void gemv_layout(const ll_net_desc *net, int G, GemvLayout &g)
+{
+    const bool i8 = net->layers[0].wtype == LL_W_I8;
+    size_t fl = 0;
+    int kmax = 0;
+    for (int l = 0; l < net->n_layers; ++l) {
+        g.rmax[l] = (net->layers[l].out_dim + G - 1) / G;
+        g.boff[l] = (uint32_t)fl;
+        fl += (size_t)g.rmax[l] * (i8 ? 2 : 1);
+        kmax = std::max(kmax, net->layers[l].in_dim);
+    }
+    size_t off = llh::round_up(fl * sizeof(float), 16);
+    for (int l = 0; l < net->n_layers; ++l) {
+        g.woff[l] = (uint32_t)std::min<size_t>(off, 1u << 30);
+        off += llh::round_up((size_t)g.rmax[l] * net->layers[l].in_dim * (i8 ? 1 : 2), 16);
+        if (l == 0)
+            g.img_a_bytes = (uint32_t)std::min<size_t>(off, 1u << 30);
+    }
+    g.img_bytes = (uint32_t)std::min<size_t>(off, 1u << 30);
+    off = llh::round_up(off, 128);
+    g.off_part = (uint32_t)std::min<size_t>(off, 1u << 30);
+    off += (size_t)kGvWarps * kGvRowGroup * kGvMaxRows * sizeof(float);
+    g.off_bar = (uint32_t)std::min<size_t>(off, 1u << 30);
+    off += 16;  // two mbarriers: image copy A (biases + layer 0) and B (the other layers)
+    g.off_x = (uint32_t)std::min<size_t>(llh::round_up(off, 128), 1u << 30);
+    g.xstride = kmax + 4;
+}
+
+// The small-batch kernel takes nets of <= 32 rows whose slices and staged rows fit one SM.
+bool gemv_fits(const ll_net_desc *net, int G)
+{
+    if (net->max_batch > kGvMaxRows)
+        return false;
+    GemvLayout g;
+    gemv_layout(net, G, g);
+    return g.smem(gemv_bp(net->max_batch)) <= kGvSmemLimit;
+}
+
+// kKindGemv for the whole net (auto for <= 32 rows when it fits, or forced), else 0.
+int net_kind(const ll_net_desc *net, const ll_batched_opts *o, int G)
+{
+    const int forced = o ? o->kernel : 0;
+    const bool tiles_forced = o && (o->bn || o->splits);
+    if (forced == kKindGemv || (forced == 0 && !tiles_forced && gemv_fits(net, G)))
+        return kKindGemv;
+    return 0;
 }
 
 template <int BN, bool I8>
@@ -159,8 +229,14 @@ int validate(const ll_net_desc *net, const ll_batched_opts *o)
         }
     }
     if (o && ((o->bn != 0 && o->bn != 64 && o->bn != 128 && o->bn != 256) || o->splits < 0 || o->splits > 16 ||
-              (o->splits & (o->splits - 1)) != 0 || o->kernel < 0 || o->kernel > 2)) {
-        llh::set_error("batched opts: bn must be 0/64/128/256 and splits 0 (auto) or a power of two <= 16");
+              (o->splits & (o->splits - 1)) != 0 || o->kernel < 0 || o->kernel > kKindGemv)) {
+        llh::set_error("batched opts: bn must be 0/64/128/256, splits 0 (auto) or a power of two <= 16, kernel 0..3");
+        return LL_ERR_INVALID_ARG;
+    }
+    if (o && o->kernel == kKindGemv && !gemv_fits(net, kGvPlanCtas)) {
+        llh::set_error("batched opts: the small-batch kernel takes <= %d rows whose weight slices and staged "
+                       "rows fit one SM's shared memory",
+                       kGvMaxRows);
         return LL_ERR_INVALID_ARG;
     }
     if (o && o->splits > 0) {
@@ -184,13 +260,25 @@ int validate(const ll_net_desc *net, const ll_batched_opts *o)
     return LL_OK;
 }
 
-void fill_info(const ll_net_desc *net, const ll_batched_opts *o, ll_batched_info *info)
+void fill_info(const ll_net_desc *net, const ll_batched_opts *o, ll_batched_info *info, int G = kGvPlanCtas)
 {
     std::memset(info, 0, sizeof(*info));
     const int rows_pad = (int)llh::round_up((size_t)net->max_batch, kSwRows);
     info->n_layers = net->n_layers;
     info->rows_pad = rows_pad;
     const bool i8 = net->layers[0].wtype == LL_W_I8;
+    if (net_kind(net, o, G) == kKindGemv) {
+        GemvLayout g;
+        gemv_layout(net, G, g);
+        for (int l = 0; l < net->n_layers; ++l) {
+            info->kind[l] = kKindGemv;
+            info->bn[l] = g.rmax[l];  // output channels per CTA
+            info->splits[l] = 1;
+            info->ctas[l] = G;
+            info->smem_bytes[l] = (int)g.smem(gemv_bp(net->max_batch));
+        }
+        return;
+    }
     for (int l = 0; l < net->n_layers; ++l) {
         int bn, s, smem;
         info->kind[l] = layer_kind(net->layers[l].out_dim, rows_pad, o);
@@ -336,6 +424,18 @@ struct ll_batched_mlp {
     cudaStream_t own = nullptr;  // non-blocking stream for ll_batched_mlp_infer
     int pdl = 1;
     unsigned long long wait_ns = 1000ull * 1000 * 1000;
+    // small-batch kernel (kKindGemv): one cooperative launch per forward
+    bool gemv = false;
+    int sms = 0;
+    GemvLayout gl;
+    GemvNetParams gp{};
+    const void *gv_kfn[6] = {};   // by batch rows 1, 2, 4, 8, 16, 32
+    uint32_t *hand[2] = {};       // hand-off words [32][widest layer]
+    uint8_t *img = nullptr;       // per-CTA shared-memory images (biases, scales, weight slices)
+    size_t hand_bytes = 0;
+    uint32_t tag_next = 1;        // tag of the next tagged forward's layer 0
+    unsigned *cnt = nullptr;      // arrival counters of the counted hand-off
+    unsigned epoch = 0;           // counted forwards since the counters were cleared
 };
 
 namespace {
@@ -355,6 +455,10 @@ void destroy_all(ll_batched_mlp *m)
     cudaFree(m->act[1]);
     cudaFree(m->out_pad);
     cudaFree(m->status);
+    cudaFree(m->hand[0]);
+    cudaFree(m->cnt);
+    cudaFree(m->img);
+    cudaFree(m->hand[1]);
     if (m->own)
         cudaStreamDestroy(m->own);
     delete m;
@@ -403,8 +507,14 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
         llh::set_error("cuTensorMapEncodeTiled is not available from the driver");
         return LL_ERR_CUDA;
     }
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms < 1) {
+        cudaGetLastError();
+        llh::set_error("device %d: cannot read the SM count", device);
+        return LL_ERR_CUDA;
+    }
     ll_batched_info info;
-    fill_info(net, opts, &info);
+    fill_info(net, opts, &info, sms);
 
     auto *m = new ll_batched_mlp();
     m->device = device;
@@ -417,6 +527,8 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
     m->pdl = opts ? opts->pdl : 1;
     if (opts && opts->wait_ns)
         m->wait_ns = opts->wait_ns;
+    m->sms = sms;
+    m->gemv = info.kind[0] == kKindGemv;
     auto fail = [&](int code) {
         destroy_all(m);
         return code;
@@ -462,6 +574,111 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
     LLB_TRY(cudaMalloc(&m->out_pad, sizeof(float) * (size_t)m->rows_pad * m->out_dim));
     LLB_TRY(cudaMalloc(&m->status, sizeof(unsigned)));
     LLB_TRY(cudaMemset(m->status, 0, sizeof(unsigned)));
+
+    if (m->gemv) {
+        gemv_layout(net, sms, m->gl);
+        const size_t need = m->gl.smem(gemv_bp(m->max_rows));
+        if (need > kGvSmemLimit) {
+            llh::set_error("small-batch kernel: %zu bytes of shared memory per SM needed", need);
+            return fail(LL_ERR_BAD_DESC);
+        }
+        m->hand_bytes = sizeof(uint32_t) * kGvTagRows * (size_t)max_w;
+        for (int i = 0; i < 2; ++i) {
+            LLB_TRY(cudaMalloc(&m->hand[i], m->hand_bytes));
+            LLB_TRY(cudaMemset(m->hand[i], 0, m->hand_bytes));  // tag 0: never written
+        }
+        LLB_TRY(cudaMalloc(&m->cnt, sizeof(unsigned) * kGvCntStride * (size_t)net->n_layers));
+        LLB_TRY(cudaMemset(m->cnt, 0, sizeof(unsigned) * kGvCntStride * (size_t)net->n_layers));
+        // per-CTA images: the CTA's bias (+ scale) slices and weight slices, laid out
+        // exactly as the front of its shared memory, so two bulk copies load them
+        std::vector<uint8_t> img((size_t)sms * m->gl.img_bytes, 0);
+        const size_t es = i8 ? 1 : 2;
+        for (int c = 0; c < sms; ++c) {
+            uint8_t *base = img.data() + (size_t)c * m->gl.img_bytes;
+            for (int l = 0; l < net->n_layers; ++l) {
+                const int K = net->layers[l].in_dim, N = net->layers[l].out_dim;
+                const int r0 = (int)((unsigned)c * (unsigned)N / (unsigned)sms);
+                const int R = (int)((unsigned)(c + 1) * (unsigned)N / (unsigned)sms) - r0;
+                float *bd = reinterpret_cast<float *>(base) + m->gl.boff[l];
+                for (int i = 0; i < R; ++i) {
+                    bd[i] = (b && b[l]) ? b[l][r0 + i] : 0.0f;
+                    if (i8)
+                        bd[m->gl.rmax[l] + i] = scales[l][r0 + i];
+                }
+                std::memcpy(base + m->gl.woff[l], static_cast<const uint8_t *>(W[l]) + (size_t)r0 * K * es,
+                            (size_t)R * K * es);
+            }
+        }
+        LLB_TRY(cudaMalloc(&m->img, img.size()));
+        LLB_TRY(cudaMemcpy(m->img, img.data(), img.size(), cudaMemcpyHostToDevice));
+        GemvNetParams &g = m->gp;
+        std::memset(&g, 0, sizeof(g));
+        g.img = m->img;
+        g.img_bytes = m->gl.img_bytes;
+        g.img_a_bytes = m->gl.img_a_bytes;
+        for (int l = 0; l < net->n_layers; ++l) {
+            g.dims[l] = net->layers[l].in_dim;
+            g.acts[l] = net->layers[l].act;
+            g.rmax[l] = m->gl.rmax[l];
+            g.woff[l] = m->gl.woff[l];
+            g.boff[l] = m->gl.boff[l];
+        }
+        g.dims[net->n_layers] = m->out_dim;
+        g.n_layers = net->n_layers;
+        g.xstride = m->gl.xstride;
+        g.off_part = m->gl.off_part;
+        g.off_bar = m->gl.off_bar;
+        g.off_x = m->gl.off_x;
+        g.hand[0] = m->hand[0];
+        g.hand[1] = m->hand[1];
+        g.act[0] = m->act[0];
+        g.act[1] = m->act[1];
+        g.cnt = m->cnt;
+        g.status = m->status;
+        g.wait_ns = m->wait_ns;
+        const void *k8[6] = {reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 1, 1>),
+                             reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 1, 2>),
+                             reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 1, 4>),
+                             reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 2, 4>),
+                             reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 4, 4>),
+                             reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 8, 4>)};
+        const void *k16[6] = {reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 1, 1>),
+                              reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 1, 2>),
+                              reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 1, 4>),
+                              reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 2, 4>),
+                              reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 4, 4>),
+                              reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 8, 4>)};
+        const int top = 31 - __builtin_clz((unsigned)gemv_bp(m->max_rows));
+        for (int i = 0; i <= top; ++i) {  // the variants of up to max_batch rows
+            m->gv_kfn[i] = i8 ? k8[i] : k16[i];
+            LLB_TRY(cudaFuncSetAttribute(m->gv_kfn[i], cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)m->gl.smem(1 << i)));
+        }
+        int per_sm = 0;
+        LLB_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, m->gv_kfn[top], kGvThreads,
+                                                              m->gl.smem(gemv_bp(m->max_rows))));
+        if (per_sm < 1) {
+            llh::set_error("small-batch kernel: a CTA does not fit one SM");
+            return fail(LL_ERR_BAD_DESC);
+        }
+        for (int l = 0; l < net->n_layers; ++l) {
+            LayerRun r;
+            r.kind = kKindGemv;
+            r.bn = info.bn[l];
+            r.splits = 1;
+            r.ctas = sms;
+            r.smem = info.smem_bytes[l];
+            r.K = net->layers[l].in_dim;
+            r.N = net->layers[l].out_dim;
+            r.act = net->layers[l].act;
+            r.out_f32 = (l + 1 == net->n_layers);
+            r.w = m->d_w[l];
+            m->runs.push_back(r);
+        }
+        m->max_ctas = sms;
+        *out = m;
+        return LL_OK;
+    }
 
     for (int l = 0; l < net->n_layers; ++l) {
         const ll_layer_desc &d = net->layers[l];
@@ -524,6 +741,44 @@ int ll_batched_mlp_forward(ll_batched_mlp *m, const float *d_x, float *d_y, int 
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     LL_CUDA_TRY(cudaSetDevice(m->device));
+    if (m->gemv) {
+        if (reinterpret_cast<uintptr_t>(d_x) % 16 != 0) {
+            llh::set_error("batched forward: x must be 16-byte aligned");
+            return LL_ERR_INVALID_ARG;
+        }
+        const int bp = gemv_bp(n_rows);
+        const int idx = 31 - __builtin_clz((unsigned)bp);
+        const bool tagged = bp <= kGvTagRows;
+        if (tagged && m->tag_next + (uint32_t)m->n_layers > kGvTagLimit) {
+            // the 16-bit tags would wrap: clear the words so no stale one can match again
+            for (int i = 0; i < 2; ++i)
+                LL_CUDA_TRY(cudaMemsetAsync(m->hand[i], 0, m->hand_bytes, st));
+            m->tag_next = 1;
+        }
+        GemvNetParams g = m->gp;
+        g.n_rows = n_rows;
+        g.x = d_x;
+        g.y = d_y;
+        g.tag_base = m->tag_next;
+        g.epoch = m->epoch + 1u;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)m->sms, 1, 1);
+        cfg.blockDim = dim3(kGvThreads, 1, 1);
+        cfg.dynamicSmemBytes = m->gl.smem(bp);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the layer barrier needs all of them
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        void *args[] = {&g};
+        LL_CUDA_TRY(cudaLaunchKernelExC(&cfg, m->gv_kfn[idx], args));
+        if (tagged)  // advanced only once the launch is in the stream
+            m->tag_next += (uint32_t)m->n_layers;
+        else
+            m->epoch = g.epoch;
+        return LL_OK;
+    }
     const size_t n = (size_t)n_rows * m->in_dim;
     to_bf16_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 1184), 256, 0, st>>>(d_x, m->act[0], n);
     LL_CUDA_TRY(cudaGetLastError());
@@ -569,6 +824,13 @@ int ll_batched_mlp_check(ll_batched_mlp *m, void *stream)
     LL_CUDA_TRY(cudaStreamSynchronize(st));
     if (s) {
         cudaMemsetAsync(m->status, 0, sizeof(unsigned), st);
+        if (m->gemv) {  // the failed forward left part of its words or counts: start over
+            for (int i = 0; i < 2; ++i)
+                cudaMemsetAsync(m->hand[i], 0, m->hand_bytes, st);
+            cudaMemsetAsync(m->cnt, 0, sizeof(unsigned) * kGvCntStride * (size_t)m->n_layers, st);
+            m->tag_next = 1;
+            m->epoch = 0;
+        }
         cudaStreamSynchronize(st);
         llh::set_error("batched forward: a device wait ran out (status 0x%x, role %u)", s, (s >> 8) & 0xffu);
         return LL_ERR_DEVICE_FAULT;
@@ -616,8 +878,10 @@ int ll_batched_mlp_set_trace(ll_batched_mlp *m, unsigned long long *d_trace, siz
         llh::set_error("trace buffer needs %zu entries", per_layer * m->runs.size());
         return LL_ERR_INVALID_ARG;
     }
-    for (size_t l = 0; l < m->runs.size(); ++l)
+    for (size_t l = 0; l < m->runs.size(); ++l) {
         m->runs[l].p.trace = d_trace ? d_trace + l * per_layer : nullptr;
+        m->gp.trace[l] = m->runs[l].p.trace;
+    }
     return LL_OK;
 }
 

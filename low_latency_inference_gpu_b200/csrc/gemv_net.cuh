@@ -1,0 +1,487 @@
+// Small-batch MLP forward (1..32 rows) as ONE cooperative launch over every SM:
+// matrix-by-vector per layer with a grid-wide layer barrier, for the batch sweep
+// of bf16 / int8 nets whose rows are too few for the tensor-core tiles.
+//
+// Mapping (one CTA per SM, G CTAs):
+//   * layer l's output channels are split into G contiguous row slices; CTA c owns
+//     rows [c*N/G, (c+1)*N/G).  At entry the CTA bulk-copies its slice of EVERY
+//     layer's weights, with its biases and scales, into shared memory from a
+//     per-CTA image packed at create time: two copies (biases + layer 0, then the
+//     other layers), since each bulk copy costs its issuing thread ~0.3 us.
+//     Weights do not depend on activations, so the whole net streams from HBM at
+//     once while layer 0 runs, and no weight byte is read twice;
+//   * layers hand off through L2, by one of two protocols chosen by batch size:
+//     - up to 4 rows (latency-bound): self-validating words.  A hidden output is
+//       one 32-bit word {bf16 value in the high half, 16-bit tag in the low half},
+//       tag = (forward, layer) number, written with a relaxed store and no fence;
+//       a consumer polls the words it needs (16-byte loads, several in flight,
+//       stale ones re-read together, bounded) until every tag is the expected one.
+//       A 32-bit access is single-copy atomic, so a matching tag vouches for its
+//       value: the layer barrier costs one L2 trip instead of a release fence, a
+//       counter and a second read.  The host clears the words before the 16-bit
+//       tags wrap, so a stale word never carries a current tag;
+//     - 8 rows and more (volume-bound: every CTA reads rows x in_dim values):
+//       plain bf16 outputs (half the bytes) and an arrival counter per layer; a
+//       producer adds 1 with release semantics after its stores, a consumer's
+//       thread 0 waits (acquire, bounded) for all producers and the CTA then reads
+//       the rows once with L2-coherent loads, all in flight;
+//     every CTA reads the same rows, so each starts at its own offset to spread the
+//     reads over the L2 slices;
+//   * inside a CTA the 8 warps split K; a lane owns one K chunk (16 weight bytes)
+//     and BPL batch rows at a time (lane = k-lane * BG + batch group, rows
+//     b = bg + BG*i), weight chunks are broadcast reads, the K lanes reduce with
+//     shuffles and the warps through shared memory; the epilogue applies the
+//     int8 scale, the bias and the activation and rounds hidden outputs to bf16.
+// Every wait is bounded by wait_ns; a CTA that gives up records the failing
+// layer in the status word, lets its own bulk copies land and returns, so the
+// others time out too and the host reads the error (no trap, no endless spin).
+//
+// Reference: the per-layer contract y = act(W x + b) over row-major W is
+// cpu_gemv_bias_relu (src/bench_persistent_mbyv_mlp.cu:50-67); the grid-wide
+// layer barrier replaces the reference's global-atomic layer barrier of the
+// persistent MByV kernel (src/bench_persistent_mbyv_mlp.cu:308-377).
+#pragma once
+#include <cuda_bf16.h>
+
+#include <cstdint>
+
+#include "ll_b200.h"
+#include "ptx.cuh"
+
+namespace llk {
+
+constexpr int kGvThreads = 256;
+constexpr int kGvWarps = kGvThreads / 32;
+constexpr int kGvRowGroup = 8;   // output rows per pass (accumulators per lane: 8 x BPL)
+constexpr int kGvMaxRows = 32;   // batch rows per launch
+constexpr int kGvTagRows = 4;     // batch rows up to which layers hand off in tagged words
+constexpr int kGvCntStride = 32;  // one arrival counter per 128-byte line
+constexpr int kGvUnroll = 16;     // 16-byte loads in flight per thread while staging
+// Tags are 1..kGvTagLimit; before a forward whose tags would pass it the host clears
+// the hand-off words (tag 0 = never written) and starts again from 1.
+constexpr uint32_t kGvTagLimit = 0xffffu;
+// A CTA leaving after a failed wait first lets its weight copies land; a copy from
+// HBM takes microseconds, so this bound only matters if the device is broken.
+constexpr unsigned long long kGvDrainNs = 1000ull * 1000 * 1000;
+
+// Per-CTA trace slots (within the 16-slot per-layer trace of the batched path):
+// per layer 0..2; layer 0's record also holds the prologue stamps 3..7.
+enum {
+    kGvTraceInput = 0,      // the layer's input rows are staged (all tags seen)
+    kGvTraceReady = 1,      // ... and its weight slice has landed
+    kGvTracePublished = 2,  // outputs stored
+    kGvTraceEntry = 3,      // kernel entry (barriers initialised)
+    kGvTraceCopy0 = 4,      // first image copy issued (biases + layer 0)
+    kGvTraceCopies = 5,     // second image copy issued
+    kGvTraceMath = 8,       // per layer, first row group: products summed within the warps
+    kGvTraceReduced = 9,    // ... partial sums in shared memory
+    kGvTraceStored = 10     // ... outputs stored
+};
+
+struct GemvNetParams {
+    unsigned long long *trace[LL_MAX_LAYERS];  // per layer: 16 slots per CTA, or null
+    const uint8_t *img;                 // per-CTA images, img_bytes apart: the CTA's shared-memory
+                                        // prefix (biases / scales at boff, weight slices at woff)
+    int dims[LL_MAX_LAYERS + 1];
+    int acts[LL_MAX_LAYERS];
+    int rmax[LL_MAX_LAYERS];            // ceil(N_l / G): rows of the largest slice
+    uint32_t woff[LL_MAX_LAYERS];       // byte offset of the layer's weight slice in shared memory
+    uint32_t boff[LL_MAX_LAYERS];       // float offset of the layer's bias (+ scale) slice
+    int n_layers;
+    int n_rows;                         // batch rows of this launch, 1..32
+    int xstride;                        // floats per staged input row (largest in_dim + 4)
+    uint32_t img_bytes;                 // per-CTA image (a multiple of 16)
+    uint32_t img_a_bytes;               // its first copy: biases + layer 0 (the second: the rest)
+    uint32_t off_part, off_bar, off_x;  // shared-memory layout, bytes (the image starts at 0)
+    const float *x;                     // [n_rows][dims[0]] fp32, 16-byte aligned
+    float *y;                           // [n_rows][dims[L]] fp32
+    uint32_t *hand[2];                  // tagged hand-off words [4][widest layer]: bf16 << 16 | tag
+    uint32_t tag_base;                  // tag of layer l's outputs = tag_base + l (1..65535)
+    __nv_bfloat16 *act[2];              // counted hand-off rows [32][widest layer] bf16
+    unsigned *cnt;                      // arrival counters, layer l at cnt[l * kGvCntStride]
+    unsigned epoch;                     // forward number: layer l's counter reaches epoch * producers
+    unsigned *status;                   // bit 0: a wait ran out; bits 8..15: 16 + failing layer
+    unsigned long long wait_ns;
+};
+
+__device__ __forceinline__ float gv_bf16_lo(uint32_t u)
+{
+    return __uint_as_float(u << 16);
+}
+
+__device__ __forceinline__ float gv_bf16_hi(uint32_t u)
+{
+    return __uint_as_float(u & 0xffff0000u);
+}
+
+__device__ __forceinline__ float gv_round_bf16(float v)
+{
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+__device__ __forceinline__ float gv_act(float v, int act)
+{
+    if (act == LL_ACT_RELU)
+        return fmaxf(v, 0.0f);
+    if (act == LL_ACT_GELU)
+        return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    return v;
+}
+
+__device__ __forceinline__ void gv_st_word(uint32_t *p, uint32_t v)
+{
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint4 gv_ld_words(const uint4 *p)
+{
+    uint4 v;
+    asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Wrap-safe: the counter of layer l grows by (producers of l) per forward.
+__device__ __forceinline__ bool gv_wait_count(const unsigned *cnt, unsigned target, unsigned long long bound_ns)
+{
+    if ((int)(ld_acquire_gpu(cnt) - target) >= 0)
+        return true;
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+        if ((int)(ld_acquire_gpu(cnt) - target) >= 0)
+            return true;
+        if (globaltimer() - t0 > bound_ns)
+            return false;
+    }
+}
+
+__device__ __forceinline__ bool gv_tags_are(uint4 v, uint32_t tag)
+{
+    return ((v.x & 0xffffu) == tag) & ((v.y & 0xffffu) == tag) & ((v.z & 0xffffu) == tag) &
+           ((v.w & 0xffffu) == tag);
+}
+
+__device__ __forceinline__ bool gv_wait_bar(uint32_t bar, unsigned long long bound_ns)
+{
+    if (mbar_try_wait(bar, 0))
+        return true;
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, 0))
+        if (globaltimer() - t0 > bound_ns)
+            return false;
+    return true;
+}
+
+__device__ __forceinline__ void gv_stamp(unsigned long long *tr, int slot)
+{
+    if (tr)
+        tr[slot] = globaltimer();
+}
+
+// 16 weight bytes -> CH floats (bf16: 8 values, exact; int8: 16 values, exact).
+template <bool WINT8>
+__device__ __forceinline__ void gv_weights(uint4 q, float (&w)[WINT8 ? 16 : 8])
+{
+    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+    if constexpr (WINT8) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                w[4 * j + e] = (float)(int8_t)(u[j] >> (8 * e));
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            w[2 * j] = gv_bf16_lo(u[j]);
+            w[2 * j + 1] = gv_bf16_hi(u[j]);
+        }
+    }
+}
+
+template <bool WINT8, int BG, int BPL>
+__global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid_constant__ GemvNetParams p)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int BP = BG * BPL;         // batch rows this instantiation covers
+    constexpr int KL = 32 / BG;          // lanes along K in a warp
+    constexpr int CH = WINT8 ? 16 : 8;   // K elements per 16-byte weight chunk
+    constexpr int ES = WINT8 ? 1 : 2;    // weight element size
+    constexpr bool kTagged = BP <= kGvTagRows;  // hand-off protocol (see the top of this file)
+    static_assert(BP <= kGvMaxRows && (32 % BG) == 0, "batch mapping");
+    static_assert(sizeof(GemvNetParams) % 4 == 0, "parameter copy");
+
+    // The per-layer tables are indexed at run time; read from the parameter space
+    // every such access is a constant-cache miss, so the CTA copies them once, all
+    // threads in parallel, and reads the shared-memory copy.
+    __shared__ GemvNetParams sp;
+    __shared__ uint32_t s_fail;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int kl = lane / BG, bg = lane - kl * BG;
+    const int G = (int)gridDim.x, c = (int)blockIdx.x;
+    const uint32_t sbase = smem_u32(smem);
+    {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(&p);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(&sp);
+        for (int i = tid; i < (int)(sizeof(GemvNetParams) / 4); i += kGvThreads)
+            dst[i] = src[i];
+    }
+    if (tid == 0) {
+        s_fail = 0u;
+        mbar_init(sbase + p.off_bar, 1);       // image copy A: biases + layer 0
+        mbar_init(sbase + p.off_bar + 8u, 1);  // image copy B: layers 1..
+        fence_mbar_init_cluster();
+    }
+    __syncthreads();
+    const int L = sp.n_layers, nr = sp.n_rows, XS = sp.xstride;
+    float *xs = reinterpret_cast<float *>(smem + sp.off_x);
+    float *part = reinterpret_cast<float *>(smem + sp.off_part);
+    const float *sbias = reinterpret_cast<const float *>(smem);
+    const uint32_t bar_a = sbase + sp.off_bar, bar_b = bar_a + 8u;
+    const bool has_b = sp.img_bytes > sp.img_a_bytes;
+
+    auto slice = [&](int l, int &r0) {
+        const unsigned N = (unsigned)sp.dims[l + 1];
+        r0 = (int)((unsigned)c * N / (unsigned)G);
+        return (int)((unsigned)(c + 1) * N / (unsigned)G) - r0;
+    };
+
+    unsigned long long *tr0 = sp.trace[0] ? sp.trace[0] + (size_t)c * 16 : nullptr;
+    if (tid == 0) {
+        gv_stamp(tr0, kGvTraceEntry);
+        const uint8_t *img = sp.img + (size_t)c * sp.img_bytes;
+        mbar_arrive_expect_tx(bar_a, sp.img_a_bytes);
+        bulk_g2s(sbase, img, sp.img_a_bytes, bar_a);
+        gv_stamp(tr0, kGvTraceCopy0);
+        if (has_b) {
+            mbar_arrive_expect_tx(bar_b, sp.img_bytes - sp.img_a_bytes);
+            bulk_g2s(sbase + sp.img_a_bytes, img + sp.img_a_bytes, sp.img_bytes - sp.img_a_bytes, bar_b);
+        }
+        gv_stamp(tr0, kGvTraceCopies);
+    }
+    // batch rows past n_rows stay zero in the staged input for the whole launch
+    for (int i = tid; i < (BP - nr) * XS; i += kGvThreads)
+        xs[(size_t)nr * XS + i] = 0.0f;
+    bool a_ready = false, b_ready = false;
+
+    for (int l = 0; l < L; ++l) {
+        int r0;
+        const int R = slice(l, r0);
+        if (R == 0)
+            continue;  // no rows here: this CTA neither reads layer l's input nor writes its output
+        const int K = sp.dims[l], N = sp.dims[l + 1];
+        unsigned long long *tr = sp.trace[l] ? sp.trace[l] + (size_t)c * 16 : nullptr;
+
+        // ---- input: layer 0 from the caller, later layers from the previous layer ----
+        // A thread issues up to kGvUnroll 16-byte loads before it stores any of them, so
+        // the L2 round trips overlap; every CTA starts at its own rotation of the rows.
+        bool ok = true;
+        if (l > 0 && !kTagged) {
+            if (tid == 0) {
+                const unsigned producers = (unsigned)min(G, K);  // layer l-1 has K rows over G CTAs
+                if (!gv_wait_count(sp.cnt + (size_t)(l - 1) * kGvCntStride, sp.epoch * producers, sp.wait_ns)) {
+                    s_fail = 1u;
+                    atomicOr(sp.status, 1u | ((16u + (unsigned)l) << 8));
+                }
+            }
+            __syncthreads();
+            if (s_fail)
+                break;
+        }
+        {
+            // groups of 16 bytes: 4 fp32 inputs (layer 0), 4 tagged words, or 8 bf16 values
+            const int per = (l == 0 || kTagged) ? 4 : 8;
+            const int q = K / per, total = nr * q, rot = (int)((unsigned)c * (unsigned)total / (unsigned)G);
+            const uint4 *src = l == 0 ? reinterpret_cast<const uint4 *>(sp.x)
+                               : kTagged ? reinterpret_cast<const uint4 *>(sp.hand[(l - 1) & 1])
+                                         : reinterpret_cast<const uint4 *>(sp.act[(l - 1) & 1]);
+            const uint32_t tag = sp.tag_base + (uint32_t)(l - 1);
+            for (int i0 = tid; i0 < total && ok; i0 += kGvThreads * kGvUnroll) {
+                uint4 v[kGvUnroll];
+                int gi[kGvUnroll];
+                uint32_t pending = 0u;
+#pragma unroll
+                for (int u = 0; u < kGvUnroll; ++u) {
+                    int i = i0 + u * kGvThreads + rot;
+                    gi[u] = i - (i >= total ? total : 0);
+                    if (i0 + u * kGvThreads < total) {
+                        v[u] = (l > 0 && kTagged) ? gv_ld_words(src + gi[u]) : __ldcg(src + gi[u]);
+                        pending |= 1u << u;
+                    }
+                }
+                uint64_t t0 = 0;
+                for (;;) {
+#pragma unroll
+                    for (int u = 0; u < kGvUnroll; ++u) {
+                        if (!((pending >> u) & 1u))
+                            continue;
+                        const int b = gi[u] / q, e = per * (gi[u] - b * q);
+                        float *d = xs + (size_t)b * XS + e;
+                        if (l == 0) {
+                            *reinterpret_cast<float4 *>(d) =
+                                make_float4(gv_round_bf16(__uint_as_float(v[u].x)), gv_round_bf16(__uint_as_float(v[u].y)),
+                                            gv_round_bf16(__uint_as_float(v[u].z)), gv_round_bf16(__uint_as_float(v[u].w)));
+                        } else if (kTagged) {
+                            if (!gv_tags_are(v[u], tag))
+                                continue;
+                            *reinterpret_cast<float4 *>(d) = make_float4(
+                                __uint_as_float(v[u].x & 0xffff0000u), __uint_as_float(v[u].y & 0xffff0000u),
+                                __uint_as_float(v[u].z & 0xffff0000u), __uint_as_float(v[u].w & 0xffff0000u));
+                        } else {
+                            *reinterpret_cast<float4 *>(d) = make_float4(gv_bf16_lo(v[u].x), gv_bf16_hi(v[u].x),
+                                                                         gv_bf16_lo(v[u].y), gv_bf16_hi(v[u].y));
+                            *reinterpret_cast<float4 *>(d + 4) = make_float4(gv_bf16_lo(v[u].z), gv_bf16_hi(v[u].z),
+                                                                             gv_bf16_lo(v[u].w), gv_bf16_hi(v[u].w));
+                        }
+                        pending &= ~(1u << u);
+                    }
+                    if (!pending)
+                        break;
+                    const uint64_t now = globaltimer();  // only tagged words can still be pending
+                    if (!t0)
+                        t0 = now;
+                    else if (now - t0 > sp.wait_ns) {
+                        ok = false;
+                        break;
+                    }
+#pragma unroll
+                    for (int u = 0; u < kGvUnroll; ++u)
+                        if ((pending >> u) & 1u)
+                            v[u] = gv_ld_words(src + gi[u]);
+                }
+            }
+        }
+        if (tid == 0)
+            gv_stamp(tr, kGvTraceInput);
+        // ---- the image copies: A (biases + layer 0) first, B (later layers) from layer 1 ----
+        if (ok && !a_ready && !gv_wait_bar(bar_a, sp.wait_ns))
+            ok = false;
+        if (ok && l > 0 && !b_ready && !gv_wait_bar(bar_b, sp.wait_ns))
+            ok = false;
+        a_ready = true;
+        b_ready = b_ready || l > 0;
+        if (!ok) {
+            s_fail = 1u;
+            atomicOr(sp.status, 1u | ((16u + (unsigned)l) << 8));
+        }
+        __syncthreads();
+        if (s_fail)
+            break;
+        if (tid == 0)
+            gv_stamp(tr, kGvTraceReady);
+
+        const uint8_t *ws = smem + sp.woff[l];
+        const float *sb = sbias + sp.boff[l];
+        const int rmax = sp.rmax[l], act = sp.acts[l];
+        const int nch = K / CH;
+        for (int rg = 0; rg < R; rg += kGvRowGroup) {
+            float acc[kGvRowGroup][BPL];
+#pragma unroll
+            for (int r = 0; r < kGvRowGroup; ++r)
+#pragma unroll
+                for (int i = 0; i < BPL; ++i)
+                    acc[r][i] = 0.0f;
+            for (int cc = warp * KL + kl; cc < nch; cc += kGvWarps * KL) {
+                const int k = cc * CH;
+                float xv[BPL][CH];
+#pragma unroll
+                for (int i = 0; i < BPL; ++i) {
+                    const float4 *xp = reinterpret_cast<const float4 *>(xs + (size_t)(bg + BG * i) * XS + k);
+#pragma unroll
+                    for (int j = 0; j < CH / 4; ++j) {
+                        const float4 v = xp[j];
+                        xv[i][4 * j] = v.x;
+                        xv[i][4 * j + 1] = v.y;
+                        xv[i][4 * j + 2] = v.z;
+                        xv[i][4 * j + 3] = v.w;
+                    }
+                }
+                // every row's chunk first, then the products j-outer: consecutive FMAs
+                // are independent (a lane keeps kGvRowGroup x BPL sums)
+                uint4 wq[kGvRowGroup];
+#pragma unroll
+                for (int r = 0; r < kGvRowGroup; ++r)
+                    wq[r] = rg + r < R ? *reinterpret_cast<const uint4 *>(ws + ((size_t)(rg + r) * K + k) * ES)
+                                       : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int h = 0; h < CH / 8; ++h) {  // 8 inputs at a time (int8 chunks hold 16)
+                    float wf[kGvRowGroup][8];
+#pragma unroll
+                    for (int r = 0; r < kGvRowGroup; ++r) {
+                        float w16[CH];
+                        gv_weights<WINT8>(wq[r], w16);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            wf[r][j] = w16[8 * h + j];
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+#pragma unroll
+                        for (int r = 0; r < kGvRowGroup; ++r)
+#pragma unroll
+                            for (int i = 0; i < BPL; ++i)
+                                acc[r][i] = fmaf(wf[r][j], xv[i][8 * h + j], acc[r][i]);
+                }
+            }
+            // the K lanes of a batch group hold partial sums of the same outputs
+#pragma unroll
+            for (int r = 0; r < kGvRowGroup; ++r)
+#pragma unroll
+                for (int i = 0; i < BPL; ++i)
+#pragma unroll
+                    for (int off = 16; off >= BG; off >>= 1)
+                        acc[r][i] += __shfl_xor_sync(0xffffffffu, acc[r][i], off);
+            if (tid == 0 && rg == 0)
+                gv_stamp(tr, kGvTraceMath);
+            if (kl == 0) {
+#pragma unroll
+                for (int r = 0; r < kGvRowGroup; ++r)
+#pragma unroll
+                    for (int i = 0; i < BPL; ++i)
+                        part[(warp * kGvRowGroup + r) * kGvMaxRows + bg + BG * i] = acc[r][i];
+            }
+            __syncthreads();
+            if (tid == 0 && rg == 0)
+                gv_stamp(tr, kGvTraceReduced);
+            for (int t = tid; t < kGvRowGroup * BP; t += kGvThreads) {
+                const int r = t / BP, b = t - r * BP;
+                if (rg + r < R && b < nr) {
+                    float s = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < kGvWarps; ++w)
+                        s += part[(w * kGvRowGroup + r) * kGvMaxRows + b];
+                    float v = WINT8 ? __fadd_rn(__fmul_rn(sb[rmax + rg + r], s), sb[rg + r]) : __fadd_rn(s, sb[rg + r]);
+                    v = gv_act(v, act);
+                    const size_t o = (size_t)b * N + r0 + rg + r;
+                    if (l + 1 == L)
+                        sp.y[o] = v;
+                    else if (kTagged)
+                        gv_st_word(sp.hand[l & 1] + o,
+                                   ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v)) << 16) |
+                                       (sp.tag_base + (uint32_t)l));
+                    else
+                        sp.act[l & 1][o] = __float2bfloat16_rn(v);
+                }
+            }
+            if (tid == 0 && rg == 0)
+                gv_stamp(tr, kGvTraceStored);
+            __syncthreads();
+        }
+        // counted hand-off: the barrier above orders every thread's outputs before
+        // thread 0's release
+        if (!kTagged && l + 1 < L && tid == 0)
+            red_release_gpu_add(sp.cnt + (size_t)l * kGvCntStride, 1u);
+        if (tid == 0)
+            gv_stamp(tr, kGvTracePublished);
+    }
+
+    // A CTA that gave up may still have copies in flight: let them land first.
+    if (s_fail && tid == 0) {
+        gv_wait_bar(bar_a, kGvDrainNs);
+        if (has_b)
+            gv_wait_bar(bar_b, kGvDrainNs);
+    }
+}
+
+}  // namespace llk

@@ -17,9 +17,30 @@ def test_config3_fills_the_gpu():
 
 def test_config2_batch_sweep_plans():
     for rows in (1, 2, 4, 8, 16, 32):
+        # up to 32 rows: the small-batch kernel, one CTA per SM holding 7 rows of each
+        # 1024-wide layer (1 of the 64-wide last layer) in shared memory
         p = ll.batched_plan(ll.config_net(2, rows))
-        assert p["rows_pad"] == 256 and p["kind"] == [1] * 6  # split-K tiles for small batches
-        assert all(1 <= c <= 148 for c in p["ctas"])
+        assert p["kind"] == [ll.KERNEL_GEMV] * 6
+        assert p["ctas"] == [148] * 6 and p["bn"] == [7] * 5 + [1]
+        assert p["smem_bytes"][0] <= 227 * 1024
+        # the tensor-core tiles on request
+        t = ll.batched_plan(ll.config_net(2, rows), ll.batched_opts(kernel=ll.KERNEL_SPLITK))
+        assert t["rows_pad"] == 256 and t["kind"] == [1] * 6
+        assert all(1 <= c <= 148 for c in t["ctas"])
+    # 33 rows is past the small-batch kernel
+    assert ll.batched_plan(ll.config_net(2, 33))["kind"] == [1] * 6
+    with pytest.raises(ll.LLError):
+        ll.batched_plan(ll.config_net(2, 33), ll.batched_opts(kernel=ll.KERNEL_GEMV))
+
+
+def test_small_batch_kernel_needs_the_slices_to_fit():
+    # config 3 (int8, 2048 wide): one row fits beside the weight slices, eight rows do not
+    assert ll.batched_plan(ll.config_net(3, 1))["kind"] == [ll.KERNEL_GEMV] * 8
+    assert ll.batched_plan(ll.config_net(3, 8))["kind"] == [1] * 8
+    # forcing tile options keeps the tensor-core tiles
+    net = ll.mlp([256, 256, 256], ll.ACT_RELU, ll.ACT_IDENTITY, ll.W_BF16, 16)
+    assert ll.batched_plan(net)["kind"] == [ll.KERNEL_GEMV] * 2
+    assert ll.batched_plan(net, ll.batched_opts(bn=64))["kind"] == [1, 1]
 
 
 def test_forced_tiles_are_honoured_and_checked():
