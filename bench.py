@@ -211,6 +211,7 @@ def run_batched(ll, torch, dev, iters=30):
     wbytes = sum(w.nbytes for w in Wd) + sum(b.nbytes for b in bd)
     hbm, hbm_kind = measured_peak("hbm_gbs", FALLBACK_HBM_GBS)
     sweep = []
+    # the small-batch kernel (auto for <= 32 rows): one launch per forward
     with ll.BatchedMLP(net, Wd, bd, sd, device=dev) as m:
         for rows in (1, 2, 4, 8, 16, 32):
             ms, e2e = timed(m, rows, 2)
@@ -221,8 +222,14 @@ def run_batched(ll, torch, dev, iters=30):
                           "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "peak_kind": hbm_kind,
                                        "unit": "GB/s", "frac": gbs / hbm}})
         tiling = m.info()
-    out["bf16_gelu_mlp_256x1024x4x64_sweep"] = {"points": sweep, "tiling": tiling,
-                                                "algorithmic": "bf16 weights + biases + rows x (in + out) fp32"}
+    # the same sweep on the tensor-core tiles (one launch per layer), for comparison
+    with ll.BatchedMLP(net, Wd, bd, sd, device=dev, opts=ll.batched_opts(kernel=ll.KERNEL_SPLITK)) as m:
+        for pt in sweep:
+            ms, e2e = timed(m, pt["rows"], 2)
+            pt["split_k_tiles_us_per_forward"] = ms * 1e3
+    out["bf16_gelu_mlp_256x1024x4x64_sweep"] = {
+        "points": sweep, "tiling": tiling, "kernel": "small-batch (one cooperative launch per forward)",
+        "algorithmic": "bf16 weights + biases + rows x (in + out) fp32"}
     return out
 
 

@@ -70,7 +70,7 @@ enum {
     kTcTraceClusterA = 5,  // after the first cluster barrier
     kTcTraceClusterB = 6,  // after the partial rows were exchanged
     kTcTraceEnd = 7,       // rows written
-    kTcTraceStaged = 8,    // split-K: partial tile staged in shared memory
+    kTcTraceStaged = 8,    // split-K: this CTA's partial rows sent to their owners
     kTcTraceStageReady = 9,   // 9..12: MMA thread, K steps 0..3 ready (landed and converted)
     kTcTraceReissue = 13,     // producer: first stage re-issued (after the MMAs freed it)
     kTcTraceReissueReady = 14,// MMA thread: that re-issued stage ready
@@ -101,26 +101,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
 
 // Bulk copy of this CTA's shared memory into a peer's (cluster address), completing
 // the byte count on the peer's mbarrier (cluster address).
-__device__ __forceinline__ void bulk_s2cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
-                                               uint32_t bar_cluster)
-{
-    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     dst_cluster),
-                 "r"(src_cta), "r"(bytes), "r"(bar_cluster)
-                 : "memory");
-}
-
-__device__ __forceinline__ void bulk_commit_group()
-{
-    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-
-// Wait until every committed bulk copy of this thread has finished reading its source.
-__device__ __forceinline__ void bulk_wait_group_read0()
-{
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-
 __device__ __forceinline__ void mbar_arrive_local(uint32_t bar)
 {
     asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
@@ -308,11 +288,11 @@ struct TcSmem {
     static constexpr int OFF_W = STAGES * XB;
     static constexpr int OFF_Q = OFF_W + STAGES * WB;
     static constexpr int PIPE_END = OFF_Q + STAGES * QB;
-    // split-K exchange, reusing the pipeline buffers once the MMAs are done: the CTA's
-    // partial tile (rows of RS bytes, padded against bank conflicts), then S slots of
-    // R rows each that receive the owners' rows (slot `src` = partial rows of CTA src)
+    // split-K exchange, reusing the pipeline buffers once the MMAs are done: S slots of
+    // R rows (RS bytes each, padded against bank conflicts) that receive the partial
+    // rows this CTA owns (slot `src` = the rows from CTA src), placed after one tile's
+    // worth of rows so the 256-wide tile keeps its current split rule
     static constexpr int RS = BN * 4 + 16;
-    static constexpr int OFF_STAGE = 0;
     static constexpr int OFF_SLOT = kTcRows * RS;
     static constexpr int XCHG_END = 2 * kTcRows * RS;
     static constexpr bool CAN_SPLIT = XCHG_END + 8 * 1024 <= 227 * 1024;
@@ -496,12 +476,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
     // ---------------- epilogue ----------------
     // Warps 4..7 read the accumulator (warp w owns TMEM lanes 32*(w%4)..+31 = tile rows).
     // Without a K split they finish their rows straight from TMEM.  With a split, the S
-    // CTAs of the cluster each own R = 128/S rows of the tile: every CTA stages its
-    // partial tile in shared memory and sends each owner its R rows with one bulk copy
-    // into the owner's slot for it (completing on the owner's exchange barrier); the
-    // owner adds the S slots in rank order (deterministic) and finishes its rows.
-    // The exchange runs on every path, failed or not, so no copy ever targets a CTA
-    // that has left; only the final writes depend on success.
+    // CTAs of the cluster each own R = 128/S rows of the tile: an epilogue thread whose
+    // row another CTA owns stores it straight into that owner's slot for this CTA
+    // (st.async, 16 bytes at a time, completing on the owner's exchange barrier), its
+    // own rows into its own slot; the owner adds the S slots in rank order
+    // (deterministic) and finishes its rows.  The exchange runs on every path, failed
+    // or not, so every owner receives all its bytes; only the final writes depend on
+    // success.
     const bool epi = warp >= kTcEpiWarp0 && warp < kTcEpiWarp0 + 4;
     const int q = warp & 3;
     const int trow = 32 * q + lane;  // tile row of this epilogue thread
@@ -514,7 +495,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
     const uint32_t rank = S > 1 ? cluster_ctarank() : 0u;
     if (S > 1) {
         if (tid == 0)  // bytes the S-1 peers will send into this CTA's slots
-            mbar_arrive_expect_tx(b_xchg, (uint32_t)((S - 1) * R * L::RS));
+            mbar_arrive_expect_tx(b_xchg, (uint32_t)((S - 1) * R * BN * 4));
         __syncwarp();
         cluster_sync();  // A: every CTA's MMAs are done: its pipeline buffers may be overwritten
     } else {
@@ -524,10 +505,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
         stamp(kTcTraceClusterA);
     const bool go = *fail == 0u;  // the roles have all finished: stable from here on
     if (epi && (go || S > 1)) {
-        // own rows go straight into this CTA's own slot; the others to the staging tile
+        // own rows go into this CTA's own slot, the others into their owner's slot for it
         const int owner = trow / R;
-        uint8_t *dst_row = (S > 1 && owner != (int)rank) ? smem + L::OFF_STAGE + (size_t)trow * L::RS
-                                                         : smem + L::OFF_SLOT + (size_t)(rank * R + (trow - owner * R)) * L::RS;
+        const bool remote = S > 1 && owner != (int)rank;
+        const uint32_t slot_row = (uint32_t)(L::OFF_SLOT + (rank * R + (trow - owner * R)) * L::RS);
+        uint8_t *dst_row = smem + slot_row;
+        const uint32_t rdst = remote ? mapa(sbase + slot_row, (uint32_t)owner) : 0u;
+        const uint32_t rbar = remote ? mapa(b_xchg, (uint32_t)owner) : 0u;
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 64) {
             float v[64];
@@ -556,6 +540,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
                         dst[i] = make_uint4(u[0], u[1], u[2], u[3]);
                     }
                 }
+            } else if (remote) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    st_async_v4(rdst + (uint32_t)(c0 + 4 * i) * 4u,
+                                make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]), rbar);
             } else {
                 float4 *d4 = reinterpret_cast<float4 *>(dst_row + (size_t)c0 * 4);
 #pragma unroll
@@ -563,27 +552,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
                     d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             }
         }
-        if (S > 1)
-            fence_proxy_async_smem();  // staged rows -> visible to the bulk-copy engine
     }
     if (S > 1) {
-        __syncthreads();  // the staging tile is complete
-        if (tid == 0) {
+        if (tid == kTcEpiWarp0 * 32)
             stamp(kTcTraceStaged);
-            for (int o = 0; o < S; ++o) {
-                if (o == (int)rank)
-                    continue;
-                const uint32_t src = sbase + (uint32_t)(L::OFF_STAGE + o * R * L::RS);
-                const uint32_t dst = mapa(sbase + (uint32_t)(L::OFF_SLOT + (int)rank * R * L::RS), (uint32_t)o);
-                bulk_s2cluster(dst, src, (uint32_t)(R * L::RS), mapa(b_xchg, (uint32_t)o));
-            }
-            bulk_commit_group();
-        }
         if (warp == 0) {  // every peer's rows have arrived in this CTA's slots
             tc_wait_warp(b_xchg, 0, p.wait_ns, fail, p.status, 5);
         }
-        if (tid == 0)
-            bulk_wait_group_read0();  // this CTA's outgoing copies have read the staging tile
         __syncthreads();
         if (tid == 0)
             stamp(kTcTraceClusterB);
