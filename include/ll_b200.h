@@ -302,7 +302,11 @@ typedef struct {
                             are not forced), else per layer 2 for >= 96 weights-in-TMEM tiles
                             (stacked batches) and 1 otherwise. */
     uint64_t wait_ns;    /* bound on every device-side wait; 0 = 1 s */
-    int32_t reserved[4];
+    int32_t graph;       /* 1 = replay the per-layer launches of a forward from a CUDA graph captured
+                            on first use (default; recaptured when the pointers or the row count
+                            change), so the host enqueues one graph instead of one launch per layer;
+                            0 = launch every layer from the host */
+    int32_t reserved[3];
 } ll_batched_opts;
 typedef struct {
     int32_t n_layers;

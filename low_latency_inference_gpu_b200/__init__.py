@@ -121,7 +121,8 @@ class Plan(ctypes.Structure):
 
 class BatchedOpts(ctypes.Structure):
     _fields_ = [("bn", ctypes.c_int32), ("splits", ctypes.c_int32), ("pdl", ctypes.c_int32),
-                ("kernel", ctypes.c_int32), ("wait_ns", ctypes.c_uint64), ("reserved", ctypes.c_int32 * 4)]
+                ("kernel", ctypes.c_int32), ("wait_ns", ctypes.c_uint64), ("graph", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 3)]
 
 
 class BatchedInfo(ctypes.Structure):
@@ -626,10 +627,11 @@ def mlp_forward_noalloc(net: Net, d_W_ptrs, d_b_ptrs, d_x_ptr: int, d_y_ptr: int
 KERNEL_SPLITK, KERNEL_WEIGHTS_IN_TMEM, KERNEL_GEMV = 1, 2, 3
 
 
-def batched_opts(bn: int = 0, splits: int = 0, pdl: int = 1, wait_ns: int = 0, kernel: int = 0) -> BatchedOpts:
+def batched_opts(bn: int = 0, splits: int = 0, pdl: int = 1, wait_ns: int = 0, kernel: int = 0,
+                 graph: int = 1) -> BatchedOpts:
     o = BatchedOpts()
     lib().ll_batched_opts_default(ctypes.byref(o))
-    o.bn, o.splits, o.pdl, o.wait_ns, o.kernel = bn, splits, pdl, wait_ns, kernel
+    o.bn, o.splits, o.pdl, o.wait_ns, o.kernel, o.graph = bn, splits, pdl, wait_ns, kernel, graph
     return o
 
 

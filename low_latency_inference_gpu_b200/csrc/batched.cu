@@ -286,7 +286,7 @@ void fill_info(const ll_net_desc *net, const ll_batched_opts *o, ll_batched_info
             info->bn[l] = kSwChan;
             info->splits[l] = 1;
             info->ctas[l] = (net->layers[l].out_dim / kSwChan) * (rows_pad / kSwRows);
-            info->smem_bytes[l] = TcSwapSmem::ALLOC;
+            info->smem_bytes[l] = i8 ? TcSwapSmem<true>::ALLOC : TcSwapSmem<false>::ALLOC;
             continue;
         }
         plan_layer(net->layers[l].in_dim, net->layers[l].out_dim, net->max_batch, i8, o, bn, s);
@@ -314,7 +314,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
 
 // 2-D row-major tensor map: inner dim `cols` elements, `rows` rows, box {64, box_rows}.
 bool make_map(CUtensorMap *m, CUtensorMapDataType t, int esize, const void *base, int cols, int rows, int box_rows,
-              bool swizzle)
+              CUtensorMapSwizzle swizzle)
 {
     auto fn = encode_fn();
     if (!fn)
@@ -324,8 +324,7 @@ bool make_map(CUtensorMap *m, CUtensorMapDataType t, int esize, const void *base
     cuuint32_t box[2] = {(cuuint32_t)kTcK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     return fn(m, t, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+              swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // fp32 rows -> bf16 (round to nearest even) into the padded layer-0 buffer.
@@ -436,6 +435,12 @@ struct ll_batched_mlp {
     uint32_t tag_next = 1;        // tag of the next tagged forward's layer 0
     unsigned *cnt = nullptr;      // arrival counters of the counted hand-off
     unsigned epoch = 0;           // counted forwards since the counters were cleared
+    // tensor-core path: the last forward's launches as a CUDA graph, and what it was captured for
+    int use_graph = 1;
+    cudaGraphExec_t gexec = nullptr;
+    const float *g_x = nullptr;
+    float *g_y = nullptr;
+    int g_rows = 0;
 };
 
 namespace {
@@ -457,6 +462,8 @@ void destroy_all(ll_batched_mlp *m)
     cudaFree(m->status);
     cudaFree(m->hand[0]);
     cudaFree(m->cnt);
+    if (m->gexec)
+        cudaGraphExecDestroy(m->gexec);
     cudaFree(m->img);
     cudaFree(m->hand[1]);
     if (m->own)
@@ -464,6 +471,10 @@ void destroy_all(ll_batched_mlp *m)
     delete m;
 }
 
+}  // namespace
+
+namespace {
+int enqueue_tc(ll_batched_mlp *m, const float *d_x, float *d_y, int n_rows, cudaStream_t st);
 }  // namespace
 
 extern "C" {
@@ -474,6 +485,7 @@ void ll_batched_opts_default(ll_batched_opts *o)
         return;
     std::memset(o, 0, sizeof(*o));
     o->pdl = 1;
+    o->graph = 1;
 }
 
 int ll_batched_plan(const ll_net_desc *net, const ll_batched_opts *opts, ll_batched_info *info)
@@ -529,6 +541,7 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
         m->wait_ns = opts->wait_ns;
     m->sms = sms;
     m->gemv = info.kind[0] == kKindGemv;
+    m->use_graph = opts ? opts->graph : 1;
     auto fail = [&](int code) {
         destroy_all(m);
         return code;
@@ -696,7 +709,7 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
             r.bn = kSwChan;
             r.splits = 1;
             r.ctas = info.ctas[l];
-            r.smem = TcSwapSmem::ALLOC;
+            r.smem = i8 ? TcSwapSmem<true>::ALLOC : TcSwapSmem<false>::ALLOC;
             r.kfn = i8 ? reinterpret_cast<const void *>(&ll_tc_swap_kernel<true>)
                        : reinterpret_cast<const void *>(&ll_tc_swap_kernel<false>);
             LLB_TRY(cudaFuncSetAttribute(r.kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, r.smem));
@@ -705,11 +718,17 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
             return fail(LL_ERR_BAD_DESC);
         }
         TcLayerParams &p = r.p;
-        const int x_box = r.kind == kKindWeightsInTmem ? kSwRows : kTcRows;
+        const bool swk = r.kind == kKindWeightsInTmem;
+        const int x_box = swk ? kSwRows : kTcRows;
+        // weights: bf16 128-byte swizzled (the MMA operand layout, or conflict-free row reads);
+        // int8 unswizzled for the split-K converters, 64-byte swizzled for the row reads of
+        // the weights-in-TMEM converters
+        const CUtensorMapSwizzle wsw = !i8 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                           : swk ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE;
         if (!make_map(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->act[l & 1], d.in_dim, m->rows_pad, x_box,
-                      true) ||
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
             !make_map(&p.tm_w, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, i8 ? 1 : 2,
-                      m->d_w[l], d.in_dim, d.out_dim, r.bn, !i8)) {
+                      m->d_w[l], d.in_dim, d.out_dim, r.bn, wsw)) {
             llh::set_error("layer %d: tensor map encoding failed", l);
             return fail(LL_ERR_CUDA);
         }
@@ -779,6 +798,50 @@ int ll_batched_mlp_forward(ll_batched_mlp *m, const float *d_x, float *d_y, int 
             m->epoch = g.epoch;
         return LL_OK;
     }
+    if (m->use_graph) {
+        if (!m->gexec || m->g_x != d_x || m->g_y != d_y || m->g_rows != n_rows) {
+            // capture on the object's own stream (the caller's may be the legacy default
+            // stream, which cannot be captured); the graph then runs on the caller's stream
+            if (m->gexec) {
+                cudaGraphExecDestroy(m->gexec);
+                m->gexec = nullptr;
+            }
+            LL_CUDA_TRY(cudaStreamBeginCapture(m->own, cudaStreamCaptureModeThreadLocal));
+            const int rc = enqueue_tc(m, d_x, d_y, n_rows, m->own);
+            cudaGraph_t graph = nullptr;
+            const cudaError_t ec = cudaStreamEndCapture(m->own, &graph);
+            if (rc != LL_OK || ec != cudaSuccess) {
+                if (graph)
+                    cudaGraphDestroy(graph);
+                if (rc == LL_OK)
+                    llh::set_error("batched forward: graph capture failed: %s", cudaGetErrorString(ec));
+                return rc != LL_OK ? rc : LL_ERR_CUDA;
+            }
+            const cudaError_t ei = cudaGraphInstantiate(&m->gexec, graph, 0);
+            cudaGraphDestroy(graph);
+            if (ei != cudaSuccess) {
+                m->gexec = nullptr;
+                llh::set_error("batched forward: graph instantiation failed: %s", cudaGetErrorString(ei));
+                return LL_ERR_CUDA;
+            }
+            m->g_x = d_x;
+            m->g_y = d_y;
+            m->g_rows = n_rows;
+        }
+        LL_CUDA_TRY(cudaGraphLaunch(m->gexec, st));
+        return LL_OK;
+    }
+    return enqueue_tc(m, d_x, d_y, n_rows, st);
+}
+
+}  // extern "C"
+
+namespace {
+
+// The tensor-core forward's launches: input rows to bf16, one kernel per layer (chained
+// with programmatic dependent launch), the caller's rows out of the padded output.
+int enqueue_tc(ll_batched_mlp *m, const float *d_x, float *d_y, int n_rows, cudaStream_t st)
+{
     const size_t n = (size_t)n_rows * m->in_dim;
     to_bf16_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 1184), 256, 0, st>>>(d_x, m->act[0], n);
     LL_CUDA_TRY(cudaGetLastError());
@@ -801,16 +864,18 @@ int ll_batched_mlp_forward(ll_batched_mlp *m, const float *d_x, float *d_y, int 
         attr[1].val.clusterDim.z = (unsigned)r.splits;
         cfg.attrs = attr;
         cfg.numAttrs = 2;
-        const uint8_t *wp = static_cast<const uint8_t *>(r.w);
-        void *args_sw[] = {&r.p, &wp};
         void *args[] = {&r.p};
-        LL_CUDA_TRY(cudaLaunchKernelExC(&cfg, r.kfn, sw ? args_sw : args));
+        LL_CUDA_TRY(cudaLaunchKernelExC(&cfg, r.kfn, args));
     }
     // the last layer wrote [rows_pad x out] fp32; hand the caller its n_rows
     LL_CUDA_TRY(cudaMemcpyAsync(d_y, m->out_pad, sizeof(float) * (size_t)n_rows * m->out_dim,
                                 cudaMemcpyDeviceToDevice, st));
     return LL_OK;
 }
+
+}  // namespace
+
+extern "C" {
 
 int ll_batched_mlp_check(ll_batched_mlp *m, void *stream)
 {
@@ -881,6 +946,10 @@ int ll_batched_mlp_set_trace(ll_batched_mlp *m, unsigned long long *d_trace, siz
     for (size_t l = 0; l < m->runs.size(); ++l) {
         m->runs[l].p.trace = d_trace ? d_trace + l * per_layer : nullptr;
         m->gp.trace[l] = m->runs[l].p.trace;
+    }
+    if (m->gexec) {  // the captured launches carry the old trace pointers
+        cudaGraphExecDestroy(m->gexec);
+        m->gexec = nullptr;
     }
     return LL_OK;
 }

@@ -294,6 +294,8 @@ struct TcSmem {
     // worth of rows so the 256-wide tile keeps its current split rule
     static constexpr int RS = BN * 4 + 16;
     static constexpr int OFF_SLOT = kTcRows * RS;
+    // without a split: the finished tile, row-major (RSO bytes per row, padded), at offset 0
+    static constexpr int RSO = BN * 4 + 16;
     static constexpr int XCHG_END = 2 * kTcRows * RS;
     static constexpr bool CAN_SPLIT = XCHG_END + 8 * 1024 <= 227 * 1024;
     static constexpr int REGION = (PIPE_END > XCHG_END || !CAN_SPLIT) ? PIPE_END : XCHG_END;
@@ -306,6 +308,7 @@ struct TcSmem {
     static_assert(XB % 1024 == 0 && WB % 1024 == 0 && QB % 1024 == 0, "1024-byte aligned tiles");
     static_assert(BN == 64 || BN == 128 || BN == 256, "N tile");
     static_assert(ALLOC <= 227 * 1024, "shared memory");
+    static_assert(kTcRows * RSO <= PIPE_END, "the finished tile fits the idle pipeline buffers");
 };
 
 template <int BN, bool WINT8, int STAGES>
@@ -517,18 +520,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
             float v[64];
             tc_ld_64cols(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
             if (S == 1) {
-                const int n = n0 + c0;
+                // finished rows go to a row-major staging tile in the (idle) pipeline buffers,
+                // written out below with whole-row stores
 #pragma unroll
                 for (int i = 0; i < 64; ++i)
                     v[i] = tc_act(fmaf(v[i], s_scale[c0 + i], s_bias[c0 + i]), p.act);
-                const size_t off = (size_t)(m0 + trow) * p.N + n;
+                uint8_t *srow = smem + (size_t)trow * L::RSO;
                 if (p.out_f32) {
-                    float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.out) + off);
+                    float4 *dst = reinterpret_cast<float4 *>(srow + (size_t)c0 * 4);
 #pragma unroll
                     for (int i = 0; i < 16; ++i)
                         dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                 } else {
-                    uint4 *dst = reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(p.out) + off);
+                    uint4 *dst = reinterpret_cast<uint4 *>(srow + (size_t)c0 * 2);
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         uint32_t u[4];
@@ -551,6 +555,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
                 for (int i = 0; i < 16; ++i)
                     d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             }
+        }
+    }
+    if (S == 1 && epi && go) {
+        // Whole rows out of the staging tile: consecutive threads write consecutive 16-byte
+        // pieces of one row.  (Each thread storing its own row gives 32 rows' 16-byte
+        // pieces per warp store; draining those kept a stacked layer's grid alive for
+        // ~12 us after its last CTA had finished.)
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps: tile staged
+        const int esz = p.out_f32 ? 4 : 2;
+        const int cpr = BN * esz / 16;  // 16-byte pieces per row
+        uint8_t *out = static_cast<uint8_t *>(p.out);
+        for (int idx = tid - kTcEpiWarp0 * 32; idx < kTcRows * cpr; idx += 128) {
+            const int r = idx / cpr, ch = idx - r * cpr;
+            *reinterpret_cast<uint4 *>(out + ((size_t)(m0 + r) * p.N + n0) * esz + (size_t)ch * 16) =
+                *reinterpret_cast<const uint4 *>(smem + (size_t)r * L::RSO + (size_t)ch * 16);
         }
     }
     if (S > 1) {

@@ -4,15 +4,17 @@
 //   D[128 channels x 256 rows] = W[n0:n0+128, :] . X[m0:m0+256, :]^T     (fp32, TMEM)
 //   Y[row][channel] = act(D * scale[channel] + bias[channel])
 //
-// Per 64-deep K step the SM moves only X through shared memory (TMA, 128-byte
-// swizzle, read once by the MMA as the B operand): the weight tile goes global ->
-// registers -> (int8: exact bf16 conversion) -> tensor memory with tcgen05.st,
-// where tcgen05.mma reads it as A.  That halves the shared-memory traffic of the
-// split-K layer kernel (tc_layer.cuh), whose int8 operand conversion made shared
-// memory the bound.  K is not split: one CTA owns a 128 x 256 output tile.
-// Roles (256 threads): warp 0 TMA for X; warp 1 TMEM allocation + the MMA thread;
-// warps 4..7 load/convert/store the weight stages to their TMEM lane quarter and
-// run the epilogue for the same lanes (= channels).  Every wait is bounded.
+// Per 64-deep K step X passes through shared memory once (TMA, 128-byte swizzle,
+// read by the MMA as the B operand); the weight tile arrives by TMA too (int8 with
+// 64-byte swizzle, bf16 with 128-byte swizzle, so that the 32 lanes of a warp,
+// one channel row each, read it without bank conflicts), is read once into
+// registers, converted (int8: exact bf16) and stored to tensor memory with
+// tcgen05.st, where tcgen05.mma reads it as A.  The weight loads start before the
+// dependency on the previous layer resolves.  K is not split: one CTA owns a
+// 128 x 256 output tile.  Roles (256 threads): warps 0 and 2 TMA for X; warp 1
+// TMEM allocation + the MMA thread; warp 3 TMA for the weights; warps 4..7 convert
+// the weight stages into their TMEM lane quarter and run the epilogue for the same
+// lanes (= channels).  Every wait is bounded.
 #pragma once
 #include "tc_layer.cuh"
 
@@ -21,26 +23,24 @@ namespace llk {
 constexpr int kSwRows = 256;      // rows per tile (MMA N)
 constexpr int kSwChan = 128;      // channels per tile (MMA M)
 constexpr int kSwThreads = 256;
-constexpr int kSwXStages = 6;     // X ring in shared memory (32 KB each); even: each producer owns fixed stages
+constexpr int kSwXStages = 4;     // X ring in shared memory (32 KB each)
 constexpr int kSwAStages = 4;     // weight stages in TMEM (32 columns each)
-// weight stages held in registers ahead of use: int8 slices are 4 x 16 B, bf16 8 x 16 B
-template <bool WINT8>
-constexpr int sw_prefetch()
-{
-    return WINT8 ? 8 : 4;
-}
 constexpr uint32_t kSwTmemCols = 512;  // D: columns [0, 256); A stages: [256, 384)
 
+template <bool WINT8>
 struct TcSwapSmem {
-    static constexpr int XB = kSwRows * kTcK * 2;  // 32 KB
+    static constexpr int XB = kSwRows * kTcK * 2;                // 32 KB
+    static constexpr int WB = kSwChan * kTcK * (WINT8 ? 1 : 2);  // 8 KB int8, 16 KB bf16
+    static constexpr int WSTAGES = WINT8 ? 8 : 4;                // weight ring in shared memory
     static constexpr int OFF_X = 0;
-    static constexpr int OFF_BAR = kSwXStages * XB;  // xfull[S], xempty[S], afull[A], aempty[A], accf
-    static constexpr int N_BAR = 2 * kSwXStages + 2 * kSwAStages + 1;
+    static constexpr int OFF_W = kSwXStages * XB;
+    static constexpr int OFF_BAR = OFF_W + WSTAGES * WB;  // xfull[S], xempty[S], wfull[W], wempty[W], afull[A], aempty[A], accf
+    static constexpr int N_BAR = 2 * kSwXStages + 2 * WSTAGES + 2 * kSwAStages + 1;
     static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;  // tmem base, fail flag
     static constexpr int OFF_BIAS = OFF_MISC + 16;        // bias[128], scale[128]
     static constexpr int BYTES = OFF_BIAS + 8 * kSwChan;
     static constexpr int ALLOC = BYTES + 1024;
-    static_assert(XB % 1024 == 0, "1024-byte aligned tiles");
+    static_assert(XB % 1024 == 0 && WB % 1024 == 0, "1024-byte aligned tiles");
     static_assert(ALLOC <= 227 * 1024, "shared memory");
 };
 
@@ -69,54 +69,11 @@ __device__ __forceinline__ void tc_mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a,
         : "memory");
 }
 
-__device__ __forceinline__ uint4 ld_nc_v4(const void *p)
-{
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-
-// One weight row's 64-deep K slice as packed bf16 pairs (low half = even k).
 template <bool WINT8>
-struct WSlice {
-    static constexpr int NV = WINT8 ? 4 : 8;  // 16-byte loads per slice
-    uint4 v[NV];
-    __device__ __forceinline__ void load(const uint8_t *row, int k0)
-    {
-#pragma unroll
-        for (int i = 0; i < NV; ++i)
-            v[i] = ld_nc_v4(row + (size_t)k0 * (WINT8 ? 1 : 2) + 16 * i);
-    }
-    __device__ __forceinline__ void pack(uint32_t (&o)[32]) const
-    {
-        if constexpr (WINT8) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                uint32_t t[8];
-                i8x16_to_bf16(v[i], t);
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    o[8 * i + j] = t[j];
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                o[4 * i] = v[i].x;
-                o[4 * i + 1] = v[i].y;
-                o[4 * i + 2] = v[i].z;
-                o[4 * i + 3] = v[i].w;
-            }
-        }
-    }
-};
-
-template <bool WINT8>
-__global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_constant__ TcLayerParams p,
-                                                                    const uint8_t *__restrict__ wbase)
+__global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_constant__ TcLayerParams p)
 {
-    using L = TcSwapSmem;
+    using L = TcSwapSmem<WINT8>;
+    constexpr int WS = L::WSTAGES;
     extern __shared__ uint8_t sw_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sw_smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
@@ -128,9 +85,11 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     auto bar = [&](int i) { return sbase + (uint32_t)L::OFF_BAR + 8u * (uint32_t)i; };
     auto b_xfull = [&](int s) { return bar(s); };
     auto b_xempty = [&](int s) { return bar(kSwXStages + s); };
-    auto b_afull = [&](int s) { return bar(2 * kSwXStages + s); };
-    auto b_aempty = [&](int s) { return bar(2 * kSwXStages + kSwAStages + s); };
-    const uint32_t b_accf = bar(2 * kSwXStages + 2 * kSwAStages);
+    auto b_wfull = [&](int s) { return bar(2 * kSwXStages + s); };
+    auto b_wempty = [&](int s) { return bar(2 * kSwXStages + WS + s); };
+    auto b_afull = [&](int s) { return bar(2 * kSwXStages + 2 * WS + s); };
+    auto b_aempty = [&](int s) { return bar(2 * kSwXStages + 2 * WS + kSwAStages + s); };
+    const uint32_t b_accf = bar(2 * kSwXStages + 2 * WS + 2 * kSwAStages);
 
     const uint32_t cta_lin = blockIdx.x + gridDim.x * blockIdx.y;
     auto stamp = [&](int k) {
@@ -148,6 +107,10 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
             mbar_init(b_xfull(s), 1);
             mbar_init(b_xempty(s), 1);
         }
+        for (int s = 0; s < WS; ++s) {
+            mbar_init(b_wfull(s), 1);
+            mbar_init(b_wempty(s), 4);  // one arrive per converter warp
+        }
         for (int s = 0; s < kSwAStages; ++s) {
             mbar_init(b_afull(s), 4);  // one arrive per converter warp
             mbar_init(b_aempty(s), 1);
@@ -156,6 +119,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
         misc[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         prefetch_tmap(&p.tm_x);
+        prefetch_tmap(&p.tm_w);
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -173,23 +137,26 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     const bool conv = warp >= 4;
     const int q = warp & 3;
     const int chan = 32 * q + lane;  // this thread's TMEM lane = output channel within the tile
-    const uint8_t *wrow = wbase + (size_t)(n0 + chan) * p.K * (WINT8 ? 1 : 2);
-    constexpr int kSwPrefetch = sw_prefetch<WINT8>();
-    WSlice<WINT8> pre[kSwPrefetch];
-    if (conv) {
-        // weights, biases and scales do not depend on the previous layer
-#pragma unroll
-        for (int i = 0; i < kSwPrefetch; ++i)
-            if (i < nk)
-                pre[i].load(wrow, i * kTcK);
-        if (q == 0) {
-            for (int i = lane; i < kSwChan; i += 32) {
-                s_bias[i] = __ldg(p.bias + n0 + i);
-                s_scale[i] = p.scale ? __ldg(p.scale + n0 + i) : 1.0f;
+    if (warp == 3) {
+        // ---------------- TMA producer: weight tiles (independent of the previous layer) ----------------
+        if (lane == 0) {
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % WS;
+                if (kb >= WS && !tc_wait(b_wempty(s), ((kb / WS) - 1) & 1, p.wait_ns, fail, p.status, 6))
+                    break;
+                mbar_arrive_expect_tx(b_wfull(s), L::WB);
+                tma_load_2d(sbase + L::OFF_W + s * L::WB, &p.tm_w, kb * kTcK, n0, b_wfull(s));
             }
         }
+    } else if (conv && q == 0) {
+        // biases and scales do not depend on the previous layer either
+        for (int i = lane; i < kSwChan; i += 32) {
+            s_bias[i] = __ldg(p.bias + n0 + i);
+            s_scale[i] = p.scale ? __ldg(p.scale + n0 + i) : 1.0f;
+        }
     }
-    griddep_wait();  // X belongs to the previous layer (and Y to the one before it) until here
+    if (warp != 3)
+        griddep_wait();  // X belongs to the previous layer (and Y to the one before it) until here
     if (tid == 0)
         stamp(kTcTraceDepDone);
 
@@ -236,19 +203,42 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
             tc_commit(b_accf);
         }
     } else if (conv) {
-        // ---------------- weights: registers -> bf16 -> TMEM (lanes of quarter q) ----------------
+        // ---------------- weights: shared memory -> registers -> bf16 -> TMEM (lanes of quarter q) ----------------
         for (int kb = 0; kb < nk; ++kb) {
-            const int sa = kb % kSwAStages;
+            const int sa = kb % kSwAStages, sw = kb % WS;
             if (kb >= kSwAStages &&
                 !tc_wait_warp(b_aempty(sa), ((kb / kSwAStages) - 1) & 1, p.wait_ns, fail, p.status, 3))
                 break;
+            if (!tc_wait_warp(b_wfull(sw), (kb / WS) & 1, p.wait_ns, fail, p.status, 3))
+                break;
+            // this lane's channel row of the stage; the TMA swizzle moved 16-byte chunk j of
+            // row r to chunk j ^ (r / 2 % 4) (int8, 64-byte rows) or j ^ (r % 8) (bf16, 128-byte
+            // rows), so the warp's 32 rows spread over all banks
+            const uint8_t *wr = smem + L::OFF_W + sw * L::WB + chan * (kTcK * (WINT8 ? 1 : 2));
             uint32_t o[32];
-            pre[0].pack(o);
+            if constexpr (WINT8) {
 #pragma unroll
-            for (int i = 0; i + 1 < kSwPrefetch; ++i)
-                pre[i] = pre[i + 1];
-            if (kb + kSwPrefetch < nk)
-                pre[kSwPrefetch - 1].load(wrow, (kb + kSwPrefetch) * kTcK);
+                for (int j = 0; j < 4; ++j) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(wr + 16 * (j ^ ((chan >> 1) & 3)));
+                    uint32_t t[8];
+                    i8x16_to_bf16(v, t);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        o[8 * j + e] = t[e];
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(wr + 16 * (j ^ (chan & 7)));
+                    o[4 * j] = v.x;
+                    o[4 * j + 1] = v.y;
+                    o[4 * j + 2] = v.z;
+                    o[4 * j + 3] = v.w;
+                }
+            }
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive_local(b_wempty(sw));  // the stage is read: the producer may refill it
             tc_st_32cols(tmem + ((uint32_t)(32 * q) << 16) + 256u + (uint32_t)sa * 32u, o);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
@@ -270,8 +260,16 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     __syncthreads();  // every role is done; bias and scale are in shared memory
     const bool go = *fail == 0u;
     if (conv && go) {
+        // The accumulator holds a channel per lane and a row per column; Y is row-major.
+        // Stage the tile row-major in the X ring (idle: every MMA has completed), then
+        // write whole rows with 16-byte stores.  (Storing straight from the lanes gives
+        // 64-byte pieces 4 KB apart; draining 8 MB of those kept a layer's grid alive
+        // ~18 us after its last CTA had finished.)
         const float sc = s_scale[chan], bi = s_bias[chan];
-        const int n = n0 + chan;
+        const int esz = p.out_f32 ? 4 : 2;
+        const int row_bytes = kSwChan * esz;  // one tile row: 256 (bf16) or 512 (fp32) bytes
+        uint8_t *stage = smem + L::OFF_X;
+        static_assert(kSwRows * kSwChan * 4 <= kSwXStages * L::XB, "fp32 tile fits the X ring");
 #pragma unroll 1
         for (int c0 = 0; c0 < kSwRows; c0 += 64) {
             float v[64];
@@ -279,12 +277,20 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
                 const float y = tc_act(fmaf(v[i], sc, bi), p.act);
-                const size_t off = (size_t)(m0 + c0 + i) * p.N + n;  // 32 consecutive channels per warp store
+                uint8_t *d = stage + (size_t)(c0 + i) * row_bytes + (size_t)chan * esz;
                 if (p.out_f32)
-                    static_cast<float *>(p.out)[off] = y;
+                    *reinterpret_cast<float *>(d) = y;
                 else
-                    static_cast<__nv_bfloat16 *>(p.out)[off] = __float2bfloat16_rn(y);
+                    *reinterpret_cast<__nv_bfloat16 *>(d) = __float2bfloat16_rn(y);
             }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps: the tile is staged
+        const int cpr = row_bytes / 16;  // 16-byte chunks per row
+        uint8_t *out = static_cast<uint8_t *>(p.out);
+        for (int idx = tid - 128; idx < kSwRows * cpr; idx += 128) {
+            const int r = idx / cpr, ch = idx - r * cpr;
+            *reinterpret_cast<uint4 *>(out + ((size_t)(m0 + r) * p.N + n0) * esz + (size_t)ch * 16) =
+                *reinterpret_cast<const uint4 *>(stage + (size_t)r * row_bytes + (size_t)ch * 16);
         }
     }
 

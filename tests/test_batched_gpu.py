@@ -86,6 +86,21 @@ def test_config3_repeated_forwards_are_identical():
     assert np.array_equal(ys[0], y_host)
 
 
+def test_graph_replay_matches_direct_launches():
+    # forwards replayed from the captured CUDA graph (default) against per-layer launches
+    # from the host; a new row count or new pointers make the object capture again
+    net = ll.config_net(3)
+    Ws, bs = ll.config_params(3)[1:]
+    xs = ll.config_inputs(3, 256)
+    with make(net, Ws, bs) as g, make(net, Ws, bs, graph=0) as d:
+        for rows in (256, 100, 256):
+            yg = run_device(g, xs[:rows])
+            yd = run_device(d, xs[:rows])
+            assert np.array_equal(yg, yd), rows
+    ref = oracle_out(net, Ws, bs, xs[:8])
+    assert rel_err(yg[:8], ref) <= TOL[ll.W_I8]
+
+
 @pytest.mark.parametrize("rows", [1, 2, 4, 8, 16, 32])
 def test_config2_bf16_gelu_batch_sweep(rows):
     net = ll.config_net(2)
