@@ -233,6 +233,35 @@ def run_batched(ll, torch, dev, iters=30):
     return out
 
 
+# name -> (workload config, rows per forward, batched options)
+PROFILE_CASES = {
+    "bf16-gelu-256x1024x4x64-1row": (2, 1, {}),
+    "bf16-gelu-256x1024x4x64-32rows": (2, 32, {}),
+    "int8-1024x2048x6x256-256rows": (3, 256, {}),
+    "int8-1024x2048x6x256-2048rows": (3, 2048, {}),
+}
+
+
+def run_profile_case(name):
+    """Three forwards of one batched workload (the small-batch kernel for the bf16 GELU net,
+    the tensor-core tiles for the int8 net), nothing else on the device."""
+    import torch
+
+    import low_latency_inference_gpu_b200 as ll
+
+    cfg, rows, opts = PROFILE_CASES[name]
+    net, Ws, bs = ll.config_params(cfg)
+    run_net = ll.Net(net.dims, net.acts, net.wtype, rows) if cfg == 3 else net
+    Wd, bd, sd = ll.device_weights(net, Ws, bs)
+    stream = torch.cuda.current_stream().cuda_stream
+    with ll.BatchedMLP(run_net, Wd, bd, sd, device=0, opts=ll.batched_opts(**opts) if opts else None) as m:
+        dx = torch.from_numpy(ll.config_inputs(cfg, rows)).cuda()
+        dy = torch.empty((rows, m.out_dim), dtype=torch.float32, device="cuda")
+        for _ in range(3):
+            m.forward(dx.data_ptr(), dy.data_ptr(), rows, stream)
+        m.check(stream)
+
+
 def measured_peak_hbm():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -356,8 +385,14 @@ def main():
                     help="value: run only the device-queue phase (bounded launches; usable under ncu, which "
                          "serialises launches and so cannot drive the resident mailbox kernel); batched: only "
                          "the batched tensor-core section, printed as its own JSON line")
+    ap.add_argument("--profile-case", default=None, choices=sorted(PROFILE_CASES),
+                    help="run three forwards of one batched workload and exit (a small, self-contained "
+                         "target for ncu captures; prints nothing)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.profile_case:
+        run_profile_case(args.profile_case)
+        return
 
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)
