@@ -189,6 +189,60 @@ __device__ __forceinline__ float tc_act(float v, int act)
     return v;
 }
 
+template <int ACT>
+__device__ __forceinline__ float tc_act_t(float v)
+{
+    if constexpr (ACT == 1)
+        return fmaxf(v, 0.0f);
+    else if constexpr (ACT == 2)
+        return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    else
+        return v;
+}
+
+// v = act(v * scale + bias) over 64 accumulator columns.  The activation is a template
+// argument, chosen once per tile: unrolled 64 times with the run-time switch (GELU's erf
+// inlined into every element) the epilogue was ~50 KB of straight-line code that ran once
+// per launch, and streaming it through the instruction cache cost ~14 us per tile.
+template <int ACT>
+__device__ __forceinline__ void tc_finish_64(float (&v)[64], const float *scale, const float *bias)
+{
+#pragma unroll
+    for (int i = 0; i < 64; ++i)
+        v[i] = tc_act_t<ACT>(fmaf(v[i], scale[i], bias[i]));
+}
+
+// One tile row (this thread's TMEM lane) finished into its row of the staging tile.
+template <int BN, int ACT>
+__device__ __forceinline__ void tc_stage_rows(uint32_t tq, uint8_t *srow, const float *scale, const float *bias,
+                                              bool out_f32)
+{
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 64) {
+        float v[64];
+        tc_ld_64cols(tq + (uint32_t)c0, v);
+        tc_finish_64<ACT>(v, scale + c0, bias + c0);
+        if (out_f32) {
+            float4 *dst = reinterpret_cast<float4 *>(srow + (size_t)c0 * 4);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else {
+            uint4 *dst = reinterpret_cast<uint4 *>(srow + (size_t)c0 * 2);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                uint32_t u[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * i + 2 * e], v[8 * i + 2 * e + 1]);
+                    u[e] = *reinterpret_cast<const uint32_t *>(&h);
+                }
+                dst[i] = make_uint4(u[0], u[1], u[2], u[3]);
+            }
+        }
+    }
+}
+
 // Bounded mbarrier wait; false when the bound ran out (or another role already failed).
 __device__ __forceinline__ bool tc_wait(uint32_t bar, uint32_t parity, unsigned long long bound_ns,
                                         volatile uint32_t *fail, unsigned *status, uint32_t role)
@@ -515,36 +569,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
         uint8_t *dst_row = smem + slot_row;
         const uint32_t rdst = remote ? mapa(sbase + slot_row, (uint32_t)owner) : 0u;
         const uint32_t rbar = remote ? mapa(b_xchg, (uint32_t)owner) : 0u;
+        const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
+        if (S == 1) {
+            // finished rows go to a row-major staging tile in the (idle) pipeline buffers,
+            // written out below with whole-row stores; one instantiation per activation
+            uint8_t *srow = smem + (size_t)trow * L::RSO;
+            if (p.act == 1)
+                tc_stage_rows<BN, 1>(tq, srow, s_scale, s_bias, p.out_f32 != 0);
+            else if (p.act == 2)
+                tc_stage_rows<BN, 2>(tq, srow, s_scale, s_bias, p.out_f32 != 0);
+            else
+                tc_stage_rows<BN, 0>(tq, srow, s_scale, s_bias, p.out_f32 != 0);
+        }
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 64) {
+        for (int c0 = 0; S > 1 && c0 < BN; c0 += 64) {
             float v[64];
-            tc_ld_64cols(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-            if (S == 1) {
-                // finished rows go to a row-major staging tile in the (idle) pipeline buffers,
-                // written out below with whole-row stores
-#pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    v[i] = tc_act(fmaf(v[i], s_scale[c0 + i], s_bias[c0 + i]), p.act);
-                uint8_t *srow = smem + (size_t)trow * L::RSO;
-                if (p.out_f32) {
-                    float4 *dst = reinterpret_cast<float4 *>(srow + (size_t)c0 * 4);
-#pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                } else {
-                    uint4 *dst = reinterpret_cast<uint4 *>(srow + (size_t)c0 * 2);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        uint32_t u[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const __nv_bfloat162 h = __floats2bfloat162_rn(v[8 * i + 2 * e], v[8 * i + 2 * e + 1]);
-                            u[e] = *reinterpret_cast<const uint32_t *>(&h);
-                        }
-                        dst[i] = make_uint4(u[0], u[1], u[2], u[3]);
-                    }
-                }
-            } else if (remote) {
+            tc_ld_64cols(tq + (uint32_t)c0, v);
+            if (remote) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
                     st_async_v4(rdst + (uint32_t)(c0 + 4 * i) * 4u,

@@ -69,6 +69,28 @@ __device__ __forceinline__ void tc_mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a,
         : "memory");
 }
 
+// Epilogue of one lane quarter: this lane's channel over the tile's 256 rows (TMEM columns),
+// act(D * scale + bias), into the row-major staging tile.
+template <int ACT, bool F32>
+__device__ __forceinline__ void sw_stage_tile(uint32_t tq, uint8_t *stage, int chan, float sc, float bi)
+{
+    constexpr int ESZ = F32 ? 4 : 2, ROW = kSwChan * ESZ;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kSwRows; c0 += 64) {
+        float v[64];
+        tc_ld_64cols(tq + (uint32_t)c0, v);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            const float y = tc_act_t<ACT>(fmaf(v[i], sc, bi));
+            uint8_t *d = stage + (size_t)(c0 + i) * ROW + (size_t)chan * ESZ;
+            if constexpr (F32)
+                *reinterpret_cast<float *>(d) = y;
+            else
+                *reinterpret_cast<__nv_bfloat16 *>(d) = __float2bfloat16_rn(y);
+        }
+    }
+}
+
 template <bool WINT8>
 __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_constant__ TcLayerParams p)
 {
@@ -270,19 +292,22 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
         const int row_bytes = kSwChan * esz;  // one tile row: 256 (bf16) or 512 (fp32) bytes
         uint8_t *stage = smem + L::OFF_X;
         static_assert(kSwRows * kSwChan * 4 <= kSwXStages * L::XB, "fp32 tile fits the X ring");
-#pragma unroll 1
-        for (int c0 = 0; c0 < kSwRows; c0 += 64) {
-            float v[64];
-            tc_ld_64cols(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-#pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                const float y = tc_act(fmaf(v[i], sc, bi), p.act);
-                uint8_t *d = stage + (size_t)(c0 + i) * row_bytes + (size_t)chan * esz;
-                if (p.out_f32)
-                    *reinterpret_cast<float *>(d) = y;
-                else
-                    *reinterpret_cast<__nv_bfloat16 *>(d) = __float2bfloat16_rn(y);
-            }
+        const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16);
+        // one instantiation per (activation, output type), chosen once (see tc_finish_64)
+        if (p.out_f32) {
+            if (p.act == 1)
+                sw_stage_tile<1, true>(tq, stage, chan, sc, bi);
+            else if (p.act == 2)
+                sw_stage_tile<2, true>(tq, stage, chan, sc, bi);
+            else
+                sw_stage_tile<0, true>(tq, stage, chan, sc, bi);
+        } else {
+            if (p.act == 1)
+                sw_stage_tile<1, false>(tq, stage, chan, sc, bi);
+            else if (p.act == 2)
+                sw_stage_tile<2, false>(tq, stage, chan, sc, bi);
+            else
+                sw_stage_tile<0, false>(tq, stage, chan, sc, bi);
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps: the tile is staged
         const int cpr = row_bytes / 16;  // 16-byte chunks per row
