@@ -136,6 +136,37 @@ def run_serving(ll, net, Ws, bs, xs, rank, world, hg, dev):
             "mailbox": "tagged, 8-slot request ring", "seconds_of_arrivals": SERVING_SECONDS, "rates": out}
 
 
+def run_config1(ll, torch, dev):
+    """The 10-layer fp32 MLP 128->512x8->32 at batch 1 (weights 8.7 MB, too large for one
+    cluster: the generic resident kernel pipelines it over several clusters): end-to-end
+    latency through the tagged mailbox (closed loop, host clock) and the device-queue time
+    per request (inputs in HBM, CUDA events around one launch of 2000 requests)."""
+    net, Ws, bs = ll.config_params(1)
+    xs = ll.config_inputs(1, 1000)
+    o = ll.default_opts()
+    o.mailbox_format = 1
+    out = {"workload": "config-1 MLP 128->512x8->32 fp32 (ReLU, identity out), batch 1, sequential requests"}
+    with ll.Engine(net, Ws, bs, device=dev, opts=o) as e:
+        info = e.info()
+        e.bench_closed_loop(xs, 2000)
+        lat, _ = e.bench_closed_loop(xs, 10000)
+        s = ll.compute_stats(lat)
+        out["e2e"] = {"p50_us": s["p50"], "p99_us": s["p99"], "mailbox": "tagged (mailbox_format 1)"}
+        out["engine"] = {"stages": info.n_stages, "cluster_size": info.cluster_size, "threads": info.threads,
+                         "smem_bytes": info.smem_bytes}
+    with ll.Engine(net, Ws, bs, device=dev) as e:
+        n = 2000
+        dx = torch.from_numpy(np.ascontiguousarray(np.resize(xs, (n, net.dims[0])))).to(f"cuda:{dev}")
+        dy = torch.empty((n, net.dims[-1]), dtype=torch.float32, device=f"cuda:{dev}")
+        e.run_queue(dx.data_ptr(), dy.data_ptr(), n, 1)
+        ms = min(e.run_queue(dx.data_ptr(), dy.data_ptr(), n, 1) for _ in range(3))
+        out["device_us_per_request"] = ms * 1e3 / n
+    wbytes = sum(w.nbytes for w in Ws) + sum(b.nbytes for b in bs)
+    out["roofline"] = {"bound": "latency", "note": f"{wbytes / 1e6:.2f} MB of weights stay in shared memory across "
+                       "the resident clusters; per request only x (512 B) and y (128 B) move"}
+    return out
+
+
 def measured_peak(key, fallback):
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -531,8 +562,10 @@ def main():
     if full and not args.no_serving:
         serving = run_serving(ll, net, Ws, bs, xs_all, rank, world, hg, dev)
     batched = None
+    config1 = None
     if world == 1 and full and not args.no_batched:
         batched = run_batched(ll, torch, dev)
+        config1 = run_config1(ll, torch, dev)
     if rank == 0 and world == 1 and full:
         import oracle
 
@@ -597,6 +630,7 @@ def main():
                              "path is latency-bound, latency_floor is its relevant bound"},
         "cpu_baseline": cpu_baseline,
         "batched": batched,
+        "config1": config1,
         "serving": serving,
         "clocks": clk,
         "gpu_launches": K + e2e_launches,

@@ -327,12 +327,16 @@ bool make_map(CUtensorMap *m, CUtensorMapDataType t, int esize, const void *base
               swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// fp32 rows -> bf16 (round to nearest even) into the padded layer-0 buffer.
-__global__ void to_bf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ out, size_t n)
+// fp32 rows -> bf16 (round to nearest even) into the padded layer-0 buffer, four values
+// per thread and step (16-byte loads, 8-byte stores; n4 = n / 4, n a multiple of 64).
+__global__ void to_bf16_kernel(const float4 *__restrict__ x, uint2 *__restrict__ out, size_t n4)
 {
     griddep_wait();
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        out[i] = __float2bfloat16_rn(x[i]);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 v = __ldg(x + i);
+        const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        out[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+    }
     griddep_launch_dependents();
 }
 
@@ -760,11 +764,11 @@ int ll_batched_mlp_forward(ll_batched_mlp *m, const float *d_x, float *d_y, int 
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     LL_CUDA_TRY(cudaSetDevice(m->device));
+    if (reinterpret_cast<uintptr_t>(d_x) % 16 != 0) {  // both paths read x 16 bytes at a time
+        llh::set_error("batched forward: x must be 16-byte aligned");
+        return LL_ERR_INVALID_ARG;
+    }
     if (m->gemv) {
-        if (reinterpret_cast<uintptr_t>(d_x) % 16 != 0) {
-            llh::set_error("batched forward: x must be 16-byte aligned");
-            return LL_ERR_INVALID_ARG;
-        }
         const int bp = gemv_bp(n_rows);
         const int idx = 31 - __builtin_clz((unsigned)bp);
         const bool tagged = bp <= kGvTagRows;
@@ -842,8 +846,9 @@ namespace {
 // with programmatic dependent launch), the caller's rows out of the padded output.
 int enqueue_tc(ll_batched_mlp *m, const float *d_x, float *d_y, int n_rows, cudaStream_t st)
 {
-    const size_t n = (size_t)n_rows * m->in_dim;
-    to_bf16_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 1184), 256, 0, st>>>(d_x, m->act[0], n);
+    const size_t n4 = (size_t)n_rows * m->in_dim / 4;  // in_dim is a multiple of 64
+    to_bf16_kernel<<<(unsigned)std::min<size_t>((n4 + 255) / 256, 1184), 256, 0, st>>>(
+        reinterpret_cast<const float4 *>(d_x), reinterpret_cast<uint2 *>(m->act[0]), n4);
     LL_CUDA_TRY(cudaGetLastError());
     const int mt = (n_rows + kTcRows - 1) / kTcRows;
     const int mt_sw = (n_rows + kSwRows - 1) / kSwRows;
