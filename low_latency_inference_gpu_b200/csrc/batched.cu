@@ -327,6 +327,23 @@ bool make_map(CUtensorMap *m, CUtensorMapDataType t, int esize, const void *base
               swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D view of a row-major [rows][cols] matrix as {64, rows, cols / 64} (x = position in a
+// 64-wide column block, y = row, z = block), box {64, box_rows, group}: one load brings
+// `group` consecutive column blocks of box_rows rows, each block's tile contiguous.
+bool make_map_grouped(CUtensorMap *m, CUtensorMapDataType t, int esize, const void *base, int cols, int rows,
+                      int box_rows, int group, CUtensorMapSwizzle swizzle)
+{
+    auto fn = encode_fn();
+    if (!fn)
+        return false;
+    cuuint64_t dims[3] = {(cuuint64_t)kTcK, (cuuint64_t)rows, (cuuint64_t)(cols / kTcK)};
+    cuuint64_t strides[2] = {(cuuint64_t)cols * (cuuint64_t)esize, (cuuint64_t)kTcK * (cuuint64_t)esize};
+    cuuint32_t box[3] = {(cuuint32_t)kTcK, (cuuint32_t)box_rows, (cuuint32_t)group};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, t, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // fp32 rows -> bf16 (round to nearest even) into the padded layer-0 buffer, four values
 // per thread and step (16-byte loads, 8-byte stores; n4 = n / 4, n a multiple of 64).
 __global__ void to_bf16_kernel(const float4 *__restrict__ x, uint2 *__restrict__ out, size_t n4)
@@ -729,10 +746,14 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
         // the weights-in-TMEM converters
         const CUtensorMapSwizzle wsw = !i8 ? CU_TENSOR_MAP_SWIZZLE_128B
                                            : swk ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE;
+        const CUtensorMapDataType wt = i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        const bool wmap_ok =
+            swk ? make_map_grouped(&p.tm_w, wt, i8 ? 1 : 2, m->d_w[l], d.in_dim, d.out_dim, r.bn,
+                                   i8 ? sw_wgroup<true>() : sw_wgroup<false>(), wsw)
+                : make_map(&p.tm_w, wt, i8 ? 1 : 2, m->d_w[l], d.in_dim, d.out_dim, r.bn, wsw);
         if (!make_map(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->act[l & 1], d.in_dim, m->rows_pad, x_box,
                       CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !make_map(&p.tm_w, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, i8 ? 1 : 2,
-                      m->d_w[l], d.in_dim, d.out_dim, r.bn, wsw)) {
+            !wmap_ok) {
             llh::set_error("layer %d: tensor map encoding failed", l);
             return fail(LL_ERR_CUDA);
         }

@@ -88,6 +88,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *tm,
         : "memory");
 }
 
+// 3-D tiled load {x, y, z} (the grouped weight boxes: x = K within a 64-wide block,
+// y = row, z = 64-wide K block).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm, int x, int y, int z, uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *tm)
 {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");

@@ -27,20 +27,31 @@ constexpr int kSwXStages = 4;     // X ring in shared memory (32 KB each)
 constexpr int kSwAStages = 4;     // weight stages in TMEM (32 columns each)
 constexpr uint32_t kSwTmemCols = 512;  // D: columns [0, 256); A stages: [256, 384)
 
+// An SM's TMA engine completes roughly one box per ~400-600 cycles almost whatever its size
+// (up to 32 KB), so a K step's 8 KB int8 weight tile as its own box cost as much as the 32 KB
+// row tile: one box carries WGROUP consecutive 64-deep K blocks (a 3-D view of W), 32 KB.
+template <bool WINT8>
+constexpr int sw_wgroup()
+{
+    return WINT8 ? 4 : 2;
+}
+
 template <bool WINT8>
 struct TcSwapSmem {
     static constexpr int XB = kSwRows * kTcK * 2;                // 32 KB
-    static constexpr int WB = kSwChan * kTcK * (WINT8 ? 1 : 2);  // 8 KB int8, 16 KB bf16
-    static constexpr int WSTAGES = WINT8 ? 8 : 4;                // weight ring in shared memory
+    static constexpr int WB = kSwChan * kTcK * (WINT8 ? 1 : 2);  // one K block of weights: 8 KB int8, 16 KB bf16
+    static constexpr int WG = sw_wgroup<WINT8>();                // K blocks per weight box
+    static constexpr int WSB = WG * WB;                          // weight stage (one box): 32 KB
+    static constexpr int WSTAGES = 2;                            // weight ring in shared memory
     static constexpr int OFF_X = 0;
     static constexpr int OFF_W = kSwXStages * XB;
-    static constexpr int OFF_BAR = OFF_W + WSTAGES * WB;  // xfull[S], xempty[S], wfull[W], wempty[W], afull[A], aempty[A], accf
+    static constexpr int OFF_BAR = OFF_W + WSTAGES * WSB;  // xfull[S], xempty[S], wfull[W], wempty[W], afull[A], aempty[A], accf
     static constexpr int N_BAR = 2 * kSwXStages + 2 * WSTAGES + 2 * kSwAStages + 1;
     static constexpr int OFF_MISC = OFF_BAR + 8 * N_BAR;  // tmem base, fail flag
     static constexpr int OFF_BIAS = OFF_MISC + 16;        // bias[128], scale[128]
     static constexpr int BYTES = OFF_BIAS + 8 * kSwChan;
     static constexpr int ALLOC = BYTES + 1024;
-    static_assert(XB % 1024 == 0 && WB % 1024 == 0, "1024-byte aligned tiles");
+    static_assert(XB % 1024 == 0 && WB % 1024 == 0 && WSB % 1024 == 0, "1024-byte aligned tiles");
     static_assert(ALLOC <= 227 * 1024, "shared memory");
 };
 
@@ -162,12 +173,14 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     if (warp == 3) {
         // ---------------- TMA producer: weight tiles (independent of the previous layer) ----------------
         if (lane == 0) {
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % WS;
-                if (kb >= WS && !tc_wait(b_wempty(s), ((kb / WS) - 1) & 1, p.wait_ns, fail, p.status, 6))
+            // one box per WG K blocks (a box past K is filled with zeros and still counts its bytes)
+            const int ng = (nk + L::WG - 1) / L::WG;
+            for (int g = 0; g < ng; ++g) {
+                const int s = g % WS;
+                if (g >= WS && !tc_wait(b_wempty(s), ((g / WS) - 1) & 1, p.wait_ns, fail, p.status, 6))
                     break;
-                mbar_arrive_expect_tx(b_wfull(s), L::WB);
-                tma_load_2d(sbase + L::OFF_W + s * L::WB, &p.tm_w, kb * kTcK, n0, b_wfull(s));
+                mbar_arrive_expect_tx(b_wfull(s), L::WSB);
+                tma_load_3d(sbase + L::OFF_W + s * L::WSB, &p.tm_w, 0, n0, g * L::WG, b_wfull(s));
             }
         }
     } else if (conv && q == 0) {
@@ -227,16 +240,16 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     } else if (conv) {
         // ---------------- weights: shared memory -> registers -> bf16 -> TMEM (lanes of quarter q) ----------------
         for (int kb = 0; kb < nk; ++kb) {
-            const int sa = kb % kSwAStages, sw = kb % WS;
+            const int sa = kb % kSwAStages, g = kb / L::WG, sub = kb - g * L::WG, sw = g % WS;
             if (kb >= kSwAStages &&
                 !tc_wait_warp(b_aempty(sa), ((kb / kSwAStages) - 1) & 1, p.wait_ns, fail, p.status, 3))
                 break;
-            if (!tc_wait_warp(b_wfull(sw), (kb / WS) & 1, p.wait_ns, fail, p.status, 3))
+            if (sub == 0 && !tc_wait_warp(b_wfull(sw), (g / WS) & 1, p.wait_ns, fail, p.status, 3))
                 break;
-            // this lane's channel row of the stage; the TMA swizzle moved 16-byte chunk j of
-            // row r to chunk j ^ (r / 2 % 4) (int8, 64-byte rows) or j ^ (r % 8) (bf16, 128-byte
-            // rows), so the warp's 32 rows spread over all banks
-            const uint8_t *wr = smem + L::OFF_W + sw * L::WB + chan * (kTcK * (WINT8 ? 1 : 2));
+            // this lane's channel row of K block `sub` of the stage; the TMA swizzle moved 16-byte
+            // chunk j of row r to chunk j ^ (r / 2 % 4) (int8, 64-byte rows) or j ^ (r % 8) (bf16,
+            // 128-byte rows), so the warp's 32 rows spread over all banks
+            const uint8_t *wr = smem + L::OFF_W + sw * L::WSB + sub * L::WB + chan * (kTcK * (WINT8 ? 1 : 2));
             uint32_t o[32];
             if constexpr (WINT8) {
 #pragma unroll
@@ -259,7 +272,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
                 }
             }
             __syncwarp();
-            if (lane == 0)
+            if (lane == 0 && (sub == L::WG - 1 || kb == nk - 1))
                 mbar_arrive_local(b_wempty(sw));  // the stage is read: the producer may refill it
             tc_st_32cols(tmem + ((uint32_t)(32 * q) << 16) + 256u + (uint32_t)sa * 32u, o);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
