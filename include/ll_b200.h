@@ -273,9 +273,9 @@ int ll_mlp_forward_noalloc(const ll_net_desc *net, const float *const *d_W, cons
  * Batched dense path on the tensor cores (tcgen05 + TMEM), for the batched
  * configurations: an MLP forward over up to max_batch rows as one tensor-core
  * layer kernel per layer (128-row x bn tiles; the K splits of a tile run as one
- * thread-block cluster and add their partials in rank order through distributed
- * shared memory, so results are deterministic), chained with programmatic
- * dependent launch.  No counterpart
+ * thread-block cluster and add their partials in rank order through an L2 scratch
+ * buffer, so results are deterministic), chained with programmatic dependent
+ * launch.  No counterpart
  * kernel in the reference, whose batched GEMMs are cuBLAS SGEMM calls
  * (src/bench_cublas_mlp.cu, src/bench_cublas_mlp_graph.cu:119-187); the layer
  * contract y = act(W x + b) and the row-major weight layout are the reference's.

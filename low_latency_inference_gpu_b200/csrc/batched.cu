@@ -454,6 +454,7 @@ struct ll_batched_mlp {
     uint8_t *img = nullptr;       // per-CTA shared-memory images (biases, scales, weight slices)
     size_t hand_bytes = 0;
     uint32_t tag_next = 1;        // tag of the next tagged forward's layer 0
+    float *scratch = nullptr;     // split-K partial tiles (exchange through L2)
     unsigned *cnt = nullptr;      // arrival counters of the counted hand-off
     unsigned epoch = 0;           // counted forwards since the counters were cleared
     // tensor-core path: the last forward's launches as a CUDA graph, and what it was captured for
@@ -483,6 +484,7 @@ void destroy_all(ll_batched_mlp *m)
     cudaFree(m->status);
     cudaFree(m->hand[0]);
     cudaFree(m->cnt);
+    cudaFree(m->scratch);
     if (m->gexec)
         cudaGraphExecDestroy(m->gexec);
     cudaFree(m->img);
@@ -769,8 +771,21 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
         p.out_f32 = r.out_f32;
         p.wait_ns = m->wait_ns;
         p.trace = nullptr;
+        p.scratch = nullptr;
         m->max_ctas = std::max(m->max_ctas, r.ctas);
         m->runs.push_back(r);
+    }
+    // split-K layers exchange their partial tiles through one L2 scratch buffer (layers run
+    // one after another: a layer writes it only after the previous one completed)
+    size_t scratch_bytes = 0;
+    for (const LayerRun &r : m->runs)
+        if (r.kind == kKindSplitK && r.splits > 1)
+            scratch_bytes = std::max(scratch_bytes, (size_t)r.ctas * kTcRows * (size_t)r.bn * sizeof(float));
+    if (scratch_bytes) {
+        LLB_TRY(cudaMalloc(&m->scratch, scratch_bytes));
+        for (LayerRun &r : m->runs)
+            if (r.kind == kKindSplitK && r.splits > 1)
+                r.p.scratch = m->scratch;
     }
 #undef LLB_TRY
     *out = m;
