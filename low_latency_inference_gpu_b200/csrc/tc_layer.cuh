@@ -369,6 +369,7 @@ struct TcSmem {
     static_assert(BN == 64 || BN == 128 || BN == 256, "N tile");
     static_assert(ALLOC <= 227 * 1024, "shared memory");
     static_assert(kTcRows * RSO <= PIPE_END, "the finished tile fits the idle pipeline buffers");
+    static_assert(kTcRows / 2 * (BN + 4) * 4 <= PIPE_END, "split-K sums (at most 64 rows) fit them too");
 };
 
 template <int BN, bool WINT8, int STAGES>
@@ -611,19 +612,51 @@ __global__ void __launch_bounds__(kTcThreads, 1) ll_tc_layer_kernel(const __grid
             constexpr int C4 = BN / 4;
             const float4 *tile_parts = reinterpret_cast<const float4 *>(p.scratch) +
                                        (size_t)(blockIdx.x + gridDim.x * blockIdx.y) * S * (kTcRows * C4);
-            for (int idx = tid; idx < R * C4; idx += kTcThreads) {
-                // consecutive threads take consecutive rows of one column group (coalesced);
-                // L2-coherent loads: this SM may hold the addresses from an earlier forward
-                const int r = idx % R, c = (idx / R) * 4;
-                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int src = 0; src < S; ++src) {
-                    const float4 v = __ldcg(tile_parts + (size_t)src * (kTcRows * C4) + (size_t)(c / 4) * kTcRows +
-                                            (int)rank * R + r);
-                    a.x += v.x;
-                    a.y += v.y;
-                    a.z += v.z;
-                    a.w += v.w;
+            // (1) sums, row-fastest so the L2 loads are coalesced: a thread issues the loads of
+            // up to 3 items x 4 partials before adding (rank order kept), into a padded
+            // row-major tile in the idle pipeline buffers
+            constexpr int SR = BN + 4;  // staged row stride in floats (16-byte pad: no bank conflicts)
+            float *sums = reinterpret_cast<float *>(smem);
+            const int n_items = R * C4;
+            for (int base = tid; base < n_items; base += 3 * kTcThreads) {
+                float4 acc[3];
+#pragma unroll
+                for (int u = 0; u < 3; ++u)
+                    acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int s0 = 0; s0 < S; s0 += 4) {
+                    float4 v[3][4];
+#pragma unroll
+                    for (int u = 0; u < 3; ++u) {
+                        const int idx = base + u * kTcThreads, r = idx % R, c4 = idx / R;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (idx < n_items && s0 + j < S)
+                                v[u][j] = __ldcg(tile_parts + (size_t)(s0 + j) * (kTcRows * C4) +
+                                                 (size_t)c4 * kTcRows + (int)rank * R + r);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 3; ++u)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (base + u * kTcThreads < n_items && s0 + j < S) {
+                                acc[u].x += v[u][j].x;
+                                acc[u].y += v[u][j].y;
+                                acc[u].z += v[u][j].z;
+                                acc[u].w += v[u][j].w;
+                            }
                 }
+#pragma unroll
+                for (int u = 0; u < 3; ++u) {
+                    const int idx = base + u * kTcThreads;
+                    if (idx < n_items)
+                        *reinterpret_cast<float4 *>(sums + (idx % R) * SR + (idx / R) * 4) = acc[u];
+                }
+            }
+            __syncthreads();
+            // (2) finish and write whole rows: consecutive threads, consecutive columns
+            for (int idx = tid; idx < n_items; idx += kTcThreads) {
+                const int r = idx / C4, c = (idx % C4) * 4;
+                const float4 a = *reinterpret_cast<const float4 *>(sums + r * SR + c);
                 float o4[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
