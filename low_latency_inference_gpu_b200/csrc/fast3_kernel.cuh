@@ -4,8 +4,11 @@
 // Every weight lives in a register for the whole launch (the register file is
 // 256 KB per SM; a cluster of C CTAs holds the net), so per request only x and
 // the activations move, through shared memory and DSMEM:
-//   rank 0  : polls the mailbox header (one 16-byte acquire load), reads x once,
-//             pushes {seq, x} into every peer's shared memory (st.async, one mbarrier);
+//   request : rank 0 polls the mailbox (the header with one 16-byte acquire load, or
+//             the tagged slot, whose chunks carry x), reads x once and pushes {seq, x}
+//             into every peer's shared memory (st.async, one mbarrier); in queue mode
+//             every CTA loads x from HBM and rank 0 sends each peer a 16-byte go {seq}
+//             that the peer waits for before its layer-3 partial;
 //   layer 1 : replicated in every CTA, S1 = T/H1 threads per row, K1 = IN/S1 weights
 //             per thread, butterfly over the S1 lanes;
 //   layer 2 : rows split over the cluster (R2 = H2/C per CTA), S2 = T/R2 threads per
@@ -131,42 +134,59 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
         if (p.mode == MODE_QUEUE && (int)n_done >= p.q_n)
             break;
         // ---------------- request ----------------
-        if (leader) {
-            if (p.mode == MODE_QUEUE) {
-                seq = n_done + 1;
-                if (tid == 0)
+        // Queue mode: every CTA loads x itself from HBM, so x is not pushed over DSMEM.  Rank 0
+        // sends each peer a 16-byte go {seq} once it has started the request (and so has
+        // finished the previous one); a peer waits for it before its layer-3 partial, so a
+        // peer that runs ahead never overwrites partials rank 0 still reads.  (On the
+        // mailbox every CTA polling host memory over PCIe made the requests 4x slower, so
+        // there rank 0 alone polls and pushes x.)
+        const bool own_x = p.mode == MODE_QUEUE;
+        if (own_x) {
+            seq = n_done + 1;
+            if (tid == 0) {
+                if (leader)
                     trace(k, n_done, 0);
-                const float *src = p.q_x + (size_t)n_done * IN;
-                if (tid < IN / 4)
-                    reinterpret_cast<float4 *>(xs)[tid] = __ldg(reinterpret_cast<const float4 *>(src) + tid);
-            } else {
-                if (p.mailbox_format == 1) {
-                    if (warp == 0) {
-                        const uint32_t c = poll_tagged(k, last, xs, ring_slot(p, n_done));  // x arrives with the doorbell
-                        if (tid == 0) {
-                            if (c == kCmdExit)
-                                broadcast_abort(k);
-                            sh.cmd = c;
-                            trace(k, n_done, 0);
-                        }
+                else
+                    mbar_arrive_expect_tx(bar_req, 16u);
+            }
+            const float *src = p.q_x + (size_t)n_done * IN;
+            if (tid < IN / 4)
+                reinterpret_cast<float4 *>(xs)[tid] = __ldg(reinterpret_cast<const float4 *>(src) + tid);
+            __syncthreads();
+            if (leader && tid > 0 && tid < C)
+                st_async_v4(mapa(h_addr, (uint32_t)tid), make_float4(__uint_as_float(seq), 0.f, 0.f, 0.f),
+                            mapa(bar_req, (uint32_t)tid));
+            if (leader && tid == 0)
+                trace(k, n_done, 1);
+        } else if (leader) {
+            if (p.mailbox_format == 1) {
+                if (warp == 0) {
+                    const uint32_t c = poll_tagged(k, last, xs, ring_slot(p, n_done));  // x arrives with the doorbell
+                    if (tid == 0) {
+                        if (c == kCmdExit)
+                            broadcast_abort(k);
+                        sh.cmd = c;
+                        trace(k, n_done, 0);
                     }
-                } else if (tid == 0) {
-                    const uint32_t c = poll_mailbox(k, last);
-                    if (c == kCmdExit)
-                        broadcast_abort(k);
-                    sh.cmd = c;
-                    trace(k, n_done, 0);
                 }
-                __syncthreads();
-                seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
-                if (seq == kCmdExit)
-                    break;
-                // batch 1: no header fetch (n_rows is 1; stop is seen on the idle cadence, so a
-                // stop that comes with a doorbell bump costs one extra, harmless reply)
-                if (p.mailbox_format == 0 && tid < IN / 4)
-                    reinterpret_cast<float4 *>(xs)[tid] = ld_relaxed_sys_v4(p.mb_x + tid * 4);
+            } else if (tid == 0) {
+                const uint32_t c = poll_mailbox(k, last);
+                if (c == kCmdExit)
+                    broadcast_abort(k);
+                sh.cmd = c;
+                trace(k, n_done, 0);
             }
             __syncthreads();
+            seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
+            if (seq == kCmdExit)
+                break;
+            // batch 1: no header fetch (n_rows is 1; stop is seen on the idle cadence, so a
+            // stop that comes with a doorbell bump costs one extra, harmless reply)
+            if (p.mailbox_format == 0) {
+                if (tid < IN / 4)
+                    reinterpret_cast<float4 *>(xs)[tid] = ld_relaxed_sys_v4(p.mb_x + tid * 4);
+                __syncthreads();
+            }
             if (tid == 0)
                 trace(k, n_done, 1);
             // push {seq} + x to every peer: (C-1) * (1 + IN/4) st.async of 16 bytes, one mbarrier each
@@ -234,7 +254,14 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             if (s2 == 0)
                 h2[r2] = relu_or(acc + bias[H1 + r2], act2);
         }
-        __syncthreads();
+        if (own_x && !leader) {
+            // rank 0's go for this request (sent while layers 1-2 ran); ends on its abort
+            if (!cta_wait_bar(k, bar_req, ph_req & 1u, EW_PEER_POLL, p.step_ns))
+                break;
+            ++ph_req;
+        } else {
+            __syncthreads();
+        }
         if (leader && tid == 0)
             trace(k, n_done, 4);
         // ---------------- layer 3 (K-split partials -> rank 0) ----------------
