@@ -99,7 +99,11 @@ typedef struct ll_engine_opts {
     int32_t ring_slots;         /* tagged mailbox only: request slots (1..64; 0 = 1).  Up to ring_slots
                                    requests may be outstanding (ll_submit before the earlier ll_poll);
                                    the device serves them in order, slot after slot */
-    int32_t reserved[3];
+    int32_t micro_batch;        /* request ring on the register-resident kernel: the device takes up to
+                                   this many waiting requests (consecutive slots, each complete) in one
+                                   poll and runs them as one small batch (1..4, at most ring_slots;
+                                   0 = 1).  Replies still go to each request's own slot. */
+    int32_t reserved[2];
 } ll_engine_opts;
 
 typedef struct ll_engine_info {
@@ -116,6 +120,10 @@ typedef struct ll_engine_info {
     int32_t layer_modes[24];
     int32_t kernel_variant; /* 1 generic, 2 register-resident */
     int32_t weight_regs;    /* register-resident: weights held per thread */
+    uint32_t passes;        /* register-resident: passes over the layers by the launches that have
+                               exited (ll_engine_stop, idle exit, queue runs) */
+    uint32_t rows;          /* ... and the requests those passes took: rows / passes is the mean
+                               micro-batch */
 } ll_engine_info;
 
 /*

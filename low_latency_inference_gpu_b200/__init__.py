@@ -83,7 +83,8 @@ class EngineOpts(ctypes.Structure):
                 ("write_combined", ctypes.c_int32), ("mailbox_format", ctypes.c_int32),
                 ("idle_timeout_ns", ctypes.c_uint64), ("step_timeout_ns", ctypes.c_uint64),
                 ("max_stages", ctypes.c_int32), ("min_stages", ctypes.c_int32), ("diag_wait_never", ctypes.c_int32),
-                ("kernel_variant", ctypes.c_int32), ("ring_slots", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+                ("kernel_variant", ctypes.c_int32), ("ring_slots", ctypes.c_int32), ("micro_batch", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 2)]
 
 
 class EngineInfo(ctypes.Structure):
@@ -91,7 +92,7 @@ class EngineInfo(ctypes.Structure):
                 ("smem_bytes", ctypes.c_int32), ("image_bytes", ctypes.c_int32), ("launches", ctypes.c_int32),
                 ("state", ctypes.c_int32), ("status", ctypes.c_int32), ("err_where", ctypes.c_int32),
                 ("served", ctypes.c_uint32), ("layer_modes", ctypes.c_int32 * 24), ("kernel_variant", ctypes.c_int32),
-                ("weight_regs", ctypes.c_int32)]
+                ("weight_regs", ctypes.c_int32), ("passes", ctypes.c_uint32), ("rows", ctypes.c_uint32)]
 
 
 class Stats(ctypes.Structure):

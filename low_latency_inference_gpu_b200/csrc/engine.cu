@@ -316,6 +316,7 @@ struct Fast3Entry {
     const void *fn;
     int K1, K2, K3, NB;
     int S1, S2, R2;
+    int rows;  // rows one pass carries (micro-batching)
 };
 
 template <int IN, int H1, int H2, int OUT, int C>
@@ -323,7 +324,7 @@ Fast3Entry fast3_entry()
 {
     using S = Fast3Shape<IN, H1, H2, OUT, C>;
     return Fast3Entry{IN, H1, H2, OUT, C, reinterpret_cast<const void *>(&ll_fast3_kernel<IN, H1, H2, OUT, C>),
-                      S::K1, S::K2, S::K3, S::NB, S::S1, S::S2, S::R2};
+                      S::K1, S::K2, S::K3, S::NB, S::S1, S::S2, S::R2, S::MaxRows};
 }
 
 const Fast3Entry *find_fast3(const ll_net_desc &net, int C)
@@ -415,6 +416,9 @@ struct ll_engine {
     bool attrs_set = false;
     const void *kfn = nullptr;  // kernel launched (generic or register-resident)
     int variant = 1;
+    int micro = 1;      // ring slots the device may take together
+    int micro_max = 1;  // rows the kernel can carry in one pass
+    uint32_t passes = 0, rows = 0;  // summed over exited launches
     int weight_regs = 0;
 };
 
@@ -485,6 +489,19 @@ int alloc_mailbox(ll_engine *e)
         llh::set_error("a request ring (ring_slots %d) needs the tagged mailbox and at most 64 slots", e->ring);
         return LL_ERR_UNSUPPORTED;
     }
+    e->micro = e->opts.micro_batch < 1 ? 1 : e->opts.micro_batch;
+    if (e->micro > 1) {
+        // the multi-slot poll holds every chunk of the slots it reads in warp 0's registers
+        const int chunks = e->micro * ((e->in_dim + 2) / 3);
+        if (e->opts.mailbox_format != 1 || e->micro > e->ring || e->micro > e->micro_max ||
+            chunks > 32 * kTagChunksPerLane) {
+            llh::set_error("micro_batch %d needs the tagged mailbox, at most ring_slots (%d), at most the rows "
+                           "the kernel carries (%d: the register-resident kernel of a shape with room for "
+                           "%d), and at most %d x chunks per poll (%d)",
+                           e->micro, e->ring, e->micro_max, kFast3Rows, 32 * kTagChunksPerLane, chunks);
+            return LL_ERR_UNSUPPORTED;
+        }
+    }
     if (e->opts.mailbox_format == 1) {
         e->ring_stride = llh::round_up(ll_tagged_y_offset(e->in_dim) + 16 * (size_t)((e->out_dim + 2) / 3), 64);
         e->mb_bytes = e->ring_stride * (size_t)e->ring;  // one slot: exactly ll_tagged_mailbox_bytes
@@ -547,6 +564,7 @@ int finish_setup(ll_engine *e)
     p.ring_slots = e->ring;
     p.ring_stride_f = (uint32_t)(e->ring_stride / 4);
     p.ring_base = 0;
+    p.micro_batch = e->micro;
     p.idle_ns = e->opts.idle_timeout_ns;
     p.step_ns = e->opts.step_timeout_ns;
     p.peer_margin_ns = 2ull * 1000 * 1000 * 1000;
@@ -597,6 +615,8 @@ int launch(ll_engine *e, const Params &p)
     e->ctrl_host->err_where = 0;
     e->ctrl_host->exit_reason = EXIT_NONE;
     e->ctrl_host->served = p.last_seq;
+    e->ctrl_host->passes = 0;
+    e->ctrl_host->rows = 0;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)e->grid, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -634,6 +654,8 @@ int reap(ll_engine *e)
         return LL_ERR_CUDA;
     }
     e->last_served = static_cast<ll_tick_header *>(e->mb_host)->seq_out;
+    e->passes += e->ctrl_host->passes;
+    e->rows += e->ctrl_host->rows;
     if (e->ctrl_host->status != LL_OK) {
         llh::set_error("resident kernel reported status %u at location 0x%x", e->ctrl_host->status,
                        e->ctrl_host->err_where);
@@ -959,6 +981,7 @@ int create_fast3(const ll_net_desc *net, const void *const *W, const float *cons
     e->max_batch = 1;
     e->kfn = f.fn;
     e->variant = 2;
+    e->micro_max = f.rows;
     e->weight_regs = f.K1 + f.K2 + f.K3;
     int rc = engine_common_create(e, &o);
     if (rc) {
@@ -1279,6 +1302,8 @@ int ll_engine_get_info(ll_engine *e, ll_engine_info *info)
         info->layer_modes[l] = e->base.L[l].mode;
     info->kernel_variant = e->variant;
     info->weight_regs = e->weight_regs;
+    info->passes = e->passes;
+    info->rows = e->rows;
     return LL_OK;
 }
 

@@ -63,7 +63,9 @@ struct EngineCtrl {
     volatile uint32_t served;
     volatile uint32_t exit_reason;
     volatile uint32_t launches;
-    volatile uint32_t pad[10];
+    volatile uint32_t passes;  // register-resident kernel, at exit: passes over the layers this launch
+    volatile uint32_t rows;    // ... and requests taken (more than passes when micro-batched)
+    volatile uint32_t pad[8];
 };
 
 struct Params {
@@ -99,6 +101,7 @@ struct Params {
     int32_t ring_slots;
     uint32_t ring_stride_f;
     uint32_t ring_base;
+    int32_t micro_batch;  // register-resident kernel: ring slots taken together (1 = one request)
     int32_t diag_wait_never;
     unsigned long long *trace;  // optional [trace_n][kTraceSlots] timeline of the first requests
     int32_t trace_n;

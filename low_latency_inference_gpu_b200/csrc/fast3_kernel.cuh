@@ -22,11 +22,18 @@
 // global scratch per thread, src/bench_persistent_mbyv_mlp.cu:159-221) and re-reads
 // the rest every tick; its layer barriers are global atomics (:308-377).
 #pragma once
+#include <type_traits>
 #include "engine_types.h"
 #include "ptx.cuh"
 #include "resident_kernel.cuh"
 
 namespace llk {
+
+// Rows one pass of the register-resident kernel can carry: requests taken together from
+// the ring (micro-batching); a pass over 2..4 rows runs the 4-row code.  Shapes whose
+// weights leave fewer than ~70 registers free (more than 56 weights per thread) carry one
+// row: the 4-row accumulators would spill.
+constexpr int kFast3Rows = 4;
 
 template <int IN, int H1, int H2, int OUT, int C>
 struct Fast3Shape {
@@ -45,6 +52,7 @@ struct Fast3Shape {
     static_assert(S1 <= 32 && S2 <= 32 && (S1 & (S1 - 1)) == 0 && (S2 & (S2 - 1)) == 0, "butterfly groups");
     static_assert(IN % 4 == 0, "x is moved in 16-byte pieces");
     static constexpr int NB = H1 + R2 + OUT;  // biases per CTA image
+    static constexpr int MaxRows = NW <= 56 ? kFast3Rows : 1;
 };
 
 __device__ __forceinline__ float relu_or(float v, int act)
@@ -56,11 +64,14 @@ template <int IN, int H1, int H2, int OUT, int C>
 __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_constant__ Params pg)
 {
     using S = Fast3Shape<IN, H1, H2, OUT, C>;
-    __shared__ __align__(16) float xs[IN];
-    __shared__ __align__(16) float h1[H1];
-    __shared__ __align__(16) float h2[S::R2];
-    __shared__ __align__(16) float gath[C * OUT];
-    __shared__ __align__(16) float yo[3 * ((OUT + 2) / 3) + 4];  // the output row, zero-padded
+    constexpr int MB = S::MaxRows;
+    constexpr int YO = 3 * ((OUT + 2) / 3) + 4;  // one output row, zero-padded
+    __shared__ __align__(16) float xs[MB * IN];
+    __shared__ __align__(16) float h1[MB * H1];
+    __shared__ __align__(16) float h2[MB * S::R2];
+    __shared__ __align__(16) float gath[MB * C * OUT];  // [row][rank][output]
+    __shared__ __align__(16) float yo[MB * YO];
+    __shared__ uint32_t rseq[MB];  // rank 0: sequence number of each row taken together
     __shared__ __align__(16) float bias[S::NB];
     __shared__ __align__(16) Shared sh;
     __shared__ __align__(16) Params sp;
@@ -83,6 +94,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
     const uint32_t bar_req = smem_u32(&sh.bar[5]);
     const uint32_t bar_g = smem_u32(&sh.bar[3]);
     const uint32_t bar_diag = smem_u32(&sh.bar[4]);
+    const uint32_t bar_x = smem_u32(&sh.bar[6]);
     const int act1 = p.L[0].act, act2 = p.L[1].act, act3 = p.L[2].act;
 
     if (tid == 0) {
@@ -111,9 +123,9 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
         w3[j] = ld_once_f32(img + (size_t)(S::K1 + S::K2 + j) * kThreads + tid);
     for (int i = tid; i < S::NB; i += kThreads)
         bias[i] = __ldg(img + (size_t)S::NW * kThreads + i);
-    for (int i = tid; i < C * OUT; i += kThreads)
+    for (int i = tid; i < MB * C * OUT; i += kThreads)
         gath[i] = 0.0f;
-    for (int i = tid; i < 3 * ((OUT + 2) / 3) + 4; i += kThreads)
+    for (int i = tid; i < MB * YO; i += kThreads)
         yo[i] = 0.0f;
     __syncthreads();
     cluster_sync();
@@ -127,10 +139,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
     const int r1 = tid / S::S1, s1 = tid % S::S1;
     const int r2 = tid / S::S2, s2 = tid % S::S2;
     const uint32_t x_addr = smem_u32(xs), h_addr = smem_u32(sh.hdr), g_addr = smem_u32(gath);
-    uint32_t last = p.last_seq, n_done = 0, ph_req = 0, ph_g = 0;
+    uint32_t last = p.last_seq, n_done = 0, ph_req = 0, ph_g = 0, ph_x = 0, passes = 0;
+    bool backlog = false;  // rank 0, warp 0: the host had posted beyond the last request taken
 
     while (ok) {
-        uint32_t seq;
+        uint32_t seq, nb = 1;
         if (p.mode == MODE_QUEUE && (int)n_done >= p.q_n)
             break;
         // ---------------- request ----------------
@@ -161,7 +174,28 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
         } else if (leader) {
             if (p.mailbox_format == 1) {
                 if (warp == 0) {
-                    const uint32_t c = poll_tagged(k, last, xs, ring_slot(p, n_done));  // x arrives with the doorbell
+                    // x arrives with the doorbell.  On a micro-batched ring the poll also reads
+                    // the host's seq_in (the last sequence number posted); when it is ahead of
+                    // the request just taken, requests are waiting, and the next pass takes up to
+                    // micro_batch of them with one read of their slots.  Otherwise (and when that
+                    // read finds nothing) the single-slot poll waits for the next request: a read
+                    // spanning several slots was measured ~2 us slower to see a new request.
+                    uint32_t c = 0, posted = 0;
+                    int got = 0;
+                    if constexpr (MB > 1) {
+                        if (backlog) {
+                            got = take_tagged_rows(k, last, xs, n_done, p.micro_batch, rseq, &posted);
+                            if (got > 0)
+                                c = seq_after(last, got);
+                        }
+                    }
+                    if (got == 0) {
+                        c = poll_tagged(k, last, xs, ring_slot(p, n_done), p.micro_batch > 1 ? &posted : nullptr);
+                        got = 1;
+                    }
+                    backlog = p.micro_batch > 1 && c != kCmdExit && (int32_t)(posted - c) > 0;
+                    if (tid == 0)
+                        sh.nrows = (uint32_t)got;
                     if (tid == 0) {
                         if (c == kCmdExit)
                             broadcast_abort(k);
@@ -180,6 +214,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
             if (seq == kCmdExit)
                 break;
+            if (p.mailbox_format == 1)
+                nb = *reinterpret_cast<volatile uint32_t *>(&sh.nrows);
             // batch 1: no header fetch (n_rows is 1; stop is seen on the idle cadence, so a
             // stop that comes with a doorbell bump costs one extra, harmless reply)
             if (p.mailbox_format == 0) {
@@ -189,16 +225,33 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             }
             if (tid == 0)
                 trace(k, n_done, 1);
-            // push {seq} + x to every peer: (C-1) * (1 + IN/4) st.async of 16 bytes, one mbarrier each
-            constexpr int per = 1 + IN / 4;
-            if (tid < (C - 1) * per) {
-                const uint32_t d = 1u + (uint32_t)(tid / per);
-                const int j = tid % per;
-                if (j == 0)
-                    st_async_v4(mapa(h_addr, d), make_float4(__uint_as_float(seq), 0.f, 0.f, 0.f), mapa(bar_req, d));
-                else
-                    st_async_v4(mapa(x_addr + (uint32_t)(j - 1) * 16u, d), reinterpret_cast<const float4 *>(xs)[j - 1],
-                                mapa(bar_req, d));
+            // push {seq, nb} + the nb rows of x to every peer: 16-byte st.async, (C-1) * (1 + nb*IN/4)
+            // in all; the header and row 0 complete the peer's request barrier, rows 1.. its x
+            // barrier (the peer learns nb from the header)
+            if (nb == 1) {
+                constexpr int per = 1 + IN / 4;
+                if (tid < (C - 1) * per) {
+                    const uint32_t d = 1u + (uint32_t)(tid / per);
+                    const int j = tid % per;
+                    if (j == 0)
+                        st_async_v4(mapa(h_addr, d), make_float4(__uint_as_float(seq), __uint_as_float(1u), 0.f, 0.f),
+                                    mapa(bar_req, d));
+                    else
+                        st_async_v4(mapa(x_addr + (uint32_t)(j - 1) * 16u, d),
+                                    reinterpret_cast<const float4 *>(xs)[j - 1], mapa(bar_req, d));
+                }
+            } else {
+                const int per = 1 + (int)nb * (IN / 4);
+                for (int t = tid; t < (C - 1) * per; t += kThreads) {
+                    const uint32_t d = 1u + (uint32_t)(t / per);
+                    const int j = t % per;
+                    if (j == 0)
+                        st_async_v4(mapa(h_addr, d), make_float4(__uint_as_float(seq), __uint_as_float(nb), 0.f, 0.f),
+                                    mapa(bar_req, d));
+                    else
+                        st_async_v4(mapa(x_addr + (uint32_t)(j - 1) * 16u, d),
+                                    reinterpret_cast<const float4 *>(xs)[j - 1], mapa(j <= IN / 4 ? bar_req : bar_x, d));
+                }
             }
             if (tid == 0)
                 trace(k, n_done, 2);
@@ -209,135 +262,187 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                 break;
             ++ph_req;
             seq = *reinterpret_cast<volatile uint32_t *>(&sh.hdr[0]);
+            nb = *reinterpret_cast<volatile uint32_t *>(&sh.hdr[1]);
+            nb = nb < 1u ? 1u : (nb > (uint32_t)MB ? (uint32_t)MB : nb);
+            if (nb > 1) {
+                if (tid == 0)
+                    mbar_arrive_expect_tx(bar_x, 4u * IN * (nb - 1));
+                if (!cta_wait_bar(k, bar_x, ph_x & 1u, EW_PEER_POLL, p.step_ns))
+                    break;
+                ++ph_x;
+            }
             if (tid == 0 && k.rank == 1)
                 trace(k, n_done, 15);
         }
 
-        // ---------------- layer 1 (replicated) ----------------
-        {
-            const float4 *x4 = reinterpret_cast<const float4 *>(xs) + s1;
-            float a0 = 0.f, a1 = 0.f;
+        // ---------------- the layers, over nb rows (weights used once per row) ----------------
+        auto pass = [&](auto rows) -> bool {
+            constexpr int NB = decltype(rows)::value;
+            // ---------------- layer 1 (replicated) ----------------
+            {
+                const float4 *x4 = reinterpret_cast<const float4 *>(xs) + s1;
+                float a0[NB], a1[NB];
 #pragma unroll
-            for (int j = 0; j < S::K1 / 4; ++j) {
-                const float4 v = x4[j * S::S1];
-                a0 = fmaf(w1[4 * j], v.x, a0);
-                a1 = fmaf(w1[4 * j + 1], v.y, a1);
-                a0 = fmaf(w1[4 * j + 2], v.z, a0);
-                a1 = fmaf(w1[4 * j + 3], v.w, a1);
-            }
-            float acc = a0 + a1;
+                for (int r = 0; r < NB; ++r)
+                    a0[r] = a1[r] = 0.f;
 #pragma unroll
-            for (int o = S::S1 / 2; o > 0; o >>= 1)
-                acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            if (s1 == 0)
-                h1[r1] = relu_or(acc + bias[r1], act1);
-        }
-        __syncthreads();
-        if (leader && tid == 0)
-            trace(k, n_done, 3);
-        // ---------------- layer 2 (rows split over the cluster) ----------------
-        {
-            const float4 *v4 = reinterpret_cast<const float4 *>(h1) + s2;
-            float a0 = 0.f, a1 = 0.f;
+                for (int j = 0; j < S::K1 / 4; ++j) {
 #pragma unroll
-            for (int j = 0; j < S::K2 / 4; ++j) {
-                const float4 v = v4[j * S::S2];
-                a0 = fmaf(w2[4 * j], v.x, a0);
-                a1 = fmaf(w2[4 * j + 1], v.y, a1);
-                a0 = fmaf(w2[4 * j + 2], v.z, a0);
-                a1 = fmaf(w2[4 * j + 3], v.w, a1);
-            }
-            float acc = a0 + a1;
-#pragma unroll
-            for (int o = S::S2 / 2; o > 0; o >>= 1)
-                acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            if (s2 == 0)
-                h2[r2] = relu_or(acc + bias[H1 + r2], act2);
-        }
-        if (own_x && !leader) {
-            // rank 0's go for this request (sent while layers 1-2 ran); ends on its abort
-            if (!cta_wait_bar(k, bar_req, ph_req & 1u, EW_PEER_POLL, p.step_ns))
-                break;
-            ++ph_req;
-        } else {
-            __syncthreads();
-        }
-        if (leader && tid == 0)
-            trace(k, n_done, 4);
-        // ---------------- layer 3 (K-split partials -> rank 0) ----------------
-        if (warp < OUT) {
-            float acc = 0.f;
-#pragma unroll
-            for (int j = 0; j < S::K3; ++j)
-                acc = fmaf(w3[j], h2[lane + 32 * j], acc);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-                acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            if (lane == 0)
-                st_async_u32(mapa(g_addr + (uint32_t)(k.rank * OUT + warp) * 4u, 0u), __float_as_uint(acc),
-                             mapa(bar_g, 0u));
-        }
-        if (leader && tid == 0)
-            trace(k, n_done, 5);
-
-        // ---------------- rank 0: sum partials, write y, publish ----------------
-        if (leader) {
-            if (tid == 0)
-                mbar_arrive_expect_tx(bar_g, (uint32_t)(C * OUT * 4));
-            ok = cta_wait_bar(k, bar_g, ph_g & 1u, EW_GATHER, p.step_ns);
-            ++ph_g;
-            if (!ok)
-                break;
-            if (tid == 0)
-                trace(k, n_done, 12);
-            if (warp == 0) {
-                // the output row goes through shared memory: lanes < OUT finish one output
-                // each, then the storing lanes pick up their 16-byte groups (full-warp
-                // shuffles here cost ~1650 cycles in this loop, the shared-memory round ~60)
-                if (lane < OUT) {
-                    float v = 0.f;
-#pragma unroll
-                    for (int c = 0; c < C; ++c)
-                        v += gath[c * OUT + lane];
-                    yo[lane] = relu_or(v + bias[H1 + S::R2 + lane], act3);
-                }
-                __syncwarp();
-                const bool tagged = p.mode == MODE_MAILBOX && p.mailbox_format == 1;
-                // tagged output: lane c packs {y[3c], y[3c+1], y[3c+2], seq}
-                constexpr int NYC = (OUT + 2) / 3;
-                if (tagged) {
-                    if (lane < NYC)
-                        st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done) * p.ring_stride_f + 4 * lane,
-                                          make_float4(yo[3 * lane], yo[3 * lane + 1], yo[3 * lane + 2],
-                                                      __uint_as_float(seq)));
-                } else if (lane < OUT / 4) {
-                    const float4 q = reinterpret_cast<const float4 *>(yo)[lane];
-                    if (p.mode == MODE_QUEUE)
-                        reinterpret_cast<float4 *>(p.q_y + (size_t)n_done * OUT)[lane] = q;
-                    else
-                        st_relaxed_sys_v4(p.mb_y + 4 * lane, q);
-                }
-                __syncwarp();
-                if (lane == 0) {
-                    trace(k, n_done, 13);
-                    if (p.mode == MODE_QUEUE) {
-                        if (p.q_stamp)
-                            p.q_stamp[n_done] = globaltimer();
-                    } else if (tagged) {
-                        st_relaxed_sys_u32(&p.mb->seq_out, seq);  // bookkeeping only: the host waits on the tags
-                    } else {
-                        st_release_sys_u32(&p.mb->seq_out, seq);
+                    for (int r = 0; r < NB; ++r) {
+                        const float4 v = x4[r * (IN / 4) + j * S::S1];
+                        a0[r] = fmaf(w1[4 * j], v.x, a0[r]);
+                        a1[r] = fmaf(w1[4 * j + 1], v.y, a1[r]);
+                        a0[r] = fmaf(w1[4 * j + 2], v.z, a0[r]);
+                        a1[r] = fmaf(w1[4 * j + 3], v.w, a1[r]);
                     }
-                    trace(k, n_done, 14);
+                }
+#pragma unroll
+                for (int r = 0; r < NB; ++r) {
+                    float acc = a0[r] + a1[r];
+#pragma unroll
+                    for (int o = S::S1 / 2; o > 0; o >>= 1)
+                        acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                    if (s1 == 0)
+                        h1[r * H1 + r1] = relu_or(acc + bias[r1], act1);
                 }
             }
-        }
+            __syncthreads();
+            if (leader && tid == 0)
+                trace(k, n_done, 3);
+            // ---------------- layer 2 (rows split over the cluster) ----------------
+            {
+                const float4 *v4 = reinterpret_cast<const float4 *>(h1) + s2;
+                float a0[NB], a1[NB];
+#pragma unroll
+                for (int r = 0; r < NB; ++r)
+                    a0[r] = a1[r] = 0.f;
+#pragma unroll
+                for (int j = 0; j < S::K2 / 4; ++j) {
+#pragma unroll
+                    for (int r = 0; r < NB; ++r) {
+                        const float4 v = v4[r * (H1 / 4) + j * S::S2];
+                        a0[r] = fmaf(w2[4 * j], v.x, a0[r]);
+                        a1[r] = fmaf(w2[4 * j + 1], v.y, a1[r]);
+                        a0[r] = fmaf(w2[4 * j + 2], v.z, a0[r]);
+                        a1[r] = fmaf(w2[4 * j + 3], v.w, a1[r]);
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < NB; ++r) {
+                    float acc = a0[r] + a1[r];
+#pragma unroll
+                    for (int o = S::S2 / 2; o > 0; o >>= 1)
+                        acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                    if (s2 == 0)
+                        h2[r * S::R2 + r2] = relu_or(acc + bias[H1 + r2], act2);
+                }
+            }
+            if (own_x && !leader) {
+                // rank 0's go for this request (sent while layers 1-2 ran); ends on its abort
+                if (!cta_wait_bar(k, bar_req, ph_req & 1u, EW_PEER_POLL, p.step_ns))
+                    return false;
+                ++ph_req;
+            } else {
+                __syncthreads();
+            }
+            if (leader && tid == 0)
+                trace(k, n_done, 4);
+            // ---------------- layer 3 (K-split partials -> rank 0) ----------------
+            if (warp < OUT) {
+                float mine = 0.f;  // lane r sends row r's partial
+#pragma unroll
+                for (int r = 0; r < NB; ++r) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int j = 0; j < S::K3; ++j)
+                        acc = fmaf(w3[j], h2[r * S::R2 + lane + 32 * j], acc);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1)
+                        acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                    if (lane == r)
+                        mine = acc;
+                }
+                if (lane < (int)nb)
+                    st_async_u32(mapa(g_addr + (uint32_t)((lane * C + k.rank) * OUT + warp) * 4u, 0u),
+                                 __float_as_uint(mine), mapa(bar_g, 0u));
+            }
+            if (leader && tid == 0)
+                trace(k, n_done, 5);
+
+            // ---------------- rank 0: sum partials, write y, publish ----------------
+            if (leader) {
+                if (tid == 0)
+                    mbar_arrive_expect_tx(bar_g, (uint32_t)(C * OUT * 4) * nb);
+                const bool got = cta_wait_bar(k, bar_g, ph_g & 1u, EW_GATHER, p.step_ns);
+                ++ph_g;
+                if (!got)
+                    return false;
+                if (tid == 0)
+                    trace(k, n_done, 12);
+                if (warp < (int)nb) {
+                    // warp r finishes row r.  The output row goes through shared memory: lanes
+                    // < OUT finish one output each, then the storing lanes pick up their 16-byte
+                    // groups (full-warp shuffles here cost ~1650 cycles in this loop, the
+                    // shared-memory round ~60)
+                    const int r = NB == 1 ? 0 : warp;
+                    float *yr = yo + r * YO;
+                    if (lane < OUT) {
+                        float v = 0.f;
+#pragma unroll
+                        for (int c = 0; c < C; ++c)
+                            v += gath[(r * C + c) * OUT + lane];
+                        yr[lane] = relu_or(v + bias[H1 + S::R2 + lane], act3);
+                    }
+                    __syncwarp();
+                    const bool tagged = p.mode == MODE_MAILBOX && p.mailbox_format == 1;
+                    // tagged output: lane c packs {y[3c], y[3c+1], y[3c+2], seq}
+                    constexpr int NYC = (OUT + 2) / 3;
+                    if (tagged) {
+                        const uint32_t sq = NB == 1 ? seq : rseq[r];
+                        if (lane < NYC)
+                            st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done + (uint32_t)r) * p.ring_stride_f +
+                                                  4 * lane,
+                                              make_float4(yr[3 * lane], yr[3 * lane + 1], yr[3 * lane + 2],
+                                                          __uint_as_float(sq)));
+                    } else if (lane < OUT / 4) {
+                        const float4 q = reinterpret_cast<const float4 *>(yr)[lane];
+                        if (p.mode == MODE_QUEUE)
+                            reinterpret_cast<float4 *>(p.q_y + (size_t)n_done * OUT)[lane] = q;
+                        else
+                            st_relaxed_sys_v4(p.mb_y + 4 * lane, q);
+                    }
+                    __syncwarp();
+                    if (warp == 0 && lane == 0) {
+                        trace(k, n_done, 13);
+                        if (p.mode == MODE_QUEUE) {
+                            if (p.q_stamp)
+                                p.q_stamp[n_done] = globaltimer();
+                        } else if (tagged) {
+                            st_relaxed_sys_u32(&p.mb->seq_out, seq);  // bookkeeping only: the host waits on the tags
+                        } else {
+                            st_release_sys_u32(&p.mb->seq_out, seq);
+                        }
+                        trace(k, n_done, 14);
+                    }
+                }
+            }
+            return true;
+        };
+        if constexpr (MB == 1)
+            ok = pass(std::integral_constant<int, 1>{});
+        else
+            ok = nb == 1 ? pass(std::integral_constant<int, 1>{}) : pass(std::integral_constant<int, MB>{});
+        if (!ok)
+            break;
+        ++passes;
         last = seq;
-        ++n_done;
+        n_done += nb;
     }
     __syncthreads();
     cluster_sync();
     if (leader && tid == 0) {
+        st_relaxed_sys_u32(&p.ctrl->passes, passes);
+        st_relaxed_sys_u32(&p.ctrl->rows, n_done);
         if (p.mode == MODE_QUEUE)
             st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_QUEUE_DONE);
         st_release_sys_u32(&p.ctrl->state, ST_EXITED);

@@ -286,7 +286,12 @@ __device__ __forceinline__ uint32_t ring_slot(const Params &p, uint32_t n)
     return p.ring_slots > 1 ? (p.ring_base + n) % (uint32_t)p.ring_slots : 0u;
 }
 
-__device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uint32_t slot)
+//
+// `posted` (optional, micro-batched rings): lane 31 also reads the host's seq_in word (the
+// last sequence number it posted; bookkeeping in the tagged format) in the same round trip,
+// and *posted gets the value seen with the request, so the caller knows whether more
+// requests are waiting behind it.
+__device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uint32_t slot, uint32_t *posted = nullptr)
 {
     const Params &p = *k.p;
     const int lane = threadIdx.x & 31;
@@ -300,6 +305,9 @@ __device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uin
         for (int j = 0; j < kTagChunksPerLane; ++j)
             if (lane + 32 * j < nxc)
                 c[j] = ld_relaxed_sys_v4_u32(reinterpret_cast<const unsigned *>(chunks + lane + 32 * j));
+        uint32_t seen = 0;
+        if (posted && lane == 31)
+            seen = ld_relaxed_sys(&p.mb->seq_in);
         const uint32_t tag = __shfl_sync(0xffffffffu, c[0].w, 0);
         bool same = true;
 #pragma unroll
@@ -318,6 +326,8 @@ __device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uin
                             X[3 * ch + e] = p.act_bf16 ? round_bf16(v[e]) : v[e];
                 }
             }
+            if (posted)
+                *posted = __shfl_sync(0xffffffffu, seen, 31);
             return tag;
         }
         if ((it & 63u) == 63u) {
@@ -337,6 +347,68 @@ __device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uin
                 return kCmdExit;
         }
     }
+}
+
+// The sequence number m requests after `last` (m >= 1).
+__device__ __forceinline__ uint32_t seq_after(uint32_t last, int m)
+{
+    uint32_t s = last;
+    for (int i = 0; i < m; ++i)
+        s = next_seq_dev(s);
+    return s;
+}
+
+// Tagged request ring, micro-batched (warp 0 of the dispatcher): ONE read of the ring
+// slots of requests n .. n+maxb-1 of this launch (slot ring_slot(n + i)), taking every
+// request that is complete and follows without a gap: slot n+i is taken when each of its
+// chunks carries the (i+1)-th sequence number after `last`.  One PCIe round trip reads all
+// maxb slots (maxb * nxc <= 32 * kTagChunksPerLane chunks, checked on the host).  Row i of
+// x goes to X + i * in_dim and its sequence number to seqs[i]; *posted = the host's seq_in
+// word (the last sequence number it posted), read by lane 31 in the same round trip.
+// Returns the rows taken
+// (0 when request n is not complete yet; then the caller waits on its slot alone with
+// poll_tagged, whose single-slot round trips are shorter: a read that spans several slots
+// was measured ~2 us slower to detect a new request).
+__device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uint32_t n, int maxb, uint32_t *seqs,
+                                uint32_t *posted)
+{
+    const Params &p = *k.p;
+    const int lane = threadIdx.x & 31;
+    const int nxc = (p.in_dim + 2) / 3;
+    const int total = maxb * nxc;
+    uint4 c[kTagChunksPerLane];
+    int row[kTagChunksPerLane], ch[kTagChunksPerLane];
+#pragma unroll
+    for (int j = 0; j < kTagChunksPerLane; ++j) {
+        const int q = lane + 32 * j;
+        row[j] = q < total ? q / nxc : 0;
+        ch[j] = q - row[j] * nxc;
+        if (q < total)
+            c[j] = ld_relaxed_sys_v4_u32(reinterpret_cast<const unsigned *>(
+                p.mb_x + (size_t)ring_slot(p, n + (uint32_t)row[j]) * p.ring_stride_f + 4 * ch[j]));
+    }
+    const uint32_t seen = lane == 31 ? ld_relaxed_sys(&p.mb->seq_in) : 0u;
+    *posted = __shfl_sync(0xffffffffu, seen, 31);
+    uint32_t bad = 0;
+#pragma unroll
+    for (int j = 0; j < kTagChunksPerLane; ++j)
+        if (lane + 32 * j < total && c[j].w != seq_after(last, row[j] + 1))
+            bad |= 1u << row[j];
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    const int nb = __ffs(bad | (1u << maxb)) - 1;  // complete slots before the first gap
+#pragma unroll
+    for (int j = 0; j < kTagChunksPerLane; ++j) {
+        if (lane + 32 * j < total && row[j] < nb) {
+            const float v[3] = {__uint_as_float(c[j].x), __uint_as_float(c[j].y), __uint_as_float(c[j].z)};
+#pragma unroll
+            for (int e = 0; e < 3; ++e)
+                if (3 * ch[j] + e < p.in_dim)
+                    X[row[j] * p.in_dim + 3 * ch[j] + e] = p.act_bf16 ? round_bf16(v[e]) : v[e];
+        }
+    }
+    if (lane < nb)
+        seqs[lane] = seq_after(last, lane + 1);
+    return nb;
 }
 
 // One thread reads the 16-byte header after the doorbell: stop flag and row count.

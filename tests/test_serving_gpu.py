@@ -78,3 +78,66 @@ def test_poisson_stream_is_split_across_ranks_and_fully_served(cfg0):
         assert np.all(np.isfinite(a)) and a.min() > 0.5 and np.median(a) < 1000
     # 100k requests/s over 3000 requests is a 30 ms stream
     assert 0.025 < el < 0.5
+
+
+def test_micro_batched_ring_matches_single_requests(cfg0):
+    # requests taken together from the ring run the same FMA sequence per row as one request
+    # alone, so the replies are bit-identical to single requests (and within 1e-5 of the oracle)
+    net, Ws, bs, xs, ref = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts()) as one:
+        single = [one.infer(xs[i])[0] for i in range(45)]
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=8, micro_batch=4)) as e:
+        assert e.info().kernel_variant == 2
+        n = 0
+        for burst in (8, 1, 5, 3, 8, 7, 2, 6):  # ragged bursts; the ring wraps five times
+            seqs = [e.submit(xs[n + i]) for i in range(burst)]
+            order = range(burst) if burst % 2 else reversed(range(burst))
+            for i in order:
+                y = e.poll(seqs[i])[0]
+                assert np.array_equal(y, single[n + i])
+                assert rel_err(y, ref[n + i]) <= 1e-5
+            n += burst
+        for i in range(n, n + 5):  # single requests on the same engine
+            assert np.array_equal(e.infer(xs[i])[0], single[i])
+        e.stop()
+        inf = e.info()
+        assert inf.status == ll.LL_OK
+        assert inf.rows == n + 5
+        assert inf.passes < inf.rows  # bursts of 8 were taken several requests per pass
+
+
+def test_micro_batched_ring_survives_idle_relaunch(cfg0):
+    net, Ws, bs, xs, ref = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=4, micro_batch=4, idle_timeout_ns=30_000_000)) as e:
+        n = 0
+        for rnd in range(3):
+            seqs = [e.submit(xs[n + i]) for i in range(4)]
+            for i, s in enumerate(seqs):
+                assert rel_err(e.poll(s)[0], ref[n + i]) <= 1e-5
+            n += 4
+            time.sleep(0.15)  # the kernel leaves after 30 ms idle; the next submit relaunches it
+        assert e.info().launches >= 3
+        for i in range(n, n + 5):
+            assert rel_err(e.infer(xs[i])[0], ref[i]) <= 1e-5
+
+
+@pytest.mark.parametrize("kw", [dict(ring_slots=2, micro_batch=4),       # more rows than slots
+                                dict(ring_slots=8, micro_batch=5),       # more than one pass carries
+                                dict(ring_slots=8, micro_batch=4, kernel_variant=1),  # generic kernel
+                                dict(ring_slots=8, micro_batch=4, cluster_size=4)])   # 66 weights/thread: 1 row
+def test_micro_batch_is_refused_where_it_cannot_run(cfg0, kw):
+    net, Ws, bs, _, _ = cfg0
+    with pytest.raises(ll.LLError) as e:
+        ll.Engine(net, Ws, bs, opts=opts(**kw))
+    assert e.value.code == ll.LL_ERR_UNSUPPORTED
+
+
+def test_micro_batched_poisson_stream_is_fully_served(cfg0):
+    net, Ws, bs, xs, _ = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=8, micro_batch=4)) as e:
+        lat, el = e.serve_poisson(xs, 20000, 1_000_000.0, seed=5)
+        e.stop()
+        inf = e.info()
+        assert inf.status == ll.LL_OK
+    assert len(lat) == 20000 and np.all(np.isfinite(lat)) and lat.min() > 0.5
+    assert inf.passes < inf.rows  # an overloaded stream keeps the ring full: several rows per pass
