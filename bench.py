@@ -27,8 +27,9 @@ Reported:
           (L2 flushed between forwards; kernel-only and end-to-end with pinned
           host copies).
   serving open-loop Poisson arrivals at 50k / 200k / 1M requests/s aggregate over the
-          N GPUs (config-0 MLP on every GPU, 8-slot tagged request ring): p50/p99
-          latency from the scheduled arrival and sustained throughput.
+          N GPUs (config-0 MLP on every GPU, 8-slot tagged request ring, up to 4
+          waiting requests per kernel pass): p50/p99 latency from the scheduled
+          arrival, sustained throughput and requests per pass.
   --impl reference  runs the reference's CPU forward on all host cores instead.
 """
 import argparse
@@ -105,35 +106,48 @@ def merge_serving(per_rank, rate, n_total):
     """One line for one arrival rate from every rank's (latencies in us, elapsed s): latency
     percentiles over the merged requests of all ranks (from the scheduled arrival),
     sustained throughput = all requests served / the slowest rank's elapsed time."""
-    lat = np.concatenate([np.asarray(l, np.float64) for l, _ in per_rank]) if per_rank else np.array([])
+    lat = np.concatenate([np.asarray(r[0], np.float64) for r in per_rank]) if per_rank else np.array([])
     served = int(lat.size)
-    elapsed = max(e for _, e in per_rank) if per_rank else float("nan")
+    elapsed = max(r[1] for r in per_rank) if per_rank else float("nan")
     q = np.percentile(lat, [50, 90, 99, 99.9]) if served else [float("nan")] * 4
-    return {"offered_per_s": rate, "requests": n_total, "served": served,
-            "sustained_per_s": served / elapsed if elapsed > 0 else float("nan"),
-            "p50_us": float(q[0]), "p90_us": float(q[1]), "p99_us": float(q[2]), "p999_us": float(q[3]),
-            "per_rank_served": [int(len(l)) for l, _ in per_rank]}
+    out = {"offered_per_s": rate, "requests": n_total, "served": served,
+           "sustained_per_s": served / elapsed if elapsed > 0 else float("nan"),
+           "p50_us": float(q[0]), "p90_us": float(q[1]), "p99_us": float(q[2]), "p999_us": float(q[3]),
+           "per_rank_served": [int(len(r[0])) for r in per_rank]}
+    if per_rank and len(per_rank[0]) > 2:  # (rows, passes) of the device: requests per kernel pass
+        rows, passes = sum(r[2] for r in per_rank), sum(r[3] for r in per_rank)
+        out["requests_per_pass"] = rows / passes if passes else float("nan")
+    return out
 
 
 def run_serving(ll, net, Ws, bs, xs, rank, world, hg, dev):
     """Open-loop Poisson streams (seed 5) over all ranks: each rank serves the requests drawn
-    for it through its own engine (tagged mailbox, 8-slot ring); latency from the scheduled
-    arrival; merged on rank 0."""
+    for it through its own engine (tagged mailbox, 8-slot ring, up to 4 waiting requests
+    taken per kernel pass); latency from the scheduled arrival; merged on rank 0.  The
+    resident kernel is stopped after each stream so that its pass / request counters are
+    read (the next stream relaunches it before its first arrival)."""
     o = ll.default_opts()
     o.mailbox_format = 1
     o.ring_slots = 8
+    o.micro_batch = 4
     out = []
     with ll.Engine(net, Ws, bs, device=dev, opts=o) as e:
         e.serve_poisson(xs, 2000, 50_000.0, seed=99, rank=rank, world=world)  # warm-up stream
+        e.stop()
         for rate in SERVING_RATES:
             n_total = int(rate * SERVING_SECONDS)
             hg.barrier()
+            i0 = e.info()
+            e.infer(xs[0])  # relaunch outside the stream
             lat, el = e.serve_poisson(xs, n_total, rate, seed=5, rank=rank, world=world)
-            per_rank = hg.gather((lat.tolist(), el))
+            e.stop()
+            i1 = e.info()
+            per_rank = hg.gather((lat.tolist(), el, i1.rows - i0.rows, i1.passes - i0.passes))
             out.append(merge_serving(per_rank, rate, n_total))
     return {"workload": "config-0 MLP replicated per GPU, Poisson arrivals (std::mt19937_64 seed 5), "
                         "each request to a GPU drawn uniformly; U[-1,1] inputs",
-            "mailbox": "tagged, 8-slot request ring", "seconds_of_arrivals": SERVING_SECONDS, "rates": out}
+            "mailbox": "tagged, 8-slot request ring, micro_batch 4", "seconds_of_arrivals": SERVING_SECONDS,
+            "rates": out}
 
 
 def run_config1(ll, torch, dev):

@@ -72,6 +72,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
     __shared__ __align__(16) float gath[MB * C * OUT];  // [row][rank][output]
     __shared__ __align__(16) float yo[MB * YO];
     __shared__ uint32_t rseq[MB];  // rank 0: sequence number of each row taken together
+    constexpr int NXC = (IN + 2) / 3;  // tagged chunks per row
+    __shared__ __align__(16) uint4 xch[MB * NXC];  // peers: the tagged chunks rank 0 forwards
     __shared__ __align__(16) float bias[S::NB];
     __shared__ __align__(16) Shared sh;
     __shared__ __align__(16) Params sp;
@@ -180,17 +182,22 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     // micro_batch of them with one read of their slots.  Otherwise (and when that
                     // read finds nothing) the single-slot poll waits for the next request: a read
                     // spanning several slots was measured ~2 us slower to see a new request.
+                    // The polling lanes forward the raw chunks to the peers from registers as
+                    // soon as the tags match (header {seq, rows} + row 0 on the peers' request
+                    // barrier, rows 1.. on their x barrier).
+                    const ChunkFwd fwd{smem_u32(xch), h_addr, bar_req, bar_x, C - 1};
                     uint32_t c = 0, posted = 0;
                     int got = 0;
                     if constexpr (MB > 1) {
                         if (backlog) {
-                            got = take_tagged_rows(k, last, xs, n_done, p.micro_batch, rseq, &posted);
+                            got = take_tagged_rows(k, last, xs, n_done, p.micro_batch, rseq, &posted, &fwd);
                             if (got > 0)
                                 c = seq_after(last, got);
                         }
                     }
                     if (got == 0) {
-                        c = poll_tagged(k, last, xs, ring_slot(p, n_done), p.micro_batch > 1 ? &posted : nullptr);
+                        c = poll_tagged(k, last, xs, ring_slot(p, n_done), p.micro_batch > 1 ? &posted : nullptr,
+                                        &fwd);
                         got = 1;
                     }
                     backlog = p.micro_batch > 1 && c != kCmdExit && (int32_t)(posted - c) > 0;
@@ -225,10 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             }
             if (tid == 0)
                 trace(k, n_done, 1);
-            // push {seq, nb} + the nb rows of x to every peer: 16-byte st.async, (C-1) * (1 + nb*IN/4)
-            // in all; the header and row 0 complete the peer's request barrier, rows 1.. its x
-            // barrier (the peer learns nb from the header)
-            if (nb == 1) {
+            if (p.mailbox_format == 0) {
+                // the TickBuffer: push {seq, 1} + x to every peer, (C-1) * (1 + IN/4) st.async of
+                // 16 bytes completing the peer's request barrier
                 constexpr int per = 1 + IN / 4;
                 if (tid < (C - 1) * per) {
                     const uint32_t d = 1u + (uint32_t)(tid / per);
@@ -240,24 +246,16 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                         st_async_v4(mapa(x_addr + (uint32_t)(j - 1) * 16u, d),
                                     reinterpret_cast<const float4 *>(xs)[j - 1], mapa(bar_req, d));
                 }
-            } else {
-                const int per = 1 + (int)nb * (IN / 4);
-                for (int t = tid; t < (C - 1) * per; t += kThreads) {
-                    const uint32_t d = 1u + (uint32_t)(t / per);
-                    const int j = t % per;
-                    if (j == 0)
-                        st_async_v4(mapa(h_addr, d), make_float4(__uint_as_float(seq), __uint_as_float(nb), 0.f, 0.f),
-                                    mapa(bar_req, d));
-                    else
-                        st_async_v4(mapa(x_addr + (uint32_t)(j - 1) * 16u, d),
-                                    reinterpret_cast<const float4 *>(xs)[j - 1], mapa(j <= IN / 4 ? bar_req : bar_x, d));
-                }
             }
             if (tid == 0)
                 trace(k, n_done, 2);
         } else {
+            // a peer: the header + row 0 (tagged chunks, or the TickBuffer's float rows), then
+            // rows 1.. of a micro-batch
+            const bool chunks = p.mailbox_format == 1;
+            const uint32_t row_bytes = chunks ? 16u * NXC : 4u * IN;
             if (tid == 0)
-                mbar_arrive_expect_tx(bar_req, 16u + 4u * IN);
+                mbar_arrive_expect_tx(bar_req, 16u + row_bytes);
             if (!cta_wait_bar(k, bar_req, ph_req & 1u, EW_PEER_POLL, p.idle_ns + p.peer_margin_ns))
                 break;
             ++ph_req;
@@ -266,10 +264,24 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             nb = nb < 1u ? 1u : (nb > (uint32_t)MB ? (uint32_t)MB : nb);
             if (nb > 1) {
                 if (tid == 0)
-                    mbar_arrive_expect_tx(bar_x, 4u * IN * (nb - 1));
+                    mbar_arrive_expect_tx(bar_x, row_bytes * (nb - 1));
                 if (!cta_wait_bar(k, bar_x, ph_x & 1u, EW_PEER_POLL, p.step_ns))
                     break;
                 ++ph_x;
+            }
+            if (chunks) {
+                // unpack {v0, v1, v2, tag} chunks into the x rows
+                for (int t = tid; t < (int)nb * NXC; t += kThreads) {
+                    const int r = t / NXC, ch = t - r * NXC;
+                    const uint4 v = xch[t];
+                    float *dst = xs + r * IN + 3 * ch;
+                    dst[0] = __uint_as_float(v.x);
+                    if (3 * ch + 1 < IN)
+                        dst[1] = __uint_as_float(v.y);
+                    if (3 * ch + 2 < IN)
+                        dst[2] = __uint_as_float(v.z);
+                }
+                __syncthreads();
             }
             if (tid == 0 && k.rank == 1)
                 trace(k, n_done, 15);

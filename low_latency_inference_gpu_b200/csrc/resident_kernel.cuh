@@ -286,12 +286,42 @@ __device__ __forceinline__ uint32_t ring_slot(const Params &p, uint32_t n)
     return p.ring_slots > 1 ? (p.ring_base + n) % (uint32_t)p.ring_slots : 0u;
 }
 
-//
+// Forwarding of the raw tagged chunks to the other CTAs of a cluster (register-resident
+// kernel): the polling lanes push the chunks they hold straight from registers, so the
+// peers' copy of x leaves the moment the tags match.  Chunk ch of row r goes to the shared
+// address chunks + 16 * (r * nxc + ch) of ranks 1..peers and completes their barrier
+// bar_first (row 0) or bar_rest (rows 1..); lane 0 adds a 16-byte header {seq, rows} at hdr
+// (on bar_first).  Every address is the same offset in each CTA (mapa).
+struct ChunkFwd {
+    uint32_t chunks, hdr, bar_first, bar_rest;
+    int peers;
+};
+
+__device__ __forceinline__ void fwd_chunk(const ChunkFwd &f, int row, int ch, int nxc, uint4 c)
+{
+    const float4 v = make_float4(__uint_as_float(c.x), __uint_as_float(c.y), __uint_as_float(c.z), __uint_as_float(c.w));
+    const uint32_t a = f.chunks + 16u * (uint32_t)(row * nxc + ch);
+    const uint32_t b = row == 0 ? f.bar_first : f.bar_rest;
+    for (int d = 1; d <= f.peers; ++d)
+        st_async_v4(mapa(a, (uint32_t)d), v, mapa(b, (uint32_t)d));
+}
+
+__device__ __forceinline__ void fwd_header(const ChunkFwd &f, uint32_t seq, uint32_t rows)
+{
+    for (int d = 1; d <= f.peers; ++d)
+        st_async_v4(mapa(f.hdr, (uint32_t)d), make_float4(__uint_as_float(seq), __uint_as_float(rows), 0.f, 0.f),
+                    mapa(f.bar_first, (uint32_t)d));
+}
+
+// Warp 0 waits for the next request in a tagged ring slot (the single-slot poll) and
+// unpacks x into X.
 // `posted` (optional, micro-batched rings): lane 31 also reads the host's seq_in word (the
 // last sequence number it posted; bookkeeping in the tagged format) in the same round trip,
 // and *posted gets the value seen with the request, so the caller knows whether more
 // requests are waiting behind it.
-__device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uint32_t slot, uint32_t *posted = nullptr)
+// `fwd` (optional): forward the request's chunks to the cluster's other CTAs (ChunkFwd).
+__device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uint32_t slot, uint32_t *posted = nullptr,
+                                const ChunkFwd *fwd = nullptr)
 {
     const Params &p = *k.p;
     const int lane = threadIdx.x & 31;
@@ -315,6 +345,14 @@ __device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uin
             if (lane + 32 * j < nxc && c[j].w != tag)
                 same = false;
         if (__all_sync(0xffffffffu, same) && tag == want) {
+            if (fwd) {
+#pragma unroll
+                for (int j = 0; j < kTagChunksPerLane; ++j)
+                    if (lane + 32 * j < nxc)
+                        fwd_chunk(*fwd, 0, lane + 32 * j, nxc, c[j]);
+                if (lane == 0)
+                    fwd_header(*fwd, tag, 1u);
+            }
 #pragma unroll
             for (int j = 0; j < kTagChunksPerLane; ++j) {
                 const int ch = lane + 32 * j;
@@ -370,7 +408,7 @@ __device__ __forceinline__ uint32_t seq_after(uint32_t last, int m)
 // poll_tagged, whose single-slot round trips are shorter: a read that spans several slots
 // was measured ~2 us slower to detect a new request).
 __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uint32_t n, int maxb, uint32_t *seqs,
-                                uint32_t *posted)
+                                uint32_t *posted, const ChunkFwd *fwd = nullptr)
 {
     const Params &p = *k.p;
     const int lane = threadIdx.x & 31;
@@ -396,6 +434,14 @@ __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uin
             bad |= 1u << row[j];
     bad = __reduce_or_sync(0xffffffffu, bad);
     const int nb = __ffs(bad | (1u << maxb)) - 1;  // complete slots before the first gap
+    if (fwd && nb > 0) {
+#pragma unroll
+        for (int j = 0; j < kTagChunksPerLane; ++j)
+            if (lane + 32 * j < total && row[j] < nb)
+                fwd_chunk(*fwd, row[j], ch[j], nxc, c[j]);
+        if (lane == 0)
+            fwd_header(*fwd, seq_after(last, nb), (uint32_t)nb);
+    }
 #pragma unroll
     for (int j = 0; j < kTagChunksPerLane; ++j) {
         if (lane + 32 * j < total && row[j] < nb) {

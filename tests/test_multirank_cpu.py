@@ -62,3 +62,11 @@ def test_single_rank_merge_has_no_collectives():
     assert hg.max(3.5) == 3.5 and hg.gather("x") == ["x"]
     m = bench.merge_serving([([5.0, 6.0, 7.0], 1.0)], 50_000.0, 3)
     assert m["served"] == 3 and m["p50_us"] == 6.0 and m["sustained_per_s"] == 3.0
+
+
+def test_merge_reports_requests_per_kernel_pass():
+    # per rank: latencies, elapsed, requests taken and passes of the resident kernel
+    m = bench.merge_serving([([5.0, 6.0], 1.0, 30, 12), ([7.0], 2.0, 10, 8)], 1_000_000.0, 3)
+    assert m["requests_per_pass"] == pytest.approx(40 / 20)
+    assert m["served"] == 3 and m["sustained_per_s"] == 1.5
+    assert "requests_per_pass" not in bench.merge_serving([([5.0], 1.0)], 50_000.0, 1)
