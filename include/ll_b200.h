@@ -95,7 +95,16 @@ typedef struct ll_engine_opts {
                                    wait runs out after step_timeout_ns and the kernel reports
                                    LL_ERR_DEVICE_FAULT at location 6 and leaves (no fault is caused) */
     int32_t kernel_variant;     /* 0 = automatic, 1 = generic shared-memory kernel, 2 = register-resident
-                                   kernel compiled for the net's shape (3-layer fp32, batch 1) */
+                                   kernel compiled for the net's shape (3-layer fp32, batch 1),
+                                   3 = resident small-batch kernel: one CTA on every SM, each holding
+                                   its row slice of every layer in shared memory for the whole launch,
+                                   layers handed off through L2 (bf16 or int8 weights, up to 32 rows,
+                                   the TickBuffer mailbox, in / out widths multiples of 4; it takes
+                                   every SM, so no other resident engine may run on the GPU).
+                                   Automatic picks 2 for the shapes it is compiled for, 3 for bf16 /
+                                   int8 nets that qualify and whose weights exceed one 16-CTA
+                                   cluster's shared memory (about 3.6 MB) unless cluster options are
+                                   forced, else 1. */
     int32_t ring_slots;         /* tagged mailbox only: request slots (1..64; 0 = 1).  Up to ring_slots
                                    requests may be outstanding (ll_submit before the earlier ll_poll);
                                    the device serves them in order, slot after slot */

@@ -87,6 +87,10 @@ class EngineOpts(ctypes.Structure):
                 ("reserved", ctypes.c_int32 * 2)]
 
 
+# ll_engine_opts.kernel_variant
+VARIANT_AUTO, VARIANT_GENERIC, VARIANT_REGISTER_RESIDENT, VARIANT_RESIDENT_SMALL_BATCH = 0, 1, 2, 3
+
+
 class EngineInfo(ctypes.Structure):
     _fields_ = [("n_stages", ctypes.c_int32), ("cluster_size", ctypes.c_int32), ("threads", ctypes.c_int32),
                 ("smem_bytes", ctypes.c_int32), ("image_bytes", ctypes.c_int32), ("launches", ctypes.c_int32),

@@ -14,6 +14,7 @@
 
 #include "common.h"
 #include "gemv_net.cuh"
+#include "gemv_plan.h"
 #include "tc_layer.cuh"
 #include "tc_swap.cuh"
 
@@ -26,7 +27,6 @@ constexpr int kMaxSplitCTAs = 148;  // one CTA per SM
 enum { kKindSplitK = 1, kKindWeightsInTmem = 2, kKindGemv = 3 };
 
 constexpr int kGvPlanCtas = 148;                   // SMs assumed by the host-only plan (B200)
-constexpr size_t kGvSmemLimit = 232448 - 1024;     // dynamic shared memory per CTA, static part aside
 
 struct LayerRun {
     int kind = kKindSplitK;
@@ -47,62 +47,6 @@ int layer_kind(int N, int rows_pad, const ll_batched_opts *o)
                                                                                                 : kKindSplitK;
     const int tiles = (N % kSwChan == 0 && rows_pad % kSwRows == 0) ? (N / kSwChan) * (rows_pad / kSwRows) : 0;
     return tiles >= 96 ? kKindWeightsInTmem : kKindSplitK;
-}
-
-// Shared-memory layout of the small-batch kernel for G CTAs: the per-CTA image
-// (biases and scales of every layer's slice, then each layer's weight slice of
-// ceil(N/G) rows), the per-warp partial sums, two mbarriers, then the staged input
-// rows (fp32, largest in_dim + 4 floats apart).
-struct GemvLayout {
-    int rmax[LL_MAX_LAYERS] = {};
-    uint32_t woff[LL_MAX_LAYERS] = {}, boff[LL_MAX_LAYERS] = {};
-    uint32_t img_bytes = 0, img_a_bytes = 0;
-    uint32_t off_part = 0, off_bar = 0, off_x = 0;
-    int xstride = 0;
-    size_t smem(int bp) const { return off_x + (size_t)bp * (size_t)xstride * sizeof(float); }
-};
-
-int gemv_bp(int rows)
-{
-    return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : rows <= 8 ? 8 : rows <= 16 ? 16 : 32;
-}
-
-void gemv_layout(const ll_net_desc *net, int G, GemvLayout &g)
-{
-    const bool i8 = net->layers[0].wtype == LL_W_I8;
-    size_t fl = 0;
-    int kmax = 0;
-    for (int l = 0; l < net->n_layers; ++l) {
-        g.rmax[l] = (net->layers[l].out_dim + G - 1) / G;
-        g.boff[l] = (uint32_t)fl;
-        fl += (size_t)g.rmax[l] * (i8 ? 2 : 1);
-        kmax = std::max(kmax, net->layers[l].in_dim);
-    }
-    size_t off = llh::round_up(fl * sizeof(float), 16);
-    for (int l = 0; l < net->n_layers; ++l) {
-        g.woff[l] = (uint32_t)std::min<size_t>(off, 1u << 30);
-        off += llh::round_up((size_t)g.rmax[l] * net->layers[l].in_dim * (i8 ? 1 : 2), 16);
-        if (l == 0)
-            g.img_a_bytes = (uint32_t)std::min<size_t>(off, 1u << 30);
-    }
-    g.img_bytes = (uint32_t)std::min<size_t>(off, 1u << 30);
-    off = llh::round_up(off, 128);
-    g.off_part = (uint32_t)std::min<size_t>(off, 1u << 30);
-    off += (size_t)kGvWarps * kGvRowGroup * kGvMaxRows * sizeof(float);
-    g.off_bar = (uint32_t)std::min<size_t>(off, 1u << 30);
-    off += 16;  // two mbarriers: image copy A (biases + layer 0) and B (the other layers)
-    g.off_x = (uint32_t)std::min<size_t>(llh::round_up(off, 128), 1u << 30);
-    g.xstride = kmax + 4;
-}
-
-// The small-batch kernel takes nets of <= 32 rows whose slices and staged rows fit one SM.
-bool gemv_fits(const ll_net_desc *net, int G)
-{
-    if (net->max_batch > kGvMaxRows)
-        return false;
-    GemvLayout g;
-    gemv_layout(net, G, g);
-    return g.smem(gemv_bp(net->max_batch)) <= kGvSmemLimit;
 }
 
 // kKindGemv for the whole net (auto for <= 32 rows when it fits, or forced), else 0.
@@ -627,44 +571,11 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
         LLB_TRY(cudaMemset(m->cnt, 0, sizeof(unsigned) * kGvCntStride * (size_t)net->n_layers));
         // per-CTA images: the CTA's bias (+ scale) slices and weight slices, laid out
         // exactly as the front of its shared memory, so two bulk copies load them
-        std::vector<uint8_t> img((size_t)sms * m->gl.img_bytes, 0);
-        const size_t es = i8 ? 1 : 2;
-        for (int c = 0; c < sms; ++c) {
-            uint8_t *base = img.data() + (size_t)c * m->gl.img_bytes;
-            for (int l = 0; l < net->n_layers; ++l) {
-                const int K = net->layers[l].in_dim, N = net->layers[l].out_dim;
-                const int r0 = (int)((unsigned)c * (unsigned)N / (unsigned)sms);
-                const int R = (int)((unsigned)(c + 1) * (unsigned)N / (unsigned)sms) - r0;
-                float *bd = reinterpret_cast<float *>(base) + m->gl.boff[l];
-                for (int i = 0; i < R; ++i) {
-                    bd[i] = (b && b[l]) ? b[l][r0 + i] : 0.0f;
-                    if (i8)
-                        bd[m->gl.rmax[l] + i] = scales[l][r0 + i];
-                }
-                std::memcpy(base + m->gl.woff[l], static_cast<const uint8_t *>(W[l]) + (size_t)r0 * K * es,
-                            (size_t)R * K * es);
-            }
-        }
+        const std::vector<uint8_t> img = gemv_pack_images(net, W, b, scales, sms, m->gl);
         LLB_TRY(cudaMalloc(&m->img, img.size()));
         LLB_TRY(cudaMemcpy(m->img, img.data(), img.size(), cudaMemcpyHostToDevice));
         GemvNetParams &g = m->gp;
-        std::memset(&g, 0, sizeof(g));
-        g.img = m->img;
-        g.img_bytes = m->gl.img_bytes;
-        g.img_a_bytes = m->gl.img_a_bytes;
-        for (int l = 0; l < net->n_layers; ++l) {
-            g.dims[l] = net->layers[l].in_dim;
-            g.acts[l] = net->layers[l].act;
-            g.rmax[l] = m->gl.rmax[l];
-            g.woff[l] = m->gl.woff[l];
-            g.boff[l] = m->gl.boff[l];
-        }
-        g.dims[net->n_layers] = m->out_dim;
-        g.n_layers = net->n_layers;
-        g.xstride = m->gl.xstride;
-        g.off_part = m->gl.off_part;
-        g.off_bar = m->gl.off_bar;
-        g.off_x = m->gl.off_x;
+        gemv_static_params(net, m->gl, m->img, g);
         g.hand[0] = m->hand[0];
         g.hand[1] = m->hand[1];
         g.act[0] = m->act[0];

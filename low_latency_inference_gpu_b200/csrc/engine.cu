@@ -14,6 +14,7 @@
 #include "common.h"
 #include "engine_types.h"
 #include "fast3_kernel.cuh"
+#include "gemv_plan.h"
 #include "resident_kernel.cuh"
 
 #if defined(__x86_64__)
@@ -418,6 +419,20 @@ struct ll_engine {
     int variant = 1;
     int micro = 1;      // ring slots the device may take together
     int micro_max = 1;  // rows the kernel can carry in one pass
+    // kernel variant 3 (resident small-batch kernel, one CTA per SM, weights in shared memory)
+    GemvNetParams gv{};            // fields fixed at create time
+    GemvLayout gl;
+    int gv_bp = 1;                 // batch rows of the instantiation (gemv_bp(max_batch))
+    int gv_smem = 0;               // dynamic shared memory per CTA
+    uint8_t *gv_img = nullptr;     // per-CTA images
+    uint32_t *gv_hand[2] = {};     // tagged hand-off words [4][widest layer]
+    __nv_bfloat16 *gv_act[2] = {}; // counted hand-off rows [32][widest layer]
+    unsigned *gv_cnt = nullptr;    // arrival counters, one 128-byte line per layer
+    float *gv_relay = nullptr;     // x rows of the current request [32][in]
+    float *gv_gather = nullptr;    // last layer's outputs [32][out]
+    unsigned long long *gv_req = nullptr;  // request word
+    unsigned *gv_status = nullptr;
+    size_t gv_hand_bytes = 0, gv_act_bytes = 0;
     uint32_t passes = 0, rows = 0;  // summed over exited launches
     int weight_regs = 0;
 };
@@ -604,6 +619,53 @@ int set_kernel_attrs(ll_engine *e)
     return LL_OK;
 }
 
+// Kernel variant 3: one cooperative launch of the resident small-batch kernel over every
+// SM; its tags, counters and request word restart from zero at each launch.
+int launch_gemv(ll_engine *e, const Params &p)
+{
+    if (p.mode == MODE_QUEUE &&
+        (reinterpret_cast<uintptr_t>(p.q_x) % 16 != 0 || reinterpret_cast<uintptr_t>(p.q_y) % 16 != 0)) {
+        llh::set_error("queue buffers must be 16-byte aligned");
+        return LL_ERR_INVALID_ARG;
+    }
+    for (int i = 0; i < 2; ++i)
+        LL_CUDA_TRY(cudaMemsetAsync(e->gv_hand[i], 0, e->gv_hand_bytes, e->stream));
+    LL_CUDA_TRY(cudaMemsetAsync(e->gv_cnt, 0, sizeof(unsigned) * kGvCntStride * (size_t)e->gv.n_layers, e->stream));
+    LL_CUDA_TRY(cudaMemsetAsync(e->gv_req, 0, sizeof(unsigned long long), e->stream));
+    LL_CUDA_TRY(cudaMemsetAsync(e->gv_status, 0, sizeof(unsigned), e->stream));
+    GemvNetParams g = e->gv;
+    g.n_rows = 1;
+    GemvResident &r = g.res;
+    r.mb = p.mb;
+    r.mb_x = p.mb_x;
+    r.mb_y = p.mb_y;
+    r.ctrl = p.ctrl;
+    r.mode = p.mode;
+    r.max_rows = e->max_batch;
+    r.last_seq = p.last_seq;
+    r.idle_ns = p.idle_ns;
+    r.peer_margin_ns = p.peer_margin_ns;
+    r.q_x = p.q_x;
+    r.q_y = p.q_y;
+    r.q_n = p.q_n;
+    r.q_rows = p.q_rows;
+    r.q_stamp = p.q_stamp;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)e->grid, 1, 1);
+    cfg.blockDim = dim3(kGvThreads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)e->gv_smem;
+    cfg.stream = e->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the layers hand off across all of them
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[] = {&g};
+    LL_CUDA_TRY(cudaLaunchKernelExC(&cfg, e->kfn, args));
+    ++e->launches;
+    return LL_OK;
+}
+
 int launch(ll_engine *e, const Params &p)
 {
     int rc = set_kernel_attrs(e);
@@ -617,6 +679,8 @@ int launch(ll_engine *e, const Params &p)
     e->ctrl_host->served = p.last_seq;
     e->ctrl_host->passes = 0;
     e->ctrl_host->rows = 0;
+    if (e->variant == 3)
+        return launch_gemv(e, p);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)e->grid, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1024,6 +1088,131 @@ int create_fast3(const ll_net_desc *net, const void *const *W, const float *cons
     return LL_OK;
 }
 
+// Kernel variant 3 (resident small-batch kernel): bf16 or int8 weights of one type, up to
+// 32 rows, the TickBuffer mailbox, in and out widths multiples of 4, slices that fit one SM.
+// Returns an empty string when the net can run on it, else the reason.
+const char *gemv_engine_refusal(const ll_net_desc *net, const float *const *scales, const ll_engine_opts &o, int sms)
+{
+    const int t = net->layers[0].wtype;
+    if (t != LL_W_BF16 && t != LL_W_I8)
+        return "bf16 or int8 weights";
+    for (int l = 0; l < net->n_layers; ++l)
+        if (net->layers[l].wtype != t)
+            return "one weight type for every layer";
+    if (t == LL_W_I8 && !scales)
+        return "per-channel scales for int8 weights";
+    if (net->max_batch < 1 || net->max_batch > kGvMaxRows)
+        return "max_batch <= 32";
+    if (net->layers[0].in_dim % 4 != 0 || net->layers[net->n_layers - 1].out_dim % 4 != 0)
+        return "in_dim and out_dim multiples of 4";
+    if (o.mailbox_format != 0 || o.ring_slots > 1 || o.micro_batch > 1)
+        return "the TickBuffer mailbox (mailbox_format 0, one slot)";
+    if (!gemv_fits(net, sms))
+        return "every layer's row slice plus the staged rows in one SM's shared memory";
+    return "";
+}
+
+int create_gemv(const ll_net_desc *net, const void *const *W, const float *const *b, const float *const *scales,
+                int device, const ll_engine_opts &o, int sms, ll_engine **out)
+{
+    const int L = net->n_layers;
+    const bool i8 = net->layers[0].wtype == LL_W_I8;
+    ll_engine *e = new ll_engine();
+    auto fail = [&](int code) {
+        ll_engine_destroy(e);
+        return code;
+    };
+    e->device = device;
+    e->in_dim = net->layers[0].in_dim;
+    e->out_dim = net->layers[L - 1].out_dim;
+    e->max_batch = net->max_batch;
+    e->variant = 3;
+    e->gv_bp = gemv_bp(net->max_batch);
+    static const void *const k8[6] = {
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 1, 1, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 1, 2, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 1, 4, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 2, 4, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 4, 4, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<true, 8, 4, true>)};
+    static const void *const k16[6] = {
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 1, 1, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 1, 2, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 1, 4, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 2, 4, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 4, 4, true>),
+        reinterpret_cast<const void *>(&ll_gemv_net_kernel<false, 8, 4, true>)};
+    const int idx = 31 - __builtin_clz((unsigned)e->gv_bp);
+    e->kfn = i8 ? k8[idx] : k16[idx];
+    int rc = engine_common_create(e, &o);
+    if (rc)
+        return fail(rc);
+    gemv_layout(net, sms, e->gl);
+    e->gv_smem = (int)e->gl.smem(e->gv_bp);
+    int max_w = 0;
+    for (int l = 0; l < L; ++l)
+        max_w = std::max(max_w, net->layers[l].out_dim);
+    const std::vector<uint8_t> img = gemv_pack_images(net, W, b, scales, sms, e->gl);
+    e->gv_hand_bytes = sizeof(uint32_t) * kGvTagRows * (size_t)max_w;
+    e->gv_act_bytes = sizeof(__nv_bfloat16) * kGvMaxRows * (size_t)max_w;
+    cudaError_t ce = cudaMalloc((void **)&e->gv_img, img.size());
+    if (ce == cudaSuccess)
+        ce = cudaMemcpy(e->gv_img, img.data(), img.size(), cudaMemcpyHostToDevice);
+    for (int i = 0; i < 2 && ce == cudaSuccess; ++i) {
+        ce = cudaMalloc((void **)&e->gv_hand[i], e->gv_hand_bytes);
+        if (ce == cudaSuccess)
+            ce = cudaMalloc((void **)&e->gv_act[i], e->gv_act_bytes);
+    }
+    if (ce == cudaSuccess)
+        ce = cudaMalloc((void **)&e->gv_cnt, sizeof(unsigned) * kGvCntStride * (size_t)L);
+    if (ce == cudaSuccess)
+        ce = cudaMalloc((void **)&e->gv_relay, sizeof(float) * kGvMaxRows * (size_t)e->in_dim);
+    if (ce == cudaSuccess)
+        ce = cudaMalloc((void **)&e->gv_gather, sizeof(float) * kGvMaxRows * (size_t)e->out_dim);
+    if (ce == cudaSuccess)
+        ce = cudaMalloc((void **)&e->gv_req, sizeof(unsigned long long));
+    if (ce == cudaSuccess)
+        ce = cudaMalloc((void **)&e->gv_status, sizeof(unsigned));
+    if (ce == cudaSuccess)
+        ce = cudaFuncSetAttribute(e->kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->gv_smem);
+    int per_sm = 0;
+    if (ce == cudaSuccess)
+        ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, e->kfn, kGvThreads, (size_t)e->gv_smem);
+    if (ce != cudaSuccess) {
+        llh::set_error("resident small-batch kernel set-up: %s", cudaGetErrorString(ce));
+        return fail(LL_ERR_CUDA);
+    }
+    if (per_sm < 1) {
+        llh::set_error("resident small-batch kernel: a CTA does not fit one SM");
+        return fail(LL_ERR_BAD_DESC);
+    }
+    e->attrs_set = true;
+    GemvNetParams &g = e->gv;
+    gemv_static_params(net, e->gl, e->gv_img, g);
+    g.hand[0] = e->gv_hand[0];
+    g.hand[1] = e->gv_hand[1];
+    g.act[0] = e->gv_act[0];
+    g.act[1] = e->gv_act[1];
+    g.cnt = e->gv_cnt;
+    g.status = e->gv_status;
+    g.wait_ns = e->opts.step_timeout_ns;
+    g.res.relay_x = e->gv_relay;
+    g.res.gather_y = e->gv_gather;
+    g.res.req = e->gv_req;
+    PlanResult &pr = e->plan;
+    pr.S = 1;
+    pr.C = 1;
+    Params &p = e->base;
+    p.n_layers = L;
+    p.max_batch = net->max_batch;
+    rc = finish_setup(e);
+    if (rc)
+        return fail(rc);
+    e->grid = sms;  // one CTA per SM
+    *out = e;
+    return LL_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1055,6 +1244,24 @@ int ll_engine_create_ex(const ll_net_desc *net, const void *const *W, const floa
     }
     if (f3)
         return create_fast3(net, W, b, device, o, *f3, out);
+    if (o.kernel_variant == 3 || o.kernel_variant == 0) {
+        int sms = 0;
+        LL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+        const char *why = gemv_engine_refusal(net, scales, o, sms);
+        if (o.kernel_variant == 3 && *why) {
+            llh::set_error("the resident small-batch kernel (variant 3) needs %s", why);
+            return LL_ERR_UNSUPPORTED;
+        }
+        // automatic: when the weights exceed what one 16-CTA cluster holds in shared memory
+        // (the generic kernel would then pipeline several clusters through L2 anyway)
+        size_t wbytes = 0;
+        for (int l = 0; l < net->n_layers; ++l)
+            wbytes += (size_t)net->layers[l].in_dim * net->layers[l].out_dim *
+                      (net->layers[l].wtype == LL_W_I8 ? 1 : net->layers[l].wtype == LL_W_BF16 ? 2 : 4);
+        const bool forced_plan = o.cluster_size || o.min_stages || o.max_stages;
+        if (o.kernel_variant == 3 || (!*why && !forced_plan && wbytes > 16 * (size_t)227 * 1024))
+            return create_gemv(net, W, b, scales, device, o, sms, out);
+    }
     Packed pk;
     rc = plan_and_pack(net, W, b, scales, o, true, pk);
     if (rc)
@@ -1259,6 +1466,11 @@ int ll_engine_destroy(ll_engine *e)
         cudaFree(e->d_xfer);
     if (e->d_words)
         cudaFree(e->d_words);
+    for (void *q : {(void *)e->gv_img, (void *)e->gv_hand[0], (void *)e->gv_hand[1], (void *)e->gv_act[0],
+                    (void *)e->gv_act[1], (void *)e->gv_cnt, (void *)e->gv_relay, (void *)e->gv_gather,
+                    (void *)e->gv_req, (void *)e->gv_status})
+        if (q)
+            cudaFree(q);
     if (e->mb_host)
         cudaFreeHost(e->mb_host);
     if (e->ctrl_host)
@@ -1287,12 +1499,12 @@ int ll_engine_get_info(ll_engine *e, ll_engine_info *info)
     std::memset(info, 0, sizeof(*info));
     info->n_stages = e->plan.S;
     info->cluster_size = e->plan.C;
-    info->threads = kThreads;
-    info->smem_bytes = (int32_t)e->base.smem_bytes;
+    info->threads = e->variant == 3 ? kGvThreads : kThreads;
+    info->smem_bytes = e->variant == 3 ? (int32_t)e->gv_smem : (int32_t)e->base.smem_bytes;
     size_t mi = 0;
     for (size_t v : e->plan.stage_image)
         mi = std::max(mi, v);
-    info->image_bytes = (int32_t)mi;
+    info->image_bytes = e->variant == 3 ? (int32_t)e->gl.img_bytes : (int32_t)mi;
     info->launches = e->launches;
     info->state = (int32_t)e->ctrl_host->state;
     info->status = (int32_t)e->ctrl_host->status;
@@ -1431,32 +1643,43 @@ int ll_engine_run_queue(ll_engine *e, const float *d_x, float *d_y, int n_req, i
     int rc = engine_stop_kernel(e);
     if (rc)
         return rc;
-    Params p = e->base;
-    p.mode = MODE_QUEUE;
-    p.q_x = d_x;
-    p.q_y = d_y;
-    p.q_n = n_req;
-    p.q_rows = n_rows;
-    p.q_stamp = d_stamps;
-    cudaEvent_t a, b;
-    LL_CUDA_TRY(cudaEventCreate(&a));
-    LL_CUDA_TRY(cudaEventCreate(&b));
-    LL_CUDA_TRY(cudaEventRecord(a, e->stream));
-    rc = launch(e, p);
-    if (rc) {
+    // the resident small-batch kernel hands off in 16-bit tags up to 4 rows: a launch serves
+    // at most 65534 / n_layers requests before they run out, so longer queues take several
+    int cap = n_req;
+    if (e->variant == 3 && e->gv_bp <= kGvTagRows)
+        cap = (int)((kGvTagLimit - 1u) / (unsigned)e->gv.n_layers);
+    float total = 0.0f;
+    for (int done = 0; done < n_req && rc == LL_OK;) {
+        const int n = std::min(n_req - done, cap);
+        Params p = e->base;
+        p.mode = MODE_QUEUE;
+        p.q_x = d_x + (size_t)done * n_rows * e->in_dim;
+        p.q_y = d_y + (size_t)done * n_rows * e->out_dim;
+        p.q_n = n;
+        p.q_rows = n_rows;
+        p.q_stamp = d_stamps ? d_stamps + done : nullptr;
+        cudaEvent_t a, b;
+        LL_CUDA_TRY(cudaEventCreate(&a));
+        LL_CUDA_TRY(cudaEventCreate(&b));
+        LL_CUDA_TRY(cudaEventRecord(a, e->stream));
+        rc = launch(e, p);
+        if (rc) {
+            cudaEventDestroy(a);
+            cudaEventDestroy(b);
+            return rc;
+        }
+        LL_CUDA_TRY(cudaEventRecord(b, e->stream));
+        e->running = true;
+        rc = reap(e);
+        float t = 0;
+        cudaEventElapsedTime(&t, a, b);
         cudaEventDestroy(a);
         cudaEventDestroy(b);
-        return rc;
+        total += t;
+        done += n;
     }
-    LL_CUDA_TRY(cudaEventRecord(b, e->stream));
-    e->running = true;
-    rc = reap(e);
-    float t = 0;
-    cudaEventElapsedTime(&t, a, b);
-    cudaEventDestroy(a);
-    cudaEventDestroy(b);
     if (ms)
-        *ms = t;
+        *ms = total;
     // the mailbox kernel is relaunched lazily; its doorbell baseline is unchanged
     e->last_served = static_cast<ll_tick_header *>(e->mb_host)->seq_out;
     return rc;

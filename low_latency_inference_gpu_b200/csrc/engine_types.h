@@ -27,7 +27,10 @@ enum BufId : int32_t { BUF_X = 0, BUF_A = 1, BUF_B = 2, BUF_L = 3, BUF_G = 4, BU
 
 enum Mode : int32_t { MODE_MAILBOX = 0, MODE_QUEUE = 1 };
 
-enum ExitReason : uint32_t { EXIT_NONE = 0, EXIT_STOP = 1, EXIT_IDLE = 2, EXIT_ABORT = 3, EXIT_QUEUE_DONE = 4 };
+// EXIT_TAGS: a resident small-batch launch used up its 16-bit hand-off tags (relaunched on demand)
+enum ExitReason : uint32_t {
+    EXIT_NONE = 0, EXIT_STOP = 1, EXIT_IDLE = 2, EXIT_ABORT = 3, EXIT_QUEUE_DONE = 4, EXIT_TAGS = 5
+};
 
 enum EngineState : uint32_t { ST_IDLE = 0, ST_LOADING = 1, ST_RUNNING = 2, ST_EXITING = 3, ST_EXITED = 4 };
 

@@ -36,6 +36,19 @@
 // layer in the status word, lets its own bulk copies land and returns, so the
 // others time out too and the host reads the error (no trap, no endless spin).
 //
+// Resident mode (RES = true: the engine's kernel variant 3): the same CTAs stay up
+// and serve requests, the weight slices loaded once and kept in shared memory.
+//   * CTA 0 polls the host-mapped TickBuffer (seq_in, acquire; stop and the idle
+//     bound on a cadence) or takes the next request of a device queue, copies the
+//     request's x rows into an L2 relay buffer and publishes a 64-bit request word
+//     {seq, rows, cmd} with release; the other CTAs poll it (acquire, bounded by the
+//     idle bound + a margin) and read x from the relay like a hidden layer;
+//   * the last layer's outputs go to an L2 gather buffer behind an arrival counter;
+//     CTA 0 copies them into the mailbox's y rows and release-stores seq_out;
+//   * tags and counters restart at every launch (the host clears them); before the
+//     16-bit tags would wrap, the kernel leaves (exit reason "tags") and the host
+//     relaunches it on the next request, as after an idle exit.
+//
 // Reference: the per-layer contract y = act(W x + b) over row-major W is
 // cpu_gemv_bias_relu (src/bench_persistent_mbyv_mlp.cu:50-67); the grid-wide
 // layer barrier replaces the reference's global-atomic layer barrier of the
@@ -45,6 +58,7 @@
 
 #include <cstdint>
 
+#include "engine_types.h"
 #include "ll_b200.h"
 #include "ptx.cuh"
 
@@ -78,6 +92,25 @@ enum {
     kGvTraceStored = 10     // ... outputs stored
 };
 
+// Resident mode: the engine's mailbox / queue and the L2 buffers between CTA 0 and the rest.
+struct GemvResident {
+    ll_tick_header *mb;        // the TickBuffer (device view of the mapped host memory)
+    const float *mb_x;         // its x rows [max_batch][in]
+    float *mb_y;               // its y rows [max_batch][out]
+    EngineCtrl *ctrl;          // state, status, exit reason, counters (mapped host memory)
+    float *relay_x;            // [32][in] fp32: the current request's rows, for every CTA
+    float *gather_y;           // [32][out] fp32: the last layer's outputs, for CTA 0
+    unsigned long long *req;   // request word: seq | rows << 32 | cmd << 48 (0 at launch)
+    int mode;                  // MODE_MAILBOX or MODE_QUEUE
+    int max_rows;              // the mailbox's rows (max_batch <= the instantiation's rows)
+    uint32_t last_seq;         // the last request answered before this launch
+    unsigned long long idle_ns, peer_margin_ns;
+    const float *q_x;          // queue mode: q_n requests of q_rows rows, back to back
+    float *q_y;
+    int q_n, q_rows;
+    unsigned long long *q_stamp;  // queue mode: globaltimer when each request's y is stored
+};
+
 struct GemvNetParams {
     unsigned long long *trace[LL_MAX_LAYERS];  // per layer: 16 slots per CTA, or null
     const uint8_t *img;                 // per-CTA images, img_bytes apart: the CTA's shared-memory
@@ -102,7 +135,20 @@ struct GemvNetParams {
     unsigned epoch;                     // forward number: layer l's counter reaches epoch * producers
     unsigned *status;                   // bit 0: a wait ran out; bits 8..15: 16 + failing layer
     unsigned long long wait_ns;
+    GemvResident res;                   // resident mode only
 };
+
+__device__ __forceinline__ void gv_st_release_u64(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long gv_ld_acquire_u64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 
 __device__ __forceinline__ float gv_bf16_lo(uint32_t u)
 {
@@ -200,10 +246,11 @@ __device__ __forceinline__ void gv_weights(uint4 q, float (&w)[WINT8 ? 16 : 8])
     }
 }
 
-template <bool WINT8, int BG, int BPL>
+template <bool WINT8, int BG, int BPL, bool RES = false>
 __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid_constant__ GemvNetParams p)
 {
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t gv_dynamic_smem[];
+    uint8_t *const smem = gv_dynamic_smem;
     constexpr int BP = BG * BPL;         // batch rows this instantiation covers
     constexpr int KL = 32 / BG;          // lanes along K in a warp
     constexpr int CH = WINT8 ? 16 : 8;   // K elements per 16-byte weight chunk
@@ -217,6 +264,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
     // threads in parallel, and reads the shared-memory copy.
     __shared__ GemvNetParams sp;
     __shared__ uint32_t s_fail;
+    __shared__ uint32_t s_req[3];  // resident mode: seq, rows, cmd of the request being served
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kl = lane / BG, bg = lane - kl * BG;
     const int G = (int)gridDim.x, c = (int)blockIdx.x;
@@ -234,7 +282,8 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
         fence_mbar_init_cluster();
     }
     __syncthreads();
-    const int L = sp.n_layers, nr = sp.n_rows, XS = sp.xstride;
+    const int L = sp.n_layers, XS = sp.xstride;
+    int nr = sp.n_rows;
     float *xs = reinterpret_cast<float *>(smem + sp.off_x);
     float *part = reinterpret_cast<float *>(smem + sp.off_part);
     const float *sbias = reinterpret_cast<const float *>(smem);
@@ -260,220 +309,406 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
         }
         gv_stamp(tr0, kGvTraceCopies);
     }
-    // batch rows past n_rows stay zero in the staged input for the whole launch
-    for (int i = tid; i < (BP - nr) * XS; i += kGvThreads)
-        xs[(size_t)nr * XS + i] = 0.0f;
     bool a_ready = false, b_ready = false;
+    if constexpr (!RES) {
+        // batch rows past n_rows stay zero in the staged input for the whole launch
+        for (int i = tid; i < (BP - nr) * XS; i += kGvThreads)
+            xs[(size_t)nr * XS + i] = 0.0f;
+    } else {
+        // the weight slices stay for the whole launch: wait for both copies once
+        bool ok = gv_wait_bar(bar_a, sp.wait_ns) && (!has_b || gv_wait_bar(bar_b, sp.wait_ns));
+        if (!ok && tid == 0) {
+            s_fail = 1u;
+            atomicOr(sp.status, 1u | (15u << 8));
+        }
+        a_ready = b_ready = true;
+        __syncthreads();
+        if (c == 0 && tid == 0 && !s_fail)
+            st_relaxed_sys_u32(&sp.res.ctrl->state, ST_RUNNING);
+    }
+    uint32_t last = RES ? sp.res.last_seq : 0u, tag = 1u, served = 0u, rows_served = 0u;
+    unsigned long long last_word = 0ull;  // resident mode: the request word last seen
 
-    for (int l = 0; l < L; ++l) {
-        int r0;
-        const int R = slice(l, r0);
-        if (R == 0)
-            continue;  // no rows here: this CTA neither reads layer l's input nor writes its output
-        const int K = sp.dims[l], N = sp.dims[l + 1];
-        unsigned long long *tr = sp.trace[l] ? sp.trace[l] + (size_t)c * 16 : nullptr;
-
-        // ---- input: layer 0 from the caller, later layers from the previous layer ----
-        // A thread issues up to kGvUnroll 16-byte loads before it stores any of them, so
-        // the L2 round trips overlap; every CTA starts at its own rotation of the rows.
-        bool ok = true;
-        if (l > 0 && !kTagged) {
-            if (tid == 0) {
-                const unsigned producers = (unsigned)min(G, K);  // layer l-1 has K rows over G CTAs
-                if (!gv_wait_count(sp.cnt + (size_t)(l - 1) * kGvCntStride, sp.epoch * producers, sp.wait_ns)) {
-                    s_fail = 1u;
-                    atomicOr(sp.status, 1u | ((16u + (unsigned)l) << 8));
+    for (uint32_t n_req = 0; !s_fail; ++n_req) {
+        uint32_t seq = 0;
+        if constexpr (RES) {
+            // ---------------- request: CTA 0 takes it, the others read the request word ----------------
+            const GemvResident &rs = sp.res;
+            if (c == 0) {
+                if (tid == 0) {
+                    uint32_t cmd = 0, rows = 0, reason = EXIT_NONE;
+                    if (kTagged && tag + (uint32_t)L > kGvTagLimit) {
+                        cmd = 1u;
+                        reason = EXIT_TAGS;
+                    } else if (rs.mode == MODE_QUEUE) {
+                        if ((int)n_req >= rs.q_n) {
+                            cmd = 1u;
+                            reason = EXIT_QUEUE_DONE;
+                        } else {
+                            seq = n_req + 1u;
+                            rows = (uint32_t)rs.q_rows;
+                        }
+                    } else {
+                        // the TickBuffer doorbell: seq_in alone (acquire); stop and the idle
+                        // bound are checked every 64 polls
+                        const uint64_t t0 = globaltimer();
+                        for (uint32_t it = 0;; ++it) {
+                            const uint32_t sq = ld_acquire_sys(&rs.mb->seq_in);
+                            if (sq != last && sq != 0u) {
+                                seq = sq;
+                                break;
+                            }
+                            if ((it & 63u) == 63u) {
+                                if (ld_relaxed_sys(&rs.mb->stop)) {
+                                    cmd = 1u;
+                                    reason = EXIT_STOP;
+                                    break;
+                                }
+                                if (globaltimer() - t0 > rs.idle_ns) {
+                                    cmd = 1u;
+                                    reason = EXIT_IDLE;
+                                    break;
+                                }
+                            }
+                        }
+                        if (!cmd) {
+                            // clamped to the mailbox's rows: x and y are read and written there
+                            const uint32_t hr = ld_relaxed_sys(&rs.mb->n_rows);
+                            rows = hr == 0u ? 1u : (hr > (uint32_t)rs.max_rows ? (uint32_t)rs.max_rows : hr);
+                        }
+                    }
+                    if (cmd)
+                        st_relaxed_sys_u32(&rs.ctrl->exit_reason, reason);
+                    s_req[0] = seq;
+                    s_req[1] = rows;
+                    s_req[2] = cmd;
                 }
+                __syncthreads();
+                if (!s_req[2]) {
+                    // x rows into the relay buffer (16-byte pieces; in_dim is a multiple of 4)
+                    const int q = sp.dims[0] / 4, n4 = (int)s_req[1] * q;
+                    float4 *dst = reinterpret_cast<float4 *>(rs.relay_x);
+                    if (rs.mode == MODE_QUEUE) {
+                        const float4 *src =
+                            reinterpret_cast<const float4 *>(rs.q_x + (size_t)n_req * rs.q_rows * sp.dims[0]);
+                        for (int i = tid; i < n4; i += kGvThreads)
+                            dst[i] = __ldg(src + i);
+                    } else {
+                        for (int i = tid; i < n4; i += kGvThreads)
+                            dst[i] = ld_relaxed_sys_v4(rs.mb_x + (size_t)i * 4);
+                    }
+                    __syncthreads();  // every thread's relay stores before thread 0's release
+                }
+                if (tid == 0)
+                    gv_st_release_u64(rs.req, (unsigned long long)s_req[0] | ((unsigned long long)s_req[1] << 32) |
+                                                  ((unsigned long long)s_req[2] << 48));
+            } else {
+                if (tid == 0) {
+                    // the next request word (bounded: CTA 0 leaves at the idle bound and says so)
+                    unsigned long long w = gv_ld_acquire_u64(rs.req);
+                    const uint64_t t0 = globaltimer();
+                    while (w == last_word) {
+                        if (globaltimer() - t0 > rs.idle_ns + rs.peer_margin_ns) {
+                            w = 1ull << 48;
+                            break;
+                        }
+                        w = gv_ld_acquire_u64(rs.req);
+                    }
+                    last_word = w;
+                    s_req[0] = (uint32_t)w;
+                    s_req[1] = (uint32_t)(w >> 32) & 0xffffu;
+                    s_req[2] = (uint32_t)(w >> 48);
+                }
+                __syncthreads();
+            }
+            if (s_req[2])
+                break;
+            seq = s_req[0];
+            nr = (int)s_req[1];
+            __syncthreads();  // every thread has read s_req before thread 0 writes the request's fields
+            if (tid == 0) {
+                sp.n_rows = nr;
+                sp.x = rs.relay_x;
+                sp.y = rs.gather_y;
+                sp.tag_base = tag;
+                sp.epoch = n_req + 1u;
+            }
+            __syncthreads();
+        }
+
+        for (int l = 0; l < L; ++l) {
+            int r0;
+            const int R = slice(l, r0);
+            if (R == 0)
+                continue;  // no rows here: this CTA neither reads layer l's input nor writes its output
+            const int K = sp.dims[l], N = sp.dims[l + 1];
+            unsigned long long *tr = sp.trace[l] ? sp.trace[l] + (size_t)c * 16 : nullptr;
+
+            // ---- input: layer 0 from the caller, later layers from the previous layer ----
+            // A thread issues up to kGvUnroll 16-byte loads before it stores any of them, so
+            // the L2 round trips overlap; every CTA starts at its own rotation of the rows.
+            bool ok = true;
+            if (l > 0 && !kTagged) {
+                if (tid == 0) {
+                    const unsigned producers = (unsigned)min(G, K);  // layer l-1 has K rows over G CTAs
+                    if (!gv_wait_count(sp.cnt + (size_t)(l - 1) * kGvCntStride, sp.epoch * producers, sp.wait_ns)) {
+                        s_fail = 1u;
+                        atomicOr(sp.status, 1u | ((16u + (unsigned)l) << 8));
+                    }
+                }
+                __syncthreads();
+                if (s_fail)
+                    break;
+            }
+            {
+                // groups of 16 bytes: 4 fp32 inputs (layer 0), 4 tagged words, or 8 bf16 values
+                const int per = (l == 0 || kTagged) ? 4 : 8;
+                const int q = K / per, total = nr * q, rot = (int)((unsigned)c * (unsigned)total / (unsigned)G);
+                const uint4 *src = l == 0 ? reinterpret_cast<const uint4 *>(sp.x)
+                                   : kTagged ? reinterpret_cast<const uint4 *>(sp.hand[(l - 1) & 1])
+                                             : reinterpret_cast<const uint4 *>(sp.act[(l - 1) & 1]);
+                const uint32_t tag = sp.tag_base + (uint32_t)(l - 1);
+                for (int i0 = tid; i0 < total && ok; i0 += kGvThreads * kGvUnroll) {
+                    uint4 v[kGvUnroll];
+                    int gi[kGvUnroll];
+                    uint32_t pending = 0u;
+    #pragma unroll
+                    for (int u = 0; u < kGvUnroll; ++u) {
+                        int i = i0 + u * kGvThreads + rot;
+                        gi[u] = i - (i >= total ? total : 0);
+                        if (i0 + u * kGvThreads < total) {
+                            v[u] = (l > 0 && kTagged) ? gv_ld_words(src + gi[u]) : __ldcg(src + gi[u]);
+                            pending |= 1u << u;
+                        }
+                    }
+                    uint64_t t0 = 0;
+                    for (;;) {
+    #pragma unroll
+                        for (int u = 0; u < kGvUnroll; ++u) {
+                            if (!((pending >> u) & 1u))
+                                continue;
+                            const int b = gi[u] / q, e = per * (gi[u] - b * q);
+                            float *d = xs + (size_t)b * XS + e;
+                            if (l == 0) {
+                                *reinterpret_cast<float4 *>(d) =
+                                    make_float4(gv_round_bf16(__uint_as_float(v[u].x)), gv_round_bf16(__uint_as_float(v[u].y)),
+                                                gv_round_bf16(__uint_as_float(v[u].z)), gv_round_bf16(__uint_as_float(v[u].w)));
+                            } else if (kTagged) {
+                                if (!gv_tags_are(v[u], tag))
+                                    continue;
+                                *reinterpret_cast<float4 *>(d) = make_float4(
+                                    __uint_as_float(v[u].x & 0xffff0000u), __uint_as_float(v[u].y & 0xffff0000u),
+                                    __uint_as_float(v[u].z & 0xffff0000u), __uint_as_float(v[u].w & 0xffff0000u));
+                            } else {
+                                *reinterpret_cast<float4 *>(d) = make_float4(gv_bf16_lo(v[u].x), gv_bf16_hi(v[u].x),
+                                                                             gv_bf16_lo(v[u].y), gv_bf16_hi(v[u].y));
+                                *reinterpret_cast<float4 *>(d + 4) = make_float4(gv_bf16_lo(v[u].z), gv_bf16_hi(v[u].z),
+                                                                                 gv_bf16_lo(v[u].w), gv_bf16_hi(v[u].w));
+                            }
+                            pending &= ~(1u << u);
+                        }
+                        if (!pending)
+                            break;
+                        const uint64_t now = globaltimer();  // only tagged words can still be pending
+                        if (!t0)
+                            t0 = now;
+                        else if (now - t0 > sp.wait_ns) {
+                            ok = false;
+                            break;
+                        }
+    #pragma unroll
+                        for (int u = 0; u < kGvUnroll; ++u)
+                            if ((pending >> u) & 1u)
+                                v[u] = gv_ld_words(src + gi[u]);
+                    }
+                }
+            }
+            if (tid == 0)
+                gv_stamp(tr, kGvTraceInput);
+            // ---- the image copies: A (biases + layer 0) first, B (later layers) from layer 1 ----
+            if (ok && !a_ready && !gv_wait_bar(bar_a, sp.wait_ns))
+                ok = false;
+            if (ok && l > 0 && !b_ready && !gv_wait_bar(bar_b, sp.wait_ns))
+                ok = false;
+            a_ready = true;
+            b_ready = b_ready || l > 0;
+            if (!ok) {
+                s_fail = 1u;
+                atomicOr(sp.status, 1u | ((16u + (unsigned)l) << 8));
             }
             __syncthreads();
             if (s_fail)
                 break;
-        }
-        {
-            // groups of 16 bytes: 4 fp32 inputs (layer 0), 4 tagged words, or 8 bf16 values
-            const int per = (l == 0 || kTagged) ? 4 : 8;
-            const int q = K / per, total = nr * q, rot = (int)((unsigned)c * (unsigned)total / (unsigned)G);
-            const uint4 *src = l == 0 ? reinterpret_cast<const uint4 *>(sp.x)
-                               : kTagged ? reinterpret_cast<const uint4 *>(sp.hand[(l - 1) & 1])
-                                         : reinterpret_cast<const uint4 *>(sp.act[(l - 1) & 1]);
-            const uint32_t tag = sp.tag_base + (uint32_t)(l - 1);
-            for (int i0 = tid; i0 < total && ok; i0 += kGvThreads * kGvUnroll) {
-                uint4 v[kGvUnroll];
-                int gi[kGvUnroll];
-                uint32_t pending = 0u;
-#pragma unroll
-                for (int u = 0; u < kGvUnroll; ++u) {
-                    int i = i0 + u * kGvThreads + rot;
-                    gi[u] = i - (i >= total ? total : 0);
-                    if (i0 + u * kGvThreads < total) {
-                        v[u] = (l > 0 && kTagged) ? gv_ld_words(src + gi[u]) : __ldcg(src + gi[u]);
-                        pending |= 1u << u;
-                    }
-                }
-                uint64_t t0 = 0;
-                for (;;) {
-#pragma unroll
-                    for (int u = 0; u < kGvUnroll; ++u) {
-                        if (!((pending >> u) & 1u))
-                            continue;
-                        const int b = gi[u] / q, e = per * (gi[u] - b * q);
-                        float *d = xs + (size_t)b * XS + e;
-                        if (l == 0) {
-                            *reinterpret_cast<float4 *>(d) =
-                                make_float4(gv_round_bf16(__uint_as_float(v[u].x)), gv_round_bf16(__uint_as_float(v[u].y)),
-                                            gv_round_bf16(__uint_as_float(v[u].z)), gv_round_bf16(__uint_as_float(v[u].w)));
-                        } else if (kTagged) {
-                            if (!gv_tags_are(v[u], tag))
-                                continue;
-                            *reinterpret_cast<float4 *>(d) = make_float4(
-                                __uint_as_float(v[u].x & 0xffff0000u), __uint_as_float(v[u].y & 0xffff0000u),
-                                __uint_as_float(v[u].z & 0xffff0000u), __uint_as_float(v[u].w & 0xffff0000u));
-                        } else {
-                            *reinterpret_cast<float4 *>(d) = make_float4(gv_bf16_lo(v[u].x), gv_bf16_hi(v[u].x),
-                                                                         gv_bf16_lo(v[u].y), gv_bf16_hi(v[u].y));
-                            *reinterpret_cast<float4 *>(d + 4) = make_float4(gv_bf16_lo(v[u].z), gv_bf16_hi(v[u].z),
-                                                                             gv_bf16_lo(v[u].w), gv_bf16_hi(v[u].w));
-                        }
-                        pending &= ~(1u << u);
-                    }
-                    if (!pending)
-                        break;
-                    const uint64_t now = globaltimer();  // only tagged words can still be pending
-                    if (!t0)
-                        t0 = now;
-                    else if (now - t0 > sp.wait_ns) {
-                        ok = false;
-                        break;
-                    }
-#pragma unroll
-                    for (int u = 0; u < kGvUnroll; ++u)
-                        if ((pending >> u) & 1u)
-                            v[u] = gv_ld_words(src + gi[u]);
-                }
-            }
-        }
-        if (tid == 0)
-            gv_stamp(tr, kGvTraceInput);
-        // ---- the image copies: A (biases + layer 0) first, B (later layers) from layer 1 ----
-        if (ok && !a_ready && !gv_wait_bar(bar_a, sp.wait_ns))
-            ok = false;
-        if (ok && l > 0 && !b_ready && !gv_wait_bar(bar_b, sp.wait_ns))
-            ok = false;
-        a_ready = true;
-        b_ready = b_ready || l > 0;
-        if (!ok) {
-            s_fail = 1u;
-            atomicOr(sp.status, 1u | ((16u + (unsigned)l) << 8));
-        }
-        __syncthreads();
-        if (s_fail)
-            break;
-        if (tid == 0)
-            gv_stamp(tr, kGvTraceReady);
+            if (tid == 0)
+                gv_stamp(tr, kGvTraceReady);
 
-        const uint8_t *ws = smem + sp.woff[l];
-        const float *sb = sbias + sp.boff[l];
-        const int rmax = sp.rmax[l], act = sp.acts[l];
-        const int nch = K / CH;
-        for (int rg = 0; rg < R; rg += kGvRowGroup) {
-            float acc[kGvRowGroup][BPL];
-#pragma unroll
-            for (int r = 0; r < kGvRowGroup; ++r)
-#pragma unroll
-                for (int i = 0; i < BPL; ++i)
-                    acc[r][i] = 0.0f;
-            for (int cc = warp * KL + kl; cc < nch; cc += kGvWarps * KL) {
-                const int k = cc * CH;
-                float xv[BPL][CH];
-#pragma unroll
-                for (int i = 0; i < BPL; ++i) {
-                    const float4 *xp = reinterpret_cast<const float4 *>(xs + (size_t)(bg + BG * i) * XS + k);
-#pragma unroll
-                    for (int j = 0; j < CH / 4; ++j) {
-                        const float4 v = xp[j];
-                        xv[i][4 * j] = v.x;
-                        xv[i][4 * j + 1] = v.y;
-                        xv[i][4 * j + 2] = v.z;
-                        xv[i][4 * j + 3] = v.w;
-                    }
-                }
-                // every row's chunk first, then the products j-outer: consecutive FMAs
-                // are independent (a lane keeps kGvRowGroup x BPL sums)
-                uint4 wq[kGvRowGroup];
-#pragma unroll
+            const uint8_t *ws = smem + sp.woff[l];
+            const float *sb = sbias + sp.boff[l];
+            const int rmax = sp.rmax[l], act = sp.acts[l];
+            const int nch = K / CH;
+            for (int rg = 0; rg < R; rg += kGvRowGroup) {
+                float acc[kGvRowGroup][BPL];
+    #pragma unroll
                 for (int r = 0; r < kGvRowGroup; ++r)
-                    wq[r] = rg + r < R ? *reinterpret_cast<const uint4 *>(ws + ((size_t)(rg + r) * K + k) * ES)
-                                       : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-                for (int h = 0; h < CH / 8; ++h) {  // 8 inputs at a time (int8 chunks hold 16)
-                    float wf[kGvRowGroup][8];
-#pragma unroll
-                    for (int r = 0; r < kGvRowGroup; ++r) {
-                        float w16[CH];
-                        gv_weights<WINT8>(wq[r], w16);
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            wf[r][j] = w16[8 * h + j];
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-#pragma unroll
-                        for (int r = 0; r < kGvRowGroup; ++r)
-#pragma unroll
-                            for (int i = 0; i < BPL; ++i)
-                                acc[r][i] = fmaf(wf[r][j], xv[i][8 * h + j], acc[r][i]);
-                }
-            }
-            // the K lanes of a batch group hold partial sums of the same outputs
-#pragma unroll
-            for (int r = 0; r < kGvRowGroup; ++r)
-#pragma unroll
-                for (int i = 0; i < BPL; ++i)
-#pragma unroll
-                    for (int off = 16; off >= BG; off >>= 1)
-                        acc[r][i] += __shfl_xor_sync(0xffffffffu, acc[r][i], off);
-            if (tid == 0 && rg == 0)
-                gv_stamp(tr, kGvTraceMath);
-            if (kl == 0) {
-#pragma unroll
-                for (int r = 0; r < kGvRowGroup; ++r)
-#pragma unroll
+    #pragma unroll
                     for (int i = 0; i < BPL; ++i)
-                        part[(warp * kGvRowGroup + r) * kGvMaxRows + bg + BG * i] = acc[r][i];
+                        acc[r][i] = 0.0f;
+                for (int cc = warp * KL + kl; cc < nch; cc += kGvWarps * KL) {
+                    const int k = cc * CH;
+                    float xv[BPL][CH];
+    #pragma unroll
+                    for (int i = 0; i < BPL; ++i) {
+                        const float4 *xp = reinterpret_cast<const float4 *>(xs + (size_t)(bg + BG * i) * XS + k);
+    #pragma unroll
+                        for (int j = 0; j < CH / 4; ++j) {
+                            const float4 v = xp[j];
+                            xv[i][4 * j] = v.x;
+                            xv[i][4 * j + 1] = v.y;
+                            xv[i][4 * j + 2] = v.z;
+                            xv[i][4 * j + 3] = v.w;
+                        }
+                    }
+                    // every row's chunk first, then the products j-outer: consecutive FMAs
+                    // are independent (a lane keeps kGvRowGroup x BPL sums)
+                    uint4 wq[kGvRowGroup];
+    #pragma unroll
+                    for (int r = 0; r < kGvRowGroup; ++r)
+                        wq[r] = rg + r < R ? *reinterpret_cast<const uint4 *>(ws + ((size_t)(rg + r) * K + k) * ES)
+                                           : make_uint4(0u, 0u, 0u, 0u);
+    #pragma unroll
+                    for (int h = 0; h < CH / 8; ++h) {  // 8 inputs at a time (int8 chunks hold 16)
+                        float wf[kGvRowGroup][8];
+    #pragma unroll
+                        for (int r = 0; r < kGvRowGroup; ++r) {
+                            float w16[CH];
+                            gv_weights<WINT8>(wq[r], w16);
+    #pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                wf[r][j] = w16[8 * h + j];
+                        }
+    #pragma unroll
+                        for (int j = 0; j < 8; ++j)
+    #pragma unroll
+                            for (int r = 0; r < kGvRowGroup; ++r)
+    #pragma unroll
+                                for (int i = 0; i < BPL; ++i)
+                                    acc[r][i] = fmaf(wf[r][j], xv[i][8 * h + j], acc[r][i]);
+                    }
+                }
+                // the K lanes of a batch group hold partial sums of the same outputs
+    #pragma unroll
+                for (int r = 0; r < kGvRowGroup; ++r)
+    #pragma unroll
+                    for (int i = 0; i < BPL; ++i)
+    #pragma unroll
+                        for (int off = 16; off >= BG; off >>= 1)
+                            acc[r][i] += __shfl_xor_sync(0xffffffffu, acc[r][i], off);
+                if (tid == 0 && rg == 0)
+                    gv_stamp(tr, kGvTraceMath);
+                if (kl == 0) {
+    #pragma unroll
+                    for (int r = 0; r < kGvRowGroup; ++r)
+    #pragma unroll
+                        for (int i = 0; i < BPL; ++i)
+                            part[(warp * kGvRowGroup + r) * kGvMaxRows + bg + BG * i] = acc[r][i];
+                }
+                __syncthreads();
+                if (tid == 0 && rg == 0)
+                    gv_stamp(tr, kGvTraceReduced);
+                for (int t = tid; t < kGvRowGroup * BP; t += kGvThreads) {
+                    const int r = t / BP, b = t - r * BP;
+                    if (rg + r < R && b < nr) {
+                        float s = 0.0f;
+    #pragma unroll
+                        for (int w = 0; w < kGvWarps; ++w)
+                            s += part[(w * kGvRowGroup + r) * kGvMaxRows + b];
+                        float v = WINT8 ? __fadd_rn(__fmul_rn(sb[rmax + rg + r], s), sb[rg + r]) : __fadd_rn(s, sb[rg + r]);
+                        v = gv_act(v, act);
+                        const size_t o = (size_t)b * N + r0 + rg + r;
+                        if (l + 1 == L)
+                            sp.y[o] = v;
+                        else if (kTagged)
+                            gv_st_word(sp.hand[l & 1] + o,
+                                       ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v)) << 16) |
+                                           (sp.tag_base + (uint32_t)l));
+                        else
+                            sp.act[l & 1][o] = __float2bfloat16_rn(v);
+                    }
+                }
+                if (tid == 0 && rg == 0)
+                    gv_stamp(tr, kGvTraceStored);
+                __syncthreads();
             }
-            __syncthreads();
-            if (tid == 0 && rg == 0)
-                gv_stamp(tr, kGvTraceReduced);
-            for (int t = tid; t < kGvRowGroup * BP; t += kGvThreads) {
-                const int r = t / BP, b = t - r * BP;
-                if (rg + r < R && b < nr) {
-                    float s = 0.0f;
-#pragma unroll
-                    for (int w = 0; w < kGvWarps; ++w)
-                        s += part[(w * kGvRowGroup + r) * kGvMaxRows + b];
-                    float v = WINT8 ? __fadd_rn(__fmul_rn(sb[rmax + rg + r], s), sb[rg + r]) : __fadd_rn(s, sb[rg + r]);
-                    v = gv_act(v, act);
-                    const size_t o = (size_t)b * N + r0 + rg + r;
-                    if (l + 1 == L)
-                        sp.y[o] = v;
-                    else if (kTagged)
-                        gv_st_word(sp.hand[l & 1] + o,
-                                   ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v)) << 16) |
-                                       (sp.tag_base + (uint32_t)l));
-                    else
-                        sp.act[l & 1][o] = __float2bfloat16_rn(v);
+            // counted hand-off: the barrier above orders every thread's outputs before
+            // thread 0's release (resident mode: the last layer's outputs too, for CTA 0)
+            if (tid == 0 && ((!kTagged && l + 1 < L) || (RES && l + 1 == L)))
+                red_release_gpu_add(sp.cnt + (size_t)l * kGvCntStride, 1u);
+            if (tid == 0)
+                gv_stamp(tr, kGvTracePublished);
+        }
+
+        if constexpr (!RES) {
+            break;
+        } else {
+            if (s_fail)
+                break;
+            // ---------------- CTA 0: the outputs into the mailbox (or the queue), then seq_out ----------------
+            const GemvResident &rs = sp.res;
+            if (c == 0) {
+                const int N = sp.dims[L];
+                if (tid == 0) {
+                    const unsigned producers = (unsigned)min(G, N);
+                    if (!gv_wait_count(sp.cnt + (size_t)(L - 1) * kGvCntStride, sp.epoch * producers, sp.wait_ns)) {
+                        s_fail = 1u;
+                        atomicOr(sp.status, 1u | ((16u + (unsigned)L) << 8));
+                    }
+                }
+                __syncthreads();
+                if (s_fail)
+                    break;
+                const int n4 = nr * N / 4;  // out_dim is a multiple of 4
+                const float4 *src = reinterpret_cast<const float4 *>(rs.gather_y);
+                if (rs.mode == MODE_QUEUE) {
+                    float4 *dst = reinterpret_cast<float4 *>(rs.q_y + (size_t)n_req * rs.q_rows * N);
+                    for (int i = tid; i < n4; i += kGvThreads)
+                        dst[i] = __ldcg(src + i);
+                } else {
+                    for (int i = tid; i < n4; i += kGvThreads)
+                        st_relaxed_sys_v4(rs.mb_y + (size_t)i * 4, __ldcg(src + i));
+                }
+                __syncthreads();  // every thread's y stores before thread 0's release
+                if (tid == 0) {
+                    if (rs.mode == MODE_QUEUE) {
+                        if (rs.q_stamp)
+                            rs.q_stamp[n_req] = globaltimer();
+                    } else {
+                        st_release_sys_u32(&rs.mb->seq_out, seq);
+                    }
                 }
             }
-            if (tid == 0 && rg == 0)
-                gv_stamp(tr, kGvTraceStored);
-            __syncthreads();
+            last = seq;
+            ++served;
+            rows_served += (uint32_t)nr;
+            if (kTagged)
+                tag += (uint32_t)L;
         }
-        // counted hand-off: the barrier above orders every thread's outputs before
-        // thread 0's release
-        if (!kTagged && l + 1 < L && tid == 0)
-            red_release_gpu_add(sp.cnt + (size_t)l * kGvCntStride, 1u);
-        if (tid == 0)
-            gv_stamp(tr, kGvTracePublished);
+    }
+
+    if constexpr (RES) {
+        if (c == 0 && tid == 0) {
+            // a CTA 0 that left on a failed wait still tells the others to leave
+            if (s_fail)
+                gv_st_release_u64(sp.res.req, (unsigned long long)last | (1ull << 48));
+        }
+        if (s_fail && tid == 0) {
+            st_relaxed_sys_u32(&sp.res.ctrl->err_where, 0x200u + (unsigned)c);
+            st_relaxed_sys_u32(&sp.res.ctrl->status, (uint32_t)LL_ERR_DEVICE_FAULT);
+        }
+        if (c == 0 && tid == 0) {
+            st_relaxed_sys_u32(&sp.res.ctrl->passes, served);
+            st_relaxed_sys_u32(&sp.res.ctrl->rows, rows_served);
+            st_release_sys_u32(&sp.res.ctrl->state, ST_EXITED);
+        }
     }
 
     // A CTA that gave up may still have copies in flight: let them land first.
