@@ -371,11 +371,6 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
                                 }
                             }
                         }
-                        if (!cmd) {
-                            // clamped to the mailbox's rows: x and y are read and written there
-                            const uint32_t hr = ld_relaxed_sys(&rs.mb->n_rows);
-                            rows = hr == 0u ? 1u : (hr > (uint32_t)rs.max_rows ? (uint32_t)rs.max_rows : hr);
-                        }
                     }
                     if (cmd)
                         st_relaxed_sys_u32(&rs.ctrl->exit_reason, reason);
@@ -386,15 +381,37 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
                 __syncthreads();
                 if (!s_req[2]) {
                     // x rows into the relay buffer (16-byte pieces; in_dim is a multiple of 4)
-                    const int q = sp.dims[0] / 4, n4 = (int)s_req[1] * q;
+                    const int q = sp.dims[0] / 4;
                     float4 *dst = reinterpret_cast<float4 *>(rs.relay_x);
                     if (rs.mode == MODE_QUEUE) {
+                        const int n4 = (int)s_req[1] * q;
                         const float4 *src =
                             reinterpret_cast<const float4 *>(rs.q_x + (size_t)n_req * rs.q_rows * sp.dims[0]);
                         for (int i = tid; i < n4; i += kGvThreads)
                             dst[i] = __ldg(src + i);
                     } else {
-                        for (int i = tid; i < n4; i += kGvThreads)
+                        // the header's row count and the first rows of x in ONE PCIe round trip:
+                        // up to 4 rows (4 loads a thread) are read before the count is known,
+                        // rows past it are dropped; rows past those 4 take a second trip
+                        constexpr int kSpec = 4;
+                        const int spec = min(min(rs.max_rows, kGvTagRows) * q, kSpec * kGvThreads) / q * q;
+                        float4 v[kSpec];
+#pragma unroll
+                        for (int u = 0; u < kSpec; ++u)
+                            if (tid + u * kGvThreads < spec)
+                                v[u] = ld_relaxed_sys_v4(rs.mb_x + (size_t)(tid + u * kGvThreads) * 4);
+                        if (tid == 0) {
+                            // clamped to the mailbox's rows: x and y are read and written there
+                            const uint32_t hr = ld_relaxed_sys(&rs.mb->n_rows);
+                            s_req[1] = hr == 0u ? 1u : (hr > (uint32_t)rs.max_rows ? (uint32_t)rs.max_rows : hr);
+                        }
+                        __syncthreads();
+                        const int n4 = (int)s_req[1] * q;
+#pragma unroll
+                        for (int u = 0; u < kSpec; ++u)
+                            if (tid + u * kGvThreads < min(spec, n4))
+                                dst[tid + u * kGvThreads] = v[u];
+                        for (int i = spec + tid; i < n4; i += kGvThreads)
                             dst[i] = ld_relaxed_sys_v4(rs.mb_x + (size_t)i * 4);
                     }
                     __syncthreads();  // every thread's relay stores before thread 0's release
