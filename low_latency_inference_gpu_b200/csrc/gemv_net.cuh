@@ -411,8 +411,21 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
                         for (int u = 0; u < kSpec; ++u)
                             if (tid + u * kGvThreads < min(spec, n4))
                                 dst[tid + u * kGvThreads] = v[u];
-                        for (int i = spec + tid; i < n4; i += kGvThreads)
-                            dst[i] = ld_relaxed_sys_v4(rs.mb_x + (size_t)i * 4);
+                        // the other rows: 4 loads a thread in flight before any store (a load
+                        // of mapped host memory is one PCIe round trip; one after another they
+                        // cost a trip each)
+                        constexpr int kRest = 4;
+                        for (int i0 = spec + tid; i0 < n4; i0 += kRest * kGvThreads) {
+                            float4 w[kRest];
+#pragma unroll
+                            for (int u = 0; u < kRest; ++u)
+                                if (i0 + u * kGvThreads < n4)
+                                    w[u] = ld_relaxed_sys_v4(rs.mb_x + (size_t)(i0 + u * kGvThreads) * 4);
+#pragma unroll
+                            for (int u = 0; u < kRest; ++u)
+                                if (i0 + u * kGvThreads < n4)
+                                    dst[i0 + u * kGvThreads] = w[u];
+                        }
                     }
                     __syncthreads();  // every thread's relay stores before thread 0's release
                 }
@@ -690,8 +703,20 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
                     for (int i = tid; i < n4; i += kGvThreads)
                         dst[i] = __ldcg(src + i);
                 } else {
-                    for (int i = tid; i < n4; i += kGvThreads)
-                        st_relaxed_sys_v4(rs.mb_y + (size_t)i * 4, __ldcg(src + i));
+                    // every L2 load before the first store to the mailbox (the stores are
+                    // ordered asm, so a load after one would wait for it)
+                    constexpr int kY = 2;
+                    for (int i0 = tid; i0 < n4; i0 += kY * kGvThreads) {
+                        float4 v[kY];
+#pragma unroll
+                        for (int u = 0; u < kY; ++u)
+                            if (i0 + u * kGvThreads < n4)
+                                v[u] = __ldcg(src + i0 + u * kGvThreads);
+#pragma unroll
+                        for (int u = 0; u < kY; ++u)
+                            if (i0 + u * kGvThreads < n4)
+                                st_relaxed_sys_v4(rs.mb_y + (size_t)(i0 + u * kGvThreads) * 4, v[u]);
+                    }
                 }
                 __syncthreads();  // every thread's y stores before thread 0's release
                 if (tid == 0) {
