@@ -311,18 +311,35 @@ PROFILE_CASES = {
     "bf16-gelu-256x1024x4x64-32rows": (2, 32, {}),
     "int8-1024x2048x6x256-256rows": (3, 256, {}),
     "int8-1024x2048x6x256-2048rows": (3, 2048, {}),
+    # the resident small-batch engine (kernel variant 3): two device queues of 200 requests,
+    # one launch each (the first warms up)
+    "resident-bf16-gelu-256x1024x4x64-1row": (2, 1, {"resident": True}),
+    "resident-bf16-gelu-256x1024x4x64-32rows": (2, 32, {"resident": True}),
 }
 
 
 def run_profile_case(name):
     """Three forwards of one batched workload (the small-batch kernel for the bf16 GELU net,
-    the tensor-core tiles for the int8 net), nothing else on the device."""
+    the tensor-core tiles for the int8 net), or two queue launches of the resident engine,
+    nothing else on the device."""
     import torch
 
     import low_latency_inference_gpu_b200 as ll
 
     cfg, rows, opts = PROFILE_CASES[name]
     net, Ws, bs = ll.config_params(cfg)
+    if opts.get("resident"):
+        rnet = ll.Net(net.dims, net.acts, net.wtype, rows)
+        Wd, bd, sd = ll.device_weights(net, Ws, bs)
+        n = 200
+        dx = torch.from_numpy(ll.config_inputs(cfg, n * rows)).cuda()
+        dy = torch.empty((n * rows, net.dims[-1]), dtype=torch.float32, device="cuda")
+        with ll.Engine(rnet, Wd, bd, sd, device=0) as e:
+            if e.info().kernel_variant != 3:
+                raise RuntimeError("the resident small-batch kernel was not chosen")
+            for _ in range(2):
+                e.run_queue(dx.data_ptr(), dy.data_ptr(), n, rows)
+        return
     run_net = ll.Net(net.dims, net.acts, net.wtype, rows) if cfg == 3 else net
     Wd, bd, sd = ll.device_weights(net, Ws, bs)
     stream = torch.cuda.current_stream().cuda_stream
