@@ -27,7 +27,8 @@ def _rank(rank, world, port, q):
         top = hg.max(10.0 + rank)
         rng = np.random.default_rng(rank)
         lat = rng.uniform(3.0, 9.0, 1000 + 100 * rank)
-        per_rank = hg.gather((lat.tolist(), 0.5 + 0.25 * rank))
+        # as bench.py's serving section sends it: latencies, elapsed, requests and kernel passes
+        per_rank = hg.gather((lat.tolist(), 0.5 + 0.25 * rank, 1000 + 100 * rank, 500 + 100 * rank))
         merged = bench.merge_serving(per_rank, 200_000.0, 2100)
         q.put((rank, top, merged, lat.tolist()))
     finally:
@@ -51,6 +52,7 @@ def test_two_gloo_ranks_merge_serving_results():
         assert top == 11.0  # max over ranks
         assert merged["served"] == 2100 and merged["per_rank_served"] == [1000, 1100]
         assert merged["sustained_per_s"] == pytest.approx(2100 / 0.75)  # the slowest rank's elapsed time
+        assert merged["requests_per_pass"] == pytest.approx(2100 / 1100)
     every = np.concatenate([got[0][2], got[1][2]])
     assert got[0][1]["p99_us"] == pytest.approx(float(np.percentile(every, 99)))
     assert got[0][1] == got[1][1]  # every rank computes the same line
