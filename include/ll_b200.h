@@ -99,8 +99,9 @@ typedef struct ll_engine_opts {
                                    3 = resident small-batch kernel: one CTA on every SM, each holding
                                    its row slice of every layer in shared memory for the whole launch,
                                    layers handed off through L2 (bf16 or int8 weights, up to 32 rows,
-                                   the TickBuffer mailbox, in / out widths multiples of 4; it takes
-                                   every SM, so no other resident engine may run on the GPU).
+                                   the TickBuffer mailbox or the tagged one at max_batch 1, in / out
+                                   widths multiples of 4; it takes every SM, so no other resident
+                                   engine may run on the GPU).
                                    Automatic picks 2 for the shapes it is compiled for, 3 for bf16 /
                                    int8 nets that qualify and whose weights exceed one 16-CTA
                                    cluster's shared memory (about 3.6 MB) unless cluster options are

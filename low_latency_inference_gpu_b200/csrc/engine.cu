@@ -641,6 +641,7 @@ int launch_gemv(ll_engine *e, const Params &p)
     r.mb_y = p.mb_y;
     r.ctrl = p.ctrl;
     r.mode = p.mode;
+    r.tagged = e->opts.mailbox_format == 1 ? 1 : 0;
     r.max_rows = e->max_batch;
     r.last_seq = p.last_seq;
     r.idle_ns = p.idle_ns;
@@ -1089,7 +1090,8 @@ int create_fast3(const ll_net_desc *net, const void *const *W, const float *cons
 }
 
 // Kernel variant 3 (resident small-batch kernel): bf16 or int8 weights of one type, up to
-// 32 rows, the TickBuffer mailbox, in and out widths multiples of 4, slices that fit one SM.
+// 32 rows, the TickBuffer mailbox (or the tagged one at batch 1), in and out widths
+// multiples of 4, slices that fit one SM.
 // Returns an empty string when the net can run on it, else the reason.
 const char *gemv_engine_refusal(const ll_net_desc *net, const float *const *scales, const ll_engine_opts &o, int sms)
 {
@@ -1105,8 +1107,9 @@ const char *gemv_engine_refusal(const ll_net_desc *net, const float *const *scal
         return "max_batch <= 32";
     if (net->layers[0].in_dim % 4 != 0 || net->layers[net->n_layers - 1].out_dim % 4 != 0)
         return "in_dim and out_dim multiples of 4";
-    if (o.mailbox_format != 0 || o.ring_slots > 1 || o.micro_batch > 1)
-        return "the TickBuffer mailbox (mailbox_format 0, one slot)";
+    if (o.ring_slots > 1 || o.micro_batch > 1 || (o.mailbox_format != 0 && o.mailbox_format != 1) ||
+        (o.mailbox_format == 1 && net->max_batch != 1))
+        return "the TickBuffer mailbox, or the tagged one at max_batch 1 (one slot, no micro-batching)";
     if (!gemv_fits(net, sms))
         return "every layer's row slice plus the staged rows in one SM's shared memory";
     return "";

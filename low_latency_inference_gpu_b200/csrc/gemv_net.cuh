@@ -102,6 +102,7 @@ struct GemvResident {
     float *gather_y;           // [32][out] fp32: the last layer's outputs, for CTA 0
     unsigned long long *req;   // request word: seq | rows << 32 | cmd << 48 (0 at launch)
     int mode;                  // MODE_MAILBOX or MODE_QUEUE
+    int tagged;                // the tagged mailbox (batch 1): x and y in chunks {v0, v1, v2, seq}
     int max_rows;              // the mailbox's rows (max_batch <= the instantiation's rows)
     uint32_t last_seq;         // the last request answered before this launch
     unsigned long long idle_ns, peer_margin_ns;
@@ -137,6 +138,64 @@ struct GemvNetParams {
     unsigned long long wait_ns;
     GemvResident res;                   // resident mode only
 };
+
+// Resident mode, tagged mailbox (warp 0 of CTA 0): waits for the request after `last`, whose
+// x chunks {v0, v1, v2, seq} carry the new sequence number in every chunk, and writes x into
+// `relay` -- detection and the x read are one PCIe round trip.  Stop and the idle bound are
+// checked every 64 polls.  Returns 0 with *seq set, or 1 (leave) with *reason set.
+__device__ __forceinline__ uint32_t gv_poll_tagged(const GemvResident &rs, uint32_t last, float *relay, int in_dim,
+                                                   uint32_t *seq, uint32_t *reason)
+{
+    constexpr int kChunks = 4;  // 128 chunks per warp: in_dim <= 384 (the tagged format's limit)
+    const int lane = threadIdx.x & 31;
+    const int nxc = (in_dim + 2) / 3;
+    const uint4 *chunks = reinterpret_cast<const uint4 *>(rs.mb_x);
+    uint32_t want = last + 1u;
+    if (want == 0u || want == LL_STOP_SEQ)
+        want = 1u;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+        uint4 v[kChunks];
+        bool ok = true;
+#pragma unroll
+        for (int j = 0; j < kChunks; ++j)
+            if (lane + 32 * j < nxc)
+                v[j] = ld_relaxed_sys_v4_u32(reinterpret_cast<const unsigned *>(chunks + lane + 32 * j));
+#pragma unroll
+        for (int j = 0; j < kChunks; ++j)
+            if (lane + 32 * j < nxc && v[j].w != want)
+                ok = false;
+        if (__all_sync(0xffffffffu, ok)) {
+#pragma unroll
+            for (int j = 0; j < kChunks; ++j) {
+                const int ch = lane + 32 * j;
+                if (ch < nxc) {
+                    const float f[3] = {__uint_as_float(v[j].x), __uint_as_float(v[j].y), __uint_as_float(v[j].z)};
+#pragma unroll
+                    for (int e = 0; e < 3; ++e)
+                        if (3 * ch + e < in_dim)
+                            relay[3 * ch + e] = f[e];
+                }
+            }
+            *seq = want;
+            return 0u;
+        }
+        if ((it & 63u) == 63u) {
+            uint32_t verdict = 0u;
+            if (lane == 0) {
+                if (ld_relaxed_sys(&rs.mb->stop))
+                    verdict = EXIT_STOP;
+                else if (globaltimer() - t0 > rs.idle_ns)
+                    verdict = EXIT_IDLE;
+            }
+            verdict = __shfl_sync(0xffffffffu, verdict, 0);
+            if (verdict) {
+                *reason = verdict;
+                return 1u;
+            }
+        }
+    }
+}
 
 __device__ __forceinline__ void gv_st_release_u64(unsigned long long *p, unsigned long long v)
 {
@@ -335,99 +394,121 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
             // ---------------- request: CTA 0 takes it, the others read the request word ----------------
             const GemvResident &rs = sp.res;
             if (c == 0) {
-                if (tid == 0) {
-                    uint32_t cmd = 0, rows = 0, reason = EXIT_NONE;
-                    if (kTagged && tag + (uint32_t)L > kGvTagLimit) {
-                        cmd = 1u;
-                        reason = EXIT_TAGS;
-                    } else if (rs.mode == MODE_QUEUE) {
-                        if ((int)n_req >= rs.q_n) {
+                // the tagged mailbox (batch 1, so only the 1-row instantiations carry it)
+                if (BP == 1 && rs.tagged && rs.mode == MODE_MAILBOX) {
+                    // warp 0 polls the chunks, x arrives with the doorbell
+                    if (warp == 0) {
+                        uint32_t cmd = 0, sq = 0, reason = EXIT_NONE;
+                        if (kTagged && tag + (uint32_t)L > kGvTagLimit) {
                             cmd = 1u;
-                            reason = EXIT_QUEUE_DONE;
+                            reason = EXIT_TAGS;
+                        } else if constexpr (BP == 1) {
+                            cmd = gv_poll_tagged(rs, last, rs.relay_x, sp.dims[0], &sq, &reason);
+                        }
+                        if (lane == 0) {
+                            if (cmd)
+                                st_relaxed_sys_u32(&rs.ctrl->exit_reason, reason);
+                            s_req[0] = sq;
+                            s_req[1] = cmd ? 0u : 1u;
+                            s_req[2] = cmd;
+                        }
+                    }
+                    __syncthreads();  // warp 0's relay stores before thread 0's release
+                } else {
+                    if (tid == 0) {
+                        uint32_t cmd = 0, rows = 0, reason = EXIT_NONE;
+                        if (kTagged && tag + (uint32_t)L > kGvTagLimit) {
+                            cmd = 1u;
+                            reason = EXIT_TAGS;
+                        } else if (rs.mode == MODE_QUEUE) {
+                            if ((int)n_req >= rs.q_n) {
+                                cmd = 1u;
+                                reason = EXIT_QUEUE_DONE;
+                            } else {
+                                seq = n_req + 1u;
+                                rows = (uint32_t)rs.q_rows;
+                            }
                         } else {
-                            seq = n_req + 1u;
-                            rows = (uint32_t)rs.q_rows;
-                        }
-                    } else {
-                        // the TickBuffer doorbell: seq_in alone (acquire); stop and the idle
-                        // bound are checked every 64 polls
-                        const uint64_t t0 = globaltimer();
-                        for (uint32_t it = 0;; ++it) {
-                            const uint32_t sq = ld_acquire_sys(&rs.mb->seq_in);
-                            if (sq != last && sq != 0u) {
-                                seq = sq;
-                                break;
-                            }
-                            if ((it & 63u) == 63u) {
-                                if (ld_relaxed_sys(&rs.mb->stop)) {
-                                    cmd = 1u;
-                                    reason = EXIT_STOP;
+                            // the TickBuffer doorbell: seq_in alone (acquire); stop and the idle
+                            // bound are checked every 64 polls
+                            const uint64_t t0 = globaltimer();
+                            for (uint32_t it = 0;; ++it) {
+                                const uint32_t sq = ld_acquire_sys(&rs.mb->seq_in);
+                                if (sq != last && sq != 0u) {
+                                    seq = sq;
                                     break;
                                 }
-                                if (globaltimer() - t0 > rs.idle_ns) {
-                                    cmd = 1u;
-                                    reason = EXIT_IDLE;
-                                    break;
+                                if ((it & 63u) == 63u) {
+                                    if (ld_relaxed_sys(&rs.mb->stop)) {
+                                        cmd = 1u;
+                                        reason = EXIT_STOP;
+                                        break;
+                                    }
+                                    if (globaltimer() - t0 > rs.idle_ns) {
+                                        cmd = 1u;
+                                        reason = EXIT_IDLE;
+                                        break;
+                                    }
                                 }
                             }
                         }
+                        if (cmd)
+                            st_relaxed_sys_u32(&rs.ctrl->exit_reason, reason);
+                        s_req[0] = seq;
+                        s_req[1] = rows;
+                        s_req[2] = cmd;
                     }
-                    if (cmd)
-                        st_relaxed_sys_u32(&rs.ctrl->exit_reason, reason);
-                    s_req[0] = seq;
-                    s_req[1] = rows;
-                    s_req[2] = cmd;
-                }
-                __syncthreads();
-                if (!s_req[2]) {
-                    // x rows into the relay buffer (16-byte pieces; in_dim is a multiple of 4)
-                    const int q = sp.dims[0] / 4;
-                    float4 *dst = reinterpret_cast<float4 *>(rs.relay_x);
-                    if (rs.mode == MODE_QUEUE) {
-                        const int n4 = (int)s_req[1] * q;
-                        const float4 *src =
-                            reinterpret_cast<const float4 *>(rs.q_x + (size_t)n_req * rs.q_rows * sp.dims[0]);
-                        for (int i = tid; i < n4; i += kGvThreads)
-                            dst[i] = __ldg(src + i);
-                    } else {
-                        // the header's row count and the first rows of x in ONE PCIe round trip:
-                        // up to 4 rows (4 loads a thread) are read before the count is known,
-                        // rows past it are dropped; rows past those 4 take a second trip
-                        constexpr int kSpec = 4;
-                        const int spec = min(min(rs.max_rows, kGvTagRows) * q, kSpec * kGvThreads) / q * q;
-                        float4 v[kSpec];
-#pragma unroll
-                        for (int u = 0; u < kSpec; ++u)
-                            if (tid + u * kGvThreads < spec)
-                                v[u] = ld_relaxed_sys_v4(rs.mb_x + (size_t)(tid + u * kGvThreads) * 4);
-                        if (tid == 0) {
-                            // clamped to the mailbox's rows: x and y are read and written there
-                            const uint32_t hr = ld_relaxed_sys(&rs.mb->n_rows);
-                            s_req[1] = hr == 0u ? 1u : (hr > (uint32_t)rs.max_rows ? (uint32_t)rs.max_rows : hr);
+                    __syncthreads();
+                    if (!s_req[2]) {
+                        // x rows into the relay buffer (16-byte pieces; in_dim is a multiple of 4)
+                        const int q = sp.dims[0] / 4;
+                        float4 *dst = reinterpret_cast<float4 *>(rs.relay_x);
+                        if (rs.mode == MODE_QUEUE) {
+                            const int n4 = (int)s_req[1] * q;
+                            const float4 *src =
+                                reinterpret_cast<const float4 *>(rs.q_x + (size_t)n_req * rs.q_rows * sp.dims[0]);
+                            for (int i = tid; i < n4; i += kGvThreads)
+                                dst[i] = __ldg(src + i);
+                        } else {
+                            // the header's row count and the first rows of x in ONE PCIe round trip:
+                            // up to 4 rows (4 loads a thread) are read before the count is known,
+                            // rows past it are dropped; rows past those 4 take a second trip
+                            constexpr int kSpec = 4;
+                            const int spec = min(min(rs.max_rows, kGvTagRows) * q, kSpec * kGvThreads) / q * q;
+                            float4 v[kSpec];
+    #pragma unroll
+                            for (int u = 0; u < kSpec; ++u)
+                                if (tid + u * kGvThreads < spec)
+                                    v[u] = ld_relaxed_sys_v4(rs.mb_x + (size_t)(tid + u * kGvThreads) * 4);
+                            if (tid == 0) {
+                                // clamped to the mailbox's rows: x and y are read and written there
+                                const uint32_t hr = ld_relaxed_sys(&rs.mb->n_rows);
+                                s_req[1] = hr == 0u ? 1u : (hr > (uint32_t)rs.max_rows ? (uint32_t)rs.max_rows : hr);
+                            }
+                            __syncthreads();
+                            const int n4 = (int)s_req[1] * q;
+    #pragma unroll
+                            for (int u = 0; u < kSpec; ++u)
+                                if (tid + u * kGvThreads < min(spec, n4))
+                                    dst[tid + u * kGvThreads] = v[u];
+                            // the other rows: 4 loads a thread in flight before any store (a load
+                            // of mapped host memory is one PCIe round trip; one after another they
+                            // cost a trip each)
+                            constexpr int kRest = 4;
+                            for (int i0 = spec + tid; i0 < n4; i0 += kRest * kGvThreads) {
+                                float4 w[kRest];
+    #pragma unroll
+                                for (int u = 0; u < kRest; ++u)
+                                    if (i0 + u * kGvThreads < n4)
+                                        w[u] = ld_relaxed_sys_v4(rs.mb_x + (size_t)(i0 + u * kGvThreads) * 4);
+    #pragma unroll
+                                for (int u = 0; u < kRest; ++u)
+                                    if (i0 + u * kGvThreads < n4)
+                                        dst[i0 + u * kGvThreads] = w[u];
+                            }
                         }
-                        __syncthreads();
-                        const int n4 = (int)s_req[1] * q;
-#pragma unroll
-                        for (int u = 0; u < kSpec; ++u)
-                            if (tid + u * kGvThreads < min(spec, n4))
-                                dst[tid + u * kGvThreads] = v[u];
-                        // the other rows: 4 loads a thread in flight before any store (a load
-                        // of mapped host memory is one PCIe round trip; one after another they
-                        // cost a trip each)
-                        constexpr int kRest = 4;
-                        for (int i0 = spec + tid; i0 < n4; i0 += kRest * kGvThreads) {
-                            float4 w[kRest];
-#pragma unroll
-                            for (int u = 0; u < kRest; ++u)
-                                if (i0 + u * kGvThreads < n4)
-                                    w[u] = ld_relaxed_sys_v4(rs.mb_x + (size_t)(i0 + u * kGvThreads) * 4);
-#pragma unroll
-                            for (int u = 0; u < kRest; ++u)
-                                if (i0 + u * kGvThreads < n4)
-                                    dst[i0 + u * kGvThreads] = w[u];
-                        }
+                        __syncthreads();  // every thread's relay stores before thread 0's release
                     }
-                    __syncthreads();  // every thread's relay stores before thread 0's release
                 }
                 if (tid == 0)
                     gv_st_release_u64(rs.req, (unsigned long long)s_req[0] | ((unsigned long long)s_req[1] << 32) |
@@ -702,6 +783,15 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
                     float4 *dst = reinterpret_cast<float4 *>(rs.q_y + (size_t)n_req * rs.q_rows * N);
                     for (int i = tid; i < n4; i += kGvThreads)
                         dst[i] = __ldcg(src + i);
+                } else if (BP == 1 && rs.tagged) {
+                    // tagged y chunks {y0, y1, y2, seq}: the host waits on the tags, so no release
+                    for (int t = tid; t < (N + 2) / 3; t += kGvThreads) {
+                        float v[3];
+#pragma unroll
+                        for (int e = 0; e < 3; ++e)
+                            v[e] = 3 * t + e < N ? __ldcg(rs.gather_y + 3 * t + e) : 0.0f;
+                        st_relaxed_sys_v4(rs.mb_y + (size_t)t * 4, make_float4(v[0], v[1], v[2], __uint_as_float(seq)));
+                    }
                 } else {
                     // every L2 load before the first store to the mailbox (the stores are
                     // ordered asm, so a load after one would wait for it)
@@ -723,6 +813,8 @@ __global__ void __launch_bounds__(kGvThreads, 1) ll_gemv_net_kernel(const __grid
                     if (rs.mode == MODE_QUEUE) {
                         if (rs.q_stamp)
                             rs.q_stamp[n_req] = globaltimer();
+                    } else if (BP == 1 && rs.tagged) {
+                        st_relaxed_sys_u32(&rs.mb->seq_out, seq);  // bookkeeping for a relaunch only
                     } else {
                         st_release_sys_u32(&rs.mb->seq_out, seq);
                     }

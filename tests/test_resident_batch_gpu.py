@@ -125,3 +125,21 @@ def test_forced_variant_is_refused_where_it_cannot_run():
     with ll.Engine(small, Wd, bd, sd, device=0, opts=opts(kernel_variant=3)) as eng:
         x = ll.config_inputs(2, 3)
         assert rel_err(eng.infer(x), oracle.mlp_bf16(small.dims, small.acts, Wd, bd, x)) <= 1e-2
+
+
+def test_one_row_on_the_tagged_mailbox():
+    # x arrives with the doorbell in tagged chunks and y leaves in tagged chunks; an idle exit
+    # and relaunch continue the sequence; the replies equal the TickBuffer engine's bit for bit
+    net, Wd, bd, sd = cfg2(1)
+    xs = ll.config_inputs(2, 12)
+    ref = bf16_ref(net, Wd, bd, xs)
+    with ll.Engine(net, Wd, bd, sd, device=0, opts=opts(mailbox_format=1, idle_timeout_ns=30_000_000)) as e:
+        assert e.info().kernel_variant == ll.VARIANT_RESIDENT_SMALL_BATCH
+        ys = [e.infer(xs[i:i + 1]) for i in range(6)]
+        time.sleep(0.15)  # the kernel leaves after 30 ms idle; the next request relaunches it
+        ys += [e.infer(xs[i:i + 1]) for i in range(6, 12)]
+        assert e.info().launches >= 2 and e.info().status == ll.LL_OK
+    ys = np.concatenate(ys)
+    assert rel_err(ys, ref) <= 1e-2
+    with ll.Engine(net, Wd, bd, sd, device=0) as tick:
+        assert np.array_equal(np.concatenate([tick.infer(xs[i:i + 1]) for i in range(12)]), ys)
