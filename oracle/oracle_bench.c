@@ -1,5 +1,5 @@
 /*
- * Timed loops over the CPU oracle -- TEST INFRASTRUCTURE / CPU BASELINE ONLY.
+ * Timed loops over the CPU oracle -- test infrastructure and the timed CPU baseline only.
  *
  * Used by bench.py's cpu_baseline leg (kind "port") when the reference's own
  * CPU forward (oracle/_ref) is not available.  It restates the reference's
