@@ -323,6 +323,8 @@ PROFILE_CASES = {
     # one launch each (the first warms up)
     "resident-bf16-gelu-256x1024x4x64-1row": (2, 1, {"resident": True}),
     "resident-bf16-gelu-256x1024x4x64-32rows": (2, 32, {"resident": True}),
+    # the 10-layer fp32 net on the generic resident kernel (4 clusters of 16 CTAs), same queues
+    "resident-fp32-128x512x8x32-1row": (1, 1, {"resident": True}),
 }
 
 
@@ -343,8 +345,8 @@ def run_profile_case(name):
         dx = torch.from_numpy(ll.config_inputs(cfg, n * rows)).cuda()
         dy = torch.empty((n * rows, net.dims[-1]), dtype=torch.float32, device="cuda")
         with ll.Engine(rnet, Wd, bd, sd, device=0) as e:
-            if e.info().kernel_variant != 3:
-                raise RuntimeError("the resident small-batch kernel was not chosen")
+            if e.info().kernel_variant != (1 if cfg == 1 else 3):
+                raise RuntimeError("not the expected resident kernel for this workload")
             for _ in range(2):
                 e.run_queue(dx.data_ptr(), dy.data_ptr(), n, rows)
         return
