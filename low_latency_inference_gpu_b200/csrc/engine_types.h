@@ -40,7 +40,7 @@ enum ErrWhere : uint32_t {
     EW_LOAD = 1,         // weight image bulk load
     EW_GATHER = 2,       // rank-0 gather of the last layer
     EW_XFER = 3,         // inter-stage handoff
-    EW_QUEUE_GO = 4,     // queue-mode sequencing
+    EW_QUEUE_GO = 4,     // pipeline sequencing (the first stage waits for the last)
     EW_PEER_POLL = 5,    // a non-leader CTA outlived the leader's idle bound
     EW_DIAG = 6,         // the diagnostic never-completing wait ran out (expected)
     EW_LAYER_BASE = 0x100 // + layer index: all-gather wait of that layer

@@ -676,26 +676,30 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
         if (p.mode == MODE_QUEUE && (int)n_done >= p.q_n)
             break;  // every stage knows the queue length
         if (leader) {
-            if (p.mode == MODE_QUEUE) {
-                if (n_done > 0 && p.n_stages > 1) {
-                    if (tid == 0) {
-                        const uint64_t deadline = globaltimer() + p.step_ns;
-                        uint32_t it = 0;
-                        while (ld_acquire_gpu(p.q_done) < n_done) {
-                            if ((++it & 31u) == 0 && (global_abort(k) || globaltimer() > deadline)) {
-                                if (!global_abort(k)) {
-                                    report_error(k, LL_ERR_DEVICE_FAULT, EW_QUEUE_GO);
-                                    broadcast_abort(k);
-                                }
-                                sh.fail = 1;
-                                break;
+            // A pipeline of clusters carries one request at a time: every stage hands off
+            // through a single buffer, so the first stage takes request n only once the last
+            // stage has published request n-1 (queue mode, and a mailbox ring with several
+            // requests waiting; a closed-loop host never has two in flight).
+            if (n_done > 0 && p.n_stages > 1) {
+                if (tid == 0) {
+                    const uint64_t deadline = globaltimer() + p.step_ns;
+                    uint32_t it = 0;
+                    while (ld_acquire_gpu(p.q_done) < n_done) {
+                        if ((++it & 31u) == 0 && (global_abort(k) || globaltimer() > deadline)) {
+                            if (!global_abort(k)) {
+                                report_error(k, LL_ERR_DEVICE_FAULT, EW_QUEUE_GO);
+                                broadcast_abort(k);
                             }
+                            sh.fail = 1;
+                            break;
                         }
                     }
-                    __syncthreads();
-                    if (*reinterpret_cast<volatile uint32_t *>(&sh.fail))
-                        break;
                 }
+                __syncthreads();
+                if (*reinterpret_cast<volatile uint32_t *>(&sh.fail))
+                    break;
+            }
+            if (p.mode == MODE_QUEUE) {
                 seq = n_done + 1;
                 nrows = p.q_rows;
                 if (tid == 0)
@@ -958,6 +962,10 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 if (tid == 0) {
                     trace(k, n_done, 13);
                     st_relaxed_sys_u32(&p.mb->seq_out, seq);  // bookkeeping only: the host waits on the tags
+                    if (p.n_stages > 1) {  // the first stage may take the next request
+                        __threadfence();
+                        red_release_gpu_add(p.q_done, 1u);
+                    }
                     trace(k, n_done, 14);
                 }
             } else if (tid < 32) {
@@ -993,13 +1001,13 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                     if (p.mode == MODE_QUEUE) {
                         if (p.q_stamp)
                             p.q_stamp[n_done] = globaltimer();
-                        if (p.n_stages > 1) {
-                            __threadfence();
-                            red_release_gpu_add(p.q_done, 1u);
-                        }
                     } else {
                         // release: y reaches the host before seq_out (src/bench_persistent_mbyv_mlp.cu:365-370)
                         st_release_sys_u32(&p.mb->seq_out, seq);
+                    }
+                    if (p.n_stages > 1) {  // the first stage may take the next request
+                        __threadfence();
+                        red_release_gpu_add(p.q_done, 1u);
                     }
                     trace(k, n_done, 14);
                 }

@@ -141,3 +141,19 @@ def test_micro_batched_poisson_stream_is_fully_served(cfg0):
         assert inf.status == ll.LL_OK
     assert len(lat) == 20000 and np.all(np.isfinite(lat)) and lat.min() > 0.5
     assert inf.passes < inf.rows  # an overloaded stream keeps the ring full: several rows per pass
+
+
+def test_ring_on_a_multi_cluster_pipeline():
+    # requests waiting in the ring of a 4-stage pipeline (config 1): each stage hands off
+    # through one buffer, so the first stage takes the next request only after the last stage
+    # has published the previous one; every reply must belong to its own request
+    net, Ws, bs = ll.config_params(1)
+    xs = ll.config_inputs(1, 32)
+    ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=8)) as e:
+        assert e.info().n_stages > 1
+        for base in range(0, 32, 8):
+            seqs = [e.submit(xs[base + i]) for i in range(8)]
+            for i, s in enumerate(seqs):
+                assert rel_err(e.poll(s)[0], ref[base + i]) <= 1e-5
+        assert e.info().status == ll.LL_OK
