@@ -600,6 +600,8 @@ int finish_setup(ll_engine *e)
         LL_CUDA_TRY(cudaMemset(e->d_xfer, 0, sizeof(float) * stride * pr.S));
         p.xfer = e->d_xfer;
         p.xfer_stride = (uint32_t)stride;
+        // batch 1: 64-bit tagged words (Mp of them fit: the region holds bmax4 = 4 rows of floats)
+        p.xfer_tagged = e->max_batch == 1 ? 1 : 0;
     }
     LL_CUDA_TRY(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
     return LL_OK;
@@ -673,6 +675,8 @@ int launch(ll_engine *e, const Params &p)
     if (rc)
         return rc;
     LL_CUDA_TRY(cudaMemsetAsync(e->d_words, 0, sizeof(unsigned) * (4 * kMaxStages + 8), e->stream));
+    if (p.xfer_tagged && e->d_xfer)  // tags restart with the launch (queue mode numbers from 1)
+        LL_CUDA_TRY(cudaMemsetAsync(e->d_xfer, 0, sizeof(float) * p.xfer_stride * (size_t)e->plan.S, e->stream));
     e->ctrl_host->state = ST_IDLE;
     e->ctrl_host->status = LL_OK;
     e->ctrl_host->err_where = 0;

@@ -93,6 +93,7 @@ struct Params {
     uint32_t smem_bytes;
     float *xfer;          // [n_stages][xfer_stride] floats; header in xfer_hdr
     uint32_t xfer_stride;
+    int32_t xfer_tagged;  // batch-1 pipelines: values handed off as 64-bit words {seq, fp32}
     unsigned *xfer_cnt;   // [n_stages] monotone counters
     unsigned *xfer_hdr;   // [n_stages][2]: seq, n_rows
     unsigned *abort_flag; // global abort / exit signal

@@ -223,6 +223,19 @@ __device__ __forceinline__ uint32_t ld_relaxed_gpu_u32(const unsigned *p)
     return v;
 }
 
+// 64-bit words (single-copy atomic when 8-byte aligned): a value and its tag travel together.
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long *p, unsigned long long v)
+{
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long *p)
+{
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // A load the compiler must keep: used to pin values in registers (no rematerialisation).
 __device__ __forceinline__ float ld_once_f32(const float *p)
 {

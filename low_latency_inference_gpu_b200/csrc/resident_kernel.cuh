@@ -780,6 +780,52 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
             ++ph_x;
             if (tid == 0 && k.rank == 1)
                 trace(k, n_done, 15);
+        } else if (p.xfer_tagged) {
+            // Batch 1: the previous cluster's values arrive as words {seq, fp32}; every thread
+            // polls its words until each carries this request's number (the next after `last`;
+            // queue mode numbers requests 1, 2, ... per launch, and the words are cleared at
+            // every launch).  Thread 0 watches the abort flag and the idle bound.
+            const uint32_t want = p.mode == MODE_QUEUE ? n_done + 1u : next_seq_dev(last);
+            const unsigned long long *src =
+                reinterpret_cast<const unsigned long long *>(p.xfer + (size_t)(k.stage - 1) * p.xfer_stride);
+            float *X = buf_ptr(k, BUF_X);
+            const int ld = p.stage_in_ld[k.stage];
+            const uint64_t t0 = globaltimer();
+            bool quit = false;
+            for (uint32_t it = 0;; ++it) {
+                bool got = true;
+                for (int t = tid; t < ld; t += kThreads) {
+                    const unsigned long long w = ld_relaxed_gpu_u64(src + t);
+                    if ((uint32_t)(w >> 32) == want)
+                        X[t] = __uint_as_float((uint32_t)w);
+                    else
+                        got = false;
+                }
+                if (__syncthreads_and(got))
+                    break;
+                if ((it & 31u) == 31u) {
+                    if (tid == 0) {
+                        uint32_t stop = (sh.abort || global_abort(k)) ? 1u : 0u;
+                        if (!stop && globaltimer() - t0 > p.idle_ns + 2 * p.peer_margin_ns) {
+                            report_error(k, LL_ERR_DEVICE_FAULT, EW_XFER);
+                            broadcast_abort(k);
+                            stop = 1u;
+                        }
+                        sh.cmd = stop;
+                    }
+                    __syncthreads();
+                    quit = *reinterpret_cast<volatile uint32_t *>(&sh.cmd) != 0u;
+                    __syncthreads();  // every thread has read sh.cmd before thread 0 writes it again
+                    if (quit)
+                        break;
+                }
+            }
+            if (quit)
+                break;
+            seq = want;
+            nrows = 1;
+            if (tid == 0 && final_writer)
+                trace(k, n_done, 11);
         } else {
             // Wait for the previous cluster's rows of this request (through L2).
             if (tid == 0) {
@@ -878,6 +924,15 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 EpiRows epi{stg, L.R, bias, scale, L.act, L.round_out};
                 layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
                 __syncthreads();
+                if (p.xfer_tagged) {
+                    // batch 1: every value leaves as one 64-bit word {seq, fp32}; the next stage
+                    // polls the words themselves (one L2 trip; no header, fence or counter)
+                    unsigned long long *dw =
+                        reinterpret_cast<unsigned long long *>(p.xfer + (size_t)k.stage * p.xfer_stride) + k.rank * L.R;
+                    for (int t = tid; t < L.R; t += kThreads)
+                        st_relaxed_gpu_u64(dw + t, ((unsigned long long)seq << 32) | __float_as_uint(stg[t]));
+                    break;
+                }
                 float *dst = p.xfer + (size_t)k.stage * p.xfer_stride;
                 const int n4 = L.R >> 2;
                 for (int t = tid; t < nrows * n4; t += kThreads) {

@@ -322,3 +322,27 @@ def test_tagged_mailbox_rejects_batches():
     with pytest.raises(ll.LLError) as err:
         engine_for(net, Ws, bs, mailbox_format=1)
     assert err.value.code == ll.LL_ERR_UNSUPPORTED
+
+
+def test_config1_pipeline_hand_offs_across_queue_runs_and_relaunches():
+    # the batch-1 pipeline hands off tagged words {seq, value} between its clusters; queue runs
+    # number their requests from 1 again, and an idle exit relaunches: no stale word may match
+    torch = pytest.importorskip("torch")
+    net, Ws, bs = ll.config_params(1)
+    xs = ll.config_inputs(1, 268)
+    ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
+    with engine_for(net, Ws, bs, idle_timeout_ns=30_000_000) as e:
+        assert e.info().n_stages > 1
+        ys = [e.infer(xs[i])[0] for i in range(4)]
+        dx = torch.from_numpy(np.ascontiguousarray(xs[4:260])).cuda()
+        for _ in range(2):
+            dy = torch.zeros(256, net.dims[-1], device="cuda")
+            e.run_queue(dx.data_ptr(), dy.data_ptr(), 256, 1)
+            assert rel_err(dy.cpu().numpy(), ref[4:260]) <= 1e-5
+        ys += [e.infer(xs[i])[0] for i in range(260, 264)]
+        launches = e.info().launches
+        time.sleep(0.15)  # the kernel leaves after 30 ms idle; the next request relaunches it
+        ys += [e.infer(xs[i])[0] for i in range(264, 268)]
+        assert e.info().launches > launches and e.info().status == ll.LL_OK
+    idx = list(range(4)) + list(range(260, 268))
+    assert rel_err(np.stack(ys), ref[idx]) <= 1e-5
