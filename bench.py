@@ -11,12 +11,15 @@ Reported:
   value   inferences/s with inputs already in HBM: the resident kernel's
           device-queue mode (each request starts after the previous finished,
           so this is 1 / device latency), timed with CUDA events per launch.
-  e2e     inferences/s through the C ABI (ll_infer's closed loop) with host
-          buffers: each request writes x into the host-mapped mailbox and spins
-          until y is there, then copies y out (host steady clock; p50/p99
-          latency included).  The headline uses the tagged mailbox (x and y in
-          16-byte chunks stamped with the sequence number); `e2e_tickbuffer` is
-          the same loop on the reference's TickBuffer layout.
+  e2e     inferences/s through the C ABI with host buffers: a closed loop that
+          keeps the tagged request ring full (each request's x copied from a host
+          array into its ring slot, its y copied out to a host array as soon as
+          it is there; up to 4 waiting requests taken per kernel pass), one host
+          thread per GPU.  p50/p99 are the batch-1 latency of a single sequential
+          stream (ll_infer's closed loop: write x, spin until y is there, copy y
+          out; host steady clock) on the same engine.  The tagged mailbox carries
+          x and y in 16-byte chunks stamped with the sequence number;
+          `e2e_tickbuffer` is the sequential loop on the reference's TickBuffer.
   latency the empty-mailbox ping-pong floors (same kernel, no layers) for both
           formats and the engine's p50 over them; the cuBLAS+graph and
           launch-per-layer graph paths timed end to end in the same run (N=1).
@@ -31,7 +34,9 @@ Reported:
           N GPUs (config-0 MLP on every GPU, 8-slot tagged request ring, up to 4
           waiting requests per kernel pass): p50/p99 latency from the scheduled
           arrival, sustained throughput and requests per pass.
-  --impl reference  runs the reference's CPU forward on all host cores instead.
+  --impl reference  runs the reference's CPU forward on all host cores instead
+          (weights and inputs drawn by the oracle's own generators: that process
+          loads only oracle/ libraries).
 """
 import argparse
 import json
@@ -52,6 +57,11 @@ WORKLOAD = "config-0 MLP 64->256->256->16 fp32 (ReLU, identity out), batch 1, se
 WEIGHT_BYTES = (64 * 256 + 256 * 256 + 256 * 16) * 4 + (256 + 256 + 16) * 4  # resident weights + biases
 IO_BYTES = 64 * 4 + 16 * 4
 FALLBACK_HBM_GBS = 6650.0
+# the same `config` in both arms (ours and --impl reference)
+CONFIG = {"workload": WORKLOAD, "batch": 1, "precision": "fp32 weights, activations and accumulation",
+          "l2": "GPU arm: a 256 MiB buffer is written between timed device launches; the weights stay on chip "
+                "(registers) for a whole launch by design"}
+RING_SLOTS = 16  # e2e throughput leg: ring slots kept full
 # DRAM traffic of one device-queue launch of the 8-CTA register-resident kernel, from
 # the committed ncu capture (1.352 MB for 2000 requests): the eight per-CTA register
 # images once (812 KB), then ~270 B per request (input row, stamp); scaled to R requests.
@@ -423,11 +433,45 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def pin_host_thread(local_rank):
-    """Pin this rank's submitting thread to its own core (the C++ doorbell loop runs on it)."""
+def numa_node_of_gpu(dev):
+    """NUMA node of the GPU's PCIe device (sysfs), or None."""
     try:
-        cores = sorted(os.sched_getaffinity(0))
-        core = cores[(1 + 2 * local_rank) % len(cores)]
+        import torch
+
+        pr = torch.cuda.get_device_properties(dev)
+        path = f"/sys/bus/pci/devices/{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0/numa_node"
+        with open(path) as f:
+            return int(f.read().strip())
+    except Exception:
+        pass
+    return None
+
+
+def _cpulist(text):
+    out = []
+    for part in text.strip().split(","):
+        if "-" in part:
+            a, b = part.split("-")
+            out.extend(range(int(a), int(b) + 1))
+        elif part:
+            out.append(int(part))
+    return out
+
+
+def pin_host_thread(local_rank, dev):
+    """Pin this rank's submitting thread (the C++ doorbell loop runs on it) to its own core,
+    on the NUMA node of its GPU when sysfs says which: the engine's mailbox pages are first
+    touched by this thread, so they land next to the GPU that polls them."""
+    try:
+        allowed = sorted(os.sched_getaffinity(0))
+        node = numa_node_of_gpu(dev)
+        cores = allowed
+        if node is not None and node >= 0:
+            with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+                local = [c for c in _cpulist(f.read()) if c in set(allowed)]
+            if local:
+                cores = local
+        core = cores[(1 + local_rank) % len(cores)]
         os.sched_setaffinity(0, {core})
         return core
     except Exception:
@@ -438,21 +482,19 @@ def run_reference(args, rank, world):
     """The reference's own CPU forward (oracle/_ref, else the oracle port) on all host cores."""
     if rank != 0:
         return
-    import low_latency_inference_gpu_b200 as ll
-    import oracle
+    import oracle  # oracle/ libraries only: the product library is never loaded in this process
 
-    net, Ws, bs = ll.config_params(0)
-    xs = ll.config_inputs(0, 1024)
+    dims, acts, Ws, bs = oracle.workload_params(0)
+    xs = oracle.workload_inputs(0, 1024)
     kind = "reference" if oracle.ref_available() else "port"
     threads = max(1, len(os.sched_getaffinity(0)))
     per_thread = max(1, args.ref_requests // threads)
     cpus = sorted(os.sched_getaffinity(0))[:threads]
     for _ in range(args.warmup):
-        oracle.bench_cpu(net.dims, net.acts, Ws, bs, xs, max(1, per_thread // 10), kind=kind, threads=threads,
-                         cpus=cpus)
+        oracle.bench_cpu(dims, acts, Ws, bs, xs, max(1, per_thread // 10), kind=kind, threads=threads, cpus=cpus)
     times = []
     for _ in range(args.steps):
-        ns, _, _ = oracle.bench_cpu(net.dims, net.acts, Ws, bs, xs, per_thread, kind=kind, threads=threads, cpus=cpus)
+        ns, _, _ = oracle.bench_cpu(dims, acts, Ws, bs, xs, per_thread, kind=kind, threads=threads, cpus=cpus)
         times.append(ns / 1e9)
     total = sum(times)
     value = threads * per_thread * args.steps / total
@@ -461,8 +503,8 @@ def run_reference(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "inferences/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * total / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded Xavier-uniform weights seed 0, U[-1,1] inputs seed 1)",
-        "config": {"workload": WORKLOAD},
+        "data": "synthetic (seeded: Xavier-uniform weights and U[-0.01,0.01] biases seed 0, U[-1,1] inputs seed 1)",
+        "config": CONFIG, "parallelism": f"{threads} host threads, one sequential request stream each",
         "cpu_baseline": {"value": value, "unit": "inferences/s", "cores": threads, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": "inferences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -511,16 +553,16 @@ def main():
     if args.only == "batched":
         print(json.dumps({"batched": run_batched(ll, torch, dev, iters=10)}), flush=True)
         return
-    host_group = None
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", dev))
-        host_group = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
-    hg = HostGroup(world, host_group)
+        # host-side collectives only (barriers, max, gather) over gloo: the replicas exchange
+        # no data, and a device-side collective would wait behind the resident kernel
+        dist.init_process_group("gloo", timeout=timedelta(seconds=120))
+    hg = HostGroup(world, None)
     host_barrier, host_max, host_gather = hg.barrier, hg.max, hg.gather
 
-    core = pin_host_thread(local_rank)
+    core = pin_host_thread(local_rank, dev)
     R, K, W = args.requests, args.steps, args.warmup
 
     net, Ws, bs = ll.config_params(0)
@@ -557,8 +599,7 @@ def main():
     for _ in range(W):
         engine.run_queue(dx.data_ptr(), dy.data_ptr(), R, 1, stamps.data_ptr())
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    host_barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(dev)
     clocks.start()
@@ -571,8 +612,7 @@ def main():
         st = stamps.cpu().numpy()
         dev_lat.extend((np.diff(st) / 1000.0).tolist())
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    host_barrier()
     torch.cuda.synchronize()
     total_s = host_max(sum(launch_ms) / 1000.0)
     value = world * K * R / total_s
@@ -598,9 +638,35 @@ def main():
         eng.stop()
         return t1 - t0, np.concatenate(lat_all), relaunches
 
+    def ring_loop():
+        """K timed steps of R requests with the RING_SLOTS-slot ring kept full (micro_batch 4);
+        returns (seconds, post-to-reply latencies, relaunches)."""
+        o = opts(1)
+        o.ring_slots, o.micro_batch = RING_SLOTS, 4
+        lat_all = []
+        with ll.Engine(net, Ws, bs, device=dev, opts=o) as eng:
+            eng.start()
+            for _ in range(W):
+                eng.bench_ring(xs, R, RING_SLOTS)
+            before = eng.info().launches
+            host_barrier()
+            t0 = time.perf_counter()
+            for _ in range(K):
+                lat, _, _ = eng.bench_ring(xs, R, RING_SLOTS)
+                lat_all.append(lat)
+            t1 = time.perf_counter()
+            relaunches = eng.info().launches - before
+            host_barrier()
+            eng.stop()
+            i = eng.info()
+        return t1 - t0, np.concatenate(lat_all), relaunches, (i.rows / i.passes if i.passes else float("nan"))
+
     e2e_launches = 0
     e2e_local_s, lat_all, tb_s, lat_tb = float("nan"), np.array([float("nan")]), float("nan"), None
+    ring_s, lat_ring, ring_rpp = float("nan"), np.array([float("nan")]), float("nan")
     if full:
+        ring_s, lat_ring, n, ring_rpp = ring_loop()
+        e2e_launches += n
         e2e_local_s, lat_all, n = closed_loop(engine)
         e2e_launches += n
         with ll.Engine(net, Ws, bs, device=dev, opts=opts(0)) as tb_engine:
@@ -609,7 +675,9 @@ def main():
     clk = clocks.stop()
     e2e_s = host_max(e2e_local_s)
     s_e2e = ll.compute_stats(lat_all)
-    e2e_value = world * K * R / e2e_s
+    seq_value = world * K * R / e2e_s
+    ring_value = world * K * R / host_max(ring_s)
+    s_ring = ll.compute_stats(lat_ring)
     s_tb = ll.compute_stats(lat_tb) if lat_tb is not None else None
     tb_value = world * K * R / host_max(tb_s)
 
@@ -649,8 +717,11 @@ def main():
     peak, peak_kind = measured_peak_hbm()
     avg_launch_s = (sum(launch_ms) / len(launch_ms)) / 1000.0
     achieved = R * (WEIGHT_BYTES + IO_BYTES) / avg_launch_s / 1e9
-    per_rank = host_gather({"rank": rank, "value": K * R / (sum(launch_ms) / 1000.0), "e2e": K * R / e2e_local_s,
-                            "e2e_p50_us": s_e2e["p50"], "e2e_p99_us": s_e2e["p99"], "core": core})
+    per_rank = host_gather({"rank": rank, "value": K * R / (sum(launch_ms) / 1000.0), "e2e": K * R / ring_s,
+                            "sequential_e2e": K * R / e2e_local_s, "e2e_p50_us": s_e2e["p50"],
+                            "e2e_p99_us": s_e2e["p99"], "tagged_x_to_y_floor_p50_us": floor["tagged_x_to_y"]["p50_us"],
+                            "seq_only_floor_p50_us": floor["seq_only"]["p50_us"], "core": core,
+                            "numa_node": numa_node_of_gpu(dev)})
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -669,17 +740,24 @@ def main():
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded: Xavier-uniform weights and U[-0.01,0.01] biases seed 0, U[-1,1] inputs seed 1)",
-        "config": {"workload": WORKLOAD, "requests_per_step": R, "batch": 1,
-                   "parallelism": f"replicas x{world} (one resident kernel + mailbox per GPU, no collective)",
-                   "engine": {"stages": info.n_stages, "cluster_size": info.cluster_size, "threads": info.threads,
-                              "smem_bytes": info.smem_bytes},
-                   "kernel": "register-resident" if info.kernel_variant == 2 else "shared-memory resident",
-                   "l2": "256 MiB buffer written between timed launches; weights stay on chip (registers / "
-                         "shared memory) for the whole launch by design"},
-        "e2e": {"value": e2e_value, "unit": "inferences/s", "h2d_bytes_per_step": R * 64 * 4,
-                "d2h_bytes_per_step": R * 16 * 4, "p50_us": s_e2e["p50"], "p99_us": s_e2e["p99"],
-                "p90_us": s_e2e["p90"], "mailbox": "tagged (mailbox_format 1)",
-                "timing": "host steady_clock per request, x write to y read"},
+        "config": CONFIG,
+        "requests_per_step": R,
+        "parallelism": f"replicas x{world} (one resident kernel + mailbox per GPU, no collective; host "
+                       "barriers over gloo)",
+        "engine": {"stages": info.n_stages, "cluster_size": info.cluster_size, "threads": info.threads,
+                   "smem_bytes": info.smem_bytes,
+                   "kernel": "register-resident" if info.kernel_variant == 2 else "shared-memory resident"},
+        "e2e": {"value": ring_value, "unit": "inferences/s", "h2d_bytes_per_step": world * R * 64 * 4,
+                "d2h_bytes_per_step": world * R * 16 * 4,
+                "mode": f"closed loop keeping a {RING_SLOTS}-slot tagged request ring full, one host thread per "
+                        "GPU; x copied from a host array into the ring slot and y out to a host array per request; "
+                        "up to 4 waiting requests per kernel pass",
+                "requests_per_pass": ring_rpp,
+                "ring_latency_p50_us": s_ring["p50"], "ring_latency_p99_us": s_ring["p99"],
+                "p50_us": s_e2e["p50"], "p99_us": s_e2e["p99"], "p90_us": s_e2e["p90"],
+                "latency": "p50/p90/p99: one sequential request stream (ll_infer's loop: x write to y read, host "
+                           "steady_clock per request), tagged mailbox",
+                "sequential_value": seq_value, "bytes": "per step, all ranks"},
         "e2e_tickbuffer": None if s_tb is None else {
             "value": tb_value, "unit": "inferences/s", "p50_us": s_tb["p50"], "p99_us": s_tb["p99"],
             "p90_us": s_tb["p90"], "mailbox": "the reference's TickBuffer layout (mailbox_format 0)"},
@@ -691,11 +769,16 @@ def main():
                           "tickbuffer_p50_over_io_floor": (s_tb["p50"] if s_tb else float("nan"))
                           / floor["x_to_y"]["p50_us"]},
         "comparison_paths": compare,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind,
+        "roofline": {"bound": "latency", "achieved": s_e2e["p50"], "peak": floor["tagged_x_to_y"]["p50_us"],
+                     "unit": "us", "frac": floor["tagged_x_to_y"]["p50_us"] / s_e2e["p50"],
+                     "peak_kind": "measured in this run: the same resident kernel with no layers echoing x to y "
+                                  "through the tagged mailbox (host -> device -> host ping-pong floor)",
                      "traffic": TRAFFIC_FIXED_BYTES + R * TRAFFIC_PER_REQUEST_BYTES if info.kernel_variant == 2 else None,
-                     "note": "algorithmic bytes = resident weights+biases (345 KB) + x/y per request; the batch-1 "
-                             "path is latency-bound, latency_floor is its relevant bound"},
+                     "hbm": {"achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                             "frac": achieved / peak,
+                             "note": "algorithmic bytes = resident weights+biases (345 KB) + x/y per request over the "
+                                     "device-queue launch; the weights never leave the register file, so this is "
+                                     "not the bound"}},
         "cpu_baseline": cpu_baseline,
         "batched": batched,
         "config1": config1,
@@ -706,6 +789,8 @@ def main():
     }
     if compare:
         out["e2e"]["speedup_vs_cublas_graph_e2e_p50"] = compare["cublas_graph_e2e"]["p50_us"] / s_e2e["p50"]
+    if not full:
+        out["roofline"] = None
     if not full:  # device-queue phase only: no mailbox numbers were taken
         out["e2e"] = None
         out["e2e_tickbuffer"] = None

@@ -214,6 +214,17 @@ int ll_engine_start(ll_engine *e);
  * waits until seq_out == seq (or timeout_ns) and copies y out (y may be NULL).
  */
 int ll_submit(ll_engine *e, const float *x, int n_rows, uint32_t *seq);
+/*
+ * Burst submit (no counterpart in the reference, whose mailbox holds one
+ * request): posts k batch-1 requests, rows xs[k][in_dim], into the next k slots
+ * of the tagged request ring and returns their sequence numbers in seqs[k]
+ * (collect each with ll_poll).  Slots 1..k-1 are written first, then seq_in,
+ * then slot 0: the device takes slots strictly in order, so when it sees the
+ * burst's first request the whole burst is already waiting (a micro-batched
+ * engine then takes several per pass).  LL_ERR_BUSY when fewer than k slots
+ * are free; on the TickBuffer (one slot) k must be 1.
+ */
+int ll_submit_many(ll_engine *e, const float *xs, int k, uint32_t *seqs);
 int ll_poll(ll_engine *e, uint32_t seq, float *y, uint64_t timeout_ns);
 int ll_infer(ll_engine *e, const float *x, int n_rows, float *y, uint64_t timeout_ns);
 
@@ -231,6 +242,19 @@ int ll_engine_get_info(ll_engine *e, ll_engine_info *info);
  */
 int ll_engine_bench_closed_loop(ll_engine *e, const float *xs, int n_x, int n_req, int n_rows, float *ys,
                                 double *lat_us);
+
+/*
+ * Closed loop with the request ring kept full (throughput through the C ABI with
+ * host buffers; no counterpart in the reference, whose host loop keeps one
+ * request outstanding, src/bench_persistent_mbyv_mlp.cu:536-548): n_req batch-1
+ * requests, request r taking xs[r % n_x]; a request is posted (x copied into its
+ * slot) as soon as one of `depth` slots is free (1 <= depth <= ring_slots) and
+ * its reply copied to ys[r] (may be NULL) as soon as it is there, in order.
+ * lat_us[r] (may be NULL) = post to reply in microseconds; *elapsed_s = first
+ * post to last reply.  Tagged mailbox only.
+ */
+int ll_engine_bench_ring(ll_engine *e, const float *xs, int n_x, int n_req, int depth, float *ys, double *lat_us,
+                         double *elapsed_s);
 
 /*
  * Device-resident queue: runs n_req sequential requests whose inputs d_x
@@ -423,7 +447,9 @@ void ll_compute_stats(const double *xs, size_t n, ll_stats *out);
 /* ---- host-side mailbox protocol on any memory (used by the engine; testable without a GPU) ---- */
 /* Bytes of a mailbox for the given dims (header + x + y, rounded to 64). */
 size_t ll_mailbox_bytes(int in_dim, int out_dim, int max_batch);
-/* Write x (if non-NULL) and n_rows, then release-store seq_in = seq. */
+/* Write x (if non-NULL) and n_rows, then release-store seq_in = seq.  On the TickBuffer any
+ * seq that differs from the last one posted and from 0 starts a request (the reference's hosts
+ * use ++seq; ll_submit uses ll_next_seq). */
 void ll_mailbox_post(void *mailbox, int in_dim, const float *x, int n_rows, uint32_t seq, int write_combined);
 /* Spin until seq_out == seq (acquire) or timeout; copies n_rows*out_dim floats of y. LL_OK / LL_ERR_TIMEOUT. */
 int ll_mailbox_wait(const void *mailbox, int in_dim, int out_dim, int max_batch, uint32_t seq, float *y,
@@ -436,7 +462,9 @@ int ll_mailbox_wait(const void *mailbox, int in_dim, int out_dim, int max_batch,
  * {v0, v1, v2, tag} written with one aligned 16-byte store (atomic on x86 CPUs
  * with AVX and for one 16-byte GPU access), tag = the request's sequence number.
  * The device polls the x chunks themselves and takes the request when every tag
- * carries the same new sequence number; it writes the y chunks with relaxed
+ * carries exactly the next sequence number after the last one it served
+ * (ll_next_seq: a hand-driven host must number its requests that way; a slot's
+ * previous lap holds an older number); it writes the y chunks with relaxed
  * stores and the host waits until every y tag equals its sequence number.
  * The y chunks start on a fresh 64-byte line (ll_tagged_y_offset): no cache
  * line holds both host-written x and device-written y.
@@ -462,10 +490,14 @@ uint32_t ll_next_seq(uint32_t seq);
  * outstanding on the tagged mailbox, one on the TickBuffer); lat_us[j] (capacity
  * n_total) receives the time from the scheduled arrival of this rank's j-th
  * request to the host seeing its reply, in microseconds.  *n_served = requests
- * of this rank, *elapsed_s = start to the last reply.  Batch-1 engines.
+ * of this rank, *elapsed_s = start to the last reply.  Optional outputs (NULL to
+ * skip): ys[j][out_dim] = the reply to this rank's j-th request and req_idx[j] =
+ * its index in the whole stream (its input row is req_idx[j] % n_x); both have
+ * capacity n_total rows.  Batch-1 engines.
  */
 int ll_engine_serve_poisson(ll_engine *e, const float *xs, int n_x, int n_total, double rate_per_s, uint64_t seed,
-                            int rank, int world, double *lat_us, int *n_served, double *elapsed_s);
+                            int rank, int world, double *lat_us, int *n_served, double *elapsed_s, float *ys,
+                            int *req_idx);
 
 /*
  * Weight files (no counterpart in the reference, which generates its weights in

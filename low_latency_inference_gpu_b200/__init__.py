@@ -57,6 +57,7 @@ EXPORTED_SYMBOLS = [
     "ll_batched_mlp_check", "ll_batched_mlp_infer", "ll_batched_mlp_info", "ll_batched_mlp_destroy",
     "ll_batched_mlp_set_trace", "ll_engine_serve_poisson",
     "ll_weights_save", "ll_weights_load", "ll_weights_net", "ll_weights_arrays", "ll_weights_free",
+    "ll_submit_many", "ll_engine_bench_ring",
 ]
 MAX_LAYERS = 24
 
@@ -214,7 +215,10 @@ def _sig(lib):
         "ll_weights_free": (None, [_vp]),
         "ll_engine_serve_poisson": (ctypes.c_int, [_vp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_double,
                                                    ctypes.c_uint64, ctypes.c_int, ctypes.c_int, _dp,
-                                                   ctypes.POINTER(ctypes.c_int), _dp]),
+                                                   ctypes.POINTER(ctypes.c_int), _dp, _fp,
+                                                   ctypes.POINTER(ctypes.c_int)]),
+        "ll_submit_many": (ctypes.c_int, [_vp, _fp, ctypes.c_int, P(ctypes.c_uint32)]),
+        "ll_engine_bench_ring": (ctypes.c_int, [_vp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _fp, _dp, _dp]),
     }
     for name, (res, args) in s.items():
         f = getattr(lib, name)
@@ -443,6 +447,15 @@ class Engine:
         self._rows = x.shape[0]
         return seq.value
 
+    def submit_many(self, xs: np.ndarray) -> List[int]:
+        """Post k batch-1 requests at once (ll_submit_many: the whole burst is written before
+        the device can take its first request); returns their sequence numbers."""
+        xs = np.ascontiguousarray(xs, np.float32).reshape(-1, self.in_dim)
+        seqs = (ctypes.c_uint32 * xs.shape[0])()
+        _check(lib().ll_submit_many(self.h, _f(xs), xs.shape[0], seqs))
+        self._rows = 1
+        return list(seqs)
+
     def poll(self, seq: int, timeout_s: float = 2.0) -> np.ndarray:
         y = np.empty((self._rows, self.out_dim), np.float32)
         _check(lib().ll_poll(self.h, seq, _f(y), int(timeout_s * 1e9)))
@@ -463,16 +476,35 @@ class Engine:
         return lat, ys
 
     def serve_poisson(self, xs: np.ndarray, n_total: int, rate_per_s: float, seed: int = 5, rank: int = 0,
-                      world: int = 1):
+                      world: int = 1, keep_outputs: bool = False):
         """Open-loop Poisson stream (see ll_engine_serve_poisson): (latencies in us of this rank's
-        requests, from their scheduled arrival; seconds from the start to the last reply)."""
+        requests, from their scheduled arrival; seconds from the start to the last reply), plus
+        (replies [n][out_dim], stream index of each request) when keep_outputs."""
         xs = np.ascontiguousarray(xs, np.float32).reshape(-1, self.in_dim)
         lat = np.empty(max(1, n_total), np.float64)
         n = ctypes.c_int()
         el = ctypes.c_double()
+        ys = np.empty((max(1, n_total), self.out_dim), np.float32) if keep_outputs else None
+        idx = np.empty(max(1, n_total), np.int32) if keep_outputs else None
         _check(lib().ll_engine_serve_poisson(self.h, _f(xs), xs.shape[0], n_total, rate_per_s, seed, rank, world,
-                                             _d(lat), ctypes.byref(n), ctypes.byref(el)))
+                                             _d(lat), ctypes.byref(n), ctypes.byref(el),
+                                             _f(ys) if keep_outputs else None,
+                                             idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int)) if keep_outputs
+                                             else None))
+        if keep_outputs:
+            return lat[:n.value].copy(), el.value, ys[:n.value].copy(), idx[:n.value].copy()
         return lat[:n.value].copy(), el.value
+
+    def bench_ring(self, xs: np.ndarray, n_req: int, depth: int, keep_outputs: bool = False):
+        """Closed loop with `depth` requests kept in flight (ll_engine_bench_ring): (latencies in
+        us from post to reply, elapsed seconds, replies [n_req][out_dim] or None)."""
+        xs = np.ascontiguousarray(xs, np.float32).reshape(-1, self.in_dim)
+        lat = np.empty(max(1, n_req), np.float64)
+        ys = np.empty((max(1, n_req), self.out_dim), np.float32) if keep_outputs else None
+        el = ctypes.c_double()
+        _check(lib().ll_engine_bench_ring(self.h, _f(xs), xs.shape[0], n_req, depth,
+                                          _f(ys) if keep_outputs else None, _d(lat), ctypes.byref(el)))
+        return lat[:n_req].copy(), el.value, (ys[:n_req].copy() if keep_outputs else None)
 
     def run_queue(self, d_x_ptr: int, d_y_ptr: int, n_req: int, n_rows: int = 1, d_stamps_ptr: int = 0) -> float:
         ms = ctypes.c_float()

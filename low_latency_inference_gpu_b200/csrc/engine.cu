@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cstring>
 #include <deque>
@@ -872,19 +873,33 @@ int engine_wait(ll_engine *e, uint32_t seq, float *y, int n_rows, uint64_t timeo
     return LL_OK;
 }
 
+// Write x into one slot of the tagged ring as chunks stamped with seq (no doorbell).
+void write_tagged_slot(ll_engine *e, size_t slot, const float *x, uint32_t seq)
+{
+    char *base = static_cast<char *>(e->mb_host) + slot * e->ring_stride + sizeof(ll_tick_header);
+    const int xc = (e->in_dim + 2) / 3;
+    for (int c = 0; c < xc; ++c) {
+        uint32_t w[4] = {0u, 0u, 0u, seq};
+        for (int k = 0; k < 3 && 3 * c + k < e->in_dim; ++k)
+            std::memcpy(&w[k], &x[3 * c + k], 4);
+        llh::store16(base + 16 * c, w);  // one aligned 16-byte store per chunk
+    }
+}
+
+inline void host_store_fence()
+{
+#if defined(__x86_64__)
+    _mm_sfence();
+#else
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+#endif
+}
+
 // Post one request in the engine's mailbox format (tagged: into the next ring slot).
 void engine_post(ll_engine *e, const float *x, int n_rows, uint32_t seq)
 {
     if (e->opts.mailbox_format == 1) {
-        const size_t slot = (size_t)(e->ring_next % (uint64_t)e->ring);
-        char *base = static_cast<char *>(e->mb_host) + slot * e->ring_stride + sizeof(ll_tick_header);
-        const int xc = (e->in_dim + 2) / 3;
-        for (int c = 0; c < xc; ++c) {
-            uint32_t w[4] = {0u, 0u, 0u, seq};
-            for (int k = 0; k < 3 && 3 * c + k < e->in_dim; ++k)
-                std::memcpy(&w[k], &x[3 * c + k], 4);
-            llh::store16(base + 16 * c, w);  // one aligned 16-byte store per chunk
-        }
+        write_tagged_slot(e, (size_t)(e->ring_next % (uint64_t)e->ring), x, seq);
         auto *h = static_cast<ll_tick_header *>(e->mb_host);
         h->n_rows = 1;
         __atomic_store_n(const_cast<uint32_t *>(&h->seq_in), seq, __ATOMIC_RELEASE);  // bookkeeping only
@@ -1427,6 +1442,52 @@ int ll_submit(ll_engine *e, const float *x, int n_rows, uint32_t *seq)
     return LL_OK;
 }
 
+int ll_submit_many(ll_engine *e, const float *xs, int k, uint32_t *seqs)
+{
+    if (!e || !xs || k < 1 || !seqs) {
+        llh::set_error("ll_submit_many: null engine, x or seqs, or k %d < 1", k);
+        return LL_ERR_INVALID_ARG;
+    }
+    if (e->opts.mailbox_format != 1) {
+        if (k != 1) {
+            llh::set_error("ll_submit_many: the TickBuffer holds one request (k = %d)", k);
+            return LL_ERR_INVALID_ARG;
+        }
+        return ll_submit(e, xs, 1, seqs);
+    }
+    if (e->inflight.size() + (size_t)k > (size_t)e->ring) {
+        llh::set_error("ll_submit_many: %zu request(s) outstanding, %d more do not fit the %d-slot ring",
+                       e->inflight.size(), k, e->ring);
+        return LL_ERR_BUSY;
+    }
+    int rc = ensure_running(e);
+    if (rc)
+        return rc;
+    uint32_t s = e->last_served > e->seq ? e->last_served : e->seq;
+    for (int i = 0; i < k; ++i)
+        seqs[i] = s = ll_next_seq(s);
+    // Slots 1..k-1 first, then the doorbell word, then slot 0.  The device takes the slots
+    // strictly in order, so it can start on the burst only once slot 0 is visible, and x86
+    // stores become visible in program order: the rest of the burst is there by then.
+    const uint64_t base = e->ring_next;
+    for (int i = 1; i < k; ++i)
+        write_tagged_slot(e, (size_t)((base + (uint64_t)i) % (uint64_t)e->ring), xs + (size_t)i * e->in_dim, seqs[i]);
+    auto *h = static_cast<ll_tick_header *>(e->mb_host);
+    h->n_rows = 1;
+    if (e->wc)
+        host_store_fence();
+    __atomic_store_n(const_cast<uint32_t *>(&h->seq_in), seqs[k - 1], __ATOMIC_RELEASE);
+    if (e->wc)
+        host_store_fence();
+    write_tagged_slot(e, (size_t)(base % (uint64_t)e->ring), xs, seqs[0]);
+    if (e->wc)
+        host_store_fence();
+    for (int i = 0; i < k; ++i)
+        e->inflight.emplace_back(seqs[i], e->ring_next++);
+    e->seq = seqs[k - 1];
+    return LL_OK;
+}
+
 int ll_poll(ll_engine *e, uint32_t seq, float *y, uint64_t timeout_ns)
 {
     if (!e) {
@@ -1557,8 +1618,70 @@ int ll_engine_bench_closed_loop(ll_engine *e, const float *xs, int n_x, int n_re
     return LL_OK;
 }
 
+int ll_engine_bench_ring(ll_engine *e, const float *xs, int n_x, int n_req, int depth, float *ys, double *lat_us,
+                         double *elapsed_s)
+{
+    if (!e || !xs || n_x < 1 || n_req < 0 || depth < 1 || e->max_batch != 1 || e->opts.mailbox_format != 1 ||
+        depth > e->ring) {
+        llh::set_error("ll_engine_bench_ring: invalid arguments (needs the tagged mailbox, 1 <= depth <= ring_slots)");
+        return LL_ERR_INVALID_ARG;
+    }
+    if (!e->inflight.empty()) {
+        llh::set_error("request outstanding");
+        return LL_ERR_BUSY;
+    }
+    int rc = ensure_running(e);
+    if (rc)
+        return rc;
+    using clk = std::chrono::steady_clock;
+    const size_t xin = (size_t)e->in_dim, yout = (size_t)e->out_dim;
+    std::vector<clk::time_point> posted_at((size_t)depth);  // by request index mod depth
+    std::vector<float> ybuf(yout);
+    const auto t0 = clk::now();
+    auto last_progress = t0;
+    int posted = 0, done = 0;
+    while (done < n_req) {
+        // keep the ring full: every free slot takes the next request at once
+        while (posted < n_req && posted - done < depth) {
+            const uint32_t s = ll_next_seq(e->last_served > e->seq ? e->last_served : e->seq);
+            posted_at[(size_t)(posted % depth)] = clk::now();
+            engine_post(e, xs + (size_t)(posted % n_x) * xin, 1, s);
+            ++posted;
+        }
+        const uint32_t s = e->inflight.front().first;
+        float *y = ys ? ys + (size_t)done * yout : ybuf.data();
+        if (tagged_done(e, s, y)) {
+            rc = engine_wait(e, s, nullptr, 1, 0);  // bookkeeping: the reply is there and copied
+            if (rc)
+                return rc;
+            const auto t1 = clk::now();
+            if (lat_us)
+                lat_us[done] = std::chrono::duration<double, std::micro>(t1 - posted_at[(size_t)(done % depth)]).count();
+            ++done;
+            last_progress = t1;
+            continue;
+        }
+        cpu_relax();
+        if (clk::now() - last_progress > std::chrono::seconds(2)) {
+            if (e->ctrl_host->state == ST_EXITED) {
+                rc = ensure_running(e);
+                if (rc)
+                    return rc;
+                last_progress = clk::now();
+                continue;
+            }
+            llh::set_error("ring bench: request seq %u not answered within 2 s", s);
+            return LL_ERR_TIMEOUT;
+        }
+    }
+    if (elapsed_s)
+        *elapsed_s = std::chrono::duration<double>(clk::now() - t0).count();
+    return LL_OK;
+}
+
 int ll_engine_serve_poisson(ll_engine *e, const float *xs, int n_x, int n_total, double rate_per_s, uint64_t seed,
-                            int rank, int world, double *lat_us, int *n_served, double *elapsed_s)
+                            int rank, int world, double *lat_us, int *n_served, double *elapsed_s, float *ys,
+                            int *req_idx)
 {
     if (!e || !xs || n_x < 1 || n_total < 0 || !(rate_per_s > 0) || world < 1 || rank < 0 || rank >= world ||
         !lat_us || e->max_batch != 1) {
@@ -1609,11 +1732,14 @@ int ll_engine_serve_poisson(ll_engine *e, const float *xs, int n_x, int n_total,
                                                       e->mb_host)->seq_out),
                                                   __ATOMIC_ACQUIRE) == s;
             if (ok) {
-                rc = engine_wait(e, s, nullptr, 1, 0);  // bookkeeping: the reply is there
+                // bookkeeping (the reply is there); copies y out when asked
+                rc = engine_wait(e, s, ys ? ys + done * (size_t)e->out_dim : nullptr, 1, 0);
                 if (rc)
                     return rc;
                 const auto tdone = clk::now();
                 lat_us[done] = std::chrono::duration<double, std::micro>(tdone - at(done)).count();
+                if (req_idx)
+                    req_idx[done] = which[done];
                 ++done;
                 last_progress = tdone;
                 continue;

@@ -36,6 +36,7 @@ struct Shared {
     uint32_t fail;
     uint32_t abort;
     uint32_t hstop;  // stop flag seen in the header that came with the current doorbell
+    uint32_t xtag;   // later pipeline stages: the request number the hand-off words carry
 };
 
 __device__ __forceinline__ float act_apply(float v, int act)
@@ -782,10 +783,16 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 trace(k, n_done, 15);
         } else if (p.xfer_tagged) {
             // Batch 1: the previous cluster's values arrive as words {seq, fp32}; every thread
-            // polls its words until each carries this request's number (the next after `last`;
-            // queue mode numbers requests 1, 2, ... per launch, and the words are cleared at
-            // every launch).  Thread 0 watches the abort flag and the idle bound.
-            const uint32_t want = p.mode == MODE_QUEUE ? n_done + 1u : next_seq_dev(last);
+            // polls its words until each carries this request's number.  Queue mode numbers
+            // requests 1, 2, ... per launch.  On the mailbox the number is the host's sequence
+            // number, which a hand-driven host may advance by more than one: a word is current
+            // when its tag is neither 0 (the words are cleared at every launch) nor `last` (the
+            // request this stage served before).  Stage 0 hands over request n only after the
+            // last stage has published request n-1, so the buffer holds words of `last` or of
+            // the one new request: once every word is current they all carry the same number,
+            // read from word 0.  Thread 0 watches the abort flag and the idle bound.
+            const bool queue = p.mode == MODE_QUEUE;
+            const uint32_t want = queue ? n_done + 1u : 0u;
             const unsigned long long *src =
                 reinterpret_cast<const unsigned long long *>(p.xfer + (size_t)(k.stage - 1) * p.xfer_stride);
             float *X = buf_ptr(k, BUF_X);
@@ -796,10 +803,14 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                 bool got = true;
                 for (int t = tid; t < ld; t += kThreads) {
                     const unsigned long long w = ld_relaxed_gpu_u64(src + t);
-                    if ((uint32_t)(w >> 32) == want)
+                    const uint32_t tag = (uint32_t)(w >> 32);
+                    if (queue ? tag == want : (tag != 0u && tag != last)) {
                         X[t] = __uint_as_float((uint32_t)w);
-                    else
+                        if (t == 0)
+                            sh.xtag = tag;
+                    } else {
                         got = false;
+                    }
                 }
                 if (__syncthreads_and(got))
                     break;
@@ -822,7 +833,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
             }
             if (quit)
                 break;
-            seq = want;
+            seq = *reinterpret_cast<volatile uint32_t *>(&sh.xtag);  // written before the barrier above
             nrows = 1;
             if (tid == 0 && final_writer)
                 trace(k, n_done, 11);

@@ -64,6 +64,10 @@ def olib():
         l.oracle_bench_mlp_f32_mt.argtypes = [ctypes.c_int, _ip, _ip, ctypes.POINTER(_fp), ctypes.POINTER(_fp), _fp,
                                               ctypes.c_int, ctypes.c_long, ctypes.c_int, _ip]
         l.oracle_bench_mlp_f32_mt.restype = ctypes.c_double
+        l.oracle_fill_uniform.argtypes = [_fp, ctypes.c_size_t, ctypes.c_float, ctypes.c_float, ctypes.c_uint32]
+        l.oracle_fill_normal.argtypes = [_fp, ctypes.c_size_t, ctypes.c_float, ctypes.c_float, ctypes.c_uint32]
+        l.oracle_init_params.argtypes = [ctypes.c_int, _ip, ctypes.c_int, ctypes.c_uint32, ctypes.POINTER(_fp),
+                                         ctypes.POINTER(_fp)]
         _o = l
     return _o
 
@@ -234,3 +238,49 @@ def bench_cpu(dims, acts, Ws, bs, xs, n_req: int, kind: str = "port", threads: i
     cp = (ctypes.c_int * threads)(*(cpus if cpus else [-1] * threads))
     total = getattr(l, fn_mt)(n, d, a, Wp, bp, _f(xs), xs.shape[0], n_req, threads, cp)
     return total, None, None
+
+
+# ---- the benchmark workloads, drawn without the product library (oracle/gen.cpp) ----
+ACT_IDENTITY, ACT_RELU, ACT_GELU = 0, 1, 2
+
+# dims, hidden activation, weight init (0 Xavier-uniform, 1 N(0, 1/fan_in)), input distribution and seed
+WORKLOADS = {
+    0: dict(dims=[64, 256, 256, 16], act=ACT_RELU, normal_fanin=0, x="uniform", x_seed=1),
+    1: dict(dims=[128] + [512] * 9 + [32], act=ACT_RELU, normal_fanin=0, x="normal", x_seed=2),
+    2: dict(dims=[256] + [1024] * 5 + [64], act=ACT_GELU, normal_fanin=1, x="uniform", x_seed=3),
+    3: dict(dims=[1024] + [2048] * 7 + [256], act=ACT_RELU, normal_fanin=1, x="normal", x_seed=4),
+}
+
+
+def fill_uniform(n: int, lo: float, hi: float, seed: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    olib().oracle_fill_uniform(_f(out), n, lo, hi, seed)
+    return out
+
+
+def fill_normal(n: int, mean: float, sd: float, seed: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    olib().oracle_fill_normal(_f(out), n, mean, sd, seed)
+    return out
+
+
+def workload_params(cfg):
+    """(dims, acts, fp32 W list [out x in], b list) of a benchmark workload, parameters from seed 0."""
+    c = WORKLOADS[cfg]
+    dims = c["dims"]
+    n = len(dims) - 1
+    acts = [c["act"]] * (n - 1) + [ACT_IDENTITY]
+    Ws = [np.empty((dims[l + 1], dims[l]), np.float32) for l in range(n)]
+    bs = [np.empty(dims[l + 1], np.float32) for l in range(n)]
+    d = (ctypes.c_int * (n + 1))(*dims)
+    olib().oracle_init_params(n, d, c["normal_fanin"], 0, (_fp * n)(*[_f(w) for w in Ws]),
+                              (_fp * n)(*[_f(b) for b in bs]))
+    return list(dims), acts, Ws, bs
+
+
+def workload_inputs(cfg, n_rows: int) -> np.ndarray:
+    """The first n_rows inputs of a benchmark workload (request-major)."""
+    c = WORKLOADS[cfg]
+    n = n_rows * c["dims"][0]
+    x = fill_uniform(n, -1.0, 1.0, c["x_seed"]) if c["x"] == "uniform" else fill_normal(n, 0.0, 1.0, c["x_seed"])
+    return x.reshape(n_rows, c["dims"][0])

@@ -1,18 +1,22 @@
 // A host program written the way the reference's benches are
-// (src/bench_persistent_mbyv_mlp.cu:386-559, src/bench_custom_warp_mlp_graph.cu:96-121),
-// compiled against this library's headers only: netcfg:: dims, host_init-style
-// seeded weights, the TickBuffer mailbox driven by hand (write x, bump seq_in,
-// spin on seq_out, stop = 1 + bump), and the launch-per-layer template kernels
-// ll::dense_warp_rm_kernel<M, K, BW, Act> / ll::launch_dense_mbyv_packed<M, K>.
+// (src/bench_persistent_mbyv_mlp.cu:386-559, src/bench_custom_warp_mlp_graph.cu:96-121,
+// src/bench_custom_mbyv_mlp.cu:83-160), compiled against this library's headers only:
+// netcfg:: dims, host_init-style seeded weights, the TickBuffer mailbox driven by hand
+// (write x, bump seq_in, spin on seq_out, stop = 1 + bump), and the launch-per-layer
+// template kernels ll::dense_warp_rm_kernel<M, K, BW, Act>, ll::launch_dense_mbyv_packed<M, K>
+// and ll::dense_mbyv_kernel<ROWS, COLS, BLOCKS, WARPS, REG_N, SHMEM_N, GLOB_N> (padded
+// row-major weights, per-layer scratch, the reference bench's block / warp / storage split).
 //
 // Usage: reference_style_host <out.bin>
-// Writes, as float32: y_engine[OUT], y_warp[OUT], y_packed[OUT], then x[IN], W1, b1, W2, b2, W3, b3.
+// Writes, as float32: y_engine[OUT], y_warp[OUT], y_packed[OUT], y_mbyv[OUT], then x[IN], W1, b1, W2,
+// b2, W3, b3.
 #include <cuda_runtime.h>
 
 #include <cstdio>
 #include <cstring>
 #include <vector>
 
+#include "ll/dense_mbyv.cuh"
 #include "ll/dense_warp.cuh"
 #include "ll/engine.hpp"
 #include "ll/pack_weights.h"
@@ -33,6 +37,18 @@ using namespace netcfg;
 static void host_init(std::vector<float> &v, float scale, uint32_t seed)
 {
     ll::check_or_exit(ll_fill_normal(v.data(), v.size(), 0.0f, scale, seed), "ll_fill_normal");
+}
+
+// Row-major weights with the columns padded to ll::PaddedCols<K, WARPS> (the layout
+// ll::dense_mbyv_kernel reads; the reference bench defines the same helper locally).
+template <int M, int K, int WARPS>
+static std::vector<float> pack_weights_padded_rm(const std::vector<float> &W_rm)
+{
+    constexpr size_t P = ll::PaddedCols<K, WARPS>::padded_cols;
+    std::vector<float> out((size_t)M * P, 0.0f);
+    for (int r = 0; r < M; ++r)
+        std::memcpy(&out[(size_t)r * P], &W_rm[(size_t)r * K], sizeof(float) * K);
+    return out;
 }
 
 int main(int argc, char **argv)
@@ -129,14 +145,47 @@ int main(int argc, char **argv)
     std::vector<float> y_packed(OUT_DIM);
     CK(cudaMemcpy(y_packed.data(), d_y3p, OUT_DIM * 4, cudaMemcpyDeviceToHost));
 
+    // ---- ll::dense_mbyv_kernel, launched as src/bench_custom_mbyv_mlp.cu:83-160 does ----
+    constexpr size_t L1_BLOCKS = 4, L1_WARPS = 8, L1_REG_N = 16, L1_SHMEM_N = 16, L1_GLOB_N = 128 - 16 - 16;
+    constexpr size_t L2_BLOCKS = 2, L2_WARPS = 8, L2_REG_N = 16, L2_SHMEM_N = 8, L2_GLOB_N = 32 - 16 - 8;
+    constexpr size_t L3_BLOCKS = 1, L3_WARPS = 2, L3_REG_N = 16, L3_SHMEM_N = 0, L3_GLOB_N = 32 - 16;
+    auto h_W1pad = pack_weights_padded_rm<(int)H1_DIM, (int)IN_DIM, (int)L1_WARPS>(h_W1);
+    auto h_W2pad = pack_weights_padded_rm<(int)H2_DIM, (int)H1_DIM, (int)L2_WARPS>(h_W2);
+    auto h_W3pad = pack_weights_padded_rm<(int)OUT_DIM, (int)H2_DIM, (int)L3_WARPS>(h_W3);
+    float *d_W1p, *d_W2p, *d_W3p, *d_m1, *d_m2, *d_m3, *d_s1, *d_s2, *d_s3;
+    CK(cudaMalloc(&d_W1p, h_W1pad.size() * 4));
+    CK(cudaMalloc(&d_W2p, h_W2pad.size() * 4));
+    CK(cudaMalloc(&d_W3p, h_W3pad.size() * 4));
+    CK(cudaMalloc(&d_m1, H1_DIM * 4));
+    CK(cudaMalloc(&d_m2, H2_DIM * 4));
+    CK(cudaMalloc(&d_m3, OUT_DIM * 4));
+    CK(cudaMalloc(&d_s1, L1_BLOCKS * L1_WARPS * 32 * L1_GLOB_N * 4));
+    CK(cudaMalloc(&d_s2, L2_BLOCKS * L2_WARPS * 32 * L2_GLOB_N * 4));
+    CK(cudaMalloc(&d_s3, L3_BLOCKS * L3_WARPS * 32 * L3_GLOB_N * 4));
+    CK(cudaMemcpy(d_W1p, h_W1pad.data(), h_W1pad.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(d_W2p, h_W2pad.data(), h_W2pad.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(d_W3p, h_W3pad.data(), h_W3pad.size() * 4, cudaMemcpyHostToDevice));
+    dim3 b1(32, (unsigned)L1_WARPS, 1), b2(32, (unsigned)L2_WARPS, 1), b3(32, (unsigned)L3_WARPS, 1);
+    ll::dense_mbyv_kernel<H1_DIM, IN_DIM, L1_BLOCKS, L1_WARPS, L1_REG_N, L1_SHMEM_N, L1_GLOB_N>
+        <<<L1_BLOCKS, b1, 0, s>>>(d_W1p, d_b1, d_x, d_m1, d_s1, ll::ActRelu{});
+    ll::dense_mbyv_kernel<H2_DIM, H1_DIM, L2_BLOCKS, L2_WARPS, L2_REG_N, L2_SHMEM_N, L2_GLOB_N>
+        <<<L2_BLOCKS, b2, 0, s>>>(d_W2p, d_b2, d_m1, d_m2, d_s2, ll::ActRelu{});
+    ll::dense_mbyv_kernel<OUT_DIM, H2_DIM, L3_BLOCKS, L3_WARPS, L3_REG_N, L3_SHMEM_N, L3_GLOB_N>
+        <<<L3_BLOCKS, b3, 0, s>>>(d_W3p, d_b3, d_m2, d_m3, d_s3, ll::ActIdentity{});
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(s));
+    std::vector<float> y_mbyv(OUT_DIM);
+    CK(cudaMemcpy(y_mbyv.data(), d_m3, OUT_DIM * 4, cudaMemcpyDeviceToHost));
+
     FILE *f = std::fopen(argv[1], "wb");
     if (!f)
         return 1;
-    for (auto *v : {&y_engine, &y_warp, &y_packed, &h_x, &h_W1, &h_b1, &h_W2, &h_b2, &h_W3, &h_b3})
+    for (auto *v : {&y_engine, &y_warp, &y_packed, &y_mbyv, &h_x, &h_W1, &h_b1, &h_W2, &h_b2, &h_W3, &h_b3})
         std::fwrite(v->data(), 4, v->size(), f);
     std::fclose(f);
-    std::printf("engine %.8f warp %.8f packed %.8f\n", y_engine[0], y_warp[0], y_packed[0]);
-    for (auto p : {d_x, d_y1, d_y2, d_y3, d_W1, d_b1, d_W2, d_b2, d_W3, d_b3, d_W3cm, d_b3p, d_y3p})
+    std::printf("engine %.8f warp %.8f packed %.8f mbyv %.8f\n", y_engine[0], y_warp[0], y_packed[0], y_mbyv[0]);
+    for (auto p : {d_x, d_y1, d_y2, d_y3, d_W1, d_b1, d_W2, d_b2, d_W3, d_b3, d_W3cm, d_b3p, d_y3p, d_W1p, d_W2p,
+                   d_W3p, d_m1, d_m2, d_m3, d_s1, d_s2, d_s3})
         cudaFree(p);
     cudaStreamDestroy(s);
     return 0;

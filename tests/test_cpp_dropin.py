@@ -1,7 +1,7 @@
 """Drop-in check: a host program written like the reference's benches compiles
 against include/ (netcfg::, ll::TickBuffer, ll::dense_warp_rm_kernel<...>,
-ll::launch_dense_mbyv_packed<...>, ll::Engine) and, on a GPU, reproduces the
-reference's own golden output."""
+ll::launch_dense_mbyv_packed<...>, ll::dense_mbyv_kernel<...>, ll::PaddedCols, ll::Engine)
+and, on a GPU, reproduces the reference's own golden output on every path."""
 import os
 import subprocess
 
@@ -34,7 +34,7 @@ def test_reference_style_host_runs_and_matches_golden(tmp_path, golden):
     r = subprocess.run([exe, str(out)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     v = np.fromfile(out, np.float32)
-    y_engine, y_warp, y_packed = v[0], v[1], v[2]
+    y_engine, y_warp, y_packed, y_mbyv = v[0], v[1], v[2], v[3]
     y3 = np.array(golden["ref_bench"]["y3"], np.uint32).view(np.float32)[0]
-    for y in (y_engine, y_warp, y_packed):
+    for y in (y_engine, y_warp, y_packed, y_mbyv):
         assert abs(float(y) - float(y3)) <= 1e-5 * max(1.0, abs(float(y3)))

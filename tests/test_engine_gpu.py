@@ -184,6 +184,33 @@ def test_reference_style_raw_mailbox_host_loop():
         e.stop()
 
 
+def test_hand_driven_host_may_skip_sequence_numbers_on_a_pipeline():
+    """A TickBuffer host that advances seq_in by more than one (any new non-zero number starts
+    a request) on the 4-stage config-1 pipeline: the later stages take the number the hand-off
+    words carry, so every request is answered with its own output."""
+    net, Ws, bs = ll.config_params(1)
+    xs = ll.config_inputs(1, 6)
+    ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
+    with engine_for(net, Ws, bs) as e:
+        assert e.info().n_stages > 1
+        e.start()
+        base = e.mailbox()
+        hdr = (ctypes.c_uint32 * 4).from_address(base)
+        xbuf = np.ctypeslib.as_array((ctypes.c_float * 128).from_address(base + 16))
+        ybuf = np.ctypeslib.as_array((ctypes.c_float * 32).from_address(base + 16 + 128 * 4))
+        seq = hdr[1]
+        for i, step in enumerate((1, 3, 2, 7, 1, 5)):
+            xbuf[:] = xs[i]
+            seq += step
+            hdr[0] = seq
+            t0 = time.time()
+            while hdr[1] != seq:
+                assert time.time() - t0 < 2.0
+            assert rel_err(ybuf.copy(), ref[i]) <= 1e-5
+        assert e.info().status == ll.LL_OK
+        e.stop()
+
+
 def test_closed_loop_bench_outputs():
     net, Ws, bs = ll.config_params(0)
     xs = ll.config_inputs(0, 32)

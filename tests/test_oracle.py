@@ -172,3 +172,16 @@ def test_stats_match_reference_conventions():
     assert st["sd"] == pytest.approx(np.std(xs), rel=1e-9)
     assert ll.compute_stats([4.0])["p99"] == 4.0
     assert ll.compute_stats([])["p50"] == 0.0
+
+
+@pytest.mark.parametrize("cfg", [0, 1, 2, 3])
+def test_oracle_workload_generators_match_the_product_generators(cfg):
+    # bench.py's reference arm draws its weights and inputs from oracle/gen.cpp so that it
+    # loads no product library; both generators must give the same bytes
+    dims, acts, Wo, bo = oracle.workload_params(cfg)
+    net, Wp, bp = ll.config_params(cfg)
+    assert dims == net.dims and acts == net.acts
+    assert all(np.array_equal(a, b) for a, b in zip(Wo, Wp))
+    assert all(np.array_equal(a, b) for a, b in zip(bo, bp))
+    assert np.array_equal(oracle.workload_inputs(cfg, 37), ll.config_inputs(cfg, 37))
+    assert np.array_equal(oracle.fill_normal(1000, 0.0, 0.02, 2), ll.fill_normal(1000, 0.0, 0.02, 2))

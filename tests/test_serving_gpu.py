@@ -80,17 +80,27 @@ def test_poisson_stream_is_split_across_ranks_and_fully_served(cfg0):
     assert 0.025 < el < 0.5
 
 
-def test_micro_batched_ring_matches_single_requests(cfg0):
-    # requests taken together from the ring run the same FMA sequence per row as one request
-    # alone, so the replies are bit-identical to single requests (and within 1e-5 of the oracle)
-    net, Ws, bs, xs, ref = cfg0
+@pytest.fixture(scope="module")
+def single(cfg0):
+    """Replies to every input row served alone (one request per pass)."""
+    net, Ws, bs, xs, _ = cfg0
     with ll.Engine(net, Ws, bs, opts=opts()) as one:
-        single = [one.infer(xs[i])[0] for i in range(45)]
+        return np.stack([one.infer(xs[i])[0] for i in range(xs.shape[0])])
+
+
+def test_micro_batched_ring_matches_single_requests(cfg0, single):
+    # requests taken together from the ring run the same FMA sequence per row as one request
+    # alone, so the replies are bit-identical to single requests (and within 1e-5 of the oracle).
+    # ll_submit_many writes a whole burst before the device can take its first request, so
+    # the device finds the rest of the burst waiting and takes it several rows per pass.
+    net, Ws, bs, xs, ref = cfg0
     with ll.Engine(net, Ws, bs, opts=opts(ring_slots=8, micro_batch=4)) as e:
         assert e.info().kernel_variant == 2
         n = 0
-        for burst in (8, 1, 5, 3, 8, 7, 2, 6):  # ragged bursts; the ring wraps five times
-            seqs = [e.submit(xs[n + i]) for i in range(burst)]
+        bursts = (8, 1, 5, 3, 8, 7, 2, 6, 8, 8)  # ragged bursts; the ring wraps several times
+        for burst in bursts:
+            seqs = e.submit_many(xs[n:n + burst])
+            assert len(seqs) == burst
             order = range(burst) if burst % 2 else reversed(range(burst))
             for i in order:
                 y = e.poll(seqs[i])[0]
@@ -103,7 +113,47 @@ def test_micro_batched_ring_matches_single_requests(cfg0):
         inf = e.info()
         assert inf.status == ll.LL_OK
         assert inf.rows == n + 5
-        assert inf.passes < inf.rows  # bursts of 8 were taken several requests per pass
+        # each burst of 8 takes at most 1 + 1 + 2 passes (the first poll may read a stale
+        # seq_in; then one single-slot poll and 4-row reads), so the 8-row bursts alone save
+        # at least 4 passes each
+        assert inf.passes <= inf.rows - 4 * bursts.count(8)
+
+
+def test_submit_many_refuses_a_burst_larger_than_the_free_slots(cfg0, single):
+    net, Ws, bs, xs, _ = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=4, micro_batch=4)) as e:
+        seqs = e.submit_many(xs[:3])
+        with pytest.raises(ll.LLError) as busy:
+            e.submit_many(xs[3:5])
+        assert busy.value.code == ll.LL_ERR_BUSY
+        seqs += e.submit_many(xs[3:4])
+        for i, s in enumerate(seqs):
+            assert np.array_equal(e.poll(s)[0], single[i])
+    with ll.Engine(net, Ws, bs) as tb:  # the TickBuffer holds one request
+        with pytest.raises(ll.LLError) as bad:
+            tb.submit_many(xs[:2])
+        assert bad.value.code == ll.LL_ERR_INVALID_ARG
+        s = tb.submit_many(xs[:1])[0]
+        assert np.array_equal(tb.poll(s)[0], single[0])
+
+
+@pytest.mark.parametrize("kw", [dict(ring_slots=8, micro_batch=4), dict(ring_slots=8), dict(ring_slots=16, kernel_variant=1)])
+def test_ring_kept_full_replies_match_single_requests(cfg0, single, kw):
+    # the closed loop with every ring slot in use (bench_ring): replies come back in order and
+    # equal the single-request replies bit for bit
+    net, Ws, bs, xs, ref = cfg0
+    n = 3000
+    with ll.Engine(net, Ws, bs, opts=opts(**kw)) as e:
+        lat, el, ys = e.bench_ring(xs, n, kw["ring_slots"], keep_outputs=True)
+        e.stop()
+        inf = e.info()
+        assert inf.status == ll.LL_OK
+    rows = np.arange(n) % xs.shape[0]
+    assert np.array_equal(ys, single[rows])
+    assert rel_err(ys, ref[rows]) <= 1e-5
+    assert np.all(np.isfinite(lat)) and lat.min() > 0.0 and el > 0.0
+    if kw.get("micro_batch", 1) > 1:
+        assert inf.passes < inf.rows  # a full ring is taken several requests per pass
 
 
 def test_micro_batched_ring_survives_idle_relaunch(cfg0):
@@ -132,15 +182,35 @@ def test_micro_batch_is_refused_where_it_cannot_run(cfg0, kw):
     assert e.value.code == ll.LL_ERR_UNSUPPORTED
 
 
-def test_micro_batched_poisson_stream_is_fully_served(cfg0):
-    net, Ws, bs, xs, _ = cfg0
+def test_micro_batched_poisson_stream_is_fully_served(cfg0, single):
+    # 1 M requests/s offered overloads one GPU: the ring stays full and the device takes
+    # several requests per pass; every reply is checked against the same request served
+    # alone (bit for bit) and against the oracle
+    net, Ws, bs, xs, ref = cfg0
     with ll.Engine(net, Ws, bs, opts=opts(ring_slots=8, micro_batch=4)) as e:
-        lat, el = e.serve_poisson(xs, 20000, 1_000_000.0, seed=5)
+        lat, el, ys, idx = e.serve_poisson(xs, 20000, 1_000_000.0, seed=5, keep_outputs=True)
         e.stop()
         inf = e.info()
         assert inf.status == ll.LL_OK
     assert len(lat) == 20000 and np.all(np.isfinite(lat)) and lat.min() > 0.5
+    assert np.array_equal(idx, np.arange(20000))  # one rank: every request, in arrival order
+    rows = idx % xs.shape[0]
+    assert np.array_equal(ys, single[rows])
+    assert rel_err(ys, ref[rows]) <= 1e-5
     assert inf.passes < inf.rows  # an overloaded stream keeps the ring full: several rows per pass
+
+
+def test_poisson_replies_of_two_ranks_cover_the_stream(cfg0, single):
+    net, Ws, bs, xs, _ = cfg0
+    total = 2000
+    got = []
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=8, micro_batch=4)) as e:
+        for rank in (0, 1):
+            _, _, ys, idx = e.serve_poisson(xs, total, 200_000.0, seed=7, rank=rank, world=2, keep_outputs=True)
+            assert np.all(np.diff(idx) > 0)
+            assert np.array_equal(ys, single[idx % xs.shape[0]])
+            got.append(idx)
+    assert np.array_equal(np.sort(np.concatenate(got)), np.arange(total))
 
 
 def test_ring_on_a_multi_cluster_pipeline():

@@ -8,14 +8,17 @@ activations live in a static, library-owned device array instead.
 This file sorts last so that a run stopping at the first failure has already run
 every other test.  The checks: through the C ABI, two calls in a row on different
 inputs give the same outputs as the existing launch-per-layer entry point
-(ll_layered_mlp, which allocates its own buffers), within the fp32 tolerance used
-everywhere else (1e-5 norm-wise relative); and a net wider than the static array
-is refused with a clear error.
+(ll_layered_mlp, which allocates its own buffers) and as the CPU oracle, within the
+fp32 tolerance used everywhere else (1e-5 norm-wise relative); a bias-less net
+with three hidden layers (so both halves of the static array carry activations)
+does the same; and a net wider than the static array is refused with a clear
+error.
 """
 import numpy as np
 import pytest
 
 import low_latency_inference_gpu_b200 as ll
+import oracle
 from conftest import rel_err
 
 
@@ -41,6 +44,27 @@ def test_noalloc_forward_matches_existing_entry_point_twice():
             _, y_ref = m.bench(ll.RUN_DIRECT_KERNEL, xs[i:i + 1], 1)
             assert np.isfinite(outs[i]).all()
             assert rel_err(outs[i], y_ref) <= 1e-5
+            assert rel_err(outs[i], oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs[i:i + 1])[0]) <= 1e-5
+    assert not np.array_equal(outs[0], outs[1])  # two different requests, not one stale result
+
+
+@pytest.mark.gpu
+@pytest.mark.timeout(300)
+def test_noalloc_forward_without_biases_through_both_scratch_halves():
+    torch = pytest.importorskip("torch")
+    net = ll.mlp([64, 96, 200, 48, 16], ll.ACT_RELU)  # hidden layers write halves 0, 1, 0
+    Ws, _ = ll.init_params(net, ll.INIT_XAVIER_UNIFORM, 11)
+    zeros = [np.zeros(d, np.float32) for d in net.dims[1:]]
+    xs = ll.fill_uniform(2 * 64, -1.0, 1.0, 12).reshape(2, 64)
+    dW = [torch.from_numpy(np.ascontiguousarray(w)).cuda() for w in Ws]
+    for i in range(2):
+        dx = torch.from_numpy(np.ascontiguousarray(xs[i])).cuda()
+        dy = torch.full((net.dims[-1],), float("nan"), device="cuda")
+        ll.mlp_forward_noalloc(net, [t.data_ptr() for t in dW], None, dx.data_ptr(), dy.data_ptr())
+        torch.cuda.synchronize()
+        y = dy.cpu().numpy()
+        assert np.isfinite(y).all()
+        assert rel_err(y, oracle.mlp_f32(net.dims, net.acts, Ws, zeros, xs[i:i + 1])[0]) <= 1e-5
 
 
 @pytest.mark.gpu
