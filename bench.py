@@ -14,7 +14,7 @@ Reported:
   e2e     inferences/s through the C ABI with host buffers: a closed loop that
           keeps the tagged request ring full (each request's x copied from a host
           array into its ring slot, its y copied out to a host array as soon as
-          it is there; up to 4 waiting requests taken per kernel pass), one host
+          it is there; up to 16 waiting requests taken per kernel pass), one host
           thread per GPU.  p50/p99 are the batch-1 latency of a single sequential
           stream (ll_infer's closed loop: write x, spin until y is there, copy y
           out; host steady clock) on the same engine.  The tagged mailbox carries
@@ -31,7 +31,7 @@ Reported:
           host copies), and the same rows through the resident small-batch engine
           (TickBuffer end to end, and device time per forward from a queue).
   serving open-loop Poisson arrivals at 50k / 200k / 1M requests/s aggregate over the
-          N GPUs (config-0 MLP on every GPU, 8-slot tagged request ring, up to 4
+          N GPUs (config-0 MLP on every GPU, 32-slot tagged request ring, up to 16
           waiting requests per kernel pass): p50/p99 latency from the scheduled
           arrival, sustained throughput and requests per pass.
   --impl reference  runs the reference's CPU forward on all host cores instead
@@ -61,7 +61,8 @@ FALLBACK_HBM_GBS = 6650.0
 CONFIG = {"workload": WORKLOAD, "batch": 1, "precision": "fp32 weights, activations and accumulation",
           "l2": "GPU arm: a 256 MiB buffer is written between timed device launches; the weights stay on chip "
                 "(registers) for a whole launch by design"}
-RING_SLOTS = 16  # e2e throughput leg: ring slots kept full
+RING_SLOTS = 64  # e2e throughput leg: ring slots kept full
+MICRO_BATCH = 16  # waiting requests the register-resident kernel takes in one pass
 # DRAM traffic of one device-queue launch of the 8-CTA register-resident kernel, from
 # the committed ncu capture (1.352 MB for 2000 requests): the eight per-CTA register
 # images once (812 KB), then ~270 B per request (input row, stamp); scaled to R requests.
@@ -133,14 +134,14 @@ def merge_serving(per_rank, rate, n_total):
 
 def run_serving(ll, net, Ws, bs, xs, rank, world, hg, dev):
     """Open-loop Poisson streams (seed 5) over all ranks: each rank serves the requests drawn
-    for it through its own engine (tagged mailbox, 8-slot ring, up to 4 waiting requests
-    taken per kernel pass); latency from the scheduled arrival; merged on rank 0.  The
+    for it through its own engine (tagged mailbox, 32-slot ring, up to MICRO_BATCH waiting
+    requests taken per kernel pass); latency from the scheduled arrival; merged on rank 0.  The
     resident kernel is stopped after each stream so that its pass / request counters are
     read (the next stream relaunches it before its first arrival)."""
     o = ll.default_opts()
     o.mailbox_format = 1
-    o.ring_slots = 8
-    o.micro_batch = 4
+    o.ring_slots = 32
+    o.micro_batch = MICRO_BATCH
     out = []
     with ll.Engine(net, Ws, bs, device=dev, opts=o) as e:
         e.serve_poisson(xs, 2000, 50_000.0, seed=99, rank=rank, world=world)  # warm-up stream
@@ -157,7 +158,7 @@ def run_serving(ll, net, Ws, bs, xs, rank, world, hg, dev):
             out.append(merge_serving(per_rank, rate, n_total))
     return {"workload": "config-0 MLP replicated per GPU, Poisson arrivals (std::mt19937_64 seed 5), "
                         "each request to a GPU drawn uniformly; U[-1,1] inputs",
-            "mailbox": "tagged, 8-slot request ring, micro_batch 4", "seconds_of_arrivals": SERVING_SECONDS,
+            "mailbox": f"tagged, 32-slot request ring, micro_batch {MICRO_BATCH}", "seconds_of_arrivals": SERVING_SECONDS,
             "rates": out}
 
 
@@ -639,10 +640,10 @@ def main():
         return t1 - t0, np.concatenate(lat_all), relaunches
 
     def ring_loop():
-        """K timed steps of R requests with the RING_SLOTS-slot ring kept full (micro_batch 4);
+        """K timed steps of R requests with the RING_SLOTS-slot ring kept full (MICRO_BATCH);
         returns (seconds, post-to-reply latencies, relaunches)."""
         o = opts(1)
-        o.ring_slots, o.micro_batch = RING_SLOTS, 4
+        o.ring_slots, o.micro_batch = RING_SLOTS, MICRO_BATCH
         lat_all = []
         with ll.Engine(net, Ws, bs, device=dev, opts=o) as eng:
             eng.start()
@@ -751,7 +752,7 @@ def main():
                 "d2h_bytes_per_step": world * R * 16 * 4,
                 "mode": f"closed loop keeping a {RING_SLOTS}-slot tagged request ring full, one host thread per "
                         "GPU; x copied from a host array into the ring slot and y out to a host array per request; "
-                        "up to 4 waiting requests per kernel pass",
+                        f"up to {MICRO_BATCH} waiting requests per kernel pass",
                 "requests_per_pass": ring_rpp,
                 "ring_latency_p50_us": s_ring["p50"], "ring_latency_p99_us": s_ring["p99"],
                 "p50_us": s_e2e["p50"], "p99_us": s_e2e["p99"], "p90_us": s_e2e["p90"],

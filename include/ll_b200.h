@@ -111,8 +111,9 @@ typedef struct ll_engine_opts {
                                    the device serves them in order, slot after slot */
     int32_t micro_batch;        /* request ring on the register-resident kernel: the device takes up to
                                    this many waiting requests (consecutive slots, each complete) in one
-                                   poll and runs them as one small batch (1..4, at most ring_slots;
-                                   0 = 1).  Replies still go to each request's own slot. */
+                                   poll and runs them as one small batch (1..16, at most ring_slots;
+                                   0 = 1).  Replies still go to each request's own slot and are
+                                   bit-identical to the same requests served one at a time. */
     int32_t reserved[2];
 } ll_engine_opts;
 

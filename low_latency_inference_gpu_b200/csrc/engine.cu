@@ -507,14 +507,16 @@ int alloc_mailbox(ll_engine *e)
     }
     e->micro = e->opts.micro_batch < 1 ? 1 : e->opts.micro_batch;
     if (e->micro > 1) {
-        // the multi-slot poll holds every chunk of the slots it reads in warp 0's registers
-        const int chunks = e->micro * ((e->in_dim + 2) / 3);
+        // the multi-slot read holds whole slots in the registers of up to kTagReadWarpsMax warps
+        const int nxc = (e->in_dim + 2) / 3;
+        const int rpw = tag_rows_per_warp(nxc);
+        const int warps = rpw > 0 ? (e->micro + rpw - 1) / rpw : kTagReadWarpsMax + 1;
         if (e->opts.mailbox_format != 1 || e->micro > e->ring || e->micro > e->micro_max ||
-            chunks > 32 * kTagChunksPerLane) {
+            warps > kTagReadWarpsMax) {
             llh::set_error("micro_batch %d needs the tagged mailbox, at most ring_slots (%d), at most the rows "
                            "the kernel carries (%d: the register-resident kernel of a shape with room for "
-                           "%d), and at most %d x chunks per poll (%d)",
-                           e->micro, e->ring, e->micro_max, kFast3Rows, 32 * kTagChunksPerLane, chunks);
+                           "%d), and whole slots in at most %d reading warps (%d slot(s) per warp here)",
+                           e->micro, e->ring, e->micro_max, kFast3Rows, kTagReadWarpsMax, rpw);
             return LL_ERR_UNSUPPORTED;
         }
     }

@@ -30,10 +30,13 @@
 namespace llk {
 
 // Rows one pass of the register-resident kernel can carry: requests taken together from
-// the ring (micro-batching); a pass over 2..4 rows runs the 4-row code.  Shapes whose
-// weights leave fewer than ~70 registers free (more than 56 weights per thread) carry one
-// row: the 4-row accumulators would spill.
-constexpr int kFast3Rows = 4;
+// the ring (micro-batching).  A pass over 2..16 rows runs the 4-row code over groups of 4
+// rows, each weight held in a register used once per row in the same FMA order as for a
+// request alone (so replies are bit-identical to single requests).  Shapes whose weights
+// leave fewer than ~70 registers free (more than 56 weights per thread) carry one row: the
+// 4-row accumulators would spill.
+constexpr int kFast3Rows = 16;
+constexpr int kFast3Group = 4;
 
 template <int IN, int H1, int H2, int OUT, int C>
 struct Fast3Shape {
@@ -53,6 +56,8 @@ struct Fast3Shape {
     static_assert(IN % 4 == 0, "x is moved in 16-byte pieces");
     static constexpr int NB = H1 + R2 + OUT;  // biases per CTA image
     static constexpr int MaxRows = NW <= 56 ? kFast3Rows : 1;
+    static_assert(MaxRows <= T / 32, "rank 0 finishes one row per warp");
+    static_assert(MaxRows == 1 || MaxRows % kFast3Group == 0, "rows come in groups");
 };
 
 __device__ __forceinline__ float relu_or(float v, int act)
@@ -72,6 +77,10 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
     __shared__ __align__(16) float gath[MB * C * OUT];  // [row][rank][output]
     __shared__ __align__(16) float yo[MB * YO];
     __shared__ uint32_t rseq[MB];  // rank 0: sequence number of each row taken together
+    __shared__ uint32_t bad_words[kTagReadWarpsMax];  // rank 0: incomplete-row masks of a multi-slot read
+    // rank 0: the host had posted beyond the last request taken.  Indexed by pass parity: warp 0
+    // sets the flag for the next pass while the other reading warps may still read this pass's.
+    __shared__ uint32_t s_backlog[2];
     constexpr int NXC = (IN + 2) / 3;  // tagged chunks per row
     __shared__ __align__(16) uint4 xch[MB * NXC];  // peers: the tagged chunks rank 0 forwards
     __shared__ __align__(16) float bias[S::NB];
@@ -106,6 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
         sh.fail = 0;
         sh.abort = 0;
         sh.hstop = 0;
+        s_backlog[0] = s_backlog[1] = 0;
         fence_mbar_init_cluster();
         if (leader)
             st_relaxed_sys_u32(&p.ctrl->state, ST_LOADING);
@@ -142,7 +152,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
     const int r2 = tid / S::S2, s2 = tid % S::S2;
     const uint32_t x_addr = smem_u32(xs), h_addr = smem_u32(sh.hdr), g_addr = smem_u32(gath);
     uint32_t last = p.last_seq, n_done = 0, ph_req = 0, ph_g = 0, ph_x = 0, passes = 0;
-    bool backlog = false;  // rank 0, warp 0: the host had posted beyond the last request taken
+    // warps of rank 0 that read a multi-slot batch (whole slots per warp)
+    constexpr int NXC_ = (IN + 2) / 3;
+    constexpr int RPW = tag_rows_per_warp(NXC_);
+    static_assert(RPW >= 1, "a reading warp holds at least one slot");
+    const int read_warps = p.micro_batch > 1 ? (p.micro_batch + RPW - 1) / RPW : 1;
 
     while (ok) {
         uint32_t seq, nb = 1;
@@ -175,13 +189,14 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                 trace(k, n_done, 1);
         } else if (leader) {
             if (p.mailbox_format == 1) {
-                if (warp == 0) {
+                if (warp < read_warps) {
                     // x arrives with the doorbell.  On a micro-batched ring the poll also reads
                     // the host's seq_in (the last sequence number posted); when it is ahead of
                     // the request just taken, requests are waiting, and the next pass takes up to
-                    // micro_batch of them with one read of their slots.  Otherwise (and when that
-                    // read finds nothing) the single-slot poll waits for the next request: a read
-                    // spanning several slots was measured ~2 us slower to see a new request.
+                    // micro_batch of them with one read of their slots (warps 0..read_warps-1,
+                    // whole slots each).  Otherwise (and when that read finds nothing) warp 0's
+                    // single-slot poll waits for the next request: a read spanning several slots
+                    // was measured ~2 us slower to see a new request.
                     // The polling lanes forward the raw chunks to the peers from registers as
                     // soon as the tags match (header {seq, rows} + row 0 on the peers' request
                     // barrier, rows 1.. on their x barrier).
@@ -189,25 +204,28 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     uint32_t c = 0, posted = 0;
                     int got = 0;
                     if constexpr (MB > 1) {
-                        if (backlog) {
-                            got = take_tagged_rows(k, last, xs, n_done, p.micro_batch, rseq, &posted, &fwd);
-                            if (got > 0)
-                                c = seq_after(last, got);
+                        // written by warp 0 during the previous pass, before its barriers
+                        if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[passes & 1u]))
+                            got = take_tagged_rows(k, last, xs, n_done, p.micro_batch, rseq, &posted, bad_words,
+                                                   read_warps, &fwd);
+                    }
+                    if (warp == 0) {
+                        if (got > 0) {
+                            c = seq_after(last, got);
+                        } else {
+                            c = poll_tagged(k, last, xs, ring_slot(p, n_done), p.micro_batch > 1 ? &posted : nullptr,
+                                            &fwd);
+                            got = 1;
                         }
-                    }
-                    if (got == 0) {
-                        c = poll_tagged(k, last, xs, ring_slot(p, n_done), p.micro_batch > 1 ? &posted : nullptr,
-                                        &fwd);
-                        got = 1;
-                    }
-                    backlog = p.micro_batch > 1 && c != kCmdExit && (int32_t)(posted - c) > 0;
-                    if (tid == 0)
-                        sh.nrows = (uint32_t)got;
-                    if (tid == 0) {
-                        if (c == kCmdExit)
-                            broadcast_abort(k);
-                        sh.cmd = c;
-                        trace(k, n_done, 0);
+                        if (tid == 0) {
+                            s_backlog[(passes + 1u) & 1u] =
+                                (p.micro_batch > 1 && c != kCmdExit && (int32_t)(posted - c) > 0) ? 1u : 0u;
+                            sh.nrows = (uint32_t)got;
+                            if (c == kCmdExit)
+                                broadcast_abort(k);
+                            sh.cmd = c;
+                            trace(k, n_done, 0);
+                        }
                     }
                 }
             } else if (tid == 0) {
@@ -288,19 +306,23 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
         }
 
         // ---------------- the layers, over nb rows (weights used once per row) ----------------
-        auto pass = [&](auto rows) -> bool {
-            constexpr int NB = decltype(rows)::value;
+        // GR = rows computed together: 1 for a single request, kFast3Group for a micro-batch, whose
+        // rows are walked in groups of GR (rows past nb in the last group compute on stale inputs
+        // inside the buffers and are never sent or stored)
+        auto pass = [&](auto group_rows) -> bool {
+            constexpr int GR = decltype(group_rows)::value;
+            const int ng = GR == 1 ? 1 : ((int)nb + GR - 1) / GR;
             // ---------------- layer 1 (replicated) ----------------
-            {
-                const float4 *x4 = reinterpret_cast<const float4 *>(xs) + s1;
-                float a0[NB], a1[NB];
+            for (int g = 0; g < ng; ++g) {
+                const float4 *x4 = reinterpret_cast<const float4 *>(xs + g * GR * IN) + s1;
+                float a0[GR], a1[GR];
 #pragma unroll
-                for (int r = 0; r < NB; ++r)
+                for (int r = 0; r < GR; ++r)
                     a0[r] = a1[r] = 0.f;
 #pragma unroll
                 for (int j = 0; j < S::K1 / 4; ++j) {
 #pragma unroll
-                    for (int r = 0; r < NB; ++r) {
+                    for (int r = 0; r < GR; ++r) {
                         const float4 v = x4[r * (IN / 4) + j * S::S1];
                         a0[r] = fmaf(w1[4 * j], v.x, a0[r]);
                         a1[r] = fmaf(w1[4 * j + 1], v.y, a1[r]);
@@ -309,29 +331,29 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     }
                 }
 #pragma unroll
-                for (int r = 0; r < NB; ++r) {
+                for (int r = 0; r < GR; ++r) {
                     float acc = a0[r] + a1[r];
 #pragma unroll
                     for (int o = S::S1 / 2; o > 0; o >>= 1)
                         acc += __shfl_xor_sync(0xffffffffu, acc, o);
                     if (s1 == 0)
-                        h1[r * H1 + r1] = relu_or(acc + bias[r1], act1);
+                        h1[(g * GR + r) * H1 + r1] = relu_or(acc + bias[r1], act1);
                 }
             }
             __syncthreads();
             if (leader && tid == 0)
                 trace(k, n_done, 3);
             // ---------------- layer 2 (rows split over the cluster) ----------------
-            {
-                const float4 *v4 = reinterpret_cast<const float4 *>(h1) + s2;
-                float a0[NB], a1[NB];
+            for (int g = 0; g < ng; ++g) {
+                const float4 *v4 = reinterpret_cast<const float4 *>(h1 + g * GR * H1) + s2;
+                float a0[GR], a1[GR];
 #pragma unroll
-                for (int r = 0; r < NB; ++r)
+                for (int r = 0; r < GR; ++r)
                     a0[r] = a1[r] = 0.f;
 #pragma unroll
                 for (int j = 0; j < S::K2 / 4; ++j) {
 #pragma unroll
-                    for (int r = 0; r < NB; ++r) {
+                    for (int r = 0; r < GR; ++r) {
                         const float4 v = v4[r * (H1 / 4) + j * S::S2];
                         a0[r] = fmaf(w2[4 * j], v.x, a0[r]);
                         a1[r] = fmaf(w2[4 * j + 1], v.y, a1[r]);
@@ -340,13 +362,13 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     }
                 }
 #pragma unroll
-                for (int r = 0; r < NB; ++r) {
+                for (int r = 0; r < GR; ++r) {
                     float acc = a0[r] + a1[r];
 #pragma unroll
                     for (int o = S::S2 / 2; o > 0; o >>= 1)
                         acc += __shfl_xor_sync(0xffffffffu, acc, o);
                     if (s2 == 0)
-                        h2[r * S::R2 + r2] = relu_or(acc + bias[H1 + r2], act2);
+                        h2[(g * GR + r) * S::R2 + r2] = relu_or(acc + bias[H1 + r2], act2);
                 }
             }
             if (own_x && !leader) {
@@ -362,8 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
             // ---------------- layer 3 (K-split partials -> rank 0) ----------------
             if (warp < OUT) {
                 float mine = 0.f;  // lane r sends row r's partial
-#pragma unroll
-                for (int r = 0; r < NB; ++r) {
+                for (int r = 0; r < (GR == 1 ? 1 : (int)nb); ++r) {
                     float acc = 0.f;
 #pragma unroll
                     for (int j = 0; j < S::K3; ++j)
@@ -396,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     // < OUT finish one output each, then the storing lanes pick up their 16-byte
                     // groups (full-warp shuffles here cost ~1650 cycles in this loop, the
                     // shared-memory round ~60)
-                    const int r = NB == 1 ? 0 : warp;
+                    const int r = GR == 1 ? 0 : warp;
                     float *yr = yo + r * YO;
                     if (lane < OUT) {
                         float v = 0.f;
@@ -410,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     // tagged output: lane c packs {y[3c], y[3c+1], y[3c+2], seq}
                     constexpr int NYC = (OUT + 2) / 3;
                     if (tagged) {
-                        const uint32_t sq = NB == 1 ? seq : rseq[r];
+                        const uint32_t sq = GR == 1 ? seq : rseq[r];
                         if (lane < NYC)
                             st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done + (uint32_t)r) * p.ring_stride_f +
                                                   4 * lane,
@@ -443,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
         if constexpr (MB == 1)
             ok = pass(std::integral_constant<int, 1>{});
         else
-            ok = nb == 1 ? pass(std::integral_constant<int, 1>{}) : pass(std::integral_constant<int, MB>{});
+            ok = nb == 1 ? pass(std::integral_constant<int, 1>{}) : pass(std::integral_constant<int, kFast3Group>{});
         if (!ok)
             break;
         ++passes;

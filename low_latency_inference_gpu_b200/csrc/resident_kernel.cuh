@@ -397,50 +397,77 @@ __device__ __forceinline__ uint32_t seq_after(uint32_t last, int m)
     return s;
 }
 
-// Tagged request ring, micro-batched (warp 0 of the dispatcher): ONE read of the ring
-// slots of requests n .. n+maxb-1 of this launch (slot ring_slot(n + i)), taking every
-// request that is complete and follows without a gap: slot n+i is taken when each of its
-// chunks carries the (i+1)-th sequence number after `last`.  One PCIe round trip reads all
-// maxb slots (maxb * nxc <= 32 * kTagChunksPerLane chunks, checked on the host).  Row i of
-// x goes to X + i * in_dim and its sequence number to seqs[i]; *posted = the host's seq_in
-// word (the last sequence number it posted), read by lane 31 in the same round trip.
-// Returns the rows taken
-// (0 when request n is not complete yet; then the caller waits on its slot alone with
-// poll_tagged, whose single-slot round trips are shorter: a read that spans several slots
-// was measured ~2 us slower to detect a new request).
+// Rows of a tagged ring one reading warp holds in registers (whole slots: 32 lanes x
+// kTagChunksPerLane chunks), and the most warps a multi-slot read may use.
+__host__ __device__ constexpr int tag_rows_per_warp(int nxc)
+{
+    return (32 * kTagChunksPerLane) / nxc;
+}
+constexpr int kTagReadWarpsMax = 16;
+
+// Tagged request ring, micro-batched (warps 0..nw-1 of the dispatcher): ONE read of the
+// ring slots of requests n .. n+maxb-1 of this launch (slot ring_slot(n + i)), taking
+// every request that is complete and follows without a gap: slot n+i is taken when each
+// of its chunks carries the (i+1)-th sequence number after `last`.  Warp w reads the
+// rows [w * rpw, (w + 1) * rpw) (rpw = tag_rows_per_warp(nxc) whole slots, its chunks in
+// registers); the warps' loads are all in flight at once, so one PCIe round trip reads
+// all maxb slots (maxb <= nw * rpw <= kTagReadWarpsMax * rpw and maxb <= 32, checked on
+// the host).  Each warp's mask of incomplete rows goes through bad_words[w] (shared
+// memory) and a named barrier (id 2, nw warps), so every warp sees the same first gap.
+// Row i of x goes to X + i * in_dim and its sequence number to seqs[i] (warp 0 writes
+// them); in warp 0, *posted = the host's seq_in word (the last sequence number it
+// posted), read by lane 31 in the same round trip.
+// Returns the rows taken, the same in every reading warp (0 when request n is not
+// complete yet; then the caller waits on its slot alone with poll_tagged, whose
+// single-slot round trips are shorter: a read that spans several slots was measured
+// ~2 us slower to detect a new request).
 __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uint32_t n, int maxb, uint32_t *seqs,
-                                uint32_t *posted, const ChunkFwd *fwd = nullptr)
+                                uint32_t *posted, uint32_t *bad_words, int nw, const ChunkFwd *fwd = nullptr)
 {
     const Params &p = *k.p;
     const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     const int nxc = (p.in_dim + 2) / 3;
-    const int total = maxb * nxc;
+    const int r0 = warp * tag_rows_per_warp(nxc);
+    const int rows_here = min(tag_rows_per_warp(nxc), maxb - r0);
+    const int total = rows_here > 0 ? rows_here * nxc : 0;
     uint4 c[kTagChunksPerLane];
     int row[kTagChunksPerLane], ch[kTagChunksPerLane];
 #pragma unroll
     for (int j = 0; j < kTagChunksPerLane; ++j) {
         const int q = lane + 32 * j;
-        row[j] = q < total ? q / nxc : 0;
-        ch[j] = q - row[j] * nxc;
+        const int rl = q < total ? q / nxc : 0;
+        row[j] = r0 + rl;
+        ch[j] = q - rl * nxc;
         if (q < total)
             c[j] = ld_relaxed_sys_v4_u32(reinterpret_cast<const unsigned *>(
                 p.mb_x + (size_t)ring_slot(p, n + (uint32_t)row[j]) * p.ring_stride_f + 4 * ch[j]));
     }
-    const uint32_t seen = lane == 31 ? ld_relaxed_sys(&p.mb->seq_in) : 0u;
-    *posted = __shfl_sync(0xffffffffu, seen, 31);
+    const uint32_t seen = (warp == 0 && lane == 31) ? ld_relaxed_sys(&p.mb->seq_in) : 0u;
+    if (warp == 0)
+        *posted = __shfl_sync(0xffffffffu, seen, 31);
     uint32_t bad = 0;
 #pragma unroll
     for (int j = 0; j < kTagChunksPerLane; ++j)
         if (lane + 32 * j < total && c[j].w != seq_after(last, row[j] + 1))
             bad |= 1u << row[j];
     bad = __reduce_or_sync(0xffffffffu, bad);
-    const int nb = __ffs(bad | (1u << maxb)) - 1;  // complete slots before the first gap
+    if (nw > 1) {
+        if (lane == 0)
+            bad_words[warp] = bad;
+        asm volatile("bar.sync 2, %0;" ::"r"(32 * nw) : "memory");
+        bad = 0;
+        for (int w = 0; w < nw; ++w)
+            bad |= bad_words[w];
+    }
+    const uint32_t stop_bit = maxb < 32 ? (1u << maxb) : 0u;
+    const int nb = (bad | stop_bit) ? __ffs(bad | stop_bit) - 1 : 32;  // complete slots before the first gap
     if (fwd && nb > 0) {
 #pragma unroll
         for (int j = 0; j < kTagChunksPerLane; ++j)
             if (lane + 32 * j < total && row[j] < nb)
                 fwd_chunk(*fwd, row[j], ch[j], nxc, c[j]);
-        if (lane == 0)
+        if (warp == 0 && lane == 0)
             fwd_header(*fwd, seq_after(last, nb), (uint32_t)nb);
     }
 #pragma unroll
@@ -453,7 +480,7 @@ __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uin
                     X[row[j] * p.in_dim + 3 * ch[j] + e] = p.act_bf16 ? round_bf16(v[e]) : v[e];
         }
     }
-    if (lane < nb)
+    if (warp == 0 && lane < nb)
         seqs[lane] = seq_after(last, lane + 1);
     return nb;
 }

@@ -140,9 +140,12 @@ def test_submit_many_refuses_a_burst_larger_than_the_free_slots(cfg0, single):
 @pytest.mark.parametrize("kw", [dict(ring_slots=8, micro_batch=4), dict(ring_slots=8), dict(ring_slots=16, kernel_variant=1)])
 def test_ring_kept_full_replies_match_single_requests(cfg0, single, kw):
     # the closed loop with every ring slot in use (bench_ring): replies come back in order and
-    # equal the single-request replies bit for bit
+    # equal, bit for bit, the replies of the same kernel to single requests
     net, Ws, bs, xs, ref = cfg0
     n = 3000
+    if "kernel_variant" in kw:
+        with ll.Engine(net, Ws, bs, opts=opts(kernel_variant=kw["kernel_variant"])) as one:
+            single = np.stack([one.infer(xs[i])[0] for i in range(xs.shape[0])])
     with ll.Engine(net, Ws, bs, opts=opts(**kw)) as e:
         lat, el, ys = e.bench_ring(xs, n, kw["ring_slots"], keep_outputs=True)
         e.stop()
@@ -172,7 +175,7 @@ def test_micro_batched_ring_survives_idle_relaunch(cfg0):
 
 
 @pytest.mark.parametrize("kw", [dict(ring_slots=2, micro_batch=4),       # more rows than slots
-                                dict(ring_slots=8, micro_batch=5),       # more than one pass carries
+                                dict(ring_slots=32, micro_batch=17),     # more than one pass carries
                                 dict(ring_slots=8, micro_batch=4, kernel_variant=1),  # generic kernel
                                 dict(ring_slots=8, micro_batch=4, cluster_size=4)])   # 66 weights/thread: 1 row
 def test_micro_batch_is_refused_where_it_cannot_run(cfg0, kw):
