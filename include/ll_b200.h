@@ -101,7 +101,14 @@ typedef struct ll_engine_opts {
                                    layers handed off through L2 (bf16 or int8 weights, up to 32 rows,
                                    the TickBuffer mailbox or the tagged one at max_batch 1, in / out
                                    widths multiples of 4; it takes every SM, so no other resident
-                                   engine may run on the GPU).
+                                   engine may run on the GPU),
+                                   4 = pipelined ring kernel (no counterpart in the reference): the
+                                   register-resident kernel's C compute CTAs plus one I/O CTA per
+                                   cluster that reads the next waiting ring slots and writes the
+                                   replies while the compute CTAs run the layers of the previous
+                                   pass (tagged mailbox only; replies bit-identical to variant 2;
+                                   no device queue).  For request rates above what one pass at a
+                                   time sustains; asked for explicitly.
                                    Automatic picks 2 for the shapes it is compiled for, 3 for bf16 /
                                    int8 nets that qualify and whose weights exceed one 16-CTA
                                    cluster's shared memory (about 3.6 MB) unless cluster options are
@@ -129,7 +136,7 @@ typedef struct ll_engine_info {
     int32_t err_where;      /* device-side location code of the last error */
     uint32_t served;        /* last seq the device published */
     int32_t layer_modes[24];
-    int32_t kernel_variant; /* 1 generic, 2 register-resident */
+    int32_t kernel_variant; /* 1 generic, 2 register-resident, 3 resident small-batch, 4 pipelined ring */
     int32_t weight_regs;    /* register-resident: weights held per thread */
     uint32_t passes;        /* register-resident: passes over the layers by the launches that have
                                exited (ll_engine_stop, idle exit, queue runs) */

@@ -90,6 +90,7 @@ class EngineOpts(ctypes.Structure):
 
 # ll_engine_opts.kernel_variant
 VARIANT_AUTO, VARIANT_GENERIC, VARIANT_REGISTER_RESIDENT, VARIANT_RESIDENT_SMALL_BATCH = 0, 1, 2, 3
+VARIANT_PIPELINED_RING = 4
 
 
 class EngineInfo(ctypes.Structure):

@@ -17,6 +17,7 @@
 #include "fast3_kernel.cuh"
 #include "gemv_plan.h"
 #include "resident_kernel.cuh"
+#include "ring_kernel.cuh"
 
 #if defined(__x86_64__)
 #include <immintrin.h>
@@ -319,14 +320,18 @@ struct Fast3Entry {
     int K1, K2, K3, NB;
     int S1, S2, R2;
     int rows;  // rows one pass carries (micro-batching)
+    const void *ring_fn;  // pipelined ring kernel of the shape (variant 4), or null
 };
 
 template <int IN, int H1, int H2, int OUT, int C>
 Fast3Entry fast3_entry()
 {
     using S = Fast3Shape<IN, H1, H2, OUT, C>;
+    const void *ring = nullptr;
+    if constexpr (S::MaxRows == kFast3Rows)
+        ring = reinterpret_cast<const void *>(&ll_ring_kernel<IN, H1, H2, OUT, C>);
     return Fast3Entry{IN, H1, H2, OUT, C, reinterpret_cast<const void *>(&ll_fast3_kernel<IN, H1, H2, OUT, C>),
-                      S::K1, S::K2, S::K3, S::NB, S::S1, S::S2, S::R2, S::MaxRows};
+                      S::K1, S::K2, S::K3, S::NB, S::S1, S::S2, S::R2, S::MaxRows, ring};
 }
 
 const Fast3Entry *find_fast3(const ll_net_desc &net, int C)
@@ -1055,9 +1060,16 @@ void export_plan(const Params &p, ll_plan *out)
     }
 }
 
+// Register-resident kernel (variant 2) or, with `ring`, the pipelined ring kernel (variant 4:
+// the same C compute CTAs plus one I/O CTA per cluster; tagged mailbox only).
 int create_fast3(const ll_net_desc *net, const void *const *W, const float *const *b, int device,
-                 const ll_engine_opts &o, const Fast3Entry &f, ll_engine **out)
+                 const ll_engine_opts &o, const Fast3Entry &f, bool ring, ll_engine **out)
 {
+    if (ring && (!f.ring_fn || o.mailbox_format != 1)) {
+        llh::set_error("the pipelined ring kernel (variant 4) needs the tagged mailbox (mailbox_format 1) and a "
+                       "register-resident shape with room for multi-row passes (8 CTAs per cluster)");
+        return LL_ERR_UNSUPPORTED;
+    }
     size_t stride = 0;
     std::vector<uint8_t> img = pack_fast3(f, W, b, stride);
     ll_engine *e = new ll_engine();
@@ -1065,8 +1077,8 @@ int create_fast3(const ll_net_desc *net, const void *const *W, const float *cons
     e->in_dim = f.in;
     e->out_dim = f.out;
     e->max_batch = 1;
-    e->kfn = f.fn;
-    e->variant = 2;
+    e->kfn = ring ? f.ring_fn : f.fn;
+    e->variant = ring ? 4 : 2;
     e->micro_max = f.rows;
     e->weight_regs = f.K1 + f.K2 + f.K3;
     int rc = engine_common_create(e, &o);
@@ -1105,6 +1117,10 @@ int create_fast3(const ll_net_desc *net, const void *const *W, const float *cons
     if (rc) {
         ll_engine_destroy(e);
         return rc;
+    }
+    if (ring) {  // the I/O CTA is the cluster's last rank (its abort broadcast covers every rank)
+        e->grid = f.C + 1;
+        e->base.C = f.C + 1;
     }
     *out = e;
     return LL_OK;
@@ -1261,13 +1277,13 @@ int ll_engine_create_ex(const ll_net_desc *net, const void *const *W, const floa
         llh::set_error("W is NULL");
         return LL_ERR_INVALID_ARG;
     }
-    const Fast3Entry *f3 = o.kernel_variant == 1 ? nullptr : find_fast3(*net, o.cluster_size);
-    if (o.kernel_variant == 2 && !f3) {
+    const Fast3Entry *f3 = (o.kernel_variant == 1 || o.kernel_variant == 3) ? nullptr : find_fast3(*net, o.cluster_size);
+    if ((o.kernel_variant == 2 || o.kernel_variant == 4) && !f3) {
         llh::set_error("no register-resident kernel is compiled for this net shape / cluster size");
         return LL_ERR_UNSUPPORTED;
     }
     if (f3)
-        return create_fast3(net, W, b, device, o, *f3, out);
+        return create_fast3(net, W, b, device, o, *f3, o.kernel_variant == 4, out);
     if (o.kernel_variant == 3 || o.kernel_variant == 0) {
         int sms = 0;
         LL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
@@ -1773,6 +1789,10 @@ int ll_engine_run_queue(ll_engine *e, const float *d_x, float *d_y, int n_req, i
     if (!e || !d_x || !d_y || n_req < 1 || n_rows < 1 || n_rows > e->max_batch) {
         llh::set_error("ll_engine_run_queue: invalid arguments");
         return LL_ERR_INVALID_ARG;
+    }
+    if (e->variant == 4) {
+        llh::set_error("ll_engine_run_queue: the pipelined ring kernel (variant 4) serves the mailbox only");
+        return LL_ERR_UNSUPPORTED;
     }
     LL_CUDA_TRY(cudaSetDevice(e->device));
     int rc = engine_stop_kernel(e);

@@ -65,6 +65,101 @@ __device__ __forceinline__ float relu_or(float v, int act)
     return act == LL_ACT_RELU ? fmaxf(v, 0.0f) : (act == LL_ACT_GELU ? act_apply(v, LL_ACT_GELU) : v);
 }
 
+// The three layers of one pass, shared by the register-resident kernel and the pipelined
+// ring kernel (ring_kernel.cuh).  Rows are walked in ng groups of GR (rows past the last
+// request of the pass compute on stale inputs inside the buffers and are never sent or
+// stored); per row the FMA order is the same for every GR, so a request's reply does not
+// depend on how many rows its pass carried.
+//
+// Layer 1, replicated in every CTA: h1[row][r1] = act(W1[r1] . x[row] + b1[r1]); S1 threads
+// per output row, lane s1 of a row group takes the 16-byte input pieces s1, s1 + S1, ...
+template <class S, int GR, int IN, int H1>
+__device__ __forceinline__ void f3_layer1(const float (&w1)[S::K1], const float *xs, float *h1, const float *b1,
+                                          int ng, int r1, int s1, int act)
+{
+    for (int g = 0; g < ng; ++g) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(xs + g * GR * IN) + s1;
+        float a0[GR], a1[GR];
+#pragma unroll
+        for (int r = 0; r < GR; ++r)
+            a0[r] = a1[r] = 0.f;
+#pragma unroll
+        for (int j = 0; j < S::K1 / 4; ++j) {
+#pragma unroll
+            for (int r = 0; r < GR; ++r) {
+                const float4 v = x4[r * (IN / 4) + j * S::S1];
+                a0[r] = fmaf(w1[4 * j], v.x, a0[r]);
+                a1[r] = fmaf(w1[4 * j + 1], v.y, a1[r]);
+                a0[r] = fmaf(w1[4 * j + 2], v.z, a0[r]);
+                a1[r] = fmaf(w1[4 * j + 3], v.w, a1[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < GR; ++r) {
+            float acc = a0[r] + a1[r];
+#pragma unroll
+            for (int o = S::S1 / 2; o > 0; o >>= 1)
+                acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (s1 == 0)
+                h1[(g * GR + r) * H1 + r1] = relu_or(acc + b1[r1], act);
+        }
+    }
+}
+
+// Layer 2, rows split over the cluster: h2[row][r2] = act(W2[local row r2] . h1[row] + b2[r2]).
+template <class S, int GR, int H1>
+__device__ __forceinline__ void f3_layer2(const float (&w2)[S::K2], const float *h1, float *h2, const float *b2,
+                                          int ng, int r2, int s2, int act)
+{
+    for (int g = 0; g < ng; ++g) {
+        const float4 *v4 = reinterpret_cast<const float4 *>(h1 + g * GR * H1) + s2;
+        float a0[GR], a1[GR];
+#pragma unroll
+        for (int r = 0; r < GR; ++r)
+            a0[r] = a1[r] = 0.f;
+#pragma unroll
+        for (int j = 0; j < S::K2 / 4; ++j) {
+#pragma unroll
+            for (int r = 0; r < GR; ++r) {
+                const float4 v = v4[r * (H1 / 4) + j * S::S2];
+                a0[r] = fmaf(w2[4 * j], v.x, a0[r]);
+                a1[r] = fmaf(w2[4 * j + 1], v.y, a1[r]);
+                a0[r] = fmaf(w2[4 * j + 2], v.z, a0[r]);
+                a1[r] = fmaf(w2[4 * j + 3], v.w, a1[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < GR; ++r) {
+            float acc = a0[r] + a1[r];
+#pragma unroll
+            for (int o = S::S2 / 2; o > 0; o >>= 1)
+                acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (s2 == 0)
+                h2[(g * GR + r) * S::R2 + r2] = relu_or(acc + b2[r2], act);
+        }
+    }
+}
+
+// Layer 3, K-split over the CTA's R2 rows of h2: the warp that owns an output returns, in lane
+// r < rows, row r's partial sum over this CTA's slice (lane l takes local rows l, l + 32, ...).
+template <class S, int GR>
+__device__ __forceinline__ float f3_layer3(const float (&w3)[S::K3], const float *h2, int rows, int lane)
+{
+    float mine = 0.f;
+    for (int r = 0; r < (GR == 1 ? 1 : rows); ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < S::K3; ++j)
+            acc = fmaf(w3[j], h2[r * S::R2 + lane + 32 * j], acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+            acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == r)
+            mine = acc;
+    }
+    return mine;
+}
+
 template <int IN, int H1, int H2, int OUT, int C>
 __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_constant__ Params pg)
 {
@@ -200,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     // The polling lanes forward the raw chunks to the peers from registers as
                     // soon as the tags match (header {seq, rows} + row 0 on the peers' request
                     // barrier, rows 1.. on their x barrier).
-                    const ChunkFwd fwd{smem_u32(xch), h_addr, bar_req, bar_x, C - 1};
+                    const ChunkFwd fwd{smem_u32(xch), h_addr, bar_req, bar_x, 1, C - 1};
                     uint32_t c = 0, posted = 0;
                     int got = 0;
                     if constexpr (MB > 1) {
@@ -312,65 +407,12 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
         auto pass = [&](auto group_rows) -> bool {
             constexpr int GR = decltype(group_rows)::value;
             const int ng = GR == 1 ? 1 : ((int)nb + GR - 1) / GR;
-            // ---------------- layer 1 (replicated) ----------------
-            for (int g = 0; g < ng; ++g) {
-                const float4 *x4 = reinterpret_cast<const float4 *>(xs + g * GR * IN) + s1;
-                float a0[GR], a1[GR];
-#pragma unroll
-                for (int r = 0; r < GR; ++r)
-                    a0[r] = a1[r] = 0.f;
-#pragma unroll
-                for (int j = 0; j < S::K1 / 4; ++j) {
-#pragma unroll
-                    for (int r = 0; r < GR; ++r) {
-                        const float4 v = x4[r * (IN / 4) + j * S::S1];
-                        a0[r] = fmaf(w1[4 * j], v.x, a0[r]);
-                        a1[r] = fmaf(w1[4 * j + 1], v.y, a1[r]);
-                        a0[r] = fmaf(w1[4 * j + 2], v.z, a0[r]);
-                        a1[r] = fmaf(w1[4 * j + 3], v.w, a1[r]);
-                    }
-                }
-#pragma unroll
-                for (int r = 0; r < GR; ++r) {
-                    float acc = a0[r] + a1[r];
-#pragma unroll
-                    for (int o = S::S1 / 2; o > 0; o >>= 1)
-                        acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                    if (s1 == 0)
-                        h1[(g * GR + r) * H1 + r1] = relu_or(acc + bias[r1], act1);
-                }
-            }
+            // ---------------- layer 1 (replicated), layer 2 (rows split over the cluster) ----------------
+            f3_layer1<S, GR, IN, H1>(w1, xs, h1, bias, ng, r1, s1, act1);
             __syncthreads();
             if (leader && tid == 0)
                 trace(k, n_done, 3);
-            // ---------------- layer 2 (rows split over the cluster) ----------------
-            for (int g = 0; g < ng; ++g) {
-                const float4 *v4 = reinterpret_cast<const float4 *>(h1 + g * GR * H1) + s2;
-                float a0[GR], a1[GR];
-#pragma unroll
-                for (int r = 0; r < GR; ++r)
-                    a0[r] = a1[r] = 0.f;
-#pragma unroll
-                for (int j = 0; j < S::K2 / 4; ++j) {
-#pragma unroll
-                    for (int r = 0; r < GR; ++r) {
-                        const float4 v = v4[r * (H1 / 4) + j * S::S2];
-                        a0[r] = fmaf(w2[4 * j], v.x, a0[r]);
-                        a1[r] = fmaf(w2[4 * j + 1], v.y, a1[r]);
-                        a0[r] = fmaf(w2[4 * j + 2], v.z, a0[r]);
-                        a1[r] = fmaf(w2[4 * j + 3], v.w, a1[r]);
-                    }
-                }
-#pragma unroll
-                for (int r = 0; r < GR; ++r) {
-                    float acc = a0[r] + a1[r];
-#pragma unroll
-                    for (int o = S::S2 / 2; o > 0; o >>= 1)
-                        acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                    if (s2 == 0)
-                        h2[(g * GR + r) * S::R2 + r2] = relu_or(acc + bias[H1 + r2], act2);
-                }
-            }
+            f3_layer2<S, GR, H1>(w2, h1, h2, bias + H1, ng, r2, s2, act2);
             if (own_x && !leader) {
                 // rank 0's go for this request (sent while layers 1-2 ran); ends on its abort
                 if (!cta_wait_bar(k, bar_req, ph_req & 1u, EW_PEER_POLL, p.step_ns))
@@ -383,18 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                 trace(k, n_done, 4);
             // ---------------- layer 3 (K-split partials -> rank 0) ----------------
             if (warp < OUT) {
-                float mine = 0.f;  // lane r sends row r's partial
-                for (int r = 0; r < (GR == 1 ? 1 : (int)nb); ++r) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int j = 0; j < S::K3; ++j)
-                        acc = fmaf(w3[j], h2[r * S::R2 + lane + 32 * j], acc);
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1)
-                        acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                    if (lane == r)
-                        mine = acc;
-                }
+                const float mine = f3_layer3<S, GR>(w3, h2, (int)nb, lane);  // lane r sends row r's partial
                 if (lane < (int)nb)
                     st_async_u32(mapa(g_addr + (uint32_t)((lane * C + k.rank) * OUT + warp) * 4u, 0u),
                                  __float_as_uint(mine), mapa(bar_g, 0u));

@@ -287,15 +287,16 @@ __device__ __forceinline__ uint32_t ring_slot(const Params &p, uint32_t n)
     return p.ring_slots > 1 ? (p.ring_base + n) % (uint32_t)p.ring_slots : 0u;
 }
 
-// Forwarding of the raw tagged chunks to the other CTAs of a cluster (register-resident
-// kernel): the polling lanes push the chunks they hold straight from registers, so the
-// peers' copy of x leaves the moment the tags match.  Chunk ch of row r goes to the shared
-// address chunks + 16 * (r * nxc + ch) of ranks 1..peers and completes their barrier
-// bar_first (row 0) or bar_rest (rows 1..); lane 0 adds a 16-byte header {seq, rows} at hdr
-// (on bar_first).  Every address is the same offset in each CTA (mapa).
+// Forwarding of the raw tagged chunks to other CTAs of a cluster (register-resident and
+// pipelined ring kernels): the polling lanes push the chunks they hold straight from
+// registers, so the receivers' copy of x leaves the moment the tags match.  Chunk ch of row r
+// goes to the shared address chunks + 16 * (r * nxc + ch) of ranks first .. first+peers-1 and
+// completes their barrier bar_first (row 0) or bar_rest (rows 1..); lane 0 adds a 16-byte
+// header {seq, rows} at hdr (on bar_first).  Every address is the same offset in each CTA
+// (mapa).
 struct ChunkFwd {
     uint32_t chunks, hdr, bar_first, bar_rest;
-    int peers;
+    int first, peers;
 };
 
 __device__ __forceinline__ void fwd_chunk(const ChunkFwd &f, int row, int ch, int nxc, uint4 c)
@@ -303,19 +304,19 @@ __device__ __forceinline__ void fwd_chunk(const ChunkFwd &f, int row, int ch, in
     const float4 v = make_float4(__uint_as_float(c.x), __uint_as_float(c.y), __uint_as_float(c.z), __uint_as_float(c.w));
     const uint32_t a = f.chunks + 16u * (uint32_t)(row * nxc + ch);
     const uint32_t b = row == 0 ? f.bar_first : f.bar_rest;
-    for (int d = 1; d <= f.peers; ++d)
+    for (int d = f.first; d < f.first + f.peers; ++d)
         st_async_v4(mapa(a, (uint32_t)d), v, mapa(b, (uint32_t)d));
 }
 
 __device__ __forceinline__ void fwd_header(const ChunkFwd &f, uint32_t seq, uint32_t rows)
 {
-    for (int d = 1; d <= f.peers; ++d)
+    for (int d = f.first; d < f.first + f.peers; ++d)
         st_async_v4(mapa(f.hdr, (uint32_t)d), make_float4(__uint_as_float(seq), __uint_as_float(rows), 0.f, 0.f),
                     mapa(f.bar_first, (uint32_t)d));
 }
 
 // Warp 0 waits for the next request in a tagged ring slot (the single-slot poll) and
-// unpacks x into X.
+// unpacks x into X (unless X is null).
 // `posted` (optional, micro-batched rings): lane 31 also reads the host's seq_in word (the
 // last sequence number it posted; bookkeeping in the tagged format) in the same round trip,
 // and *posted gets the value seen with the request, so the caller knows whether more
@@ -357,7 +358,7 @@ __device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uin
 #pragma unroll
             for (int j = 0; j < kTagChunksPerLane; ++j) {
                 const int ch = lane + 32 * j;
-                if (ch < nxc) {
+                if (X && ch < nxc) {
                     const float v[3] = {__uint_as_float(c[j].x), __uint_as_float(c[j].y), __uint_as_float(c[j].z)};
 #pragma unroll
                     for (int e = 0; e < 3; ++e)
@@ -414,8 +415,8 @@ constexpr int kTagReadWarpsMax = 16;
 // all maxb slots (maxb <= nw * rpw <= kTagReadWarpsMax * rpw and maxb <= 32, checked on
 // the host).  Each warp's mask of incomplete rows goes through bad_words[w] (shared
 // memory) and a named barrier (id 2, nw warps), so every warp sees the same first gap.
-// Row i of x goes to X + i * in_dim and its sequence number to seqs[i] (warp 0 writes
-// them); in warp 0, *posted = the host's seq_in word (the last sequence number it
+// Row i of x goes to X + i * in_dim (unless X is null) and its sequence number to seqs[i]
+// (warp 0 writes them); in warp 0, *posted = the host's seq_in word (the last sequence number it
 // posted), read by lane 31 in the same round trip.
 // Returns the rows taken, the same in every reading warp (0 when request n is not
 // complete yet; then the caller waits on its slot alone with poll_tagged, whose
@@ -472,7 +473,7 @@ __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uin
     }
 #pragma unroll
     for (int j = 0; j < kTagChunksPerLane; ++j) {
-        if (lane + 32 * j < total && row[j] < nb) {
+        if (X && lane + 32 * j < total && row[j] < nb) {
             const float v[3] = {__uint_as_float(c[j].x), __uint_as_float(c[j].y), __uint_as_float(c[j].z)};
 #pragma unroll
             for (int e = 0; e < 3; ++e)

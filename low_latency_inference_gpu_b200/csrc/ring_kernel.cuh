@@ -1,0 +1,399 @@
+// Pipelined ring kernel (engine kernel variant 4) for the 3-layer fp32 nets of the
+// register-resident kernel, serving the tagged request ring at high request rates.
+//
+// The register-resident kernel (fast3_kernel.cuh) runs a pass strictly in sequence on rank 0:
+// read the waiting ring slots over PCIe, forward x to the peers, compute, gather, reply,
+// and only then read the next slots.  At 16 requests per pass that is ~6 us of reading and
+// forwarding plus ~8 us of layers.  Here a cluster of C + 1 CTAs splits the roles, so the
+// I/O of one pass overlaps the layers of the previous one:
+//   ranks 0..C-1  compute CTAs: the same register-held weight slices, layer code and FMA
+//                 order as the register-resident kernel (every reply bit-identical to it);
+//                 x arrives in one of two chunk buffers (by pass parity), the CTA unpacks it,
+//                 tells the I/O CTA the buffer is free, runs the layers and sends its
+//                 layer-3 partials into the I/O CTA's gather buffer of that parity;
+//   rank C        the I/O CTA, no weights:
+//                 warps 0..3   reader: poll the next ring slot, or read up to micro_batch
+//                              waiting slots at once, and forward their chunks to the C
+//                              compute CTAs straight from registers (the same protocol as
+//                              the register-resident kernel);
+//                 warps 4..15  gatherer: add the C partials per output in rank order, apply
+//                              bias and activation, write each reply into its slot.
+// Pass p uses buffer b = p & 1 on both sides.  Before forwarding pass p the reader waits
+// until every compute CTA has unpacked pass p-2 (mbarrier `xfree[b]`, C remote arrivals)
+// and until the gatherer has finished pass p-2 (`gfree[b]`), so no buffer is overwritten
+// while it is still read; the reader hands each pass's row count, first request index and
+// sequence numbers to the gatherer through `posted[b]`.  Requests are taken and replies
+// written in ring order, so the host-side protocol is the register-resident kernel's.
+// Every wait is bounded (step_timeout_ns inside a pass, idle_timeout_ns + a margin between
+// passes); an exit (stop, idle bound, abort) is broadcast to the cluster, and the gatherer
+// finishes the pass whose partials it is waiting for.  Mailbox only (tagged format); no
+// device queue.
+//
+// No counterpart in the reference, whose persistent kernels serve one request at a time
+// (src/bench_persistent_mbyv_mlp.cu:229-381).
+#pragma once
+#include "fast3_kernel.cuh"
+
+namespace llk {
+
+constexpr int kRingReadWarps = 4;    // I/O CTA warps 0..3
+constexpr int kRingGatherWarp0 = 4;  // I/O CTA warps 4..15
+constexpr int kRingGatherThreads = kThreads - 32 * kRingGatherWarp0;
+
+// A warp waits for an mbarrier phase.  Lane 0 watches the clock and, when `abortable`, the
+// abort flags.  Returns 1 when the phase completed, 0 on abort, -1 when the bound ran out;
+// the verdict is the same in every lane.
+__device__ __forceinline__ int warp_wait_bar(const KernelCtx &k, uint32_t bar, uint32_t parity, uint64_t bound_ns,
+                                             bool abortable)
+{
+    const int lane = threadIdx.x & 31;
+    const uint64_t t0 = lane == 0 ? globaltimer() : 0;
+    for (uint32_t it = 0;; ++it) {
+        const bool done = mbar_try_wait(bar, parity);
+        if (__all_sync(0xffffffffu, done))
+            return 1;
+        if ((it & 15u) == 15u) {
+            int verdict = 1;
+            if (lane == 0) {
+                if (abortable && (*reinterpret_cast<volatile uint32_t *>(&k.sh->abort) || global_abort(k)))
+                    verdict = 0;
+                else if (globaltimer() - t0 > bound_ns)
+                    verdict = -1;
+            }
+            verdict = __shfl_sync(0xffffffffu, verdict, 0);
+            if (verdict != 1)
+                return verdict;
+        }
+    }
+}
+
+template <int IN, int H1, int H2, int OUT, int C>
+__global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_constant__ Params pg)
+{
+    using S = Fast3Shape<IN, H1, H2, OUT, C>;
+    constexpr int MB = kFast3Rows;
+    static_assert(S::MaxRows == kFast3Rows, "the shape leaves no room for multi-row passes");
+    constexpr int NXC = (IN + 2) / 3;          // tagged chunks per row
+    constexpr int YO = 3 * ((OUT + 2) / 3) + 4;  // one output row, zero-padded
+    constexpr int IO = C;                      // rank of the I/O CTA
+    // One pool: compute CTAs use [xs | h1 | h2 | xch[2]], the I/O CTA [gath[2] | yo].  Remote
+    // writes go to the other role's region at the same offset in the receiving CTA.
+    constexpr int OFF_XS = 0;
+    constexpr int OFF_H1 = OFF_XS + 4 * MB * IN;
+    constexpr int OFF_H2 = OFF_H1 + 4 * MB * H1;
+    constexpr int OFF_XCH = (OFF_H2 + 4 * MB * S::R2 + 15) / 16 * 16;
+    constexpr int XCH_B = 16 * MB * NXC;
+    constexpr int COMPUTE_END = OFF_XCH + 2 * XCH_B;
+    constexpr int GATH_F = MB * C * OUT;  // [row][rank][output]
+    constexpr int OFF_G = 0;
+    constexpr int OFF_YO = OFF_G + 2 * 4 * GATH_F;
+    constexpr int IO_END = OFF_YO + 4 * MB * YO;
+    constexpr int POOL = COMPUTE_END > IO_END ? COMPUTE_END : IO_END;
+    __shared__ __align__(16) uint8_t pool[POOL];
+    __shared__ __align__(16) uint32_t hdr2[2][4];  // compute CTAs: {seq, rows} of the pass in buffer b
+    __shared__ __align__(8) uint64_t rb[12];       // see the barrier indices below
+    __shared__ __align__(16) float bias[S::NB];
+    __shared__ uint32_t mseq[2][MB];               // I/O: sequence number of each row of the pass in buffer b
+    __shared__ uint32_t mrows[2], mbase[2];        // I/O: rows (0 = exit) and first request index
+    __shared__ uint32_t bad_words[kTagReadWarpsMax];
+    __shared__ uint32_t s_backlog[2];
+    __shared__ __align__(16) Shared sh;
+    __shared__ __align__(16) Params sp;
+    {
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(&pg);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(&sp);
+        for (int i = threadIdx.x; i < (int)(sizeof(Params) / 4); i += kThreads)
+            dst[i] = src[i];
+    }
+    __syncthreads();
+    const Params &p = sp;
+    KernelCtx k;
+    k.p = &p;
+    k.sh = &sh;
+    k.smem = nullptr;
+    k.rank = cluster_ctarank();
+    k.stage = 0;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool io = k.rank == (uint32_t)IO;
+    // barriers: compute CTAs 0,1 bar_req[b] (header + row 0), 2,3 bar_x[b] (rows 1..);
+    // I/O CTA 4,5 bar_g[b] (partials), 6,7 xfree[b], 8,9 gfree[b], 10,11 posted[b]
+    auto bar = [&](int i) { return smem_u32(&rb[i]); };
+    const uint32_t pool_a = smem_u32(pool);
+
+    if (tid == 0) {
+        for (int i = 0; i < 4; ++i)
+            mbar_init(bar(i), 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar(4 + i), 1);
+            mbar_init(bar(6 + i), C);
+            mbar_init(bar(8 + i), 1);
+            mbar_init(bar(10 + i), 1);
+        }
+        sh.cmd = 0;
+        sh.fail = 0;
+        sh.abort = 0;
+        sh.hstop = 0;
+        s_backlog[0] = s_backlog[1] = 0;
+        fence_mbar_init_cluster();
+        if (io)
+            st_relaxed_sys_u32(&p.ctrl->state, ST_LOADING);
+    }
+    // weights into registers (compute CTAs; the I/O CTA holds none), biases into shared memory
+    // (the I/O CTA takes CTA 0's copy: it needs the layer-3 biases)
+    const float *img = reinterpret_cast<const float *>(p.image + (size_t)(io ? 0u : k.rank) * p.image_stride);
+    float w1[S::K1], w2[S::K2], w3[S::K3];
+    if (!io) {
+#pragma unroll
+        for (int j = 0; j < S::K1; ++j)
+            w1[j] = ld_once_f32(img + (size_t)j * kThreads + tid);
+#pragma unroll
+        for (int j = 0; j < S::K2; ++j)
+            w2[j] = ld_once_f32(img + (size_t)(S::K1 + j) * kThreads + tid);
+#pragma unroll
+        for (int j = 0; j < S::K3; ++j)
+            w3[j] = ld_once_f32(img + (size_t)(S::K1 + S::K2 + j) * kThreads + tid);
+    }
+    for (int i = tid; i < S::NB; i += kThreads)
+        bias[i] = __ldg(img + (size_t)S::NW * kThreads + i);
+    if (io) {
+        float *gz = reinterpret_cast<float *>(pool + OFF_G);
+        for (int i = tid; i < 2 * GATH_F + MB * YO; i += kThreads)
+            gz[i] = 0.0f;  // gath[2] and yo are contiguous
+    }
+    __syncthreads();
+    cluster_sync();  // every barrier of the cluster is initialised before any remote operation
+    if (io && tid == 0)
+        st_relaxed_sys_u32(&p.ctrl->state, ST_RUNNING);
+
+    uint32_t passes_done = 0, rows_done = 0;
+    if (!io) {
+        // ======================= compute CTA =======================
+        const int r1 = tid / S::S1, s1 = tid % S::S1;
+        const int r2 = tid / S::S2, s2 = tid % S::S2;
+        float *xs = reinterpret_cast<float *>(pool + OFF_XS);
+        float *h1 = reinterpret_cast<float *>(pool + OFF_H1);
+        float *h2 = reinterpret_cast<float *>(pool + OFF_H2);
+        const int act1 = p.L[0].act, act2 = p.L[1].act;
+        uint32_t ph_x[2] = {0u, 0u};
+        uint32_t n_req = 0;  // request index of the pass's first row (as counted by the reader)
+        for (uint32_t pass = 0;; ++pass) {
+            const int b = (int)(pass & 1u);
+            const uint32_t par = (pass >> 1) & 1u;
+            if (tid == 0)
+                mbar_arrive_expect_tx(bar(b), 16u + 16u * NXC);
+            if (!cta_wait_bar(k, bar(b), par, EW_PEER_POLL, p.idle_ns + p.peer_margin_ns))
+                break;
+            const uint32_t seq = *reinterpret_cast<volatile uint32_t *>(&hdr2[b][0]);
+            uint32_t nb = *reinterpret_cast<volatile uint32_t *>(&hdr2[b][1]);
+            nb = nb < 1u ? 1u : (nb > (uint32_t)MB ? (uint32_t)MB : nb);
+            (void)seq;
+            if (nb > 1) {
+                if (tid == 0)
+                    mbar_arrive_expect_tx(bar(2 + b), 16u * NXC * (nb - 1));
+                const uint32_t px = b ? ph_x[1] : ph_x[0];
+                if (!cta_wait_bar(k, bar(2 + b), px & 1u, EW_PEER_POLL, p.step_ns))
+                    break;
+                if (b)
+                    ++ph_x[1];
+                else
+                    ++ph_x[0];
+            }
+            // unpack {v0, v1, v2, tag} chunks into the x rows, then release the chunk buffer
+            const uint4 *xch = reinterpret_cast<const uint4 *>(pool + OFF_XCH + b * XCH_B);
+            for (int t = tid; t < (int)nb * NXC; t += kThreads) {
+                const int r = t / NXC, ch = t - r * NXC;
+                const uint4 v = xch[t];
+                float *dst = xs + r * IN + 3 * ch;
+                dst[0] = __uint_as_float(v.x);
+                if (3 * ch + 1 < IN)
+                    dst[1] = __uint_as_float(v.y);
+                if (3 * ch + 2 < IN)
+                    dst[2] = __uint_as_float(v.z);
+            }
+            __syncthreads();
+            if (tid == 0)
+                mbar_arrive_remote(mapa(bar(6 + b), (uint32_t)IO));
+            const int gr = nb == 1 ? 1 : kFast3Group;
+            const int ng = (int)(nb + (uint32_t)gr - 1) / gr;
+            if (nb == 1)
+                f3_layer1<S, 1, IN, H1>(w1, xs, h1, bias, 1, r1, s1, act1);
+            else
+                f3_layer1<S, kFast3Group, IN, H1>(w1, xs, h1, bias, ng, r1, s1, act1);
+            __syncthreads();
+            if (k.rank == 0 && tid == 0)
+                trace(k, n_req, 3);
+            if (nb == 1)
+                f3_layer2<S, 1, H1>(w2, h1, h2, bias + H1, 1, r2, s2, act2);
+            else
+                f3_layer2<S, kFast3Group, H1>(w2, h1, h2, bias + H1, ng, r2, s2, act2);
+            __syncthreads();
+            if (k.rank == 0 && tid == 0)
+                trace(k, n_req, 4);
+            // layer 3: K-split partials into the I/O CTA's gather buffer of this parity
+            if (warp < OUT) {
+                const float mine = nb == 1 ? f3_layer3<S, 1>(w3, h2, 1, lane)
+                                           : f3_layer3<S, kFast3Group>(w3, h2, (int)nb, lane);
+                const uint32_t g_addr = pool_a + OFF_G + (uint32_t)b * 4u * GATH_F;
+                if (lane < (int)nb)
+                    st_async_u32(mapa(g_addr + (uint32_t)((lane * C + (int)k.rank) * OUT + warp) * 4u, (uint32_t)IO),
+                                 __float_as_uint(mine), mapa(bar(4 + b), (uint32_t)IO));
+            }
+            if (k.rank == 0 && tid == 0)
+                trace(k, n_req, 5);
+            n_req += nb;
+        }
+    } else if (warp < kRingReadWarps) {
+        // ======================= I/O CTA: reader =======================
+        // Warp 0 makes every decision and publishes it in shared memory; the other reading
+        // warps (a multi-slot read of more than 5 slots) follow through named barrier 2, so
+        // they never part ways at a barrier.
+        constexpr int RPW = tag_rows_per_warp(NXC);
+        static_assert(RPW >= 1, "a reading warp holds at least one slot");
+        const int read_warps = p.micro_batch > 1 ? (p.micro_batch + RPW - 1) / RPW : 1;
+        if (warp < read_warps) {
+            uint32_t last = p.last_seq, n_done = 0;
+            for (uint32_t pass = 0;; ++pass) {
+                const int b = (int)(pass & 1u);
+                if (warp == 0) {
+                    int w = 1;
+                    if (pass >= 2) {
+                        // the compute CTAs have unpacked, and the gatherer has finished, pass - 2
+                        const uint32_t par = ((pass - 2u) >> 1) & 1u;
+                        w = warp_wait_bar(k, bar(6 + b), par, p.step_ns, true);
+                        if (w == 1)
+                            w = warp_wait_bar(k, bar(8 + b), par, p.step_ns, true);
+                    }
+                    if (lane == 0) {
+                        if (w < 0) {
+                            report_error(k, LL_ERR_DEVICE_FAULT, EW_GATHER);
+                            broadcast_abort(k);
+                        }
+                        // on a failed wait the abort flag is (or gets) set: the gatherer leaves on it
+                        // (no phase is posted here: pass p - 2 may still be unfinished, and a second
+                        // phase of posted[b] would look like none to the gatherer)
+                        sh.cmd = w == 1 ? 1u : 0u;
+                    }
+                }
+                if (read_warps > 1)
+                    asm volatile("bar.sync 2, %0;" ::"r"(32 * read_warps) : "memory");
+                if (*reinterpret_cast<volatile uint32_t *>(&sh.cmd) == 0u)
+                    break;
+                const ChunkFwd fwd{pool_a + OFF_XCH + (uint32_t)b * XCH_B, smem_u32(&hdr2[b][0]), bar(b), bar(2 + b), 0,
+                                   C};
+                uint32_t posted = 0;
+                int got = 0;
+                if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[pass & 1u]))
+                    got = take_tagged_rows(k, last, nullptr, n_done, p.micro_batch, mseq[b], &posted, bad_words,
+                                           read_warps, &fwd);
+                if (warp == 0) {
+                    uint32_t c;
+                    if (got > 0) {
+                        c = seq_after(last, got);
+                    } else {
+                        c = poll_tagged(k, last, nullptr, ring_slot(p, n_done), p.micro_batch > 1 ? &posted : nullptr,
+                                        &fwd);
+                        got = 1;
+                    }
+                    __syncwarp();  // the lanes' mseq writes come before lane 0's release below
+                    if (lane == 0) {
+                        if (got == 1)
+                            mseq[b][0] = c;
+                        s_backlog[(pass + 1u) & 1u] =
+                            (p.micro_batch > 1 && c != kCmdExit && (int32_t)(posted - c) > 0) ? 1u : 0u;
+                        if (c == kCmdExit)
+                            broadcast_abort(k);
+                        mrows[b] = c == kCmdExit ? 0u : (uint32_t)got;
+                        mbase[b] = n_done;
+                        trace(k, n_done, 0);
+                        mbar_arrive_remote(mapa(bar(10 + b), (uint32_t)IO));  // posted[b] (release, cluster scope)
+                    }
+                }
+                if (read_warps > 1)
+                    asm volatile("bar.sync 2, %0;" ::"r"(32 * read_warps) : "memory");
+                const uint32_t rows = *reinterpret_cast<volatile uint32_t *>(&mrows[b]);
+                if (rows == 0u)
+                    break;
+                last = seq_after(last, (int)rows);
+                n_done += rows;
+            }
+        }
+    } else {
+        // ======================= I/O CTA: gatherer =======================
+        // Gatherer warp 0 waits for the pass and its partials and publishes the row count
+        // (0 = leave); all gatherer warps then finish rows gw, gw + 12, ... of the pass.
+        const int gt = tid - 32 * kRingGatherWarp0, gw = warp - kRingGatherWarp0;
+        constexpr int NGW = kRingGatherThreads / 32;
+        for (uint32_t pass = 0;; ++pass) {
+            const int b = (int)(pass & 1u);
+            const uint32_t par = (pass >> 1) & 1u;
+            if (gw == 0) {
+                // the next pass (abortable: an exit is broadcast; every pass posted before it has
+                // already been waited for in order), then its partials (not abortable: a pass that
+                // was forwarded is finished, within the step bound)
+                uint32_t nb = 0;
+                int w = warp_wait_bar(k, bar(10 + b), par, p.idle_ns + 2 * p.peer_margin_ns, true);
+                if (w == 1) {
+                    nb = *reinterpret_cast<volatile uint32_t *>(&mrows[b]);
+                    if (nb > 0u) {
+                        if (lane == 0)
+                            mbar_arrive_expect_tx(bar(4 + b), (uint32_t)(C * OUT * 4) * nb);
+                        w = warp_wait_bar(k, bar(4 + b), par, p.step_ns, false);
+                        if (w != 1)
+                            nb = 0;
+                    }
+                }
+                if (lane == 0) {
+                    if (w < 0) {
+                        report_error(k, LL_ERR_DEVICE_FAULT, nb == 0u && mrows[b] == 0u ? EW_PEER_POLL : EW_GATHER);
+                        broadcast_abort(k);
+                    }
+                    sh.nrows = nb;
+                    if (nb > 0u)
+                        trace(k, mbase[b], 12);
+                }
+            }
+            asm volatile("bar.sync 3, %0;" ::"r"(kRingGatherThreads) : "memory");
+            const uint32_t nb = *reinterpret_cast<volatile uint32_t *>(&sh.nrows);
+            if (nb == 0u)
+                break;
+            const uint32_t base = *reinterpret_cast<volatile uint32_t *>(&mbase[b]);
+            const float *gath = reinterpret_cast<const float *>(pool + OFF_G) + (size_t)b * GATH_F;
+            for (int r = gw; r < (int)nb; r += NGW) {
+                float *yr = reinterpret_cast<float *>(pool + OFF_YO) + r * YO;
+                if (lane < OUT) {
+                    float v = 0.f;
+#pragma unroll
+                    for (int c = 0; c < C; ++c)
+                        v += gath[(r * C + c) * OUT + lane];
+                    yr[lane] = relu_or(v + bias[H1 + S::R2 + lane], p.L[2].act);
+                }
+                __syncwarp();
+                constexpr int NYC = (OUT + 2) / 3;
+                if (lane < NYC)
+                    st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, base + (uint32_t)r) * p.ring_stride_f + 4 * lane,
+                                      make_float4(yr[3 * lane], yr[3 * lane + 1], yr[3 * lane + 2],
+                                                  __uint_as_float(mseq[b][r])));
+                __syncwarp();
+            }
+            asm volatile("bar.sync 3, %0;" ::"r"(kRingGatherThreads) : "memory");  // every row of the pass written
+            if (gt == 0) {
+                trace(k, base, 13);
+                st_relaxed_sys_u32(&p.mb->seq_out, mseq[b][nb - 1]);  // bookkeeping: the host waits on the tags
+                mbar_arrive_remote(mapa(bar(8 + b), (uint32_t)IO));   // gfree[b]
+            }
+            ++passes_done;
+            rows_done += nb;
+        }
+    }
+    __syncthreads();
+    cluster_sync();
+    if (io && tid == 32 * kRingGatherWarp0) {
+        st_relaxed_sys_u32(&p.ctrl->passes, passes_done);
+        st_relaxed_sys_u32(&p.ctrl->rows, rows_done);
+    }
+    __syncthreads();
+    if (io && tid == 0)
+        st_release_sys_u32(&p.ctrl->state, ST_EXITED);
+}
+
+}  // namespace llk

@@ -1,0 +1,130 @@
+"""Pipelined ring kernel (engine kernel variant 4; needs a B200).
+
+An I/O CTA reads the waiting ring slots and writes the replies while the compute CTAs run
+the layers of the previous pass.  The compute CTAs use the register-resident kernel's
+weight slices and FMA order, so every reply must equal, bit for bit, the register-resident
+kernel's reply to the same request served alone (and be within 1e-5 of the oracle)."""
+import time
+
+import numpy as np
+import pytest
+
+import low_latency_inference_gpu_b200 as ll
+import oracle
+from conftest import rel_err
+
+pytestmark = [pytest.mark.gpu, pytest.mark.timeout(300)]
+
+
+def opts(**kw):
+    o = ll.default_opts()
+    o.mailbox_format = 1
+    o.kernel_variant = ll.VARIANT_PIPELINED_RING
+    for k, v in kw.items():
+        setattr(o, k, v)
+    return o
+
+
+@pytest.fixture(scope="module")
+def cfg0():
+    net, Ws, bs = ll.config_params(0)
+    xs = ll.config_inputs(0, 64)
+    ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
+    o = ll.default_opts()
+    o.mailbox_format = 1
+    with ll.Engine(net, Ws, bs, opts=o) as one:  # register-resident kernel, one request at a time
+        assert one.info().kernel_variant == ll.VARIANT_REGISTER_RESIDENT
+        single = np.stack([one.infer(xs[i])[0] for i in range(xs.shape[0])])
+    return net, Ws, bs, xs, ref, single
+
+
+def test_single_requests_match_the_register_resident_kernel(cfg0):
+    net, Ws, bs, xs, ref, single = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts()) as e:
+        inf = e.info()
+        assert inf.kernel_variant == ll.VARIANT_PIPELINED_RING and inf.cluster_size == 8
+        ys = np.stack([e.infer(xs[i])[0] for i in range(xs.shape[0])])
+        assert e.info().status == ll.LL_OK
+    assert np.array_equal(ys, single)
+    assert rel_err(ys, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("ring,micro", [(16, 4), (64, 16), (32, 16), (8, 1)])
+def test_ring_kept_full(cfg0, ring, micro):
+    net, Ws, bs, xs, ref, single = cfg0
+    n = 5000
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=ring, micro_batch=micro)) as e:
+        lat, el, ys = e.bench_ring(xs, n, ring, keep_outputs=True)
+        e.stop()
+        inf = e.info()
+        assert inf.status == ll.LL_OK
+        assert inf.rows == n
+    rows = np.arange(n) % xs.shape[0]
+    assert np.array_equal(ys, single[rows])
+    assert rel_err(ys, ref[rows]) <= 1e-5
+    assert np.all(np.isfinite(lat)) and el > 0
+    if micro > 1:
+        assert inf.passes < inf.rows
+
+
+def test_bursts_are_taken_several_requests_per_pass(cfg0):
+    net, Ws, bs, xs, ref, single = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=32, micro_batch=16)) as e:
+        n = 0
+        bursts = (16, 1, 7, 16, 3, 12)
+        for burst in bursts:
+            seqs = e.submit_many(xs[n:n + burst])
+            for i in (range(burst) if burst % 2 else reversed(range(burst))):
+                assert np.array_equal(e.poll(seqs[i])[0], single[n + i])
+            n += burst
+        e.stop()
+        inf = e.info()
+        assert inf.status == ll.LL_OK and inf.rows == n
+        assert inf.passes < inf.rows
+
+
+def test_poisson_replies_at_one_million_per_second(cfg0):
+    net, Ws, bs, xs, ref, single = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=64, micro_batch=16)) as e:
+        lat, el, ys, idx = e.serve_poisson(xs, 30000, 1_000_000.0, seed=5, keep_outputs=True)
+        e.stop()
+        assert e.info().status == ll.LL_OK
+    assert np.array_equal(idx, np.arange(30000))
+    assert np.array_equal(ys, single[idx % xs.shape[0]])
+    assert np.all(np.isfinite(lat))
+
+
+def test_idle_relaunch_and_stop(cfg0):
+    net, Ws, bs, xs, ref, single = cfg0
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=16, micro_batch=16, idle_timeout_ns=30_000_000)) as e:
+        n = 0
+        for rnd in range(3):
+            seqs = e.submit_many(xs[n:n + 9])
+            for i, s in enumerate(seqs):
+                assert np.array_equal(e.poll(s)[0], single[n + i])
+            n += 9
+            time.sleep(0.15)  # the kernel leaves after 30 ms idle; the next submit relaunches it
+        assert e.info().launches >= 3
+        for i in range(n, n + 5):
+            assert np.array_equal(e.infer(xs[i])[0], single[i])
+        e.stop()
+        assert e.info().status == ll.LL_OK
+
+
+def test_refused_where_it_cannot_run(cfg0):
+    net, Ws, bs, xs, ref, single = cfg0
+    o = opts()
+    o.mailbox_format = 0  # the TickBuffer
+    with pytest.raises(ll.LLError) as err:
+        ll.Engine(net, Ws, bs, opts=o)
+    assert err.value.code == ll.LL_ERR_UNSUPPORTED
+    with pytest.raises(ll.LLError) as err:  # 4 CTAs per cluster: no room for multi-row passes
+        ll.Engine(net, Ws, bs, opts=opts(cluster_size=4))
+    assert err.value.code == ll.LL_ERR_UNSUPPORTED
+    torch = pytest.importorskip("torch")
+    with ll.Engine(net, Ws, bs, opts=opts()) as e:
+        dx = torch.zeros((4, 64), device="cuda")
+        dy = torch.zeros((4, 16), device="cuda")
+        with pytest.raises(ll.LLError) as err:
+            e.run_queue(dx.data_ptr(), dy.data_ptr(), 4, 1)
+        assert err.value.code == ll.LL_ERR_UNSUPPORTED
