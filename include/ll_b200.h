@@ -115,7 +115,11 @@ typedef struct ll_engine_opts {
                                    forced, else 1. */
     int32_t ring_slots;         /* tagged mailbox only: request slots (1..64; 0 = 1).  Up to ring_slots
                                    requests may be outstanding (ll_submit before the earlier ll_poll);
-                                   the device serves them in order, slot after slot */
+                                   the device serves them in order, slot after slot.  Layout: the
+                                   16-byte header, the x chunks of slots 0..Q-1 back to back, then
+                                   from the next 64-byte boundary the y chunks of each slot, each
+                                   slot's starting on a fresh 64-byte line (one slot is exactly the
+                                   single tagged mailbox) */
     int32_t micro_batch;        /* request ring on the register-resident kernel: the device takes up to
                                    this many waiting requests (consecutive slots, each complete) in one
                                    poll and runs them as one small batch (1..16, at most ring_slots;
@@ -207,7 +211,8 @@ int ll_engine_create_ex(const ll_net_desc *net, const void *const *W, const floa
  */
 int ll_echo_engine_create(int device, int in_dim, int out_dim, const ll_engine_opts *opts, ll_engine **out);
 
-/* Host pointer of the mailbox (layout of ll_tick_header + x + y, see above). */
+/* Host pointer of the mailbox (layout of ll_tick_header + x + y, see above; on a tagged
+ * ring, _x and _y point at slot 0's x and y chunks). */
 void *ll_engine_mailbox(ll_engine *e);
 float *ll_engine_mailbox_x(ll_engine *e);
 float *ll_engine_mailbox_y(ll_engine *e);

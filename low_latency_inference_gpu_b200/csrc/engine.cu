@@ -413,7 +413,9 @@ struct ll_engine {
     // tagged ring holds up to `ring` of them, the TickBuffer one
     std::deque<std::pair<uint32_t, uint64_t>> inflight;
     int ring = 1;           // tagged ring slots
-    size_t ring_stride = 0; // bytes between slots
+    size_t ring_xstride = 0; // bytes between the x chunks of consecutive slots (contiguous)
+    size_t ring_ystride = 0; // bytes between the y chunks of consecutive slots (64-byte aligned)
+    size_t ring_ybase = 0;   // byte offset of slot 0's y chunks
     uint64_t ring_next = 0; // ring index of the next request to post
     uint32_t last_served = 0;
     bool running = false;
@@ -526,8 +528,14 @@ int alloc_mailbox(ll_engine *e)
         }
     }
     if (e->opts.mailbox_format == 1) {
-        e->ring_stride = llh::round_up(ll_tagged_y_offset(e->in_dim) + 16 * (size_t)((e->out_dim + 2) / 3), 64);
-        e->mb_bytes = e->ring_stride * (size_t)e->ring;  // one slot: exactly ll_tagged_mailbox_bytes
+        // header, the x chunks of every slot back to back (a pass that takes several waiting
+        // requests reads one contiguous run: measured ~2x faster over PCIe than slots 512 bytes
+        // apart), then from a 64-byte boundary the y chunks, each slot's on its own lines.
+        // One slot is exactly the single tagged mailbox (ll_tagged_mailbox_bytes).
+        e->ring_xstride = 16 * (size_t)((e->in_dim + 2) / 3);
+        e->ring_ystride = llh::round_up(16 * (size_t)((e->out_dim + 2) / 3), 64);
+        e->ring_ybase = llh::round_up(sizeof(ll_tick_header) + e->ring_xstride * (size_t)e->ring, 64);
+        e->mb_bytes = llh::round_up(e->ring_ybase + e->ring_ystride * (size_t)e->ring, 64);
     } else {
         e->mb_bytes = ll_mailbox_bytes(e->in_dim, e->out_dim, e->max_batch);
     }
@@ -578,14 +586,15 @@ int finish_setup(ll_engine *e)
     p.mb = e->mb_dev;
     p.mb_x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(e->mb_dev) + sizeof(ll_tick_header));
     if (e->opts.mailbox_format == 1)
-        p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + ll_tagged_y_offset(e->in_dim));
+        p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + e->ring_ybase);
     else
         p.mb_y = reinterpret_cast<float *>(reinterpret_cast<char *>(e->mb_dev) + sizeof(ll_tick_header) +
                                        sizeof(float) * (size_t)e->in_dim * e->max_batch);
     p.ctrl = e->ctrl_dev;
     p.mailbox_format = e->opts.mailbox_format;
     p.ring_slots = e->ring;
-    p.ring_stride_f = (uint32_t)(e->ring_stride / 4);
+    p.ring_xstride_f = (uint32_t)(e->ring_xstride / 4);
+    p.ring_ystride_f = (uint32_t)(e->ring_ystride / 4);
     p.ring_base = 0;
     p.micro_batch = e->micro;
     p.idle_ns = e->opts.idle_timeout_ns;
@@ -818,8 +827,7 @@ size_t ring_slot_of(const ll_engine *e, uint32_t seq)
 bool tagged_done(ll_engine *e, uint32_t seq, float *y)
 {
     const int yc = (e->out_dim + 2) / 3;
-    const char *base = static_cast<const char *>(e->mb_host) + ring_slot_of(e, seq) * e->ring_stride +
-                       ll_tagged_y_offset(e->in_dim);
+    const char *base = static_cast<const char *>(e->mb_host) + e->ring_ybase + ring_slot_of(e, seq) * e->ring_ystride;
     uint32_t w[4];
     for (int c = 0; c < yc; ++c) {
         llh::load16(base + 16 * c, w);  // the whole chunk in one load: tag and values together
@@ -883,7 +891,7 @@ int engine_wait(ll_engine *e, uint32_t seq, float *y, int n_rows, uint64_t timeo
 // Write x into one slot of the tagged ring as chunks stamped with seq (no doorbell).
 void write_tagged_slot(ll_engine *e, size_t slot, const float *x, uint32_t seq)
 {
-    char *base = static_cast<char *>(e->mb_host) + slot * e->ring_stride + sizeof(ll_tick_header);
+    char *base = static_cast<char *>(e->mb_host) + sizeof(ll_tick_header) + slot * e->ring_xstride;
     const int xc = (e->in_dim + 2) / 3;
     for (int c = 0; c < xc; ++c) {
         uint32_t w[4] = {0u, 0u, 0u, seq};
@@ -1420,8 +1428,8 @@ float *ll_engine_mailbox_y(ll_engine *e)
 {
     if (!e)
         return nullptr;
-    if (e->opts.mailbox_format == 1)  // first y chunk
-        return reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + ll_tagged_y_offset(e->in_dim));
+    if (e->opts.mailbox_format == 1)  // slot 0's first y chunk (ll_tagged_y_offset for one slot)
+        return reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + e->ring_ybase);
     return reinterpret_cast<float *>(static_cast<char *>(e->mb_host) + sizeof(ll_tick_header) +
                                      sizeof(float) * (size_t)e->in_dim * e->max_batch);
 }

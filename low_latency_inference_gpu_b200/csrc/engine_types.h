@@ -100,10 +100,12 @@ struct Params {
     unsigned *q_done;     // queue-mode completion counter (multi-stage)
     uint64_t idle_ns, step_ns, peer_margin_ns;
     uint32_t last_seq;
-    // tagged request ring: request n of this launch uses slot (ring_base + n) % ring_slots,
-    // ring_stride_f floats apart (1 slot = the single tagged mailbox)
+    // tagged request ring: request n of this launch uses slot (ring_base + n) % ring_slots; the
+    // x chunks of consecutive slots are contiguous (ring_xstride_f floats apart, from mb_x), the
+    // y chunks of a slot start ring_ystride_f floats after the previous slot's (from mb_y);
+    // one slot is the single tagged mailbox
     int32_t ring_slots;
-    uint32_t ring_stride_f;
+    uint32_t ring_xstride_f, ring_ystride_f;
     uint32_t ring_base;
     int32_t micro_batch;  // register-resident kernel: ring slots taken together (1 = one request)
     int32_t diag_wait_never;

@@ -73,7 +73,22 @@ __device__ __forceinline__ float relu_or(float v, int act)
 //
 // Layer 1, replicated in every CTA: h1[row][r1] = act(W1[r1] . x[row] + b1[r1]); S1 threads
 // per output row, lane s1 of a row group takes the 16-byte input pieces s1, s1 + S1, ...
-template <class S, int GR, int IN, int H1>
+// (a0, a1) += (w.x * v.x, w.y * v.y): one packed instruction of two independent IEEE fp32 FMAs
+// when PACKED, else two scalar FMAs; each accumulator sees the same rounding either way.
+template <bool PACKED>
+__device__ __forceinline__ void fma_pair(float &a0, float &a1, float w0, float w1, float v0, float v1)
+{
+    if constexpr (PACKED) {
+        const float2 r = __ffma2_rn(make_float2(w0, w1), make_float2(v0, v1), make_float2(a0, a1));
+        a0 = r.x;
+        a1 = r.y;
+    } else {
+        a0 = fmaf(w0, v0, a0);
+        a1 = fmaf(w1, v1, a1);
+    }
+}
+
+template <class S, int GR, int IN, int H1, bool PACKED = false>
 __device__ __forceinline__ void f3_layer1(const float (&w1)[S::K1], const float *xs, float *h1, const float *b1,
                                           int ng, int r1, int s1, int act)
 {
@@ -88,10 +103,15 @@ __device__ __forceinline__ void f3_layer1(const float (&w1)[S::K1], const float 
 #pragma unroll
             for (int r = 0; r < GR; ++r) {
                 const float4 v = x4[r * (IN / 4) + j * S::S1];
-                a0[r] = fmaf(w1[4 * j], v.x, a0[r]);
-                a1[r] = fmaf(w1[4 * j + 1], v.y, a1[r]);
-                a0[r] = fmaf(w1[4 * j + 2], v.z, a0[r]);
-                a1[r] = fmaf(w1[4 * j + 3], v.w, a1[r]);
+                if constexpr (PACKED) {
+                    fma_pair<true>(a0[r], a1[r], w1[4 * j], w1[4 * j + 1], v.x, v.y);
+                    fma_pair<true>(a0[r], a1[r], w1[4 * j + 2], w1[4 * j + 3], v.z, v.w);
+                } else {
+                    a0[r] = fmaf(w1[4 * j], v.x, a0[r]);
+                    a1[r] = fmaf(w1[4 * j + 1], v.y, a1[r]);
+                    a0[r] = fmaf(w1[4 * j + 2], v.z, a0[r]);
+                    a1[r] = fmaf(w1[4 * j + 3], v.w, a1[r]);
+                }
             }
         }
 #pragma unroll
@@ -107,7 +127,7 @@ __device__ __forceinline__ void f3_layer1(const float (&w1)[S::K1], const float 
 }
 
 // Layer 2, rows split over the cluster: h2[row][r2] = act(W2[local row r2] . h1[row] + b2[r2]).
-template <class S, int GR, int H1>
+template <class S, int GR, int H1, bool PACKED = false>
 __device__ __forceinline__ void f3_layer2(const float (&w2)[S::K2], const float *h1, float *h2, const float *b2,
                                           int ng, int r2, int s2, int act)
 {
@@ -122,10 +142,15 @@ __device__ __forceinline__ void f3_layer2(const float (&w2)[S::K2], const float 
 #pragma unroll
             for (int r = 0; r < GR; ++r) {
                 const float4 v = v4[r * (H1 / 4) + j * S::S2];
-                a0[r] = fmaf(w2[4 * j], v.x, a0[r]);
-                a1[r] = fmaf(w2[4 * j + 1], v.y, a1[r]);
-                a0[r] = fmaf(w2[4 * j + 2], v.z, a0[r]);
-                a1[r] = fmaf(w2[4 * j + 3], v.w, a1[r]);
+                if constexpr (PACKED) {
+                    fma_pair<true>(a0[r], a1[r], w2[4 * j], w2[4 * j + 1], v.x, v.y);
+                    fma_pair<true>(a0[r], a1[r], w2[4 * j + 2], w2[4 * j + 3], v.z, v.w);
+                } else {
+                    a0[r] = fmaf(w2[4 * j], v.x, a0[r]);
+                    a1[r] = fmaf(w2[4 * j + 1], v.y, a1[r]);
+                    a0[r] = fmaf(w2[4 * j + 2], v.z, a0[r]);
+                    a1[r] = fmaf(w2[4 * j + 3], v.w, a1[r]);
+                }
             }
         }
 #pragma unroll
@@ -138,6 +163,91 @@ __device__ __forceinline__ void f3_layer2(const float (&w2)[S::K2], const float 
                 h2[(g * GR + r) * S::R2 + r2] = relu_or(acc + b2[r2], act);
         }
     }
+}
+
+// One round of a transpose-reduce: N values per lane become N/2, summed with the lane's
+// partner l ^ M; the lane whose bit M is clear keeps values [0, N/2), the other [N/2, N).
+// Each kept value is own + partner, exactly the pair a butterfly step with mask M adds, so
+// after the rounds of masks S/2, S/4, ..., 1 over N = S values every lane holds the same
+// sum a butterfly would have given for its row: bit-identical, with N - 1 shuffles instead
+// of N log2(S).
+template <int N, int M>
+__device__ __forceinline__ void xreduce_round(float (&t)[16], int lane)
+{
+    const bool upper = (lane & M) != 0;
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) {
+        const float give = upper ? t[i] : t[i + N / 2];
+        const float keep = upper ? t[i + N / 2] : t[i];
+        t[i] = keep + __shfl_xor_sync(0xffffffffu, give, M);
+    }
+}
+
+// Layer 2 over 16 batch rows at once (S2 = 16 lanes per output row): the products as in
+// f3_layer2, then a transpose-reduce over the row's 16 lanes, after which lane s2 holds batch
+// row s2's sum.  Bit-identical to f3_layer2.
+template <class S, int H1, bool PACKED>
+__device__ __forceinline__ void f3_layer2_x16(const float (&w2)[S::K2], const float *h1, float *h2, const float *b2,
+                                              int r2, int s2, int act)
+{
+    static_assert(S::S2 == 16, "one batch row per lane of the row group");
+    const float4 *v4 = reinterpret_cast<const float4 *>(h1) + s2;
+    float t[16];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {  // 8 rows at a time: fewer accumulators live
+        float a0[8], a1[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            a0[r] = a1[r] = 0.f;
+#pragma unroll
+        for (int j = 0; j < S::K2 / 4; ++j) {
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const float4 v = v4[(8 * half + r) * (H1 / 4) + j * S::S2];
+                if constexpr (PACKED) {
+                    fma_pair<true>(a0[r], a1[r], w2[4 * j], w2[4 * j + 1], v.x, v.y);
+                    fma_pair<true>(a0[r], a1[r], w2[4 * j + 2], w2[4 * j + 3], v.z, v.w);
+                } else {
+                    a0[r] = fmaf(w2[4 * j], v.x, a0[r]);
+                    a1[r] = fmaf(w2[4 * j + 1], v.y, a1[r]);
+                    a0[r] = fmaf(w2[4 * j + 2], v.z, a0[r]);
+                    a1[r] = fmaf(w2[4 * j + 3], v.w, a1[r]);
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            t[8 * half + r] = a0[r] + a1[r];
+    }
+    const int lane = threadIdx.x & 31;
+    xreduce_round<16, 8>(t, lane);
+    xreduce_round<8, 4>(t, lane);
+    xreduce_round<4, 2>(t, lane);
+    xreduce_round<2, 1>(t, lane);
+    h2[s2 * S::R2 + r2] = relu_or(t[0] + b2[r2], act);  // lane s2 holds batch row s2
+}
+
+// Layer 3 over 16 batch rows at once: after the transpose-reduce over 32 lanes (masks 16, 8,
+// 4, 2, then a last butterfly step with mask 1) lanes 2r and 2r + 1 hold batch row r's
+// partial; lane r returns row r's (bit-identical to f3_layer3).
+template <class S>
+__device__ __forceinline__ float f3_layer3_x16(const float (&w3)[S::K3], const float *h2, int lane)
+{
+    float t[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < S::K3; ++j)
+            acc = fmaf(w3[j], h2[r * S::R2 + lane + 32 * j], acc);
+        t[r] = acc;
+    }
+    xreduce_round<16, 16>(t, lane);
+    xreduce_round<8, 8>(t, lane);
+    xreduce_round<4, 4>(t, lane);
+    xreduce_round<2, 2>(t, lane);
+    t[0] += __shfl_xor_sync(0xffffffffu, t[0], 1);
+    return __shfl_sync(0xffffffffu, t[0], (2 * lane) & 31);
 }
 
 // Layer 3, K-split over the CTA's R2 rows of h2: the warp that owns an output returns, in lane
@@ -464,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     if (tagged) {
                         const uint32_t sq = GR == 1 ? seq : rseq[r];
                         if (lane < NYC)
-                            st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done + (uint32_t)r) * p.ring_stride_f +
+                            st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done + (uint32_t)r) * p.ring_ystride_f +
                                                   4 * lane,
                                               make_float4(yr[3 * lane], yr[3 * lane + 1], yr[3 * lane + 2],
                                                           __uint_as_float(sq)));

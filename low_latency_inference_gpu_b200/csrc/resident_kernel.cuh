@@ -328,7 +328,7 @@ __device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uin
     const Params &p = *k.p;
     const int lane = threadIdx.x & 31;
     const int nxc = (p.in_dim + 2) / 3;
-    const uint4 *chunks = reinterpret_cast<const uint4 *>(p.mb_x + (size_t)slot * p.ring_stride_f);
+    const uint4 *chunks = reinterpret_cast<const uint4 *>(p.mb_x + (size_t)slot * p.ring_xstride_f);
     const uint32_t want = next_seq_dev(last);
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 0;; ++it) {
@@ -410,8 +410,8 @@ constexpr int kTagReadWarpsMax = 16;
 // ring slots of requests n .. n+maxb-1 of this launch (slot ring_slot(n + i)), taking
 // every request that is complete and follows without a gap: slot n+i is taken when each
 // of its chunks carries the (i+1)-th sequence number after `last`.  Warp w reads the
-// rows [w * rpw, (w + 1) * rpw) (rpw = tag_rows_per_warp(nxc) whole slots, its chunks in
-// registers); the warps' loads are all in flight at once, so one PCIe round trip reads
+// rows [w * rpw, (w + 1) * rpw) (rpw whole slots, by default tag_rows_per_warp(nxc), its
+// chunks in registers); the warps' loads are all in flight at once, so one PCIe round trip reads
 // all maxb slots (maxb <= nw * rpw <= kTagReadWarpsMax * rpw and maxb <= 32, checked on
 // the host).  Each warp's mask of incomplete rows goes through bad_words[w] (shared
 // memory) and a named barrier (id 2, nw warps), so every warp sees the same first gap.
@@ -423,14 +423,17 @@ constexpr int kTagReadWarpsMax = 16;
 // single-slot round trips are shorter: a read that spans several slots was measured
 // ~2 us slower to detect a new request).
 __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uint32_t n, int maxb, uint32_t *seqs,
-                                uint32_t *posted, uint32_t *bad_words, int nw, const ChunkFwd *fwd = nullptr)
+                                uint32_t *posted, uint32_t *bad_words, int nw, const ChunkFwd *fwd = nullptr,
+                                int rpw = 0)
 {
     const Params &p = *k.p;
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int nxc = (p.in_dim + 2) / 3;
-    const int r0 = warp * tag_rows_per_warp(nxc);
-    const int rows_here = min(tag_rows_per_warp(nxc), maxb - r0);
+    if (rpw <= 0)
+        rpw = tag_rows_per_warp(nxc);  // rows per reading warp (at most what its registers hold)
+    const int r0 = warp * rpw;
+    const int rows_here = min(rpw, maxb - r0);
     const int total = rows_here > 0 ? rows_here * nxc : 0;
     uint4 c[kTagChunksPerLane];
     int row[kTagChunksPerLane], ch[kTagChunksPerLane];
@@ -442,7 +445,7 @@ __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uin
         ch[j] = q - rl * nxc;
         if (q < total)
             c[j] = ld_relaxed_sys_v4_u32(reinterpret_cast<const unsigned *>(
-                p.mb_x + (size_t)ring_slot(p, n + (uint32_t)row[j]) * p.ring_stride_f + 4 * ch[j]));
+                p.mb_x + (size_t)ring_slot(p, n + (uint32_t)row[j]) * p.ring_xstride_f + 4 * ch[j]));
     }
     const uint32_t seen = (warp == 0 && lane == 31) ? ld_relaxed_sys(&p.mb->seq_in) : 0u;
     if (warp == 0)
@@ -453,6 +456,8 @@ __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uin
         if (lane + 32 * j < total && c[j].w != seq_after(last, row[j] + 1))
             bad |= 1u << row[j];
     bad = __reduce_or_sync(0xffffffffu, bad);
+    if (warp == 0 && lane == 0)
+        trace(k, n, 11);  // this warp's loads have landed
     if (nw > 1) {
         if (lane == 0)
             bad_words[warp] = bad;
@@ -1049,7 +1054,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
                             v[e] = G[o];
                         }
                     }
-                    st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done) * p.ring_stride_f + 4 * ch,
+                    st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, n_done) * p.ring_ystride_f + 4 * ch,
                                       make_float4(v[0], v[1], v[2], __uint_as_float(seq)));
                 }
                 __syncwarp();

@@ -12,11 +12,11 @@
 //                 tells the I/O CTA the buffer is free, runs the layers and sends its
 //                 layer-3 partials into the I/O CTA's gather buffer of that parity;
 //   rank C        the I/O CTA, no weights:
-//                 warps 0..3   reader: poll the next ring slot, or read up to micro_batch
+//                 warps 0..7   reader: poll the next ring slot, or read up to micro_batch
 //                              waiting slots at once, and forward their chunks to the C
 //                              compute CTAs straight from registers (the same protocol as
 //                              the register-resident kernel);
-//                 warps 4..15  gatherer: add the C partials per output in rank order, apply
+//                 warps 8..15  gatherer: add the C partials per output in rank order, apply
 //                              bias and activation, write each reply into its slot.
 // Pass p uses buffer b = p & 1 on both sides.  Before forwarding pass p the reader waits
 // until every compute CTA has unpacked pass p-2 (mbarrier `xfree[b]`, C remote arrivals)
@@ -36,9 +36,11 @@
 
 namespace llk {
 
-constexpr int kRingReadWarps = 4;    // I/O CTA warps 0..3
-constexpr int kRingGatherWarp0 = 4;  // I/O CTA warps 4..15
+constexpr int kRingReadWarps = 8;    // I/O CTA warps 0..7
+constexpr int kRingGatherWarp0 = 8;  // I/O CTA warps 8..15
+constexpr int kRingRowsPerReadWarp = 2;  // slots one reading warp takes of a multi-slot read
 constexpr int kRingGatherThreads = kThreads - 32 * kRingGatherWarp0;
+constexpr bool kRingPacked = true;  // layers 1-2 with packed fp32 FMAs (the same rounding as scalar ones)
 
 // A warp waits for an mbarrier phase.  Lane 0 watches the clock and, when `abortable`, the
 // abort flags.  Returns 1 when the phase completed, 0 on abort, -1 when the bound ran out;
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     if (io && tid == 0)
         st_relaxed_sys_u32(&p.ctrl->state, ST_RUNNING);
 
-    uint32_t passes_done = 0, rows_done = 0;
+    uint32_t passes_done = 0, rows_done = 0, last_replied = 0;
     if (!io) {
         // ======================= compute CTA =======================
         const int r1 = tid / S::S1, s1 = tid % S::S1;
@@ -183,6 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 mbar_arrive_expect_tx(bar(b), 16u + 16u * NXC);
             if (!cta_wait_bar(k, bar(b), par, EW_PEER_POLL, p.idle_ns + p.peer_margin_ns))
                 break;
+            if (k.rank == 0 && tid == 0)
+                trace(k, n_req, 8);
             const uint32_t seq = *reinterpret_cast<volatile uint32_t *>(&hdr2[b][0]);
             uint32_t nb = *reinterpret_cast<volatile uint32_t *>(&hdr2[b][1]);
             nb = nb < 1u ? 1u : (nb > (uint32_t)MB ? (uint32_t)MB : nb);
@@ -197,6 +201,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                     ++ph_x[1];
                 else
                     ++ph_x[0];
+                if (k.rank == 0 && tid == 0)
+                    trace(k, n_req, 9);
             }
             // unpack {v0, v1, v2, tag} chunks into the x rows, then release the chunk buffer
             const uint4 *xch = reinterpret_cast<const uint4 *>(pool + OFF_XCH + b * XCH_B);
@@ -213,26 +219,33 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             __syncthreads();
             if (tid == 0)
                 mbar_arrive_remote(mapa(bar(6 + b), (uint32_t)IO));
+            if (k.rank == 0 && tid == 0)
+                trace(k, n_req, 10);
             const int gr = nb == 1 ? 1 : kFast3Group;
             const int ng = (int)(nb + (uint32_t)gr - 1) / gr;
             if (nb == 1)
-                f3_layer1<S, 1, IN, H1>(w1, xs, h1, bias, 1, r1, s1, act1);
+                f3_layer1<S, 1, IN, H1, kRingPacked>(w1, xs, h1, bias, 1, r1, s1, act1);
             else
-                f3_layer1<S, kFast3Group, IN, H1>(w1, xs, h1, bias, ng, r1, s1, act1);
+                f3_layer1<S, kFast3Group, IN, H1, kRingPacked>(w1, xs, h1, bias, ng, r1, s1, act1);
             __syncthreads();
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 3);
+            // more than one group: all 16 rows at once with transposed reductions (the rows past
+            // nb compute on stale inputs inside the buffers and are never sent)
             if (nb == 1)
-                f3_layer2<S, 1, H1>(w2, h1, h2, bias + H1, 1, r2, s2, act2);
+                f3_layer2<S, 1, H1, kRingPacked>(w2, h1, h2, bias + H1, 1, r2, s2, act2);
+            else if (nb <= (uint32_t)kFast3Group)
+                f3_layer2<S, kFast3Group, H1, kRingPacked>(w2, h1, h2, bias + H1, ng, r2, s2, act2);
             else
-                f3_layer2<S, kFast3Group, H1>(w2, h1, h2, bias + H1, ng, r2, s2, act2);
+                f3_layer2_x16<S, H1, false>(w2, h1, h2, bias + H1, r2, s2, act2);
             __syncthreads();
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 4);
             // layer 3: K-split partials into the I/O CTA's gather buffer of this parity
             if (warp < OUT) {
                 const float mine = nb == 1 ? f3_layer3<S, 1>(w3, h2, 1, lane)
-                                           : f3_layer3<S, kFast3Group>(w3, h2, (int)nb, lane);
+                                   : nb <= (uint32_t)kFast3Group ? f3_layer3<S, kFast3Group>(w3, h2, (int)nb, lane)
+                                                                 : f3_layer3_x16<S>(w3, h2, lane);
                 const uint32_t g_addr = pool_a + OFF_G + (uint32_t)b * 4u * GATH_F;
                 if (lane < (int)nb)
                     st_async_u32(mapa(g_addr + (uint32_t)((lane * C + (int)k.rank) * OUT + warp) * 4u, (uint32_t)IO),
@@ -247,14 +260,17 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
         // Warp 0 makes every decision and publishes it in shared memory; the other reading
         // warps (a multi-slot read of more than 5 slots) follow through named barrier 2, so
         // they never part ways at a barrier.
-        constexpr int RPW = tag_rows_per_warp(NXC);
-        static_assert(RPW >= 1, "a reading warp holds at least one slot");
+        constexpr int RPW = tag_rows_per_warp(NXC) < kRingRowsPerReadWarp ? tag_rows_per_warp(NXC)
+                                                                           : kRingRowsPerReadWarp;
+        static_assert(RPW >= 1 && (kFast3Rows + RPW - 1) / RPW <= kRingReadWarps, "reading warps hold whole slots");
         const int read_warps = p.micro_batch > 1 ? (p.micro_batch + RPW - 1) / RPW : 1;
         if (warp < read_warps) {
             uint32_t last = p.last_seq, n_done = 0;
             for (uint32_t pass = 0;; ++pass) {
                 const int b = (int)(pass & 1u);
                 if (warp == 0) {
+                    if (lane == 0)
+                        trace(k, n_done, 7);
                     int w = 1;
                     if (pass >= 2) {
                         // the compute CTAs have unpacked, and the gatherer has finished, pass - 2
@@ -272,6 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                         // (no phase is posted here: pass p - 2 may still be unfinished, and a second
                         // phase of posted[b] would look like none to the gatherer)
                         sh.cmd = w == 1 ? 1u : 0u;
+                        trace(k, n_done, 6);
                     }
                 }
                 if (read_warps > 1)
@@ -284,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 int got = 0;
                 if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[pass & 1u]))
                     got = take_tagged_rows(k, last, nullptr, n_done, p.micro_batch, mseq[b], &posted, bad_words,
-                                           read_warps, &fwd);
+                                           read_warps, &fwd, RPW);
                 if (warp == 0) {
                     uint32_t c;
                     if (got > 0) {
@@ -320,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     } else {
         // ======================= I/O CTA: gatherer =======================
         // Gatherer warp 0 waits for the pass and its partials and publishes the row count
-        // (0 = leave); all gatherer warps then finish rows gw, gw + 12, ... of the pass.
+        // (0 = leave); all gatherer warps then finish rows gw, gw + 8, ... of the pass.
         const int gt = tid - 32 * kRingGatherWarp0, gw = warp - kRingGatherWarp0;
         constexpr int NGW = kRingGatherThreads / 32;
         for (uint32_t pass = 0;; ++pass) {
@@ -370,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 __syncwarp();
                 constexpr int NYC = (OUT + 2) / 3;
                 if (lane < NYC)
-                    st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, base + (uint32_t)r) * p.ring_stride_f + 4 * lane,
+                    st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, base + (uint32_t)r) * p.ring_ystride_f + 4 * lane,
                                       make_float4(yr[3 * lane], yr[3 * lane + 1], yr[3 * lane + 2],
                                                   __uint_as_float(mseq[b][r])));
                 __syncwarp();
@@ -378,12 +395,18 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             asm volatile("bar.sync 3, %0;" ::"r"(kRingGatherThreads) : "memory");  // every row of the pass written
             if (gt == 0) {
                 trace(k, base, 13);
-                st_relaxed_sys_u32(&p.mb->seq_out, mseq[b][nb - 1]);  // bookkeeping: the host waits on the tags
-                mbar_arrive_remote(mapa(bar(8 + b), (uint32_t)IO));   // gfree[b]
+                mbar_arrive_remote(mapa(bar(8 + b), (uint32_t)IO));  // gfree[b]
             }
+            last_replied = mseq[b][nb - 1];
             ++passes_done;
             rows_done += nb;
         }
+        // seq_out is bookkeeping on the tagged mailbox (the host waits on the y tags and reads
+        // seq_out after an exit, to resume the ring): written once here, not per pass, because
+        // it shares a line with seq_in, which the host writes for every request and the reader
+        // polls; a device write per pass made that line travel between CPU and GPU
+        if (gt == 0 && passes_done > 0)
+            st_relaxed_sys_u32(&p.mb->seq_out, last_replied);
     }
     __syncthreads();
     cluster_sync();
