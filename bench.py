@@ -14,7 +14,8 @@ Reported:
   e2e     inferences/s through the C ABI with host buffers: a closed loop that
           keeps the tagged request ring full (each request's x copied from a host
           array into its ring slot, its y copied out to a host array as soon as
-          it is there; up to 16 waiting requests taken per kernel pass), one host
+          it is there; up to 16 waiting requests taken per kernel pass by the
+          pipelined ring kernel), one host
           thread per GPU.  p50/p99 are the batch-1 latency of a single sequential
           stream (ll_infer's closed loop: write x, spin until y is there, copy y
           out; host steady clock) on the same engine.  The tagged mailbox carries
@@ -31,8 +32,8 @@ Reported:
           host copies), and the same rows through the resident small-batch engine
           (TickBuffer end to end, and device time per forward from a queue).
   serving open-loop Poisson arrivals at 50k / 200k / 1M requests/s aggregate over the
-          N GPUs (config-0 MLP on every GPU, 32-slot tagged request ring, up to 16
-          waiting requests per kernel pass): p50/p99 latency from the scheduled
+          N GPUs (config-0 MLP on every GPU, 64-slot tagged request ring, up to 16
+          waiting requests per kernel pass, pipelined ring kernel): p50/p99 latency from the scheduled
           arrival, sustained throughput and requests per pass.
   --impl reference  runs the reference's CPU forward on all host cores instead
           (weights and inputs drawn by the oracle's own generators: that process
@@ -134,14 +135,16 @@ def merge_serving(per_rank, rate, n_total):
 
 def run_serving(ll, net, Ws, bs, xs, rank, world, hg, dev):
     """Open-loop Poisson streams (seed 5) over all ranks: each rank serves the requests drawn
-    for it through its own engine (tagged mailbox, 32-slot ring, up to MICRO_BATCH waiting
-    requests taken per kernel pass); latency from the scheduled arrival; merged on rank 0.  The
+    for it through its own engine (tagged mailbox, RING_SLOTS-slot ring, up to MICRO_BATCH
+    waiting requests taken per kernel pass, the pipelined ring kernel); latency from the
+    scheduled arrival; merged on rank 0.  The
     resident kernel is stopped after each stream so that its pass / request counters are
     read (the next stream relaunches it before its first arrival)."""
     o = ll.default_opts()
     o.mailbox_format = 1
-    o.ring_slots = 32
+    o.ring_slots = RING_SLOTS
     o.micro_batch = MICRO_BATCH
+    o.kernel_variant = ll.VARIANT_PIPELINED_RING
     out = []
     with ll.Engine(net, Ws, bs, device=dev, opts=o) as e:
         e.serve_poisson(xs, 2000, 50_000.0, seed=99, rank=rank, world=world)  # warm-up stream
@@ -158,7 +161,8 @@ def run_serving(ll, net, Ws, bs, xs, rank, world, hg, dev):
             out.append(merge_serving(per_rank, rate, n_total))
     return {"workload": "config-0 MLP replicated per GPU, Poisson arrivals (std::mt19937_64 seed 5), "
                         "each request to a GPU drawn uniformly; U[-1,1] inputs",
-            "mailbox": f"tagged, 32-slot request ring, micro_batch {MICRO_BATCH}", "seconds_of_arrivals": SERVING_SECONDS,
+            "mailbox": f"tagged, {RING_SLOTS}-slot request ring, micro_batch {MICRO_BATCH}, pipelined ring kernel",
+            "seconds_of_arrivals": SERVING_SECONDS,
             "rates": out}
 
 
@@ -644,6 +648,7 @@ def main():
         returns (seconds, post-to-reply latencies, relaunches)."""
         o = opts(1)
         o.ring_slots, o.micro_batch = RING_SLOTS, MICRO_BATCH
+        o.kernel_variant = ll.VARIANT_PIPELINED_RING
         lat_all = []
         with ll.Engine(net, Ws, bs, device=dev, opts=o) as eng:
             eng.start()
@@ -752,7 +757,8 @@ def main():
                 "d2h_bytes_per_step": world * R * 16 * 4,
                 "mode": f"closed loop keeping a {RING_SLOTS}-slot tagged request ring full, one host thread per "
                         "GPU; x copied from a host array into the ring slot and y out to a host array per request; "
-                        f"up to {MICRO_BATCH} waiting requests per kernel pass",
+                        f"up to {MICRO_BATCH} waiting requests per kernel pass; pipelined ring kernel (an I/O CTA "
+                        "reads the next requests and writes replies while 8 compute CTAs run the previous pass)",
                 "requests_per_pass": ring_rpp,
                 "ring_latency_p50_us": s_ring["p50"], "ring_latency_p99_us": s_ring["p99"],
                 "p50_us": s_e2e["p50"], "p99_us": s_e2e["p99"], "p90_us": s_e2e["p90"],
