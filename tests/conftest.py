@@ -37,3 +37,16 @@ def rel_err(y, ref):
     ref = np.asarray(ref, np.float64)
     den = max(float(np.max(np.abs(ref))), 1e-30)
     return float(np.max(np.abs(y - ref))) / den
+
+
+def close(y, ref, tol):
+    """Both tolerance checks: norm-wise rel_err <= tol, and element-wise
+    |y - ref| <= tol * |ref| + (tol / 5) * max|ref| (relative per element, with an
+    absolute floor a fifth of the norm-wise bound for outputs near zero)."""
+    import numpy as np
+
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    scale = max(float(np.max(np.abs(ref))), 1e-30)
+    elem = np.abs(y - ref) <= tol * np.abs(ref) + (tol / 5.0) * scale
+    return rel_err(y, ref) <= tol and bool(np.all(elem))

@@ -12,7 +12,7 @@ import torch
 
 import low_latency_inference_gpu_b200 as ll
 import oracle
-from conftest import rel_err
+from conftest import close, rel_err
 
 pytestmark = [pytest.mark.gpu, pytest.mark.timeout(600)]
 
@@ -57,7 +57,7 @@ def test_small_net_every_tile_shape(wtype, bn, splits):
         assert info["bn"] == [bn, bn] and info["splits"] == [splits, splits]
         y = run_device(m, xs)
     ref = oracle_out(net, Ws, bs, xs)
-    assert rel_err(y, ref) <= TOL[wtype], (bn, splits)
+    assert close(y, ref, TOL[wtype]), (bn, splits)
 
 
 @pytest.mark.parametrize("rows", [1, 7, 128, 129, 256])
@@ -70,7 +70,7 @@ def test_config3_int8_rows(rows):
         y = run_device(m, xs)
     check = np.r_[0:min(rows, 12), max(0, rows - 12):rows]
     ref = oracle_out(net, Ws, bs, xs[check])
-    assert rel_err(y[check], ref) <= TOL[ll.W_I8]
+    assert close(y[check], ref, TOL[ll.W_I8])
 
 
 def test_config3_repeated_forwards_are_identical():
@@ -109,7 +109,7 @@ def test_config2_bf16_gelu_batch_sweep(rows):
     with make(net, Ws, bs) as m:
         y = run_device(m, xs)
     ref = oracle_out(net, Ws, bs, xs)
-    assert rel_err(y, ref) <= TOL[ll.W_BF16]
+    assert close(y, ref, TOL[ll.W_BF16])
 
 
 @pytest.mark.parametrize("rows", [1, 3, 5, 13, 31])
@@ -121,7 +121,7 @@ def test_small_batch_kernel_ragged_rows(rows):
     with make(net, Ws, bs) as m:
         assert m.info()["kind"] == [ll.KERNEL_GEMV] * 6
         y = run_device(m, xs)
-    assert rel_err(y, oracle_out(net, Ws, bs, xs)) <= TOL[ll.W_BF16]
+    assert close(y, oracle_out(net, Ws, bs, xs), TOL[ll.W_BF16])
 
 
 @pytest.mark.parametrize("rows", [1, 32])
@@ -144,7 +144,7 @@ def test_small_batch_kernel_int8(rows):
     with make(net, Ws, bs) as m:
         assert m.info()["kind"] == [ll.KERNEL_GEMV] * 3
         y = run_device(m, xs)
-    assert rel_err(y, oracle_out(net, Ws, bs, xs)) <= TOL[ll.W_I8]
+    assert close(y, oracle_out(net, Ws, bs, xs), TOL[ll.W_I8])
 
 
 def test_config3_single_row_on_small_batch_kernel():
@@ -216,7 +216,7 @@ def test_weights_in_tmem_tiles_small_net(wtype):
         y = run_device(m, xs)
         y300 = run_device(m, xs[:300])  # a ragged row count: the second row block is partial
     ref = oracle_out(net, Ws, bs, xs)
-    assert rel_err(y, ref) <= TOL[wtype]
+    assert close(y, ref, TOL[wtype])
     assert np.array_equal(y300, y[:300])
 
 
@@ -229,4 +229,4 @@ def test_config3_stacked_batches_auto():
         y = run_device(m, xs)
     check = np.r_[0:8, 1020:1030, 2040:2048]
     ref = oracle_out(net, Ws, bs, xs[check])
-    assert rel_err(y[check], ref) <= TOL[ll.W_I8]
+    assert close(y[check], ref, TOL[ll.W_I8])

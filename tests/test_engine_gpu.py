@@ -13,7 +13,7 @@ import pytest
 
 import low_latency_inference_gpu_b200 as ll
 import oracle
-from conftest import rel_err
+from conftest import close, rel_err
 
 pytestmark = [pytest.mark.gpu, pytest.mark.timeout(300)]
 
@@ -67,7 +67,7 @@ def test_config0_parity_oracle_and_golden(golden):
         info = e.info()
     assert info.kernel_variant == 2 and info.cluster_size == 8  # register-resident kernel by default
     ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
-    assert rel_err(ys, ref) <= 1e-5
+    assert close(ys, ref, 1e-5)
     gy = unbits(g["y"]).reshape(g["n"], -1)
     assert rel_err(ys[: g["n"]], gy) <= 1e-5
 
@@ -90,7 +90,7 @@ def test_config1_multi_cluster_parity(golden):
         ys = np.stack([e.infer(xs[i])[0] for i in range(16)])
         assert e.info().n_stages > 1
     ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
-    assert rel_err(ys, ref) <= 1e-5
+    assert close(ys, ref, 1e-5)
     assert rel_err(ys[: g["n"]], unbits(g["y"]).reshape(g["n"], -1)) <= 1e-5
 
 
@@ -139,7 +139,7 @@ def test_small_batches_and_precisions(wtype, act, rows):
     xs = ll.fill_uniform(rows * 40, -1, 1, 8).reshape(rows, 40)
     with engine_for(net, Ws, bs, cluster_size=4, min_stages=2) as e:
         y = e.infer(xs)
-    assert rel_err(y, oracle_out(net, Ws, bs, xs)) <= TOL[wtype]
+    assert close(y, oracle_out(net, Ws, bs, xs), TOL[wtype])
 
 
 @pytest.mark.parametrize("dims", [[33, 597, 293, 7], [5, 3], [17, 100, 1], [1, 1, 1]])
@@ -149,7 +149,7 @@ def test_odd_shapes(dims):
     xs = ll.fill_uniform(4 * dims[0], -1, 1, 4).reshape(4, -1)
     with engine_for(net, Ws, bs, cluster_size=8) as e:
         ys = np.stack([e.infer(xs[i])[0] for i in range(4)])
-    assert rel_err(ys, oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)) <= 1e-5
+    assert close(ys, oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs), 1e-5)
 
 
 def test_reference_style_raw_mailbox_host_loop():
