@@ -197,6 +197,37 @@ def run_config1(ll, torch, dev):
     return out
 
 
+# pipelined ring kernel: trace slot -> phase (globaltimer stamps of one pass; the reader's
+# stamp 0 is taken once the pass's slots are read and forwarded)
+RING_TRACE_PHASES = ((7, "reader_pass_start"), (6, "reader_flow_control_done"), (11, "reader_slots_loaded"),
+                     (8, "compute_row0_arrived"), (9, "compute_rows_arrived"), (10, "compute_unpacked"),
+                     (3, "compute_layer1_done"), (4, "compute_layer2_done"), (5, "compute_layer3_sent"),
+                     (12, "gatherer_partials_in"), (13, "gatherer_replies_written"))
+
+
+def ring_pass_trace(ll, torch, eng, xs, dev, n_req=8192, first=60, last=250):
+    """Untimed: one more closed loop on the ring engine with the device timeline on, then the
+    median offset of each phase of a pass from the reader's stamp (ns) and the median period
+    between passes, over passes `first`..`last` (steady state, ring full)."""
+    tr = torch.zeros(4096 * 32, dtype=torch.int64, device=f"cuda:{dev}")
+    eng.set_trace(tr.data_ptr(), 4096)
+    eng.bench_ring(xs, n_req, RING_SLOTS)
+    eng.stop()
+    eng.set_trace(0, 0)
+    t = tr.cpu().numpy().reshape(4096, 32)
+    starts = [i for i in range(4096) if t[i, 0] > 0]
+    sel = list(zip(starts[first:last], starts[first + 1:last + 1]))
+    if not sel:
+        return None
+    out = {"passes": len(sel), "rows_per_pass": float(np.median([b - a for a, b in sel])),
+           "period_ns": float(np.median([t[b, 0] - t[a, 0] for a, b in sel]))}
+    for slot, name in RING_TRACE_PHASES:
+        v = [int(t[a, slot]) - int(t[a, 0]) for a, _ in sel if t[a, slot] > 0]
+        if v:
+            out[name + "_ns"] = float(np.median(v))
+    return out
+
+
 def measured_peak(key, fallback):
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -665,13 +696,14 @@ def main():
             host_barrier()
             eng.stop()
             i = eng.info()
-        return t1 - t0, np.concatenate(lat_all), relaunches, (i.rows / i.passes if i.passes else float("nan"))
+            trace = ring_pass_trace(ll, torch, eng, xs, dev) if full else None
+        return t1 - t0, np.concatenate(lat_all), relaunches, (i.rows / i.passes if i.passes else float("nan")), trace
 
     e2e_launches = 0
     e2e_local_s, lat_all, tb_s, lat_tb = float("nan"), np.array([float("nan")]), float("nan"), None
-    ring_s, lat_ring, ring_rpp = float("nan"), np.array([float("nan")]), float("nan")
+    ring_s, lat_ring, ring_rpp, ring_trace = float("nan"), np.array([float("nan")]), float("nan"), None
     if full:
-        ring_s, lat_ring, n, ring_rpp = ring_loop()
+        ring_s, lat_ring, n, ring_rpp, ring_trace = ring_loop()
         e2e_launches += n
         e2e_local_s, lat_all, n = closed_loop(engine)
         e2e_launches += n
@@ -760,6 +792,7 @@ def main():
                         f"up to {MICRO_BATCH} waiting requests per kernel pass; pipelined ring kernel (an I/O CTA "
                         "reads the next requests and writes replies while 8 compute CTAs run the previous pass)",
                 "requests_per_pass": ring_rpp,
+                "ring_pass_trace": ring_trace,
                 "ring_latency_p50_us": s_ring["p50"], "ring_latency_p99_us": s_ring["p99"],
                 "p50_us": s_e2e["p50"], "p99_us": s_e2e["p99"], "p90_us": s_e2e["p90"],
                 "latency": "p50/p90/p99: one sequential request stream (ll_infer's loop: x write to y read, host "
