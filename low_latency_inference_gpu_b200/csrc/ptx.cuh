@@ -113,6 +113,46 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
                  : "memory");
 }
 
+// ---- 1-D bulk copy of this CTA's shared memory into a peer CTA's (no multicast) ----
+// dst and bar are cluster addresses (mapa), src this CTA's; bytes a multiple of 16, both
+// addresses 16-byte aligned.  The copy completes `bytes` on the peer's mbarrier.
+__device__ __forceinline__ void bulk_s2peer(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst),
+                 "r"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group()
+{
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// The issuing thread waits until every bulk group but the newest N has read its source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read()
+{
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// The issuing thread waits until every bulk group it committed has completed.
+__device__ __forceinline__ void bulk_wait_group_all()
+{
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t saddr, uint4 v)
+{
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_shared()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---- system-scope accesses (host-mapped pinned memory over PCIe) ----
 __device__ __forceinline__ uint32_t ld_acquire_sys(const volatile uint32_t *p)
 {

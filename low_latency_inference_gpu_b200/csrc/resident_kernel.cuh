@@ -294,9 +294,17 @@ __device__ __forceinline__ uint32_t ring_slot(const Params &p, uint32_t n)
 // completes their barrier bar_first (row 0) or bar_rest (rows 1..); lane 0 adds a 16-byte
 // header {seq, rows} at hdr (on bar_first).  Every address is the same offset in each CTA
 // (mapa).
+// Where the chunks of a multi-row read go: chunk `ch` of row r lands at chunks + 16 (r nxc + ch)
+// in CTAs first .. first + peers - 1 (the same shared-memory offset in each); row 0 and the
+// header {seq, rows} complete bar_first there, rows 1.. bar_rest.  stage != 0: rows 1.. are
+// written to this CTA's shared memory at `stage` (same layout) and sent to each peer by one
+// bulk copy, so the reading warps do not wait for the pushes; warp 0's lane 0 issues the
+// copies, and the caller commits them as a bulk group and keeps `stage` unwritten until
+// they have read it.
 struct ChunkFwd {
     uint32_t chunks, hdr, bar_first, bar_rest;
     int first, peers;
+    uint32_t stage;
 };
 
 __device__ __forceinline__ void fwd_chunk(const ChunkFwd &f, int row, int ch, int nxc, uint4 c)
@@ -469,12 +477,31 @@ __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uin
     const uint32_t stop_bit = maxb < 32 ? (1u << maxb) : 0u;
     const int nb = (bad | stop_bit) ? __ffs(bad | stop_bit) - 1 : 32;  // complete slots before the first gap
     if (fwd && nb > 0) {
+        const bool staged = fwd->stage != 0u;
 #pragma unroll
         for (int j = 0; j < kTagChunksPerLane; ++j)
-            if (lane + 32 * j < total && row[j] < nb)
-                fwd_chunk(*fwd, row[j], ch[j], nxc, c[j]);
+            if (lane + 32 * j < total && row[j] < nb) {
+                if (staged && row[j] > 0)
+                    st_shared_v4(fwd->stage + 16u * (uint32_t)(row[j] * nxc + ch[j]), c[j]);
+                else
+                    fwd_chunk(*fwd, row[j], ch[j], nxc, c[j]);
+            }
         if (warp == 0 && lane == 0)
             fwd_header(*fwd, seq_after(last, nb), (uint32_t)nb);
+        if (staged && nb > 1) {
+            // every reading lane's staged chunks -> visible to the bulk copies (async proxy)
+            fence_proxy_async_shared();
+            if (nw > 1)
+                asm volatile("bar.sync 2, %0;" ::"r"(32 * nw) : "memory");
+            else
+                __syncwarp();
+            if (warp == 0 && lane == 0) {
+                const uint32_t off = 16u * (uint32_t)nxc, bytes = off * (uint32_t)(nb - 1);
+                for (int d = fwd->first; d < fwd->first + fwd->peers; ++d)
+                    bulk_s2peer(mapa(fwd->chunks + off, (uint32_t)d), fwd->stage + off, bytes,
+                                mapa(fwd->bar_rest, (uint32_t)d));
+            }
+        }
     }
 #pragma unroll
     for (int j = 0; j < kTagChunksPerLane; ++j) {

@@ -14,15 +14,20 @@
 //   rank C        the I/O CTA, no weights:
 //                 warps 0..7   reader: poll the next ring slot, or read up to micro_batch
 //                              waiting slots at once, and forward their chunks to the C
-//                              compute CTAs straight from registers (the same protocol as
-//                              the register-resident kernel);
+//                              compute CTAs: row 0 and the header {seq, rows} straight from
+//                              registers (the register-resident kernel's protocol), rows
+//                              1.. through a staging copy in this CTA's shared memory and
+//                              one bulk copy per compute CTA, which runs on while the
+//                              reader starts on the next pass;
 //                 warps 8..15  gatherer: add the C partials per output in rank order, apply
 //                              bias and activation, write each reply into its slot.
-// Pass p uses buffer b = p & 1 on both sides.  Before forwarding pass p the reader waits
-// until every compute CTA has unpacked pass p-2 (mbarrier `xfree[b]`, C remote arrivals)
-// and until the gatherer has finished pass p-2 (`gfree[b]`), so no buffer is overwritten
-// while it is still read; the reader hands each pass's row count, first request index and
-// sequence numbers to the gatherer through `posted[b]`.  Requests are taken and replies
+// Pass p uses x chunk buffer b = p & 1 and gather buffer g = p % 3 (partials and the
+// pass's row metadata).  Before forwarding pass p the reader waits until every compute CTA
+// has unpacked pass p-2 (mbarrier `xfree[b]`, C remote arrivals) and until the gatherer has
+// finished pass p-3 (`gfree[g]`), so no buffer is overwritten while it is still read; the
+// third gather buffer lets the reader start a pass while the replies of the pass two
+// before it are still being written.  The reader hands each pass's row count, first
+// request index and sequence numbers to the gatherer through `posted[g]`.  Requests are taken and replies
 // written in ring order, so the host-side protocol is the register-resident kernel's.
 // Every wait is bounded (step_timeout_ns inside a pass, idle_timeout_ns + a margin between
 // passes); an exit (stop, idle bound, abort) is broadcast to the cluster, and the gatherer
@@ -39,6 +44,7 @@ namespace llk {
 constexpr int kRingReadWarps = 8;    // I/O CTA warps 0..7
 constexpr int kRingGatherWarp0 = 8;  // I/O CTA warps 8..15
 constexpr int kRingRowsPerReadWarp = 2;  // slots one reading warp takes of a multi-slot read
+constexpr int kRingGathBufs = 3;  // gather buffers: the reader may run NG - 1 passes ahead of the replies
 constexpr int kRingGatherThreads = kThreads - 32 * kRingGatherWarp0;
 constexpr bool kRingPacked = true;  // layers 1-2 with packed fp32 FMAs (the same rounding as scalar ones)
 
@@ -78,7 +84,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     constexpr int NXC = (IN + 2) / 3;          // tagged chunks per row
     constexpr int YO = 3 * ((OUT + 2) / 3) + 4;  // one output row, zero-padded
     constexpr int IO = C;                      // rank of the I/O CTA
-    // One pool: compute CTAs use [xs | h1 | h2 | xch[2]], the I/O CTA [gath[2] | yo].  Remote
+    // One pool: compute CTAs use [xs | h1 | h2 | xch[2]], the I/O CTA [gath[NG] | yo | stage[2]]
+    // (stage: its copies of the rows it forwards).  Remote
     // writes go to the other role's region at the same offset in the receiving CTA.
     constexpr int OFF_XS = 0;
     constexpr int OFF_H1 = OFF_XS + 4 * MB * IN;
@@ -88,15 +95,16 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     constexpr int COMPUTE_END = OFF_XCH + 2 * XCH_B;
     constexpr int GATH_F = MB * C * OUT;  // [row][rank][output]
     constexpr int OFF_G = 0;
-    constexpr int OFF_YO = OFF_G + 2 * 4 * GATH_F;
-    constexpr int IO_END = OFF_YO + 4 * MB * YO;
+    constexpr int OFF_YO = OFF_G + kRingGathBufs * 4 * GATH_F;
+    constexpr int OFF_STG = (OFF_YO + 4 * MB * YO + 15) / 16 * 16;
+    constexpr int IO_END = OFF_STG + 2 * XCH_B;
     constexpr int POOL = COMPUTE_END > IO_END ? COMPUTE_END : IO_END;
     __shared__ __align__(16) uint8_t pool[POOL];
     __shared__ __align__(16) uint32_t hdr2[2][4];  // compute CTAs: {seq, rows} of the pass in buffer b
-    __shared__ __align__(8) uint64_t rb[12];       // see the barrier indices below
+    __shared__ __align__(8) uint64_t rb[6 + 3 * kRingGathBufs];  // see the barrier indices below
     __shared__ __align__(16) float bias[S::NB];
-    __shared__ uint32_t mseq[2][MB];               // I/O: sequence number of each row of the pass in buffer b
-    __shared__ uint32_t mrows[2], mbase[2];        // I/O: rows (0 = exit) and first request index
+    __shared__ uint32_t mseq[kRingGathBufs][MB];   // I/O: sequence number of each row of the pass in buffer g
+    __shared__ uint32_t mrows[kRingGathBufs], mbase[kRingGathBufs];  // I/O: rows (0 = exit), first request index
     __shared__ uint32_t bad_words[kTagReadWarpsMax];
     __shared__ uint32_t s_backlog[2];
     __shared__ __align__(16) Shared sh;
@@ -118,18 +126,23 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool io = k.rank == (uint32_t)IO;
     // barriers: compute CTAs 0,1 bar_req[b] (header + row 0), 2,3 bar_x[b] (rows 1..);
-    // I/O CTA 4,5 bar_g[b] (partials), 6,7 xfree[b], 8,9 gfree[b], 10,11 posted[b]
+    // I/O CTA 4,5 xfree[b], then NG each of bar_g[g] (partials), gfree[g], posted[g]
     auto bar = [&](int i) { return smem_u32(&rb[i]); };
+    constexpr int NG = kRingGathBufs;
+    auto bar_g = [&](int g) { return bar(6 + g); };
+    auto gfree = [&](int g) { return bar(6 + NG + g); };
+    auto posted_bar = [&](int g) { return bar(6 + 2 * NG + g); };
     const uint32_t pool_a = smem_u32(pool);
 
     if (tid == 0) {
         for (int i = 0; i < 4; ++i)
             mbar_init(bar(i), 1);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(bar(4 + i), 1);
-            mbar_init(bar(6 + i), C);
-            mbar_init(bar(8 + i), 1);
-            mbar_init(bar(10 + i), 1);
+        for (int i = 0; i < 2; ++i)
+            mbar_init(bar(4 + i), C);
+        for (int i = 0; i < NG; ++i) {
+            mbar_init(bar_g(i), 1);
+            mbar_init(gfree(i), 1);
+            mbar_init(posted_bar(i), 1);
         }
         sh.cmd = 0;
         sh.fail = 0;
@@ -159,8 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
         bias[i] = __ldg(img + (size_t)S::NW * kThreads + i);
     if (io) {
         float *gz = reinterpret_cast<float *>(pool + OFF_G);
-        for (int i = tid; i < 2 * GATH_F + MB * YO; i += kThreads)
-            gz[i] = 0.0f;  // gath[2] and yo are contiguous
+        for (int i = tid; i < NG * GATH_F + MB * YO; i += kThreads)
+            gz[i] = 0.0f;  // gath[NG] and yo are contiguous
     }
     __syncthreads();
     cluster_sync();  // every barrier of the cluster is initialised before any remote operation
@@ -218,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             }
             __syncthreads();
             if (tid == 0)
-                mbar_arrive_remote(mapa(bar(6 + b), (uint32_t)IO));
+                mbar_arrive_remote(mapa(bar(4 + b), (uint32_t)IO));  // xfree[b]
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 10);
             const int gr = nb == 1 ? 1 : kFast3Group;
@@ -246,10 +259,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 const float mine = nb == 1 ? f3_layer3<S, 1>(w3, h2, 1, lane)
                                    : nb <= (uint32_t)kFast3Group ? f3_layer3<S, kFast3Group>(w3, h2, (int)nb, lane)
                                                                  : f3_layer3_x16<S>(w3, h2, lane);
-                const uint32_t g_addr = pool_a + OFF_G + (uint32_t)b * 4u * GATH_F;
+                const uint32_t g = pass % (uint32_t)NG;
+                const uint32_t g_addr = pool_a + OFF_G + g * 4u * GATH_F;
                 if (lane < (int)nb)
                     st_async_u32(mapa(g_addr + (uint32_t)((lane * C + (int)k.rank) * OUT + warp) * 4u, (uint32_t)IO),
-                                 __float_as_uint(mine), mapa(bar(4 + b), (uint32_t)IO));
+                                 __float_as_uint(mine), mapa(bar_g((int)g), (uint32_t)IO));
             }
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 5);
@@ -267,40 +281,47 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
         if (warp < read_warps) {
             uint32_t last = p.last_seq, n_done = 0;
             for (uint32_t pass = 0;; ++pass) {
-                const int b = (int)(pass & 1u);
+                const int b = (int)(pass & 1u), g = (int)(pass % (uint32_t)NG);
                 if (warp == 0) {
                     if (lane == 0)
                         trace(k, n_done, 7);
                     int w = 1;
-                    if (pass >= 2) {
-                        // the compute CTAs have unpacked, and the gatherer has finished, pass - 2
-                        const uint32_t par = ((pass - 2u) >> 1) & 1u;
-                        w = warp_wait_bar(k, bar(6 + b), par, p.step_ns, true);
-                        if (w == 1)
-                            w = warp_wait_bar(k, bar(8 + b), par, p.step_ns, true);
-                    }
+                    // the compute CTAs have unpacked pass - 2 (x buffer b), and the gatherer has
+                    // finished pass - NG (gather buffer g, row metadata g)
+                    if (pass >= 2)
+                        w = warp_wait_bar(k, bar(4 + b), ((pass - 2u) >> 1) & 1u, p.step_ns, true);
+                    if (w == 1 && pass >= (uint32_t)NG)
+                        w = warp_wait_bar(k, gfree(g), ((pass - NG) / NG) & 1u, p.step_ns, true);
                     if (lane == 0) {
                         if (w < 0) {
                             report_error(k, LL_ERR_DEVICE_FAULT, EW_GATHER);
                             broadcast_abort(k);
                         }
                         // on a failed wait the abort flag is (or gets) set: the gatherer leaves on it
-                        // (no phase is posted here: pass p - 2 may still be unfinished, and a second
-                        // phase of posted[b] would look like none to the gatherer)
+                        // (no phase is posted here: pass p - NG may still be unfinished, and a second
+                        // phase of posted[g] would look like none to the gatherer)
+                        // the bulk copies of pass p - 2 have read staging buffer b (the newest group,
+                        // pass p - 1's, may still be in flight)
+                        bulk_wait_group_read<1>();
                         sh.cmd = w == 1 ? 1u : 0u;
                         trace(k, n_done, 6);
                     }
                 }
                 if (read_warps > 1)
                     asm volatile("bar.sync 2, %0;" ::"r"(32 * read_warps) : "memory");
+                else
+                    __syncwarp();
                 if (*reinterpret_cast<volatile uint32_t *>(&sh.cmd) == 0u)
                     break;
-                const ChunkFwd fwd{pool_a + OFF_XCH + (uint32_t)b * XCH_B, smem_u32(&hdr2[b][0]), bar(b), bar(2 + b), 0,
-                                   C};
+                // rows 1.. of a multi-slot read are staged in this CTA's stage[b] and bulk-copied
+                // to the compute CTAs' chunk buffer b
+                const uint32_t xch_b = pool_a + OFF_XCH + (uint32_t)b * XCH_B;
+                const ChunkFwd fwd{xch_b, smem_u32(&hdr2[b][0]), bar(b), bar(2 + b), 0, C,
+                                   pool_a + OFF_STG + (uint32_t)b * XCH_B};
                 uint32_t posted = 0;
                 int got = 0;
                 if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[pass & 1u]))
-                    got = take_tagged_rows(k, last, nullptr, n_done, p.micro_batch, mseq[b], &posted, bad_words,
+                    got = take_tagged_rows(k, last, nullptr, n_done, p.micro_batch, mseq[g], &posted, bad_words,
                                            read_warps, &fwd, RPW);
                 if (warp == 0) {
                     uint32_t c;
@@ -313,26 +334,32 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                     }
                     __syncwarp();  // the lanes' mseq writes come before lane 0's release below
                     if (lane == 0) {
+                        // this pass's bulk copies (none for a single row: an empty group), so
+                        // that the wait above, two passes on, covers exactly pass p - 2
+                        bulk_commit_group();
                         if (got == 1)
-                            mseq[b][0] = c;
+                            mseq[g][0] = c;
                         s_backlog[(pass + 1u) & 1u] =
                             (p.micro_batch > 1 && c != kCmdExit && (int32_t)(posted - c) > 0) ? 1u : 0u;
                         if (c == kCmdExit)
                             broadcast_abort(k);
-                        mrows[b] = c == kCmdExit ? 0u : (uint32_t)got;
-                        mbase[b] = n_done;
+                        mrows[g] = c == kCmdExit ? 0u : (uint32_t)got;
+                        mbase[g] = n_done;
                         trace(k, n_done, 0);
-                        mbar_arrive_remote(mapa(bar(10 + b), (uint32_t)IO));  // posted[b] (release, cluster scope)
+                        mbar_arrive_remote(mapa(posted_bar(g), (uint32_t)IO));  // (release, cluster scope)
                     }
                 }
                 if (read_warps > 1)
                     asm volatile("bar.sync 2, %0;" ::"r"(32 * read_warps) : "memory");
-                const uint32_t rows = *reinterpret_cast<volatile uint32_t *>(&mrows[b]);
+                const uint32_t rows = *reinterpret_cast<volatile uint32_t *>(&mrows[g]);
                 if (rows == 0u)
                     break;
                 last = seq_after(last, (int)rows);
                 n_done += rows;
             }
+            // no bulk copy into a compute CTA may be in flight when the cluster leaves
+            if (warp == 0 && lane == 0)
+                bulk_wait_group_all();
         }
     } else {
         // ======================= I/O CTA: gatherer =======================
@@ -341,40 +368,40 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
         const int gt = tid - 32 * kRingGatherWarp0, gw = warp - kRingGatherWarp0;
         constexpr int NGW = kRingGatherThreads / 32;
         for (uint32_t pass = 0;; ++pass) {
-            const int b = (int)(pass & 1u);
-            const uint32_t par = (pass >> 1) & 1u;
+            const int g = (int)(pass % (uint32_t)NG);
+            const uint32_t par = (pass / NG) & 1u;
             if (gw == 0) {
                 // the next pass (abortable: an exit is broadcast; every pass posted before it has
                 // already been waited for in order), then its partials (not abortable: a pass that
                 // was forwarded is finished, within the step bound)
                 uint32_t nb = 0;
-                int w = warp_wait_bar(k, bar(10 + b), par, p.idle_ns + 2 * p.peer_margin_ns, true);
+                int w = warp_wait_bar(k, posted_bar(g), par, p.idle_ns + 2 * p.peer_margin_ns, true);
                 if (w == 1) {
-                    nb = *reinterpret_cast<volatile uint32_t *>(&mrows[b]);
+                    nb = *reinterpret_cast<volatile uint32_t *>(&mrows[g]);
                     if (nb > 0u) {
                         if (lane == 0)
-                            mbar_arrive_expect_tx(bar(4 + b), (uint32_t)(C * OUT * 4) * nb);
-                        w = warp_wait_bar(k, bar(4 + b), par, p.step_ns, false);
+                            mbar_arrive_expect_tx(bar_g(g), (uint32_t)(C * OUT * 4) * nb);
+                        w = warp_wait_bar(k, bar_g(g), par, p.step_ns, false);
                         if (w != 1)
                             nb = 0;
                     }
                 }
                 if (lane == 0) {
                     if (w < 0) {
-                        report_error(k, LL_ERR_DEVICE_FAULT, nb == 0u && mrows[b] == 0u ? EW_PEER_POLL : EW_GATHER);
+                        report_error(k, LL_ERR_DEVICE_FAULT, nb == 0u && mrows[g] == 0u ? EW_PEER_POLL : EW_GATHER);
                         broadcast_abort(k);
                     }
                     sh.nrows = nb;
                     if (nb > 0u)
-                        trace(k, mbase[b], 12);
+                        trace(k, mbase[g], 12);
                 }
             }
             asm volatile("bar.sync 3, %0;" ::"r"(kRingGatherThreads) : "memory");
             const uint32_t nb = *reinterpret_cast<volatile uint32_t *>(&sh.nrows);
             if (nb == 0u)
                 break;
-            const uint32_t base = *reinterpret_cast<volatile uint32_t *>(&mbase[b]);
-            const float *gath = reinterpret_cast<const float *>(pool + OFF_G) + (size_t)b * GATH_F;
+            const uint32_t base = *reinterpret_cast<volatile uint32_t *>(&mbase[g]);
+            const float *gath = reinterpret_cast<const float *>(pool + OFF_G) + (size_t)g * GATH_F;
             for (int r = gw; r < (int)nb; r += NGW) {
                 float *yr = reinterpret_cast<float *>(pool + OFF_YO) + r * YO;
                 if (lane < OUT) {
@@ -389,15 +416,15 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 if (lane < NYC)
                     st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, base + (uint32_t)r) * p.ring_ystride_f + 4 * lane,
                                       make_float4(yr[3 * lane], yr[3 * lane + 1], yr[3 * lane + 2],
-                                                  __uint_as_float(mseq[b][r])));
+                                                  __uint_as_float(mseq[g][r])));
                 __syncwarp();
             }
             asm volatile("bar.sync 3, %0;" ::"r"(kRingGatherThreads) : "memory");  // every row of the pass written
             if (gt == 0) {
                 trace(k, base, 13);
-                mbar_arrive_remote(mapa(bar(8 + b), (uint32_t)IO));  // gfree[b]
+                mbar_arrive_remote(mapa(gfree(g), (uint32_t)IO));
             }
-            last_replied = mseq[b][nb - 1];
+            last_replied = mseq[g][nb - 1];
             ++passes_done;
             rows_done += nb;
         }
