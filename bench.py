@@ -11,12 +11,13 @@ Reported:
   value   inferences/s with inputs already in HBM: the resident kernel's
           device-queue mode (each request starts after the previous finished,
           so this is 1 / device latency), timed with CUDA events per launch.
-  e2e     inferences/s through the C ABI with host buffers: a closed loop that
-          keeps the tagged request ring full (each request's x copied from a host
+  e2e     inferences/s through the C ABI with host buffers: closed loops that
+          keep tagged request rings full (each request's x copied from a host
           array into its ring slot, its y copied out to a host array as soon as
           it is there; up to 16 waiting requests taken per kernel pass by the
-          pipelined ring kernel), one host
-          thread per GPU.  p50/p99 are the batch-1 latency of a single sequential
+          pipelined ring kernel).  Each GPU runs several resident engines (a
+          9-SM cluster each, up to 8, half of the rank's host cores), each with
+          its own ring and host thread.  p50/p99 are the batch-1 latency of a single sequential
           stream (ll_infer's closed loop: write x, spin until y is there, copy y
           out; host steady clock) on the same engine.  The tagged mailbox carries
           x and y in 16-byte chunks stamped with the sequence number;
@@ -46,6 +47,7 @@ import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 
 import numpy as np
@@ -64,6 +66,7 @@ CONFIG = {"workload": WORKLOAD, "batch": 1, "precision": "fp32 weights, activati
                 "(registers) for a whole launch by design"}
 RING_SLOTS = 64  # e2e throughput leg: ring slots kept full
 MICRO_BATCH = 16  # waiting requests the register-resident kernel takes in one pass
+RING_ENGINES_MAX = 8  # throughput leg: resident engines per GPU (one host thread each)
 # DRAM traffic of one device-queue launch of the 8-CTA register-resident kernel, from
 # the committed ncu capture (1.352 MB for 2000 requests): the eight per-CTA register
 # images once (812 KB), then ~270 B per request (input row, stamp); scaled to R requests.
@@ -514,6 +517,25 @@ def pin_host_thread(local_rank, dev):
         return None
 
 
+def ring_thread_cores(allowed, local_rank, local_world, dev):
+    """Cores for the throughput leg's host threads, one per engine: this rank's share of the
+    allowed cores (those on its GPU's NUMA node when sysfs says which), every other one of
+    them, at most RING_ENGINES_MAX."""
+    cores = list(allowed)
+    try:
+        node = numa_node_of_gpu(dev)
+        if node is not None and node >= 0:
+            with open(f"/sys/devices/system/node/node{node}/cpulist") as f:
+                local = [c for c in _cpulist(f.read()) if c in set(allowed)]
+            if len(local) >= 2:
+                cores = local
+    except Exception:
+        pass
+    mine = cores[local_rank % len(cores)::max(1, local_world)] or cores
+    n = max(1, min(RING_ENGINES_MAX, len(mine) // 2))
+    return [mine[(1 + 2 * i) % len(mine)] for i in range(n)]
+
+
 def run_reference(args, rank, world):
     """The reference's own CPU forward (oracle/_ref, else the oracle port) on all host cores."""
     if rank != 0:
@@ -598,7 +620,9 @@ def main():
     hg = HostGroup(world, None)
     host_barrier, host_max, host_gather = hg.barrier, hg.max, hg.gather
 
+    allowed_cores = sorted(os.sched_getaffinity(0))
     core = pin_host_thread(local_rank, dev)
+    ring_cores = ring_thread_cores(allowed_cores, local_rank, env_int("LOCAL_WORLD_SIZE", world), dev)
     R, K, W = args.requests, args.steps, args.warmup
 
     net, Ws, bs = ll.config_params(0)
@@ -675,35 +699,72 @@ def main():
         return t1 - t0, np.concatenate(lat_all), relaunches
 
     def ring_loop():
-        """K timed steps of R requests with the RING_SLOTS-slot ring kept full (MICRO_BATCH);
-        returns (seconds, post-to-reply latencies, relaunches)."""
+        """K timed steps in which each of E = len(ring_cores) engines on this GPU serves R
+        requests with its RING_SLOTS-slot ring kept full (MICRO_BATCH), each engine driven by its
+        own host thread (ctypes releases the GIL for the C loop); returns (seconds, post-to-reply
+        latencies, relaunches, requests per pass, pass trace of engine 0, engines)."""
         o = opts(1)
         o.ring_slots, o.micro_batch = RING_SLOTS, MICRO_BATCH
         o.kernel_variant = ll.VARIANT_PIPELINED_RING
-        lat_all = []
-        with ll.Engine(net, Ws, bs, device=dev, opts=o) as eng:
-            eng.start()
-            for _ in range(W):
-                eng.bench_ring(xs, R, RING_SLOTS)
-            before = eng.info().launches
+        n_eng = len(ring_cores)
+        engs = [ll.Engine(net, Ws, bs, device=dev, opts=o) for _ in range(n_eng)]
+        lats = [[] for _ in range(n_eng)]
+        errors = []
+        ready, go, done = (threading.Barrier(n_eng + 1) for _ in range(3))
+
+        def drive(i):
+            try:
+                os.sched_setaffinity(0, {ring_cores[i]})  # this thread only
+                engs[i].start()
+                for _ in range(W):
+                    engs[i].bench_ring(xs, R, RING_SLOTS)
+            except Exception as ex:  # noqa: BLE001 - reported after the barriers
+                errors.append(repr(ex))
+            ready.wait()
+            go.wait()
+            try:
+                if not errors:
+                    for _ in range(K):
+                        lat, _, _ = engs[i].bench_ring(xs, R, RING_SLOTS)
+                        lats[i].append(lat)
+            except Exception as ex:  # noqa: BLE001
+                errors.append(repr(ex))
+            done.wait()
+
+        threads = [threading.Thread(target=drive, args=(i,), daemon=True) for i in range(n_eng)]
+        try:
+            for t in threads:
+                t.start()
+            ready.wait()
+            before = sum(e.info().launches for e in engs)
             host_barrier()
             t0 = time.perf_counter()
-            for _ in range(K):
-                lat, _, _ = eng.bench_ring(xs, R, RING_SLOTS)
-                lat_all.append(lat)
+            go.wait()
+            done.wait()
             t1 = time.perf_counter()
-            relaunches = eng.info().launches - before
+            for t in threads:
+                t.join()
+            if errors:
+                raise RuntimeError("ring leg: " + "; ".join(errors))
+            relaunches = sum(e.info().launches for e in engs) - before
             host_barrier()
-            eng.stop()
-            i = eng.info()
-            trace = ring_pass_trace(ll, torch, eng, xs, dev) if full else None
-        return t1 - t0, np.concatenate(lat_all), relaunches, (i.rows / i.passes if i.passes else float("nan")), trace
+            for e in engs:
+                e.stop()
+            infos = [e.info() for e in engs]
+            trace = ring_pass_trace(ll, torch, engs[0], xs, dev) if full else None
+        finally:
+            for e in engs:
+                e.close()
+        rows = sum(i.rows for i in infos)
+        passes = sum(i.passes for i in infos)
+        lat_all = np.concatenate([np.concatenate(x) for x in lats])
+        return t1 - t0, lat_all, relaunches, (rows / passes if passes else float("nan")), trace, n_eng
 
     e2e_launches = 0
     e2e_local_s, lat_all, tb_s, lat_tb = float("nan"), np.array([float("nan")]), float("nan"), None
-    ring_s, lat_ring, ring_rpp, ring_trace = float("nan"), np.array([float("nan")]), float("nan"), None
+    ring_s, lat_ring, ring_rpp, ring_trace, n_eng = float("nan"), np.array([float("nan")]), float("nan"), None, 1
     if full:
-        ring_s, lat_ring, n, ring_rpp, ring_trace = ring_loop()
+        ring_s, lat_ring, n, ring_rpp, ring_trace, n_eng = ring_loop()
         e2e_launches += n
         e2e_local_s, lat_all, n = closed_loop(engine)
         e2e_launches += n
@@ -714,7 +775,7 @@ def main():
     e2e_s = host_max(e2e_local_s)
     s_e2e = ll.compute_stats(lat_all)
     seq_value = world * K * R / e2e_s
-    ring_value = world * K * R / host_max(ring_s)
+    ring_value = world * n_eng * K * R / host_max(ring_s)
     s_ring = ll.compute_stats(lat_ring)
     s_tb = ll.compute_stats(lat_tb) if lat_tb is not None else None
     tb_value = world * K * R / host_max(tb_s)
@@ -755,7 +816,8 @@ def main():
     peak, peak_kind = measured_peak_hbm()
     avg_launch_s = (sum(launch_ms) / len(launch_ms)) / 1000.0
     achieved = R * (WEIGHT_BYTES + IO_BYTES) / avg_launch_s / 1e9
-    per_rank = host_gather({"rank": rank, "value": K * R / (sum(launch_ms) / 1000.0), "e2e": K * R / ring_s,
+    per_rank = host_gather({"rank": rank, "value": K * R / (sum(launch_ms) / 1000.0), "e2e": n_eng * K * R / ring_s,
+                            "ring_engines": n_eng, "ring_cores": ring_cores,
                             "sequential_e2e": K * R / e2e_local_s, "e2e_p50_us": s_e2e["p50"],
                             "e2e_p99_us": s_e2e["p99"], "tagged_x_to_y_floor_p50_us": floor["tagged_x_to_y"]["p50_us"],
                             "seq_only_floor_p50_us": floor["seq_only"]["p50_us"], "core": core,
@@ -785,12 +847,16 @@ def main():
         "engine": {"stages": info.n_stages, "cluster_size": info.cluster_size, "threads": info.threads,
                    "smem_bytes": info.smem_bytes,
                    "kernel": "register-resident" if info.kernel_variant == 2 else "shared-memory resident"},
-        "e2e": {"value": ring_value, "unit": "inferences/s", "h2d_bytes_per_step": world * R * 64 * 4,
-                "d2h_bytes_per_step": world * R * 16 * 4,
-                "mode": f"closed loop keeping a {RING_SLOTS}-slot tagged request ring full, one host thread per "
-                        "GPU; x copied from a host array into the ring slot and y out to a host array per request; "
-                        f"up to {MICRO_BATCH} waiting requests per kernel pass; pipelined ring kernel (an I/O CTA "
-                        "reads the next requests and writes replies while 8 compute CTAs run the previous pass)",
+        "e2e": {"value": ring_value, "unit": "inferences/s", "h2d_bytes_per_step": world * n_eng * R * 64 * 4,
+                "d2h_bytes_per_step": world * n_eng * R * 16 * 4,
+                "mode": f"{n_eng} resident engine(s) per GPU (each a 9-SM cluster running the pipelined ring "
+                        f"kernel: an I/O CTA reads the next requests and writes replies while 8 compute CTAs run "
+                        f"the previous pass), each with its own {RING_SLOTS}-slot tagged request ring kept full "
+                        "by its own host thread (a closed loop through ll_engine_bench_ring); x copied from a host "
+                        "array into the ring slot and y out to a host array per request; up to "
+                        f"{MICRO_BATCH} waiting requests per kernel pass",
+                "engines_per_gpu": n_eng, "host_threads_per_gpu": n_eng,
+                "per_engine_value": ring_value / (world * n_eng),
                 "requests_per_pass": ring_rpp,
                 "ring_pass_trace": ring_trace,
                 "ring_latency_p50_us": s_ring["p50"], "ring_latency_p99_us": s_ring["p99"],

@@ -72,3 +72,17 @@ def test_merge_reports_requests_per_kernel_pass():
     assert m["requests_per_pass"] == pytest.approx(40 / 20)
     assert m["served"] == 3 and m["sustained_per_s"] == 1.5
     assert "requests_per_pass" not in bench.merge_serving([([5.0], 1.0)], 50_000.0, 1)
+
+
+def test_ring_thread_cores_split_the_host_between_ranks():
+    # the throughput leg's host threads: distinct cores, half of each rank's share, at most 8
+    allowed = list(range(16))
+    one = bench.ring_thread_cores(allowed, 0, 1, 0)
+    assert len(one) == 8 and len(set(one)) == 8 and set(one) <= set(allowed)
+    for world in (2, 4, 8):
+        per = [bench.ring_thread_cores(allowed, r, world, r) for r in range(world)]
+        assert all(len(c) == max(1, 16 // world // 2) for c in per)
+        flat = [c for cs in per for c in cs]
+        assert len(set(flat)) == len(flat) and set(flat) <= set(allowed)
+    assert bench.ring_thread_cores([3], 0, 1, 0) == [3]
+    assert len(bench.ring_thread_cores(list(range(64)), 0, 1, 0)) == bench.RING_ENGINES_MAX
