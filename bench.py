@@ -698,15 +698,15 @@ def main():
         eng.stop()
         return t1 - t0, np.concatenate(lat_all), relaunches
 
-    def ring_loop():
-        """K timed steps in which each of E = len(ring_cores) engines on this GPU serves R
+    def ring_loop(cores, with_trace):
+        """K timed steps in which each of E = len(cores) engines on this GPU serves R
         requests with its RING_SLOTS-slot ring kept full (MICRO_BATCH), each engine driven by its
         own host thread (ctypes releases the GIL for the C loop); returns (seconds, post-to-reply
         latencies, relaunches, requests per pass, pass trace of engine 0, engines)."""
         o = opts(1)
         o.ring_slots, o.micro_batch = RING_SLOTS, MICRO_BATCH
         o.kernel_variant = ll.VARIANT_PIPELINED_RING
-        n_eng = len(ring_cores)
+        n_eng = len(cores)
         engs = [ll.Engine(net, Ws, bs, device=dev, opts=o) for _ in range(n_eng)]
         lats = [[] for _ in range(n_eng)]
         errors = []
@@ -714,7 +714,7 @@ def main():
 
         def drive(i):
             try:
-                os.sched_setaffinity(0, {ring_cores[i]})  # this thread only
+                os.sched_setaffinity(0, {cores[i]})  # this thread only
                 engs[i].start()
                 for _ in range(W):
                     engs[i].bench_ring(xs, R, RING_SLOTS)
@@ -751,7 +751,7 @@ def main():
             for e in engs:
                 e.stop()
             infos = [e.info() for e in engs]
-            trace = ring_pass_trace(ll, torch, engs[0], xs, dev) if full else None
+            trace = ring_pass_trace(ll, torch, engs[0], xs, dev) if with_trace else None
         finally:
             for e in engs:
                 e.close()
@@ -763,8 +763,11 @@ def main():
     e2e_launches = 0
     e2e_local_s, lat_all, tb_s, lat_tb = float("nan"), np.array([float("nan")]), float("nan"), None
     ring_s, lat_ring, ring_rpp, ring_trace, n_eng = float("nan"), np.array([float("nan")]), float("nan"), None, 1
+    one_s, lat_one = float("nan"), np.array([float("nan")])
     if full:
-        ring_s, lat_ring, n, ring_rpp, ring_trace, n_eng = ring_loop()
+        one_s, lat_one, n, _, _, _ = ring_loop(ring_cores[:1], False)  # one engine, one host thread
+        e2e_launches += n
+        ring_s, lat_ring, n, ring_rpp, ring_trace, n_eng = ring_loop(ring_cores, True)
         e2e_launches += n
         e2e_local_s, lat_all, n = closed_loop(engine)
         e2e_launches += n
@@ -776,6 +779,8 @@ def main():
     s_e2e = ll.compute_stats(lat_all)
     seq_value = world * K * R / e2e_s
     ring_value = world * n_eng * K * R / host_max(ring_s)
+    one_value = world * K * R / host_max(one_s)
+    s_one = ll.compute_stats(lat_one)
     s_ring = ll.compute_stats(lat_ring)
     s_tb = ll.compute_stats(lat_tb) if lat_tb is not None else None
     tb_value = world * K * R / host_max(tb_s)
@@ -857,6 +862,9 @@ def main():
                         f"{MICRO_BATCH} waiting requests per kernel pass",
                 "engines_per_gpu": n_eng, "host_threads_per_gpu": n_eng,
                 "per_engine_value": ring_value / (world * n_eng),
+                "one_engine": {"value": one_value, "ring_latency_p50_us": s_one["p50"],
+                               "ring_latency_p99_us": s_one["p99"],
+                               "mode": "the same closed loop with one engine and one host thread per GPU"},
                 "requests_per_pass": ring_rpp,
                 "ring_pass_trace": ring_trace,
                 "ring_latency_p50_us": s_ring["p50"], "ring_latency_p99_us": s_ring["p99"],
