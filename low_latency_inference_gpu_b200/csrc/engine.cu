@@ -194,12 +194,15 @@ bool build_plan(const ll_net_desc &net, int C, const std::vector<int> &bounds, b
     size_t max_img = 0;
     for (size_t v : pr.stage_image)
         max_img = std::max(max_img, v);
-    pr.buf_floats[BUF_X] = (size_t)bmax4 * x_ld_max;
-    pr.buf_floats[BUF_A] = (size_t)bmax4 * ab_w;
-    pr.buf_floats[BUF_B] = (size_t)bmax4 * ab_w;
-    pr.buf_floats[BUF_L] = (size_t)bmax4 * l_w;
+    // activation rows: a batch-1 net's kernel has no 4-row product path, so one row is all it
+    // reads or writes (the gather buffer keeps the padded row count: its layout uses it)
+    const size_t arows = net.max_batch > 1 ? (size_t)bmax4 : 1;
+    pr.buf_floats[BUF_X] = arows * x_ld_max;
+    pr.buf_floats[BUF_A] = arows * ab_w;
+    pr.buf_floats[BUF_B] = arows * ab_w;
+    pr.buf_floats[BUF_L] = arows * l_w;
     pr.buf_floats[BUF_G] = g_f;
-    pr.buf_floats[BUF_STAGE] = (size_t)bmax4 * st_w;
+    pr.buf_floats[BUF_STAGE] = arows * st_w;
     size_t total = llh::round_up(max_img, 128);
     for (int i = 0; i < BUF_COUNT; ++i)
         total += llh::round_up(std::max<size_t>(pr.buf_floats[i], 4) * 4, 128);
@@ -624,12 +627,28 @@ int finish_setup(ll_engine *e)
     return LL_OK;
 }
 
+// The generic kernel's instantiation for a plan: by the net's weight type, and without the
+// 4-row product path for batch-1 nets.
+const void *generic_kernel_for(const Params &p)
+{
+    const bool batched = p.max_batch > 1;
+    const int wt = p.n_layers > 0 ? p.L[0].wtype : LL_W_F32;
+    if (wt == LL_W_BF16)
+        return batched ? reinterpret_cast<const void *>(&ll_resident_mlp_kernel<LL_W_BF16, true>)
+                       : reinterpret_cast<const void *>(&ll_resident_mlp_kernel<LL_W_BF16, false>);
+    if (wt == LL_W_I8)
+        return batched ? reinterpret_cast<const void *>(&ll_resident_mlp_kernel<LL_W_I8, true>)
+                       : reinterpret_cast<const void *>(&ll_resident_mlp_kernel<LL_W_I8, false>);
+    return batched ? reinterpret_cast<const void *>(&ll_resident_mlp_kernel<LL_W_F32, true>)
+                   : reinterpret_cast<const void *>(&ll_resident_mlp_kernel<LL_W_F32, false>);
+}
+
 int set_kernel_attrs(ll_engine *e)
 {
     if (e->attrs_set)
         return LL_OK;
     if (!e->kfn)
-        e->kfn = reinterpret_cast<const void *>(&ll_resident_mlp_kernel);
+        e->kfn = generic_kernel_for(e->base);
     if (e->base.smem_bytes > 0)
         LL_CUDA_TRY(cudaFuncSetAttribute(e->kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->base.smem_bytes));
     if (e->base.C > 8)

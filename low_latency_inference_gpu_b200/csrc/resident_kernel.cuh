@@ -91,6 +91,11 @@ struct UnitInfo {
 
 // dot(W[r, 0:K], in[b, 0:K]) for r < R, b < B, computed by `lpr` lanes per row
 // with a butterfly reduction; epi(b, r, value) runs on the row's first lane.
+// Batch-1 products (BB = 1) take two rows per lane where the warp has a second row
+// (r and r + the rows one pass of the CTA covers): each x piece read from shared memory
+// then serves two rows, which cuts the layer's shared-memory traffic by a quarter, and
+// the two FMA chains overlap.  Each row's sum is formed exactly as with one row per lane
+// (same K slices per lane, same FMA order, same butterfly), so results do not change.
 template <int WT, int BB, class Epi>
 __device__ __forceinline__ void rows_dot(const uint8_t *W, int R, int K, const float *in, int in_ld, int B,
                                          int lpr_log2, Epi &&epi)
@@ -102,13 +107,50 @@ __device__ __forceinline__ void rows_dot(const uint8_t *W, int R, int K, const f
     const int warp = threadIdx.x >> 5;
     const int sub = lane & (lpr - 1);
     const int rpw = 32 >> lpr_log2;  // rows per warp pass
+    const int step = (kThreads / 32) * rpw;  // rows one pass of the CTA covers
     const size_t row_bytes = (size_t)K * UnitInfo<WT>::wbytes;
     for (int b0 = 0; b0 < B; b0 += BB) {
-        for (int rb = warp * rpw; rb < R; rb += (kThreads / 32) * rpw) {
+        for (int rb = warp * rpw; rb < R;) {
             const int r = rb + (lane >> lpr_log2);
             const bool valid = r < R;
             const int rr = valid ? r : R - 1;
             const uint8_t *wrow = W + (size_t)rr * row_bytes;
+            if (BB == 1 && rb + step < R) {
+                const int r2 = r + step;
+                const bool valid2 = r2 < R;
+                const uint8_t *wrow2 = W + (size_t)(valid2 ? r2 : R - 1) * row_bytes;
+                float acc = 0.0f, acc2 = 0.0f;
+                for (int u = sub; u < U; u += lpr) {
+                    float w[E], w2[E];
+                    load_unit<WT>(wrow + (size_t)u * 16, w);
+                    load_unit<WT>(wrow2 + (size_t)u * 16, w2);
+                    const float *xr = in + (size_t)b0 * in_ld + u * E;
+#pragma unroll
+                    for (int e = 0; e < E; e += 4) {
+                        const float4 x4 = *reinterpret_cast<const float4 *>(xr + e);
+                        acc = fmaf(w[e], x4.x, acc);
+                        acc = fmaf(w[e + 1], x4.y, acc);
+                        acc = fmaf(w[e + 2], x4.z, acc);
+                        acc = fmaf(w[e + 3], x4.w, acc);
+                        acc2 = fmaf(w2[e], x4.x, acc2);
+                        acc2 = fmaf(w2[e + 1], x4.y, acc2);
+                        acc2 = fmaf(w2[e + 2], x4.z, acc2);
+                        acc2 = fmaf(w2[e + 3], x4.w, acc2);
+                    }
+                }
+                for (int off = lpr >> 1; off > 0; off >>= 1) {
+                    acc += __shfl_xor_sync(0xffffffffu, acc, off);
+                    acc2 += __shfl_xor_sync(0xffffffffu, acc2, off);
+                }
+                if (sub == 0) {
+                    if (valid)
+                        epi(b0, r, acc);
+                    if (valid2)
+                        epi(b0, r2, acc2);
+                }
+                rb += 2 * step;
+                continue;
+            }
             float acc[BB];
 #pragma unroll
             for (int bb = 0; bb < BB; ++bb)
@@ -140,30 +182,25 @@ __device__ __forceinline__ void rows_dot(const uint8_t *W, int R, int K, const f
                     if (b0 + bb < B)
                         epi(b0 + bb, r, acc[bb]);
             }
+            rb += step;
         }
     }
 }
 
-template <int BB, class Epi>
-__device__ __forceinline__ void rows_dot_any(int wtype, const uint8_t *W, int R, int K, const float *in, int in_ld,
-                                             int B, int lpr_log2, Epi &&epi)
+// One layer's products.  The kernel is instantiated per weight type and for batch-1 nets
+// without the 4-row path: every layer of a net has the same weight type, and the code a
+// request runs through stays small enough for the instruction cache.
+template <int WT, bool BATCHED, class Epi>
+__device__ __forceinline__ void layer_dot(const uint8_t *W, int R, int K, const float *in, int in_ld, int B,
+                                          int lpr_log2, Epi &&epi)
 {
-    if (wtype == LL_W_BF16)
-        rows_dot<LL_W_BF16, BB>(W, R, K, in, in_ld, B, lpr_log2, epi);
-    else if (wtype == LL_W_I8)
-        rows_dot<LL_W_I8, BB>(W, R, K, in, in_ld, B, lpr_log2, epi);
-    else
-        rows_dot<LL_W_F32, BB>(W, R, K, in, in_ld, B, lpr_log2, epi);
-}
-
-template <class Epi>
-__device__ __forceinline__ void layer_dot(int wtype, const uint8_t *W, int R, int K, const float *in, int in_ld,
-                                          int B, int lpr_log2, Epi &&epi)
-{
-    if (B == 1)
-        rows_dot_any<1>(wtype, W, R, K, in, in_ld, 1, lpr_log2, epi);
-    else
-        rows_dot_any<4>(wtype, W, R, K, in, in_ld, B, lpr_log2, epi);
+    if constexpr (BATCHED) {
+        if (B > 1) {
+            rows_dot<WT, 4>(W, R, K, in, in_ld, B, lpr_log2, epi);
+            return;
+        }
+    }
+    rows_dot<WT, 1>(W, R, K, in, in_ld, B, lpr_log2, epi);
 }
 
 struct KernelCtx {
@@ -645,6 +682,7 @@ __device__ __forceinline__ void push_rows(const KernelCtx &k, const float *stage
     }
 }
 
+template <int WT, bool BATCHED>
 __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __grid_constant__ Params pg)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -954,13 +992,13 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
             case LM_REPLICATED:
             case LM_ROWSPLIT_LOCAL: {
                 EpiRows epi{buf_ptr(k, L.out_buf), L.out_ld, bias, scale, L.act, L.round_out};
-                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                layer_dot<WT, BATCHED>(W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
                 __syncthreads();
                 break;
             }
             case LM_ROWSPLIT_ALLGATHER: {
                 EpiRows epi{stg, L.R, bias, scale, L.act, L.round_out};
-                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                layer_dot<WT, BATCHED>(W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
                 __syncthreads();
                 const bool use_a = L.out_buf == BUF_A;
                 const uint32_t bar = use_a ? bar_a : bar_b;
@@ -977,7 +1015,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
             }
             case LM_KSPLIT_GATHER: {
                 EpiRaw epi{stg, L.R};
-                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                layer_dot<WT, BATCHED>(W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
                 __syncthreads();
                 // partials -> G[rank][b][OUTp] of rank 0
                 push_rows(k, stg, L.R, nrows, buf_addr(k, BUF_G) + k.rank * (uint32_t)(p.bmax4 * L.R * 4), L.R, 0,
@@ -986,14 +1024,14 @@ __global__ void __launch_bounds__(kThreads, 1) ll_resident_mlp_kernel(const __gr
             }
             case LM_ROWSPLIT_GATHER: {
                 EpiRows epi{stg, L.R, bias, scale, L.act, 0};
-                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                layer_dot<WT, BATCHED>(W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
                 __syncthreads();
                 push_rows(k, stg, L.R, nrows, buf_addr(k, BUF_G), L.Mp, (int)k.rank * L.R, bar_g, 0, 1);
                 break;
             }
             case LM_ROWSPLIT_GLOBAL: {
                 EpiRows epi{stg, L.R, bias, scale, L.act, L.round_out};
-                layer_dot(L.wtype, W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
+                layer_dot<WT, BATCHED>(W, L.R, L.K, in, L.in_ld, nrows, L.lpr_log2, epi);
                 __syncthreads();
                 if (p.xfer_tagged) {
                     // batch 1: every value leaves as one 64-bit word {seq, fp32}; the next stage
