@@ -67,6 +67,42 @@ def test_ring_kept_full(cfg0, ring, micro):
         assert inf.passes < inf.rows
 
 
+@pytest.mark.parametrize("n_eng", [2, 4])
+def test_several_engines_on_one_gpu(cfg0, n_eng):
+    # the e2e throughput leg: several ring engines on one GPU, each kept full by its own host
+    # thread (ctypes releases the GIL); every reply equals the one-at-a-time reply
+    import threading
+
+    net, Ws, bs, xs, ref, single = cfg0
+    n = 4000
+    engs = [ll.Engine(net, Ws, bs, opts=opts(ring_slots=64, micro_batch=16)) for _ in range(n_eng)]
+    out, errors = [None] * n_eng, []
+
+    def drive(i):
+        try:
+            out[i] = engs[i].bench_ring(xs[i:] if i else xs, n, 64, keep_outputs=True)[2]
+        except Exception as ex:  # noqa: BLE001 - reported below
+            errors.append(repr(ex))
+
+    try:
+        threads = [threading.Thread(target=drive, args=(i,)) for i in range(n_eng)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join(120)
+        assert not errors, errors
+        for e in engs:
+            e.stop()
+            assert e.info().status == ll.LL_OK
+    finally:
+        for e in engs:
+            e.close()
+    for i in range(n_eng):
+        rows = i + np.arange(n) % (xs.shape[0] - i) if i else np.arange(n) % xs.shape[0]
+        assert np.array_equal(out[i], single[rows])
+        assert rel_err(out[i], ref[rows]) <= 1e-5
+
+
 def test_bursts_are_taken_several_requests_per_pass(cfg0):
     net, Ws, bs, xs, ref, single = cfg0
     with ll.Engine(net, Ws, bs, opts=opts(ring_slots=32, micro_batch=16)) as e:
