@@ -368,6 +368,8 @@ PROFILE_CASES = {
     "bf16-gelu-256x1024x4x64-32rows": (2, 32, {}),
     "int8-1024x2048x6x256-256rows": (3, 256, {}),
     "int8-1024x2048x6x256-2048rows": (3, 2048, {}),
+    # the same with the weights-in-TMEM tiles on SM pairs (2-SM MMA)
+    "int8-1024x2048x6x256-2048rows-pairs": (3, 2048, {"sm_pairs": 1}),
     # the resident small-batch engine (kernel variant 3): two device queues of 200 requests,
     # one launch each (the first warms up)
     "resident-bf16-gelu-256x1024x4x64-1row": (2, 1, {"resident": True}),

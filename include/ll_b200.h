@@ -361,7 +361,13 @@ typedef struct {
                             on first use (default; recaptured when the pointers or the row count
                             change), so the host enqueues one graph instead of one launch per layer;
                             0 = launch every layer from the host */
-    int32_t reserved[3];
+    int32_t sm_pairs;    /* kernel 2 tiles on SM pairs: 1 = a layer with an even number of 128-channel
+                            tiles runs them as 256-channel tiles of two CTAs, one 2-SM MMA
+                            (cta_group::2) reading each CTA's weights from its tensor memory and each
+                            CTA's half of the rows from its shared memory, so the rows cross the
+                            L2-to-SM crossbar once per pair (measured: 40 % fewer bytes, 3 % slower
+                            on stacked config 3); 0 = one CTA per 128-channel tile (default) */
+    int32_t reserved[2];
 } ll_batched_opts;
 typedef struct {
     int32_t n_layers;

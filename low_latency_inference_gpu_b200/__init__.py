@@ -129,7 +129,7 @@ class Plan(ctypes.Structure):
 class BatchedOpts(ctypes.Structure):
     _fields_ = [("bn", ctypes.c_int32), ("splits", ctypes.c_int32), ("pdl", ctypes.c_int32),
                 ("kernel", ctypes.c_int32), ("wait_ns", ctypes.c_uint64), ("graph", ctypes.c_int32),
-                ("reserved", ctypes.c_int32 * 3)]
+                ("sm_pairs", ctypes.c_int32), ("reserved", ctypes.c_int32 * 2)]
 
 
 class BatchedInfo(ctypes.Structure):
@@ -666,10 +666,11 @@ KERNEL_SPLITK, KERNEL_WEIGHTS_IN_TMEM, KERNEL_GEMV = 1, 2, 3
 
 
 def batched_opts(bn: int = 0, splits: int = 0, pdl: int = 1, wait_ns: int = 0, kernel: int = 0,
-                 graph: int = 1) -> BatchedOpts:
+                 graph: int = 1, sm_pairs: int = 0) -> BatchedOpts:
     o = BatchedOpts()
     lib().ll_batched_opts_default(ctypes.byref(o))
     o.bn, o.splits, o.pdl, o.wait_ns, o.kernel, o.graph = bn, splits, pdl, wait_ns, kernel, graph
+    o.sm_pairs = sm_pairs
     return o
 
 

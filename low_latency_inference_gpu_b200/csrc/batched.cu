@@ -17,6 +17,7 @@
 #include "gemv_plan.h"
 #include "tc_layer.cuh"
 #include "tc_swap.cuh"
+#include "tc_swap2.cuh"
 
 using namespace llk;
 
@@ -31,6 +32,7 @@ constexpr int kGvPlanCtas = 148;                   // SMs assumed by the host-on
 struct LayerRun {
     int kind = kKindSplitK;
     int bn = 256, splits = 1, ctas = 0, smem = 0;
+    bool pair = false;  // weights-in-TMEM tiles on SM pairs (2-SM MMA; clusters of 2 along x)
     int K = 0, N = 0, act = 0, out_f32 = 0;
     const void *kfn = nullptr;
     const void *w = nullptr;  // device weights (weights-in-TMEM kernel)
@@ -643,9 +645,16 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
             r.bn = kSwChan;
             r.splits = 1;
             r.ctas = info.ctas[l];
-            r.smem = i8 ? TcSwapSmem<true>::ALLOC : TcSwapSmem<false>::ALLOC;
-            r.kfn = i8 ? reinterpret_cast<const void *>(&ll_tc_swap_kernel<true>)
-                       : reinterpret_cast<const void *>(&ll_tc_swap_kernel<false>);
+            r.pair = (d.out_dim / kSwChan) % 2 == 0 && opts && opts->sm_pairs > 0;
+            if (r.pair) {
+                r.smem = i8 ? TcSwap2Smem<true>::ALLOC : TcSwap2Smem<false>::ALLOC;
+                r.kfn = i8 ? reinterpret_cast<const void *>(&ll_tc_swap2_kernel<true>)
+                           : reinterpret_cast<const void *>(&ll_tc_swap2_kernel<false>);
+            } else {
+                r.smem = i8 ? TcSwapSmem<true>::ALLOC : TcSwapSmem<false>::ALLOC;
+                r.kfn = i8 ? reinterpret_cast<const void *>(&ll_tc_swap_kernel<true>)
+                           : reinterpret_cast<const void *>(&ll_tc_swap_kernel<false>);
+            }
             LLB_TRY(cudaFuncSetAttribute(r.kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, r.smem));
         } else if (!choose_tiling(d.in_dim, d.out_dim, m->max_rows, i8, opts, r)) {
             llh::set_error("layer %d: no tile / cluster shape can be scheduled on this device", l);
@@ -653,7 +662,7 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
         }
         TcLayerParams &p = r.p;
         const bool swk = r.kind == kKindWeightsInTmem;
-        const int x_box = swk ? kSwRows : kTcRows;
+        const int x_box = swk ? (r.pair ? kSw2Half : kSwRows) : kTcRows;
         // weights: bf16 128-byte swizzled (the MMA operand layout, or conflict-free row reads);
         // int8 unswizzled for the split-K converters, 64-byte swizzled for the row reads of
         // the weights-in-TMEM converters
@@ -664,9 +673,13 @@ int ll_batched_mlp_create(const ll_net_desc *net, const void *const *W, const fl
             swk ? make_map_grouped(&p.tm_w, wt, i8 ? 1 : 2, m->d_w[l], d.in_dim, d.out_dim, r.bn,
                                    i8 ? sw_wgroup<true>() : sw_wgroup<false>(), wsw)
                 : make_map(&p.tm_w, wt, i8 ? 1 : 2, m->d_w[l], d.in_dim, d.out_dim, r.bn, wsw);
-        if (!make_map(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->act[l & 1], d.in_dim, m->rows_pad, x_box,
-                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !wmap_ok) {
+        // SM pairs load kSw2XG K blocks of their half of the rows per tensor load (a 3-D view of X)
+        const bool xmap_ok =
+            r.pair ? make_map_grouped(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->act[l & 1], d.in_dim,
+                                      m->rows_pad, x_box, kSw2XG, CU_TENSOR_MAP_SWIZZLE_128B)
+                   : make_map(&p.tm_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->act[l & 1], d.in_dim, m->rows_pad, x_box,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+        if (!xmap_ok || !wmap_ok) {
             llh::set_error("layer %d: tensor map encoding failed", l);
             return fail(LL_ERR_CUDA);
         }
@@ -811,7 +824,7 @@ int enqueue_tc(ll_batched_mlp *m, const float *d_x, float *d_y, int n_rows, cuda
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = m->pdl ? 1 : 0;
         attr[1].id = cudaLaunchAttributeClusterDimension;  // the K splits of a tile form one cluster
-        attr[1].val.clusterDim.x = 1;
+        attr[1].val.clusterDim.x = r.pair ? 2u : 1u;       // an SM pair shares one 256-channel tile
         attr[1].val.clusterDim.y = 1;
         attr[1].val.clusterDim.z = (unsigned)r.splits;
         cfg.attrs = attr;

@@ -70,6 +70,14 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar)
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
+// The same arrival with release at CTA scope: for a signal that only says "done reading" (the
+// reads it follows have returned their values) or that guards this CTA's own shared memory.
+// Measured on B200: the cluster-scope release holds the arriving thread ~0.5 us.
+__device__ __forceinline__ void mbar_arrive_remote_cta(uint32_t cluster_bar)
+{
+    asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
 {
     uint32_t ok;

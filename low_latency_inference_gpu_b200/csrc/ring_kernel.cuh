@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             }
             __syncthreads();
             if (tid == 0)
-                mbar_arrive_remote(mapa(bar(4 + b), (uint32_t)IO));  // xfree[b]
+                mbar_arrive_remote_cta(mapa(bar(4 + b), (uint32_t)IO));  // xfree[b]: x buffer b read
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 10);
             const int gr = nb == 1 ? 1 : kFast3Group;
@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                         mrows[g] = c == kCmdExit ? 0u : (uint32_t)got;
                         mbase[g] = n_done;
                         trace(k, n_done, 0);
-                        mbar_arrive_remote(mapa(posted_bar(g), (uint32_t)IO));  // (release, cluster scope)
+                        mbar_arrive_remote_cta(mapa(posted_bar(g), (uint32_t)IO));  // this CTA's own barrier
                     }
                 }
                 if (read_warps > 1)
@@ -422,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             asm volatile("bar.sync 3, %0;" ::"r"(kRingGatherThreads) : "memory");  // every row of the pass written
             if (gt == 0) {
                 trace(k, base, 13);
-                mbar_arrive_remote(mapa(gfree(g), (uint32_t)IO));
+                mbar_arrive_remote_cta(mapa(gfree(g), (uint32_t)IO));  // this CTA's own barrier
             }
             last_replied = mseq[g][nb - 1];
             ++passes_done;

@@ -22,10 +22,11 @@ namespace llk {
 
 constexpr int kSwRows = 256;      // rows per tile (MMA N)
 constexpr int kSwChan = 128;      // channels per tile (MMA M)
-constexpr int kSwThreads = 256;
+constexpr int kSwConvGroups = 2;  // converter warp groups: group g converts the K steps kb = g mod 2
+constexpr int kSwThreads = 128 + 128 * kSwConvGroups;
 constexpr int kSwXStages = 4;     // X ring in shared memory (32 KB each)
-constexpr int kSwAStages = 4;     // weight stages in TMEM (32 columns each)
-constexpr uint32_t kSwTmemCols = 512;  // D: columns [0, 256); A stages: [256, 384)
+constexpr int kSwAStages = 8;     // weight stages in TMEM (32 columns each)
+constexpr uint32_t kSwTmemCols = 512;  // D: columns [0, 256); A stages: [256, 512)
 
 // An SM's TMA engine completes roughly one box per ~400-600 cycles almost whatever its size
 // (up to 32 KB), so a K step's 8 KB int8 weight tile as its own box cost as much as the 32 KB
@@ -142,7 +143,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
         }
         for (int s = 0; s < WS; ++s) {
             mbar_init(b_wfull(s), 1);
-            mbar_init(b_wempty(s), 4);  // one arrive per converter warp
+            mbar_init(b_wempty(s), 4 * kSwConvGroups);  // each converter warp, after its last K block of the stage
         }
         for (int s = 0; s < kSwAStages; ++s) {
             mbar_init(b_afull(s), 4);  // one arrive per converter warp
@@ -167,7 +168,9 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     const uint32_t tmem = misc[0];
     griddep_launch_dependents();
 
-    const bool conv = warp >= 4;
+    const bool conv = warp >= 4;               // converters: warps 4.. in groups of 4
+    const int cgrp = conv ? (warp - 4) >> 2 : 0;  // converter group (its K steps: kb = cgrp mod kSwConvGroups)
+    const bool epi = warp >= 4 && warp < 8;      // epilogue: the first converter group
     const int q = warp & 3;
     const int chan = 32 * q + lane;  // this thread's TMEM lane = output channel within the tile
     if (warp == 3) {
@@ -183,7 +186,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
                 tma_load_3d(sbase + L::OFF_W + s * L::WSB, &p.tm_w, 0, n0, g * L::WG, b_wfull(s));
             }
         }
-    } else if (conv && q == 0) {
+    } else if (epi && q == 0) {
         // biases and scales do not depend on the previous layer either
         for (int i = lane; i < kSwChan; i += 32) {
             s_bias[i] = __ldg(p.bias + n0 + i);
@@ -239,12 +242,13 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
         }
     } else if (conv) {
         // ---------------- weights: shared memory -> registers -> bf16 -> TMEM (lanes of quarter q) ----------------
-        for (int kb = 0; kb < nk; ++kb) {
+        for (int kb = cgrp; kb < nk; kb += kSwConvGroups) {
             const int sa = kb % kSwAStages, g = kb / L::WG, sub = kb - g * L::WG, sw = g % WS;
             if (kb >= kSwAStages &&
                 !tc_wait_warp(b_aempty(sa), ((kb / kSwAStages) - 1) & 1, p.wait_ns, fail, p.status, 3))
                 break;
-            if (sub == 0 && !tc_wait_warp(b_wfull(sw), (g / WS) & 1, p.wait_ns, fail, p.status, 3))
+            // this group's first K block of the stage: wait for the stage
+            if (sub < kSwConvGroups && !tc_wait_warp(b_wfull(sw), (g / WS) & 1, p.wait_ns, fail, p.status, 3))
                 break;
             // this lane's channel row of K block `sub` of the stage; the TMA swizzle moved 16-byte
             // chunk j of row r to chunk j ^ (r / 2 % 4) (int8, 64-byte rows) or j ^ (r % 8) (bf16,
@@ -272,7 +276,8 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
                 }
             }
             __syncwarp();
-            if (lane == 0 && (sub == L::WG - 1 || kb == nk - 1))
+            // this group's last K block of the stage: the stage is read as far as this warp goes
+            if (lane == 0 && (sub + kSwConvGroups >= L::WG || kb + kSwConvGroups >= nk))
                 mbar_arrive_local(b_wempty(sw));  // the stage is read: the producer may refill it
             tc_st_32cols(tmem + ((uint32_t)(32 * q) << 16) + 256u + (uint32_t)sa * 32u, o);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -286,7 +291,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     }
 
     // ---------------- epilogue: warps 4..7, lane = channel, columns = rows ----------------
-    if (conv) {
+    if (epi) {
         tc_wait_warp(b_accf, 0, p.wait_ns, fail, p.status, 4);
         tc_fence_after();
         if (tid == 128)
@@ -294,7 +299,7 @@ __global__ void __launch_bounds__(kSwThreads, 1) ll_tc_swap_kernel(const __grid_
     }
     __syncthreads();  // every role is done; bias and scale are in shared memory
     const bool go = *fail == 0u;
-    if (conv && go) {
+    if (epi && go) {
         // The accumulator holds a channel per lane and a row per column; Y is row-major.
         // Stage the tile row-major in the X ring (idle: every MMA has completed), then
         // write whole rows with 16-byte stores.  (Storing straight from the lanes gives

@@ -220,6 +220,25 @@ def test_weights_in_tmem_tiles_small_net(wtype):
     assert np.array_equal(y300, y[:300])
 
 
+@pytest.mark.parametrize("wtype", [ll.W_BF16, ll.W_I8])
+def test_weights_in_tmem_tiles_on_sm_pairs(wtype):
+    # 256 -> 512 -> 256 over 512 rows: both layers have an even number of 128-channel tiles, so
+    # the weights-in-TMEM tiles run on SM pairs (one 2-SM MMA per 256-channel tile); the same
+    # net with one CTA per tile is the comparison
+    net = ll.mlp([256, 512, 256], ll.ACT_RELU, ll.ACT_IDENTITY, wtype, 512)
+    Ws, bs = params(net, 23)
+    xs = ll.fill_uniform(512 * 256, -1.0, 1.0, 24).reshape(512, 256)
+    with make(net, Ws, bs, kernel=2, sm_pairs=1) as m:
+        y = run_device(m, xs)
+        y300 = run_device(m, xs[:300])
+    with make(net, Ws, bs, kernel=2) as m1:
+        y1 = run_device(m1, xs)
+    ref = oracle_out(net, Ws, bs, xs)
+    assert close(y, ref, TOL[wtype]) and close(y1, ref, TOL[wtype])
+    assert np.array_equal(y300, y[:300])
+    assert np.array_equal(y, y1)  # the same MMA sums, K step by K step (measured bit-identical)
+
+
 def test_config3_stacked_batches_auto():
     net = ll.config_net(3, 2048)
     Ws, bs = ll.config_params(3)[1:]
