@@ -268,6 +268,13 @@ int ll_engine_bench_closed_loop(ll_engine *e, const float *xs, int n_x, int n_re
  */
 int ll_engine_bench_ring(ll_engine *e, const float *xs, int n_x, int n_req, int depth, float *ys, double *lat_us,
                          double *elapsed_s);
+/* The same closed loop on two host threads: a poster thread (pinned to poster_cpu when
+ * >= 0) writes each request into its slot as soon as one of `depth` slots is free, while
+ * the calling thread collects the replies in order; sequence numbers and slots follow the
+ * same rule as ll_engine_bench_ring.  Needs the kernel to stay up during the run (a relaunch
+ * in the middle is reported as a timeout). */
+int ll_engine_bench_ring_mt(ll_engine *e, const float *xs, int n_x, int n_req, int depth, float *ys, double *lat_us,
+                            double *elapsed_s, int poster_cpu);
 
 /*
  * Device-resident queue: runs n_req sequential requests whose inputs d_x

@@ -57,7 +57,7 @@ EXPORTED_SYMBOLS = [
     "ll_batched_mlp_check", "ll_batched_mlp_infer", "ll_batched_mlp_info", "ll_batched_mlp_destroy",
     "ll_batched_mlp_set_trace", "ll_engine_serve_poisson",
     "ll_weights_save", "ll_weights_load", "ll_weights_net", "ll_weights_arrays", "ll_weights_free",
-    "ll_submit_many", "ll_engine_bench_ring",
+    "ll_submit_many", "ll_engine_bench_ring", "ll_engine_bench_ring_mt",
 ]
 MAX_LAYERS = 24
 
@@ -220,6 +220,8 @@ def _sig(lib):
                                                    ctypes.POINTER(ctypes.c_int)]),
         "ll_submit_many": (ctypes.c_int, [_vp, _fp, ctypes.c_int, P(ctypes.c_uint32)]),
         "ll_engine_bench_ring": (ctypes.c_int, [_vp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _fp, _dp, _dp]),
+        "ll_engine_bench_ring_mt": (ctypes.c_int, [_vp, _fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _fp, _dp, _dp,
+                                                    ctypes.c_int]),
     }
     for name, (res, args) in s.items():
         f = getattr(lib, name)
@@ -505,6 +507,19 @@ class Engine:
         el = ctypes.c_double()
         _check(lib().ll_engine_bench_ring(self.h, _f(xs), xs.shape[0], n_req, depth,
                                           _f(ys) if keep_outputs else None, _d(lat), ctypes.byref(el)))
+        return lat[:n_req].copy(), el.value, (ys[:n_req].copy() if keep_outputs else None)
+
+    def bench_ring_mt(self, xs: np.ndarray, n_req: int, depth: int, poster_cpu: int = -1,
+                      keep_outputs: bool = False):
+        """bench_ring on two host threads (ll_engine_bench_ring_mt): a poster thread (pinned to
+        poster_cpu when >= 0) and the calling thread collecting replies."""
+        xs = np.ascontiguousarray(xs, np.float32).reshape(-1, self.in_dim)
+        lat = np.empty(max(1, n_req), np.float64)
+        ys = np.empty((max(1, n_req), self.out_dim), np.float32) if keep_outputs else None
+        el = ctypes.c_double()
+        _check(lib().ll_engine_bench_ring_mt(self.h, _f(xs), xs.shape[0], n_req, depth,
+                                             _f(ys) if keep_outputs else None, _d(lat), ctypes.byref(el),
+                                             int(poster_cpu)))
         return lat[:n_req].copy(), el.value, (ys[:n_req].copy() if keep_outputs else None)
 
     def run_queue(self, d_x_ptr: int, d_y_ptr: int, n_req: int, n_rows: int = 1, d_stamps_ptr: int = 0) -> float:

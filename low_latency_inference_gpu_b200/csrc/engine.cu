@@ -4,6 +4,8 @@
 
 #include <algorithm>
 #include <atomic>
+#include <pthread.h>
+#include <sched.h>
 #include <chrono>
 #include <cstring>
 #include <deque>
@@ -1722,6 +1724,116 @@ int ll_engine_bench_ring(ll_engine *e, const float *xs, int n_x, int n_req, int 
     if (elapsed_s)
         *elapsed_s = std::chrono::duration<double>(clk::now() - t0).count();
     return LL_OK;
+}
+
+int ll_engine_bench_ring_mt(ll_engine *e, const float *xs, int n_x, int n_req, int depth, float *ys, double *lat_us,
+                            double *elapsed_s, int poster_cpu)
+{
+    if (!e || !xs || n_x < 1 || n_req < 1 || depth < 1 || e->max_batch != 1 || e->opts.mailbox_format != 1 ||
+        depth > e->ring) {
+        llh::set_error("ll_engine_bench_ring_mt: invalid arguments (needs the tagged mailbox, 1 <= depth <= ring_slots)");
+        return LL_ERR_INVALID_ARG;
+    }
+    if (!e->inflight.empty()) {
+        llh::set_error("request outstanding");
+        return LL_ERR_BUSY;
+    }
+    int rc = ensure_running(e);
+    if (rc)
+        return rc;
+    using clk = std::chrono::steady_clock;
+    const size_t xin = (size_t)e->in_dim, yout = (size_t)e->out_dim;
+    const int yc = (e->out_dim + 2) / 3;
+    // every request's sequence number and ring slot are fixed up front (the rule engine_post
+    // follows: consecutive numbers after the last one posted or served)
+    std::vector<uint32_t> seqs((size_t)n_req);
+    uint32_t s = e->last_served > e->seq ? e->last_served : e->seq;
+    for (int k = 0; k < n_req; ++k)
+        seqs[(size_t)k] = s = ll_next_seq(s);
+    const uint64_t base = e->ring_next;
+    std::vector<int64_t> posted_at((size_t)n_req);  // steady_clock ns, written by the poster
+    std::atomic<int> posted{0}, done{0};
+    std::atomic<bool> quit{false};
+    auto *h = static_cast<ll_tick_header *>(e->mb_host);
+    auto now_ns = []() { return std::chrono::duration_cast<std::chrono::nanoseconds>(clk::now().time_since_epoch()).count(); };
+    const auto t0 = clk::now();
+    std::thread poster([&] {
+        if (poster_cpu >= 0) {
+            cpu_set_t set;
+            CPU_ZERO(&set);
+            CPU_SET(poster_cpu, &set);
+            pthread_setaffinity_np(pthread_self(), sizeof(set), &set);  // best effort
+        }
+        int k = 0;
+        while (k < n_req && !quit.load(std::memory_order_relaxed)) {
+            const int lim = std::min(n_req, done.load(std::memory_order_acquire) + depth);
+            if (k >= lim) {
+                cpu_relax();
+                continue;
+            }
+            for (; k < lim; ++k) {
+                posted_at[(size_t)k] = now_ns();
+                write_tagged_slot(e, (size_t)((base + (uint64_t)k) % (uint64_t)e->ring), xs + (size_t)(k % n_x) * xin,
+                                  seqs[(size_t)k]);
+            }
+            h->n_rows = 1;
+            __atomic_store_n(const_cast<uint32_t *>(&h->seq_in), seqs[(size_t)k - 1], __ATOMIC_RELEASE);
+            posted.store(k, std::memory_order_release);
+        }
+    });
+    std::vector<float> ybuf(yout);
+    const char *ybase = static_cast<const char *>(e->mb_host) + e->ring_ybase;
+    auto last_progress = clk::now();
+    rc = LL_OK;
+    for (int k = 0; k < n_req && rc == LL_OK; ++k) {
+        const char *yl = ybase + (size_t)((base + (uint64_t)k) % (uint64_t)e->ring) * e->ring_ystride;
+        float *y = ys ? ys + (size_t)k * yout : ybuf.data();
+        for (uint32_t spins = 0;; ++spins) {
+            bool ok = true;
+            uint32_t w[4];
+            for (int c = 0; c < yc && ok; ++c) {
+                llh::load16(yl + 16 * c, w);  // the whole chunk in one load: tag and values together
+                if (w[3] != seqs[(size_t)k]) {
+                    ok = false;
+                } else {
+                    float v[3];
+                    std::memcpy(v, w, 12);
+                    for (int j = 0; j < 3 && 3 * c + j < e->out_dim; ++j)
+                        y[3 * c + j] = v[j];
+                }
+            }
+            if (ok)
+                break;
+            cpu_relax();
+            if ((spins & 1023u) == 1023u && clk::now() - last_progress > std::chrono::seconds(2)) {
+                llh::set_error("ring bench: request seq %u not answered within 2 s (device state %u, status %u)",
+                               seqs[(size_t)k], e->ctrl_host->state, e->ctrl_host->status);
+                rc = LL_ERR_TIMEOUT;
+                break;
+            }
+        }
+        if (rc != LL_OK)
+            break;
+        const int64_t t1 = now_ns();
+        last_progress = clk::now();
+        while (posted.load(std::memory_order_acquire) <= k) {
+        }  // orders the poster's posted_at[k] before this read (the reply already implies the post)
+        if (lat_us)
+            lat_us[k] = (double)(t1 - posted_at[(size_t)k]) / 1000.0;
+        done.store(k + 1, std::memory_order_release);
+    }
+    quit.store(true, std::memory_order_relaxed);
+    poster.join();
+    // the engine's host-side position: every request posted was answered (or the run failed:
+    // the caller stops the engine)
+    const int n_posted = posted.load(std::memory_order_acquire);
+    if (n_posted > 0) {
+        e->seq = seqs[(size_t)n_posted - 1];
+        e->ring_next = base + (uint64_t)n_posted;
+    }
+    if (elapsed_s)
+        *elapsed_s = std::chrono::duration<double>(clk::now() - t0).count();
+    return rc;
 }
 
 int ll_engine_serve_poisson(ll_engine *e, const float *xs, int n_x, int n_total, double rate_per_s, uint64_t seed,

@@ -67,6 +67,24 @@ def test_ring_kept_full(cfg0, ring, micro):
         assert inf.passes < inf.rows
 
 
+@pytest.mark.parametrize("ring,micro", [(64, 16), (16, 4)])
+def test_ring_kept_full_from_two_host_threads(cfg0, ring, micro):
+    # ll_engine_bench_ring_mt: a poster thread fills the free slots while the caller collects
+    net, Ws, bs, xs, ref, single = cfg0
+    n = 20000
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=ring, micro_batch=micro)) as e:
+        lat, el, ys = e.bench_ring_mt(xs, n, ring, keep_outputs=True)
+        lat2, _, ys2 = e.bench_ring(xs, 1000, ring, keep_outputs=True)  # the engine goes on after it
+        e.stop()
+        inf = e.info()
+        assert inf.status == ll.LL_OK and inf.rows == n + 1000
+    rows = np.arange(n) % xs.shape[0]
+    assert np.array_equal(ys, single[rows])
+    assert np.array_equal(ys2, single[np.arange(1000) % xs.shape[0]])
+    assert rel_err(ys, ref[rows]) <= 1e-5
+    assert np.all(np.isfinite(lat)) and np.all(lat > 0) and el > 0
+
+
 @pytest.mark.parametrize("n_eng", [2, 4])
 def test_several_engines_on_one_gpu(cfg0, n_eng):
     # the e2e throughput leg: several ring engines on one GPU, each kept full by its own host
