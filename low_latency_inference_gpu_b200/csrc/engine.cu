@@ -394,6 +394,43 @@ std::vector<uint8_t> pack_fast3(const Fast3Entry &f, const void *const *W, const
     return img;
 }
 
+// Per-CTA image of the pipelined ring kernel: the register-resident image's format (the same
+// size, layer 3 and biases), with layers 1 and 2 blocked as ring_layers.cuh reads them:
+// thread t holds 4 layer-1 rows x the 16-byte input pieces s1, s1 + 8, ... (g1 = t / 8,
+// s1 = t % 8) and 2 local layer-2 rows x the h1 pieces lane, lane + 32, ... (one row pair per warp).
+std::vector<uint8_t> pack_ring(const Fast3Entry &f, const void *const *W, const float *const *b, size_t &stride)
+{
+    constexpr int RB1 = 4, RB2 = 2;
+    const int T = kThreads;
+    const int G1 = f.h1 / RB1, L1 = T / G1, P1 = f.in / 4 / L1, K1 = RB1 * 4 * P1;
+    const int L2 = 32, P2 = f.h1 / 4 / L2, K2 = RB2 * 4 * P2;
+    std::vector<uint8_t> img = pack_fast3(f, W, b, stride);  // layer 3 and biases as there
+    if (K1 != f.K1 || K2 != f.K2 || f.R2 != RB2 * (T / 32)) {
+        llh::set_error("ring image: the blocked layers do not fit the register-resident image");
+        return {};
+    }
+    const float *W1 = static_cast<const float *>(W[0]);
+    const float *W2 = static_cast<const float *>(W[1]);
+    for (int c = 0; c < f.C; ++c) {
+        float *o = reinterpret_cast<float *>(img.data() + (size_t)c * stride);
+        for (int t = 0; t < T; ++t) {
+            const int g1 = t / L1, s1 = t % L1;
+            for (int r = 0; r < RB1; ++r)
+                for (int p = 0; p < P1; ++p)
+                    for (int e = 0; e < 4; ++e)
+                        o[(size_t)(r * 4 * P1 + 4 * p + e) * T + t] =
+                            W1[(size_t)(RB1 * g1 + r) * f.in + 4 * (s1 + L1 * p) + e];
+            const int g2 = t / 32, s2 = t % 32;
+            for (int r = 0; r < RB2; ++r)
+                for (int p = 0; p < P2; ++p)
+                    for (int e = 0; e < 4; ++e)
+                        o[(size_t)(K1 + r * 4 * P2 + 4 * p + e) * T + t] =
+                            W2[(size_t)(c * f.R2 + RB2 * g2 + r) * f.h1 + 4 * (s2 + L2 * p) + e];
+        }
+    }
+    return img;
+}
+
 }  // namespace
 
 struct ll_engine {
@@ -1100,7 +1137,9 @@ int create_fast3(const ll_net_desc *net, const void *const *W, const float *cons
         return LL_ERR_UNSUPPORTED;
     }
     size_t stride = 0;
-    std::vector<uint8_t> img = pack_fast3(f, W, b, stride);
+    std::vector<uint8_t> img = ring ? pack_ring(f, W, b, stride) : pack_fast3(f, W, b, stride);
+    if (img.empty())
+        return LL_ERR_UNSUPPORTED;
     ll_engine *e = new ll_engine();
     e->device = device;
     e->in_dim = f.in;

@@ -335,9 +335,9 @@ __device__ __forceinline__ uint32_t ring_slot(const Params &p, uint32_t n)
 // in CTAs first .. first + peers - 1 (the same shared-memory offset in each); row 0 and the
 // header {seq, rows} complete bar_first there, rows 1.. bar_rest.  stage != 0: rows 1.. are
 // written to this CTA's shared memory at `stage` (same layout) and sent to each peer by one
-// bulk copy, so the reading warps do not wait for the pushes; warp 0's lane 0 issues the
-// copies, and the caller commits them as a bulk group and keeps `stage` unwritten until
-// they have read it.
+// bulk copy, so the reading warps do not wait for the pushes; lanes 0 .. peers - 1 of warp 0
+// issue one copy each, and the caller has those lanes commit them as bulk groups and keeps
+// `stage` unwritten until they have read it.
 struct ChunkFwd {
     uint32_t chunks, hdr, bar_first, bar_rest;
     int first, peers;
@@ -510,6 +510,8 @@ __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uin
         bad = 0;
         for (int w = 0; w < nw; ++w)
             bad |= bad_words[w];
+        if (warp == 0 && lane == 0)
+            trace(k, n, 15);  // every reading warp's loads have landed
     }
     const uint32_t stop_bit = maxb < 32 ? (1u << maxb) : 0u;
     const int nb = (bad | stop_bit) ? __ffs(bad | stop_bit) - 1 : 32;  // complete slots before the first gap
@@ -532,12 +534,16 @@ __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uin
                 asm volatile("bar.sync 2, %0;" ::"r"(32 * nw) : "memory");
             else
                 __syncwarp();
-            if (warp == 0 && lane == 0) {
+            // one copy per peer, each from its own lane of warp 0 (the issuing thread waits for
+            // the copy engine to take each one)
+            if (warp == 0 && lane < fwd->peers) {
                 const uint32_t off = 16u * (uint32_t)nxc, bytes = off * (uint32_t)(nb - 1);
-                for (int d = fwd->first; d < fwd->first + fwd->peers; ++d)
-                    bulk_s2peer(mapa(fwd->chunks + off, (uint32_t)d), fwd->stage + off, bytes,
-                                mapa(fwd->bar_rest, (uint32_t)d));
+                const int d = fwd->first + lane;
+                bulk_s2peer(mapa(fwd->chunks + off, (uint32_t)d), fwd->stage + off, bytes,
+                            mapa(fwd->bar_rest, (uint32_t)d));
             }
+            if (warp == 0 && lane == 0)
+                trace(k, n, 14);  // the copies are issued
         }
     }
 #pragma unroll

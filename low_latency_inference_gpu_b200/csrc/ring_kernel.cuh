@@ -6,8 +6,10 @@
 // and only then read the next slots.  At 16 requests per pass that is ~6 us of reading and
 // forwarding plus ~8 us of layers.  Here a cluster of C + 1 CTAs splits the roles, so the
 // I/O of one pass overlaps the layers of the previous one:
-//   ranks 0..C-1  compute CTAs: the same register-held weight slices, layer code and FMA
-//                 order as the register-resident kernel (every reply bit-identical to it);
+//   ranks 0..C-1  compute CTAs: the register-resident kernel's weights, held in registers
+//                 blocked for many rows per pass (ring_layers.cuh: each input value read from
+//                 shared memory serves 4 or 2 output rows); a request's reply is the same
+//                 bit for bit whatever the size of its pass;
 //                 x arrives in one of two chunk buffers (by pass parity), the CTA unpacks it,
 //                 tells the I/O CTA the buffer is free, runs the layers and sends its
 //                 layer-3 partials into the I/O CTA's gather buffer of that parity;
@@ -38,6 +40,7 @@
 // (src/bench_persistent_mbyv_mlp.cu:229-381).
 #pragma once
 #include "fast3_kernel.cuh"
+#include "ring_layers.cuh"
 
 namespace llk {
 
@@ -46,7 +49,6 @@ constexpr int kRingGatherWarp0 = 8;  // I/O CTA warps 8..15
 constexpr int kRingRowsPerReadWarp = 2;  // slots one reading warp takes of a multi-slot read
 constexpr int kRingGathBufs = 3;  // gather buffers: the reader may run NG - 1 passes ahead of the replies
 constexpr int kRingGatherThreads = kThreads - 32 * kRingGatherWarp0;
-constexpr bool kRingPacked = true;  // layers 1-2 with packed fp32 FMAs (the same rounding as scalar ones)
 
 // A warp waits for an mbarrier phase.  Lane 0 watches the clock and, when `abortable`, the
 // abort flags.  Returns 1 when the phase completed, 0 on abort, -1 when the bound ran out;
@@ -78,7 +80,10 @@ __device__ __forceinline__ int warp_wait_bar(const KernelCtx &k, uint32_t bar, u
 template <int IN, int H1, int H2, int OUT, int C>
 __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_constant__ Params pg)
 {
-    using S = Fast3Shape<IN, H1, H2, OUT, C>;
+    using S = Fast3Shape<IN, H1, H2, OUT, C>;    // layer 3 and the buffer shapes
+    using RS = RingShape<IN, H1, H2, OUT, C>;    // the blocked weights of layers 1 and 2
+    static_assert(RS::NW == S::NW && RS::NB == S::NB && RS::R2 == S::R2 && RS::K3 == S::K3,
+                  "the ring image has the register-resident image's size and layer-3 slice");
     constexpr int MB = kFast3Rows;
     static_assert(S::MaxRows == kFast3Rows, "the shape leaves no room for multi-row passes");
     constexpr int NXC = (IN + 2) / 3;          // tagged chunks per row
@@ -156,17 +161,17 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     // weights into registers (compute CTAs; the I/O CTA holds none), biases into shared memory
     // (the I/O CTA takes CTA 0's copy: it needs the layer-3 biases)
     const float *img = reinterpret_cast<const float *>(p.image + (size_t)(io ? 0u : k.rank) * p.image_stride);
-    float w1[S::K1], w2[S::K2], w3[S::K3];
+    float w1[RS::K1], w2[RS::K2], w3[S::K3];
     if (!io) {
 #pragma unroll
-        for (int j = 0; j < S::K1; ++j)
+        for (int j = 0; j < RS::K1; ++j)
             w1[j] = ld_once_f32(img + (size_t)j * kThreads + tid);
 #pragma unroll
-        for (int j = 0; j < S::K2; ++j)
-            w2[j] = ld_once_f32(img + (size_t)(S::K1 + j) * kThreads + tid);
+        for (int j = 0; j < RS::K2; ++j)
+            w2[j] = ld_once_f32(img + (size_t)(RS::K1 + j) * kThreads + tid);
 #pragma unroll
         for (int j = 0; j < S::K3; ++j)
-            w3[j] = ld_once_f32(img + (size_t)(S::K1 + S::K2 + j) * kThreads + tid);
+            w3[j] = ld_once_f32(img + (size_t)(RS::K1 + RS::K2 + j) * kThreads + tid);
     }
     for (int i = tid; i < S::NB; i += kThreads)
         bias[i] = __ldg(img + (size_t)S::NW * kThreads + i);
@@ -183,8 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     uint32_t passes_done = 0, rows_done = 0, last_replied = 0;
     if (!io) {
         // ======================= compute CTA =======================
-        const int r1 = tid / S::S1, s1 = tid % S::S1;
-        const int r2 = tid / S::S2, s2 = tid % S::S2;
+        const int g1 = tid / RS::L1, s1 = tid % RS::L1;  // layer-1 row group and K slice
+        const int g2 = warp;                              // layer-2 row group
         float *xs = reinterpret_cast<float *>(pool + OFF_XS);
         float *h1 = reinterpret_cast<float *>(pool + OFF_H1);
         float *h2 = reinterpret_cast<float *>(pool + OFF_H2);
@@ -234,23 +239,19 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 mbar_arrive_remote_cta(mapa(bar(4 + b), (uint32_t)IO));  // xfree[b]: x buffer b read
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 10);
-            const int gr = nb == 1 ? 1 : kFast3Group;
-            const int ng = (int)(nb + (uint32_t)gr - 1) / gr;
+            // layers 1 and 2 with the blocked weights (ring_layers.cuh): one row, or up to 16 at
+            // once (the rows past nb compute on stale inputs inside the buffers and are never sent)
             if (nb == 1)
-                f3_layer1<S, 1, IN, H1, kRingPacked>(w1, xs, h1, bias, 1, r1, s1, act1);
+                ring_layer1_x1<RS, IN, H1>(w1, xs, h1, bias, g1, s1, act1);
             else
-                f3_layer1<S, kFast3Group, IN, H1, kRingPacked>(w1, xs, h1, bias, ng, r1, s1, act1);
+                ring_layer1_x16<RS, IN, H1>(w1, xs, h1, bias, g1, s1, act1, nb <= 8u ? 1 : 2);
             __syncthreads();
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 3);
-            // more than one group: all 16 rows at once with transposed reductions (the rows past
-            // nb compute on stale inputs inside the buffers and are never sent)
             if (nb == 1)
-                f3_layer2<S, 1, H1, kRingPacked>(w2, h1, h2, bias + H1, 1, r2, s2, act2);
-            else if (nb <= (uint32_t)kFast3Group)
-                f3_layer2<S, kFast3Group, H1, kRingPacked>(w2, h1, h2, bias + H1, ng, r2, s2, act2);
+                ring_layer2_x1<RS, H1>(w2, h1, h2, bias + H1, g2, act2);
             else
-                f3_layer2_x16<S, H1, false>(w2, h1, h2, bias + H1, r2, s2, act2);
+                ring_layer2_x16<RS, H1>(w2, h1, h2, bias + H1, g2, act2);
             __syncthreads();
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 4);
@@ -300,12 +301,15 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                         // on a failed wait the abort flag is (or gets) set: the gatherer leaves on it
                         // (no phase is posted here: pass p - NG may still be unfinished, and a second
                         // phase of posted[g] would look like none to the gatherer)
-                        // the bulk copies of pass p - 2 have read staging buffer b (the newest group,
-                        // pass p - 1's, may still be in flight)
-                        bulk_wait_group_read<1>();
                         sh.cmd = w == 1 ? 1u : 0u;
                         trace(k, n_done, 6);
                     }
+                }
+                if (warp == 0) {
+                    // the bulk copies of pass p - 2 (issued by lanes 0 .. C-1) have read staging
+                    // buffer b; the newest group, pass p - 1's, may still be in flight
+                    bulk_wait_group_read<1>();
+                    __syncwarp();
                 }
                 if (read_warps > 1)
                     asm volatile("bar.sync 2, %0;" ::"r"(32 * read_warps) : "memory");
@@ -332,11 +336,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                                         &fwd);
                         got = 1;
                     }
+                    // this pass's bulk copies, one group per issuing lane (an empty group for a
+                    // single row), so that the wait above, two passes on, covers exactly pass p - 2
+                    bulk_commit_group();
                     __syncwarp();  // the lanes' mseq writes come before lane 0's release below
                     if (lane == 0) {
-                        // this pass's bulk copies (none for a single row: an empty group), so
-                        // that the wait above, two passes on, covers exactly pass p - 2
-                        bulk_commit_group();
                         if (got == 1)
                             mseq[g][0] = c;
                         s_backlog[(pass + 1u) & 1u] =
@@ -358,7 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 n_done += rows;
             }
             // no bulk copy into a compute CTA may be in flight when the cluster leaves
-            if (warp == 0 && lane == 0)
+            if (warp == 0)
                 bulk_wait_group_all();
         }
     } else {
