@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_fast3_kernel(const __grid_cons
                     // The polling lanes forward the raw chunks to the peers from registers as
                     // soon as the tags match (header {seq, rows} + row 0 on the peers' request
                     // barrier, rows 1.. on their x barrier).
-                    const ChunkFwd fwd{smem_u32(xch), h_addr, bar_req, bar_x, 1, C - 1, 0u};
+                    const ChunkFwd fwd{smem_u32(xch), h_addr, bar_req, bar_x, 1, C - 1, 0};
                     uint32_t c = 0, posted = 0;
                     int got = 0;
                     if constexpr (MB > 1) {

@@ -333,22 +333,19 @@ __device__ __forceinline__ uint32_t ring_slot(const Params &p, uint32_t n)
 // (mapa).
 // Where the chunks of a multi-row read go: chunk `ch` of row r lands at chunks + 16 (r nxc + ch)
 // in CTAs first .. first + peers - 1 (the same shared-memory offset in each); row 0 and the
-// header {seq, rows} complete bar_first there, rows 1.. bar_rest.  stage != 0: rows 1.. are
-// written to this CTA's shared memory at `stage` (same layout) and sent to each peer by one
-// bulk copy, so the reading warps do not wait for the pushes; lanes 0 .. peers - 1 of warp 0
-// issue one copy each, and the caller has those lanes commit them as bulk groups and keeps
-// `stage` unwritten until they have read it.
+// header {seq, rows} complete bar_first there, rows 1.. bar_rest (row0_rest != 0: the header
+// alone completes bar_first, every row bar_rest).
 struct ChunkFwd {
     uint32_t chunks, hdr, bar_first, bar_rest;
     int first, peers;
-    uint32_t stage;
+    int row0_rest;
 };
 
 __device__ __forceinline__ void fwd_chunk(const ChunkFwd &f, int row, int ch, int nxc, uint4 c)
 {
     const float4 v = make_float4(__uint_as_float(c.x), __uint_as_float(c.y), __uint_as_float(c.z), __uint_as_float(c.w));
     const uint32_t a = f.chunks + 16u * (uint32_t)(row * nxc + ch);
-    const uint32_t b = row == 0 ? f.bar_first : f.bar_rest;
+    const uint32_t b = (row == 0 && !f.row0_rest) ? f.bar_first : f.bar_rest;
     for (int d = f.first; d < f.first + f.peers; ++d)
         st_async_v4(mapa(a, (uint32_t)d), v, mapa(b, (uint32_t)d));
 }
@@ -510,41 +507,16 @@ __device__ int take_tagged_rows(const KernelCtx &k, uint32_t last, float *X, uin
         bad = 0;
         for (int w = 0; w < nw; ++w)
             bad |= bad_words[w];
-        if (warp == 0 && lane == 0)
-            trace(k, n, 15);  // every reading warp's loads have landed
     }
     const uint32_t stop_bit = maxb < 32 ? (1u << maxb) : 0u;
     const int nb = (bad | stop_bit) ? __ffs(bad | stop_bit) - 1 : 32;  // complete slots before the first gap
     if (fwd && nb > 0) {
-        const bool staged = fwd->stage != 0u;
 #pragma unroll
         for (int j = 0; j < kTagChunksPerLane; ++j)
-            if (lane + 32 * j < total && row[j] < nb) {
-                if (staged && row[j] > 0)
-                    st_shared_v4(fwd->stage + 16u * (uint32_t)(row[j] * nxc + ch[j]), c[j]);
-                else
-                    fwd_chunk(*fwd, row[j], ch[j], nxc, c[j]);
-            }
+            if (lane + 32 * j < total && row[j] < nb)
+                fwd_chunk(*fwd, row[j], ch[j], nxc, c[j]);
         if (warp == 0 && lane == 0)
             fwd_header(*fwd, seq_after(last, nb), (uint32_t)nb);
-        if (staged && nb > 1) {
-            // every reading lane's staged chunks -> visible to the bulk copies (async proxy)
-            fence_proxy_async_shared();
-            if (nw > 1)
-                asm volatile("bar.sync 2, %0;" ::"r"(32 * nw) : "memory");
-            else
-                __syncwarp();
-            // one copy per peer, each from its own lane of warp 0 (the issuing thread waits for
-            // the copy engine to take each one)
-            if (warp == 0 && lane < fwd->peers) {
-                const uint32_t off = 16u * (uint32_t)nxc, bytes = off * (uint32_t)(nb - 1);
-                const int d = fwd->first + lane;
-                bulk_s2peer(mapa(fwd->chunks + off, (uint32_t)d), fwd->stage + off, bytes,
-                            mapa(fwd->bar_rest, (uint32_t)d));
-            }
-            if (warp == 0 && lane == 0)
-                trace(k, n, 14);  // the copies are issued
-        }
     }
 #pragma unroll
     for (int j = 0; j < kTagChunksPerLane; ++j) {

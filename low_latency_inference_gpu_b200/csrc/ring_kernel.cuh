@@ -14,13 +14,13 @@
 //                 tells the I/O CTA the buffer is free, runs the layers and sends its
 //                 layer-3 partials into the I/O CTA's gather buffer of that parity;
 //   rank C        the I/O CTA, no weights:
-//                 warps 0..7   reader: poll the next ring slot, or read up to micro_batch
-//                              waiting slots at once, and forward their chunks to the C
-//                              compute CTAs: row 0 and the header {seq, rows} straight from
-//                              registers (the register-resident kernel's protocol), rows
-//                              1.. through a staging copy in this CTA's shared memory and
-//                              one bulk copy per compute CTA, which runs on while the
-//                              reader starts on the next pass;
+//                 warp 0       reader: poll the next ring slot (and push its chunks to the C
+//                              compute CTAs from registers, the register-resident kernel's
+//                              protocol), or read up to micro_batch waiting slots at once by
+//                              bulk copies from host memory into this CTA's shared memory and
+//                              forward them by bulk copies, one per compute CTA and part,
+//                              which run on while the reader starts on the next pass
+//                              (ring_take_rows);
 //                 warps 8..15  gatherer: add the C partials per output in rank order, apply
 //                              bias and activation, write each reply into its slot.
 // Pass p uses x chunk buffer b = p & 1 and gather buffer g = p % 3 (partials and the
@@ -46,7 +46,6 @@ namespace llk {
 
 constexpr int kRingReadWarps = 8;    // I/O CTA warps 0..7
 constexpr int kRingGatherWarp0 = 8;  // I/O CTA warps 8..15
-constexpr int kRingRowsPerReadWarp = 2;  // slots one reading warp takes of a multi-slot read
 constexpr int kRingGathBufs = 3;  // gather buffers: the reader may run NG - 1 passes ahead of the replies
 constexpr int kRingGatherThreads = kThreads - 32 * kRingGatherWarp0;
 
@@ -75,6 +74,67 @@ __device__ __forceinline__ int warp_wait_bar(const KernelCtx &k, uint32_t bar, u
                 return verdict;
         }
     }
+}
+
+// Reader warp: take up to maxb waiting ring slots (requests n, n + 1, ...) in one read.  Lane 0
+// copies the slots from host memory into `stage` (this CTA's shared memory, slot layout kept)
+// with one or two 1-D bulk copies (TMA; two when the slots wrap around the ring), which read
+// host memory in large requests (measured on B200: 16 slots in 1.6 us against 2.6 us for 16-byte
+// loads spread over 8 warps); lane 31 reads seq_in meanwhile.  After the copies land (bounded
+// wait) the lanes check the tags; rows 0 .. nb-1 (the complete slots before the first gap) go
+// to the C compute CTAs: the header {seq, rows} by st.async completing bar_first there, the
+// rows by one bulk copy per CTA completing bar_rest (lane d serves compute CTA d).
+// Returns nb (0: request n is not complete yet), or -1 when the copies did not land in time.
+template <int NXC, int C>
+__device__ int ring_take_rows(const KernelCtx &k, uint32_t last, uint32_t n, int maxb, uint32_t *seqs,
+                              uint32_t *posted, const uint4 *stage_p, uint32_t stage, uint32_t rbar, uint32_t rpar,
+                              uint32_t chunks, uint32_t hdr, uint32_t bar_first, uint32_t bar_rest)
+{
+    const Params &p = *k.p;
+    const int lane = threadIdx.x & 31;
+    constexpr uint32_t RB = 16u * NXC;  // bytes per slot
+    if (lane == 0) {
+        const uint32_t s0 = ring_slot(p, n);
+        const int first = min(maxb, p.ring_slots - (int)s0);
+        mbar_arrive_expect_tx(rbar, RB * (uint32_t)maxb);
+        bulk_g2s(stage, p.mb_x + (size_t)s0 * p.ring_xstride_f, RB * (uint32_t)first, rbar);
+        if (first < maxb)
+            bulk_g2s(stage + RB * (uint32_t)first, p.mb_x, RB * (uint32_t)(maxb - first), rbar);
+    }
+    const uint32_t seen = lane == 31 ? ld_relaxed_sys(&p.mb->seq_in) : 0u;
+    *posted = __shfl_sync(0xffffffffu, seen, 31);
+    if (warp_wait_bar(k, rbar, rpar, p.step_ns, false) != 1)
+        return -1;
+    if (lane == 0)
+        trace(k, n, 11);  // the slots have landed
+    // lane r < maxb computes request r's sequence number once; chunk i of row r must carry it
+    const uint32_t want = lane < maxb ? seq_after(last, lane + 1) : 0u;
+    const uint32_t *tags = reinterpret_cast<const uint32_t *>(stage_p) + 3;  // word 3 of each chunk
+    uint32_t bad = 0;
+    for (int i0 = 0; i0 < maxb * NXC; i0 += 32) {
+        const int i = i0 + lane;
+        const int row = (i < maxb * NXC ? i : 0) / NXC;
+        const uint32_t expect = __shfl_sync(0xffffffffu, want, row);
+        if (i < maxb * NXC && tags[4 * i] != expect)
+            bad |= 1u << row;
+    }
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    const uint32_t stop_bit = maxb < 32 ? (1u << maxb) : 0u;
+    const int nb = (bad | stop_bit) ? __ffs(bad | stop_bit) - 1 : 32;
+    if (nb > 0) {
+        if (lane < C) {
+            const uint32_t d = (uint32_t)lane;
+            st_async_v4(mapa(hdr, d),
+                        make_float4(__uint_as_float(seq_after(last, nb)), __uint_as_float((uint32_t)nb), 0.f, 0.f),
+                        mapa(bar_first, d));
+            bulk_s2peer(mapa(chunks, d), stage, RB * (uint32_t)nb, mapa(bar_rest, d));
+        }
+        if (lane < nb)
+            seqs[lane] = seq_after(last, lane + 1);
+        if (lane == 0)
+            trace(k, n, 14);  // the copies are issued
+    }
+    return nb;
 }
 
 template <int IN, int H1, int H2, int OUT, int C>
@@ -106,11 +166,10 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     constexpr int POOL = COMPUTE_END > IO_END ? COMPUTE_END : IO_END;
     __shared__ __align__(16) uint8_t pool[POOL];
     __shared__ __align__(16) uint32_t hdr2[2][4];  // compute CTAs: {seq, rows} of the pass in buffer b
-    __shared__ __align__(8) uint64_t rb[6 + 3 * kRingGathBufs];  // see the barrier indices below
+    __shared__ __align__(8) uint64_t rb[7 + 3 * kRingGathBufs];  // see the barrier indices below
     __shared__ __align__(16) float bias[S::NB];
     __shared__ uint32_t mseq[kRingGathBufs][MB];   // I/O: sequence number of each row of the pass in buffer g
     __shared__ uint32_t mrows[kRingGathBufs], mbase[kRingGathBufs];  // I/O: rows (0 = exit), first request index
-    __shared__ uint32_t bad_words[kTagReadWarpsMax];
     __shared__ uint32_t s_backlog[2];
     __shared__ __align__(16) Shared sh;
     __shared__ __align__(16) Params sp;
@@ -130,13 +189,14 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     k.stage = 0;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool io = k.rank == (uint32_t)IO;
-    // barriers: compute CTAs 0,1 bar_req[b] (header + row 0), 2,3 bar_x[b] (rows 1..);
+    // barriers: compute CTAs 0,1 bar_req[b] (the header {seq, rows}), 2,3 bar_x[b] (the rows);
     // I/O CTA 4,5 xfree[b], then NG each of bar_g[g] (partials), gfree[g], posted[g]
     auto bar = [&](int i) { return smem_u32(&rb[i]); };
     constexpr int NG = kRingGathBufs;
     auto bar_g = [&](int g) { return bar(6 + g); };
     auto gfree = [&](int g) { return bar(6 + NG + g); };
     auto posted_bar = [&](int g) { return bar(6 + 2 * NG + g); };
+    const uint32_t rbar = bar(6 + 3 * NG);  // I/O CTA: the reader's slot copies from host memory
     const uint32_t pool_a = smem_u32(pool);
 
     if (tid == 0) {
@@ -149,6 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             mbar_init(gfree(i), 1);
             mbar_init(posted_bar(i), 1);
         }
+        mbar_init(rbar, 1);
         sh.cmd = 0;
         sh.fail = 0;
         sh.abort = 0;
@@ -200,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             const int b = (int)(pass & 1u);
             const uint32_t par = (pass >> 1) & 1u;
             if (tid == 0)
-                mbar_arrive_expect_tx(bar(b), 16u + 16u * NXC);
+                mbar_arrive_expect_tx(bar(b), 16u);  // the header {seq, rows} alone
             if (!cta_wait_bar(k, bar(b), par, EW_PEER_POLL, p.idle_ns + p.peer_margin_ns))
                 break;
             if (k.rank == 0 && tid == 0)
@@ -209,9 +270,9 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             uint32_t nb = *reinterpret_cast<volatile uint32_t *>(&hdr2[b][1]);
             nb = nb < 1u ? 1u : (nb > (uint32_t)MB ? (uint32_t)MB : nb);
             (void)seq;
-            if (nb > 1) {
+            {  // the pass's rows, every one on bar_x
                 if (tid == 0)
-                    mbar_arrive_expect_tx(bar(2 + b), 16u * NXC * (nb - 1));
+                    mbar_arrive_expect_tx(bar(2 + b), 16u * NXC * nb);
                 const uint32_t px = b ? ph_x[1] : ph_x[0];
                 if (!cta_wait_bar(k, bar(2 + b), px & 1u, EW_PEER_POLL, p.step_ns))
                     break;
@@ -272,15 +333,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
         }
     } else if (warp < kRingReadWarps) {
         // ======================= I/O CTA: reader =======================
-        // Warp 0 makes every decision and publishes it in shared memory; the other reading
-        // warps (a multi-slot read of more than 5 slots) follow through named barrier 2, so
-        // they never part ways at a barrier.
-        constexpr int RPW = tag_rows_per_warp(NXC) < kRingRowsPerReadWarp ? tag_rows_per_warp(NXC)
-                                                                           : kRingRowsPerReadWarp;
-        static_assert(RPW >= 1 && (kFast3Rows + RPW - 1) / RPW <= kRingReadWarps, "reading warps hold whole slots");
-        const int read_warps = p.micro_batch > 1 ? (p.micro_batch + RPW - 1) / RPW : 1;
+        // Warp 0 alone: a multi-slot read is one or two bulk copies from host memory
+        // (ring_take_rows); warps 1 .. kRingReadWarps - 1 have no part.
+        const int read_warps = 1;
         if (warp < read_warps) {
-            uint32_t last = p.last_seq, n_done = 0;
+            uint32_t last = p.last_seq, n_done = 0, rphase = 0;
             for (uint32_t pass = 0;; ++pass) {
                 const int b = (int)(pass & 1u), g = (int)(pass % (uint32_t)NG);
                 if (warp == 0) {
@@ -320,13 +377,24 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 // rows 1.. of a multi-slot read are staged in this CTA's stage[b] and bulk-copied
                 // to the compute CTAs' chunk buffer b
                 const uint32_t xch_b = pool_a + OFF_XCH + (uint32_t)b * XCH_B;
-                const ChunkFwd fwd{xch_b, smem_u32(&hdr2[b][0]), bar(b), bar(2 + b), 0, C,
-                                   pool_a + OFF_STG + (uint32_t)b * XCH_B};
+                const ChunkFwd fwd{xch_b, smem_u32(&hdr2[b][0]), bar(b), bar(2 + b), 0, C, 1};
                 uint32_t posted = 0;
                 int got = 0;
-                if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[pass & 1u]))
-                    got = take_tagged_rows(k, last, nullptr, n_done, p.micro_batch, mseq[g], &posted, bad_words,
-                                           read_warps, &fwd, RPW);
+                if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[pass & 1u])) {
+                    const uint32_t stg = pool_a + OFF_STG + (uint32_t)b * XCH_B;
+                    got = ring_take_rows<NXC, C>(k, last, n_done, p.micro_batch, mseq[g], &posted,
+                                                 reinterpret_cast<const uint4 *>(pool + OFF_STG + b * XCH_B), stg,
+                                                 rbar, rphase & 1u, xch_b, smem_u32(&hdr2[b][0]), bar(b), bar(2 + b));
+                    ++rphase;
+                    if (got < 0) {
+                        // the slot copies did not land: leave (the final drain waits for them)
+                        if (lane == 0) {
+                            report_error(k, LL_ERR_DEVICE_FAULT, EW_PEER_POLL);
+                            broadcast_abort(k);
+                        }
+                        got = 0;
+                    }
+                }
                 if (warp == 0) {
                     uint32_t c;
                     if (got > 0) {
