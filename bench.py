@@ -205,7 +205,7 @@ def run_config1(ll, torch, dev):
 # pipelined ring kernel: trace slot -> phase (globaltimer stamps of one pass; the reader's
 # stamp 0 is taken once the pass's slots are read and forwarded)
 RING_TRACE_PHASES = ((7, "reader_pass_start"), (6, "reader_flow_control_done"), (11, "reader_slots_landed"),
-                     (14, "reader_copies_issued"),
+                     (15, "reader_tags_checked"), (1, "reader_committed"), (14, "forwarder_copies_issued"),
                      (8, "compute_row0_arrived"), (9, "compute_rows_arrived"), (10, "compute_unpacked"),
                      (3, "compute_layer1_done"), (4, "compute_layer2_done"), (5, "compute_layer3_sent"),
                      (12, "gatherer_partials_in"), (13, "gatherer_replies_written"))

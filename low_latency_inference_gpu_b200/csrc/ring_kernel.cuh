@@ -76,19 +76,17 @@ __device__ __forceinline__ int warp_wait_bar(const KernelCtx &k, uint32_t bar, u
     }
 }
 
-// Reader warp: take up to maxb waiting ring slots (requests n, n + 1, ...) in one read.  Lane 0
+// Reader warp: read up to maxb waiting ring slots (requests n, n + 1, ...) in one go.  Lane 0
 // copies the slots from host memory into `stage` (this CTA's shared memory, slot layout kept)
 // with one or two 1-D bulk copies (TMA; two when the slots wrap around the ring), which read
 // host memory in large requests (measured on B200: 16 slots in 1.6 us against 2.6 us for 16-byte
 // loads spread over 8 warps); lane 31 reads seq_in meanwhile.  After the copies land (bounded
-// wait) the lanes check the tags; rows 0 .. nb-1 (the complete slots before the first gap) go
-// to the C compute CTAs: the header {seq, rows} by st.async completing bar_first there, the
-// rows by one bulk copy per CTA completing bar_rest (lane d serves compute CTA d).
-// Returns nb (0: request n is not complete yet), or -1 when the copies did not land in time.
-template <int NXC, int C>
+// wait) the lanes check the tags.  Returns nb, the complete slots before the first gap (0: request
+// n is not complete yet), or -1 when the copies did not land in time.  The forwarder warp sends
+// the rows on (ring_forward).
+template <int NXC>
 __device__ int ring_take_rows(const KernelCtx &k, uint32_t last, uint32_t n, int maxb, uint32_t *seqs,
-                              uint32_t *posted, const uint4 *stage_p, uint32_t stage, uint32_t rbar, uint32_t rpar,
-                              uint32_t chunks, uint32_t hdr, uint32_t bar_first, uint32_t bar_rest)
+                              uint32_t *posted, const uint4 *stage_p, uint32_t stage, uint32_t rbar, uint32_t rpar)
 {
     const Params &p = *k.p;
     const int lane = threadIdx.x & 31;
@@ -119,22 +117,31 @@ __device__ int ring_take_rows(const KernelCtx &k, uint32_t last, uint32_t n, int
             bad |= 1u << row;
     }
     bad = __reduce_or_sync(0xffffffffu, bad);
+    if (lane == 0)
+        trace(k, n, 15);  // the tags are checked
     const uint32_t stop_bit = maxb < 32 ? (1u << maxb) : 0u;
     const int nb = (bad | stop_bit) ? __ffs(bad | stop_bit) - 1 : 32;
-    if (nb > 0) {
-        if (lane < C) {
-            const uint32_t d = (uint32_t)lane;
-            st_async_v4(mapa(hdr, d),
-                        make_float4(__uint_as_float(seq_after(last, nb)), __uint_as_float((uint32_t)nb), 0.f, 0.f),
-                        mapa(bar_first, d));
-            bulk_s2peer(mapa(chunks, d), stage, RB * (uint32_t)nb, mapa(bar_rest, d));
-        }
-        if (lane < nb)
-            seqs[lane] = seq_after(last, lane + 1);
-        if (lane == 0)
-            trace(k, n, 14);  // the copies are issued
-    }
+    if (lane < nb)
+        seqs[lane] = seq_after(last, lane + 1);
     return nb;
+}
+
+// Forwarder warp: send a pass's rows from `stage` to the C compute CTAs (lane d serves CTA d):
+// the header {seq, rows} by st.async completing bar_first, the rows by one bulk copy per CTA
+// completing bar_rest.  The copies move ~25 GB/s out of the SM, so a 16-row pass takes ~2 us
+// of this warp while the reader goes on to the next pass.
+template <int NXC, int C>
+__device__ __forceinline__ void ring_forward(uint32_t seq, int nb, uint32_t stage, uint32_t chunks, uint32_t hdr,
+                                             uint32_t bar_first, uint32_t bar_rest)
+{
+    const int lane = threadIdx.x & 31;
+    constexpr uint32_t RB = 16u * NXC;
+    if (lane < C) {
+        const uint32_t d = (uint32_t)lane;
+        st_async_v4(mapa(hdr, d), make_float4(__uint_as_float(seq), __uint_as_float((uint32_t)nb), 0.f, 0.f),
+                    mapa(bar_first, d));
+        bulk_s2peer(mapa(chunks, d), stage, RB * (uint32_t)nb, mapa(bar_rest, d));
+    }
 }
 
 template <int IN, int H1, int H2, int OUT, int C>
@@ -166,7 +173,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     constexpr int POOL = COMPUTE_END > IO_END ? COMPUTE_END : IO_END;
     __shared__ __align__(16) uint8_t pool[POOL];
     __shared__ __align__(16) uint32_t hdr2[2][4];  // compute CTAs: {seq, rows} of the pass in buffer b
-    __shared__ __align__(8) uint64_t rb[7 + 3 * kRingGathBufs];  // see the barrier indices below
+    __shared__ __align__(8) uint64_t rb[11 + 3 * kRingGathBufs];  // see the barrier indices below
+    __shared__ uint32_t fq[2][4];                   // I/O: reader -> forwarder, per stage buffer: rows, seq, kind, n
     __shared__ __align__(16) float bias[S::NB];
     __shared__ uint32_t mseq[kRingGathBufs][MB];   // I/O: sequence number of each row of the pass in buffer g
     __shared__ uint32_t mrows[kRingGathBufs], mbase[kRingGathBufs];  // I/O: rows (0 = exit), first request index
@@ -197,6 +205,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     auto gfree = [&](int g) { return bar(6 + NG + g); };
     auto posted_bar = [&](int g) { return bar(6 + 2 * NG + g); };
     const uint32_t rbar = bar(6 + 3 * NG);  // I/O CTA: the reader's slot copies from host memory
+    auto fready = [&](int b) { return bar(7 + 3 * NG + b); };  // I/O CTA: stage[b] handed to the forwarder
+    auto sfree = [&](int b) { return bar(9 + 3 * NG + b); };   // I/O CTA: the forwarder is done with stage[b]
     const uint32_t pool_a = smem_u32(pool);
 
     if (tid == 0) {
@@ -210,6 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             mbar_init(posted_bar(i), 1);
         }
         mbar_init(rbar, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(fready(i), 1);
+            mbar_init(sfree(i), 1);
+        }
         sh.cmd = 0;
         sh.fail = 0;
         sh.abort = 0;
@@ -332,11 +346,34 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             n_req += nb;
         }
     } else if (warp < kRingReadWarps) {
-        // ======================= I/O CTA: reader =======================
-        // Warp 0 alone: a multi-slot read is one or two bulk copies from host memory
-        // (ring_take_rows); warps 1 .. kRingReadWarps - 1 have no part.
+        // ======================= I/O CTA: reader (warp 0) and forwarder (warp 1) =======================
+        // The reader polls or reads the slots of each pass (a multi-slot read is one or two bulk
+        // copies from host memory, ring_take_rows) and posts the pass to the gatherer; the
+        // forwarder sends a multi-slot pass's rows to the compute CTAs (ring_forward), handed
+        // over per stage buffer b through `fready[b]` and returned through `sfree[b]`.  Warps 2 ..
+        // kRingReadWarps - 1 have no part.
         const int read_warps = 1;
-        if (warp < read_warps) {
+        if (warp == 1) {
+            for (uint32_t pass = 0;; ++pass) {
+                const int b = (int)(pass & 1u);
+                // abortable: every exit of the reader comes with the abort flag set
+                if (warp_wait_bar(k, fready(b), (pass >> 1) & 1u, p.idle_ns + 2 * p.peer_margin_ns, true) != 1)
+                    break;
+                if (fq[b][2] == 1u) {
+                    ring_forward<NXC, C>(fq[b][1], (int)fq[b][0], pool_a + OFF_STG + (uint32_t)b * XCH_B,
+                                         pool_a + OFF_XCH + (uint32_t)b * XCH_B, smem_u32(&hdr2[b][0]), bar(b),
+                                         bar(2 + b));
+                    if (lane == 0)
+                        trace(k, fq[b][3], 14);  // the copies are issued
+                    bulk_commit_group();
+                    bulk_wait_group_read<0>();  // the copies have read stage[b]
+                }
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive_remote_cta(mapa(sfree(b), (uint32_t)IO));  // this CTA's own barrier
+            }
+            bulk_wait_group_all();  // no copy into a compute CTA may be in flight when the cluster leaves
+        } else if (warp < read_warps) {
             uint32_t last = p.last_seq, n_done = 0, rphase = 0;
             for (uint32_t pass = 0;; ++pass) {
                 const int b = (int)(pass & 1u), g = (int)(pass % (uint32_t)NG);
@@ -362,10 +399,15 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                         trace(k, n_done, 6);
                     }
                 }
-                if (warp == 0) {
-                    // the bulk copies of pass p - 2 (issued by lanes 0 .. C-1) have read staging
-                    // buffer b; the newest group, pass p - 1's, may still be in flight
-                    bulk_wait_group_read<1>();
+                if (warp == 0 && pass >= 2 && *reinterpret_cast<volatile uint32_t *>(&sh.cmd) != 0u) {
+                    // the forwarder is done with stage buffer b (pass p - 2)
+                    const int w = warp_wait_bar(k, sfree(b), ((pass - 2u) >> 1) & 1u, p.step_ns, true);
+                    if (lane == 0 && w != 1) {
+                        if (w < 0)
+                            report_error(k, LL_ERR_DEVICE_FAULT, EW_GATHER);
+                        broadcast_abort(k);
+                        sh.cmd = 0u;
+                    }
                     __syncwarp();
                 }
                 if (read_warps > 1)
@@ -380,12 +422,14 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 const ChunkFwd fwd{xch_b, smem_u32(&hdr2[b][0]), bar(b), bar(2 + b), 0, C, 1};
                 uint32_t posted = 0;
                 int got = 0;
+                bool staged = false;  // the pass's rows sit in stage[b] for the forwarder
                 if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[pass & 1u])) {
                     const uint32_t stg = pool_a + OFF_STG + (uint32_t)b * XCH_B;
-                    got = ring_take_rows<NXC, C>(k, last, n_done, p.micro_batch, mseq[g], &posted,
-                                                 reinterpret_cast<const uint4 *>(pool + OFF_STG + b * XCH_B), stg,
-                                                 rbar, rphase & 1u, xch_b, smem_u32(&hdr2[b][0]), bar(b), bar(2 + b));
+                    got = ring_take_rows<NXC>(k, last, n_done, p.micro_batch, mseq[g], &posted,
+                                              reinterpret_cast<const uint4 *>(pool + OFF_STG + b * XCH_B), stg, rbar,
+                                              rphase & 1u);
                     ++rphase;
+                    staged = got > 0;
                     if (got < 0) {
                         // the slot copies did not land: leave (the final drain waits for them)
                         if (lane == 0) {
@@ -404,11 +448,17 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                                         &fwd);
                         got = 1;
                     }
-                    // this pass's bulk copies, one group per issuing lane (an empty group for a
-                    // single row), so that the wait above, two passes on, covers exactly pass p - 2
-                    bulk_commit_group();
+                    bulk_commit_group();  // the slot reads (completion is awaited on rbar)
                     __syncwarp();  // the lanes' mseq writes come before lane 0's release below
                     if (lane == 0) {
+                        trace(k, n_done, 1);
+                        // hand stage[b] to the forwarder: the rows to send (a multi-slot pass), or
+                        // nothing (a polled request, pushed above from registers)
+                        fq[b][0] = (uint32_t)got;
+                        fq[b][1] = c;
+                        fq[b][2] = staged ? 1u : 0u;
+                        fq[b][3] = n_done;
+                        mbar_arrive_remote_cta(mapa(fready(b), (uint32_t)IO));  // this CTA's own barrier
                         if (got == 1)
                             mseq[g][0] = c;
                         s_backlog[(pass + 1u) & 1u] =
