@@ -431,13 +431,19 @@ __device__ uint32_t poll_tagged(const KernelCtx &k, uint32_t last, float *X, uin
     }
 }
 
-// The sequence number m requests after `last` (m >= 1).
-__device__ __forceinline__ uint32_t seq_after(uint32_t last, int m)
+// The sequence number m requests after `last` (0 <= m < 2^31): m steps of next_seq_dev in closed
+// form.  The sequence cycles through 1 .. LL_STOP_SEQ - 1 (period 2^32 - 2); 0 and LL_STOP_SEQ
+// step to 1, like LL_STOP_SEQ - 1 does.
+__host__ __device__ __forceinline__ uint32_t seq_after(uint32_t last, int m)
 {
-    uint32_t s = last;
-    for (int i = 0; i < m; ++i)
-        s = next_seq_dev(s);
-    return s;
+    constexpr uint64_t kPeriod = 0xFFFFFFFEull;
+    if (m == 0)
+        return last;
+    const uint64_t pos = (last == 0u || last == LL_STOP_SEQ) ? kPeriod - 1u : (uint64_t)last - 1u;
+    uint64_t q = pos + (uint64_t)m;
+    if (q >= kPeriod)
+        q -= kPeriod;
+    return (uint32_t)q + 1u;
 }
 
 // Rows of a tagged ring one reading warp holds in registers (whole slots: 32 lanes x

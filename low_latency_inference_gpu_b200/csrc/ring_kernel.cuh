@@ -84,7 +84,7 @@ __device__ __forceinline__ int warp_wait_bar(const KernelCtx &k, uint32_t bar, u
 // wait) the lanes check the tags.  Returns nb, the complete slots before the first gap (0: request
 // n is not complete yet), or -1 when the copies did not land in time.  The forwarder warp sends
 // the rows on (ring_forward).
-template <int NXC>
+template <int NXC, int MAXB>
 __device__ int ring_take_rows(const KernelCtx &k, uint32_t last, uint32_t n, int maxb, uint32_t *seqs,
                               uint32_t *posted, const uint4 *stage_p, uint32_t stage, uint32_t rbar, uint32_t rpar)
 {
@@ -105,15 +105,19 @@ __device__ int ring_take_rows(const KernelCtx &k, uint32_t last, uint32_t n, int
         return -1;
     if (lane == 0)
         trace(k, n, 11);  // the slots have landed
-    // lane r < maxb computes request r's sequence number once; chunk i of row r must carry it
-    const uint32_t want = lane < maxb ? seq_after(last, lane + 1) : 0u;
+    // lane r < maxb holds request r's sequence number; chunk i of row r must carry it.  The
+    // loop has a fixed trip count (MAXB rows), so its shared loads and shuffles issue back to
+    // back.
+    const uint32_t want = seq_after(last, lane + 1);
     const uint32_t *tags = reinterpret_cast<const uint32_t *>(stage_p) + 3;  // word 3 of each chunk
     uint32_t bad = 0;
-    for (int i0 = 0; i0 < maxb * NXC; i0 += 32) {
+#pragma unroll
+    for (int i0 = 0; i0 < MAXB * NXC; i0 += 32) {
         const int i = i0 + lane;
-        const int row = (i < maxb * NXC ? i : 0) / NXC;
+        const bool in = i < maxb * NXC;
+        const int row = (in ? i : 0) / NXC;
         const uint32_t expect = __shfl_sync(0xffffffffu, want, row);
-        if (i < maxb * NXC && tags[4 * i] != expect)
+        if (in && tags[4 * i] != expect)
             bad |= 1u << row;
     }
     bad = __reduce_or_sync(0xffffffffu, bad);
@@ -122,7 +126,7 @@ __device__ int ring_take_rows(const KernelCtx &k, uint32_t last, uint32_t n, int
     const uint32_t stop_bit = maxb < 32 ? (1u << maxb) : 0u;
     const int nb = (bad | stop_bit) ? __ffs(bad | stop_bit) - 1 : 32;
     if (lane < nb)
-        seqs[lane] = seq_after(last, lane + 1);
+        seqs[lane] = want;
     return nb;
 }
 
@@ -425,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 bool staged = false;  // the pass's rows sit in stage[b] for the forwarder
                 if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[pass & 1u])) {
                     const uint32_t stg = pool_a + OFF_STG + (uint32_t)b * XCH_B;
-                    got = ring_take_rows<NXC>(k, last, n_done, p.micro_batch, mseq[g], &posted,
+                    got = ring_take_rows<NXC, MB>(k, last, n_done, p.micro_batch, mseq[g], &posted,
                                               reinterpret_cast<const uint4 *>(pool + OFF_STG + b * XCH_B), stg, rbar,
                                               rphase & 1u);
                     ++rphase;
