@@ -20,6 +20,7 @@
 #include "gemv_plan.h"
 #include "resident_kernel.cuh"
 #include "ring_kernel.cuh"
+#include "deep_kernel.cuh"
 
 #if defined(__x86_64__)
 #include <immintrin.h>
@@ -426,6 +427,98 @@ std::vector<uint8_t> pack_ring(const Fast3Entry &f, const void *const *W, const 
                     for (int e = 0; e < 4; ++e)
                         o[(size_t)(K1 + r * 4 * P2 + 4 * p + e) * T + t] =
                             W2[(size_t)(c * f.R2 + RB2 * g2 + r) * f.h1 + 4 * (s2 + L2 * p) + e];
+        }
+    }
+    return img;
+}
+
+// Register-resident kernels compiled for deep nets of one hidden width (IN -> H x (NL-1) -> OUT).
+struct DeepEntry {
+    int in, h, out, nl, C, lps;
+    const void *fn;
+    int NW, NB, NS;
+};
+
+template <int IN, int H, int OUT, int NL, int C, int LPS>
+DeepEntry deep_entry()
+{
+    using D = DeepShape<IN, H, OUT, NL, C, LPS>;
+    return DeepEntry{IN, H, OUT, NL, C, LPS, reinterpret_cast<const void *>(&ll_deep_kernel<IN, H, OUT, NL, C, LPS>),
+                     D::NW, D::NB, D::NS};
+}
+
+const DeepEntry *find_deep(const ll_net_desc &net, int C)
+{
+    static const DeepEntry table[] = {
+        deep_entry<128, 512, 32, 10, 16, 2>(),  // fp32 128 -> 512 x 9 -> 32 on 5 clusters of 16
+    };
+    if (net.max_batch != 1)
+        return nullptr;
+    for (const DeepEntry &e : table) {
+        if (net.n_layers != e.nl || (C != 0 && C != e.C))
+            continue;
+        bool match = true;
+        for (int l = 0; l < e.nl && match; ++l) {
+            const ll_layer_desc &d = net.layers[l];
+            match = d.wtype == LL_W_F32 && d.in_dim == (l == 0 ? e.in : e.h) && d.out_dim == (l == e.nl - 1 ? e.out : e.h);
+        }
+        if (match)
+            return &e;
+    }
+    return nullptr;
+}
+
+// Per-CTA image of the deep kernel (CTA = stage * C + rank): [NW][kThreads] weights
+// (thread-minor) then NB biases.  Hidden layer (KL = kin / 32 weights per row): warp w, lane l
+// holds rows 2w and 2w + 1 (global rank * R + 2w + r), weight r KL + j pairing with input
+// element 4 (l + 32 (j / 4)) + j % 4; the last layer: warp w, lane l holds
+// W[OPW w + o][rank * R + l], o < OPW.
+std::vector<uint8_t> pack_deep(const DeepEntry &d, const void *const *W, const float *const *b, size_t &stride)
+{
+    const int T = kThreads, R = d.h / d.C, OPW = d.out / (T / 32);
+    stride = llh::round_up(((size_t)d.NW * T + d.NB) * 4, 256);
+    std::vector<uint8_t> img((size_t)d.NS * d.C * stride, 0);
+    for (int st = 0; st < d.NS; ++st) {
+        const int l0 = st * d.lps, l1 = st == d.NS - 1 ? d.nl - 1 : (st + 1) * d.lps - 1;
+        for (int c = 0; c < d.C; ++c) {
+            float *o = reinterpret_cast<float *>(img.data() + ((size_t)st * d.C + c) * stride);
+            float *bo = o + (size_t)d.NW * T;
+            int woff = 0, boff = 0;
+            for (int l = l0; l <= l1; ++l) {
+                const float *Wl = static_cast<const float *>(W[l]);
+                const int kin = l == 0 ? d.in : d.h;
+                if (l == d.nl - 1) {
+                    for (int t = 0; t < T; ++t)
+                        for (int q = 0; q < OPW; ++q)
+                            o[(size_t)(woff + q) * T + t] = Wl[(size_t)(OPW * (t / 32) + q) * kin + c * R + t % 32];
+                    for (int i = 0; i < d.out; ++i)
+                        bo[boff + i] = b && b[l] ? b[l][i] : 0.0f;
+                    woff += OPW;
+                    boff += d.out;
+                } else {
+                    const int KL = kin / 32, K = 2 * KL;
+                    if (R != 2 * (T / 32) || kin % 128 != 0) {
+                        llh::set_error("deep kernel image: 2 rows per warp and 16-byte pieces per lane");
+                        return {};
+                    }
+                    for (int t = 0; t < T; ++t) {
+                        const int wp = t / 32, ln = t % 32;
+                        for (int r = 0; r < 2; ++r)
+                            for (int j = 0; j < KL; ++j)
+                                o[(size_t)(woff + r * KL + j) * T + t] =
+                                    Wl[(size_t)(c * R + 2 * wp + r) * kin + 4 * (ln + 32 * (j / 4)) + j % 4];
+                    }
+                    for (int i = 0; i < R; ++i)
+                        bo[boff + i] = b && b[l] ? b[l][c * R + i] : 0.0f;
+                    woff += K;
+                    boff += R;
+                }
+            }
+            if (woff > d.NW || boff > d.NB) {
+                llh::set_error("deep kernel image: stage %d needs %d weights / %d biases per thread / CTA", st, woff,
+                               boff);
+                return {};
+            }
         }
     }
     return img;
@@ -1194,6 +1287,93 @@ int create_fast3(const ll_net_desc *net, const void *const *W, const float *cons
     return LL_OK;
 }
 
+// Register-resident kernel for a deep net (variant 2, several clusters): one request at a time,
+// TickBuffer or tagged mailbox (ring slots, no micro-batching), or the device queue.
+int create_deep(const ll_net_desc *net, const void *const *W, const float *const *b, int device,
+                const ll_engine_opts &o, const DeepEntry &d, ll_engine **out)
+{
+    size_t stride = 0;
+    std::vector<uint8_t> img = pack_deep(d, W, b, stride);
+    if (img.empty())
+        return LL_ERR_UNSUPPORTED;
+    ll_engine *e = new ll_engine();
+    e->device = device;
+    e->in_dim = d.in;
+    e->out_dim = d.out;
+    e->max_batch = 1;
+    e->kfn = d.fn;
+    e->variant = 2;
+    e->micro_max = 1;
+    e->weight_regs = d.NW;
+    int rc = engine_common_create(e, &o);
+    if (rc) {
+        ll_engine_destroy(e);
+        return rc;
+    }
+    PlanResult &pr = e->plan;
+    pr.S = d.NS;
+    pr.C = d.C;
+    pr.L.assign(d.nl, LayerPlan{});
+    Params &p = e->base;
+    p.n_layers = d.nl;
+    p.act_bf16 = 0;
+    for (int st = 0; st < d.NS; ++st) {
+        const int l0 = st * d.lps, l1 = st == d.NS - 1 ? d.nl - 1 : (st + 1) * d.lps - 1;
+        pr.stage_first.push_back(l0);
+        pr.stage_last.push_back(l1);
+        pr.stage_in_ld.push_back(l0 == 0 ? d.in : d.h);
+        pr.stage_image.push_back(stride);
+        for (int l = l0; l <= l1; ++l) {
+            LayerPlan &lp = pr.L[l];
+            lp.in = net->layers[l].in_dim;
+            lp.out = net->layers[l].out_dim;
+            lp.act = net->layers[l].act;
+            lp.wtype = LL_W_F32;
+            lp.K = lp.in;
+            lp.stage = st;
+            lp.Mp = l == d.nl - 1 ? d.out : d.h;
+            lp.R = l == d.nl - 1 ? d.out : d.h / d.C;
+            // how the layer's outputs leave the CTA
+            lp.mode = l == d.nl - 1                        ? LM_KSPLIT_GATHER
+                      : l + 1 == d.nl - 1 && l + 1 <= l1    ? LM_ROWSPLIT_LOCAL
+                      : l == l1                             ? LM_ROWSPLIT_GLOBAL
+                                                            : LM_ROWSPLIT_ALLGATHER;
+            p.L[l] = LayerDev{};
+            p.L[l].mode = lp.mode;
+            p.L[l].act = lp.act;
+            p.L[l].wtype = LL_W_F32;
+            p.L[l].K = lp.K;
+            p.L[l].M = lp.out;
+            p.L[l].Mp = lp.Mp;
+            p.L[l].R = lp.R;
+        }
+    }
+    layout_buffers(p, pr, d.in, d.out, 1);
+    p.smem_bytes = 0;  // all shared memory of this kernel is static
+    p.image_stride = (uint32_t)stride;
+    cudaError_t ce = cudaMalloc((void **)&e->d_image, img.size());
+    if (ce == cudaSuccess)
+        ce = cudaMemcpy(e->d_image, img.data(), img.size(), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        llh::set_error("uploading register images: %s", cudaGetErrorString(ce));
+        ll_engine_destroy(e);
+        return LL_ERR_CUDA;
+    }
+    p.image = e->d_image;
+    rc = finish_setup(e);  // grid S * C; the L2 hand-off buffers of the ROWSPLIT_GLOBAL layers
+    if (rc) {
+        ll_engine_destroy(e);
+        return rc;
+    }
+    if (!p.xfer_tagged || (size_t)p.xfer_stride < 2 * (size_t)d.h) {
+        llh::set_error("deep kernel: the hand-off buffers hold %u floats per stage, %d needed", p.xfer_stride, 2 * d.h);
+        ll_engine_destroy(e);
+        return LL_ERR_UNSUPPORTED;
+    }
+    *out = e;
+    return LL_OK;
+}
+
 // Kernel variant 3 (resident small-batch kernel): bf16 or int8 weights of one type, up to
 // 32 rows, the TickBuffer mailbox (or the tagged one at batch 1), in and out widths
 // multiples of 4, slices that fit one SM.
@@ -1346,12 +1526,21 @@ int ll_engine_create_ex(const ll_net_desc *net, const void *const *W, const floa
         return LL_ERR_INVALID_ARG;
     }
     const Fast3Entry *f3 = (o.kernel_variant == 1 || o.kernel_variant == 3) ? nullptr : find_fast3(*net, o.cluster_size);
-    if ((o.kernel_variant == 2 || o.kernel_variant == 4) && !f3) {
+    if (((o.kernel_variant == 2 && (o.micro_batch > 1 || !find_deep(*net, o.cluster_size))) || o.kernel_variant == 4) &&
+        !f3) {
         llh::set_error("no register-resident kernel is compiled for this net shape / cluster size");
         return LL_ERR_UNSUPPORTED;
     }
     if (f3)
         return create_fast3(net, W, b, device, o, *f3, o.kernel_variant == 4, out);
+    // deep nets of one hidden width: the multi-cluster register-resident kernel, unless a plan
+    // is forced (cluster size aside) or requests are to be taken several at a time
+    const DeepEntry *dp = (o.kernel_variant == 0 || o.kernel_variant == 2) && !o.min_stages && !o.max_stages &&
+                                  o.replicate_first < 0 && o.micro_batch <= 1
+                              ? find_deep(*net, o.cluster_size)
+                              : nullptr;
+    if (dp)
+        return create_deep(net, W, b, device, o, *dp, out);
     if (o.kernel_variant == 3 || o.kernel_variant == 0) {
         int sms = 0;
         LL_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));

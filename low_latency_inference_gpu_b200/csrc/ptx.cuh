@@ -100,6 +100,14 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, float4 v, uin
                  : "memory");
 }
 
+__device__ __forceinline__ void st_async_v2(uint32_t cluster_addr, float2 v, uint32_t cluster_bar)
+{
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                     cluster_addr),
+                 "f"(v.x), "f"(v.y), "r"(cluster_bar)
+                 : "memory");
+}
+
 __device__ __forceinline__ void st_async_u32(uint32_t cluster_addr, uint32_t v, uint32_t cluster_bar)
 {
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(cluster_addr),

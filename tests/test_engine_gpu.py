@@ -94,6 +94,42 @@ def test_config1_multi_cluster_parity(golden):
     assert rel_err(ys[: g["n"]], unbits(g["y"]).reshape(g["n"], -1)) <= 1e-5
 
 
+def test_config1_register_resident_deep_kernel_every_request_path():
+    """Config 1 runs on the deep register-resident kernel (5 clusters of 16, 64 weights per
+    thread): the tagged ring, the TickBuffer and the device queue give bit-identical replies
+    (one kernel, one summation order), within 1e-5 of the oracle and of the generic kernel,
+    which still serves the net when asked for."""
+    torch = pytest.importorskip("torch")
+    net, Ws, bs = ll.config_params(1)
+    xs = ll.config_inputs(1, 40)
+    ref = oracle.mlp_f32(net.dims, net.acts, Ws, bs, xs)
+    with engine_for(net, Ws, bs, mailbox_format=1, ring_slots=8) as e:
+        inf = e.info()
+        assert inf.kernel_variant == ll.VARIANT_REGISTER_RESIDENT
+        assert inf.n_stages == 5 and inf.cluster_size == 16 and inf.weight_regs == 64
+        # per stage: rows split + all-gather over DSMEM (1), rows split + L2 hand-off to the next
+        # cluster (5); the last stage keeps its rows local (2) for the K-split last layer (3)
+        assert list(inf.layer_modes[:10]) == [1, 5] * 4 + [2, 3]
+        tagged = np.stack([e.infer(xs[i])[0] for i in range(16)])
+        seqs = e.submit_many(xs[16:24])
+        tagged = np.concatenate([tagged, np.stack([e.poll(s)[0] for s in seqs])])
+        e.stop()
+        dx = torch.from_numpy(np.ascontiguousarray(xs)).cuda()
+        dy = torch.zeros(40, net.dims[-1], device="cuda")
+        e.run_queue(dx.data_ptr(), dy.data_ptr(), 40, 1)
+        queued = dy.cpu().numpy()
+        assert e.info().status == ll.LL_OK
+    with engine_for(net, Ws, bs, mailbox_format=0) as e:
+        assert e.info().kernel_variant == ll.VARIANT_REGISTER_RESIDENT
+        tick = np.stack([e.infer(xs[i])[0] for i in range(24)])
+    with engine_for(net, Ws, bs, kernel_variant=1) as e:
+        assert e.info().kernel_variant == ll.VARIANT_GENERIC
+        generic = np.stack([e.infer(xs[i])[0] for i in range(24)])
+    assert np.array_equal(tagged, tick) and np.array_equal(tagged, queued[:24])
+    assert close(queued, ref, 1e-5) and rel_err(queued, ref) <= 1e-5
+    assert close(tagged, generic, 1e-5)
+
+
 @pytest.mark.parametrize("C,rep", [(2, 0), (4, 1), (8, 0), (8, 1), (16, 0), (16, 1)])
 def test_config0_generic_kernel_cluster_sizes(C, rep):
     net, Ws, bs = ll.config_params(0)
