@@ -338,10 +338,12 @@ def run_batched(ll, torch, dev, iters=30):
     # end, host clock per request) and from a device queue (device time per forward: CUDA
     # events around a launch that serves the queue; the weights are not re-read, so there is
     # nothing for an L2 flush to evict)
+    o3 = ll.default_opts()
+    o3.kernel_variant = ll.VARIANT_RESIDENT_SMALL_BATCH
     for pt in sweep:
         rows = pt["rows"]
         rnet = ll.Net(net.dims, net.acts, net.wtype, rows)
-        with ll.Engine(rnet, Wd, bd, sd, device=dev) as e:
+        with ll.Engine(rnet, Wd, bd, sd, device=dev, opts=o3) as e:
             xs = ll.config_inputs(2, 256 * rows).reshape(256, rows * net.dims[0])
             e.bench_closed_loop(xs, 300, rows)
             lat, _ = e.bench_closed_loop(xs, 2000, rows)
@@ -357,10 +359,28 @@ def run_batched(ll, torch, dev, iters=30):
         if rows == 1:  # batch 1 also runs on the tagged mailbox (x with the doorbell, y without a release)
             o = ll.default_opts()
             o.mailbox_format = 1
+            o.kernel_variant = ll.VARIANT_RESIDENT_SMALL_BATCH
             with ll.Engine(rnet, Wd, bd, sd, device=dev, opts=o) as e:
                 e.bench_closed_loop(xs, 300, 1)
                 tl, _ = e.bench_closed_loop(xs, 2000, 1)
             tagged = {"e2e_tagged_p50_us": float(np.median(tl)), "e2e_tagged_p99_us": float(np.percentile(tl, 99))}
+            # the batch-1 default: the deep register-resident kernel (5 clusters of 16 CTAs, two
+            # bf16 weights per register), tagged mailbox end to end and the device queue
+            o = ll.default_opts()
+            o.mailbox_format = 1
+            with ll.Engine(rnet, Wd, bd, sd, device=dev, opts=o) as e:
+                inf = e.info()
+                e.bench_closed_loop(xs, 300, 1)
+                dl, _ = e.bench_closed_loop(xs, 3000, 1)
+                e.stop()
+                e.run_queue(dx.data_ptr(), dy.data_ptr(), n, 1)
+                dms = min(e.run_queue(dx.data_ptr(), dy.data_ptr(), n, 1) for _ in range(3))
+            pt["register_resident_engine"] = {
+                "kernel_variant": inf.kernel_variant, "stages": inf.n_stages, "cluster_size": inf.cluster_size,
+                "weight_registers_per_thread": inf.weight_regs, "e2e_tagged_p50_us": float(np.median(dl)),
+                "e2e_tagged_p99_us": float(np.percentile(dl, 99)), "us_per_forward_queue": dms * 1e3 / n,
+                "roofline": {"bound": "latency", "note": "9.0 MB of bf16 weights stay in registers; per request "
+                             "x (1 KB), 4 KB of tagged L2 words per stage boundary and y (256 B) move"}}
         pt["resident_engine"] = {
             "kernel_variant": variant, "e2e_p50_us": float(np.median(lat)), "e2e_p99_us": float(np.percentile(lat, 99)),
             **tagged, "us_per_forward_queue": us,
@@ -368,7 +388,9 @@ def run_batched(ll, torch, dev, iters=30):
                          "frac": gbs / hbm}}
     out["bf16_gelu_mlp_256x1024x4x64_sweep"] = {
         "points": sweep, "tiling": tiling, "kernel": "small-batch (one cooperative launch per forward); "
-                                                      "resident_engine: the same kernel resident (engine variant 3)",
+                                                      "resident_engine: the same kernel resident (engine variant 3); "
+                                                      "register_resident_engine (1 row): the deep register-resident "
+                                                      "kernel, the batch-1 default",
         "algorithmic": "bf16 weights + biases + rows x (in + out) fp32"}
     return out
 

@@ -434,23 +434,24 @@ std::vector<uint8_t> pack_ring(const Fast3Entry &f, const void *const *W, const 
 
 // Register-resident kernels compiled for deep nets of one hidden width (IN -> H x (NL-1) -> OUT).
 struct DeepEntry {
-    int in, h, out, nl, C, lps;
+    int wt, in, h, out, nl, C, lps;
     const void *fn;
-    int NW, NB, NS;
+    int NW, NB, NS, RPW, RL, OPW;
 };
 
-template <int IN, int H, int OUT, int NL, int C, int LPS>
+template <int WT, int IN, int H, int OUT, int NL, int C, int LPS>
 DeepEntry deep_entry()
 {
-    using D = DeepShape<IN, H, OUT, NL, C, LPS>;
-    return DeepEntry{IN, H, OUT, NL, C, LPS, reinterpret_cast<const void *>(&ll_deep_kernel<IN, H, OUT, NL, C, LPS>),
-                     D::NW, D::NB, D::NS};
+    using D = DeepShape<WT, IN, H, OUT, NL, C, LPS>;
+    return DeepEntry{WT,   IN,   H,    OUT,   NL,    C,     LPS,  reinterpret_cast<const void *>(&ll_deep_kernel<WT, IN, H, OUT, NL, C, LPS>),
+                     D::NW, D::NB, D::NS, D::RPW, D::RL, D::OPW};
 }
 
 const DeepEntry *find_deep(const ll_net_desc &net, int C)
 {
     static const DeepEntry table[] = {
-        deep_entry<128, 512, 32, 10, 16, 2>(),  // fp32 128 -> 512 x 9 -> 32 on 5 clusters of 16
+        deep_entry<LL_W_F32, 128, 512, 32, 10, 16, 2>(),   // 128 -> 512 x 9 -> 32 on 5 clusters of 16
+        deep_entry<LL_W_BF16, 256, 1024, 64, 6, 16, 1>(),  // 256 -> 1024 x 5 -> 64 on 5 clusters of 16
     };
     if (net.max_batch != 1)
         return nullptr;
@@ -460,7 +461,7 @@ const DeepEntry *find_deep(const ll_net_desc &net, int C)
         bool match = true;
         for (int l = 0; l < e.nl && match; ++l) {
             const ll_layer_desc &d = net.layers[l];
-            match = d.wtype == LL_W_F32 && d.in_dim == (l == 0 ? e.in : e.h) && d.out_dim == (l == e.nl - 1 ? e.out : e.h);
+            match = d.wtype == e.wt && d.in_dim == (l == 0 ? e.in : e.h) && d.out_dim == (l == e.nl - 1 ? e.out : e.h);
         }
         if (match)
             return &e;
@@ -468,55 +469,68 @@ const DeepEntry *find_deep(const ll_net_desc &net, int C)
     return nullptr;
 }
 
-// Per-CTA image of the deep kernel (CTA = stage * C + rank): [NW][kThreads] weights
-// (thread-minor) then NB biases.  Hidden layer (KL = kin / 32 weights per row): warp w, lane l
-// holds rows 2w and 2w + 1 (global rank * R + 2w + r), weight r KL + j pairing with input
-// element 4 (l + 32 (j / 4)) + j % 4; the last layer: warp w, lane l holds
-// W[OPW w + o][rank * R + l], o < OPW.
+// Per-CTA image of the deep kernel (CTA = stage * C + rank): [NW][kThreads] 32-bit weight
+// registers (thread-minor; fp32, or two bf16 per register: logical weight 2m in the low half of
+// register m) then NB fp32 biases.  Hidden layer (KP = kin / 128 pieces per lane): warp w, lane
+// l holds rows RPW w + r (global rank * R + RPW w + r), logical weight (r KP + j) 4 + e pairing
+// with input element 4 (l + 32 j) + e; the last layer: logical weight o RL + j of warp w, lane l
+// is W[OPW w + o][rank * R + l + 32 j].
 std::vector<uint8_t> pack_deep(const DeepEntry &d, const void *const *W, const float *const *b, size_t &stride)
 {
-    const int T = kThreads, R = d.h / d.C, OPW = d.out / (T / 32);
+    const int T = kThreads, R = d.h / d.C, EPR = d.wt == LL_W_BF16 ? 2 : 1;
     stride = llh::round_up(((size_t)d.NW * T + d.NB) * 4, 256);
     std::vector<uint8_t> img((size_t)d.NS * d.C * stride, 0);
+    // logical weight i of thread t's slice at register `off` (bf16: bit patterns, two per register)
+    auto put = [&](uint32_t *o, int off, int i, int t, const void *Wl, size_t idx) {
+        uint32_t &reg = o[(size_t)(off + i / EPR) * T + t];
+        if (EPR == 1) {
+            std::memcpy(&reg, static_cast<const float *>(Wl) + idx, 4);
+        } else {
+            const uint32_t h = static_cast<const uint16_t *>(Wl)[idx];
+            reg |= (i & 1) ? h << 16 : h;
+        }
+    };
     for (int st = 0; st < d.NS; ++st) {
         const int l0 = st * d.lps, l1 = st == d.NS - 1 ? d.nl - 1 : (st + 1) * d.lps - 1;
         for (int c = 0; c < d.C; ++c) {
-            float *o = reinterpret_cast<float *>(img.data() + ((size_t)st * d.C + c) * stride);
-            float *bo = o + (size_t)d.NW * T;
+            uint32_t *o = reinterpret_cast<uint32_t *>(img.data() + ((size_t)st * d.C + c) * stride);
+            float *bo = reinterpret_cast<float *>(o + (size_t)d.NW * T);
             int woff = 0, boff = 0;
             for (int l = l0; l <= l1; ++l) {
-                const float *Wl = static_cast<const float *>(W[l]);
                 const int kin = l == 0 ? d.in : d.h;
                 if (l == d.nl - 1) {
                     for (int t = 0; t < T; ++t)
-                        for (int q = 0; q < OPW; ++q)
-                            o[(size_t)(woff + q) * T + t] = Wl[(size_t)(OPW * (t / 32) + q) * kin + c * R + t % 32];
+                        for (int q = 0; q < d.OPW; ++q)
+                            for (int j = 0; j < d.RL; ++j)
+                                put(o, woff, q * d.RL + j, t, W[l],
+                                    (size_t)(d.OPW * (t / 32) + q) * kin + c * R + t % 32 + 32 * j);
                     for (int i = 0; i < d.out; ++i)
                         bo[boff + i] = b && b[l] ? b[l][i] : 0.0f;
-                    woff += OPW;
+                    woff += d.OPW * d.RL / EPR;
                     boff += d.out;
                 } else {
-                    const int KL = kin / 32, K = 2 * KL;
-                    if (R != 2 * (T / 32) || kin % 128 != 0) {
-                        llh::set_error("deep kernel image: 2 rows per warp and 16-byte pieces per lane");
+                    const int KP = kin / 128;
+                    if (R != d.RPW * (T / 32) || kin % 128 != 0) {
+                        llh::set_error("deep kernel image: %d rows per warp and 16-byte pieces per lane", d.RPW);
                         return {};
                     }
                     for (int t = 0; t < T; ++t) {
                         const int wp = t / 32, ln = t % 32;
-                        for (int r = 0; r < 2; ++r)
-                            for (int j = 0; j < KL; ++j)
-                                o[(size_t)(woff + r * KL + j) * T + t] =
-                                    Wl[(size_t)(c * R + 2 * wp + r) * kin + 4 * (ln + 32 * (j / 4)) + j % 4];
+                        for (int r = 0; r < d.RPW; ++r)
+                            for (int j = 0; j < KP; ++j)
+                                for (int e = 0; e < 4; ++e)
+                                    put(o, woff, (r * KP + j) * 4 + e, t, W[l],
+                                        (size_t)(c * R + d.RPW * wp + r) * kin + 4 * (ln + 32 * j) + e);
                     }
                     for (int i = 0; i < R; ++i)
                         bo[boff + i] = b && b[l] ? b[l][c * R + i] : 0.0f;
-                    woff += K;
+                    woff += d.RPW * KP * 4 / EPR;
                     boff += R;
                 }
             }
             if (woff > d.NW || boff > d.NB) {
-                llh::set_error("deep kernel image: stage %d needs %d weights / %d biases per thread / CTA", st, woff,
-                               boff);
+                llh::set_error("deep kernel image: stage %d needs %d weight registers / %d biases per thread / CTA",
+                               st, woff, boff);
                 return {};
             }
         }
@@ -1316,7 +1330,7 @@ int create_deep(const ll_net_desc *net, const void *const *W, const float *const
     pr.L.assign(d.nl, LayerPlan{});
     Params &p = e->base;
     p.n_layers = d.nl;
-    p.act_bf16 = 0;
+    p.act_bf16 = d.wt == LL_W_BF16 ? 1 : 0;  // the tagged poll rounds x to bf16 for a bf16 net
     for (int st = 0; st < d.NS; ++st) {
         const int l0 = st * d.lps, l1 = st == d.NS - 1 ? d.nl - 1 : (st + 1) * d.lps - 1;
         pr.stage_first.push_back(l0);
@@ -1328,7 +1342,7 @@ int create_deep(const ll_net_desc *net, const void *const *W, const float *const
             lp.in = net->layers[l].in_dim;
             lp.out = net->layers[l].out_dim;
             lp.act = net->layers[l].act;
-            lp.wtype = LL_W_F32;
+            lp.wtype = d.wt;
             lp.K = lp.in;
             lp.stage = st;
             lp.Mp = l == d.nl - 1 ? d.out : d.h;
@@ -1341,7 +1355,8 @@ int create_deep(const ll_net_desc *net, const void *const *W, const float *const
             p.L[l] = LayerDev{};
             p.L[l].mode = lp.mode;
             p.L[l].act = lp.act;
-            p.L[l].wtype = LL_W_F32;
+            p.L[l].wtype = d.wt;
+            p.L[l].round_out = d.wt == LL_W_BF16 && l < d.nl - 1 ? 1 : 0;
             p.L[l].K = lp.K;
             p.L[l].M = lp.out;
             p.L[l].Mp = lp.Mp;

@@ -130,6 +130,41 @@ def test_config1_register_resident_deep_kernel_every_request_path():
     assert close(tagged, generic, 1e-5)
 
 
+def test_config2_batch1_on_the_deep_kernel_with_bf16_weight_pairs():
+    """Config 2 at batch 1 (bf16 256 -> 1024 x 5 -> 64, GELU) runs on the deep register-resident
+    kernel with two bf16 weights per register (5 clusters, one layer each): x and the hidden
+    outputs rounded to bf16 as the oracle does; the tagged ring, the TickBuffer and the device
+    queue agree bit for bit; within the bf16 tolerance of the oracle and of the resident
+    small-batch kernel (another summation order)."""
+    torch = pytest.importorskip("torch")
+    net32, Ws, bs = ll.config_params(2)
+    net = ll.mlp(net32.dims, ll.ACT_GELU, ll.ACT_IDENTITY, ll.W_BF16, 1)
+    xs = ll.config_inputs(2, 24)
+    ref = oracle_out(net, Ws, bs, xs)
+    with engine_for(net, Ws, bs, mailbox_format=1, ring_slots=8) as e:
+        inf = e.info()
+        assert inf.kernel_variant == ll.VARIANT_REGISTER_RESIDENT and inf.n_stages == 5
+        assert inf.weight_regs == 68  # 64 of the hidden layer + 4 of the last layer's K-split
+        assert list(inf.layer_modes[:6]) == [5, 5, 5, 5, 2, 3]
+        tagged = np.stack([e.infer(xs[i])[0] for i in range(8)])
+        seqs = e.submit_many(xs[8:16])
+        tagged = np.concatenate([tagged, np.stack([e.poll(s)[0] for s in seqs])])
+        e.stop()
+        dx = torch.from_numpy(np.ascontiguousarray(xs)).cuda()
+        dy = torch.zeros(24, net.dims[-1], device="cuda")
+        e.run_queue(dx.data_ptr(), dy.data_ptr(), 24, 1)
+        queued = dy.cpu().numpy()
+        assert e.info().status == ll.LL_OK
+    with engine_for(net, Ws, bs, mailbox_format=0) as e:
+        tick = np.stack([e.infer(xs[i])[0] for i in range(16)])
+    with engine_for(net, Ws, bs, kernel_variant=3) as e:
+        assert e.info().kernel_variant == ll.VARIANT_RESIDENT_SMALL_BATCH
+        small = np.stack([e.infer(xs[i])[0] for i in range(16)])
+    assert np.array_equal(tagged, tick) and np.array_equal(tagged, queued[:16])
+    assert close(queued, ref, TOL[ll.W_BF16]) and rel_err(queued, ref) <= TOL[ll.W_BF16]
+    assert close(tagged, small, TOL[ll.W_BF16])
+
+
 @pytest.mark.parametrize("C,rep", [(2, 0), (4, 1), (8, 0), (8, 1), (16, 0), (16, 1)])
 def test_config0_generic_kernel_cluster_sizes(C, rep):
     net, Ws, bs = ll.config_params(0)
