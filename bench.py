@@ -405,10 +405,14 @@ PROFILE_CASES = {
     "int8-1024x2048x6x256-2048rows-pairs": (3, 2048, {"sm_pairs": 1}),
     # the resident small-batch engine (kernel variant 3): two device queues of 200 requests,
     # one launch each (the first warms up)
-    "resident-bf16-gelu-256x1024x4x64-1row": (2, 1, {"resident": True}),
-    "resident-bf16-gelu-256x1024x4x64-32rows": (2, 32, {"resident": True}),
-    # the 10-layer fp32 net on the generic resident kernel (4 clusters of 16 CTAs), same queues
-    "resident-fp32-128x512x8x32-1row": (1, 1, {"resident": True}),
+    "resident-bf16-gelu-256x1024x4x64-1row": (2, 1, {"resident": 3}),
+    "resident-bf16-gelu-256x1024x4x64-32rows": (2, 32, {"resident": 3}),
+    # the 10-layer fp32 net on the generic resident kernel (3 clusters of 16 CTAs), same queues
+    "resident-fp32-128x512x8x32-1row": (1, 1, {"resident": 1}),
+    # the deep register-resident kernel (variant 2, 5 clusters of 16 CTAs): configs 1 and 2 at
+    # batch 1, same queues
+    "deep-fp32-128x512x8x32-1row": (1, 1, {"resident": 2}),
+    "deep-bf16-gelu-256x1024x4x64-1row": (2, 1, {"resident": 2}),
 }
 
 
@@ -428,8 +432,10 @@ def run_profile_case(name):
         n = 200
         dx = torch.from_numpy(ll.config_inputs(cfg, n * rows)).cuda()
         dy = torch.empty((n * rows, net.dims[-1]), dtype=torch.float32, device="cuda")
-        with ll.Engine(rnet, Wd, bd, sd, device=0) as e:
-            if e.info().kernel_variant != (1 if cfg == 1 else 3):
+        eo = ll.default_opts()
+        eo.kernel_variant = opts["resident"]
+        with ll.Engine(rnet, Wd, bd, sd, device=0, opts=eo) as e:
+            if e.info().kernel_variant != opts["resident"]:
                 raise RuntimeError("not the expected resident kernel for this workload")
             for _ in range(2):
                 e.run_queue(dx.data_ptr(), dy.data_ptr(), n, rows)
