@@ -327,6 +327,7 @@ struct Fast3Entry {
     int S1, S2, R2;
     int rows;  // rows one pass carries (micro-batching)
     const void *ring_fn;  // pipelined ring kernel of the shape (variant 4), or null
+    int ring_smem;        // its dynamic shared memory (bytes)
 };
 
 template <int IN, int H1, int H2, int OUT, int C>
@@ -334,10 +335,13 @@ Fast3Entry fast3_entry()
 {
     using S = Fast3Shape<IN, H1, H2, OUT, C>;
     const void *ring = nullptr;
-    if constexpr (S::MaxRows == kFast3Rows)
+    int ring_smem = 0;
+    if constexpr (S::MaxRows == kFast3Rows) {
         ring = reinterpret_cast<const void *>(&ll_ring_kernel<IN, H1, H2, OUT, C>);
+        ring_smem = RingPool<IN, H1, H2, OUT, C>::BYTES;
+    }
     return Fast3Entry{IN, H1, H2, OUT, C, reinterpret_cast<const void *>(&ll_fast3_kernel<IN, H1, H2, OUT, C>),
-                      S::K1, S::K2, S::K3, S::NB, S::S1, S::S2, S::R2, S::MaxRows, ring};
+                      S::K1, S::K2, S::K3, S::NB, S::S1, S::S2, S::R2, S::MaxRows, ring, ring_smem};
 }
 
 const Fast3Entry *find_fast3(const ll_net_desc &net, int C)
@@ -395,39 +399,54 @@ std::vector<uint8_t> pack_fast3(const Fast3Entry &f, const void *const *W, const
     return img;
 }
 
-// Per-CTA image of the pipelined ring kernel: the register-resident image's format (the same
-// size, layer 3 and biases), with layers 1 and 2 blocked as ring_layers.cuh reads them:
-// thread t holds 4 layer-1 rows x the 16-byte input pieces s1, s1 + 8, ... (g1 = t / 8,
-// s1 = t % 8) and 2 local layer-2 rows x the h1 pieces lane, lane + 32, ... (one row pair per warp).
+// Per-CTA image of the pipelined ring kernel (CTA c), [NW][kThreads] weights then the register-
+// resident image's biases (b1[H1], this CTA's b2 rows, b3[OUT]); thread t = (warp w, lane l):
+//   layer 1, one-row pass: 4 q + e  ->  W1[32 q + 2 w + (l >> 4)][4 (l & 15) + e], q < H1 / 32;
+//   layer 1, split pass:   4 i + e  ->  W1[c R1 + 2 w + i][4 (l & 15) + e], i < 2;
+//   layer 2: 2 local rows x the h1 pieces l, l + 32, ... (one row pair per warp), as ring_layers.cuh
+//            reads them;
+//   layer 3: as in the register-resident image (warp w = output w, local rows l + 32 j).
 std::vector<uint8_t> pack_ring(const Fast3Entry &f, const void *const *W, const float *const *b, size_t &stride)
 {
-    constexpr int RB1 = 4, RB2 = 2;
+    constexpr int RB2 = 2;
     const int T = kThreads;
-    const int G1 = f.h1 / RB1, L1 = T / G1, P1 = f.in / 4 / L1, K1 = RB1 * 4 * P1;
+    const int Q1 = f.h1 / 32, K1 = 4 * Q1, K1S = 8, R1 = f.h1 / f.C;
     const int L2 = 32, P2 = f.h1 / 4 / L2, K2 = RB2 * 4 * P2;
-    std::vector<uint8_t> img = pack_fast3(f, W, b, stride);  // layer 3 and biases as there
-    if (K1 != f.K1 || K2 != f.K2 || f.R2 != RB2 * (T / 32)) {
-        llh::set_error("ring image: the blocked layers do not fit the register-resident image");
+    const int NW = K1 + K1S + K2 + f.K3;
+    if (f.in != 64 || T != 512 || f.h1 % 32 != 0 || R1 != 2 * (T / 32) || f.R2 != RB2 * (T / 32) || K2 != f.K2) {
+        llh::set_error("ring image: the shape does not fit the blocked layers");
         return {};
     }
+    stride = llh::round_up(((size_t)NW * T + f.NB) * 4, 256);
+    std::vector<uint8_t> img((size_t)f.C * stride, 0);
     const float *W1 = static_cast<const float *>(W[0]);
     const float *W2 = static_cast<const float *>(W[1]);
+    const float *W3 = static_cast<const float *>(W[2]);
     for (int c = 0; c < f.C; ++c) {
         float *o = reinterpret_cast<float *>(img.data() + (size_t)c * stride);
         for (int t = 0; t < T; ++t) {
-            const int g1 = t / L1, s1 = t % L1;
-            for (int r = 0; r < RB1; ++r)
-                for (int p = 0; p < P1; ++p)
-                    for (int e = 0; e < 4; ++e)
-                        o[(size_t)(r * 4 * P1 + 4 * p + e) * T + t] =
-                            W1[(size_t)(RB1 * g1 + r) * f.in + 4 * (s1 + L1 * p) + e];
-            const int g2 = t / 32, s2 = t % 32;
+            const int w = t / 32, l = t % 32, s = l & 15;
+            for (int q = 0; q < Q1; ++q)
+                for (int e = 0; e < 4; ++e)
+                    o[(size_t)(4 * q + e) * T + t] = W1[(size_t)(32 * q + 2 * w + (l >> 4)) * f.in + 4 * s + e];
+            for (int i = 0; i < 2; ++i)
+                for (int e = 0; e < 4; ++e)
+                    o[(size_t)(K1 + 4 * i + e) * T + t] = W1[(size_t)(c * R1 + 2 * w + i) * f.in + 4 * s + e];
             for (int r = 0; r < RB2; ++r)
                 for (int p = 0; p < P2; ++p)
                     for (int e = 0; e < 4; ++e)
-                        o[(size_t)(K1 + r * 4 * P2 + 4 * p + e) * T + t] =
-                            W2[(size_t)(c * f.R2 + RB2 * g2 + r) * f.h1 + 4 * (s2 + L2 * p) + e];
+                        o[(size_t)(K1 + K1S + r * 4 * P2 + 4 * p + e) * T + t] =
+                            W2[(size_t)(c * f.R2 + RB2 * w + r) * f.h1 + 4 * (l + L2 * p) + e];
+            for (int j = 0; j < f.K3; ++j)
+                o[(size_t)(K1 + K1S + K2 + j) * T + t] = w < f.out ? W3[(size_t)w * f.h2 + c * f.R2 + l + 32 * j] : 0.0f;
         }
+        float *bo = o + (size_t)NW * T;
+        for (int i = 0; i < f.h1; ++i)
+            bo[i] = b && b[0] ? b[0][i] : 0.0f;
+        for (int i = 0; i < f.R2; ++i)
+            bo[f.h1 + i] = b && b[1] ? b[1][c * f.R2 + i] : 0.0f;
+        for (int i = 0; i < f.out; ++i)
+            bo[f.h1 + f.R2 + i] = b && b[2] ? b[2][i] : 0.0f;
     }
     return img;
 }
@@ -1255,7 +1274,7 @@ int create_fast3(const ll_net_desc *net, const void *const *W, const float *cons
     e->kfn = ring ? f.ring_fn : f.fn;
     e->variant = ring ? 4 : 2;
     e->micro_max = f.rows;
-    e->weight_regs = f.K1 + f.K2 + f.K3;
+    e->weight_regs = ring ? 4 * (f.h1 / 32) + 8 + f.K2 + f.K3 : f.K1 + f.K2 + f.K3;
     int rc = engine_common_create(e, &o);
     if (rc) {
         ll_engine_destroy(e);
@@ -1277,7 +1296,7 @@ int create_fast3(const ll_net_desc *net, const void *const *W, const float *cons
         p.L[l].M = net->layers[l].out_dim;
     }
     layout_buffers(p, pr, f.in, f.out, 1);
-    p.smem_bytes = 0;  // all shared memory of this kernel is static
+    p.smem_bytes = ring ? (uint32_t)f.ring_smem : 0u;  // the ring kernel's pool is dynamic; the rest static
     p.image_stride = (uint32_t)stride;
     cudaError_t ce = cudaMalloc((void **)&e->d_image, img.size());
     if (ce == cudaSuccess)

@@ -148,36 +148,55 @@ __device__ __forceinline__ void ring_forward(uint32_t seq, int nb, uint32_t stag
     }
 }
 
+// Layout of the ring kernel's dynamic shared-memory pool (bytes).  Compute CTAs use [xs | h1[3]
+// | h2 | xch[2]], the I/O CTA [gath[NG] | yo | stage[2]] (stage: its copies of the rows it
+// forwards).  Remote writes go to the other role's region at the same offset in the receiving
+// CTA.  h1 holds layer 1's outputs slice-major (ring_layers.cuh); a split pass's slices arrive
+// from every compute CTA, so there are three buffers, used by pass % 3: the slowest compute CTA
+// is at most two passes behind the fastest (the reader hands pass p + 2 over only when every
+// compute CTA has unpacked pass p), so a slice never lands in a buffer still being read.
+template <int IN, int H1, int H2, int OUT, int C>
+struct RingPool {
+    static constexpr int MB = kFast3Rows;
+    static constexpr int NXC = (IN + 2) / 3;            // tagged chunks per row
+    static constexpr int YO = 3 * ((OUT + 2) / 3) + 4;  // one output row, zero-padded
+    static constexpr int R2 = H2 / C;
+    static constexpr int NH1 = 3;
+    static constexpr int OFF_XS = 0;
+    static constexpr int H1_B = 4 * MB * H1;  // one h1 buffer
+    static constexpr int OFF_H1 = OFF_XS + 4 * MB * IN;
+    static constexpr int OFF_H2 = OFF_H1 + NH1 * H1_B;
+    static constexpr int OFF_XCH = (OFF_H2 + 4 * MB * R2 + 15) / 16 * 16;
+    static constexpr int XCH_B = 16 * MB * NXC;
+    static constexpr int COMPUTE_END = OFF_XCH + 2 * XCH_B;
+    static constexpr int GATH_F = MB * C * OUT;  // [row][rank][output]
+    static constexpr int OFF_G = 0;
+    static constexpr int OFF_YO = OFF_G + kRingGathBufs * 4 * GATH_F;
+    static constexpr int OFF_STG = (OFF_YO + 4 * MB * YO + 15) / 16 * 16;
+    static constexpr int IO_END = OFF_STG + 2 * XCH_B;
+    static constexpr int BYTES = COMPUTE_END > IO_END ? COMPUTE_END : IO_END;
+};
+
 template <int IN, int H1, int H2, int OUT, int C>
 __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_constant__ Params pg)
 {
     using S = Fast3Shape<IN, H1, H2, OUT, C>;    // layer 3 and the buffer shapes
     using RS = RingShape<IN, H1, H2, OUT, C>;    // the blocked weights of layers 1 and 2
-    static_assert(RS::NW == S::NW && RS::NB == S::NB && RS::R2 == S::R2 && RS::K3 == S::K3,
-                  "the ring image has the register-resident image's size and layer-3 slice");
+    using PL = RingPool<IN, H1, H2, OUT, C>;
+    static_assert(RS::NB == S::NB && RS::R2 == S::R2 && RS::K3 == S::K3 && RS::R1 == RS::R2,
+                  "the ring image's biases and layer-3 slice are the register-resident image's; a layer-1 "
+                  "slice block stages in h2's place");
     constexpr int MB = kFast3Rows;
     static_assert(S::MaxRows == kFast3Rows, "the shape leaves no room for multi-row passes");
-    constexpr int NXC = (IN + 2) / 3;          // tagged chunks per row
-    constexpr int YO = 3 * ((OUT + 2) / 3) + 4;  // one output row, zero-padded
-    constexpr int IO = C;                      // rank of the I/O CTA
-    // One pool: compute CTAs use [xs | h1 | h2 | xch[2]], the I/O CTA [gath[NG] | yo | stage[2]]
-    // (stage: its copies of the rows it forwards).  Remote
-    // writes go to the other role's region at the same offset in the receiving CTA.
-    constexpr int OFF_XS = 0;
-    constexpr int OFF_H1 = OFF_XS + 4 * MB * IN;
-    constexpr int OFF_H2 = OFF_H1 + 4 * MB * H1;
-    constexpr int OFF_XCH = (OFF_H2 + 4 * MB * S::R2 + 15) / 16 * 16;
-    constexpr int XCH_B = 16 * MB * NXC;
-    constexpr int COMPUTE_END = OFF_XCH + 2 * XCH_B;
-    constexpr int GATH_F = MB * C * OUT;  // [row][rank][output]
-    constexpr int OFF_G = 0;
-    constexpr int OFF_YO = OFF_G + kRingGathBufs * 4 * GATH_F;
-    constexpr int OFF_STG = (OFF_YO + 4 * MB * YO + 15) / 16 * 16;
-    constexpr int IO_END = OFF_STG + 2 * XCH_B;
-    constexpr int POOL = COMPUTE_END > IO_END ? COMPUTE_END : IO_END;
-    __shared__ __align__(16) uint8_t pool[POOL];
+    constexpr int NXC = PL::NXC;
+    constexpr int YO = PL::YO;
+    constexpr int IO = C;  // rank of the I/O CTA
+    constexpr int OFF_XS = PL::OFF_XS, OFF_H1 = PL::OFF_H1, OFF_H2 = PL::OFF_H2, OFF_XCH = PL::OFF_XCH;
+    constexpr int XCH_B = PL::XCH_B, GATH_F = PL::GATH_F, OFF_G = PL::OFF_G, OFF_YO = PL::OFF_YO;
+    constexpr int OFF_STG = PL::OFF_STG;
+    extern __shared__ __align__(128) uint8_t pool[];  // PL::BYTES, dynamic
     __shared__ __align__(16) uint32_t hdr2[2][4];  // compute CTAs: {seq, rows} of the pass in buffer b
-    __shared__ __align__(8) uint64_t rb[11 + 3 * kRingGathBufs];  // see the barrier indices below
+    __shared__ __align__(8) uint64_t rb[14 + 3 * kRingGathBufs];  // see the barrier indices below
     __shared__ uint32_t fq[2][4];                   // I/O: reader -> forwarder, per stage buffer: rows, seq, kind, n
     __shared__ __align__(16) float bias[S::NB];
     __shared__ uint32_t mseq[kRingGathBufs][MB];   // I/O: sequence number of each row of the pass in buffer g
@@ -211,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     const uint32_t rbar = bar(6 + 3 * NG);  // I/O CTA: the reader's slot copies from host memory
     auto fready = [&](int b) { return bar(7 + 3 * NG + b); };  // I/O CTA: stage[b] handed to the forwarder
     auto sfree = [&](int b) { return bar(9 + 3 * NG + b); };   // I/O CTA: the forwarder is done with stage[b]
+    auto h1bar = [&](int j) { return bar(11 + 3 * NG + j); };  // compute CTAs: layer-1 slices in h1[j]
     const uint32_t pool_a = smem_u32(pool);
 
     if (tid == 0) {
@@ -228,6 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             mbar_init(fready(i), 1);
             mbar_init(sfree(i), 1);
         }
+        for (int j = 0; j < PL::NH1; ++j)
+            mbar_init(h1bar(j), 1);
         sh.cmd = 0;
         sh.fail = 0;
         sh.abort = 0;
@@ -240,20 +262,23 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     // weights into registers (compute CTAs; the I/O CTA holds none), biases into shared memory
     // (the I/O CTA takes CTA 0's copy: it needs the layer-3 biases)
     const float *img = reinterpret_cast<const float *>(p.image + (size_t)(io ? 0u : k.rank) * p.image_stride);
-    float w1[RS::K1], w2[RS::K2], w3[S::K3];
+    float w1[RS::K1], w1s[RS::K1S], w2[RS::K2], w3[S::K3];
     if (!io) {
 #pragma unroll
         for (int j = 0; j < RS::K1; ++j)
             w1[j] = ld_once_f32(img + (size_t)j * kThreads + tid);
 #pragma unroll
+        for (int j = 0; j < RS::K1S; ++j)
+            w1s[j] = ld_once_f32(img + (size_t)(RS::K1 + j) * kThreads + tid);
+#pragma unroll
         for (int j = 0; j < RS::K2; ++j)
-            w2[j] = ld_once_f32(img + (size_t)(RS::K1 + j) * kThreads + tid);
+            w2[j] = ld_once_f32(img + (size_t)(RS::K1 + RS::K1S + j) * kThreads + tid);
 #pragma unroll
         for (int j = 0; j < S::K3; ++j)
-            w3[j] = ld_once_f32(img + (size_t)(RS::K1 + RS::K2 + j) * kThreads + tid);
+            w3[j] = ld_once_f32(img + (size_t)(RS::K1 + RS::K1S + RS::K2 + j) * kThreads + tid);
     }
     for (int i = tid; i < S::NB; i += kThreads)
-        bias[i] = __ldg(img + (size_t)S::NW * kThreads + i);
+        bias[i] = __ldg(img + (size_t)RS::NW * kThreads + i);
     if (io) {
         float *gz = reinterpret_cast<float *>(pool + OFF_G);
         for (int i = tid; i < NG * GATH_F + MB * YO; i += kThreads)
@@ -267,13 +292,12 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     uint32_t passes_done = 0, rows_done = 0, last_replied = 0;
     if (!io) {
         // ======================= compute CTA =======================
-        const int g1 = tid / RS::L1, s1 = tid % RS::L1;  // layer-1 row group and K slice
-        const int g2 = warp;                              // layer-2 row group
+        const int g2 = warp;  // layer-2 row group
         float *xs = reinterpret_cast<float *>(pool + OFF_XS);
-        float *h1 = reinterpret_cast<float *>(pool + OFF_H1);
         float *h2 = reinterpret_cast<float *>(pool + OFF_H2);
         const int act1 = p.L[0].act, act2 = p.L[1].act;
         uint32_t ph_x[2] = {0u, 0u};
+        uint32_t ph_h1 = 0u;  // bit j: the phase of h1bar(j)
         uint32_t n_req = 0;  // request index of the pass's first row (as counted by the reader)
         for (uint32_t pass = 0;; ++pass) {
             const int b = (int)(pass & 1u);
@@ -320,11 +344,30 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 trace(k, n_req, 10);
             // layers 1 and 2 with the blocked weights (ring_layers.cuh): one row, or up to 16 at
             // once (the rows past nb compute on stale inputs inside the buffers and are never sent)
-            if (nb == 1)
-                ring_layer1_x1<RS, IN, H1>(w1, xs, h1, bias, g1, s1, act1);
-            else
-                ring_layer1_x16<RS, IN, H1>(w1, xs, h1, bias, g1, s1, act1, nb <= 8u ? 1 : 2);
-            __syncthreads();
+            const int hj = (int)(pass % (uint32_t)PL::NH1);
+            float *h1 = reinterpret_cast<float *>(pool + OFF_H1 + hj * PL::H1_B);
+            if (nb == 1) {
+                ring_layer1_x1<RS, IN, H1>(w1, xs, h1, bias, act1);
+                __syncthreads();
+            } else {
+                // this CTA's slice, staged in h2's place (free until layer 2), then one bulk copy
+                // of it into every compute CTA's h1[hj] (thread d serves CTA d)
+                ring_layer1_split<RS, IN, H1>(w1s, xs, h2, bias, (int)k.rank, act1);
+                fence_proxy_async_shared();  // this thread's staging stores, visible to the copies
+                __syncthreads();
+                constexpr uint32_t SLICE_B = 4u * MB * RS::R1;
+                if (tid < C) {
+                    bulk_s2peer(mapa(pool_a + OFF_H1 + (uint32_t)hj * PL::H1_B + k.rank * SLICE_B, (uint32_t)tid),
+                                smem_u32(h2), SLICE_B, mapa(h1bar(hj), (uint32_t)tid));
+                    bulk_commit_group();
+                    bulk_wait_group_read<0>();  // h2 is written by layer 2 after the barrier below
+                }
+                if (tid == 0)
+                    mbar_arrive_expect_tx(h1bar(hj), C * SLICE_B);
+                if (!cta_wait_bar(k, h1bar(hj), (ph_h1 >> hj) & 1u, EW_LAYER_BASE, p.step_ns))
+                    break;
+                ph_h1 ^= 1u << hj;
+            }
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 3);
             if (nb == 1)
@@ -561,6 +604,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
         if (gt == 0 && passes_done > 0)
             st_relaxed_sys_u32(&p.mb->seq_out, last_replied);
     }
+    if (!io && tid < C)
+        bulk_wait_group_all();  // this CTA's layer-1 slices have landed in every compute CTA
     __syncthreads();
     cluster_sync();
     if (io && tid == 32 * kRingGatherWarp0) {
