@@ -74,6 +74,11 @@ RING_ENGINES_MAX = 8  # throughput leg: resident engines per GPU (one host threa
 # images once (812 KB), then ~270 B per request (input row, stamp); scaled to R requests.
 TRAFFIC_FIXED_BYTES = 812_500
 TRAFFIC_PER_REQUEST_BYTES = 270
+# the same for the value leg's queue on the pipelined ring kernel (ncu: 1.526 MB read for a
+# queue of 2000 requests, nothing written back within the launch): the 8 compute CTAs' register
+# images and the biases once (~1.01 MB), then the 256-byte input row per request
+RING_TRAFFIC_FIXED_BYTES = 1_014_000
+RING_TRAFFIC_PER_REQUEST_BYTES = 256
 
 
 def env_int(name, default):
@@ -413,6 +418,9 @@ PROFILE_CASES = {
     # batch 1, same queues
     "deep-fp32-128x512x8x32-1row": (1, 1, {"resident": 2}),
     "deep-bf16-gelu-256x1024x4x64-1row": (2, 1, {"resident": 2}),
+    # the config-0 device queue of bench.py's value leg on the pipelined ring kernel (variant 4,
+    # up to 16 requests per pass): two queues of 2000 requests, one launch each
+    "ring-queue-fp32-64x256x256x16": (0, 1, {"resident": 4}),
 }
 
 
@@ -429,11 +437,13 @@ def run_profile_case(name):
     if opts.get("resident"):
         rnet = ll.Net(net.dims, net.acts, net.wtype, rows)
         Wd, bd, sd = ll.device_weights(net, Ws, bs)
-        n = 200
+        n = 2000 if opts["resident"] == 4 else 200
         dx = torch.from_numpy(ll.config_inputs(cfg, n * rows)).cuda()
         dy = torch.empty((n * rows, net.dims[-1]), dtype=torch.float32, device="cuda")
         eo = ll.default_opts()
         eo.kernel_variant = opts["resident"]
+        if opts["resident"] == 4:
+            eo.mailbox_format, eo.ring_slots, eo.micro_batch = 1, RING_SLOTS, MICRO_BATCH
         with ll.Engine(rnet, Wd, bd, sd, device=0, opts=eo) as e:
             if e.info().kernel_variant != opts["resident"]:
                 raise RuntimeError("not the expected resident kernel for this workload")
@@ -692,32 +702,46 @@ def main():
     engine = ll.Engine(net, Ws, bs, device=dev, opts=opts(1))
     info = engine.info()
 
-    # ---------------- value: device-resident sequential queue ----------------
+    # ---------------- value: device-resident queue through the pipelined ring kernel ----------------
+    # R requests per step already in HBM, served by the ring kernel (its I/O CTA takes up to
+    # MICRO_BATCH queued requests per pass while the compute CTAs run the previous pass; the
+    # replies go to an output queue in HBM); CUDA events around each launch, L2 flushed between
+    # steps (outside the event-timed span)
     dx = torch.from_numpy(xs).to(f"cuda:{dev}")
     dy = torch.zeros((R, 16), dtype=torch.float32, device=f"cuda:{dev}")
     stamps = torch.zeros(R, dtype=torch.int64, device=f"cuda:{dev}")
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=f"cuda:{dev}")  # > 126 MB L2
+    ro = opts(1)
+    ro.kernel_variant = ll.VARIANT_PIPELINED_RING
+    ro.ring_slots, ro.micro_batch = RING_SLOTS, MICRO_BATCH
+    qeng = ll.Engine(net, Ws, bs, device=dev, opts=ro)
+    qinfo = qeng.info()
     for _ in range(W):
-        engine.run_queue(dx.data_ptr(), dy.data_ptr(), R, 1, stamps.data_ptr())
+        qeng.run_queue(dx.data_ptr(), dy.data_ptr(), R, 1)
     torch.cuda.synchronize()
     host_barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(dev)
     clocks.start()
     launch_ms = []
-    dev_lat = []
     for _ in range(K):
-        flush.zero_()  # L2 flushed between timed launches (outside the event-timed span)
+        flush.zero_()
         torch.cuda.current_stream().synchronize()
-        launch_ms.append(engine.run_queue(dx.data_ptr(), dy.data_ptr(), R, 1, stamps.data_ptr()))
-        st = stamps.cpu().numpy()
-        dev_lat.extend((np.diff(st) / 1000.0).tolist())
+        launch_ms.append(qeng.run_queue(dx.data_ptr(), dy.data_ptr(), R, 1))
     torch.cuda.synchronize()
     host_barrier()
     torch.cuda.synchronize()
     total_s = host_max(sum(launch_ms) / 1000.0)
     value = world * K * R / total_s
-    dev_stats = ll.compute_stats(np.array(dev_lat))
+    q_out = dy.cpu().numpy()
+    qeng.close()
+    # device time of one request alone: a sequential queue through the register-resident kernel,
+    # per-request completion stamps (untimed)
+    engine.run_queue(dx.data_ptr(), dy.data_ptr(), R, 1, stamps.data_ptr())
+    seq_ms = engine.run_queue(dx.data_ptr(), dy.data_ptr(), R, 1, stamps.data_ptr())
+    dev_stats = ll.compute_stats(np.diff(stamps.cpu().numpy()) / 1000.0)
+    if not np.allclose(q_out, dy.cpu().numpy(), rtol=1e-5, atol=1e-6):
+        raise RuntimeError("device queue: the ring kernel's replies differ from the register-resident kernel's")
 
     # ---------------- e2e: mailbox with host buffers through the C ABI ----------------
     def closed_loop(eng):
@@ -896,6 +920,12 @@ def main():
         "engine": {"stages": info.n_stages, "cluster_size": info.cluster_size, "threads": info.threads,
                    "smem_bytes": info.smem_bytes,
                    "kernel": "register-resident" if info.kernel_variant == 2 else "shared-memory resident"},
+        "value_engine": {"kernel": "pipelined ring (variant 4): I/O CTA + 8 compute CTAs, up to "
+                                   f"{MICRO_BATCH} queued requests per pass", "cluster_size": qinfo.cluster_size,
+                         "queue": "R requests per step in HBM, replies to HBM; CUDA events per launch, L2 flushed "
+                                  "between steps"},
+        "sequential_device": {"value": R / (seq_ms / 1000.0), "unit": "inferences/s",
+                              "note": "the same queue one request at a time through the register-resident kernel"},
         "e2e": {"value": one_value, "unit": "inferences/s", "h2d_bytes_per_step": world * R * 64 * 4,
                 "d2h_bytes_per_step": world * R * 16 * 4,
                 "mode": f"one resident engine per GPU (one persistent kernel and mailbox: a 9-SM cluster running "
@@ -922,7 +952,8 @@ def main():
         "e2e_tickbuffer": None if s_tb is None else {
             "value": tb_value, "unit": "inferences/s", "p50_us": s_tb["p50"], "p99_us": s_tb["p99"],
             "p90_us": s_tb["p90"], "mailbox": "the reference's TickBuffer layout (mailbox_format 0)"},
-        "device_latency_us": {"p50": dev_stats["p50"], "p99": dev_stats["p99"], "mean": dev_stats["mean"]},
+        "device_latency_us": {"p50": dev_stats["p50"], "p99": dev_stats["p99"], "mean": dev_stats["mean"],
+                              "note": "per request alone (sequential queue, completion stamps)"},
         "latency_floor": {**floor,
                           "e2e_p50_over_seq_floor": s_e2e["p50"] / floor_p50,
                           "e2e_p50_over_tagged_io_floor": s_e2e["p50"] / floor["tagged_x_to_y"]["p50_us"],
@@ -934,7 +965,9 @@ def main():
                      "unit": "us", "frac": floor["tagged_x_to_y"]["p50_us"] / s_e2e["p50"],
                      "peak_kind": "measured in this run: the same resident kernel with no layers echoing x to y "
                                   "through the tagged mailbox (host -> device -> host ping-pong floor)",
-                     "traffic": TRAFFIC_FIXED_BYTES + R * TRAFFIC_PER_REQUEST_BYTES if info.kernel_variant == 2 else None,
+                     "traffic": RING_TRAFFIC_FIXED_BYTES + R * RING_TRAFFIC_PER_REQUEST_BYTES,
+                     "traffic_note": "DRAM bytes of one value-leg launch (ring kernel, R queued requests), scaled "
+                                     "from the ncu capture of a 2000-request queue",
                      "hbm": {"achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                              "frac": achieved / peak,
                              "note": "algorithmic bytes = resident weights+biases (345 KB) + x/y per request over the "

@@ -2191,10 +2191,6 @@ int ll_engine_run_queue(ll_engine *e, const float *d_x, float *d_y, int n_req, i
         llh::set_error("ll_engine_run_queue: invalid arguments");
         return LL_ERR_INVALID_ARG;
     }
-    if (e->variant == 4) {
-        llh::set_error("ll_engine_run_queue: the pipelined ring kernel (variant 4) serves the mailbox only");
-        return LL_ERR_UNSUPPORTED;
-    }
     LL_CUDA_TRY(cudaSetDevice(e->device));
     int rc = engine_stop_kernel(e);
     if (rc)

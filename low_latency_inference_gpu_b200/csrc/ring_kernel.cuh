@@ -309,9 +309,10 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
             if (k.rank == 0 && tid == 0)
                 trace(k, n_req, 8);
             const uint32_t seq = *reinterpret_cast<volatile uint32_t *>(&hdr2[b][0]);
+            if (seq == kCmdExit)
+                break;  // the device queue is served (a live request never carries 0)
             uint32_t nb = *reinterpret_cast<volatile uint32_t *>(&hdr2[b][1]);
             nb = nb < 1u ? 1u : (nb > (uint32_t)MB ? (uint32_t)MB : nb);
-            (void)seq;
             {  // the pass's rows, every one on bar_x
                 if (tid == 0)
                     mbar_arrive_expect_tx(bar(2 + b), 16u * NXC * nb);
@@ -418,6 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 __syncwarp();
                 if (lane == 0)
                     mbar_arrive_remote_cta(mapa(sfree(b), (uint32_t)IO));  // this CTA's own barrier
+                if (fq[b][1] == kCmdExit)
+                    break;  // the reader's last pass (the queue is served, or the mailbox closed)
             }
             bulk_wait_group_all();  // no copy into a compute CTA may be in flight when the cluster leaves
         } else if (warp < read_warps) {
@@ -470,7 +473,28 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 uint32_t posted = 0;
                 int got = 0;
                 bool staged = false;  // the pass's rows sit in stage[b] for the forwarder
-                if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[pass & 1u])) {
+                const bool queue = p.mode == MODE_QUEUE;
+                if (queue) {
+                    // device queue: the next up-to-micro_batch requests of q_x (rows in HBM), put
+                    // into stage[b] in the ring's chunk format for the forwarder; none left: the
+                    // exit pass below
+                    const int left = p.q_n - (int)n_done;
+                    got = left < p.micro_batch ? left : p.micro_batch;
+                    uint4 *stg_p = reinterpret_cast<uint4 *>(pool + OFF_STG + b * XCH_B);
+                    for (int i = lane; i < got * NXC; i += 32) {
+                        const int r = i / NXC, ch = i - r * NXC;
+                        const float *src = p.q_x + (size_t)(n_done + (uint32_t)r) * IN + 3 * ch;
+                        const float v0 = __ldg(src);
+                        const float v1 = 3 * ch + 1 < IN ? __ldg(src + 1) : 0.f;
+                        const float v2 = 3 * ch + 2 < IN ? __ldg(src + 2) : 0.f;
+                        stg_p[i] = make_uint4(__float_as_uint(v0), __float_as_uint(v1), __float_as_uint(v2),
+                                              n_done + (uint32_t)r + 1u);
+                    }
+                    if (lane < got)
+                        mseq[g][lane] = seq_after(last, lane + 1);
+                    fence_proxy_async_shared();  // the forwarder's bulk copies read stage[b]
+                    staged = got > 0;
+                } else if (*reinterpret_cast<volatile uint32_t *>(&s_backlog[pass & 1u])) {
                     const uint32_t stg = pool_a + OFF_STG + (uint32_t)b * XCH_B;
                     got = ring_take_rows<NXC, MB>(k, last, n_done, p.micro_batch, mseq[g], &posted,
                                               reinterpret_cast<const uint4 *>(pool + OFF_STG + b * XCH_B), stg, rbar,
@@ -490,6 +514,12 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                     uint32_t c;
                     if (got > 0) {
                         c = seq_after(last, got);
+                    } else if (queue) {
+                        // the queue is served: an exit header to every compute CTA (on this pass's
+                        // buffer: they leave after the passes before it) and 0 rows to the gatherer
+                        c = kCmdExit;
+                        if (lane == 0)
+                            fwd_header(fwd, kCmdExit, 0u);
                     } else {
                         c = poll_tagged(k, last, nullptr, ring_slot(p, n_done), p.micro_batch > 1 ? &posted : nullptr,
                                         &fwd);
@@ -510,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                             mseq[g][0] = c;
                         s_backlog[(pass + 1u) & 1u] =
                             (p.micro_batch > 1 && c != kCmdExit && (int32_t)(posted - c) > 0) ? 1u : 0u;
-                        if (c == kCmdExit)
+                        if (c == kCmdExit && !queue)
                             broadcast_abort(k);
                         mrows[g] = c == kCmdExit ? 0u : (uint32_t)got;
                         mbase[g] = n_done;
@@ -582,10 +612,16 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                 }
                 __syncwarp();
                 constexpr int NYC = (OUT + 2) / 3;
-                if (lane < NYC)
+                if (p.mode == MODE_QUEUE) {
+                    if (lane < OUT)
+                        p.q_y[(size_t)(base + (uint32_t)r) * OUT + lane] = yr[lane];
+                    if (lane == 0 && p.q_stamp)
+                        p.q_stamp[base + (uint32_t)r] = globaltimer();
+                } else if (lane < NYC) {
                     st_relaxed_sys_v4(p.mb_y + (size_t)ring_slot(p, base + (uint32_t)r) * p.ring_ystride_f + 4 * lane,
                                       make_float4(yr[3 * lane], yr[3 * lane + 1], yr[3 * lane + 2],
                                                   __uint_as_float(mseq[g][r])));
+                }
                 __syncwarp();
             }
             asm volatile("bar.sync 3, %0;" ::"r"(kRingGatherThreads) : "memory");  // every row of the pass written
@@ -601,7 +637,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
         // seq_out after an exit, to resume the ring): written once here, not per pass, because
         // it shares a line with seq_in, which the host writes for every request and the reader
         // polls; a device write per pass made that line travel between CPU and GPU
-        if (gt == 0 && passes_done > 0)
+        if (gt == 0 && passes_done > 0 && p.mode != MODE_QUEUE)
             st_relaxed_sys_u32(&p.mb->seq_out, last_replied);
     }
     if (!io && tid < C)
@@ -613,8 +649,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
         st_relaxed_sys_u32(&p.ctrl->rows, rows_done);
     }
     __syncthreads();
-    if (io && tid == 0)
+    if (io && tid == 0) {
+        if (p.mode == MODE_QUEUE)
+            st_relaxed_sys_u32(&p.ctrl->exit_reason, EXIT_QUEUE_DONE);
         st_release_sys_u32(&p.ctrl->state, ST_EXITED);
+    }
 }
 
 }  // namespace llk

@@ -180,10 +180,23 @@ def test_refused_where_it_cannot_run(cfg0):
     with pytest.raises(ll.LLError) as err:  # 4 CTAs per cluster: no room for multi-row passes
         ll.Engine(net, Ws, bs, opts=opts(cluster_size=4))
     assert err.value.code == ll.LL_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("n", [1, 16, 37, 3000])
+def test_device_queue_on_the_ring_kernel(cfg0, n):
+    """A device queue (inputs in HBM) through the pipelined ring kernel: the reader takes up to
+    16 queued requests per pass, the gatherer writes the replies to the output queue, and the
+    last pass tells every CTA to leave.  Replies are bit-identical to single requests; the
+    mailbox works again after the queue launch."""
     torch = pytest.importorskip("torch")
-    with ll.Engine(net, Ws, bs, opts=opts()) as e:
-        dx = torch.zeros((4, 64), device="cuda")
-        dy = torch.zeros((4, 16), device="cuda")
-        with pytest.raises(ll.LLError) as err:
-            e.run_queue(dx.data_ptr(), dy.data_ptr(), 4, 1)
-        assert err.value.code == ll.LL_ERR_UNSUPPORTED
+    net, Ws, bs, xs, ref, single = cfg0
+    idx = np.arange(n) % xs.shape[0]
+    dx = torch.from_numpy(np.ascontiguousarray(xs[idx])).cuda()
+    dy = torch.full((n, 16), float("nan"), device="cuda")
+    with ll.Engine(net, Ws, bs, opts=opts(ring_slots=64, micro_batch=16)) as e:
+        ms = e.run_queue(dx.data_ptr(), dy.data_ptr(), n, 1)
+        inf = e.info()
+        assert inf.status == ll.LL_OK and ms > 0
+        assert inf.rows == n and inf.passes == -(-n // 16)  # full passes of 16, the rest in one
+        assert np.array_equal(e.infer(xs[5])[0], single[5])
+    assert np.array_equal(dy.cpu().numpy(), single[idx])
