@@ -2191,6 +2191,11 @@ int ll_engine_run_queue(ll_engine *e, const float *d_x, float *d_y, int n_req, i
         llh::set_error("ll_engine_run_queue: invalid arguments");
         return LL_ERR_INVALID_ARG;
     }
+    if (e->variant == 4 && reinterpret_cast<uintptr_t>(d_x) % 16 != 0) {
+        llh::set_error("ll_engine_run_queue: the pipelined ring kernel reads the queue by bulk copies: d_x must be "
+                       "16-byte aligned");
+        return LL_ERR_INVALID_ARG;
+    }
     LL_CUDA_TRY(cudaSetDevice(e->device));
     int rc = engine_stop_kernel(e);
     if (rc)

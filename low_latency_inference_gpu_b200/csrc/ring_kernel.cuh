@@ -149,8 +149,8 @@ __device__ __forceinline__ void ring_forward(uint32_t seq, int nb, uint32_t stag
 }
 
 // Layout of the ring kernel's dynamic shared-memory pool (bytes).  Compute CTAs use [xs | h1[3]
-// | h2 | xch[2]], the I/O CTA [gath[NG] | yo | stage[2]] (stage: its copies of the rows it
-// forwards).  Remote writes go to the other role's region at the same offset in the receiving
+// | h2 | xch[2]], the I/O CTA [gath[NG] | yo | stage[2] | qx] (stage: its copies of the rows it
+// forwards; qx: a device-queue pass's rows as they are stored in HBM).  Remote writes go to the other role's region at the same offset in the receiving
 // CTA.  h1 holds layer 1's outputs slice-major (ring_layers.cuh); a split pass's slices arrive
 // from every compute CTA, so there are three buffers, used by pass % 3: the slowest compute CTA
 // is at most two passes behind the fastest (the reader hands pass p + 2 over only when every
@@ -173,7 +173,8 @@ struct RingPool {
     static constexpr int OFF_G = 0;
     static constexpr int OFF_YO = OFF_G + kRingGathBufs * 4 * GATH_F;
     static constexpr int OFF_STG = (OFF_YO + 4 * MB * YO + 15) / 16 * 16;
-    static constexpr int IO_END = OFF_STG + 2 * XCH_B;
+    static constexpr int OFF_QX = OFF_STG + 2 * XCH_B;  // device queue: a pass's rows as stored in HBM
+    static constexpr int IO_END = OFF_QX + 4 * MB * IN;
     static constexpr int BYTES = COMPUTE_END > IO_END ? COMPUTE_END : IO_END;
 };
 
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
     constexpr int IO = C;  // rank of the I/O CTA
     constexpr int OFF_XS = PL::OFF_XS, OFF_H1 = PL::OFF_H1, OFF_H2 = PL::OFF_H2, OFF_XCH = PL::OFF_XCH;
     constexpr int XCH_B = PL::XCH_B, GATH_F = PL::GATH_F, OFF_G = PL::OFF_G, OFF_YO = PL::OFF_YO;
-    constexpr int OFF_STG = PL::OFF_STG;
+    constexpr int OFF_STG = PL::OFF_STG, OFF_QX = PL::OFF_QX;
     extern __shared__ __align__(128) uint8_t pool[];  // PL::BYTES, dynamic
     __shared__ __align__(16) uint32_t hdr2[2][4];  // compute CTAs: {seq, rows} of the pass in buffer b
     __shared__ __align__(8) uint64_t rb[14 + 3 * kRingGathBufs];  // see the barrier indices below
@@ -481,12 +482,32 @@ __global__ void __launch_bounds__(kThreads, 1) ll_ring_kernel(const __grid_const
                     const int left = p.q_n - (int)n_done;
                     got = left < p.micro_batch ? left : p.micro_batch;
                     uint4 *stg_p = reinterpret_cast<uint4 *>(pool + OFF_STG + b * XCH_B);
+                    if (got > 0) {
+                        // the rows, contiguous in HBM, by one bulk copy into qx (bounded wait),
+                        // then into the chunk format from shared memory
+                        __syncwarp();
+                        if (lane == 0) {
+                            fence_proxy_async_shared();  // the previous pass's reads of qx come first
+                            mbar_arrive_expect_tx(rbar, 4u * IN * (uint32_t)got);
+                            bulk_g2s(pool_a + OFF_QX, p.q_x + (size_t)n_done * IN, 4u * IN * (uint32_t)got, rbar);
+                        }
+                        const int w = warp_wait_bar(k, rbar, rphase & 1u, p.step_ns, false);
+                        ++rphase;
+                        if (w != 1) {
+                            if (lane == 0) {
+                                report_error(k, LL_ERR_DEVICE_FAULT, EW_PEER_POLL);
+                                broadcast_abort(k);
+                            }
+                            got = 0;
+                        }
+                    }
+                    const float *qrow = reinterpret_cast<const float *>(pool + OFF_QX);
                     for (int i = lane; i < got * NXC; i += 32) {
                         const int r = i / NXC, ch = i - r * NXC;
-                        const float *src = p.q_x + (size_t)(n_done + (uint32_t)r) * IN + 3 * ch;
-                        const float v0 = __ldg(src);
-                        const float v1 = 3 * ch + 1 < IN ? __ldg(src + 1) : 0.f;
-                        const float v2 = 3 * ch + 2 < IN ? __ldg(src + 2) : 0.f;
+                        const float *src = qrow + r * IN + 3 * ch;
+                        const float v0 = src[0];
+                        const float v1 = 3 * ch + 1 < IN ? src[1] : 0.f;
+                        const float v2 = 3 * ch + 2 < IN ? src[2] : 0.f;
                         stg_p[i] = make_uint4(__float_as_uint(v0), __float_as_uint(v1), __float_as_uint(v2),
                                               n_done + (uint32_t)r + 1u);
                     }
