@@ -9,8 +9,9 @@
 // per register) 64 on 5 clusters (1 layer each).  A bf16 net computes in fp32 on bf16 inputs:
 // x and every hidden output are rounded to bf16, the last layer's output is not.  Per request
 // only x and the activations move:
-//   stage 0  : rank 0 takes the request (tagged slot, TickBuffer or device queue) and pushes
-//              {seq} + x into the other CTAs' shared memory (st.async, one mbarrier);
+//   stage 0  : on the mailbox rank 0 takes the request (tagged slot or TickBuffer) and pushes
+//              {seq} + x into the other CTAs' shared memory (st.async, one mbarrier); from a
+//              device queue every CTA of the stage loads x from HBM itself (no push);
 //   a layer  : rows split over the cluster, R = H / C rows per CTA, RPW = R / 16 per warp:
 //              lane l takes the 16-byte input pieces l, l + 32, ... for all RPW rows (a
 //              quarter-warp reads 128 consecutive bytes), then a transpose-reduce over the warp
@@ -22,8 +23,8 @@
 //              poll those words until each carries the request's number;
 //   last layer: K-split over the local rows of the layer before it (no all-gather): warp w
 //              owns outputs OPW w .. OPW w + OPW - 1, lane l takes local rows l, l + 32, ...;
-//              the CTA's OUT partials go to rank 0 as one bulk copy, and rank 0 adds the C partials in rank order, writes y
-//              and publishes.
+//              the CTA's OUT partials go to rank 0 as one bulk copy, and rank 0 adds the C
+//              partials in rank order, writes y and publishes.
 // One request is in flight at a time: stage 0 takes request n once the last stage has
 // published request n-1 (a counter), so every hand-off buffer holds one request.
 // Measured (config 1, device queue): 12.4 us per request against 19.5 for the generic
@@ -319,7 +320,9 @@ __global__ void __launch_bounds__(kThreads, 1) ll_deep_kernel(const __grid_const
                 break;  // every stage knows the queue length
             uint32_t seq;
             // ---------------- 1. the stage's input ----------------
-            if (s == 0 && k.rank == 0) {
+            // Device queue: every CTA of stage 0 takes the request itself (x from HBM), so x
+            // needs no push between them; on the mailbox rank 0 takes it and pushes x.
+            if (s == 0 && (k.rank == 0 || p.mode == MODE_QUEUE)) {
                 if (n_done > 0) {
                     // the last stage has published request n_done - 1 (bounded wait)
                     if (tid == 0) {
@@ -343,7 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_deep_kernel(const __grid_const
                 if (p.mode == MODE_QUEUE) {
                     if (tid == 0) {
                         sh.cmd = n_done + 1u;
-                        trace(k, n_done, 0);
+                        if (k.rank == 0)
+                            trace(k, n_done, 0);
                     }
                     if (tid < IN / 4) {
                         float4 v = __ldg(reinterpret_cast<const float4 *>(p.q_x + (size_t)n_done * IN) + tid);
@@ -382,11 +386,11 @@ __global__ void __launch_bounds__(kThreads, 1) ll_deep_kernel(const __grid_const
                 seq = *reinterpret_cast<volatile uint32_t *>(&sh.cmd);
                 if (seq == kCmdExit)
                     break;
-                if (tid == 0)
+                if (tid == 0 && k.rank == 0)
                     trace(k, n_done, 1);
                 // {seq} + x into the other CTAs of the stage: (C - 1) (1 + IN / 4) stores of 16 bytes
                 constexpr int per = 1 + IN / 4;
-                for (int i = tid; i < (C - 1) * per; i += kThreads) {
+                for (int i = tid; p.mode != MODE_QUEUE && i < (C - 1) * per; i += kThreads) {
                     const uint32_t d = 1u + (uint32_t)(i / per);
                     const int j = i % per;
                     if (j == 0)
@@ -396,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) ll_deep_kernel(const __grid_const
                         st_async_v4(mapa(x_addr + (uint32_t)(j - 1) * 16u, d), reinterpret_cast<const float4 *>(xs)[j - 1],
                                     mapa(bar_req, d));
                 }
-                if (tid == 0)
+                if (tid == 0 && k.rank == 0)
                     trace(k, n_done, 2);
             } else if (s == 0) {
                 if (tid == 0)
