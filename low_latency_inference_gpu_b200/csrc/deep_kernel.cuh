@@ -9,8 +9,9 @@
 // per register) 64 on 5 clusters (1 layer each).  A bf16 net computes in fp32 on bf16 inputs:
 // x and every hidden output are rounded to bf16, the last layer's output is not.  Per request
 // only x and the activations move:
-//   stage 0  : on the mailbox rank 0 takes the request (tagged slot or TickBuffer) and pushes
-//              {seq} + x into the other CTAs' shared memory (st.async, one mbarrier); from a
+//   stage 0  : on the mailbox rank 0 takes the request and sends it to the other CTAs' shared
+//              memory (st.async, one mbarrier): a tagged slot's chunks straight from the polling
+//              lanes' registers, the TickBuffer's {seq} + x from shared memory; from a
 //              device queue every CTA of the stage loads x from HBM itself (no push);
 //   a layer  : rows split over the cluster, R = H / C rows per CTA, RPW = R / 16 per warp:
 //              lane l takes the 16-byte input pieces l, l + 32, ... for all RPW rows (a
@@ -239,6 +240,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_deep_kernel(const __grid_const
     constexpr int XW = IN > H ? IN : H;
     constexpr int NYC = (OUT + 2) / 3;  // tagged y chunks
     __shared__ __align__(16) float xs[XW];      // the stage's input: x (stage 0) or the previous stage's outputs
+    constexpr int NXC = (IN + 2) / 3;           // tagged chunks of x
+    __shared__ __align__(16) uint4 xch[NXC];    // stage 0 peers: x's tagged chunks, forwarded by rank 0
     __shared__ __align__(16) float hb[2][H];    // all-gathered hidden vectors, alternating by layer
     __shared__ __align__(16) float hloc[D::R];  // this CTA's rows of the layer before a K-split last layer
     __shared__ __align__(16) float gath[C * OUT];  // last stage, rank 0: partials [rank][output]
@@ -357,7 +360,10 @@ __global__ void __launch_bounds__(kThreads, 1) ll_deep_kernel(const __grid_const
                     }
                 } else if (p.mailbox_format == 1) {
                     if (warp == 0) {
-                        const uint32_t c = poll_tagged(k, last, xs, ring_slot(p, n_done));
+                        // the polling lanes forward the chunks to the peers straight from registers
+                        // (with the header {seq, 1}, on the peers' request barrier)
+                        const ChunkFwd fwd{smem_u32(xch), h_addr, bar_req, bar_req, 1, C - 1, 0};
+                        const uint32_t c = poll_tagged(k, last, xs, ring_slot(p, n_done), nullptr, &fwd);
                         if (lane == 0) {
                             if (c == kCmdExit)
                                 broadcast_abort(k);
@@ -390,7 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1) ll_deep_kernel(const __grid_const
                     trace(k, n_done, 1);
                 // {seq} + x into the other CTAs of the stage: (C - 1) (1 + IN / 4) stores of 16 bytes
                 constexpr int per = 1 + IN / 4;
-                for (int i = tid; p.mode != MODE_QUEUE && i < (C - 1) * per; i += kThreads) {
+                const bool push = p.mode == MODE_MAILBOX && p.mailbox_format == 0;  // (tagged: forwarded)
+                for (int i = tid; push && i < (C - 1) * per; i += kThreads) {
                     const uint32_t d = 1u + (uint32_t)(i / per);
                     const int j = i % per;
                     if (j == 0)
@@ -404,11 +411,23 @@ __global__ void __launch_bounds__(kThreads, 1) ll_deep_kernel(const __grid_const
                     trace(k, n_done, 2);
             } else if (s == 0) {
                 if (tid == 0)
-                    mbar_arrive_expect_tx(bar_req, 16u + 4u * IN);
+                    mbar_arrive_expect_tx(bar_req, 16u + (p.mailbox_format == 1 ? 16u * NXC : 4u * IN));
                 if (!cta_wait_bar(k, bar_req, ph_req & 1u, EW_PEER_POLL, p.idle_ns + p.peer_margin_ns))
                     break;
                 ++ph_req;
                 seq = *reinterpret_cast<volatile uint32_t *>(&sh.hdr[0]);
+                if (p.mailbox_format == 1) {
+                    // unpack the forwarded {v0, v1, v2, tag} chunks into x (rounded to bf16 for a
+                    // bf16 net, as rank 0's poll does)
+                    for (int ch = tid; ch < NXC; ch += kThreads) {
+                        const uint4 v = xch[ch];
+                        const float f[3] = {__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z)};
+#pragma unroll
+                        for (int e = 0; e < 3; ++e)
+                            if (3 * ch + e < IN)
+                                xs[3 * ch + e] = kBf16 ? round_bf16(f[e]) : f[e];
+                    }
+                }
             } else {
                 // The previous stage's outputs arrive as words {seq, fp32} (deep_poll_words).
                 // Queue mode numbers requests 1, 2, ... per launch (the words are cleared at every
